@@ -1,0 +1,326 @@
+// Paged-KV grouped-query decode attention (one new token per sequence).
+//
+// Grid (splits, kv_heads, batch); a CTA of 4 warps owns one (sequence, kv head) pair and a range of
+// 16-token KV pages. All G = nq / nkv query heads of the group are processed together as the
+// 16-row A operand of m16n8k16 tensor-core MMAs (rows >= G are zero padding), so each KV byte is
+// read once per group: S = Q K^T and O += P V per page, online softmax in the log2 domain.
+// Each warp streams its own pages (double-buffered, XOR-swizzled shared memory so ldmatrix is
+// conflict-free); warps are merged in shared memory and splits are merged by the last CTA of the
+// (sequence, head) pair, found with an atomic counter that the merging CTA resets to zero.
+//
+// KV layout: [num_blocks, nkv, 16, D] (one 4 KB contiguous page per head at D = 128, bf16).
+#include <float.h>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace cob {
+namespace {
+
+constexpr int kD = 128, kBS = 16, kWarps = 4, kRows = 16;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                                        uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// element offset of 16-byte chunk `ch` of row `r` in a swizzled [rows][kD] tile
+__device__ __forceinline__ int swz(int r, int ch) { return r * kD + ((ch ^ (r & 7)) << 3); }
+
+__device__ __forceinline__ float safe_exp2_diff(float a, float b) { return a == -INFINITY ? 0.f : exp2f(a - b); }
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const AttnParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  T* sQ = reinterpret_cast<T*>(smem);                 // [16][kD]
+  T* sKV = sQ + kRows * kD;                           // [kWarps][2 stages][K,V][kBS][kD]
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.nq / p.nkv;
+  constexpr int CH = kD / 8;  // 16-byte chunks per row
+
+  pdl_wait();
+  const int seq = p.seq_lens[b];
+  const int npages = (seq + kBS - 1) / kBS;
+  const int pg0 = split * p.pages_per_split, pg1 = min(npages, pg0 + p.pages_per_split);
+
+  const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
+  for (int c = threadIdx.x; c < kRows * CH; c += blockDim.x) {
+    const int r = c / CH, ch = c % CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = reinterpret_cast<const uint4*>(q + (size_t)r * kD)[ch];
+    *reinterpret_cast<uint4*>(sQ + swz(r, ch)) = v;
+  }
+  __syncthreads();
+  uint32_t qa[kD / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < kD / 16; ++ks) {
+    const int r = lane & 15, ch = ks * 2 + (lane >> 4);
+    ldsm_x4(qa[ks], sQ + swz(r, ch));
+  }
+
+  const T* kc = reinterpret_cast<const T*>(p.k_cache);
+  const T* vc = reinterpret_cast<const T*>(p.v_cache);
+  T* myKV = sKV + (size_t)warp * 2 * 2 * kBS * kD;
+  auto stageK = [&](int st) { return myKV + (size_t)st * 2 * kBS * kD; };
+  auto stageV = [&](int st) { return myKV + (size_t)st * 2 * kBS * kD + kBS * kD; };
+  auto issue = [&](int pg, int st) {
+    const int blk = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg];
+    const size_t off = ((size_t)blk * p.nkv + kvh) * kBS * kD;
+    T* dk = stageK(st);
+    T* dv = stageV(st);
+#pragma unroll
+    for (int c = lane; c < kBS * CH; c += 32) {
+      const int r = c / CH, ch = c % CH;
+      cp_async16(dk + swz(r, ch), kc + off + (size_t)r * kD + ch * 8);
+      cp_async16(dv + swz(r, ch), vc + off + (size_t)r * kD + ch * 8);
+    }
+    cp_async_commit();
+  };
+
+  const float sl2 = p.scale * kLog2e;
+  float o[kD / 8][4];
+#pragma unroll
+  for (int n = 0; n < kD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  int st = 0;
+  if (pg0 + warp < pg1) issue(pg0 + warp, 0);
+  for (int pg = pg0 + warp; pg < pg1; pg += kWarps, st ^= 1) {
+    const int nxt = pg + kWarps;
+    if (nxt < pg1) {
+      issue(nxt, st ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    const T* sK = stageK(st);
+    const T* sV = stageV(st);
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < kD / 16; ++ks) {
+        const int tok = nt * 8 + (lane & 7), ch = ks * 2 + ((lane >> 3) & 1);
+        uint32_t b0, b1;
+        ldsm_x2(b0, b1, sK + swz(tok, ch));
+        mma16816<T>(s[nt], qa[ks], b0, b1);
+      }
+    }
+    // scale, mask the tail of the last page, online softmax (rows lane/4 and lane/4 + 8)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int tok = pg * kBS + nt * 8 + 2 * (lane & 3) + (j & 1);
+        s[nt][j] = tok < seq ? s[nt][j] * sl2 : -INFINITY;
+      }
+      mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float a0 = safe_exp2_diff(m0, mn0), a1 = safe_exp2_diff(m1, mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float pr[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      pr[nt][0] = exp2f(s[nt][0] - mn0);
+      pr[nt][1] = exp2f(s[nt][1] - mn0);
+      pr[nt][2] = exp2f(s[nt][2] - mn1);
+      pr[nt][3] = exp2f(s[nt][3] - mn1);
+    }
+    l0 = l0 * a0 + pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1];
+    l1 = l1 * a1 + pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3];
+    uint32_t pa[4];
+    pa[0] = pack2<T>(pr[0][0], pr[0][1]);
+    pa[1] = pack2<T>(pr[0][2], pr[0][3]);
+    pa[2] = pack2<T>(pr[1][0], pr[1][1]);
+    pa[3] = pack2<T>(pr[1][2], pr[1][3]);
+#pragma unroll
+    for (int n = 0; n < kD / 8; ++n) {
+      o[n][0] *= a0;
+      o[n][1] *= a0;
+      o[n][2] *= a1;
+      o[n][3] *= a1;
+      const int tok = lane & 15;  // lanes 0-7: tokens 0-7, lanes 8-15: tokens 8-15
+      uint32_t b0, b1;
+      ldsm_x2_t(b0, b1, sV + swz(tok, n));
+      mma16816<T>(o[n], pa, b0, b1);
+    }
+    __syncwarp();
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  // ---- merge the warps (shared memory reused)
+  __syncthreads();
+  float* sO = reinterpret_cast<float*>(sKV);           // [kWarps][16][kD]
+  float* sML = sO + kWarps * kRows * kD;               // [kWarps][16][2]
+  {
+    const int r = lane >> 2, c = 2 * (lane & 3);
+#pragma unroll
+    for (int n = 0; n < kD / 8; ++n) {
+      float* base = sO + ((size_t)warp * kRows) * kD + n * 8 + c;
+      base[(size_t)r * kD] = o[n][0];
+      base[(size_t)r * kD + 1] = o[n][1];
+      base[(size_t)(r + 8) * kD] = o[n][2];
+      base[(size_t)(r + 8) * kD + 1] = o[n][3];
+    }
+    if ((lane & 3) == 0) {
+      sML[(warp * kRows + r) * 2] = m0;
+      sML[(warp * kRows + r) * 2 + 1] = l0;
+      sML[(warp * kRows + r + 8) * 2] = m1;
+      sML[(warp * kRows + r + 8) * 2 + 1] = l1;
+    }
+  }
+  __syncthreads();
+  T* out = reinterpret_cast<T*>(p.out) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
+  const size_t pair = (size_t)b * p.nkv + kvh;
+  float* po = p.part_o + (pair * p.splits + split) * (size_t)G * kD;
+  float* pml = p.part_ml + (pair * p.splits + split) * (size_t)G * 2;
+  for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
+    const int g = idx / kD, d = idx - g * kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sML[(w * kRows + g) * 2]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = safe_exp2_diff(sML[(w * kRows + g) * 2], M);
+      L += f * sML[(w * kRows + g) * 2 + 1];
+      O += f * sO[((size_t)w * kRows + g) * kD + d];
+    }
+    if (p.splits == 1) {
+      out[(size_t)g * kD + d] = from_f<T>(O / L);
+    } else {
+      po[idx] = O;
+      if (d == 0) {
+        pml[g * 2] = M;
+        pml[g * 2 + 1] = L;
+      }
+    }
+  }
+  if (p.splits == 1) return;
+  // ---- the last split of this (sequence, head) pair merges all splits
+  __threadfence();
+  __syncthreads();
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(&p.counters[pair], 1);
+    s_last = prev == p.splits - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* po0 = p.part_o + pair * p.splits * (size_t)G * kD;
+  const float* pml0 = p.part_ml + pair * p.splits * (size_t)G * 2;
+  for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
+    const int g = idx / kD;
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(pml0 + ((size_t)sp * G + g) * 2));
+    float L = 0.f, O = 0.f;
+    for (int sp = 0; sp < p.splits; ++sp) {
+      const float f = safe_exp2_diff(__ldcg(pml0 + ((size_t)sp * G + g) * 2), M);
+      L += f * __ldcg(pml0 + ((size_t)sp * G + g) * 2 + 1);
+      O += f * __ldcg(po0 + (size_t)sp * G * kD + idx);
+    }
+    out[idx] = from_f<T>(O / L);
+  }
+  if (threadIdx.x == 0) p.counters[pair] = 0;
+}
+
+}  // namespace
+
+size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_dim) {
+  const size_t pairs = (size_t)batch * nkv;
+  return pairs * splits * group * head_dim * sizeof(float) + pairs * splits * group * 2 * sizeof(float) +
+         pairs * sizeof(int32_t);
+}
+
+cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
+  if (p.head_dim != kD || p.block_size != kBS || p.nkv <= 0 || p.nq % p.nkv != 0 || p.nq / p.nkv > kRows ||
+      p.splits <= 0 || p.pages_per_split <= 0 || p.batch <= 0)
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)kRows * kD * 2 + (size_t)kWarps * 2 * 2 * kBS * kD * 2;
+  static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 <= kWarps * 2 * 2 * kBS * kD * 2,
+                "merge buffers must fit in the KV stages");
+  const dim3 grid(p.splits, p.nkv, p.batch);
+  cudaError_t e;
+  if (p.dtype == kBF16) {
+    e = cudaFuncSetAttribute(k_decode_attn<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_decode_attn<__nv_bfloat16><<<grid, kWarps * 32, smem, s>>>(p);
+  } else if (p.dtype == kF16) {
+    e = cudaFuncSetAttribute(k_decode_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_decode_attn<__half><<<grid, kWarps * 32, smem, s>>>(p);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace cob

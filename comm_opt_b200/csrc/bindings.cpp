@@ -1,0 +1,173 @@
+// Python bindings of comm_opt_b200._C. Kernel sources are plain CUDA (no torch headers); this file
+// only converts tensors to raw pointers, picks the current stream and turns error codes into
+// exceptions.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "fused_ar.h"
+#include "ops.h"
+#include "types.h"
+
+namespace {
+
+using cob::Layout;
+
+std::vector<int64_t> layout_to_vec(const Layout& L) {
+  return {L.state, L.flags, L.nvls,  L.land1,    L.rs,     L.ag,     L.agp,   L.stage,      L.hbuf,
+          L.hpart, L.gather, L.total, L.world, L.max_rows, L.max_hv, L.sv_max, L.esize, L.max_gather};
+}
+
+Layout vec_to_layout(const std::vector<int64_t>& v) {
+  TORCH_CHECK(v.size() == 18, "layout must have 18 fields");
+  Layout L;
+  L.state = v[0];
+  L.flags = v[1];
+  L.nvls = v[2];
+  L.land1 = v[3];
+  L.rs = v[4];
+  L.ag = v[5];
+  L.agp = v[6];
+  L.stage = v[7];
+  L.hbuf = v[8];
+  L.hpart = v[9];
+  L.gather = v[10];
+  L.total = v[11];
+  L.world = (int)v[12];
+  L.max_rows = (int)v[13];
+  L.max_hv = (int)v[14];
+  L.sv_max = (int)v[15];
+  L.esize = (int)v[16];
+  L.max_gather = (int)v[17];
+  return L;
+}
+
+int dtype_code(const torch::Tensor& t) {
+  switch (t.scalar_type()) {
+    case torch::kFloat: return cob::kF32;
+    case torch::kHalf: return cob::kF16;
+    case torch::kBFloat16: return cob::kBF16;
+    default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+  }
+  return -1;
+}
+
+void check_cuda(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+}
+
+void check_dense(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+std::vector<int64_t> py_plan_layout(int64_t world, int64_t max_rows, int64_t max_hidden, int64_t esize,
+                                    int64_t max_gather) {
+  return layout_to_vec(cob::plan_layout((int)world, (int)max_rows, (int)max_hidden, (int)esize, (int)max_gather));
+}
+
+void py_init_heap(torch::Tensor heap, std::vector<int64_t> layout, int64_t dtype) {
+  check_dense(heap, "heap");
+  const Layout L = vec_to_layout(layout);
+  TORCH_CHECK(heap.numel() * heap.element_size() >= L.total, "heap smaller than layout");
+  const c10::cuda::CUDAGuard g(heap.device());
+  check_cuda(cob::init_heap(reinterpret_cast<char*>(heap.data_ptr()), L, (int)dtype,
+                            at::cuda::getCurrentCUDAStream()),
+             "init_heap");
+}
+
+// Returns {status, variant, blocks, threads, cluster}; status is a cudaError_t of the configuration
+// check (the Python side raises with the resolved geometry in the message).
+std::vector<int64_t> py_fused_ar(std::vector<int64_t> bases, int64_t mc, std::vector<int64_t> layout,
+                                 torch::Tensor x, torch::Tensor residual, torch::Tensor gamma, torch::Tensor out,
+                                 int64_t rank, int64_t rows, int64_t hidden, double eps, int64_t variant,
+                                 int64_t blocks, int64_t threads, int64_t cluster, int64_t emulate, int64_t pdl,
+                                 int64_t norm, int64_t timeout_ns, int64_t x_rs, int64_t res_rs, int64_t out_rs,
+                                 bool dry_run) {
+  cob::ARParams p = {};
+  TORCH_CHECK(bases.size() >= 2 && bases.size() <= cob::kMaxWorld, "world must be 2..8");
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
+  p.mc = reinterpret_cast<char*>(mc);
+  p.L = vec_to_layout(layout);
+  check_dense(x, "x");
+  check_dense(out, "out");
+  TORCH_CHECK(out.scalar_type() == x.scalar_type(), "out dtype must match x");
+  if (norm) {
+    check_dense(residual, "residual");
+    check_dense(gamma, "gamma");
+    TORCH_CHECK(residual.scalar_type() == x.scalar_type() && gamma.scalar_type() == x.scalar_type(),
+                "x, residual and gamma must share a dtype");
+    p.residual = residual.data_ptr();
+    p.gamma = gamma.data_ptr();
+  }
+  p.x = x.data_ptr();
+  p.out = out.data_ptr();
+  p.x_rs = x_rs;
+  p.res_rs = res_rs;
+  p.out_rs = out_rs;
+  p.rank = (int)rank;
+  p.world = (int)bases.size();
+  p.rows = (int)rows;
+  p.hidden = (int)hidden;
+  p.eps = (float)eps;
+  p.variant = (int)variant;
+  p.blocks = (int)blocks;
+  p.threads = (int)threads;
+  p.cluster = (int)cluster;
+  p.emulate = (int)emulate;
+  p.pdl = (int)pdl;
+  p.norm = (int)norm;
+  p.dtype = dtype_code(x);
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  TORCH_CHECK(p.L.world == p.world, "layout world ", p.L.world, " != ", p.world);
+  TORCH_CHECK(p.L.esize == (int)x.element_size(), "communicator dtype size ", p.L.esize, " != input ",
+              x.element_size());
+  TORCH_CHECK(p.variant >= 1 && p.variant < cob::kNumVariants, "variant must be resolved by the caller");
+  const c10::cuda::CUDAGuard g(x.device());
+  int sms = 0;
+  check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index()), "sm count");
+  const cudaError_t rc = cob::resolve_config(p, sms);
+  if (rc == cudaSuccess && !dry_run)
+    check_cuda(cob::launch_fused_ar(p, at::cuda::getCurrentCUDAStream()), "fused_ar launch");
+  return {(int64_t)rc, p.variant, p.blocks, p.threads, p.cluster};
+}
+
+void py_allgather_u32(std::vector<int64_t> bases, std::vector<int64_t> layout, torch::Tensor in, torch::Tensor out,
+                      int64_t rank, int64_t n, int64_t emulate, int64_t timeout_ns, int64_t in_rs, int64_t out_rs) {
+  cob::GatherParams p = {};
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
+  p.L = vec_to_layout(layout);
+  check_dense(in, "in");
+  check_dense(out, "out");
+  TORCH_CHECK(in.element_size() == 4 && out.element_size() == 4, "32-bit words only");
+  p.in = reinterpret_cast<const uint32_t*>(in.data_ptr());
+  p.out = reinterpret_cast<uint32_t*>(out.data_ptr());
+  p.in_rs = in_rs;
+  p.out_rs = out_rs;
+  p.rank = (int)rank;
+  p.world = (int)bases.size();
+  p.n = (int)n;
+  p.emulate = (int)emulate;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  const c10::cuda::CUDAGuard g(in.device());
+  check_cuda(cob::launch_allgather_u32(p, at::cuda::getCurrentCUDAStream()), "allgather_u32");
+}
+
+}  // namespace
+
+void register_ops(pybind11::module& m);  // ops_bindings.cpp
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "comm_opt_b200 native kernels (sm_100a)";
+  m.def("plan_layout", &py_plan_layout);
+  m.def("init_heap", &py_init_heap);
+  m.def("fused_ar", &py_fused_ar);
+  m.def("allgather_u32", &py_allgather_u32);
+  m.attr("kMaxBlocks") = cob::kMaxBlocks;
+  m.attr("kMaxWorld") = cob::kMaxWorld;
+  m.attr("kRankStateBytes") = (int64_t)sizeof(cob::RankState);
+  register_ops(m);
+}

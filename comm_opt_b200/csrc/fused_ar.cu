@@ -1,0 +1,713 @@
+// Fused tensor-parallel all-reduce + residual add + RMSNorm over NVLink 5 / NVSwitch peer memory.
+//
+//   out, residual <- RMSNorm(residual + sum_r x_r) * gamma, residual + sum_r x_r
+//
+// One kernel per call, no host barrier, safe under CUDA-graph replay. Capability parity with the
+// A100 prototype of the reference (exp/M17_epoch_ab/fused_ar_norm_nf.cu:90-199: start barrier ->
+// pull reduce-scatter -> residual + RMSNorm -> LL128 push all-gather -> poll -> last block advances
+// the epoch), re-designed for Blackwell:
+//   * world 2/4/8 (the reference hard-codes 8, fused_ar_norm_nf.cu:28),
+//   * every rank ends with the FULL new residual (the reference keeps it sharded by rows,
+//     fused_ar_norm_nf.cu:13), because the all-gather carries h = residual + sum(x) and every rank
+//     normalises locally; the two-shot variants shard columns, not rows, so T < world still uses
+//     every rank, and the per-row sum of squares travels with the data,
+//   * arrival detection without 128-byte line atomicity (the reference's unproven assumption A,
+//     docs/method_design.md:35): Lamport negative-zero sentinels (per-element atomicity only) for
+//     bulk data and {value, epoch} 8-byte words for partials,
+//   * NVSwitch multicast (multimem.ld_reduce / multimem.st / multimem.red barriers), which the
+//     A100 NV12 system of the reference did not have,
+//   * thread-block clusters with DSMEM so a single row can be spread over up to 8 SMs,
+//   * every wait bounded by %globaltimer; a timeout sets the rank's error word and the kernel
+//     returns (the reference's spins are unbounded, fused_ar_norm_nf.cu:95-96, 181-183),
+//   * global epoch advanced by the last block (same rule as the reference's M16 fix,
+//     exp/M16_epoch_fix/fused_ar_norm.cu:190-198) so graphs of different grid sizes interleave.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "fused_ar.h"
+
+namespace cob {
+namespace {
+
+namespace cg = cooperative_groups;
+
+constexpr int kVPT = 4;  // max 16-byte vectors per thread per row chunk
+
+__host__ __device__ __forceinline__ long long align_up(long long v, long long a) { return (v + a - 1) / a * a; }
+
+__device__ __forceinline__ RankState* state_of(const ARParams& p, int r) {
+  return reinterpret_cast<RankState*>(p.base[r] + p.L.state);
+}
+__device__ __forceinline__ uint4* land1_at(const ARParams& p, int owner, int slot, int src, int row, int v) {
+  return reinterpret_cast<uint4*>(p.base[owner] + p.L.land1) +
+         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.max_hv + v);
+}
+__device__ __forceinline__ uint4* rs_at(const ARParams& p, int owner, int slot, int src, int row, int i) {
+  return reinterpret_cast<uint4*>(p.base[owner] + p.L.rs) +
+         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i);
+}
+__device__ __forceinline__ uint4* ag_at(const ARParams& p, int owner, int slot, int src, int row, int i) {
+  return reinterpret_cast<uint4*>(p.base[owner] + p.L.ag) +
+         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i);
+}
+__device__ __forceinline__ unsigned long long* agp_at(const ARParams& p, int owner, int slot, int src, int row) {
+  return reinterpret_cast<unsigned long long*>(p.base[owner] + p.L.agp) +
+         (((size_t)slot * p.L.world + src) * p.L.max_rows + row);
+}
+__device__ __forceinline__ size_t stage_idx(const ARParams& p, int parity, int row, int v) {
+  return ((size_t)parity * p.L.max_rows + row) * p.L.max_hv + v;
+}
+__device__ __forceinline__ uint4* stage_at(const ARParams& p, int owner, int parity, int row, int v) {
+  return reinterpret_cast<uint4*>(p.base[owner] + p.L.stage) + stage_idx(p, parity, row, v);
+}
+
+__device__ void record_error(RankState* st, uint32_t bit, uint64_t variant_phase, uint64_t where,
+                             uint64_t peer, uint64_t epoch) {
+  if (atomicOr(&st->error, bit) == 0u) {
+    st->err_detail[0] = variant_phase;
+    st->err_detail[1] = where;
+    st->err_detail[2] = peer;
+    st->err_detail[3] = epoch;
+  }
+}
+
+// Last block of this rank's call advances the epoch (M16 rule: every block reads the same epoch at
+// start; the count of finished blocks, not the block index, decides who advances it).
+__device__ __forceinline__ void finish_call(RankState* st, uint64_t e, int blocks_per_rank) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&st->done, 1u);
+    if (prev == (unsigned)blocks_per_rank - 1u) {
+      st->done = 0u;
+      *reinterpret_cast<volatile unsigned long long*>(&st->epoch) = e;
+    }
+  }
+}
+
+// Cluster-wide (or block-wide when C == 1) sum with a fixed order. `it` alternates the shared
+// slot so one cluster barrier per row is enough.
+__device__ __forceinline__ float row_sum(float v, float* scratch, float* s_part, int it, int C) {
+  float part = block_sum(v, scratch);
+  if (C == 1) return part;
+  cg::cluster_group cluster = cg::this_cluster();
+  if (threadIdx.x == 0) s_part[it & 1] = part;
+  cluster.sync();
+  float tot = 0.f;
+  for (int c = 0; c < C; ++c) tot += *cluster.map_shared_rank(&s_part[it & 1], c);
+  return tot;
+}
+
+template <typename T>
+__device__ __forceinline__ void store_norm(const ARParams& p, T* out, T* res, int row, int v, const float* h,
+                                           const uint4& hbits, float rstd) {
+  using V = Vec<T>;
+  uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * p.hidden);
+  if (p.norm) {
+    float g[V::N], o[V::N];
+    V::to_float(ld_nc_v4(reinterpret_cast<const uint4*>(p.gamma) + v), g);
+#pragma unroll
+    for (int i = 0; i < V::N; ++i) o[i] = h[i] * rstd * g[i];
+    orow[v] = V::from_float(o);
+    reinterpret_cast<uint4*>(res + (size_t)row * p.hidden)[v] = hbits;
+  } else {
+    orow[v] = hbits;
+  }
+}
+
+// Poll a Lamport vector until every element has arrived. Returns false on timeout.
+template <typename T>
+__device__ __forceinline__ bool poll_vec(const uint4* addr, uint4& d, Waiter& w) {
+  while (!LamportOf<T>::ready(d)) {
+    if (w.expired()) return false;
+    d = ld_vol_v4(addr);
+  }
+  return true;
+}
+
+// Flag barrier between block b of every rank: each block posts its per-block call count into every
+// peer's slot and waits until all peers' counts reach it. A peer can be at most one call ahead, so
+// the comparison is ">=".
+__device__ __forceinline__ bool flag_barrier(const ARParams& p, int rank, RankState* st, uint32_t bc, Waiter& w) {
+  bool ok = true;
+  if (threadIdx.x < (unsigned)p.L.world) {
+    const int peer = threadIdx.x;
+    unsigned long long* dst =
+        reinterpret_cast<unsigned long long*>(p.base[peer] + p.L.flags) + (size_t)blockIdx.x * kMaxWorld + rank;
+    st_release_u64(dst, bc);
+    const unsigned long long* mine =
+        reinterpret_cast<unsigned long long*>(p.base[rank] + p.L.flags) + (size_t)blockIdx.x * kMaxWorld + peer;
+    while ((long long)(ld_acquire_u64(mine) - (unsigned long long)bc) < 0) {
+      if (w.expired()) {
+        record_error(st, kErrTimeoutFlag, ((uint64_t)p.variant << 32) | 0, blockIdx.x, peer, bc);
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __syncthreads_and(ok);
+}
+
+// NVLS barrier k of block b: one multicast add per rank, wait for world * calls on the local copy.
+__device__ __forceinline__ bool nvls_barrier(const ARParams& p, int rank, RankState* st, int k, uint32_t calls,
+                                             Waiter& w) {
+  bool ok = true;
+  if (threadIdx.x == 0) {
+    const size_t off = p.L.nvls + ((size_t)blockIdx.x * 2 + k) * sizeof(unsigned int);
+    mm_red_add_u32(p.mc + off, 1u);
+    const uint32_t target = calls * (uint32_t)p.L.world;
+    while ((int)(ld_acquire_u32(p.base[rank] + off) - target) < 0) {
+      if (w.expired()) {
+        record_error(st, kErrTimeoutNvls, ((uint64_t)p.variant << 32) | (uint64_t)k, blockIdx.x, 0, calls);
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __syncthreads_and(ok);
+}
+
+// ---------------------------------------------------------------------------------------------
+// One-shot kernels: cluster of C CTAs per row, chunk of the row per CTA.
+//   LAMPORT: push x to all peers' land1[slot][rank] -> poll own land1[slot][*] -> sum
+//   PULL   : copy x to stage[parity] -> flag barrier -> read every peer's stage -> sum
+//   NVLS   : copy x to stage[parity] -> multicast barrier -> multimem.ld_reduce -> sum
+// ---------------------------------------------------------------------------------------------
+template <typename T, int W, int MODE>
+__global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
+  using V = Vec<T>;
+  using LP = LamportOf<T>;
+  const int rank = p.emulate ? (int)blockIdx.y : p.rank;
+  const int tid = threadIdx.x, NT = blockDim.x;
+  RankState* st = state_of(p, rank);
+  const T* x = reinterpret_cast<const T*>(p.x) + (size_t)rank * p.x_rs;
+  T* res = reinterpret_cast<T*>(p.residual) + (size_t)rank * p.res_rs;
+  T* out = reinterpret_cast<T*>(p.out) + (size_t)rank * p.out_rs;
+  const int hv = p.hidden / V::N;
+  const int C = p.cluster;
+  const int crank = blockIdx.x % C, cl = blockIdx.x / C, ncl = gridDim.x / C;
+  const int chunk = (hv + C - 1) / C;
+  const int v0 = crank * chunk, v1 = min(hv, v0 + chunk);
+  __shared__ float s_scr[32];
+  __shared__ float s_part[2];
+
+  pdl_wait();
+  const uint64_t e = ld_vol_u64(&st->epoch) + 1;
+  const int slot = (int)(e & 1);
+  Waiter w(p.timeout_ns, &st->error);
+  bool ok = true;
+
+  if (MODE == kLamport1S) {
+    for (int row = cl; row < p.rows; row += ncl) {
+      const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
+#pragma unroll
+      for (int k = 0; k < kVPT; ++k) {
+        const int v = v0 + tid + k * NT;
+        if (v < v1) {
+          const uint4 d = LP::clean(ld_nc_v4(xr + v));
+#pragma unroll
+          for (int i = 1; i < W; ++i) st_vol_v4(land1_at(p, (rank + i) % W, slot, rank, row, v), d);
+        }
+      }
+    }
+  } else {
+    for (int row = cl; row < p.rows; row += ncl) {
+      const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
+#pragma unroll
+      for (int k = 0; k < kVPT; ++k) {
+        const int v = v0 + tid + k * NT;
+        if (v < v1) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (MODE == kPull1S) {
+      const uint32_t bc = st->flag_calls[blockIdx.x] + 1u;
+      ok = flag_barrier(p, rank, st, bc, w);
+      if (tid == 0) st->flag_calls[blockIdx.x] = bc;
+    } else {
+      const uint32_t nc = st->nvls_calls[blockIdx.x][0] + 1u;
+      ok = nvls_barrier(p, rank, st, 0, nc, w);
+      if (tid == 0) st->nvls_calls[blockIdx.x][0] = nc;
+    }
+  }
+  pdl_trigger();
+
+  int it = 0;
+  for (int row = cl; row < p.rows; row += ncl, ++it) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
+    float h[kVPT][V::N];
+    uint4 hb[kVPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < kVPT; ++k) {
+      const int v = v0 + tid + k * NT;
+      if (v < v1) {
+        float a[V::N];
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) a[i] = 0.f;
+        if (MODE == kNvls1S) {
+          const uint4 s = ok ? mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, v) * 16) : make_uint4(0, 0, 0, 0);
+          V::to_float(s, a);
+        } else {
+          uint4 d[W];
+#pragma unroll
+          for (int s = 0; s < W; ++s) {
+            if (MODE == kLamport1S)
+              d[s] = (s == rank) ? ld_nc_v4(xr + v) : ld_vol_v4(land1_at(p, rank, slot, s, row, v));
+            else
+              d[s] = ok ? ld_vol_v4(stage_at(p, s, slot, row, v)) : make_uint4(0, 0, 0, 0);
+          }
+          if (MODE == kLamport1S) {
+#pragma unroll
+            for (int s = 0; s < W; ++s) {
+              if (s != rank && ok && !poll_vec<T>(land1_at(p, rank, slot, s, row, v), d[s], w)) {
+                record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 2, ((uint64_t)row << 32) | v, s, e);
+                ok = false;
+              }
+            }
+#pragma unroll
+            for (int s = 0; s < W; ++s)
+              if (s != rank) st_vol_v4(land1_at(p, rank, slot, s, row, v), LP::fill());
+          }
+#pragma unroll
+          for (int s = 0; s < W; ++s) {
+            float f[V::N];
+            V::to_float(d[s], f);
+#pragma unroll
+            for (int i = 0; i < V::N; ++i) a[i] += f[i];
+          }
+        }
+        if (p.norm) {
+          float r[V::N];
+          V::to_float(reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden)[v], r);
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) a[i] += r[i];
+        }
+        hb[k] = V::from_float(a);  // h is stored in the element type; the norm uses the stored values
+        V::to_float(hb[k], h[k]);
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) ss += h[k][i] * h[k][i];
+      }
+    }
+    float rstd = 0.f;
+    if (p.norm) {
+      const float tot = row_sum(ss, s_scr, s_part, it, C);
+      rstd = rsqrtf(tot / (float)p.hidden + p.eps);
+    }
+#pragma unroll
+    for (int k = 0; k < kVPT; ++k) {
+      const int v = v0 + tid + k * NT;
+      if (v < v1) store_norm<T>(p, out, res, row, v, h[k], hb[k], rstd);
+    }
+  }
+  if (C > 1) cg::this_cluster().sync();  // no CTA leaves while a peer CTA may read its shared memory
+  finish_call(st, e, gridDim.x);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Two-shot kernels. Rank r owns columns [r*SV, (r+1)*SV) of every row (SV = HV / W vectors).
+//   phase 1 (LAMPORT): push slice d of x to rank d's rs[slot][rank]           (flat over (row, v))
+//   phase 1 (PULL)   : copy x to stage[parity], flag barrier                    (rows of this block)
+//   phase 1 (NVLS)   : copy x to stage[parity], multicast barrier               (rows of this block)
+//   phase 2 (owner)  : sum the owned slice of each row (+ residual) -> h, partial sum of squares;
+//                      LAMPORT/PULL push h + {partial, epoch} to every rank's ag/agp,
+//                      NVLS multimem.st h + partial into every rank's hbuf/hpart then barrier 2
+//   phase 3          : every rank reads all slices of h + all partials -> out, residual
+// ---------------------------------------------------------------------------------------------
+template <typename T, int W, int MODE>
+__global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
+  using V = Vec<T>;
+  using LP = LamportOf<T>;
+  const int rank = p.emulate ? (int)blockIdx.y : p.rank;
+  const int tid = threadIdx.x, NT = blockDim.x, lane = tid & 31;
+  RankState* st = state_of(p, rank);
+  const T* x = reinterpret_cast<const T*>(p.x) + (size_t)rank * p.x_rs;
+  T* res = reinterpret_cast<T*>(p.residual) + (size_t)rank * p.res_rs;
+  T* out = reinterpret_cast<T*>(p.out) + (size_t)rank * p.out_rs;
+  const int hv = p.hidden / V::N, sv = hv / W;
+  const long long total = (long long)p.rows * hv;
+  const long long gtid = (long long)blockIdx.x * NT + tid, gthreads = (long long)gridDim.x * NT;
+  __shared__ float s_scr[32];
+
+  pdl_wait();
+  const uint64_t e = ld_vol_u64(&st->epoch) + 1;
+  const int slot = (int)(e & 1);
+  const uint32_t etag = (uint32_t)e;
+  Waiter w(p.timeout_ns, &st->error);
+  bool ok = true;
+
+  // ---- phase 1
+  if (MODE == kLamport2S) {
+    for (long long u = gtid; u < total; u += gthreads) {
+      const int row = (int)(u / hv), v = (int)(u - (long long)row * hv);
+      const int dst = v / sv, i = v - dst * sv;
+      if (dst != rank) {
+        const uint4 d = LP::clean(ld_nc_v4(reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden) + v));
+        st_vol_v4(rs_at(p, dst, slot, rank, row, i), d);
+      }
+    }
+  } else {
+    for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+      const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
+      for (int v = tid; v < hv; v += NT) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
+    }
+    __threadfence();
+    __syncthreads();
+    if (MODE == kPull2S) {
+      const uint32_t bc = st->flag_calls[blockIdx.x] + 1u;
+      ok = flag_barrier(p, rank, st, bc, w);
+      if (tid == 0) st->flag_calls[blockIdx.x] = bc;
+    } else {
+      const uint32_t nc = st->nvls_calls[blockIdx.x][0] + 1u;
+      ok = nvls_barrier(p, rank, st, 0, nc, w);
+      if (tid == 0) st->nvls_calls[blockIdx.x][0] = nc;
+    }
+  }
+  pdl_trigger();
+
+  // ---- phase 2: owned slice of this block's rows
+  for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    float ss = 0.f;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
+#pragma unroll
+    for (int k = 0; k < kVPT; ++k) {
+      const int i = tid + k * NT;
+      if (i < sv) {
+        const int v = rank * sv + i;
+        float a[V::N];
+#pragma unroll
+        for (int q = 0; q < V::N; ++q) a[q] = 0.f;
+        if (MODE == kNvls2S) {
+          const uint4 s = ok ? mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, v) * 16) : make_uint4(0, 0, 0, 0);
+          V::to_float(s, a);
+        } else {
+          uint4 d[W];
+#pragma unroll
+          for (int s = 0; s < W; ++s) {
+            if (MODE == kLamport2S)
+              d[s] = (s == rank) ? ld_nc_v4(xr + v) : ld_vol_v4(rs_at(p, rank, slot, s, row, i));
+            else
+              d[s] = ok ? ld_vol_v4(stage_at(p, s, slot, row, v)) : make_uint4(0, 0, 0, 0);
+          }
+          if (MODE == kLamport2S) {
+#pragma unroll
+            for (int s = 0; s < W; ++s) {
+              if (s != rank && ok && !poll_vec<T>(rs_at(p, rank, slot, s, row, i), d[s], w)) {
+                record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 2, ((uint64_t)row << 32) | v, s, e);
+                ok = false;
+              }
+            }
+#pragma unroll
+            for (int s = 0; s < W; ++s)
+              if (s != rank) st_vol_v4(rs_at(p, rank, slot, s, row, i), LP::fill());
+          }
+#pragma unroll
+          for (int s = 0; s < W; ++s) {
+            float f[V::N];
+            V::to_float(d[s], f);
+#pragma unroll
+            for (int q = 0; q < V::N; ++q) a[q] += f[q];
+          }
+        }
+        if (p.norm) {
+          float r[V::N];
+          V::to_float(reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden)[v], r);
+#pragma unroll
+          for (int q = 0; q < V::N; ++q) a[q] += r[q];
+        }
+        const uint4 hb = LP::clean(V::from_float(a));
+        float hf[V::N];
+        V::to_float(hb, hf);
+#pragma unroll
+        for (int q = 0; q < V::N; ++q) ss += hf[q] * hf[q];
+        if (MODE == kNvls2S) {
+          mm_st_v4(p.mc + p.L.hbuf + ((size_t)row * p.L.max_hv + v) * 16, hb);
+        } else {
+#pragma unroll
+          for (int dd = 0; dd < W; ++dd) st_vol_v4(ag_at(p, (rank + dd) % W, slot, rank, row, i), hb);
+        }
+      }
+    }
+    const float part = p.norm ? block_sum(ss, s_scr) : 0.f;
+    const unsigned long long word = ((unsigned long long)etag << 32) | __float_as_uint(part);
+    if (MODE == kNvls2S) {
+      if (tid == 0) mm_st_u64(p.mc + p.L.hpart + ((size_t)row * p.L.world + rank) * 8, word);
+    } else if (tid < W) {
+      st_vol_u64(agp_at(p, tid, slot, rank, row), word);
+    }
+  }
+
+  if (MODE == kNvls2S) {
+    __threadfence_system();
+    __syncthreads();
+    const uint32_t nc = st->nvls_calls[blockIdx.x][1] + 1u;
+    ok = nvls_barrier(p, rank, st, 1, nc, w) && ok;
+    if (tid == 0) st->nvls_calls[blockIdx.x][1] = nc;
+    // phase 3 (NVLS): rows of this block only (the barrier covered exactly these rows)
+    for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+      float tot = 0.f;
+      if (p.norm) {
+        for (int q = 0; q < W; ++q) {
+          const unsigned long long wd =
+              ld_vol_u64(p.base[rank] + p.L.hpart + ((size_t)row * p.L.world + q) * 8);
+          if ((uint32_t)(wd >> 32) != etag && ok) {
+            if (tid == 0) record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, row, q, e);
+            ok = false;
+          }
+          tot += __uint_as_float((uint32_t)wd);
+        }
+      }
+      const float rstd = rsqrtf(tot / (float)p.hidden + p.eps);
+      for (int v = tid; v < hv; v += NT) {
+        const uint4 hb = ld_vol_v4(p.base[rank] + p.L.hbuf + ((size_t)row * p.L.max_hv + v) * 16);
+        float hf[V::N];
+        V::to_float(hb, hf);
+        store_norm<T>(p, out, res, row, v, hf, hb, rstd);
+      }
+    }
+  } else {
+    // phase 3 (LAMPORT/PULL): flat over (row, v); a warp shares one row (hv % 32 == 0)
+    for (long long u0 = gtid - lane; u0 < total; u0 += gthreads) {
+      const long long u = u0 + lane;
+      const int row = (int)(u0 / hv);
+      float tot = 0.f;
+      if (p.norm) {
+        unsigned long long wd = 0ull;
+        if (lane < W) {
+          const unsigned long long* a = agp_at(p, rank, slot, lane, row);
+          wd = ld_vol_u64(a);
+          while ((uint32_t)(wd >> 32) != etag && ok) {
+            if (w.expired()) {
+              record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, row, lane, e);
+              ok = false;
+              break;
+            }
+            wd = ld_vol_u64(a);
+          }
+        }
+        __syncwarp();
+        const float mine = __uint_as_float((uint32_t)wd);
+#pragma unroll
+        for (int q = 0; q < W; ++q) tot += __shfl_sync(0xffffffffu, mine, q);
+      }
+      if (u < total) {
+        const int v = (int)(u - (long long)row * hv);
+        const int s = v / sv, i = v - s * sv;
+        uint4* a = ag_at(p, rank, slot, s, row, i);
+        uint4 hb = ld_vol_v4(a);
+        if (ok && !poll_vec<T>(a, hb, w)) {
+          record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 3, ((uint64_t)row << 32) | v, s, e);
+          ok = false;
+        }
+        st_vol_v4(a, LP::fill());
+        float hf[V::N];
+        V::to_float(hb, hf);
+        const float rstd = rsqrtf(tot / (float)p.hidden + p.eps);
+        store_norm<T>(p, out, res, row, v, hf, hb, rstd);
+      }
+    }
+  }
+  finish_call(st, e, gridDim.x);
+}
+
+// Fill a region with a 32-bit pattern.
+__global__ void k_fill_u32(uint32_t* p, uint32_t v, long long n) {
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+// Small all-gather with LL words {data32, epoch32}: one block, tags make clearing unnecessary.
+__global__ void __launch_bounds__(1024) k_allgather_u32(const GatherParams p) {
+  const int rank = p.emulate ? (int)blockIdx.y : p.rank;
+  RankState* st = reinterpret_cast<RankState*>(p.base[rank] + p.L.state);
+  const uint32_t* in = p.in + (size_t)rank * p.in_rs;
+  uint32_t* out = p.out + (size_t)rank * p.out_rs;
+  pdl_wait();
+  const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&st->gather_epoch) + 1u;
+  const int slot = (int)(e & 1u);
+  auto at = [&](int owner, int src, int i) {
+    return reinterpret_cast<unsigned long long*>(p.base[owner] + p.L.gather) +
+           (((size_t)slot * p.L.world + src) * p.L.max_gather + i);
+  };
+  for (int i = threadIdx.x; i < p.n; i += blockDim.x) {
+    const unsigned long long word = ((unsigned long long)e << 32) | in[i];
+    for (int d = 0; d < p.world; ++d) st_vol_u64(at(d, rank, i), word);
+  }
+  Waiter w(p.timeout_ns, &st->error);
+  bool ok = true;
+  for (int idx = threadIdx.x; idx < p.n * p.world; idx += blockDim.x) {
+    const int src = idx / p.n, i = idx - src * p.n;
+    const unsigned long long* a = at(rank, src, i);
+    unsigned long long wd = ld_vol_u64(a);
+    while ((uint32_t)(wd >> 32) != e && ok) {
+      if (w.expired()) {
+        record_error(st, kErrTimeoutGather, 0, i, src, e);
+        ok = false;
+        break;
+      }
+      wd = ld_vol_u64(a);
+    }
+    out[idx] = (uint32_t)wd;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t*>(&st->gather_epoch) = e;
+}
+
+template <typename T, int W>
+cudaError_t launch_typed(const ARParams& p, cudaStream_t stream) {
+  void (*fn)(const ARParams);
+  switch (p.variant) {
+    case kLamport1S: fn = k_oneshot<T, W, kLamport1S>; break;
+    case kPull1S: fn = k_oneshot<T, W, kPull1S>; break;
+    case kNvls1S: fn = k_oneshot<T, W, kNvls1S>; break;
+    case kLamport2S: fn = k_twoshot<T, W, kLamport2S>; break;
+    case kPull2S: fn = k_twoshot<T, W, kPull2S>; break;
+    case kNvls2S: fn = k_twoshot<T, W, kNvls2S>; break;
+    default: return cudaErrorInvalidValue;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.blocks, p.emulate ? p.world : 1, 1);
+  cfg.blockDim = dim3(p.threads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  if (p.cluster > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = p.cluster;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (p.pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, fn, p);
+}
+
+template <typename T>
+cudaError_t launch_world(const ARParams& p, cudaStream_t s) {
+  switch (p.world) {
+    case 2: return launch_typed<T, 2>(p, s);
+    case 4: return launch_typed<T, 4>(p, s);
+    case 8: return launch_typed<T, 8>(p, s);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int elems_per_vec(int dtype) { return dtype == kF32 ? 4 : 8; }
+
+}  // namespace
+
+Layout plan_layout(int world, int max_rows, int max_hidden, int esize, int max_gather) {
+  Layout L = {};
+  L.world = world;
+  L.max_rows = max_rows;
+  L.esize = esize;
+  L.max_hv = (int)((long long)max_hidden * esize / 16);
+  L.sv_max = (L.max_hv + world - 1) / world;
+  L.max_gather = max_gather;
+  long long off = 0;
+  auto take = [&](long long bytes) {
+    const long long o = off;
+    off = align_up(off + bytes, 4096);
+    return o;
+  };
+  const long long R = max_rows, W = world, HV = L.max_hv, SV = L.sv_max;
+  L.state = take(sizeof(RankState));
+  L.flags = take((long long)kMaxBlocks * kMaxWorld * 8);
+  L.nvls = take((long long)kMaxBlocks * 2 * 4);
+  L.land1 = take(2 * W * R * HV * 16);
+  L.rs = take(2 * W * R * SV * 16);
+  L.ag = take(2 * W * R * SV * 16);
+  L.agp = take(2 * W * R * 8);
+  L.stage = take(2 * R * HV * 16);
+  L.hbuf = take(R * HV * 16);
+  L.hpart = take(R * W * 8);
+  L.gather = take(2 * W * (long long)max_gather * 8);
+  L.total = align_up(off, 2 << 20);
+  return L;
+}
+
+cudaError_t init_heap(char* heap, const Layout& L, int dtype, cudaStream_t stream) {
+  const uint32_t fill = dtype == kF32 ? 0x80000000u : 0x80008000u;
+  cudaError_t err = cudaMemsetAsync(heap, 0, L.total, stream);
+  if (err != cudaSuccess) return err;
+  const long long lam_begin = L.land1, lam_end = L.agp;  // land1, rs, ag are contiguous
+  const long long n = (lam_end - lam_begin) / 4;
+  k_fill_u32<<<592, 256, 0, stream>>>(reinterpret_cast<uint32_t*>(heap + lam_begin), fill, n);
+  return cudaGetLastError();
+}
+
+cudaError_t resolve_config(ARParams& p, int num_sms) {
+  const int epv = elems_per_vec(p.dtype);
+  if (p.world < 2 || p.world > kMaxWorld || (p.world & (p.world - 1)) != 0) return cudaErrorInvalidValue;
+  if (p.hidden <= 0 || p.hidden % epv != 0) return cudaErrorInvalidValue;
+  if (p.rows <= 0 || p.rows > p.L.max_rows) return cudaErrorInvalidValue;
+  const int hv = p.hidden / epv;
+  if (hv > p.L.max_hv) return cudaErrorInvalidValue;
+  const bool two = p.variant == kLamport2S || p.variant == kPull2S || p.variant == kNvls2S;
+  const bool nvls = p.variant == kNvls1S || p.variant == kNvls2S;
+  if (nvls && p.mc == nullptr) return cudaErrorNotSupported;
+  if (two && (hv % p.world != 0 || hv % 32 != 0)) return cudaErrorInvalidValue;
+  const int ranks_per_gpu = p.emulate ? p.world : 1;
+  const int budget = std::max(1, num_sms / ranks_per_gpu);  // resident CTAs (one per SM) per rank
+  if (!two) {
+    if (p.cluster <= 0) {
+      // spread a row over enough CTAs that small batches still engage several SMs, and over at
+      // least enough that each thread holds <= kVPT vectors of 512 threads
+      int c = 1;
+      while (c < 8 && (long long)p.rows * c * 2 <= budget) c *= 2;
+      while (c < 8 && (hv + c - 1) / c > 512 * kVPT) c *= 2;
+      while (c > 1 && p.blocks > 0 && p.blocks % c != 0) c /= 2;  // must divide a given block count
+      p.cluster = c;
+    }
+    const int chunk = (hv + p.cluster - 1) / p.cluster;
+    if (p.threads <= 0) p.threads = std::min(512, std::max(64, (chunk + 31) / 32 * 32));
+    if (chunk > p.threads * kVPT) return cudaErrorInvalidValue;
+    if (p.blocks <= 0) {
+      const int clusters = std::max(1, std::min(p.rows, budget / p.cluster));
+      p.blocks = clusters * p.cluster;
+    }
+    if (p.blocks % p.cluster != 0) return cudaErrorInvalidValue;
+  } else {
+    const int sv = hv / p.world;
+    if (p.threads <= 0) p.threads = sv > 1024 ? 512 : (sv > 256 ? 256 : 128);
+    p.threads = std::max(p.threads, 32);
+    if (sv > p.threads * kVPT) return cudaErrorInvalidValue;
+    p.cluster = 1;
+    if (p.blocks <= 0) {
+      // enough CTAs for the flat push / gather phases: ~2 vectors per thread, capped by the budget
+      const long long flat = ((long long)p.rows * hv + 2LL * p.threads - 1) / (2LL * p.threads);
+      long long b = std::max<long long>(p.rows, flat);
+      if (p.variant != kLamport2S) b = p.rows;  // barrier variants: one block per row group
+      p.blocks = (int)std::max<long long>(1, std::min<long long>(b, budget));
+    }
+  }
+  if (p.blocks > kMaxBlocks || p.blocks > budget) return cudaErrorInvalidValue;
+  if (p.threads > 512 || p.threads % 32 != 0) return cudaErrorInvalidValue;
+  return cudaSuccess;
+}
+
+cudaError_t launch_fused_ar(ARParams p, cudaStream_t stream) {
+  switch (p.dtype) {
+    case kF32: return launch_world<float>(p, stream);
+    case kF16: return launch_world<__half>(p, stream);
+    case kBF16: return launch_world<__nv_bfloat16>(p, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_allgather_u32(GatherParams p, cudaStream_t stream) {
+  if (p.n <= 0 || p.n > p.L.max_gather || p.world < 1 || p.world > kMaxWorld) return cudaErrorInvalidValue;
+  k_allgather_u32<<<dim3(1, p.emulate ? p.world : 1, 1), 1024, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace cob

@@ -1,0 +1,52 @@
+// Host entry points of the single-GPU decode kernels (plain CUDA, no torch types).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cob {
+
+// out = x * rsqrt(mean(x^2) + eps) * gamma                      (rows x hidden, one CTA per row)
+cudaError_t rmsnorm(const void* x, const void* gamma, void* out, int rows, int hidden, float eps, int dtype,
+                    cudaStream_t s);
+// residual += x; out = RMSNorm(residual) * gamma  (world-size-1 form of the fused op)
+cudaError_t add_rmsnorm(const void* x, void* residual, const void* gamma, void* out, int rows, int hidden,
+                        float eps, int dtype, cudaStream_t s);
+// out[i] = table[ids[i]]                                        (bf16/fp16/fp32 rows, int32 ids)
+cudaError_t embedding(const int32_t* ids, const void* table, void* out, int rows, int hidden, int dtype,
+                      cudaStream_t s);
+// qkv: [B, (nq + 2*nkv) * D]; rotates q and k by position (rotate-half RoPE, cos/sin tables
+// [max_pos, D/2] fp32), writes rotated q to q_out [B, nq, D] and k, v into the paged caches
+// [num_blocks, nkv, block, D] at slot (block_tables[b][pos / block], pos % block).
+cudaError_t rope_append_kv(const void* qkv, const int32_t* positions, const float* cos_t, const float* sin_t,
+                           const int32_t* block_tables, int max_blocks_per_seq, void* q_out, void* k_cache,
+                           void* v_cache, int batch, int nq, int nkv, int head_dim, int block_size, int dtype,
+                           cudaStream_t s);
+// out[b, i] = silu(gu[b, i]) * gu[b, I + i]
+cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s);
+// Per row: (max value as f32 bits, vocab_offset + argmax) -> words[row*2 + {0,1}]
+cudaError_t argmax_local(const void* logits, uint32_t* words, int rows, int vocab, int vocab_offset, int dtype,
+                         cudaStream_t s);
+// words: [world, rows, 2] gathered from every rank -> ids[row] (ties: lowest index)
+cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, cudaStream_t s);
+
+// Paged GQA decode attention (split-KV with in-kernel combine by the last split).
+struct AttnParams {
+  const void* q;             // [B, nq, D]
+  const void* k_cache;       // [num_blocks, nkv, block, D]
+  const void* v_cache;
+  const int32_t* block_tables;  // [B, max_blocks_per_seq]
+  const int32_t* seq_lens;      // [B]
+  void* out;                 // [B, nq, D]
+  float* part_o;             // scratch [B, nkv, splits, G, D] fp32
+  float* part_ml;            // scratch [B, nkv, splits, G, 2] fp32
+  int32_t* counters;         // scratch [B * nkv] int32, zero between calls (kernel restores it)
+  int batch, nq, nkv, head_dim, block_size, max_blocks_per_seq, splits, pages_per_split;
+  float scale;
+  int dtype;
+};
+// bytes of scratch needed for a given geometry
+size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_dim);
+cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s);
+
+}  // namespace cob

@@ -1,0 +1,159 @@
+// Bindings of the single-GPU decode kernels (see ops.h).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "ops.h"
+#include "types.h"
+
+namespace {
+
+int code_of(const torch::Tensor& t) {
+  switch (t.scalar_type()) {
+    case torch::kFloat: return cob::kF32;
+    case torch::kHalf: return cob::kF16;
+    case torch::kBFloat16: return cob::kBF16;
+    default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+  }
+  return -1;
+}
+
+void ok(cudaError_t e, const char* what) { TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
+
+void dense(const torch::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous(), n, " must be a contiguous CUDA tensor");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, n, " must be 16-byte aligned");
+}
+
+cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
+
+void py_rmsnorm(torch::Tensor x, torch::Tensor gamma, torch::Tensor out, double eps) {
+  dense(x, "x");
+  dense(gamma, "gamma");
+  dense(out, "out");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t H = x.size(-1);
+  ok(cob::rmsnorm(x.data_ptr(), gamma.data_ptr(), out.data_ptr(), (int)(x.numel() / H), (int)H, (float)eps,
+                  code_of(x), cur()),
+     "rmsnorm");
+}
+
+void py_add_rmsnorm(torch::Tensor x, torch::Tensor residual, torch::Tensor gamma, torch::Tensor out, double eps) {
+  dense(x, "x");
+  dense(residual, "residual");
+  dense(gamma, "gamma");
+  dense(out, "out");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int64_t H = x.size(-1);
+  ok(cob::add_rmsnorm(x.data_ptr(), residual.data_ptr(), gamma.data_ptr(), out.data_ptr(), (int)(x.numel() / H),
+                      (int)H, (float)eps, code_of(x), cur()),
+     "add_rmsnorm");
+}
+
+void py_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
+  dense(ids, "ids");
+  dense(table, "table");
+  dense(out, "out");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32, "ids must be int32");
+  const c10::cuda::CUDAGuard g(ids.device());
+  ok(cob::embedding(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), (int)ids.numel(),
+                    (int)table.size(1), code_of(table), cur()),
+     "embedding");
+}
+
+void py_rope_append_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_t, torch::Tensor sin_t,
+                       torch::Tensor block_tables, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
+                       int64_t nq, int64_t nkv) {
+  for (auto* t : {&qkv, &positions, &cos_t, &sin_t, &block_tables, &q_out, &k_cache, &v_cache}) dense(*t, "arg");
+  TORCH_CHECK(positions.scalar_type() == torch::kInt32 && block_tables.scalar_type() == torch::kInt32,
+              "positions and block_tables must be int32");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int D = (int)k_cache.size(3), bs = (int)k_cache.size(2);
+  ok(cob::rope_append_kv(qkv.data_ptr(), positions.data_ptr<int32_t>(), cos_t.data_ptr<float>(),
+                         sin_t.data_ptr<float>(), block_tables.data_ptr<int32_t>(), (int)block_tables.size(1),
+                         q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), (int)qkv.size(0), (int)nq,
+                         (int)nkv, D, bs, code_of(qkv), cur()),
+     "rope_append_kv");
+}
+
+void py_silu_mul(torch::Tensor gu, torch::Tensor out) {
+  dense(gu, "gu");
+  dense(out, "out");
+  const c10::cuda::CUDAGuard g(gu.device());
+  ok(cob::silu_mul(gu.data_ptr(), out.data_ptr(), (int)gu.size(0), (int)out.size(1), code_of(gu), cur()),
+     "silu_mul");
+}
+
+void py_argmax_local(torch::Tensor logits, torch::Tensor words, int64_t vocab_offset) {
+  dense(logits, "logits");
+  dense(words, "words");
+  const c10::cuda::CUDAGuard g(logits.device());
+  ok(cob::argmax_local(logits.data_ptr(), reinterpret_cast<uint32_t*>(words.data_ptr()), (int)logits.size(0),
+                       (int)logits.size(1), (int)vocab_offset, code_of(logits), cur()),
+     "argmax_local");
+}
+
+void py_argmax_combine(torch::Tensor words, torch::Tensor ids, int64_t world) {
+  dense(words, "words");
+  dense(ids, "ids");
+  const c10::cuda::CUDAGuard g(words.device());
+  ok(cob::argmax_combine(reinterpret_cast<const uint32_t*>(words.data_ptr()), ids.data_ptr<int32_t>(),
+                         (int)ids.numel(), (int)world, cur()),
+     "argmax_combine");
+}
+
+int64_t py_attn_scratch_bytes(int64_t batch, int64_t nkv, int64_t splits, int64_t group, int64_t head_dim) {
+  return (int64_t)cob::attn_scratch_bytes((int)batch, (int)nkv, (int)splits, (int)group, (int)head_dim);
+}
+
+// scratch: uint8 tensor of at least attn_scratch_bytes; its counter part must be zero before the
+// first call (the kernel leaves it zero).
+void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                         torch::Tensor seq_lens, torch::Tensor out, torch::Tensor scratch, int64_t splits,
+                         int64_t pages_per_split, double scale) {
+  for (auto* t : {&q, &k_cache, &v_cache, &block_tables, &seq_lens, &out, &scratch}) dense(*t, "arg");
+  TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && seq_lens.scalar_type() == torch::kInt32,
+              "block_tables and seq_lens must be int32");
+  cob::AttnParams p = {};
+  p.batch = (int)q.size(0);
+  p.nq = (int)q.size(1);
+  p.head_dim = (int)q.size(2);
+  p.nkv = (int)k_cache.size(1);
+  p.block_size = (int)k_cache.size(2);
+  p.max_blocks_per_seq = (int)block_tables.size(1);
+  p.splits = (int)splits;
+  p.pages_per_split = (int)pages_per_split;
+  p.scale = (float)scale;
+  p.dtype = code_of(q);
+  const int group = p.nq / p.nkv;
+  const size_t need = cob::attn_scratch_bytes(p.batch, p.nkv, p.splits, group, p.head_dim);
+  TORCH_CHECK((size_t)scratch.numel() * scratch.element_size() >= need, "attention scratch too small: need ", need);
+  const size_t pairs = (size_t)p.batch * p.nkv;
+  char* base = reinterpret_cast<char*>(scratch.data_ptr());
+  p.part_o = reinterpret_cast<float*>(base);
+  p.part_ml = reinterpret_cast<float*>(base + pairs * p.splits * group * p.head_dim * sizeof(float));
+  p.counters = reinterpret_cast<int32_t*>(base + pairs * p.splits * group * p.head_dim * sizeof(float) +
+                                          pairs * p.splits * group * 2 * sizeof(float));
+  p.q = q.data_ptr();
+  p.k_cache = k_cache.data_ptr();
+  p.v_cache = v_cache.data_ptr();
+  p.block_tables = block_tables.data_ptr<int32_t>();
+  p.seq_lens = seq_lens.data_ptr<int32_t>();
+  p.out = out.data_ptr();
+  const c10::cuda::CUDAGuard g(q.device());
+  ok(cob::paged_decode_attention(p, cur()), "paged_decode_attention");
+}
+
+}  // namespace
+
+void register_ops(pybind11::module& m) {
+  m.def("rmsnorm", &py_rmsnorm);
+  m.def("add_rmsnorm", &py_add_rmsnorm);
+  m.def("embedding", &py_embedding);
+  m.def("rope_append_kv", &py_rope_append_kv);
+  m.def("silu_mul", &py_silu_mul);
+  m.def("argmax_local", &py_argmax_local);
+  m.def("argmax_combine", &py_argmax_combine);
+  m.def("attn_scratch_bytes", &py_attn_scratch_bytes);
+  m.def("decode_attention", &py_decode_attention);
+}

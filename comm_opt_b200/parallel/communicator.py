@@ -1,0 +1,223 @@
+"""Tensor-parallel communicator: the public entry point of the fused decode collective.
+
+    comm = TPCommunicator(group, device=dev, dtype=torch.bfloat16, max_rows=512, max_hidden=8192)
+    out, residual = comm.fused_allreduce_add_rmsnorm(x, residual, gamma, eps)
+
+`x` is this rank's partial sum (the row-parallel projection output), `residual` is replicated on
+every rank and updated in place to ``residual + sum_ranks(x)``; `out` is
+``RMSNorm(residual + sum_ranks(x)) * gamma`` on every rank. The call semantics follow the
+reference's fused op (exp/M17_epoch_ab/fused_ar_norm_nf.cu:203-206: x in symmetric memory,
+residual/gamma/out local), except that x may be any CUDA tensor and every rank receives the full
+new residual.
+
+One kernel per call; the ranks synchronise through the data itself (see csrc/fused_ar.cu), so the
+call needs no host barrier and can be captured in CUDA graphs of any grid size and replayed in any
+order. Every device-side wait is bounded; a timeout leaves an error word that `check()` turns into
+`TPCommTimeout`, after which `reset()` (collective) re-initialises the protocol state.
+
+Emulation: ``TPCommunicator(emulate_world=W, device=dev)`` runs all W ranks in one process on one
+GPU; inputs then carry a leading rank dimension ``[W, rows, hidden]`` and every call is a single
+kernel launch covering all ranks.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .._ext import native
+from .symm import DTYPE_CODE, HeapLayout, SymmetricHeap, plan_layout
+from .variant_table import NVLS_VARIANTS, VARIANT_NAMES, VARIANTS, Choice, VariantTable
+
+ERR_BITS = {
+    1: "timeout waiting for landing data",
+    2: "timeout in flag barrier",
+    4: "timeout in NVLS barrier",
+    8: "timeout waiting for a row partial",
+    16: "bad arguments",
+    32: "timeout in all-gather",
+    64: "timeout in grid barrier",
+}
+
+
+class TPCommError(RuntimeError):
+    pass
+
+
+class TPCommTimeout(TPCommError):
+    pass
+
+
+def default_timeout_ms() -> float:
+    return float(os.environ.get("COB_WAIT_TIMEOUT_MS", "1000"))
+
+
+class TPCommunicator:
+    def __init__(self, group=None, *, emulate_world: int | None = None, device=None, dtype=torch.bfloat16,
+                 max_rows: int = 512, max_hidden: int = 8192, max_gather: int = 4096,
+                 timeout_ms: float | None = None, pdl: bool = False, table: VariantTable | None = None,
+                 allow_nvls: bool = True):
+        import torch.distributed as dist
+
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.dtype = dtype
+        self.esize = torch.tensor([], dtype=dtype).element_size()
+        self.max_rows = max_rows
+        self.max_hidden = max_hidden
+        self.timeout_ns = int((timeout_ms if timeout_ms is not None else default_timeout_ms()) * 1e6)
+        self.pdl = pdl
+        self.table = table if table is not None else VariantTable.load()
+        self.group = group
+        self.emulated = emulate_world is not None
+        if self.emulated:
+            self.world, self.rank = int(emulate_world), 0
+        elif group is not None or (dist.is_available() and dist.is_initialized()):
+            self.group = group if group is not None else dist.group.WORLD
+            self.world, self.rank = dist.get_world_size(self.group), dist.get_rank(self.group)
+        else:
+            self.world, self.rank = 1, 0
+        self.heap: SymmetricHeap | None = None
+        self.layout: HeapLayout | None = None
+        if self.world > 1:
+            self.layout = plan_layout(self.world, max_rows, max_hidden, self.esize, max_gather)
+            if self.emulated:
+                self.heap = SymmetricHeap.emulated(self.world, self.layout, self.device)
+            else:
+                self.heap = SymmetricHeap.from_group(self.group, self.layout, self.device)
+            self._layout_list = self.layout.as_list()
+            self._init_state()
+        self.have_nvls = bool(self.heap and self.heap.mc and allow_nvls)
+        self.last_choice: Choice | None = None
+
+    # ------------------------------------------------------------------ state management
+    def _host_barrier(self):
+        if not self.emulated and self.world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(group=self.group, device_ids=[self.device.index]) if dist.get_backend(
+                self.group) == "nccl" else dist.barrier(group=self.group)
+
+    def _init_state(self):
+        with torch.cuda.device(self.device):
+            for h in self.heap.local_heaps():
+                native().init_heap(h, self._layout_list, DTYPE_CODE[self.dtype])
+            torch.cuda.synchronize(self.device)
+        self._host_barrier()
+
+    def reset(self):
+        """Collective: re-initialise flags, epochs and landing buffers on every rank (after an error)."""
+        if self.world == 1:
+            return
+        torch.cuda.synchronize(self.device)
+        self._host_barrier()
+        self._init_state()
+
+    def error_state(self) -> list[dict]:
+        """Synchronises and reads the error word of each local rank."""
+        if self.world == 1:
+            return []
+        torch.cuda.synchronize(self.device)
+        out = []
+        for r, h in enumerate(self.heap.local_heaps()):
+            w = self.heap.state_words(h).cpu().tolist()
+            err = (w[1] >> 32) & 0xFFFFFFFF
+            out.append(dict(rank=r if self.emulated else self.rank, epoch=w[0], error=err,
+                            detail=w[2:6], reasons=[m for b, m in ERR_BITS.items() if err & b]))
+        return out
+
+    def epochs(self) -> list[int]:
+        return [s["epoch"] for s in self.error_state()]
+
+    def check(self):
+        """Raise TPCommTimeout if any local rank recorded a bounded-wait timeout."""
+        for s in self.error_state():
+            if s["error"]:
+                raise TPCommTimeout(f"rank {s['rank']}: {', '.join(s['reasons'])} "
+                                    f"(detail {[hex(d) for d in s['detail']]}, epoch {s['epoch']}); "
+                                    "call reset() on every rank before reuse")
+
+    # ------------------------------------------------------------------ variant choice
+    def choose(self, rows: int, hidden: int, variant="auto", blocks=0, threads=0, cluster=0) -> Choice:
+        if variant in (None, "auto", 0):
+            c = self.table.lookup(self.world, self.dtype, self.esize, hidden, rows, self.have_nvls)
+            c = Choice(c.variant, blocks or c.blocks, threads or c.threads, cluster or c.cluster, c.p50_us)
+        else:
+            v = VARIANTS[variant] if isinstance(variant, str) else int(variant)
+            if v in NVLS_VARIANTS and not self.have_nvls:
+                raise TPCommError(f"{VARIANT_NAMES[v]} needs NVSwitch multicast, not available here")
+            c = Choice(v, blocks, threads, cluster)
+        return c
+
+    # ------------------------------------------------------------------ ops
+    def _shape(self, x: torch.Tensor) -> tuple[int, int]:
+        hidden = x.shape[-1]
+        if self.emulated:
+            assert x.shape[0] == self.world, "emulated inputs are [world, rows, hidden]"
+            rows = x[0].numel() // hidden
+        else:
+            rows = x.numel() // hidden
+        if rows > self.max_rows or hidden > self.max_hidden:
+            raise TPCommError(f"[{rows}, {hidden}] exceeds the communicator capacity "
+                              f"[{self.max_rows}, {self.max_hidden}]")
+        return rows, hidden
+
+    def _launch(self, x, residual, gamma, out, eps, norm, variant, blocks, threads, cluster, dry_run=False):
+        rows, hidden = self._shape(x)
+        if x.dtype != self.dtype:
+            raise TPCommError(f"communicator dtype is {self.dtype}, got {x.dtype}")
+        c = self.choose(rows, hidden, variant, blocks, threads, cluster)
+        stride = rows * hidden if self.emulated else 0
+        with torch.cuda.device(self.device):
+            rc, v, b, t, cl = native().fused_ar(
+                self.heap.bases, self.heap.mc, self._layout_list, x, residual if norm else x,
+                gamma if norm else x, out, self.rank, rows, hidden, float(eps), c.variant, c.blocks, c.threads,
+                c.cluster, int(self.emulated), int(self.pdl), int(norm), self.timeout_ns, stride, stride, stride,
+                dry_run)
+        if rc != 0:
+            raise TPCommError(f"fused_ar: unsupported configuration {VARIANT_NAMES.get(v, v)} rows={rows} "
+                              f"hidden={hidden} world={self.world} blocks={b} threads={t} cluster={cl} "
+                              f"(cuda status {rc})")
+        self.last_choice = Choice(v, b, t, cl, c.p50_us)
+        return self.last_choice
+
+    def fused_allreduce_add_rmsnorm(self, x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor,
+                                    eps: float = 1e-6, out: torch.Tensor | None = None, variant="auto",
+                                    blocks: int = 0, threads: int = 0, cluster: int = 0):
+        """Returns (out, residual); residual is updated in place."""
+        if out is None:
+            out = torch.empty_like(x)
+        if self.world == 1:
+            native().add_rmsnorm(x, residual, gamma, out, float(eps))
+            return out, residual
+        self._launch(x, residual, gamma, out, eps, 1, variant, blocks, threads, cluster)
+        return out, residual
+
+    def all_reduce(self, x: torch.Tensor, out: torch.Tensor | None = None, variant="auto", blocks: int = 0,
+                   threads: int = 0, cluster: int = 0) -> torch.Tensor:
+        """Plain sum over ranks (same kernels with the residual/norm epilogue switched off)."""
+        if out is None:
+            out = torch.empty_like(x)
+        if self.world == 1:
+            out.copy_(x)
+            return out
+        self._launch(x, None, None, out, 0.0, 0, variant, blocks, threads, cluster)
+        return out
+
+    def all_gather_u32(self, inp: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Gather a small int32/uint32/float32 vector from every rank: out [world, n]."""
+        n = inp.shape[-1]
+        if out is None:
+            out = torch.empty((self.world, n) if not self.emulated else (self.world, self.world, n),
+                              dtype=inp.dtype, device=inp.device)
+        if self.world == 1:
+            out.view(-1).copy_(inp.view(-1))
+            return out
+        with torch.cuda.device(self.device):
+            native().allgather_u32(self.heap.bases, self._layout_list, inp, out, self.rank, n, int(self.emulated),
+                                   self.timeout_ns, n if self.emulated else 0, self.world * n if self.emulated else 0)
+        return out
+
+    def describe(self) -> dict:
+        return dict(world=self.world, rank=self.rank, emulated=self.emulated, dtype=str(self.dtype),
+                    max_rows=self.max_rows, max_hidden=self.max_hidden, nvls=self.have_nvls,
+                    heap_bytes=self.layout.total if self.layout else 0, timeout_ms=self.timeout_ns / 1e6)

@@ -1,0 +1,226 @@
+"""Host-side model checker of the cross-GPU synchronisation protocol of csrc/fused_ar.cu.
+
+The reference argued the correctness of its barrier-free all-gather in prose
+(docs/method_design.md:37-67: Q1 arrival via flag, Q2 no overwrite by epoch parity, Q3 stale data
+rejected by epoch) and tested it with one interleaving test (exp/M16_epoch_fix/test_interleave.py).
+Here the protocol itself is executed step by step by simulated ranks under random and adversarial
+schedules, with the invariants checked on every memory operation:
+
+* a sender never overwrites a landing cell that still holds unconsumed data (no lost update),
+* a receiver only accepts data of its own call (no stale read),
+* a staged input is never overwritten while a peer may still read it for an older call,
+* every rank finishes every call (no deadlock), with different grid sizes per call and any mix of
+  variants (one CUDA graph per batch size, replayed in any order).
+
+Each simulated memory cell stores (epoch, payload) or FILL, standing for the Lamport -0 sentinel.
+The unit of interleaving is one memory operation; blocks of one rank are modelled for the
+barrier-based variants because their barriers are per block.
+"""
+from __future__ import annotations
+
+import random
+from dataclasses import dataclass, field
+
+FILL = None
+
+L1S, L2S, P1S, P2S = 1, 2, 5, 6
+
+
+class ProtocolViolation(AssertionError):
+    pass
+
+
+@dataclass
+class Call:
+    variant: int
+    blocks: int
+    rows: int
+
+
+@dataclass
+class Memory:
+    world: int
+    nslots: int = 2  # landing slots by epoch parity (1 = a deliberately broken protocol)
+    land1: dict = field(default_factory=dict)   # (owner, slot, src, row) -> (epoch, value) | FILL
+    rs: dict = field(default_factory=dict)      # (owner, slot, src, row)
+    ag: dict = field(default_factory=dict)      # (owner, slot, src, row)
+    agp: dict = field(default_factory=dict)     # (owner, slot, src, row) -> epoch tag (never cleared)
+    stage: dict = field(default_factory=dict)   # (owner, parity, row) -> epoch
+    flags: dict = field(default_factory=dict)   # (owner, block, src) -> count
+
+
+def value(rank: int, epoch: int, row: int) -> int:
+    """Distinct payload per (sender, call, row): a stale or foreign value never matches."""
+    return (epoch * 1000003 + rank * 7919 + row) & 0xFFFFFFFF
+
+
+class Rank:
+    """One simulated GPU: a generator of steps; a step returns False while it must wait."""
+
+    def __init__(self, rank: int, mem: Memory, calls: list[Call], seed: int = 0):
+        self.rank, self.mem, self.calls = rank, mem, calls
+        self.rng = random.Random(seed * 131 + rank)
+        self.epoch = 0
+        self.flag_calls: dict[int, int] = {}
+        self.done = False
+        self.gen = self._run()
+        self.results: list[dict] = []
+
+    # ---- helpers -------------------------------------------------------------------------
+    def _put(self, table: dict, key, val):
+        if table.get(key, FILL) is not FILL:
+            raise ProtocolViolation(f"rank {self.rank} overwrites unconsumed cell {key}: {table[key]}")
+        table[key] = val
+
+    def _take(self, table: dict, key, epoch: int):
+        v = table.get(key, FILL)
+        if v is FILL:
+            return None
+        if v[0] != epoch:
+            raise ProtocolViolation(f"rank {self.rank} call {epoch} reads stale cell {key}: {v}")
+        table[key] = FILL
+        return v
+
+    # ---- the protocol ---------------------------------------------------------------------
+    def _run(self):
+        for call in self.calls:
+            e = self.epoch + 1  # every block reads the same epoch; the last block advances it
+            got: dict = {}
+            blocks = [self._block(call, e, b, got) for b in range(call.blocks)]
+            live = list(blocks)
+            while live:
+                g = self.rng.choice(live)
+                try:
+                    yield next(g)
+                except StopIteration:
+                    live.remove(g)
+            expect = call.rows * self.mem.world
+            if len(got) != expect:
+                raise ProtocolViolation(f"rank {self.rank} call {e}: {len(got)} of {expect} row pieces")
+            for (src, row), v in got.items():
+                if v != value(src, e, row):
+                    raise ProtocolViolation(f"rank {self.rank} call {e}: wrong payload from {src} row {row}")
+            self.results.append(dict(epoch=e, n=len(got)))
+            self.epoch = e
+            yield True
+        self.done = True
+
+    def _block(self, call: Call, e: int, b: int, got: dict):
+        """One CTA of this rank: rows b, b + blocks, ... (all phases use the same rows)."""
+        W = self.mem.world
+        slot = e % self.mem.nslots
+        rows = range(b, call.rows, call.blocks)
+        if call.variant == L1S:
+            for row in rows:
+                for i in range(1, W):
+                    self._put(self.mem.land1, ((self.rank + i) % W, slot, self.rank, row),
+                              (e, value(self.rank, e, row)))
+                    yield True
+            for row in rows:
+                for src in range(W):
+                    if src == self.rank:
+                        got[(src, row)] = value(src, e, row)
+                        continue
+                    while (v := self._take(self.mem.land1, (self.rank, slot, src, row), e)) is None:
+                        yield False
+                    got[(src, row)] = v[1]
+                    yield True
+        elif call.variant in (L2S, P2S):
+            if call.variant == L2S:
+                for row in rows:
+                    for dst in range(W):
+                        if dst != self.rank:
+                            self._put(self.mem.rs, (dst, slot, self.rank, row), (e, value(self.rank, e, row)))
+                            yield True
+            else:
+                yield from self._stage_and_barrier(e, b, rows)
+            for row in rows:
+                for src in range(W):
+                    if src == self.rank:
+                        continue
+                    if call.variant == L2S:
+                        while self._take(self.mem.rs, (self.rank, slot, src, row), e) is None:
+                            yield False
+                    else:
+                        self._read_stage(src, e, row)
+                    yield True
+                for dst in range(W):
+                    self._put(self.mem.ag, (dst, slot, self.rank, row), (e, value(self.rank, e, row)))
+                    self.mem.agp[(dst, slot, self.rank, row)] = e
+                    yield True
+            for row in rows:
+                for src in range(W):
+                    while (v := self._take(self.mem.ag, (self.rank, slot, src, row), e)) is None:
+                        yield False
+                    while self.mem.agp.get((self.rank, slot, src, row)) != e:
+                        yield False
+                    got[(src, row)] = v[1]
+                    yield True
+        elif call.variant == P1S:
+            yield from self._stage_and_barrier(e, b, rows)
+            for row in rows:
+                for src in range(W):
+                    self._read_stage(src, e, row)
+                    got[(src, row)] = value(src, e, row)
+                    yield True
+        else:
+            raise ValueError(call.variant)
+
+    def _stage_and_barrier(self, e: int, b: int, rows):
+        """Copy this block's rows into stage[parity], then block b's flag barrier."""
+        W = self.mem.world
+        for row in rows:
+            self.mem.stage[(self.rank, e % self.mem.nslots, row)] = e
+            yield True
+        bc = self.flag_calls.get(b, 0) + 1
+        self.flag_calls[b] = bc
+        for peer in range(W):
+            self.mem.flags[(peer, b, self.rank)] = bc
+            yield True
+        for peer in range(W):
+            while self.mem.flags.get((self.rank, b, peer), 0) < bc:
+                yield False
+
+    def _read_stage(self, src: int, e: int, row: int):
+        got = self.mem.stage.get((src, e % self.mem.nslots, row))
+        if got != e:
+            raise ProtocolViolation(f"rank {self.rank} call {e} reads stage of {src} row {row} holding call {got}")
+
+    def step(self) -> bool:
+        if self.done:
+            return False
+        try:
+            return next(self.gen)
+        except StopIteration:
+            self.done = True
+            return True
+
+
+def simulate(world: int, calls: list[Call], seed: int = 0, max_steps: int = 2_000_000,
+             slow_rank: int | None = None, slow_factor: int = 20, nslots: int = 2) -> dict:
+    """Run all ranks under a random schedule. `slow_rank` is scheduled `slow_factor` times less often."""
+    mem = Memory(world, nslots)
+    ranks = [Rank(r, mem, calls, seed) for r in range(world)]
+    rng = random.Random(seed)
+    weights = [1.0 if r != slow_rank else 1.0 / slow_factor for r in range(world)]
+    steps = 0
+    idle = 0
+    while not all(r.done for r in ranks):
+        live = [r for r in ranks if not r.done]
+        r = rng.choices(live, weights=[weights[x.rank] for x in live])[0]
+        progressed = r.step()
+        idle = 0 if progressed else idle + 1
+        steps += 1
+        if idle > 50 * world * world + 1000:
+            raise ProtocolViolation(f"deadlock: epochs {[x.epoch for x in ranks]}")
+        if steps > max_steps:
+            raise ProtocolViolation("step budget exhausted")
+    leftovers = [k for t in (mem.land1, mem.rs, mem.ag) for k, v in t.items() if v is not FILL]
+    if leftovers:
+        raise ProtocolViolation(f"landing cells not restored to the sentinel: {leftovers[:4]}")
+    return dict(steps=steps, epochs=[r.epoch for r in ranks])
+
+
+def random_calls(n: int, seed: int, variants=(L1S, L2S, P1S, P2S), rows=(1, 3, 8), blocks=(1, 2, 4)) -> list[Call]:
+    rng = random.Random(seed)
+    return [Call(rng.choice(variants), rng.choice(blocks), rng.choice(rows)) for _ in range(n)]

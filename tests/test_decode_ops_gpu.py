@@ -1,0 +1,94 @@
+"""Numerics of the single-GPU decode kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+
+from comm_opt_b200.ops import kernels as K
+from comm_opt_b200.ops.reference import paged_attention_ref, rel_err, rmsnorm_ref, rope_ref, rope_tables, silu_mul_ref
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.bfloat16, torch.float16, torch.float32]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("rows,hidden", [(1, 8192), (7, 4096), (64, 5120), (3, 16384)])
+def test_rmsnorm_and_add(cuda, dtype, rows, hidden):
+    x = torch.randn(rows, hidden, device=cuda).to(dtype)
+    r0 = torch.randn(rows, hidden, device=cuda).to(dtype)
+    g = (1 + 0.1 * torch.randn(hidden, device=cuda)).to(dtype)
+    tol = 1e-5 if dtype == torch.float32 else 2 ** -7
+    assert rel_err(K.rmsnorm(x, g, 1e-5), rmsnorm_ref(x, g, 1e-5)) <= tol
+    res = r0.clone()
+    out = K.add_rmsnorm(x, res, g, 1e-5)
+    h = (x.float() + r0.float())
+    assert rel_err(res, h) <= tol
+    assert rel_err(out, rmsnorm_ref(res.float(), g, 1e-5)) <= tol
+
+
+def test_embedding(cuda):
+    table = torch.randn(1000, 4096, device=cuda).to(torch.bfloat16)
+    ids = torch.tensor([0, 999, 5, 5, 123], device=cuda, dtype=torch.int32)
+    assert torch.equal(K.embedding(ids, table), table[ids.long()])
+
+
+@pytest.mark.parametrize("nq,nkv", [(8, 1), (32, 8), (4, 4)])
+def test_rope_append_kv(cuda, nq, nkv):
+    B, D, bs, maxb = 5, 128, 16, 8
+    dtype = torch.bfloat16
+    cos, sin = rope_tables(maxb * bs, D, 500000.0, cuda)
+    qkv = torch.randn(B, (nq + 2 * nkv) * D, device=cuda).to(dtype)
+    pos = torch.tensor([0, 17, 33, 127, 64], device=cuda, dtype=torch.int32)
+    bt = torch.randperm(B * maxb, device=cuda).to(torch.int32).view(B, maxb)
+    kc = torch.zeros(B * maxb, nkv, bs, D, device=cuda, dtype=dtype)
+    vc = torch.zeros_like(kc)
+    q = torch.empty(B, nq, D, device=cuda, dtype=dtype)
+    K.rope_append_kv(qkv, pos, cos, sin, bt, q, kc, vc, nq, nkv)
+    heads = qkv.view(B, nq + 2 * nkv, D)
+    assert rel_err(q, rope_ref(heads[:, :nq], pos, cos, sin)) <= 2 ** -7
+    kref = rope_ref(heads[:, nq:nq + nkv], pos, cos, sin)
+    for b in range(B):
+        p = int(pos[b])
+        blk = int(bt[b, p // bs])
+        assert rel_err(kc[blk, :, p % bs], kref[b]) <= 2 ** -7
+        assert torch.equal(vc[blk, :, p % bs], heads[b, nq + nkv:])
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_silu_mul(cuda, dtype):
+    gu = torch.randn(9, 2 * 3584, device=cuda).to(dtype)
+    tol = 1e-5 if dtype == torch.float32 else 2 ** -7
+    assert rel_err(K.silu_mul(gu), silu_mul_ref(gu)) <= tol
+
+
+def test_argmax_local_and_combine(cuda):
+    V, world, rows = 16032, 4, 6
+    logits = torch.randn(world, rows, V, device=cuda).to(torch.bfloat16)
+    logits[2, 3, 77] = 100.0  # unique max on rank 2
+    words = torch.stack([K.argmax_local(logits[r], r * V) for r in range(world)])
+    ids = K.argmax_combine(words.contiguous(), world)
+    ref = torch.cat(list(logits), dim=-1).float().argmax(-1)
+    assert torch.equal(ids.long(), ref)
+    assert int(ids[3]) == 2 * V + 77
+
+
+@pytest.mark.parametrize("nq,nkv", [(8, 1), (32, 8), (16, 4)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_attention(cuda, nq, nkv, dtype):
+    B, D, bs, maxb = 6, 128, 16, 40
+    seq = torch.tensor([1, 15, 16, 17, 300, 640], device=cuda, dtype=torch.int32)
+    nblocks = B * maxb
+    kc = torch.randn(nblocks, nkv, bs, D, device=cuda).to(dtype)
+    vc = torch.randn(nblocks, nkv, bs, D, device=cuda).to(dtype)
+    bt = torch.randperm(nblocks, device=cuda).to(torch.int32).view(B, maxb)
+    q = torch.randn(B, nq, D, device=cuda).to(dtype)
+    scale = 1 / math.sqrt(D)
+    ref = paged_attention_ref(q, kc, vc, bt, seq, scale)
+    for num_sms in (148, 1):  # many splits (in-kernel combine) and a single split
+        attn = K.DecodeAttention(B, nq, nkv, D, maxb, cuda, num_sms=num_sms)
+        out = torch.empty_like(q)
+        for _ in range(2):  # second call checks the split counters were reset
+            attn(q, kc, vc, bt, seq, out, scale)
+            torch.cuda.synchronize()
+            assert rel_err(out, ref) <= 2 ** -7, (num_sms, rel_err(out, ref))

@@ -1,0 +1,35 @@
+"""Host-side model checking of the synchronisation protocol (no GPU)."""
+import pytest
+
+from comm_opt_b200.parallel.protocol_sim import (L1S, L2S, P1S, P2S, Call, ProtocolViolation, random_calls,
+                                                 simulate)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_random_interleavings(world):
+    for seed in range(4):
+        res = simulate(world, random_calls(24, seed + 10 * world), seed=seed)
+        assert res["epochs"] == [24] * world
+
+
+@pytest.mark.parametrize("variant", [L1S, L2S, P1S, P2S])
+def test_slow_rank_each_variant(variant):
+    calls = [Call(variant, b, t) for b, t in [(1, 1), (4, 8), (2, 3), (8, 8), (1, 5)] * 3]
+    for slow in range(4):
+        simulate(4, calls, seed=slow, slow_rank=slow, slow_factor=50)
+
+
+def test_mixed_grids_like_graph_per_batch():
+    # one CUDA graph per batch size, replayed in random order: grid sizes differ call to call
+    calls = random_calls(40, 3, rows=(1, 2, 8, 13), blocks=(1, 3, 8))
+    simulate(8, calls, seed=5, slow_rank=7)
+
+
+def test_checker_detects_single_slot_protocol():
+    caught = 0
+    for seed in range(6):
+        try:
+            simulate(4, random_calls(20, seed), seed=seed, slow_rank=1, nslots=1)
+        except ProtocolViolation:
+            caught += 1
+    assert caught == 6
