@@ -177,10 +177,13 @@ __global__ void __launch_bounds__(1024) k_argmax_local(const T* __restrict__ log
 }
 
 __global__ void k_argmax_combine(const uint32_t* __restrict__ words, int32_t* __restrict__ ids, int rows,
-                                 int world) {
+                                 int world, int32_t* __restrict__ positions, int32_t* __restrict__ seq_lens) {
   pdl_wait();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
+  // decode feedback: the token just produced sits at the next position
+  if (positions) positions[row] += 1;
+  if (seq_lens) seq_lens[row] += 1;
   float best = -FLT_MAX;
   int bi = 0x7fffffff;
   for (int r = 0; r < world; ++r) {
@@ -282,9 +285,10 @@ cudaError_t argmax_local(const void* logits, uint32_t* words, int rows, int voca
   });
 }
 
-cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, cudaStream_t s) {
+cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, int32_t* positions,
+                           int32_t* seq_lens, cudaStream_t s) {
   if (rows <= 0 || world <= 0) return cudaErrorInvalidValue;
-  k_argmax_combine<<<(rows + 127) / 128, 128, 0, s>>>(words, ids, rows, world);
+  k_argmax_combine<<<(rows + 127) / 128, 128, 0, s>>>(words, ids, rows, world, positions, seq_lens);
   return cudaGetLastError();
 }
 

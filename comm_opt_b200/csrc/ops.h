@@ -27,8 +27,10 @@ cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, 
 // Per row: (max value as f32 bits, vocab_offset + argmax) -> words[row*2 + {0,1}]
 cudaError_t argmax_local(const void* logits, uint32_t* words, int rows, int vocab, int vocab_offset, int dtype,
                          cudaStream_t s);
-// words: [world, rows, 2] gathered from every rank -> ids[row] (ties: lowest index)
-cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, cudaStream_t s);
+// words: [world, rows, 2] gathered from every rank -> ids[row] (ties: lowest index); when given,
+// positions[row] and seq_lens[row] are incremented (decode-step feedback inside a CUDA graph)
+cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, int32_t* positions,
+                           int32_t* seq_lens, cudaStream_t s);
 
 // Paged GQA decode attention (split-KV with in-kernel combine by the last split).
 struct AttnParams {

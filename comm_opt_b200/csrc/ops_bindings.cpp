@@ -3,6 +3,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "gemm.h"
 #include "ops.h"
 #include "types.h"
 
@@ -93,12 +94,23 @@ void py_argmax_local(torch::Tensor logits, torch::Tensor words, int64_t vocab_of
      "argmax_local");
 }
 
-void py_argmax_combine(torch::Tensor words, torch::Tensor ids, int64_t world) {
+void py_argmax_combine(torch::Tensor words, torch::Tensor ids, int64_t world, c10::optional<torch::Tensor> positions,
+                       c10::optional<torch::Tensor> seq_lens) {
   dense(words, "words");
   dense(ids, "ids");
+  int32_t* pos = nullptr;
+  int32_t* lens = nullptr;
+  if (positions.has_value()) {
+    TORCH_CHECK(positions->scalar_type() == torch::kInt32 && positions->numel() == ids.numel(), "positions");
+    pos = positions->data_ptr<int32_t>();
+  }
+  if (seq_lens.has_value()) {
+    TORCH_CHECK(seq_lens->scalar_type() == torch::kInt32 && seq_lens->numel() == ids.numel(), "seq_lens");
+    lens = seq_lens->data_ptr<int32_t>();
+  }
   const c10::cuda::CUDAGuard g(words.device());
   ok(cob::argmax_combine(reinterpret_cast<const uint32_t*>(words.data_ptr()), ids.data_ptr<int32_t>(),
-                         (int)ids.numel(), (int)world, cur()),
+                         (int)ids.numel(), (int)world, pos, lens, cur()),
      "argmax_combine");
 }
 
@@ -144,16 +156,46 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
   ok(cob::paged_decode_attention(p, cur()), "paged_decode_attention");
 }
 
+// y = x @ w^T on the tcgen05 tensor cores. Returns {bn, tiles, splits, kps}.
+std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor err, int64_t splits,
+                             bool pdl, int64_t timeout_ns) {
+  dense(x, "x");
+  dense(w, "w");
+  dense(err, "err");
+  TORCH_CHECK(y.is_cuda() && y.stride(-1) == 1, "y must be row-major");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
+  TORCH_CHECK(y.size(0) == x.size(0) && y.size(1) == w.size(0), "y must be [M, N]");
+  TORCH_CHECK(x.scalar_type() == w.scalar_type() && y.scalar_type() == x.scalar_type(), "dtypes must match");
+  TORCH_CHECK(err.scalar_type() == torch::kInt32, "err must be int32");
+  const c10::cuda::CUDAGuard g(x.device());
+  static int sms = 0;
+  if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
+  cob::GemmPlan p;
+  ok(cob::gemm_decode(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)w.size(0), (int)x.size(1),
+                      (int)y.stride(0), code_of(x), err.data_ptr<int32_t>(), sms, (int)splits, pdl,
+                      (unsigned long long)timeout_ns, cur(), &p),
+     "gemm_decode");
+  return {p.bn, p.tiles, p.splits, p.kps};
+}
+
+std::vector<int64_t> py_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, int64_t splits) {
+  const cob::GemmPlan p = cob::plan_gemm((int)M, (int)N, (int)K, (int)sms, (int)splits);
+  return {p.bn, p.tiles, p.splits, p.kps};
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
+  m.def("gemm", &py_gemm);
+  m.def("gemm_plan", &py_gemm_plan);
   m.def("rmsnorm", &py_rmsnorm);
   m.def("add_rmsnorm", &py_add_rmsnorm);
   m.def("embedding", &py_embedding);
   m.def("rope_append_kv", &py_rope_append_kv);
   m.def("silu_mul", &py_silu_mul);
   m.def("argmax_local", &py_argmax_local);
-  m.def("argmax_combine", &py_argmax_combine);
+  m.def("argmax_combine", &py_argmax_combine, pybind11::arg("words"), pybind11::arg("ids"),
+        pybind11::arg("world"), pybind11::arg("positions") = pybind11::none(), pybind11::arg("seq_lens") = pybind11::none());
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);
   m.def("decode_attention", &py_decode_attention);
 }

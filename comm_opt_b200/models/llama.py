@@ -1,0 +1,406 @@
+"""Llama-shaped tensor-parallel decoder for decode-time measurement (TP = 1/2/4/8).
+
+The reference measured the share of communication in TP=8 decode through vLLM
+(exp/M5_e2e_comm_share/infer.py:37-88) and never replaced vLLM's kernels; this runner is the
+framework layer that puts the fused collective where it belongs: both row-parallel outputs of
+every layer (o_proj and down_proj, the two all-reduce points of exp/M5_e2e_comm_share/README.md:111)
+go through ``TPCommunicator.fused_allreduce_add_rmsnorm``, which also performs the residual add
+and the following RMSNorm. Everything in the decode step is one of this package's kernels:
+embedding, RMSNorm, the projection GEMMs, RoPE + paged-KV append, paged GQA decode attention,
+SiLU*mul, the fused collective, and a distributed greedy argmax; one step is captured in a CUDA
+graph per batch size.
+
+Sharding (Megatron style): QKV and gate/up are column-parallel, o_proj and down_proj are
+row-parallel, the LM head is vocab-parallel, the embedding table is replicated (2.1 GB at vocab
+128256 x 8192 bf16 - cheap on a 180 GB part and saves a collective per step).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, replace
+
+import torch
+import torch.nn.functional as F
+
+from ..ops import kernels as K
+from ..ops.reference import rope_tables
+from ..parallel.communicator import TPCommunicator
+from .gemm import Linear
+
+
+@dataclass(frozen=True)
+class LlamaConfig:
+    name: str
+    hidden: int
+    layers: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    inter: int
+    vocab: int
+    eps: float = 1e-5
+    rope_theta: float = 500000.0
+
+    def shard(self, tp: int) -> dict:
+        assert self.heads % tp == 0 and self.kv_heads % tp == 0 and self.inter % tp == 0 and self.vocab % tp == 0, \
+            f"{self.name} does not shard {tp} ways"
+        return dict(nq=self.heads // tp, nkv=self.kv_heads // tp, inter=self.inter // tp, vocab=self.vocab // tp)
+
+    @property
+    def params(self) -> int:
+        H, D = self.hidden, self.head_dim
+        per_layer = H * (self.heads + 2 * self.kv_heads) * D + self.heads * D * H + 3 * H * self.inter + 2 * H
+        return self.layers * per_layer + 2 * self.vocab * H + H
+
+
+LLAMA3_8B = LlamaConfig("llama3-8b", 4096, 32, 32, 8, 128, 14336, 128256)
+LLAMA3_70B = LlamaConfig("llama3-70b", 8192, 80, 64, 8, 128, 28672, 128256)
+TINY = LlamaConfig("tiny", 1024, 2, 16, 8, 128, 2048, 4096)
+PRESETS = {"llama3-8b": LLAMA3_8B, "8b": LLAMA3_8B, "llama3-70b": LLAMA3_70B, "70b": LLAMA3_70B, "tiny": TINY}
+
+
+class LayerWeights:
+    def __init__(self, wqkv, wo, wgu, wdown, ln1, ln2):
+        self.wqkv, self.wo, self.wgu, self.wdown, self.ln1, self.ln2 = wqkv, wo, wgu, wdown, ln1, ln2
+
+
+class LlamaWeights:
+    """This rank's shards. Weight matrices are [out_features, in_features] (K-major)."""
+
+    def __init__(self, cfg: LlamaConfig, tp_rank: int, tp: int, device, dtype=torch.bfloat16, seed: int = 0,
+                 std: float = 0.02, full: dict | None = None):
+        self.cfg, self.tp_rank, self.tp, self.dtype = cfg, tp_rank, tp, dtype
+        s = cfg.shard(tp)
+        H, D = cfg.hidden, cfg.head_dim
+        gen = torch.Generator(device=device)
+
+        def rnd(shape, key):
+            gen.manual_seed(seed * 1_000_003 + key * 8 + tp_rank)
+            return torch.empty(shape, dtype=dtype, device=device).normal_(0.0, std, generator=gen)
+
+        def norm_w(key):
+            gen.manual_seed(seed * 1_000_003 + key)
+            return (1.0 + 0.1 * torch.randn(H, device=device, generator=gen)).to(dtype)
+
+        if full is not None:  # slices of one full model (tests: TP result == TP1 result)
+            self.embed = full["embed"].to(device)
+            self.final_norm = full["final_norm"].to(device)
+            self.lm_head = full["lm_head"].chunk(tp, 0)[tp_rank].contiguous().to(device)
+            self.layers = []
+            for L in full["layers"]:
+                q, k, v = L["wqkv"].split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], 0)
+                wqkv = torch.cat([q.chunk(tp, 0)[tp_rank], k.chunk(tp, 0)[tp_rank], v.chunk(tp, 0)[tp_rank]], 0)
+                g, u = L["wgu"].chunk(2, 0)
+                wgu = torch.cat([g.chunk(tp, 0)[tp_rank], u.chunk(tp, 0)[tp_rank]], 0)
+                self.layers.append(LayerWeights(
+                    wqkv.contiguous().to(device), L["wo"].chunk(tp, 1)[tp_rank].contiguous().to(device),
+                    wgu.contiguous().to(device), L["wdown"].chunk(tp, 1)[tp_rank].contiguous().to(device),
+                    L["ln1"].to(device), L["ln2"].to(device)))
+            return
+        gen.manual_seed(seed * 1_000_003 + 1)  # replicated tensors: same seed on every rank
+        self.embed = torch.empty(cfg.vocab, H, dtype=dtype, device=device).normal_(0.0, 1.0, generator=gen)
+        self.final_norm = norm_w(2)
+        self.lm_head = rnd((s["vocab"], H), 3)
+        self.layers = []
+        for i in range(cfg.layers):
+            k0 = 16 + 8 * i
+            self.layers.append(LayerWeights(
+                rnd(((s["nq"] + 2 * s["nkv"]) * D, H), k0), rnd((H, s["nq"] * D), k0 + 1),
+                rnd((2 * s["inter"], H), k0 + 2), rnd((H, s["inter"]), k0 + 3), norm_w(k0 + 4), norm_w(k0 + 5)))
+
+    @staticmethod
+    def full_random(cfg: LlamaConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0, std: float = 0.02) -> dict:
+        """Unsharded weights (small configs only), to be sliced by every rank."""
+        g = torch.Generator(device=device).manual_seed(seed)
+        H, D = cfg.hidden, cfg.head_dim
+
+        def rnd(*shape, scale=std):
+            return (scale * torch.randn(*shape, generator=g, device=device)).to(dtype)
+
+        def nw():
+            return (1.0 + 0.1 * torch.randn(H, generator=g, device=device)).to(dtype)
+
+        layers = [dict(wqkv=rnd((cfg.heads + 2 * cfg.kv_heads) * D, H), wo=rnd(H, cfg.heads * D),
+                       wgu=rnd(2 * cfg.inter, H), wdown=rnd(H, cfg.inter), ln1=nw(), ln2=nw())
+                  for _ in range(cfg.layers)]
+        return dict(embed=rnd(cfg.vocab, H, scale=1.0), final_norm=nw(), lm_head=rnd(cfg.vocab, H), layers=layers)
+
+
+class BlockAllocator:
+    """Free list of 16-token KV pages shared by all layers (same page id in every layer)."""
+
+    def __init__(self, num_blocks: int):
+        self.free = list(range(num_blocks - 1, -1, -1))
+
+    def alloc(self, n: int) -> list[int]:
+        if n > len(self.free):
+            raise RuntimeError(f"KV cache exhausted: need {n} pages, {len(self.free)} free")
+        return [self.free.pop() for _ in range(n)]
+
+    def release(self, pages: list[int]):
+        self.free.extend(reversed(pages))
+
+
+class PagedKVCache:
+    BLOCK = 16
+
+    def __init__(self, cfg: LlamaConfig, tp: int, max_batch: int, max_seq: int, device, dtype=torch.bfloat16,
+                 extra_blocks: int = 0):
+        s = cfg.shard(tp)
+        self.max_blocks_per_seq = (max_seq + self.BLOCK - 1) // self.BLOCK
+        self.num_blocks = max_batch * self.max_blocks_per_seq + extra_blocks
+        shape = (self.num_blocks, s["nkv"], self.BLOCK, cfg.head_dim)
+        self.k = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(cfg.layers)]
+        self.v = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(cfg.layers)]
+        self.alloc = BlockAllocator(self.num_blocks)
+        self.block_tables = torch.zeros(max_batch, self.max_blocks_per_seq, dtype=torch.int32, device=device)
+        self.pages: list[list[int]] = [[] for _ in range(max_batch)]
+
+    def reserve(self, batch: int, seq: int):
+        """Give sequences 0..batch-1 pages for `seq` tokens (shuffled pages: the indirection is real)."""
+        nb = (seq + self.BLOCK - 1) // self.BLOCK
+        assert nb <= self.max_blocks_per_seq
+        for b in range(batch):
+            if len(self.pages[b]) < nb:
+                self.pages[b] += self.alloc.alloc(nb - len(self.pages[b]))
+        rows = torch.tensor([p + [0] * (self.max_blocks_per_seq - len(p)) for p in self.pages[:batch]],
+                            dtype=torch.int32)
+        self.block_tables[:batch].copy_(rows)
+
+    @property
+    def bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.k + self.v)
+
+
+class TPDecodeRunner:
+    """Greedy TP decoding: torch prefill, then graph-captured decode steps built from our kernels."""
+
+    def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
+                 device, gemm: str = "cob", nccl_group=None):
+        self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
+        self.tp, self.rank = comm.world, comm.rank
+        self.s = cfg.shard(self.tp)
+        self.max_batch, self.max_seq = max_batch, max_seq
+        self.dtype = weights.dtype
+        self.nccl_group = nccl_group
+        self.cache = PagedKVCache(cfg, self.tp, max_batch, max_seq, self.device, self.dtype)
+        self.cos, self.sin = rope_tables(max_seq, cfg.head_dim, cfg.rope_theta, self.device)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.gemm = gemm
+        self.lin = {}
+        for i, L in enumerate(weights.layers):
+            self.lin[(i, "qkv")] = Linear(L.wqkv, gemm)
+            self.lin[(i, "o")] = Linear(L.wo, gemm)
+            self.lin[(i, "gu")] = Linear(L.wgu, gemm)
+            self.lin[(i, "down")] = Linear(L.wdown, gemm)
+        self.lin["head"] = Linear(weights.lm_head, gemm)
+        self.graphs: dict[int, tuple] = {}
+        self.kernels_per_step: dict[int, int] = {}
+
+    # ------------------------------------------------------------------ prefill (plain torch)
+    def _ar(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(x, group=self.nccl_group)
+        return x
+
+    @torch.no_grad()
+    def prefill(self, prompts: torch.Tensor, chunk_tokens: int = 4096) -> torch.Tensor:
+        """prompts [B, P] int -> first generated token ids [B] (int32, on device)."""
+        cfg, s, D = self.cfg, self.s, self.cfg.head_dim
+        B, P = prompts.shape
+        self.cache.reserve(B, self.max_seq)
+        bt = self.cache.block_tables[:B].long()
+        pos = torch.arange(P, device=self.device)
+        x = self.w.embed[prompts.to(self.device).long()]  # [B, P, H]
+        c, sn = self.cos[pos][None, :, None, :], self.sin[pos][None, :, None, :]
+
+        def rope(t):  # [B, P, heads, D]
+            t1, t2 = t[..., :D // 2].float(), t[..., D // 2:].float()
+            return torch.cat([t1 * c - t2 * sn, t2 * c + t1 * sn], -1).to(self.dtype)
+
+        res = x
+        for i, L in enumerate(self.w.layers):
+            h = F.rms_norm(res.float(), (cfg.hidden,), L.ln1.float(), cfg.eps).to(self.dtype)
+            qkv = h @ L.wqkv.t()
+            q, k, v = qkv.split([s["nq"] * D, s["nkv"] * D, s["nkv"] * D], -1)
+            q = rope(q.view(B, P, s["nq"], D))
+            k = rope(k.view(B, P, s["nkv"], D))
+            v = v.view(B, P, s["nkv"], D)
+            nb = (P + 15) // 16
+            pad = nb * 16 - P
+            kp = F.pad(k, (0, 0, 0, 0, 0, pad)).view(B, nb, 16, s["nkv"], D).permute(0, 1, 3, 2, 4)
+            vp = F.pad(v, (0, 0, 0, 0, 0, pad)).view(B, nb, 16, s["nkv"], D).permute(0, 1, 3, 2, 4)
+            self.cache.k[i][bt[:, :nb]] = kp
+            self.cache.v[i][bt[:, :nb]] = vp
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               is_causal=True, enable_gqa=True, scale=self.scale)
+            o = self._ar(a.transpose(1, 2).reshape(B, P, -1) @ L.wo.t())
+            res = res + o
+            h = F.rms_norm(res.float(), (cfg.hidden,), L.ln2.float(), cfg.eps).to(self.dtype)
+            g, u = (h @ L.wgu.t()).chunk(2, -1)
+            d = self._ar((F.silu(g.float()) * u.float()).to(self.dtype) @ L.wdown.t())
+            res = res + d
+        h = F.rms_norm(res[:, -1].float(), (cfg.hidden,), self.w.final_norm.float(), cfg.eps).to(self.dtype)
+        logits = (h @ self.w.lm_head.t()).float()
+        val, idx = logits.max(-1)
+        idx = idx + self.rank * self.s["vocab"]
+        if self.tp > 1:
+            import torch.distributed as dist
+
+            vals = [torch.empty_like(val) for _ in range(self.tp)]
+            idxs = [torch.empty_like(idx) for _ in range(self.tp)]
+            dist.all_gather(vals, val, group=self.nccl_group)
+            dist.all_gather(idxs, idx, group=self.nccl_group)
+            v = torch.stack(vals)
+            best = v.argmax(0)
+            idx = torch.stack(idxs).gather(0, best[None])[0]
+        self.prompt_len = P
+        return idx.to(torch.int32)
+
+    # ------------------------------------------------------------------ decode step (our kernels)
+    def _buffers(self, B: int) -> dict:
+        cfg, s, D, dev, dt = self.cfg, self.s, self.cfg.head_dim, self.device, self.dtype
+        e = lambda *shape: torch.empty(*shape, dtype=dt, device=dev)  # noqa: E731
+        return dict(
+            ids=torch.zeros(B, dtype=torch.int32, device=dev),
+            pos=torch.zeros(B, dtype=torch.int32, device=dev),
+            lens=torch.zeros(B, dtype=torch.int32, device=dev),
+            res=e(B, cfg.hidden), h=e(B, cfg.hidden), part=e(B, cfg.hidden),
+            qkv=e(B, (s["nq"] + 2 * s["nkv"]) * D), q=e(B, s["nq"], D), attn=e(B, s["nq"], D),
+            gu=e(B, 2 * s["inter"]), act=e(B, s["inter"]), logits=e(B, s["vocab"]),
+            words=torch.empty(B, 2, dtype=torch.int32, device=dev),
+            gathered=torch.empty(self.tp, B * 2, dtype=torch.int32, device=dev),
+            attn_op=K.DecodeAttention(B, s["nq"], s["nkv"], D, self.cache.max_blocks_per_seq, dev,
+                                      torch.cuda.get_device_properties(dev).multi_processor_count),
+        )
+
+    def _step(self, B: int, buf: dict) -> int:
+        """Issue one decode step on the current stream; returns the number of kernels launched."""
+        cfg, s, w, comm = self.cfg, self.s, self.w, self.comm
+        bt = self.cache.block_tables[:B]
+        n = 0
+        K.embedding(buf["ids"], w.embed, out=buf["res"])  # residual stream starts as the embedding
+        K.rmsnorm(buf["res"], w.layers[0].ln1, cfg.eps, out=buf["h"])
+        n += 2
+        ours = 1 if self.gemm == "cob" else 0
+        for i, L in enumerate(w.layers):
+            self.lin[(i, "qkv")](buf["h"], out=buf["qkv"])
+            K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
+                             self.cache.v[i], s["nq"], s["nkv"])
+            buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
+            self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
+            comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], L.ln2, cfg.eps, out=buf["h"])
+            self.lin[(i, "gu")](buf["h"], out=buf["gu"])
+            K.silu_mul(buf["gu"], out=buf["act"])
+            self.lin[(i, "down")](buf["act"], out=buf["part"])
+            nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
+            comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], nxt, cfg.eps, out=buf["h"])
+            n += 5 + 4 * ours
+        self.lin["head"](buf["h"], out=buf["logits"])
+        K.argmax_local(buf["logits"], self.rank * s["vocab"], words=buf["words"])
+        n += 1 + ours
+        if self.tp > 1:
+            comm.all_gather_u32(buf["words"].view(-1), out=buf["gathered"])
+            n += 1
+        K.argmax_combine(buf["gathered"].view(self.tp, B, 2) if self.tp > 1 else buf["words"].view(1, B, 2), self.tp,
+                         ids=buf["ids"], positions=buf["pos"], seq_lens=buf["lens"])
+        return n + 1
+
+    def start(self, B: int, first_ids: torch.Tensor, prompt_len: int):
+        """Set up decoding of B sequences whose prompts (length prompt_len) are in the cache."""
+        if B not in self.graphs:
+            self.graphs[B] = (None, self._buffers(B))
+        buf = self.graphs[B][1]
+        buf["ids"].copy_(first_ids.to(torch.int32))
+        buf["pos"].fill_(prompt_len)
+        buf["lens"].fill_(prompt_len + 1)
+        return buf
+
+    def capture(self, B: int):
+        """Capture one decode step for batch B in a CUDA graph (buffers are static)."""
+        buf = self.graphs[B][1]
+        saved = {k: v.clone() for k, v in buf.items() if k in ("ids", "pos", "lens")}
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            self._step(B, buf)  # warm-up outside the graph (also compiles lazy modules)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        for k, v in saved.items():
+            buf[k].copy_(v)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.kernels_per_step[B] = self._step(B, buf)
+        self.graphs[B] = (g, buf)
+        # the warm-up step advanced the device state once; restore the decode position
+        for k, v in saved.items():
+            buf[k].copy_(v)
+        torch.cuda.synchronize(self.device)
+        return g
+
+    def step(self, B: int, use_graph: bool = True) -> torch.Tensor:
+        g, buf = self.graphs[B]
+        if use_graph and g is not None:
+            g.replay()
+        else:
+            self._step(B, buf)
+        return buf["ids"]
+
+    def decode(self, B: int, host_ids: torch.Tensor, host_out: torch.Tensor) -> torch.Tensor:
+        """One end-to-end greedy step through the public API: copy this step's input token ids from
+        pinned host memory, run the captured step, read the next ids back into pinned host memory."""
+        g, buf = self.graphs[B]
+        buf["ids"].copy_(host_ids, non_blocking=True)
+        if g is not None:
+            g.replay()
+        else:
+            self._step(B, buf)
+        host_out.copy_(buf["ids"], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return host_out
+
+    def release_graphs(self):
+        """Drop captured graphs (required before destroying the process group)."""
+        self.graphs = {B: (None, buf) for B, (g, buf) in self.graphs.items()}
+
+
+def reference_greedy(cfg: LlamaConfig, full: dict, prompts: torch.Tensor, steps: int, device) -> torch.Tensor:
+    """Unsharded fp32 greedy decoding (no KV cache: full recompute), tokens [B, steps+1]."""
+    W = {k: v for k, v in full.items() if k != "layers"}
+    layers = full["layers"]
+    D = cfg.head_dim
+    cos, sin = rope_tables(prompts.shape[1] + steps + 1, D, cfg.rope_theta, device)
+    toks = prompts.to(device).long()
+    out = []
+    for _ in range(steps + 1):
+        B, P = toks.shape
+        x = W["embed"].to(device).float()[toks]
+        c, sn = cos[:P][None, :, None, :], sin[:P][None, :, None, :]
+
+        def rope(t):
+            t1, t2 = t[..., :D // 2], t[..., D // 2:]
+            return torch.cat([t1 * c - t2 * sn, t2 * c + t1 * sn], -1)
+
+        for L in layers:
+            L = {k: v.to(device).float() for k, v in L.items()}
+            h = F.rms_norm(x, (cfg.hidden,), L["ln1"], cfg.eps)
+            q, k, v = (h @ L["wqkv"].t()).split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
+            q, k = rope(q.view(B, P, cfg.heads, D)), rope(k.view(B, P, cfg.kv_heads, D))
+            v = v.view(B, P, cfg.kv_heads, D)
+            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
+                                               enable_gqa=True, scale=1.0 / math.sqrt(D))
+            x = x + a.transpose(1, 2).reshape(B, P, -1) @ L["wo"].t()
+            h = F.rms_norm(x, (cfg.hidden,), L["ln2"], cfg.eps)
+            g, u = (h @ L["wgu"].t()).chunk(2, -1)
+            x = x + (F.silu(g) * u) @ L["wdown"].t()
+        h = F.rms_norm(x[:, -1], (cfg.hidden,), W["final_norm"].to(device).float(), cfg.eps)
+        nxt = (h @ W["lm_head"].to(device).float().t()).argmax(-1)
+        out.append(nxt)
+        toks = torch.cat([toks, nxt[:, None]], 1)
+    return torch.stack(out, 1)
+
+
+def tiny_config(**kw) -> LlamaConfig:
+    return replace(TINY, **kw)

@@ -43,10 +43,13 @@ def argmax_local(logits: torch.Tensor, vocab_offset: int, words: torch.Tensor | 
     return words
 
 
-def argmax_combine(words: torch.Tensor, world: int, ids: torch.Tensor | None = None) -> torch.Tensor:
+def argmax_combine(words: torch.Tensor, world: int, ids: torch.Tensor | None = None, positions=None,
+                   seq_lens=None) -> torch.Tensor:
+    """Global greedy token per row from every rank's (max, index) words; optionally advances the
+    decode positions / sequence lengths in the same kernel."""
     rows = words.shape[-2]
     ids = torch.empty(rows, dtype=torch.int32, device=words.device) if ids is None else ids
-    native().argmax_combine(words, ids, int(world))
+    native().argmax_combine(words, ids, int(world), positions, seq_lens)
     return ids
 
 

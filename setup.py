@@ -25,6 +25,7 @@ SOURCES = [
     "fused_ar.cu",
     "decode_ops.cu",
     "attention.cu",
+    "gemm_sm100.cu",
 ]
 SOURCES += [s for s in os.environ.get("COB_EXTRA_SOURCES", "").split(",") if s]
 

@@ -1,0 +1,54 @@
+"""tcgen05 decode GEMM against a plain fp32 PyTorch matmul."""
+import pytest
+import torch
+
+from comm_opt_b200.models.gemm import gemm, gemm_error_word
+from comm_opt_b200.ops.reference import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (8, 1280, 8192), (3, 300, 200), (16, 8192, 1024),
+                                   (32, 7168, 1024), (64, 1024, 3584), (128, 16032, 512), (200, 512, 4096),
+                                   (256, 256, 256), (300, 384, 128)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_matches_fp32(cuda, M, N, K, dtype):
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + N)
+    x = torch.randn(M, K, device=cuda, generator=g).to(dtype)
+    w = (0.05 * torch.randn(N, K, device=cuda, generator=g)).to(dtype)
+    ref = x.float() @ w.float().t()
+    y = gemm(x, w)
+    torch.cuda.synchronize()
+    assert int(gemm_error_word(cuda)) == 0
+    assert rel_err(y, ref) <= 2 ** -7, rel_err(y, ref)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 8])
+def test_gemm_split_k_deterministic(cuda, splits):
+    x = torch.randn(8, 4096, device=cuda).to(torch.bfloat16)
+    w = (0.05 * torch.randn(512, 4096, device=cuda)).to(torch.bfloat16)
+    from comm_opt_b200._ext import native
+
+    y1 = torch.empty(8, 512, device=cuda, dtype=torch.bfloat16)
+    y2 = torch.empty_like(y1)
+    native().gemm(x, w, y1, gemm_error_word(cuda), splits, False, int(2e9))
+    native().gemm(x, w, y2, gemm_error_word(cuda), splits, False, int(2e9))
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    assert rel_err(y1, x.float() @ w.float().t()) <= 2 ** -7
+
+
+def test_gemm_into_strided_output_and_graph(cuda):
+    x = torch.randn(4, 1024, device=cuda).to(torch.bfloat16)
+    w = (0.05 * torch.randn(2048, 1024, device=cuda)).to(torch.bfloat16)
+    big = torch.zeros(4, 4096, device=cuda, dtype=torch.bfloat16)
+    out = big[:, 1024:3072]
+    gemm(x, w, out)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gemm(x, w, out)
+    x.mul_(2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert rel_err(out, x.float() @ w.float().t()) <= 2 ** -7
+    assert torch.all(big[:, :1024] == 0) and torch.all(big[:, 3072:] == 0)
