@@ -324,3 +324,97 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
 }
 
 }  // namespace cob
+
+// ------------------------------------------------------------------------------------------------
+// Allocation-free entry point (see attention_noalloc.h for who calls it and its limits).
+// ------------------------------------------------------------------------------------------------
+#include <mutex>
+#include <string>
+
+#include "attention_noalloc.h"
+
+// One fixed scratch area per GPU, part of the library image: split-KV partial outputs, their
+// (max, sum) pairs and the per-(sequence, head) arrival counters of the kernel above.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[COB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+std::mutex g_noalloc_mu;
+thread_local std::string g_noalloc_err;
+
+int noalloc_fail(int code, const std::string& msg) {
+  g_noalloc_err = msg;
+  return code;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) size_t cob_noalloc_scratch_capacity(void) {
+  return COB_NOALLOC_SCRATCH_BYTES;
+}
+
+extern "C" __attribute__((visibility("default"))) const char* cob_noalloc_last_error(void) {
+  return g_noalloc_err.c_str();
+}
+
+extern "C" __attribute__((visibility("default"))) int cob_decode_attention_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int32_t* block_tables, const int32_t* seq_lens,
+    void* out, int batch, int nq, int nkv, int head_dim, int block_size, int max_blocks_per_seq, int splits,
+    int pages_per_split, float scale, int dtype, void* stream) {
+  g_noalloc_err.clear();
+  if (batch <= 0 || nkv <= 0 || nq <= 0 || nq % nkv != 0 || splits <= 0 || head_dim <= 0)
+    return noalloc_fail(cudaErrorInvalidValue, "invalid geometry");
+  const size_t need = cob::attn_scratch_bytes(batch, nkv, splits, nq / nkv, head_dim);
+  if (need > COB_NOALLOC_SCRATCH_BYTES)
+    return noalloc_fail(cudaErrorInvalidValue, "split-KV scratch of " + std::to_string(need) +
+                                                   " bytes exceeds the built-in limit of " +
+                                                   std::to_string((size_t)COB_NOALLOC_SCRATCH_BYTES) +
+                                                   " bytes; use fewer splits or a smaller batch");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(e, "cudaGetDevice failed");
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return noalloc_fail(cudaErrorInvalidDevice, "device index too large");
+  void* base = nullptr;
+  {
+    // set-up, once per device, with that device current: host code needs the array's device address
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      e = cudaGetSymbolAddress(&g_noalloc_addr[dev], g_noalloc_scratch);
+      if (e != cudaSuccess) {
+        g_noalloc_addr[dev] = nullptr;
+        return noalloc_fail(e, std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e));
+      }
+    }
+    base = g_noalloc_addr[dev];
+  }
+  const size_t pairs = (size_t)batch * nkv, group = (size_t)(nq / nkv);
+  char* b = static_cast<char*>(base);
+  cob::AttnParams p = {};
+  p.q = q;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.block_tables = block_tables;
+  p.seq_lens = seq_lens;
+  p.out = out;
+  p.part_o = reinterpret_cast<float*>(b);
+  p.part_ml = reinterpret_cast<float*>(b + pairs * splits * group * head_dim * sizeof(float));
+  p.counters = reinterpret_cast<int32_t*>(b + pairs * splits * group * head_dim * sizeof(float) +
+                                          pairs * splits * group * 2 * sizeof(float));
+  p.batch = batch;
+  p.nq = nq;
+  p.nkv = nkv;
+  p.head_dim = head_dim;
+  p.block_size = block_size;
+  p.max_blocks_per_seq = max_blocks_per_seq;
+  p.splits = splits;
+  p.pages_per_split = pages_per_split;
+  p.scale = scale;
+  p.dtype = dtype;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the counters must start at zero (the array keeps whatever the previous call left)
+  e = cudaMemsetAsync(p.counters, 0, pairs * sizeof(int32_t), s);
+  if (e != cudaSuccess) return noalloc_fail(e, std::string("clearing counters failed: ") + cudaGetErrorString(e));
+  e = cob::paged_decode_attention(p, s);
+  if (e != cudaSuccess) return noalloc_fail(e, std::string("launch failed: ") + cudaGetErrorString(e));
+  return 0;
+}
