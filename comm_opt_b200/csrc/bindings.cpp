@@ -159,6 +159,7 @@ void py_allgather_u32(std::vector<int64_t> bases, std::vector<int64_t> layout, t
 }  // namespace
 
 void register_ops(pybind11::module& m);  // ops_bindings.cpp
+void register_ipc(pybind11::module& m);  // ipc_bindings.cpp
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "comm_opt_b200 native kernels (sm_100a)";
@@ -170,4 +171,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("kMaxWorld") = cob::kMaxWorld;
   m.attr("kRankStateBytes") = (int64_t)sizeof(cob::RankState);
   register_ops(m);
+  register_ipc(m);
 }

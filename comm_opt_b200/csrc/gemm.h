@@ -8,18 +8,22 @@
 namespace cob {
 
 struct GemmPlan {
-  int bn;      // padded batch width (tcgen05 N): 16, 32, 64, 128 or 256
-  int tiles;   // 128-row output tiles
-  int splits;  // K split over a thread-block cluster (1..8)
-  int kps;     // 64-wide K steps per split
+  int bn;     // padded batch width (tcgen05 N): 16, 32, 64, 128 or 256
+  int tiles;  // 128-row output tiles
+  int ctas;   // persistent CTAs (stream-K partition of tiles x k-steps)
 };
 
-GemmPlan plan_gemm(int M, int N, int K, int num_sms, int splits_override);
+GemmPlan plan_gemm(int M, int N, int K, int num_sms, int ctas_override);
+// fp32 workspace needed for the partial tiles of a launch with `num_ctas` CTAs
+size_t gemm_workspace_bytes(int num_ctas, int bn);
 
 // Y[M, N] (row stride ldy) = X[M, K] * W[N, K]^T; bf16 or fp16 in and out, fp32 accumulation.
-// M <= 256. `err` (device int) receives 1 if a bounded wait timed out.
-cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int* err,
-                        int num_sms, int splits_override, bool pdl, unsigned long long timeout_ns,
-                        cudaStream_t stream, GemmPlan* used);
+// M <= 256. `ws` is the fp32 partial-tile workspace, `tile_ctr` max_tiles int32 that must be zero
+// before the first call (the kernel restores them). `err` (device int) is set if a bounded wait
+// timed out.
+cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
+                        size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
+                        bool pdl, bool small_smem, unsigned long long timeout_ns, cudaStream_t stream,
+                        GemmPlan* used);
 
 }  // namespace cob

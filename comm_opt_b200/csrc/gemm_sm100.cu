@@ -8,10 +8,12 @@
 //                         not depend on the previous kernel); activation tiles after it.
 //   warp 1 / one thread : tcgen05.mma issuer, fp32 accumulator in TMEM (BN columns), releases ring
 //                         slots with tcgen05.commit -> mbarrier.
-//   all 4 warps         : epilogue, tcgen05.ld of their 32 TMEM lanes, bf16 stores.
-// Split-K: when there are fewer output tiles than SMs, the K range is split over a thread-block
-// cluster (<= 8 CTAs along grid.y); partial tiles are summed through distributed shared memory in a
-// fixed order (deterministic, no global workspace).
+//   warps 2-5           : epilogue, tcgen05.ld of their 32 TMEM lanes, bf16 stores / partials.
+// Persistent stream-K: one CTA per SM; CTA c owns an equal, contiguous share of the flattened
+// (output tile, 64-wide k-step) space, so every SM streams the same number of weight bytes whatever
+// the tile count (no wave quantisation). Accumulators are double-buffered in TMEM so the epilogue of
+// one tile overlaps the MMAs of the next. A tile split between CTAs is finished by its last
+// contributor, which sums every contributor's fp32 partial (workspace) in CTA order: deterministic.
 // Every mbarrier wait is bounded by %globaltimer; a timeout sets *err and the CTA drains and exits.
 #include <cooperative_groups.h>
 #include <cudaTypedefs.h>
@@ -28,20 +30,24 @@ namespace {
 namespace cg = cooperative_groups;
 using namespace sm100;
 
-constexpr int BM = 128, BK = 64, kThreads = 128;
+constexpr int BM = 128, BK = 64;
+constexpr int kThreads = 192;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue
+constexpr int kSmemBudget = 220 * 1024;
+constexpr int kMaxContrib = 48;  // CTAs sharing one tile (the planner keeps it below this)
 
-template <int BN>
+// SMALL: half the shared-memory ring, so two CTAs (this kernel and the next one in the stream under
+// programmatic dependent launch) fit on one SM.
+template <int BN, bool SMALL = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;  // 16 KB weight tile
   static constexpr int B_BYTES = BN * BK * 2;  // activation tile
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES = BN <= 32 ? 8 : (BN <= 64 ? 6 : (BN <= 128 ? 5 : 4));
+  static constexpr int STAGES_RAW = ((SMALL ? kSmemBudget / 2 : kSmemBudget) - 2048) / STAGE;
+  static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   static constexpr int PIPE = STAGES * STAGE;
-  static constexpr int RED_STRIDE = BN + 1;  // fp32 partial row stride (bank-conflict padding)
-  static constexpr int RED_BYTES = BM * RED_STRIDE * 4;
-  static constexpr int BODY = PIPE > RED_BYTES ? PIPE : RED_BYTES;
-  static constexpr int SMEM = BODY + 1024 + 256;  // alignment slack + barriers
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int SMEM = PIPE + 1024 + 512;  // alignment slack + barriers + contributor table
+  static constexpr int TC = BN < 32 ? 32 : BN;    // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * TC;        // double-buffered accumulator
 };
 
 template <bool BF16>
@@ -52,28 +58,44 @@ __device__ __forceinline__ void store_out(void* Y, size_t idx, float v) {
     reinterpret_cast<__half*>(Y)[idx] = __float2half_rn(v);
 }
 
-template <int BN, bool BF16>
+// Stream-K partition: CTA c owns flattened k-steps [beg(c), beg(c+1)) of tiles x KT.
+__device__ __forceinline__ long long sk_beg(int c, long long total, int P) { return (long long)c * total / P; }
+__device__ __forceinline__ int sk_owner(long long g, long long total, int P) {
+  int c = (int)((g * P) / total);
+  while (c + 1 < P && sk_beg(c + 1, total, P) <= g) ++c;
+  while (c > 0 && sk_beg(c, total, P) > g) --c;
+  return c;
+}
+
+// Named barrier among the 4 epilogue warps (ids 1.., count 128)
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int BN, bool BF16, bool SMALL>
 __global__ void __launch_bounds__(kThreads, 1)
-    k_gemm_swapab(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
-                  int N, int K, int kps, int ldy, int* err, unsigned long long timeout_ns) {
-  using C = Cfg<BN>;
+    k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
+                   int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns) {
+  using C = Cfg<BN, SMALL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BODY);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::PIPE);
   uint64_t* empty = full + C::STAGES;
-  uint64_t* accum = empty + C::STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = empty + C::STAGES;  // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;         // [2] accumulator drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* s_fail = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* s_issued = const_cast<int*>(s_fail) + 1;
   int* s_consumed = s_issued + 1;
+  int* s_last = s_consumed + 1;
+  int* s_contrib = s_last + 1;  // [kMaxContrib] workspace offsets of a tile's contributors
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BM;
-  const int KT = (K + BK - 1) / BK;
-  const int kt0 = blockIdx.y * kps;
-  const int nk = min(KT, kt0 + kps) - kt0;
+  const int P = gridDim.x, cta = blockIdx.x;
+  const int KT = (K + BK - 1) / BK, tiles = (N + BM - 1) / BM;
+  const long long total = (long long)tiles * KT;
+  const long long beg = sk_beg(cta, total, P), end = sk_beg(cta + 1, total, P);
+  const int first_tile = (int)(beg / KT);
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmW);
@@ -82,7 +104,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accum, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrival per epilogue warp
+    }
     *s_fail = 0;
     *s_issued = 0;
     *s_consumed = 0;
@@ -94,95 +119,172 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    const int pre = min(C::STAGES, nk);
-    for (int i = 0; i < pre; ++i) {
-      mbar_arrive_expect_tx(&full[i], C::STAGE);
-      tma_load_2d(sA + i * C::A_BYTES, &tmW, &full[i], (kt0 + i) * BK, n0);
-    }
-    pdl_wait();  // activations come from the previous kernel
-    for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * C::B_BYTES, &tmX, &full[i], (kt0 + i) * BK, 0);
-    int issued = pre;
-    for (int i = pre; i < nk; ++i) {
-      const int s = i % C::STAGES;
-      if (!mbar_wait(&empty[s], ((i / C::STAGES) & 1) ^ 1, timeout_ns) || *s_fail) {
-        *s_fail = 1;
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      const int nsteps = (int)(end - beg);
+      const int pre = min(C::STAGES, nsteps);
+      // weights first: they do not depend on the previous kernel
+      for (int i = 0; i < pre; ++i) {
+        const long long g = beg + i;
+        mbar_arrive_expect_tx(&full[i], C::STAGE);
+        tma_load_2d(sA + i * C::A_BYTES, &tmW, &full[i], (int)(g % KT) * BK, (int)(g / KT) * BM);
       }
-      mbar_arrive_expect_tx(&full[s], C::STAGE);
-      tma_load_2d(sA + s * C::A_BYTES, &tmW, &full[s], (kt0 + i) * BK, n0);
-      tma_load_2d(sB + s * C::B_BYTES, &tmX, &full[s], (kt0 + i) * BK, 0);
-      issued = i + 1;
-    }
-    *s_issued = issued;
-  } else if (warp == 1 && lane == 0) {
-    constexpr uint32_t idesc = idesc_f16(BM, BN, BF16);
-    int consumed = 0;
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % C::STAGES;
-      if (!mbar_wait(&full[s], (i / C::STAGES) & 1, timeout_ns) || *s_fail) {
-        *s_fail = 1;
-        break;
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const long long g = beg + i;
+        tma_load_2d(sB + i * C::B_BYTES, &tmX, &full[i], (int)(g % KT) * BK, 0);
       }
-      tc_fence_after();
-      const uint32_t a = smem_addr(sA + s * C::A_BYTES), b = smem_addr(sB + s * C::B_BYTES);
+      int issued = pre;
+      for (int i = pre; i < nsteps; ++i) {
+        const int s = i % C::STAGES;
+        if (!mbar_wait(&empty[s], ((i / C::STAGES) & 1) ^ 1, timeout_ns) || *s_fail) {
+          *s_fail = 1;
+          break;
+        }
+        const long long g = beg + i;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        tma_load_2d(sA + s * C::A_BYTES, &tmW, &full[s], (int)(g % KT) * BK, (int)(g / KT) * BM);
+        tma_load_2d(sB + s * C::B_BYTES, &tmX, &full[s], (int)(g % KT) * BK, 0);
+        issued = i + 1;
+      }
+      *s_issued = issued;
+      pdl_trigger();  // every load is issued: the next kernel may start its prologue
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      constexpr uint32_t idesc = idesc_f16(BM, BN, BF16);
+      int i = 0, j = 0;
+      bool ok = true;
+      for (long long g = beg; g < end && ok; ++j) {
+        const int k0 = (int)(g % KT);
+        const int k1 = (int)(((long long)KT < k0 + (end - g)) ? (long long)KT : k0 + (end - g));
+        const int acc = j & 1;
+        if (!mbar_wait(&tempty[acc], ((j >> 1) & 1) ^ 1, timeout_ns)) {
+          *s_fail = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + acc * C::TC;
+        for (int k = k0; k < k1; ++k, ++i) {
+          const int s = i % C::STAGES;
+          if (!mbar_wait(&full[s], (i / C::STAGES) & 1, timeout_ns) || *s_fail) {
+            *s_fail = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_addr(sA + s * C::A_BYTES), b = smem_addr(sB + s * C::B_BYTES);
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk)
-        mma_f16(tmem, desc_k_sw128(a + kk * 32), desc_k_sw128(b + kk * 32), idesc, (i | kk) != 0);
-      mma_commit(&empty[s]);
-      consumed = i + 1;
-    }
-    *s_consumed = consumed;
-    mma_commit(accum);
-  }
-
-  // ---------------------------------------------------------------- epilogue (all 4 warps)
-  if (!mbar_wait(accum, 0, timeout_ns)) *s_fail = 1;
-  __syncwarp();  // tcgen05.ld below is .sync.aligned: the warp must be converged
-  tc_fence_after();
-  pdl_trigger();
-  const int row = warp * 32 + lane;
-  const int n = n0 + row;
-  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-  const int mcols = min(M, BN);
-  if (gridDim.y == 1) {
-    for (int c0 = 0; c0 < mcols; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-      if (n < N) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c0 + j < M) store_out<BF16>(Y, (size_t)(c0 + j) * ldy + n, v[j]);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16(d, desc_k_sw128(a + kk * 32), desc_k_sw128(b + kk * 32), idesc, (k > k0 || kk > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&tfull[acc]);
+        g += k1 - k0;
       }
+      *s_consumed = i;
     }
   } else {
-    // split-K: partial tile -> own shared memory -> sum over the cluster through DSMEM
-    cg::cluster_group cluster = cg::this_cluster();
-    float* red = reinterpret_cast<float*>(smem);
-    __syncthreads();  // every MMA read of the ring has completed (accum), reuse it
-    for (int c0 = 0; c0 < mcols; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
+    // ------------------------------------------------ epilogue: warps 2..5, TMEM lane quarter = warp % 4
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int mcols = min(M, BN);
+    int j = 0;
+    for (long long g = beg; g < end; ++j) {
+      const int t = (int)(g / KT);
+      const int k0 = (int)(g % KT);
+      const int k1 = (int)(((long long)KT < k0 + (end - g)) ? (long long)KT : k0 + (end - g));
+      const int acc = j & 1;
+      const int n = t * BM + row;
+      const bool whole = (k0 == 0 && k1 == KT);
+      if (!mbar_wait(&tfull[acc], (j >> 1) & 1, timeout_ns)) *s_fail = 1;
+      __syncwarp();
+      tc_fence_after();
+      const uint32_t taddr = tmem + acc * C::TC + ((uint32_t)(q * 32) << 16);
+      // partial segments go to workspace slot 0 (first tile of this CTA) or 1 (its last tile),
+      // row-major [row][BN] so the finisher reads 16-byte vectors
+      float* part = ws + ((size_t)cta * 2 + (t == first_tile ? 0 : 1)) * BN * BM + (size_t)row * BN;
+      for (int c0 = 0; c0 < mcols; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+        if (whole) {
+          if (n < N) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) red[row * C::RED_STRIDE + c0 + j] = v[j];
+            for (int jj = 0; jj < 16; ++jj)
+              if (c0 + jj < M) store_out<BF16>(Y, (size_t)(c0 + jj) * ldy + n, v[jj]);
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 16; jj += 4)
+            *reinterpret_cast<float4*>(part + c0 + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&tempty[acc])) : "memory");
+      if (!whole) {
+        // last contributor of tile t sums every contributor's partial in CTA order
+        const int cfirst = sk_owner((long long)t * KT, total, P);
+        const int clast = sk_owner((long long)(t + 1) * KT - 1, total, P);
+        const int nc = clast - cfirst + 1;
+        __threadfence();
+        epi_sync();
+        if (q == 2 && lane == 0) *s_last = (atomicAdd(&tile_ctr[t], 1) == nc - 1);
+        epi_sync();
+        if (*s_last) {
+          __threadfence();
+          // contributor slot offsets, computed once per tile (64-bit divisions off the load path)
+          for (int c = threadIdx.x - 64; c < nc && c < kMaxContrib; c += 128) {
+            const int cc = cfirst + c;
+            s_contrib[c] = (cc * 2 + ((t == (int)(sk_beg(cc, total, P) / KT)) ? 0 : 1)) * BN * BM;
+          }
+          epi_sync();
+          const float* base = ws + (size_t)row * BN;
+          const int ncap = nc < kMaxContrib ? nc : kMaxContrib;
+          for (int c0 = 0; c0 < mcols; c0 += 4) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            int c = 0;
+            for (; c + 8 <= ncap; c += 8) {
+              float4 v[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(base + s_contrib[c + u] + c0));
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                a.x += v[u].x;
+                a.y += v[u].y;
+                a.z += v[u].z;
+                a.w += v[u].w;
+              }
+            }
+            for (; c < ncap; ++c) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(base + s_contrib[c] + c0));
+              a.x += v.x;
+              a.y += v.y;
+              a.z += v.z;
+              a.w += v.w;
+            }
+            if (n < N) {
+              const float o[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                if (c0 + u < M) store_out<BF16>(Y, (size_t)(c0 + u) * ldy + n, o[u]);
+            }
+          }
+          if (q == 2 && lane == 0) tile_ctr[t] = 0;
+        }
+        epi_sync();
+      }
+      g += k1 - k0;
     }
-    cluster.sync();
-    const int cs = gridDim.y, r = blockIdx.y;
-    const int per = (BM + cs - 1) / cs, r0 = r * per, r1 = min(BM, r0 + per), nr = r1 - r0;
-    for (int idx = threadIdx.x; idx < nr * mcols; idx += kThreads) {
-      const int rr = r0 + idx % nr, b = idx / nr;
-      float acc = 0.f;
-      for (int c = 0; c < cs; ++c) acc += cluster.map_shared_rank(red, c)[rr * C::RED_STRIDE + b];
-      if (n0 + rr < N) store_out<BF16>(Y, (size_t)b * ldy + n0 + rr, acc);
-    }
-    cluster.sync();
   }
 
-  // ---------------------------------------------------------------- teardown
+  // ------------------------------------------------ teardown
   __syncthreads();
   if (threadIdx.x == 0 && *s_fail) {
     atomicOr(err, 1);
-    // drain TMA loads that were issued but never consumed before the shared memory goes away
+    // drain TMA loads that were issued but never consumed before shared memory is released
     for (int i = *s_consumed; i < *s_issued; ++i) mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, timeout_ns);
   }
   tc_fence_before();
@@ -248,11 +350,11 @@ cudaError_t tensor_map(const void* ptr, int rows, int cols, int box_rows, bool b
   return cudaSuccess;
 }
 
-template <int BN, bool BF16>
-cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int M, int N, int K, int kps, int splits,
-                      int ldy, int* err, unsigned long long timeout_ns, bool pdl, cudaStream_t stream) {
-  using C = Cfg<BN>;
-  auto fn = k_gemm_swapab<BN, BF16>;
+template <int BN, bool BF16, bool SMALL>
+cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int M, int N, int K, int ctas, int ldy,
+                      float* ws, int* ctr, int* err, unsigned long long timeout_ns, bool pdl, cudaStream_t stream) {
+  using C = Cfg<BN, SMALL>;
+  auto fn = k_gemm_streamk<BN, BF16, SMALL>;
   static bool attr_set = false;
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -260,19 +362,12 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
     attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((N + BM - 1) / BM, splits, 1);
+  cfg.gridDim = dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[2];
+  cudaLaunchAttribute attrs[1];
   int na = 0;
-  if (splits > 1) {
-    attrs[na].id = cudaLaunchAttributeClusterDimension;
-    attrs[na].val.clusterDim.x = 1;
-    attrs[na].val.clusterDim.y = splits;
-    attrs[na].val.clusterDim.z = 1;
-    ++na;
-  }
   if (pdl) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
@@ -280,51 +375,72 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, kps, ldy, err, timeout_ns);
+  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns);
 }
 
-template <bool BF16>
-cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K, int kps,
-                         int splits, int ldy, int* err, unsigned long long t, bool pdl, cudaStream_t s) {
+template <bool BF16, bool SMALL>
+cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K,
+                          int ctas, int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl,
+                          cudaStream_t s) {
   switch (bn) {
-    case 16: return launch_bn<16, BF16>(mw, mx, Y, M, N, K, kps, splits, ldy, err, t, pdl, s);
-    case 32: return launch_bn<32, BF16>(mw, mx, Y, M, N, K, kps, splits, ldy, err, t, pdl, s);
-    case 64: return launch_bn<64, BF16>(mw, mx, Y, M, N, K, kps, splits, ldy, err, t, pdl, s);
-    case 128: return launch_bn<128, BF16>(mw, mx, Y, M, N, K, kps, splits, ldy, err, t, pdl, s);
-    case 256: return launch_bn<256, BF16>(mw, mx, Y, M, N, K, kps, splits, ldy, err, t, pdl, s);
+    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
     default: return cudaErrorInvalidValue;
   }
 }
 
+template <bool BF16>
+cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K, int ctas,
+                         int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl, bool small,
+                         cudaStream_t s) {
+  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s)
+               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+}
+
 }  // namespace
 
-GemmPlan plan_gemm(int M, int N, int K, int num_sms, int splits_override) {
+GemmPlan plan_gemm(int M, int N, int K, int num_sms, int ctas_override) {
   GemmPlan p = {};
   p.bn = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256)));
-  const int tiles = (N + BM - 1) / BM, KT = (K + BK - 1) / BK;
-  int s = splits_override > 0 ? splits_override : (tiles >= num_sms ? 1 : std::max(1, num_sms / tiles));
-  s = std::max(1, std::min(std::min(s, 8), KT));
-  p.kps = (KT + s - 1) / s;
-  p.splits = (KT + p.kps - 1) / p.kps;
-  p.tiles = tiles;
+  p.tiles = (N + BM - 1) / BM;
+  const int KT = (K + BK - 1) / BK;
+  const long long total = (long long)p.tiles * KT;
+  int ctas = ctas_override > 0 ? ctas_override : num_sms;
+  if (ctas_override <= 0) {
+    // wide batch tiles make split tiles expensive to finish: bound the CTAs sharing one tile
+    const int max_share = p.bn <= 32 ? 32 : (p.bn <= 64 ? 8 : 4);
+    ctas = (int)std::min<long long>(ctas, (long long)p.tiles * max_share);
+  }
+  p.ctas = (int)std::min<long long>(std::max(1, ctas), total);
+  // a tile is shared by at most ceil(KT / (total / ctas)) + 1 CTAs; keep that within kMaxContrib
+  while (p.ctas > 1 && ((long long)KT * p.ctas + total - 1) / total + 1 > kMaxContrib) --p.ctas;
   return p;
 }
 
-cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, int* err,
-                        int num_sms, int splits_override, bool pdl, unsigned long long timeout_ns,
-                        cudaStream_t stream, GemmPlan* used) {
+size_t gemm_workspace_bytes(int num_ctas, int bn) { return (size_t)num_ctas * 2 * BM * bn * sizeof(float); }
+
+cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
+                        size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
+                        bool pdl, bool small_smem, unsigned long long timeout_ns, cudaStream_t stream,
+                        GemmPlan* used) {
   if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % 8 || (dtype != kBF16 && dtype != kF16))
     return cudaErrorInvalidValue;
-  const GemmPlan p = plan_gemm(M, N, K, num_sms, splits_override);
+  const GemmPlan p = plan_gemm(M, N, K, num_sms, ctas_override);
   if (used) *used = p;
+  if (p.tiles > max_tiles || gemm_workspace_bytes(p.ctas, p.bn) > ws_bytes) return cudaErrorInvalidValue;
   const bool bf16 = dtype == kBF16;
   CUtensorMap mw, mx;
   cudaError_t e = tensor_map(W, N, K, BM, bf16, &mw);
   if (e != cudaSuccess) return e;
   e = tensor_map(X, M, K, p.bn, bf16, &mx);
   if (e != cudaSuccess) return e;
-  return bf16 ? launch_typed<true>(mw, mx, p.bn, Y, M, N, K, p.kps, p.splits, ldy, err, timeout_ns, pdl, stream)
-              : launch_typed<false>(mw, mx, p.bn, Y, M, N, K, p.kps, p.splits, ldy, err, timeout_ns, pdl, stream);
+  return bf16 ? launch_typed<true>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
+                                   small_smem, stream)
+              : launch_typed<false>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
+                                    small_smem, stream);
 }
 
 }  // namespace cob

@@ -156,9 +156,10 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
   ok(cob::paged_decode_attention(p, cur()), "paged_decode_attention");
 }
 
-// y = x @ w^T on the tcgen05 tensor cores. Returns {bn, tiles, splits, kps}.
-std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor err, int64_t splits,
-                             bool pdl, int64_t timeout_ns) {
+// y = x @ w^T on the tcgen05 tensor cores. `ws` float32 workspace, `ctr` int32 tile counters
+// (zero-initialised, left zero). Returns {bn, tiles, ctas}.
+std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor ws, torch::Tensor ctr,
+                             torch::Tensor err, int64_t ctas, bool pdl, bool small_smem, int64_t timeout_ns) {
   dense(x, "x");
   dense(w, "w");
   dense(err, "err");
@@ -166,21 +167,23 @@ std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, 
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
   TORCH_CHECK(y.size(0) == x.size(0) && y.size(1) == w.size(0), "y must be [M, N]");
   TORCH_CHECK(x.scalar_type() == w.scalar_type() && y.scalar_type() == x.scalar_type(), "dtypes must match");
-  TORCH_CHECK(err.scalar_type() == torch::kInt32, "err must be int32");
+  TORCH_CHECK(err.scalar_type() == torch::kInt32 && ctr.scalar_type() == torch::kInt32, "err, ctr must be int32");
+  TORCH_CHECK(ws.scalar_type() == torch::kFloat && ws.is_cuda() && ctr.is_cuda(), "ws must be float32 CUDA");
   const c10::cuda::CUDAGuard g(x.device());
   static int sms = 0;
   if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
   cob::GemmPlan p;
   ok(cob::gemm_decode(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)w.size(0), (int)x.size(1),
-                      (int)y.stride(0), code_of(x), err.data_ptr<int32_t>(), sms, (int)splits, pdl,
-                      (unsigned long long)timeout_ns, cur(), &p),
+                      (int)y.stride(0), code_of(x), ws.data_ptr<float>(), (size_t)ws.numel() * 4,
+                      ctr.data_ptr<int32_t>(), (int)ctr.numel(), err.data_ptr<int32_t>(), sms, (int)ctas, pdl,
+                      small_smem, (unsigned long long)timeout_ns, cur(), &p),
      "gemm_decode");
-  return {p.bn, p.tiles, p.splits, p.kps};
+  return {p.bn, p.tiles, p.ctas};
 }
 
-std::vector<int64_t> py_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, int64_t splits) {
-  const cob::GemmPlan p = cob::plan_gemm((int)M, (int)N, (int)K, (int)sms, (int)splits);
-  return {p.bn, p.tiles, p.splits, p.kps};
+std::vector<int64_t> py_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, int64_t ctas) {
+  const cob::GemmPlan p = cob::plan_gemm((int)M, (int)N, (int)K, (int)sms, (int)ctas);
+  return {p.bn, p.tiles, p.ctas, (int64_t)cob::gemm_workspace_bytes(p.ctas, p.bn)};
 }
 
 }  // namespace

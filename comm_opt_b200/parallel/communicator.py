@@ -56,7 +56,7 @@ class TPCommunicator:
     def __init__(self, group=None, *, emulate_world: int | None = None, device=None, dtype=torch.bfloat16,
                  max_rows: int = 512, max_hidden: int = 8192, max_gather: int = 4096,
                  timeout_ms: float | None = None, pdl: bool = False, table: VariantTable | None = None,
-                 allow_nvls: bool = True):
+                 allow_nvls: bool = True, backend: str = "symm_mem"):
         import torch.distributed as dist
 
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
@@ -82,6 +82,8 @@ class TPCommunicator:
             self.layout = plan_layout(self.world, max_rows, max_hidden, self.esize, max_gather)
             if self.emulated:
                 self.heap = SymmetricHeap.emulated(self.world, self.layout, self.device)
+            elif backend == "ipc":
+                self.heap = SymmetricHeap.from_group_ipc(self.group, self.layout, self.device)
             else:
                 self.heap = SymmetricHeap.from_group(self.group, self.layout, self.device)
             self._layout_list = self.layout.as_list()
@@ -216,6 +218,17 @@ class TPCommunicator:
             native().allgather_u32(self.heap.bases, self._layout_list, inp, out, self.rank, n, int(self.emulated),
                                    self.timeout_ns, n if self.emulated else 0, self.world * n if self.emulated else 0)
         return out
+
+    def close(self):
+        """Collective teardown: every rank unmaps its peers' heaps before any heap is freed."""
+        if self.heap is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self._host_barrier()
+        if hasattr(self.heap, "close_ipc"):
+            self.heap.close_ipc()
+        self._host_barrier()
+        self.heap = None
 
     def describe(self) -> dict:
         return dict(world=self.world, rank=self.rank, emulated=self.emulated, dtype=str(self.dtype),

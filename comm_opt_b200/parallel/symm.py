@@ -10,6 +10,9 @@ Two back ends:
   memory (``torch.distributed._symmetric_memory``: cuMem allocation, peer mapping and, when the
   NVSwitch supports it, a multicast object), exchanged over the process group. The reference
   allocates its prototype buffers the same way (exp/M17_epoch_ab/bench_ab.py:78-86).
+* ``SymmetricHeap.from_group_ipc`` - one process per GPU; our own heap (cudaMalloc) shared through
+  CUDA IPC handles exchanged over the process group: plain NVLink peer mappings, never bound to a
+  multicast object (used where NVLS must stay off, e.g. fault-injection tests).
 * ``SymmetricHeap.emulated`` - all ranks on ONE GPU: ``world`` separate regions of one allocation,
   used to run the whole multi-rank protocol inside a single kernel launch on one GPU.
 """
@@ -117,11 +120,36 @@ class SymmetricHeap:
 
         t = symm_mem.empty(layout.total, dtype=torch.uint8, device=device)
         hdl = symm_mem.rendezvous(t, group)
+        rank = dist.get_rank(group)
+        ptrs = [int(p) for p in hdl.buffer_ptrs]
+        off = t.data_ptr() - ptrs[rank]  # the tensor may sit at an offset inside the symmetric allocation
         try:
             mc = int(hdl.multicast_ptr or 0)
         except (RuntimeError, AttributeError):  # no NVSwitch multicast on this system
             mc = 0
-        return cls(layout, list(hdl.buffer_ptrs), mc, t, dist.get_rank(group), emulated=False, handle=hdl)
+        return cls(layout, [p + off for p in ptrs], mc + off if mc else 0, t, rank, emulated=False, handle=hdl)
+
+    @classmethod
+    def from_group_ipc(cls, group, layout: HeapLayout, device: torch.device) -> "SymmetricHeap":
+        import torch.distributed as dist
+
+        C = native()
+        idx = torch.device(device).index
+        t = C.ipc_alloc(layout.total, idx)
+        handles = [None] * dist.get_world_size(group)
+        dist.all_gather_object(handles, C.ipc_handle(t), group=group)
+        rank = dist.get_rank(group)
+        bases = [t.data_ptr() if r == rank else C.ipc_open(h, idx) for r, h in enumerate(handles)]
+        heap = cls(layout, bases, 0, t, rank, emulated=False)
+        heap.opened = [b for r, b in enumerate(bases) if r != rank]
+        heap.device_index = idx
+        return heap
+
+    def close_ipc(self):
+        """Unmap peers' heaps (collective use: call on every rank, then barrier, before freeing)."""
+        for b in getattr(self, "opened", []):
+            native().ipc_close(b, self.device_index)
+        self.opened = []
 
     @classmethod
     def emulated(cls, world: int, layout: HeapLayout, device: torch.device) -> "SymmetricHeap":

@@ -22,6 +22,7 @@ CXX = ["-O3", "-std=c++17"]
 SOURCES = [
     "bindings.cpp",
     "ops_bindings.cpp",
+    "ipc_bindings.cpp",
     "fused_ar.cu",
     "decode_ops.cu",
     "attention.cu",
