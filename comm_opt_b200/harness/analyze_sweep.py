@@ -1,0 +1,91 @@
+"""Analyzer of fused-op sweeps: per-size table of p50 device latency for every implementation, the
+speedup of our best measured variant over the best baseline, and (``--calibrate``) the measured
+variant table used by ``TPCommunicator`` (the reference's calibrate step, exp/M18_incremental/run_b.py:60-73).
+
+    python -m comm_opt_b200.harness.analyze_sweep results/fused_sweep/<ts>/sweep.json [--calibrate]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+from ..parallel.variant_table import VARIANTS, Choice, VariantTable
+
+BASELINES = ("nccl_norm", "vllm_car", "trt_oneshot", "trt_twoshot", "ref_m16nf")
+
+
+def load(paths: list[str]) -> list[dict]:
+    rows = []
+    for p in paths:
+        d = json.loads(Path(p).read_text())
+        rows += d["rows"]
+    return rows
+
+
+def table(rows: list[dict]) -> tuple[str, list[dict]]:
+    impls = sorted({r["impl"] for r in rows}, key=lambda s: (not s.startswith("ours"), s))
+    out, summary = [], []
+    for world in sorted({r["world"] for r in rows}):
+        sub = [r for r in rows if r["world"] == world]
+        sizes = sorted({r["tokens"] for r in sub})
+        out.append(f"\n## world {world}, hidden {sub[0]['hidden']}, {sub[0]['dtype']}: p50 us per op (max over ranks)\n")
+        out.append("| tokens | KB | " + " | ".join(impls) + " | best ours | best baseline | speedup |")
+        out.append("|" + "---|" * (len(impls) + 5))
+        for T in sizes:
+            cells, best_o, best_b = [], (None, 1e30), (None, 1e30)
+            for name in impls:
+                r = next((x for x in sub if x["tokens"] == T and x["impl"] == name), None)
+                v = r and r["p50_us"] if r and r["correct"] else None
+                cells.append(f"{v:.2f}" if v else ("skip" if r and r["skip"] else "-"))
+                if v and name.startswith("ours") and name != "ours:auto" and v < best_o[1]:
+                    best_o = (name, v)
+                if v and name in BASELINES and v < best_b[1]:
+                    best_b = (name, v)
+            kb = T * sub[0]["hidden"] * 2 // 1024
+            sp = best_b[1] / best_o[1] if best_o[0] and best_b[0] else None
+            out.append(f"| {T} | {kb} | " + " | ".join(cells) +
+                       f" | {best_o[0] or '-'} | {best_b[0] or '-'} | {sp:.2f}x |" if sp else
+                       f"| {T} | {kb} | " + " | ".join(cells) + " | - | - | - |")
+            summary.append(dict(world=world, tokens=T, kb=kb, best_ours=best_o, best_baseline=best_b, speedup=sp))
+    return "\n".join(out), summary
+
+
+def calibrate(rows: list[dict], table_path: Path | None = None) -> VariantTable:
+    """Fastest correct variant (with its geometry) per (world, dtype, hidden, rows bucket)."""
+    import torch
+
+    t = VariantTable.load(table_path)
+    for r in rows:
+        if not r["impl"].startswith("ours:") or r["impl"] == "ours:auto" or not r["correct"] or not r["p50_us"]:
+            continue
+        dtype = getattr(torch, r["dtype"])
+        key = VariantTable.key(r["world"], dtype, r["hidden"], r["tokens"])
+        cur = t.entries.get(key)
+        if cur is None or cur.p50_us is None or r["p50_us"] < cur.p50_us:
+            v = r.get("variant") or {}
+            t.entries[key] = Choice(VARIANTS[r["impl"].split(":", 1)[1]], v.get("blocks", 0), v.get("threads", 0),
+                                    v.get("cluster", 0), round(r["p50_us"], 3))
+    return t
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("sweeps", nargs="+")
+    ap.add_argument("--calibrate", action="store_true", help="update the committed variant table")
+    ap.add_argument("--table", default=None)
+    a = ap.parse_args()
+    rows = load(a.sweeps)
+    text, _ = table(rows)
+    print(text)
+    if a.calibrate:
+        from ..parallel.variant_table import DEFAULT_TABLE
+
+        path = Path(a.table) if a.table else DEFAULT_TABLE
+        t = calibrate(rows, path)
+        t.save(path)
+        print(f"\nvariant table: {len(t.entries)} entries -> {path}")
+
+
+if __name__ == "__main__":
+    main()
