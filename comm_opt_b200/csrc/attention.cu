@@ -13,6 +13,8 @@
 
 #include "common.cuh"
 #include "ops.h"
+#include "sm100.cuh"
+#include "tma_host.h"
 
 namespace cob {
 namespace {
@@ -77,26 +79,55 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// element offset of 16-byte chunk `ch` of row `r` in a swizzled [rows][kD] tile
+// element offset of 16-byte chunk `ch` of row `r` in the Q tile ([16][kD], chunk ^= row % 8)
 __device__ __forceinline__ int swz(int r, int ch) { return r * kD + ((ch ^ (r & 7)) << 3); }
+// element offset of chunk `ch` (0..15) of row `r` in a KV page loaded by two TMA boxes of 64 columns
+// with the 128-byte swizzle: [2 halves][16 rows][64 cols], chunk-within-half ^= row % 8
+__device__ __forceinline__ int swzp(int r, int ch) { return ((ch >> 3) << 10) + r * 64 + (((ch & 7) ^ (r & 7)) << 3); }
 
 __device__ __forceinline__ float safe_exp2_diff(float a, float b) { return a == -INFINITY ? 0.f : exp2f(a - b); }
 
+constexpr int kStages = 3;                    // KV pages in flight per warp
+constexpr int kPageElems = kBS * kD;          // one K (or V) page: 16 x 128
+constexpr int kMaxPagesPerSplit = 512;
+
+struct alignas(64) AttnArgs {
+  CUtensorMap tk, tv;  // K / V caches as 2-D [num_blocks * nkv * 16, 128], box 64 x 16, 128-byte swizzle
+  AttnParams p;
+};
+
+__host__ __device__ constexpr size_t attn_smem_bytes() {
+  return 1024 /*align*/ + (size_t)kWarps * kStages * 2 * kPageElems * 2 + (size_t)kRows * kD * 2 +
+         (size_t)kWarps * kStages * 8 + kMaxPagesPerSplit * 4 + 64;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const AttnParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  T* sQ = reinterpret_cast<T*>(smem);                 // [16][kD]
-  T* sKV = sQ + kRows * kD;                           // [kWarps][2 stages][K,V][kBS][kD]
+__global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_constant__ AttnArgs args) {
+  using namespace sm100;
+  const AttnParams& p = args.p;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  T* sKV = reinterpret_cast<T*>(base);  // [kWarps][kStages][K,V][2 halves][16][64]
+  T* sQ = sKV + (size_t)kWarps * kStages * 2 * kPageElems;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + kRows * kD);  // [kWarps][kStages]
+  int* s_pages = reinterpret_cast<int*>(bars + kWarps * kStages);
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.nq / p.nkv;
   constexpr int CH = kD / 8;  // 16-byte chunks per row
 
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&args.tk);
+    prefetch_tmap(&args.tv);
+    for (int i = 0; i < kWarps * kStages; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
   pdl_wait();
   const int seq = p.seq_lens[b];
   const int npages = (seq + kBS - 1) / kBS;
   const int pg0 = split * p.pages_per_split, pg1 = min(npages, pg0 + p.pages_per_split);
-
+  for (int i = threadIdx.x; i < pg1 - pg0; i += blockDim.x)
+    s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
   const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
   for (int c = threadIdx.x; c < kRows * CH; c += blockDim.x) {
     const int r = c / CH, ch = c % CH;
@@ -112,44 +143,43 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const AttnParams p)
     ldsm_x4(qa[ks], sQ + swz(r, ch));
   }
 
-  const T* kc = reinterpret_cast<const T*>(p.k_cache);
-  const T* vc = reinterpret_cast<const T*>(p.v_cache);
-  T* myKV = sKV + (size_t)warp * 2 * 2 * kBS * kD;
-  auto stageK = [&](int st) { return myKV + (size_t)st * 2 * kBS * kD; };
-  auto stageV = [&](int st) { return myKV + (size_t)st * 2 * kBS * kD + kBS * kD; };
-  auto issue = [&](int pg, int st) {
-    const int blk = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg];
-    const size_t off = ((size_t)blk * p.nkv + kvh) * kBS * kD;
-    T* dk = stageK(st);
-    T* dv = stageV(st);
-#pragma unroll
-    for (int c = lane; c < kBS * CH; c += 32) {
-      const int r = c / CH, ch = c % CH;
-      cp_async16(dk + swz(r, ch), kc + off + (size_t)r * kD + ch * 8);
-      cp_async16(dv + swz(r, ch), vc + off + (size_t)r * kD + ch * 8);
-    }
-    cp_async_commit();
+  T* myKV = sKV + (size_t)warp * kStages * 2 * kPageElems;
+  uint64_t* mybar = bars + warp * kStages;
+  // page i of this warp is pg0 + warp + i * kWarps
+  const int my_pages = pg1 - pg0 > warp ? (pg1 - pg0 - warp + kWarps - 1) / kWarps : 0;
+  auto issue = [&](int i) {
+    if (i >= my_pages || lane != 0) return;
+    const int st = i % kStages;
+    const int blk = s_pages[warp + i * kWarps];
+    const int row = (blk * p.nkv + kvh) * kBS;
+    T* dk = myKV + (size_t)st * 2 * kPageElems;
+    T* dv = dk + kPageElems;
+    mbar_arrive_expect_tx(&mybar[st], 2 * kPageElems * sizeof(T));
+    tma_load_2d(dk, &args.tk, &mybar[st], 0, row);
+    tma_load_2d(dk + kPageElems / 2, &args.tk, &mybar[st], 64, row);
+    tma_load_2d(dv, &args.tv, &mybar[st], 0, row);
+    tma_load_2d(dv + kPageElems / 2, &args.tv, &mybar[st], 64, row);
   };
+#pragma unroll
+  for (int i = 0; i < kStages; ++i) issue(i);
 
   const float sl2 = p.scale * kLog2e;
   float o[kD / 8][4];
 #pragma unroll
   for (int n = 0; n < kD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  bool ok = true;
 
-  int st = 0;
-  if (pg0 + warp < pg1) issue(pg0 + warp, 0);
-  for (int pg = pg0 + warp; pg < pg1; pg += kWarps, st ^= 1) {
-    const int nxt = pg + kWarps;
-    if (nxt < pg1) {
-      issue(nxt, st ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+  for (int i = 0; i < my_pages && ok; ++i) {
+    const int st = i % kStages;
+    const int pg = pg0 + warp + i * kWarps;
+    if (!mbar_wait(&mybar[st], (i / kStages) & 1, 1000000000ull)) {
+      ok = false;
+      if (p.err) atomicOr(p.err, 1);
+      break;
     }
-    __syncwarp();
-    const T* sK = stageK(st);
-    const T* sV = stageV(st);
+    const T* sK = myKV + (size_t)st * 2 * kPageElems;
+    const T* sV = sK + kPageElems;
     float s[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -158,11 +188,10 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const AttnParams p)
       for (int ks = 0; ks < kD / 16; ++ks) {
         const int tok = nt * 8 + (lane & 7), ch = ks * 2 + ((lane >> 3) & 1);
         uint32_t b0, b1;
-        ldsm_x2(b0, b1, sK + swz(tok, ch));
+        ldsm_x2(b0, b1, sK + swzp(tok, ch));
         mma16816<T>(s[nt], qa[ks], b0, b1);
       }
     }
-    // scale, mask the tail of the last page, online softmax (rows lane/4 and lane/4 + 8)
     float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -203,12 +232,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const AttnParams p)
       o[n][1] *= a0;
       o[n][2] *= a1;
       o[n][3] *= a1;
-      const int tok = lane & 15;  // lanes 0-7: tokens 0-7, lanes 8-15: tokens 8-15
+      const int tok = lane & 15;
       uint32_t b0, b1;
-      ldsm_x2_t(b0, b1, sV + swz(tok, n));
+      ldsm_x2_t(b0, b1, sV + swzp(tok, n));
       mma16816<T>(o[n], pa, b0, b1);
     }
-    __syncwarp();
+    __syncwarp();   // every lane is done with this stage before it is refilled
+    issue(i + kStages);
+  }
+  // a warp that gave up still has copies in flight: wait for them (bounded) before smem is reused
+  if (!ok && lane == 0) {
+    for (int i = 0; i < my_pages && i < kStages; ++i) mbar_wait(&mybar[i % kStages], 0, 1000000000ull);
   }
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -217,17 +251,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const AttnParams p)
 
   // ---- merge the warps (shared memory reused)
   __syncthreads();
-  float* sO = reinterpret_cast<float*>(sKV);           // [kWarps][16][kD]
-  float* sML = sO + kWarps * kRows * kD;               // [kWarps][16][2]
+  float* sO = reinterpret_cast<float*>(sKV);    // [kWarps][16][kD]
+  float* sML = sO + kWarps * kRows * kD;        // [kWarps][16][2]
   {
     const int r = lane >> 2, c = 2 * (lane & 3);
 #pragma unroll
     for (int n = 0; n < kD / 8; ++n) {
-      float* base = sO + ((size_t)warp * kRows) * kD + n * 8 + c;
-      base[(size_t)r * kD] = o[n][0];
-      base[(size_t)r * kD + 1] = o[n][1];
-      base[(size_t)(r + 8) * kD] = o[n][2];
-      base[(size_t)(r + 8) * kD + 1] = o[n][3];
+      float* bp = sO + ((size_t)warp * kRows) * kD + n * 8 + c;
+      bp[(size_t)r * kD] = o[n][0];
+      bp[(size_t)r * kD + 1] = o[n][1];
+      bp[(size_t)(r + 8) * kD] = o[n][2];
+      bp[(size_t)(r + 8) * kD + 1] = o[n][3];
     }
     if ((lane & 3) == 0) {
       sML[(warp * kRows + r) * 2] = m0;
@@ -302,25 +336,27 @@ size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_di
 
 cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
   if (p.head_dim != kD || p.block_size != kBS || p.nkv <= 0 || p.nq % p.nkv != 0 || p.nq / p.nkv > kRows ||
-      p.splits <= 0 || p.pages_per_split <= 0 || p.batch <= 0)
+      p.splits <= 0 || p.pages_per_split <= 0 || p.pages_per_split > kMaxPagesPerSplit || p.batch <= 0 ||
+      (p.dtype != kBF16 && p.dtype != kF16))
     return cudaErrorInvalidValue;
-  const size_t smem = (size_t)kRows * kD * 2 + (size_t)kWarps * 2 * 2 * kBS * kD * 2;
-  static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 <= kWarps * 2 * 2 * kBS * kD * 2,
+  static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 <= kWarps * kStages * 2 * kPageElems * 2,
                 "merge buffers must fit in the KV stages");
+  AttnArgs a;
+  a.p = p;
+  // rows of the 2-D cache view; when the caller does not know the block count a large bound is used
+  // (only rows named by the block tables are ever read)
+  const uint64_t rows = (uint64_t)(p.num_blocks > 0 ? p.num_blocks : (1 << 22)) * p.nkv * kBS;
+  const bool bf16 = p.dtype == kBF16;
+  cudaError_t e = tensor_map_2d(p.k_cache, rows, kD, kD * 2, kBS, 64, bf16, &a.tk);
+  if (e != cudaSuccess) return e;
+  e = tensor_map_2d(p.v_cache, rows, kD, kD * 2, kBS, 64, bf16, &a.tv);
+  if (e != cudaSuccess) return e;
+  const size_t smem = attn_smem_bytes();
   const dim3 grid(p.splits, p.nkv, p.batch);
-  cudaError_t e;
-  if (p.dtype == kBF16) {
-    e = cudaFuncSetAttribute(k_decode_attn<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k_decode_attn<__nv_bfloat16><<<grid, kWarps * 32, smem, s>>>(p);
-  } else if (p.dtype == kF16) {
-    e = cudaFuncSetAttribute(k_decode_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k_decode_attn<__half><<<grid, kWarps * 32, smem, s>>>(p);
-  } else {
-    return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  auto fn = bf16 ? k_decode_attn<__nv_bfloat16> : k_decode_attn<__half>;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_k(fn, grid, dim3(kWarps * 32), smem, s, a);
 }
 
 }  // namespace cob

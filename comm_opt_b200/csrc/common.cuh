@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "types.h"
 
 namespace cob {
@@ -251,6 +253,30 @@ __device__ __forceinline__ void mm_red_add_u32(void* mc, uint32_t v) {
 // Programmatic dependent launch. Both are no-ops when the kernel was not launched with PDL.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Process-wide switch: launch every kernel with programmatic stream serialization, so consecutive
+// kernels in a stream or CUDA graph overlap launch latency and prologue. Every kernel of this
+// library calls pdl_wait() before it reads data produced by (or writes data read by) its
+// predecessor. Defined in decode_ops.cu.
+bool& pdl_flag();
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl_flag()) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------------------------
 // reductions

@@ -9,6 +9,12 @@
 #include "ops.h"
 
 namespace cob {
+
+bool& pdl_flag() {
+  static bool on = false;
+  return on;
+}
+
 namespace {
 
 constexpr int kVPT = 4;
@@ -74,38 +80,37 @@ __global__ void k_embedding(const int32_t* __restrict__ ids, const T* __restrict
   for (int v = threadIdx.x; v < hv; v += blockDim.x) dst[v] = ld_nc_v4(src + v);
 }
 
+// One block per (sequence, head): q and k heads are rotated (rotate-half RoPE), q goes to q_out,
+// k and v heads go to their slot of the paged cache.
 template <typename T>
-__global__ void k_rope_append(const T* __restrict__ qkv, const int32_t* __restrict__ positions,
-                              const float* __restrict__ cos_t, const float* __restrict__ sin_t,
-                              const int32_t* __restrict__ block_tables, int max_blocks, T* __restrict__ q_out,
-                              T* __restrict__ k_cache, T* __restrict__ v_cache, int nq, int nkv, int D, int bs) {
+__global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, const int32_t* __restrict__ positions,
+                                                    const float* __restrict__ cos_t, const float* __restrict__ sin_t,
+                                                    const int32_t* __restrict__ block_tables, int max_blocks,
+                                                    T* __restrict__ q_out, T* __restrict__ k_cache,
+                                                    T* __restrict__ v_cache, int nq, int nkv, int D, int bs) {
   pdl_wait();
-  const int b = blockIdx.x;
+  const int b = blockIdx.x, head = blockIdx.y;
   const int pos = positions[b];
   const int half = D / 2;
-  const T* row = qkv + (size_t)b * (nq + 2 * nkv) * D;
-  const float* c = cos_t + (size_t)pos * half;
-  const float* s = sin_t + (size_t)pos * half;
-  const int blk = block_tables[(size_t)b * max_blocks + pos / bs], off = pos % bs;
-  // rotated pairs of q heads then k heads
-  for (int t = threadIdx.x; t < (nq + nkv) * half; t += blockDim.x) {
-    const int head = t / half, i = t - head * half;
-    const T* src = row + (size_t)head * D;
-    const float x1 = to_f(src[i]), x2 = to_f(src[i + half]);
-    const float o1 = x1 * c[i] - x2 * s[i], o2 = x2 * c[i] + x1 * s[i];
-    T* dst;
-    if (head < nq) {
-      dst = q_out + ((size_t)b * nq + head) * D;
-    } else {
-      dst = k_cache + (((size_t)blk * nkv + (head - nq)) * bs + off) * D;
-    }
-    dst[i] = from_f<T>(o1);
-    dst[i + half] = from_f<T>(o2);
+  const T* src = qkv + ((size_t)b * (nq + 2 * nkv) + head) * D;
+  T* dst;
+  if (head < nq) {
+    dst = q_out + ((size_t)b * nq + head) * D;
+  } else {
+    const int blk = block_tables[(size_t)b * max_blocks + pos / bs], off = pos % bs;
+    const int kv = head < nq + nkv ? head - nq : head - nq - nkv;
+    T* cache = head < nq + nkv ? k_cache : v_cache;
+    dst = cache + (((size_t)blk * nkv + kv) * bs + off) * D;
   }
-  // v heads copied as is
-  for (int t = threadIdx.x; t < nkv * D; t += blockDim.x) {
-    const int h = t / D, d = t - h * D;
-    v_cache[(((size_t)blk * nkv + h) * bs + off) * D + d] = row[(size_t)(nq + nkv + h) * D + d];
+  if (head < nq + nkv) {
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      const float c = cos_t[(size_t)pos * half + i], sn = sin_t[(size_t)pos * half + i];
+      const float x1 = to_f(src[i]), x2 = to_f(src[i + half]);
+      dst[i] = from_f<T>(x1 * c - x2 * sn);
+      dst[i + half] = from_f<T>(x2 * c + x1 * sn);
+    }
+  } else {
+    for (int i = threadIdx.x; i < D; i += blockDim.x) dst[i] = src[i];
   }
 }
 
@@ -128,69 +133,54 @@ __global__ void k_silu_mul(const T* __restrict__ gu, T* __restrict__ out, int in
   }
 }
 
-// (value, index) pair reduction: larger value wins, ties -> smaller index
-__device__ __forceinline__ void amax_merge(float& v, int& i, float v2, int i2) {
-  if (v2 > v || (v2 == v && i2 < i)) {
-    v = v2;
-    i = i2;
-  }
+// Greedy argmax key: order-preserving 32-bit image of the value in the high word, inverted index in
+// the low word, so the maximum key is the largest value and, among equal values, the lowest index.
+__device__ __forceinline__ unsigned long long amax_key(float v, uint32_t idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (0xFFFFFFFFu - idx);
 }
+__device__ __forceinline__ unsigned long long umax64(unsigned long long a, unsigned long long b) { return a > b ? a : b; }
 
+constexpr int kArgmaxChunk = 2048;
+
+// grid (rows, chunks of the local vocabulary): each CTA folds its chunk into keys[row] (atomicMax);
+// keys must be zero before (argmax_combine clears them)
 template <typename T>
-__global__ void __launch_bounds__(1024) k_argmax_local(const T* __restrict__ logits, uint32_t* __restrict__ words,
-                                                       int vocab, int vocab_offset) {
+__global__ void __launch_bounds__(256) k_argmax_local(const T* __restrict__ logits, unsigned long long* keys,
+                                                      int vocab, int vocab_offset) {
   pdl_wait();
   const int row = blockIdx.x;
+  const int i0 = blockIdx.y * kArgmaxChunk, i1 = min(vocab, i0 + kArgmaxChunk);
   const T* lr = logits + (size_t)row * vocab;
-  float best = -FLT_MAX;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) amax_merge(best, bi, to_f(lr[i]), i);
+  unsigned long long best = 0ull;
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) best = umax64(best, amax_key(to_f(lr[i]), i + vocab_offset));
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-    amax_merge(best, bi, v2, i2);
-  }
-  __shared__ float sv[32];
-  __shared__ int si[32];
+  for (int o = 16; o > 0; o >>= 1) best = umax64(best, __shfl_xor_sync(0xffffffffu, best, o));
+  __shared__ unsigned long long sk[8];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) {
-    sv[warp] = best;
-    si[warp] = bi;
-  }
+  if (lane == 0) sk[warp] = best;
   __syncthreads();
-  if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    best = lane < nw ? sv[lane] : -FLT_MAX;
-    bi = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-      amax_merge(best, bi, v2, i2);
-    }
-    if (lane == 0) {
-      words[row * 2] = __float_as_uint(best);
-      words[row * 2 + 1] = (uint32_t)(bi + vocab_offset);
-    }
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = umax64(best, sk[w]);
+    atomicMax(keys + row, best);
   }
 }
 
-__global__ void k_argmax_combine(const uint32_t* __restrict__ words, int32_t* __restrict__ ids, int rows,
-                                 int world, int32_t* __restrict__ positions, int32_t* __restrict__ seq_lens) {
+// keys gathered from every rank [world][rows] -> global greedy id per row; optionally advance the
+// decode positions / lengths and clear this rank's local keys for the next step
+__global__ void k_argmax_combine(const unsigned long long* __restrict__ gathered, int32_t* __restrict__ ids, int rows,
+                                 int world, int32_t* __restrict__ positions, int32_t* __restrict__ seq_lens,
+                                 unsigned long long* __restrict__ local_keys) {
   pdl_wait();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
-  // decode feedback: the token just produced sits at the next position
+  unsigned long long best = 0ull;
+  for (int r = 0; r < world; ++r) best = umax64(best, gathered[(size_t)r * rows + row]);
+  ids[row] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
   if (positions) positions[row] += 1;
   if (seq_lens) seq_lens[row] += 1;
-  float best = -FLT_MAX;
-  int bi = 0x7fffffff;
-  for (int r = 0; r < world; ++r) {
-    const uint32_t* w = words + ((size_t)r * rows + row) * 2;
-    amax_merge(best, bi, __uint_as_float(w[0]), (int)w[1]);
-  }
-  ids[row] = bi;
+  if (local_keys) local_keys[row] = 0ull;
 }
 
 template <typename F>
@@ -219,9 +209,8 @@ cudaError_t rmsnorm(const void* x, const void* gamma, void* out, int rows, int h
     const int hv = hidden / Vec<T>::N;
     if (hidden % Vec<T>::N || hv > 512 * 2 * kVPT || rows <= 0) return cudaErrorInvalidValue;
     auto k = hv > 512 * kVPT ? k_rmsnorm<T, false, 2 * kVPT> : k_rmsnorm<T, false, kVPT>;
-    k<<<rows, threads_for(hv), 0, s>>>(reinterpret_cast<const T*>(x), nullptr, reinterpret_cast<const T*>(gamma),
-                                       reinterpret_cast<T*>(out), hidden, eps);
-    return cudaGetLastError();
+    return launch_k(k, dim3(rows), dim3(threads_for(hv)), 0, s, reinterpret_cast<const T*>(x), (T*)nullptr,
+                    reinterpret_cast<const T*>(gamma), reinterpret_cast<T*>(out), hidden, eps);
   });
 }
 
@@ -232,10 +221,9 @@ cudaError_t add_rmsnorm(const void* x, void* residual, const void* gamma, void* 
     const int hv = hidden / Vec<T>::N;
     if (hidden % Vec<T>::N || hv > 512 * 2 * kVPT || rows <= 0) return cudaErrorInvalidValue;
     auto k = hv > 512 * kVPT ? k_rmsnorm<T, true, 2 * kVPT> : k_rmsnorm<T, true, kVPT>;
-    k<<<rows, threads_for(hv), 0, s>>>(
-        reinterpret_cast<const T*>(x), reinterpret_cast<T*>(residual), reinterpret_cast<const T*>(gamma),
-        reinterpret_cast<T*>(out), hidden, eps);
-    return cudaGetLastError();
+    return launch_k(k, dim3(rows), dim3(threads_for(hv)), 0, s, reinterpret_cast<const T*>(x),
+                    reinterpret_cast<T*>(residual), reinterpret_cast<const T*>(gamma), reinterpret_cast<T*>(out),
+                    hidden, eps);
   });
 }
 
@@ -244,8 +232,8 @@ cudaError_t embedding(const int32_t* ids, const void* table, void* out, int rows
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
     if ((hidden * (int)sizeof(T)) % 16 || rows <= 0) return cudaErrorInvalidValue;
-    k_embedding<T><<<rows, 256, 0, s>>>(ids, reinterpret_cast<const T*>(table), reinterpret_cast<T*>(out), hidden);
-    return cudaGetLastError();
+    return launch_k(k_embedding<T>, dim3(rows), dim3(256), 0, s, ids, reinterpret_cast<const T*>(table),
+                    reinterpret_cast<T*>(out), hidden);
   });
 }
 
@@ -256,11 +244,9 @@ cudaError_t rope_append_kv(const void* qkv, const int32_t* positions, const floa
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
     if (batch <= 0 || head_dim % 2) return cudaErrorInvalidValue;
-    k_rope_append<T><<<batch, 256, 0, s>>>(reinterpret_cast<const T*>(qkv), positions, cos_t, sin_t, block_tables,
-                                           max_blocks_per_seq, reinterpret_cast<T*>(q_out),
-                                           reinterpret_cast<T*>(k_cache), reinterpret_cast<T*>(v_cache), nq, nkv,
-                                           head_dim, block_size);
-    return cudaGetLastError();
+    return launch_k(k_rope_append<T>, dim3(batch, nq + 2 * nkv), dim3(64), 0, s, reinterpret_cast<const T*>(qkv),
+                    positions, cos_t, sin_t, block_tables, max_blocks_per_seq, reinterpret_cast<T*>(q_out),
+                    reinterpret_cast<T*>(k_cache), reinterpret_cast<T*>(v_cache), nq, nkv, head_dim, block_size);
   });
 }
 
@@ -270,26 +256,26 @@ cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, 
     if (inter % Vec<T>::N || rows <= 0) return cudaErrorInvalidValue;
     const int iv = inter / Vec<T>::N;
     const int bx = std::min(64, (iv + 255) / 256);
-    k_silu_mul<T><<<dim3(bx, rows), 256, 0, s>>>(reinterpret_cast<const T*>(gu), reinterpret_cast<T*>(out), inter);
-    return cudaGetLastError();
+    return launch_k(k_silu_mul<T>, dim3(bx, rows), dim3(256), 0, s, reinterpret_cast<const T*>(gu),
+                    reinterpret_cast<T*>(out), inter);
   });
 }
 
-cudaError_t argmax_local(const void* logits, uint32_t* words, int rows, int vocab, int vocab_offset, int dtype,
-                         cudaStream_t s) {
+cudaError_t argmax_local(const void* logits, unsigned long long* keys, int rows, int vocab, int vocab_offset,
+                         int dtype, cudaStream_t s) {
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
     if (rows <= 0 || vocab <= 0) return cudaErrorInvalidValue;
-    k_argmax_local<T><<<rows, 1024, 0, s>>>(reinterpret_cast<const T*>(logits), words, vocab, vocab_offset);
-    return cudaGetLastError();
+    return launch_k(k_argmax_local<T>, dim3(rows, (vocab + kArgmaxChunk - 1) / kArgmaxChunk), dim3(256), 0, s,
+                    reinterpret_cast<const T*>(logits), keys, vocab, vocab_offset);
   });
 }
 
-cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, int32_t* positions,
-                           int32_t* seq_lens, cudaStream_t s) {
+cudaError_t argmax_combine(const unsigned long long* gathered, int32_t* ids, int rows, int world, int32_t* positions,
+                           int32_t* seq_lens, unsigned long long* local_keys, cudaStream_t s) {
   if (rows <= 0 || world <= 0) return cudaErrorInvalidValue;
-  k_argmax_combine<<<(rows + 127) / 128, 128, 0, s>>>(words, ids, rows, world, positions, seq_lens);
-  return cudaGetLastError();
+  return launch_k(k_argmax_combine, dim3((rows + 127) / 128), dim3(128), 0, s, gathered, ids, rows, world, positions,
+                  seq_lens, local_keys);
 }
 
 }  // namespace cob

@@ -581,7 +581,7 @@ cudaError_t launch_typed(const ARParams& p, cudaStream_t stream) {
     attrs[na].val.clusterDim.z = 1;
     ++na;
   }
-  if (p.pdl) {
+  if (p.pdl || pdl_flag()) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
@@ -706,8 +706,7 @@ cudaError_t launch_fused_ar(ARParams p, cudaStream_t stream) {
 
 cudaError_t launch_allgather_u32(GatherParams p, cudaStream_t stream) {
   if (p.n <= 0 || p.n > p.L.max_gather || p.world < 1 || p.world > kMaxWorld) return cudaErrorInvalidValue;
-  k_allgather_u32<<<dim3(1, p.emulate ? p.world : 1, 1), 1024, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_k(k_allgather_u32, dim3(1, p.emulate ? p.world : 1, 1), dim3(1024), 0, stream, p);
 }
 
 }  // namespace cob

@@ -23,6 +23,7 @@
 
 #include "gemm.h"
 #include "sm100.cuh"
+#include "tma_host.h"
 
 namespace cob {
 namespace {
@@ -292,62 +293,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem, C::TMEM_COLS);
 }
 
-// ------------------------------------------------------------------------ tensor maps (host)
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-struct MapKey {
-  uint64_t ptr;
-  int rows, cols, box_rows, bf16;
-  bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows && bf16 == o.bf16;
-  }
-};
-struct MapHash {
-  size_t operator()(const MapKey& k) const {
-    return std::hash<uint64_t>()(k.ptr) ^ ((size_t)k.rows * 1000003u) ^ ((size_t)k.cols << 20) ^
-           ((size_t)k.box_rows << 40) ^ (size_t)k.bf16;
-  }
-};
-
 // Row-major [rows, cols] 16-bit matrix, box = 64 columns (128 bytes, one swizzle span) x box_rows.
 cudaError_t tensor_map(const void* ptr, int rows, int cols, int box_rows, bool bf16, CUtensorMap* out) {
-  static std::mutex mu;
-  static std::unordered_map<MapKey, CUtensorMap, MapHash> cache;
-  const MapKey key{reinterpret_cast<uint64_t>(ptr), rows, cols, box_rows, bf16 ? 1 : 0};
-  std::lock_guard<std::mutex> g(mu);
-  auto it = cache.find(key);
-  if (it != cache.end()) {
-    *out = it->second;
-    return cudaSuccess;
-  }
-  auto enc = encode_fn();
-  if (!enc) return cudaErrorNotSupported;
-  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (cols * 2) % 16) return cudaErrorMisalignedAddress;
-  CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                         const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  if (cache.size() > 8192) cache.clear();
-  cache.emplace(key, m);
-  *out = m;
-  return cudaSuccess;
+  return tensor_map_2d(ptr, (uint64_t)rows, (uint64_t)cols, (uint64_t)cols * 2, (uint32_t)box_rows, (uint32_t)BK,
+                       bf16, out);
 }
 
 template <int BN, bool BF16, bool SMALL>
@@ -368,7 +317,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   cfg.stream = stream;
   cudaLaunchAttribute attrs[1];
   int na = 0;
-  if (pdl) {
+  if (pdl || pdl_flag()) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;

@@ -24,13 +24,14 @@ cudaError_t rope_append_kv(const void* qkv, const int32_t* positions, const floa
                            cudaStream_t s);
 // out[b, i] = silu(gu[b, i]) * gu[b, I + i]
 cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s);
-// Per row: (max value as f32 bits, vocab_offset + argmax) -> words[row*2 + {0,1}]
-cudaError_t argmax_local(const void* logits, uint32_t* words, int rows, int vocab, int vocab_offset, int dtype,
-                         cudaStream_t s);
-// words: [world, rows, 2] gathered from every rank -> ids[row] (ties: lowest index); when given,
-// positions[row] and seq_lens[row] are incremented (decode-step feedback inside a CUDA graph)
-cudaError_t argmax_combine(const uint32_t* words, int32_t* ids, int rows, int world, int32_t* positions,
-                           int32_t* seq_lens, cudaStream_t s);
+// Per row: fold max over the local vocabulary into keys[row] (atomicMax of an order-preserving
+// 64-bit key: value high, inverted global index low; keys must be zero before).
+cudaError_t argmax_local(const void* logits, unsigned long long* keys, int rows, int vocab, int vocab_offset,
+                         int dtype, cudaStream_t s);
+// gathered: [world, rows] keys from every rank -> ids[row] (ties: lowest index); when given,
+// positions/seq_lens are incremented (decode-step feedback inside a CUDA graph) and local_keys cleared
+cudaError_t argmax_combine(const unsigned long long* gathered, int32_t* ids, int rows, int world, int32_t* positions,
+                           int32_t* seq_lens, unsigned long long* local_keys, cudaStream_t s);
 
 // Paged GQA decode attention (split-KV with in-kernel combine by the last split).
 struct AttnParams {
@@ -46,6 +47,8 @@ struct AttnParams {
   int batch, nq, nkv, head_dim, block_size, max_blocks_per_seq, splits, pages_per_split;
   float scale;
   int dtype;
+  int num_blocks;            // rows of the caches / (nkv * block); 0 = unknown
+  int* err;                  // optional: set to 1 if a bounded wait gave up
 };
 // bytes of scratch needed for a given geometry
 size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_dim);

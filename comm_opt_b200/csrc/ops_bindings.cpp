@@ -3,6 +3,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "common_host.h"
 #include "gemm.h"
 #include "ops.h"
 #include "types.h"
@@ -85,21 +86,26 @@ void py_silu_mul(torch::Tensor gu, torch::Tensor out) {
      "silu_mul");
 }
 
-void py_argmax_local(torch::Tensor logits, torch::Tensor words, int64_t vocab_offset) {
+// keys: int64 [rows], zero before the first call (argmax_combine clears them)
+void py_argmax_local(torch::Tensor logits, torch::Tensor keys, int64_t vocab_offset) {
   dense(logits, "logits");
-  dense(words, "words");
+  dense(keys, "keys");
+  TORCH_CHECK(keys.scalar_type() == torch::kInt64 && keys.numel() == logits.size(0), "keys must be int64 [rows]");
   const c10::cuda::CUDAGuard g(logits.device());
-  ok(cob::argmax_local(logits.data_ptr(), reinterpret_cast<uint32_t*>(words.data_ptr()), (int)logits.size(0),
+  ok(cob::argmax_local(logits.data_ptr(), reinterpret_cast<unsigned long long*>(keys.data_ptr()), (int)logits.size(0),
                        (int)logits.size(1), (int)vocab_offset, code_of(logits), cur()),
      "argmax_local");
 }
 
-void py_argmax_combine(torch::Tensor words, torch::Tensor ids, int64_t world, c10::optional<torch::Tensor> positions,
-                       c10::optional<torch::Tensor> seq_lens) {
-  dense(words, "words");
+void py_argmax_combine(torch::Tensor gathered, torch::Tensor ids, int64_t world, c10::optional<torch::Tensor> positions,
+                       c10::optional<torch::Tensor> seq_lens, c10::optional<torch::Tensor> local_keys) {
+  dense(gathered, "gathered");
   dense(ids, "ids");
+  TORCH_CHECK(gathered.scalar_type() == torch::kInt64 && gathered.numel() == world * ids.numel(),
+              "gathered must be int64 [world, rows]");
   int32_t* pos = nullptr;
   int32_t* lens = nullptr;
+  unsigned long long* lk = nullptr;
   if (positions.has_value()) {
     TORCH_CHECK(positions->scalar_type() == torch::kInt32 && positions->numel() == ids.numel(), "positions");
     pos = positions->data_ptr<int32_t>();
@@ -108,9 +114,13 @@ void py_argmax_combine(torch::Tensor words, torch::Tensor ids, int64_t world, c1
     TORCH_CHECK(seq_lens->scalar_type() == torch::kInt32 && seq_lens->numel() == ids.numel(), "seq_lens");
     lens = seq_lens->data_ptr<int32_t>();
   }
-  const c10::cuda::CUDAGuard g(words.device());
-  ok(cob::argmax_combine(reinterpret_cast<const uint32_t*>(words.data_ptr()), ids.data_ptr<int32_t>(),
-                         (int)ids.numel(), (int)world, pos, lens, cur()),
+  if (local_keys.has_value()) {
+    TORCH_CHECK(local_keys->scalar_type() == torch::kInt64 && local_keys->numel() == ids.numel(), "local_keys");
+    lk = reinterpret_cast<unsigned long long*>(local_keys->data_ptr());
+  }
+  const c10::cuda::CUDAGuard g(gathered.device());
+  ok(cob::argmax_combine(reinterpret_cast<const unsigned long long*>(gathered.data_ptr()), ids.data_ptr<int32_t>(),
+                         (int)ids.numel(), (int)world, pos, lens, lk, cur()),
      "argmax_combine");
 }
 
@@ -152,6 +162,8 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
   p.block_tables = block_tables.data_ptr<int32_t>();
   p.seq_lens = seq_lens.data_ptr<int32_t>();
   p.out = out.data_ptr();
+  p.num_blocks = (int)k_cache.size(0);
+  p.err = nullptr;
   const c10::cuda::CUDAGuard g(q.device());
   ok(cob::paged_decode_attention(p, cur()), "paged_decode_attention");
 }
@@ -197,8 +209,11 @@ void register_ops(pybind11::module& m) {
   m.def("rope_append_kv", &py_rope_append_kv);
   m.def("silu_mul", &py_silu_mul);
   m.def("argmax_local", &py_argmax_local);
-  m.def("argmax_combine", &py_argmax_combine, pybind11::arg("words"), pybind11::arg("ids"),
-        pybind11::arg("world"), pybind11::arg("positions") = pybind11::none(), pybind11::arg("seq_lens") = pybind11::none());
+  m.def("argmax_combine", &py_argmax_combine, pybind11::arg("gathered"), pybind11::arg("ids"),
+        pybind11::arg("world"), pybind11::arg("positions") = pybind11::none(), pybind11::arg("seq_lens") = pybind11::none(),
+        pybind11::arg("local_keys") = pybind11::none());
+  m.def("set_pdl", [](bool on) { cob::pdl_flag() = on; });
+  m.def("get_pdl", []() { return cob::pdl_flag(); });
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);
   m.def("decode_attention", &py_decode_attention);
 }

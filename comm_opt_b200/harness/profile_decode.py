@@ -27,13 +27,19 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--gemm", default="cob")
     ap.add_argument("--eager", action="store_true")
+    ap.add_argument("--tp-shape", type=int, default=1,
+                    help="shard the weights this many ways (one GPU, the all-reduce replaced by add+RMSNorm) to "
+                         "profile the per-rank kernels of a TP run")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     cfg = replace(PRESETS[a.model], layers=a.layers)
-    w = LlamaWeights(cfg, 0, 1, dev, seed=0)
+    w = LlamaWeights(cfg, 0, a.tp_shape, dev, seed=0)
     comm = TPCommunicator(None, device=dev, dtype=torch.bfloat16, max_rows=max(8, a.batch), max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, w, comm, max_batch=a.batch, max_seq=a.prompt + a.steps + 64, device=dev, gemm=a.gemm)
+    if a.tp_shape > 1:  # per-rank shard shapes with the collective replaced by its local form
+        runner.s = cfg.shard(a.tp_shape)
+        runner.cache = type(runner.cache)(cfg, a.tp_shape, a.batch, a.prompt + a.steps + 64, dev)
     prompts = torch.randint(0, cfg.vocab, (a.batch, a.prompt), generator=torch.Generator().manual_seed(0))
     first = runner.prefill(prompts)
     runner.start(a.batch, first, a.prompt)

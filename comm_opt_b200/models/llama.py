@@ -176,7 +176,7 @@ class TPDecodeRunner:
     """Greedy TP decoding: torch prefill, then graph-captured decode steps built from our kernels."""
 
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
-                 device, gemm: str = "cob", nccl_group=None):
+                 device, gemm: str = "cob", nccl_group=None, pdl: bool = True):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -196,6 +196,7 @@ class TPDecodeRunner:
         self.lin["head"] = Linear(weights.lm_head, gemm)
         self.graphs: dict[int, tuple] = {}
         self.kernels_per_step: dict[int, int] = {}
+        self.pdl = pdl  # programmatic dependent launch between the kernels of a captured step
 
     # ------------------------------------------------------------------ prefill (plain torch)
     def _ar(self, x: torch.Tensor) -> torch.Tensor:
@@ -270,8 +271,8 @@ class TPDecodeRunner:
             res=e(B, cfg.hidden), h=e(B, cfg.hidden), part=e(B, cfg.hidden),
             qkv=e(B, (s["nq"] + 2 * s["nkv"]) * D), q=e(B, s["nq"], D), attn=e(B, s["nq"], D),
             gu=e(B, 2 * s["inter"]), act=e(B, s["inter"]), logits=e(B, s["vocab"]),
-            words=torch.empty(B, 2, dtype=torch.int32, device=dev),
-            gathered=torch.empty(self.tp, B * 2, dtype=torch.int32, device=dev),
+            keys=torch.zeros(B, dtype=torch.int64, device=dev),
+            gathered=torch.zeros(self.tp, B, dtype=torch.int64, device=dev),
             attn_op=K.DecodeAttention(B, s["nq"], s["nkv"], D, self.cache.max_blocks_per_seq, dev,
                                       torch.cuda.get_device_properties(dev).multi_processor_count),
         )
@@ -299,13 +300,13 @@ class TPDecodeRunner:
             comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], nxt, cfg.eps, out=buf["h"])
             n += 5 + 4 * ours
         self.lin["head"](buf["h"], out=buf["logits"])
-        K.argmax_local(buf["logits"], self.rank * s["vocab"], words=buf["words"])
+        K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         n += 1 + ours
         if self.tp > 1:
-            comm.all_gather_u32(buf["words"].view(-1), out=buf["gathered"])
+            comm.all_gather_u32(buf["keys"].view(torch.int32), out=buf["gathered"].view(torch.int32).view(self.tp, 2 * B))
             n += 1
-        K.argmax_combine(buf["gathered"].view(self.tp, B, 2) if self.tp > 1 else buf["words"].view(1, B, 2), self.tp,
-                         ids=buf["ids"], positions=buf["pos"], seq_lens=buf["lens"])
+        K.argmax_combine(buf["gathered"] if self.tp > 1 else buf["keys"].view(1, B), self.tp, ids=buf["ids"],
+                         positions=buf["pos"], seq_lens=buf["lens"], local_keys=buf["keys"])
         return n + 1
 
     def start(self, B: int, first_ids: torch.Tensor, prompt_len: int):
@@ -331,8 +332,12 @@ class TPDecodeRunner:
         for k, v in saved.items():
             buf[k].copy_(v)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            self.kernels_per_step[B] = self._step(B, buf)
+        old = K.set_pdl(self.pdl)
+        try:
+            with torch.cuda.graph(g):
+                self.kernels_per_step[B] = self._step(B, buf)
+        finally:
+            K.set_pdl(old)
         self.graphs[B] = (g, buf)
         # the warm-up step advanced the device state once; restore the decode position
         for k, v in saved.items():

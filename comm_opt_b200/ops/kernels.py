@@ -37,27 +37,40 @@ def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     return out
 
 
-def argmax_local(logits: torch.Tensor, vocab_offset: int, words: torch.Tensor | None = None) -> torch.Tensor:
-    words = torch.empty(logits.shape[0], 2, dtype=torch.int32, device=logits.device) if words is None else words
-    native().argmax_local(logits, words, int(vocab_offset))
-    return words
+def set_pdl(on: bool) -> bool:
+    """Launch every kernel of this package with programmatic dependent launch (returns the old value)."""
+    old = native().get_pdl()
+    native().set_pdl(bool(on))
+    return old
 
 
-def argmax_combine(words: torch.Tensor, world: int, ids: torch.Tensor | None = None, positions=None,
-                   seq_lens=None) -> torch.Tensor:
-    """Global greedy token per row from every rank's (max, index) words; optionally advances the
-    decode positions / sequence lengths in the same kernel."""
-    rows = words.shape[-2]
-    ids = torch.empty(rows, dtype=torch.int32, device=words.device) if ids is None else ids
-    native().argmax_combine(words, ids, int(world), positions, seq_lens)
+def argmax_local(logits: torch.Tensor, vocab_offset: int, keys: torch.Tensor | None = None) -> torch.Tensor:
+    """Fold the row maxima of this rank's vocabulary shard into int64 keys (zero before use)."""
+    keys = torch.zeros(logits.shape[0], dtype=torch.int64, device=logits.device) if keys is None else keys
+    native().argmax_local(logits, keys, int(vocab_offset))
+    return keys
+
+
+def argmax_combine(gathered: torch.Tensor, world: int, ids: torch.Tensor | None = None, positions=None,
+                   seq_lens=None, local_keys=None) -> torch.Tensor:
+    """Global greedy token per row from every rank's keys [world, rows]; optionally advances the decode
+    positions / sequence lengths and clears this rank's keys in the same kernel."""
+    rows = gathered.shape[-1]
+    ids = torch.empty(rows, dtype=torch.int32, device=gathered.device) if ids is None else ids
+    native().argmax_combine(gathered, ids, int(world), positions, seq_lens, local_keys)
     return ids
 
 
+ATTN_CTAS_PER_SM = 2  # the kernel's shared memory (~106 KB) allows two resident CTAs per SM
+
+
 def attention_split_plan(batch: int, nkv: int, max_pages: int, num_sms: int = 148) -> tuple[int, int]:
-    """Split-KV geometry: about two CTAs per SM over (batch, kv head, split)."""
+    """Split-KV geometry: as many CTAs over (batch, kv head, split) as fit in ONE wave of resident CTAs
+    (a partial second wave would double the kernel time)."""
     pairs = max(1, batch * nkv)
-    splits = max(1, min(max_pages, (2 * num_sms + pairs - 1) // pairs))
-    pps = (max_pages + splits - 1) // splits
+    slots = ATTN_CTAS_PER_SM * num_sms
+    splits = max(1, min(max_pages, slots // pairs))
+    pps = min(512, (max_pages + splits - 1) // splits)
     splits = (max_pages + pps - 1) // pps
     return splits, pps
 

@@ -27,6 +27,7 @@ SOURCES = [
     "decode_ops.cu",
     "attention.cu",
     "gemm_sm100.cu",
+    "tma_host.cpp",
 ]
 SOURCES += [s for s in os.environ.get("COB_EXTRA_SOURCES", "").split(",") if s]
 

@@ -66,11 +66,19 @@ def test_argmax_local_and_combine(cuda):
     V, world, rows = 16032, 4, 6
     logits = torch.randn(world, rows, V, device=cuda).to(torch.bfloat16)
     logits[2, 3, 77] = 100.0  # unique max on rank 2
-    words = torch.stack([K.argmax_local(logits[r], r * V) for r in range(world)])
-    ids = K.argmax_combine(words.contiguous(), world)
+    keys = torch.stack([K.argmax_local(logits[r], r * V) for r in range(world)])
+    local = keys[0].clone()
+    ids = K.argmax_combine(keys.contiguous(), world, local_keys=local)
     ref = torch.cat(list(logits), dim=-1).float().argmax(-1)
     assert torch.equal(ids.long(), ref)
     assert int(ids[3]) == 2 * V + 77
+    assert torch.all(local == 0)  # cleared for the next step
+    # ties resolve to the lowest global index, negative values order correctly
+    t = torch.full((2, 1, 4096), -3.0, device=cuda).to(torch.bfloat16)
+    t[0, 0, 100] = -1.0
+    t[1, 0, 5] = -1.0
+    k2 = torch.stack([K.argmax_local(t[r], r * 4096) for r in range(2)])
+    assert int(K.argmax_combine(k2.contiguous(), 2)[0]) == 100
 
 
 @pytest.mark.parametrize("nq,nkv", [(8, 1), (32, 8), (16, 4)])
