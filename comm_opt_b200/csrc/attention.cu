@@ -311,17 +311,40 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   __threadfence();
   const float* po0 = p.part_o + pair * p.splits * (size_t)G * kD;
   const float* pml0 = p.part_ml + pair * p.splits * (size_t)G * 2;
+  // split weights computed once: w[sp][g] = 2^(m_sp,g - M_g), inv_l[g] = 1 / sum_sp w * l
+  float* s_w = reinterpret_cast<float*>(sKV);      // [splits][G] (KV stages are free now)
+  float* s_l = s_w + (size_t)p.splits * G;         // [splits][G]
+  float* s_inv = s_l + (size_t)p.splits * G;       // [G]
+  for (int i = threadIdx.x; i < p.splits * G; i += blockDim.x) {
+    s_w[i] = __ldcg(pml0 + (size_t)i * 2);
+    s_l[i] = __ldcg(pml0 + (size_t)i * 2 + 1);
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, s_w[sp * G + g]);
+    float L = 0.f;
+    for (int sp = 0; sp < p.splits; ++sp) {
+      const float f = safe_exp2_diff(s_w[sp * G + g], M);
+      s_w[sp * G + g] = f;
+      L += f * s_l[sp * G + g];
+    }
+    s_inv[g] = 1.f / L;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
     const int g = idx / kD;
-    float M = -INFINITY;
-    for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(pml0 + ((size_t)sp * G + g) * 2));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < p.splits; ++sp) {
-      const float f = safe_exp2_diff(__ldcg(pml0 + ((size_t)sp * G + g) * 2), M);
-      L += f * __ldcg(pml0 + ((size_t)sp * G + g) * 2 + 1);
-      O += f * __ldcg(po0 + (size_t)sp * G * kD + idx);
+    float O = 0.f;
+    int sp = 0;
+    for (; sp + 8 <= p.splits; sp += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldcg(po0 + (size_t)(sp + u) * G * kD + idx);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) O += s_w[(sp + u) * G + g] * v[u];
     }
-    out[idx] = from_f<T>(O / L);
+    for (; sp < p.splits; ++sp) O += s_w[sp * G + g] * __ldcg(po0 + (size_t)sp * G * kD + idx);
+    out[idx] = from_f<T>(O * s_inv[g]);
   }
   if (threadIdx.x == 0) p.counters[pair] = 0;
 }
@@ -337,6 +360,7 @@ size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_di
 cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
   if (p.head_dim != kD || p.block_size != kBS || p.nkv <= 0 || p.nq % p.nkv != 0 || p.nq / p.nkv > kRows ||
       p.splits <= 0 || p.pages_per_split <= 0 || p.pages_per_split > kMaxPagesPerSplit || p.batch <= 0 ||
+      (size_t)p.splits * (p.nq / p.nkv) * 2 + kRows > (size_t)kWarps * kStages * 2 * kPageElems / 2 ||
       (p.dtype != kBF16 && p.dtype != kF16))
     return cudaErrorInvalidValue;
   static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 <= kWarps * kStages * 2 * kPageElems * 2,

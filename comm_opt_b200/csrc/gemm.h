@@ -23,7 +23,9 @@ size_t gemm_workspace_bytes(int num_ctas, int bn);
 // timed out.
 cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
                         size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
-                        bool pdl, bool small_smem, unsigned long long timeout_ns, cudaStream_t stream,
-                        GemmPlan* used);
+                        bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
+                        cudaStream_t stream, GemmPlan* used);
+// cluster_splits > 0 selects the cluster split-K schedule (grid tiles x splits, DSMEM reduction,
+// M <= 64, splits <= 8) instead of stream-K.
 
 }  // namespace cob

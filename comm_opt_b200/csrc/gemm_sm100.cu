@@ -71,10 +71,14 @@ __device__ __forceinline__ int sk_owner(long long g, long long total, int P) {
 // Named barrier among the 4 epilogue warps (ids 1.., count 128)
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int BN, bool BF16, bool SMALL>
+// CLUSTER: instead of the stream-K partition, CTA (t, r) of grid (tiles, s) owns k-range r of tile t and
+// the s CTAs of a tile form a thread-block cluster that sums its partial tiles through distributed
+// shared memory (no global workspace, no L2 round trips on the tail). `kps` = k-steps per split.
+template <int BN, bool BF16, bool SMALL, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
-                   int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns) {
+                   int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
+                   int kps) {
   using C = Cfg<BN, SMALL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -95,7 +99,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int P = gridDim.x, cta = blockIdx.x;
   const int KT = (K + BK - 1) / BK, tiles = (N + BM - 1) / BM;
   const long long total = (long long)tiles * KT;
-  const long long beg = sk_beg(cta, total, P), end = sk_beg(cta + 1, total, P);
+  long long beg, end;
+  if (CLUSTER) {
+    beg = (long long)blockIdx.x * KT + (long long)blockIdx.y * kps;
+    end = min((long long)blockIdx.x * KT + KT, beg + kps);
+  } else {
+    beg = sk_beg(cta, total, P);
+    end = sk_beg(cta + 1, total, P);
+  }
   const int first_tile = (int)(beg / KT);
 
   if (threadIdx.x == 0) {
@@ -205,8 +216,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem + acc * C::TC + ((uint32_t)(q * 32) << 16);
       // partial segments go to workspace slot 0 (first tile of this CTA) or 1 (its last tile),
-      // row-major [row][BN] so the finisher reads 16-byte vectors
-      float* part = ws + ((size_t)cta * 2 + (t == first_tile ? 0 : 1)) * BN * BM + (size_t)row * BN;
+      // row-major [row][BN] so the finisher reads 16-byte vectors; in cluster mode to this CTA's
+      // own shared memory (the ring is drained: this is the CTA's only segment)
+      float* part = CLUSTER ? reinterpret_cast<float*>(smem) + (size_t)row * (BN + 4)
+                            : ws + ((size_t)cta * 2 + (t == first_tile ? 0 : 1)) * BN * BM + (size_t)row * BN;
       for (int c0 = 0; c0 < mcols; c0 += 16) {
         float v[16];
         tmem_ld16(taddr + c0, v);
@@ -225,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&tempty[acc])) : "memory");
-      if (!whole) {
+      if (!CLUSTER && !whole) {
         // last contributor of tile t sums every contributor's partial in CTA order
         const int cfirst = sk_owner((long long)t * KT, total, P);
         const int clast = sk_owner((long long)(t + 1) * KT - 1, total, P);
@@ -281,6 +294,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // ------------------------------------------------ cluster split-K: sum the partials over DSMEM (all threads)
+  if (CLUSTER && gridDim.y > 1) {
+    __syncthreads();  // this CTA's partial tile is in its shared memory
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int cs = gridDim.y, r = blockIdx.y, t = blockIdx.x;
+    const int mcols = min(M, BN);
+    const int per = (BM + cs - 1) / cs, r0 = r * per, r1 = min(BM, r0 + per), nr = r1 - r0;
+    const int ncol4 = (mcols + 3) / 4;
+    for (int idx = threadIdx.x; idx < nr * ncol4; idx += kThreads) {
+      const int rr = r0 + idx % nr, c4 = (idx / nr) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = 0; c < cs; ++c) {
+        const float4 v = *reinterpret_cast<const float4*>(
+            cluster.map_shared_rank(reinterpret_cast<float*>(smem), c) + (size_t)rr * (BN + 4) + c4);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      const int nn = t * BM + rr;
+      if (nn < N) {
+        const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (c4 + u < M) store_out<BF16>(Y, (size_t)(c4 + u) * ldy + nn, o[u]);
+      }
+    }
+    cluster.sync();  // no CTA leaves while another still reads its shared memory
+  }
+
   // ------------------------------------------------ teardown
   __syncthreads();
   if (threadIdx.x == 0 && *s_fail) {
@@ -301,22 +345,33 @@ cudaError_t tensor_map(const void* ptr, int rows, int cols, int box_rows, bool b
 
 template <int BN, bool BF16, bool SMALL>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int M, int N, int K, int ctas, int ldy,
-                      float* ws, int* ctr, int* err, unsigned long long timeout_ns, bool pdl, cudaStream_t stream) {
+                      float* ws, int* ctr, int* err, unsigned long long timeout_ns, bool pdl, int splits,
+                      cudaStream_t stream) {
   using C = Cfg<BN, SMALL>;
-  auto fn = k_gemm_streamk<BN, BF16, SMALL>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  const bool clustered = splits > 0;
+  auto fn = clustered ? k_gemm_streamk<BN, BF16, SMALL, true> : k_gemm_streamk<BN, BF16, SMALL, false>;
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[clustered]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set[clustered] = true;
   }
+  const int KT = (K + BK - 1) / BK;
+  const int kps = clustered ? (KT + splits - 1) / splits : 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ctas, 1, 1);
+  cfg.gridDim = clustered ? dim3((N + BM - 1) / BM, (KT + kps - 1) / kps, 1) : dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   int na = 0;
+  if (clustered && cfg.gridDim.y > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 1;
+    attrs[na].val.clusterDim.y = cfg.gridDim.y;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
   if (pdl || pdl_flag()) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
@@ -324,19 +379,19 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns);
+  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps);
 }
 
 template <bool BF16, bool SMALL>
 cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K,
                           int ctas, int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl,
-                          cudaStream_t s) {
+                          int splits, cudaStream_t s) {
   switch (bn) {
-    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
-    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
-    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
-    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
-    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
+    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
+    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
+    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
+    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -344,9 +399,9 @@ cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, 
 template <bool BF16>
 cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K, int ctas,
                          int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl, bool small,
-                         cudaStream_t s) {
-  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s)
-               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, s);
+                         int splits, cudaStream_t s) {
+  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s)
+               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
 }
 
 }  // namespace
@@ -373,8 +428,9 @@ size_t gemm_workspace_bytes(int num_ctas, int bn) { return (size_t)num_ctas * 2 
 
 cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
                         size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
-                        bool pdl, bool small_smem, unsigned long long timeout_ns, cudaStream_t stream,
-                        GemmPlan* used) {
+                        bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
+                        cudaStream_t stream, GemmPlan* used) {
+  if (cluster_splits > 8 || (cluster_splits > 0 && M > 64)) return cudaErrorInvalidValue;
   if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % 8 || (dtype != kBF16 && dtype != kF16))
     return cudaErrorInvalidValue;
   const GemmPlan p = plan_gemm(M, N, K, num_sms, ctas_override);
@@ -387,9 +443,9 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
   e = tensor_map(X, M, K, p.bn, bf16, &mx);
   if (e != cudaSuccess) return e;
   return bf16 ? launch_typed<true>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
-                                   small_smem, stream)
+                                   small_smem, cluster_splits, stream)
               : launch_typed<false>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
-                                    small_smem, stream);
+                                    small_smem, cluster_splits, stream);
 }
 
 }  // namespace cob

@@ -171,7 +171,8 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
 // y = x @ w^T on the tcgen05 tensor cores. `ws` float32 workspace, `ctr` int32 tile counters
 // (zero-initialised, left zero). Returns {bn, tiles, ctas}.
 std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor ws, torch::Tensor ctr,
-                             torch::Tensor err, int64_t ctas, bool pdl, bool small_smem, int64_t timeout_ns) {
+                             torch::Tensor err, int64_t ctas, bool pdl, bool small_smem, int64_t cluster_splits,
+                             int64_t timeout_ns) {
   dense(x, "x");
   dense(w, "w");
   dense(err, "err");
@@ -188,7 +189,7 @@ std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, 
   ok(cob::gemm_decode(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)w.size(0), (int)x.size(1),
                       (int)y.stride(0), code_of(x), ws.data_ptr<float>(), (size_t)ws.numel() * 4,
                       ctr.data_ptr<int32_t>(), (int)ctr.numel(), err.data_ptr<int32_t>(), sms, (int)ctas, pdl,
-                      small_smem, (unsigned long long)timeout_ns, cur(), &p),
+                      small_smem, (int)cluster_splits, (unsigned long long)timeout_ns, cur(), &p),
      "gemm_decode");
   return {p.bn, p.tiles, p.ctas};
 }

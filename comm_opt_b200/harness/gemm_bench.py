@@ -65,16 +65,23 @@ VARIANTS = {  # name -> gemm() keyword arguments
     "small_pdl": dict(small_smem=True, pdl=True),
     "tiles": dict(ctas=-1),  # one CTA per output tile (no split tiles)
     "tiles_small_pdl": dict(ctas=-1, small_smem=True, pdl=True),
+    "cl2": dict(cluster_splits=2), "cl4": dict(cluster_splits=4), "cl8": dict(cluster_splits=8),
+    "cl2_small_pdl": dict(cluster_splits=2, small_smem=True, pdl=True),
+    "cl4_small_pdl": dict(cluster_splits=4, small_smem=True, pdl=True),
+    "cl8_small_pdl": dict(cluster_splits=8, small_smem=True, pdl=True),
 }
 
 
-def sweep(shape_sets: list[str], batches: list[int], variants: list[str], iters: int = 50, dev=None) -> list[dict]:
+def sweep(shape_sets: list[str], batches: list[int], variants: list[str], iters: int = 50, dev=None,
+          ops: list[str] | None = None) -> list[dict]:
     """Time several launch variants of our kernel per shape (graph-captured, weights > L2)."""
     dev = dev or torch.device("cuda", 0)
     peak = peak_hbm_gbs()
     rows = []
     for sset in shape_sets:
         for name, N, K in shapes_for(sset):
+            if ops and name not in ops:
+                continue
             wbytes = N * K * 2
             copies = max(2, (2 * L2_BYTES) // wbytes + 1)
             ws = [torch.empty(N, K, dtype=torch.bfloat16, device=dev).normal_(0, 0.02) for _ in range(copies)]
@@ -129,9 +136,11 @@ def main():
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--out", default=None)
     ap.add_argument("--variants", default=None, help="comma list of launch variants to compare: " + ",".join(VARIANTS))
+    ap.add_argument("--ops", default=None, help="only these projections (qkv,o,gate_up,down,lm_head)")
     a = ap.parse_args()
     if a.variants:
-        rows = sweep(a.shapes.split(","), [int(b) for b in a.batch.split(",")], a.variants.split(","), a.iters)
+        rows = sweep(a.shapes.split(","), [int(b) for b in a.batch.split(",")], a.variants.split(","), a.iters,
+                     ops=a.ops.split(",") if a.ops else None)
     else:
         rows = run(a.shapes.split(","), [int(b) for b in a.batch.split(",")], a.iters)
     if a.out:

@@ -46,13 +46,17 @@ def main():
     if not a.eager:
         runner.capture(a.batch)
     torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("decode")
+    e0.record()
     for _ in range(a.steps):
         runner.step(a.batch, use_graph=not a.eager)
+    e1.record()
     torch.cuda.synchronize()
     torch.cuda.nvtx.range_pop()
     runner.release_graphs()
-    print("ok", runner.kernels_per_step.get(a.batch))
+    print(f"ok kernels/step {runner.kernels_per_step.get(a.batch)} ms/step {e0.elapsed_time(e1) / a.steps:.3f} "
+          f"(layers {a.layers}, tp-shape {a.tp_shape}, batch {a.batch})")
 
 
 if __name__ == "__main__":

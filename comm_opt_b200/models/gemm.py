@@ -34,26 +34,85 @@ def gemm_error_word(device) -> torch.Tensor:
 
 
 def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ctas: int = 0, pdl: bool = False,
-         small_smem: bool = False, timeout_ms: float = 2000.0) -> torch.Tensor:
-    """out[M, N] = x[M, K] @ w[N, K]^T (bf16/fp16, fp32 accumulation); M <= 256 per launch."""
+         small_smem: bool = False, cluster_splits: int = 0, timeout_ms: float = 2000.0) -> torch.Tensor:
+    """out[M, N] = x[M, K] @ w[N, K]^T (bf16/fp16, fp32 accumulation); M <= 256 per launch.
+
+    Schedules: persistent stream-K (default) or, with ``cluster_splits`` = s > 0 (M <= 64), one CTA per
+    (tile, K split) with the s CTAs of a tile in a cluster reducing through distributed shared memory.
+    ``small_smem`` halves the TMA ring so the next kernel can share the SM (programmatic launch)."""
     M, N = x.shape[0], w.shape[0]
     out = torch.empty(M, N, dtype=x.dtype, device=x.device) if out is None else out
     st = _state(x.device)
     for m0 in range(0, M, 256):
         m1 = min(M, m0 + 256)
         native().gemm(x[m0:m1], w, out[m0:m1], st["ws"], st["ctr"], st["err"], ctas, pdl, small_smem,
-                      int(timeout_ms * 1e6))
+                      cluster_splits if m1 - m0 <= 64 else 0, int(timeout_ms * 1e6))
     return out
+
+
+def candidates(M: int, N: int, K: int, num_sms: int = 148) -> list[dict]:
+    """Launch configurations worth measuring for one decode shape."""
+    cands = [dict(), dict(small_smem=True)]
+    tiles = (N + 127) // 128
+    if M <= 64 and tiles < num_sms:
+        for s in (2, 3, 4, 6, 8):
+            if tiles * s <= num_sms * 1.25 and s <= (K + 63) // 64:
+                cands += [dict(cluster_splits=s), dict(cluster_splits=s, small_smem=True)]
+    return cands
+
+
+_TUNED: dict[tuple, dict] = {}
+
+
+def tune(w: torch.Tensor, M: int, iters: int = 15) -> dict:
+    """Measure every candidate schedule for (M, N, K) with CUDA events around single launches (L2
+    flushed before each, as in decode where other layers evict the weights); cache the fastest."""
+    N, K = w.shape
+    key = (M, N, K, w.dtype, w.device.index)
+    if key in _TUNED:
+        return _TUNED[key]
+    dev = w.device
+    x = torch.randn(M, K, device=dev).to(w.dtype)
+    y = torch.empty(M, N, device=dev, dtype=w.dtype)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    best, best_t = {}, float("inf")
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    for cand in candidates(M, N, K, sms):
+        try:
+            gemm(x, w, y, **cand)
+        except RuntimeError:
+            continue
+        ts = []
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            gemm(x, w, y, **cand)
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        t = sorted(ts)[len(ts) // 2]
+        if t < best_t:
+            best, best_t = cand, t
+    _TUNED[key] = dict(best, us=round(best_t * 1000, 2))
+    del flush
+    return _TUNED[key]
 
 
 class Linear:
     def __init__(self, weight: torch.Tensor, impl: str = "cob", pdl: bool = False):
         assert impl in ("cob", "torch")
         self.weight, self.impl, self.pdl = weight, impl, pdl
+        self.cfg: dict[int, dict] = {}  # batch rows -> tuned launch configuration
+
+    def tune(self, M: int) -> dict:
+        if self.impl == "cob" and M not in self.cfg:
+            self.cfg[M] = {k: v for k, v in tune(self.weight, M).items() if k != "us"}
+        return self.cfg.get(M, {})
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         if self.impl == "torch":
             if out is None:
                 return x @ self.weight.t()
             return torch.matmul(x, self.weight.t(), out=out)
-        return gemm(x, self.weight, out, pdl=self.pdl)
+        return gemm(x, self.weight, out, pdl=self.pdl, **self.cfg.get(x.shape[0], {}))

@@ -319,8 +319,15 @@ class TPDecodeRunner:
         buf["lens"].fill_(prompt_len + 1)
         return buf
 
-    def capture(self, B: int):
+    def tune(self, B: int):
+        """Pick the fastest measured GEMM schedule of every projection shape for batch B (cached per shape)."""
+        for lin in self.lin.values():
+            lin.tune(B)
+
+    def capture(self, B: int, tune: bool = True):
         """Capture one decode step for batch B in a CUDA graph (buffers are static)."""
+        if tune and self.gemm == "cob":
+            self.tune(B)
         buf = self.graphs[B][1]
         saved = {k: v.clone() for k, v in buf.items() if k in ("ids", "pos", "lens")}
         s = torch.cuda.Stream(self.device)

@@ -51,3 +51,29 @@ def test_gemm_into_strided_output_and_graph(cuda):
     torch.cuda.synchronize()
     assert rel_err(out, x.float() @ w.float().t()) <= 2 ** -7
     assert torch.all(big[:, :1024] == 0) and torch.all(big[:, 3072:] == 0)
+
+
+@pytest.mark.parametrize("splits", [2, 3, 5, 8])
+@pytest.mark.parametrize("small", [False, True])
+def test_gemm_cluster_split_k(cuda, splits, small):
+    """Cluster split-K schedule (DSMEM reduction) against fp32, deterministic across calls."""
+    for M, N, K in [(1, 1280, 8192), (8, 300, 1000), (64, 8192, 1024)]:
+        x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+        w = (0.05 * torch.randn(N, K, device=cuda)).to(torch.bfloat16)
+        y1 = gemm(x, w, cluster_splits=splits, small_smem=small)
+        y2 = gemm(x, w, cluster_splits=splits, small_smem=small)
+        torch.cuda.synchronize()
+        assert int(gemm_error_word(cuda)) == 0
+        assert torch.equal(y1, y2)
+        assert rel_err(y1, x.float() @ w.float().t()) <= 2 ** -7, (M, N, K, rel_err(y1, x.float() @ w.float().t()))
+
+
+def test_gemm_tuner_picks_valid_config(cuda):
+    from comm_opt_b200.models.gemm import Linear
+
+    w = (0.05 * torch.randn(1280, 8192, device=cuda)).to(torch.bfloat16)
+    lin = Linear(w)
+    cfg = lin.tune(8)
+    assert isinstance(cfg, dict)
+    x = torch.randn(8, 8192, device=cuda).to(torch.bfloat16)
+    assert rel_err(lin(x), x.float() @ w.float().t()) <= 2 ** -7
