@@ -26,6 +26,9 @@ import torch
 import torch.distributed as dist
 
 ROOT = Path(__file__).resolve().parents[2]
+# Prebuilt JIT baselines live under <repo>/baseline; COB_ROOT lets a run name the repository by the
+# same path it was built under, so the JIT builders find their outputs up to date.
+BASE = Path(os.environ.get("COB_ROOT", str(ROOT))) / "baseline"
 
 
 class Impl:
@@ -139,7 +142,7 @@ class VllmCar(Impl):
 
 class FlashInferTrt(Impl):
     def __init__(self, rank, world, max_rows, hidden, cpu_group, oneshot: bool):
-        os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", str(ROOT / "baseline" / "_flashinfer"))
+        os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", str(BASE / "_flashinfer"))
         import flashinfer.comm.trtllm_ar as fi
 
         self.fi, self.rank, self.world, self.oneshot = fi, rank, world, oneshot
@@ -184,10 +187,10 @@ class RefProto(Impl):
 
         if world != 8:
             raise RuntimeError("the reference prototype is hard-wired to 8 ranks")
-        src = ROOT / "baseline" / "_ref" / "exp" / "M17_epoch_ab" / "fused_ar_norm_nf.cu"
+        src = BASE / "_ref" / "exp" / "M17_epoch_ab" / "fused_ar_norm_nf.cu"
         if not src.exists():
             raise RuntimeError(f"reference source not present at {src}")
-        bdir = ROOT / "baseline" / "_ref_build"
+        bdir = BASE / "_ref_build"
         bdir.mkdir(parents=True, exist_ok=True)
         self.ext = load(name="ref_m17nf_fused_ar_norm", sources=[str(src)],
                         extra_cuda_cflags=["-O3", "-gencode=arch=compute_100a,code=sm_100a"],

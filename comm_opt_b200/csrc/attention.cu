@@ -11,6 +11,8 @@
 // KV layout: [num_blocks, nkv, 16, D] (one 4 KB contiguous page per head at D = 128, bf16).
 #include <float.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "ops.h"
 #include "sm100.cuh"
@@ -18,6 +20,8 @@
 
 namespace cob {
 namespace {
+
+namespace cg = cooperative_groups;
 
 constexpr int kD = 128, kBS = 16, kWarps = 4, kRows = 16;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -101,7 +105,10 @@ __host__ __device__ constexpr size_t attn_smem_bytes() {
          (size_t)kWarps * kStages * 8 + kMaxPagesPerSplit * 4 + 64;
 }
 
-template <typename T>
+// CLUSTER: the splits of one (sequence, kv head) pair form a thread-block cluster (splits <= 8) and
+// are merged through distributed shared memory; otherwise they are merged through the global
+// scratch by the last split to finish.
+template <typename T, bool CLUSTER>
 __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_constant__ AttnArgs args) {
   using namespace sm100;
   const AttnParams& p = args.p;
@@ -273,8 +280,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   __syncthreads();
   T* out = reinterpret_cast<T*>(p.out) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
   const size_t pair = (size_t)b * p.nkv + kvh;
-  float* po = p.part_o + (pair * p.splits + split) * (size_t)G * kD;
-  float* pml = p.part_ml + (pair * p.splits + split) * (size_t)G * 2;
+  // cluster mode: this CTA's merged partial stays in shared memory for its cluster peers
+  float* cO = sML + kWarps * kRows * 2;  // [G][kD]
+  float* cML = cO + kRows * kD;          // [G][2]
+  float* po = CLUSTER ? cO : p.part_o + (pair * p.splits + split) * (size_t)G * kD;
+  float* pml = CLUSTER ? cML : p.part_ml + (pair * p.splits + split) * (size_t)G * 2;
   for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
     const int g = idx / kD, d = idx - g * kD;
     float M = -INFINITY;
@@ -298,6 +308,27 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     }
   }
   if (p.splits == 1) return;
+  if (CLUSTER) {
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const int cs = p.splits, r = split;  // cluster spans the splits of this pair
+    const int per = (G * kD + cs - 1) / cs;
+    for (int idx = r * per + threadIdx.x; idx < min(G * kD, (r + 1) * per); idx += blockDim.x) {
+      const int g = idx / kD;
+      float M = -INFINITY;
+      for (int c = 0; c < cs; ++c) M = fmaxf(M, cluster.map_shared_rank(cML, c)[g * 2]);
+      float L = 0.f, O = 0.f;
+      for (int c = 0; c < cs; ++c) {
+        const float* ml = cluster.map_shared_rank(cML, c);
+        const float f = safe_exp2_diff(ml[g * 2], M);
+        L += f * ml[g * 2 + 1];
+        O += f * cluster.map_shared_rank(cO, c)[idx];
+      }
+      out[idx] = from_f<T>(O / L);
+    }
+    cluster.sync();
+    return;
+  }
   // ---- the last split of this (sequence, head) pair merges all splits
   __threadfence();
   __syncthreads();
@@ -363,7 +394,8 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
       (size_t)p.splits * (p.nq / p.nkv) * 2 + kRows > (size_t)kWarps * kStages * 2 * kPageElems / 2 ||
       (p.dtype != kBF16 && p.dtype != kF16))
     return cudaErrorInvalidValue;
-  static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 <= kWarps * kStages * 2 * kPageElems * 2,
+  static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 + kRows * kD * 4 + kRows * 2 * 4 <=
+                    kWarps * kStages * 2 * kPageElems * 2,
                 "merge buffers must fit in the KV stages");
   AttnArgs a;
   a.p = p;
@@ -377,10 +409,31 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const size_t smem = attn_smem_bytes();
   const dim3 grid(p.splits, p.nkv, p.batch);
-  auto fn = bf16 ? k_decode_attn<__nv_bfloat16> : k_decode_attn<__half>;
+  const bool cluster = p.cluster && p.splits > 1 && p.splits <= 8;
+  auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true> : k_decode_attn<__nv_bfloat16, false>)
+                 : (cluster ? k_decode_attn<__half, true> : k_decode_attn<__half, false>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  return launch_k(fn, grid, dim3(kWarps * 32), smem, s, a);
+  if (!cluster) return launch_k(fn, grid, dim3(kWarps * 32), smem, s, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  int na = 1;
+  if (pdl_flag()) {
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
 }  // namespace cob

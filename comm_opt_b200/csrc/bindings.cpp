@@ -5,11 +5,17 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "check.h"
+
 #include <vector>
 
 #include "fused_ar.h"
 #include "ops.h"
 #include "types.h"
+
+namespace cob {
+void fail(const std::string& m) { throw std::runtime_error(m); }
+}  // namespace cob
 
 namespace {
 
@@ -21,7 +27,7 @@ std::vector<int64_t> layout_to_vec(const Layout& L) {
 }
 
 Layout vec_to_layout(const std::vector<int64_t>& v) {
-  TORCH_CHECK(v.size() == 18, "layout must have 18 fields");
+  COB_CHECK(v.size() == 18, "layout must have 18 fields");
   Layout L;
   L.state = v[0];
   L.flags = v[1];
@@ -49,19 +55,19 @@ int dtype_code(const torch::Tensor& t) {
     case torch::kFloat: return cob::kF32;
     case torch::kHalf: return cob::kF16;
     case torch::kBFloat16: return cob::kBF16;
-    default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+    default: COB_CHECK(false, "unsupported dtype ", std::string(c10::toString(t.scalar_type())));
   }
   return -1;
 }
 
 void check_cuda(cudaError_t e, const char* what) {
-  TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
+  COB_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e));
 }
 
 void check_dense(const torch::Tensor& t, const char* name) {
-  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
-  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+  COB_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  COB_CHECK(t.is_contiguous(), name, " must be contiguous");
+  COB_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
 }
 
 std::vector<int64_t> py_plan_layout(int64_t world, int64_t max_rows, int64_t max_hidden, int64_t esize,
@@ -72,7 +78,7 @@ std::vector<int64_t> py_plan_layout(int64_t world, int64_t max_rows, int64_t max
 void py_init_heap(torch::Tensor heap, std::vector<int64_t> layout, int64_t dtype) {
   check_dense(heap, "heap");
   const Layout L = vec_to_layout(layout);
-  TORCH_CHECK(heap.numel() * heap.element_size() >= L.total, "heap smaller than layout");
+  COB_CHECK(heap.numel() * heap.element_size() >= L.total, "heap smaller than layout");
   const c10::cuda::CUDAGuard g(heap.device());
   check_cuda(cob::init_heap(reinterpret_cast<char*>(heap.data_ptr()), L, (int)dtype,
                             at::cuda::getCurrentCUDAStream()),
@@ -88,17 +94,17 @@ std::vector<int64_t> py_fused_ar(std::vector<int64_t> bases, int64_t mc, std::ve
                                  int64_t norm, int64_t timeout_ns, int64_t x_rs, int64_t res_rs, int64_t out_rs,
                                  bool dry_run) {
   cob::ARParams p = {};
-  TORCH_CHECK(bases.size() >= 2 && bases.size() <= cob::kMaxWorld, "world must be 2..8");
+  COB_CHECK(bases.size() >= 2 && bases.size() <= cob::kMaxWorld, "world must be 2..8");
   for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
   p.mc = reinterpret_cast<char*>(mc);
   p.L = vec_to_layout(layout);
   check_dense(x, "x");
   check_dense(out, "out");
-  TORCH_CHECK(out.scalar_type() == x.scalar_type(), "out dtype must match x");
+  COB_CHECK(out.scalar_type() == x.scalar_type(), "out dtype must match x");
   if (norm) {
     check_dense(residual, "residual");
     check_dense(gamma, "gamma");
-    TORCH_CHECK(residual.scalar_type() == x.scalar_type() && gamma.scalar_type() == x.scalar_type(),
+    COB_CHECK(residual.scalar_type() == x.scalar_type() && gamma.scalar_type() == x.scalar_type(),
                 "x, residual and gamma must share a dtype");
     p.residual = residual.data_ptr();
     p.gamma = gamma.data_ptr();
@@ -122,10 +128,10 @@ std::vector<int64_t> py_fused_ar(std::vector<int64_t> bases, int64_t mc, std::ve
   p.norm = (int)norm;
   p.dtype = dtype_code(x);
   p.timeout_ns = (unsigned long long)timeout_ns;
-  TORCH_CHECK(p.L.world == p.world, "layout world ", p.L.world, " != ", p.world);
-  TORCH_CHECK(p.L.esize == (int)x.element_size(), "communicator dtype size ", p.L.esize, " != input ",
+  COB_CHECK(p.L.world == p.world, "layout world ", p.L.world, " != ", p.world);
+  COB_CHECK(p.L.esize == (int)x.element_size(), "communicator dtype size ", p.L.esize, " != input ",
               x.element_size());
-  TORCH_CHECK(p.variant >= 1 && p.variant < cob::kNumVariants, "variant must be resolved by the caller");
+  COB_CHECK(p.variant >= 1 && p.variant < cob::kNumVariants, "variant must be resolved by the caller");
   const c10::cuda::CUDAGuard g(x.device());
   int sms = 0;
   check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index()), "sm count");
@@ -142,7 +148,7 @@ void py_allgather_u32(std::vector<int64_t> bases, std::vector<int64_t> layout, t
   p.L = vec_to_layout(layout);
   check_dense(in, "in");
   check_dense(out, "out");
-  TORCH_CHECK(in.element_size() == 4 && out.element_size() == 4, "32-bit words only");
+  COB_CHECK(in.element_size() == 4 && out.element_size() == 4, "32-bit words only");
   p.in = reinterpret_cast<const uint32_t*>(in.data_ptr());
   p.out = reinterpret_cast<uint32_t*>(out.data_ptr());
   p.in_rs = in_rs;

@@ -4,11 +4,13 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "check.h"
+
 #include <cstring>
 
 namespace {
 
-void ok(cudaError_t e, const char* what) { TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
+void ok(cudaError_t e, const char* what) { COB_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
 
 // Device allocation owned by the returned uint8 tensor (freed with cudaFree when it dies).
 torch::Tensor ipc_alloc(int64_t bytes, int64_t device) {
@@ -29,7 +31,7 @@ pybind11::bytes ipc_handle(torch::Tensor heap) {
 
 int64_t ipc_open(pybind11::bytes handle, int64_t device) {
   const std::string s = handle;
-  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  COB_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
   cudaIpcMemHandle_t h;
   std::memcpy(&h, s.data(), sizeof(h));
   const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);

@@ -49,6 +49,7 @@ struct AttnParams {
   int dtype;
   int num_blocks;            // rows of the caches / (nkv * block); 0 = unknown
   int* err;                  // optional: set to 1 if a bounded wait gave up
+  int cluster;               // 1: merge splits (<= 8) inside a thread-block cluster, no scratch used
 };
 // bytes of scratch needed for a given geometry
 size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_dim);

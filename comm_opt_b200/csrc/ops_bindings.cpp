@@ -3,6 +3,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "check.h"
+
 #include "common_host.h"
 #include "gemm.h"
 #include "ops.h"
@@ -15,16 +17,16 @@ int code_of(const torch::Tensor& t) {
     case torch::kFloat: return cob::kF32;
     case torch::kHalf: return cob::kF16;
     case torch::kBFloat16: return cob::kBF16;
-    default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+    default: COB_CHECK(false, "unsupported dtype ", std::string(c10::toString(t.scalar_type())));
   }
   return -1;
 }
 
-void ok(cudaError_t e, const char* what) { TORCH_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
+void ok(cudaError_t e, const char* what) { COB_CHECK(e == cudaSuccess, what, ": ", cudaGetErrorString(e)); }
 
 void dense(const torch::Tensor& t, const char* n) {
-  TORCH_CHECK(t.is_cuda() && t.is_contiguous(), n, " must be a contiguous CUDA tensor");
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, n, " must be 16-byte aligned");
+  COB_CHECK(t.is_cuda() && t.is_contiguous(), n, " must be a contiguous CUDA tensor");
+  COB_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, n, " must be 16-byte aligned");
 }
 
 cudaStream_t cur() { return at::cuda::getCurrentCUDAStream(); }
@@ -56,7 +58,7 @@ void py_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
   dense(ids, "ids");
   dense(table, "table");
   dense(out, "out");
-  TORCH_CHECK(ids.scalar_type() == torch::kInt32, "ids must be int32");
+  COB_CHECK(ids.scalar_type() == torch::kInt32, "ids must be int32");
   const c10::cuda::CUDAGuard g(ids.device());
   ok(cob::embedding(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), (int)ids.numel(),
                     (int)table.size(1), code_of(table), cur()),
@@ -67,7 +69,7 @@ void py_rope_append_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor
                        torch::Tensor block_tables, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
                        int64_t nq, int64_t nkv) {
   for (auto* t : {&qkv, &positions, &cos_t, &sin_t, &block_tables, &q_out, &k_cache, &v_cache}) dense(*t, "arg");
-  TORCH_CHECK(positions.scalar_type() == torch::kInt32 && block_tables.scalar_type() == torch::kInt32,
+  COB_CHECK(positions.scalar_type() == torch::kInt32 && block_tables.scalar_type() == torch::kInt32,
               "positions and block_tables must be int32");
   const c10::cuda::CUDAGuard g(qkv.device());
   const int D = (int)k_cache.size(3), bs = (int)k_cache.size(2);
@@ -90,7 +92,7 @@ void py_silu_mul(torch::Tensor gu, torch::Tensor out) {
 void py_argmax_local(torch::Tensor logits, torch::Tensor keys, int64_t vocab_offset) {
   dense(logits, "logits");
   dense(keys, "keys");
-  TORCH_CHECK(keys.scalar_type() == torch::kInt64 && keys.numel() == logits.size(0), "keys must be int64 [rows]");
+  COB_CHECK(keys.scalar_type() == torch::kInt64 && keys.numel() == logits.size(0), "keys must be int64 [rows]");
   const c10::cuda::CUDAGuard g(logits.device());
   ok(cob::argmax_local(logits.data_ptr(), reinterpret_cast<unsigned long long*>(keys.data_ptr()), (int)logits.size(0),
                        (int)logits.size(1), (int)vocab_offset, code_of(logits), cur()),
@@ -101,21 +103,21 @@ void py_argmax_combine(torch::Tensor gathered, torch::Tensor ids, int64_t world,
                        c10::optional<torch::Tensor> seq_lens, c10::optional<torch::Tensor> local_keys) {
   dense(gathered, "gathered");
   dense(ids, "ids");
-  TORCH_CHECK(gathered.scalar_type() == torch::kInt64 && gathered.numel() == world * ids.numel(),
+  COB_CHECK(gathered.scalar_type() == torch::kInt64 && gathered.numel() == world * ids.numel(),
               "gathered must be int64 [world, rows]");
   int32_t* pos = nullptr;
   int32_t* lens = nullptr;
   unsigned long long* lk = nullptr;
   if (positions.has_value()) {
-    TORCH_CHECK(positions->scalar_type() == torch::kInt32 && positions->numel() == ids.numel(), "positions");
+    COB_CHECK(positions->scalar_type() == torch::kInt32 && positions->numel() == ids.numel(), "positions");
     pos = positions->data_ptr<int32_t>();
   }
   if (seq_lens.has_value()) {
-    TORCH_CHECK(seq_lens->scalar_type() == torch::kInt32 && seq_lens->numel() == ids.numel(), "seq_lens");
+    COB_CHECK(seq_lens->scalar_type() == torch::kInt32 && seq_lens->numel() == ids.numel(), "seq_lens");
     lens = seq_lens->data_ptr<int32_t>();
   }
   if (local_keys.has_value()) {
-    TORCH_CHECK(local_keys->scalar_type() == torch::kInt64 && local_keys->numel() == ids.numel(), "local_keys");
+    COB_CHECK(local_keys->scalar_type() == torch::kInt64 && local_keys->numel() == ids.numel(), "local_keys");
     lk = reinterpret_cast<unsigned long long*>(local_keys->data_ptr());
   }
   const c10::cuda::CUDAGuard g(gathered.device());
@@ -132,9 +134,9 @@ int64_t py_attn_scratch_bytes(int64_t batch, int64_t nkv, int64_t splits, int64_
 // first call (the kernel leaves it zero).
 void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                          torch::Tensor seq_lens, torch::Tensor out, torch::Tensor scratch, int64_t splits,
-                         int64_t pages_per_split, double scale) {
+                         int64_t pages_per_split, double scale, bool cluster) {
   for (auto* t : {&q, &k_cache, &v_cache, &block_tables, &seq_lens, &out, &scratch}) dense(*t, "arg");
-  TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && seq_lens.scalar_type() == torch::kInt32,
+  COB_CHECK(block_tables.scalar_type() == torch::kInt32 && seq_lens.scalar_type() == torch::kInt32,
               "block_tables and seq_lens must be int32");
   cob::AttnParams p = {};
   p.batch = (int)q.size(0);
@@ -149,7 +151,7 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
   p.dtype = code_of(q);
   const int group = p.nq / p.nkv;
   const size_t need = cob::attn_scratch_bytes(p.batch, p.nkv, p.splits, group, p.head_dim);
-  TORCH_CHECK((size_t)scratch.numel() * scratch.element_size() >= need, "attention scratch too small: need ", need);
+  COB_CHECK((size_t)scratch.numel() * scratch.element_size() >= need, "attention scratch too small: need ", need);
   const size_t pairs = (size_t)p.batch * p.nkv;
   char* base = reinterpret_cast<char*>(scratch.data_ptr());
   p.part_o = reinterpret_cast<float*>(base);
@@ -164,6 +166,7 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
   p.out = out.data_ptr();
   p.num_blocks = (int)k_cache.size(0);
   p.err = nullptr;
+  p.cluster = cluster ? 1 : 0;
   const c10::cuda::CUDAGuard g(q.device());
   ok(cob::paged_decode_attention(p, cur()), "paged_decode_attention");
 }
@@ -176,12 +179,12 @@ std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, 
   dense(x, "x");
   dense(w, "w");
   dense(err, "err");
-  TORCH_CHECK(y.is_cuda() && y.stride(-1) == 1, "y must be row-major");
-  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
-  TORCH_CHECK(y.size(0) == x.size(0) && y.size(1) == w.size(0), "y must be [M, N]");
-  TORCH_CHECK(x.scalar_type() == w.scalar_type() && y.scalar_type() == x.scalar_type(), "dtypes must match");
-  TORCH_CHECK(err.scalar_type() == torch::kInt32 && ctr.scalar_type() == torch::kInt32, "err, ctr must be int32");
-  TORCH_CHECK(ws.scalar_type() == torch::kFloat && ws.is_cuda() && ctr.is_cuda(), "ws must be float32 CUDA");
+  COB_CHECK(y.is_cuda() && y.stride(-1) == 1, "y must be row-major");
+  COB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
+  COB_CHECK(y.size(0) == x.size(0) && y.size(1) == w.size(0), "y must be [M, N]");
+  COB_CHECK(x.scalar_type() == w.scalar_type() && y.scalar_type() == x.scalar_type(), "dtypes must match");
+  COB_CHECK(err.scalar_type() == torch::kInt32 && ctr.scalar_type() == torch::kInt32, "err, ctr must be int32");
+  COB_CHECK(ws.scalar_type() == torch::kFloat && ws.is_cuda() && ctr.is_cuda(), "ws must be float32 CUDA");
   const c10::cuda::CUDAGuard g(x.device());
   static int sms = 0;
   if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());

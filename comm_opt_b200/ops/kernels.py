@@ -64,27 +64,33 @@ def argmax_combine(gathered: torch.Tensor, world: int, ids: torch.Tensor | None 
 ATTN_CTAS_PER_SM = 2  # the kernel's shared memory (~106 KB) allows two resident CTAs per SM
 
 
-def attention_split_plan(batch: int, nkv: int, max_pages: int, num_sms: int = 148) -> tuple[int, int]:
-    """Split-KV geometry: as many CTAs over (batch, kv head, split) as fit in ONE wave of resident CTAs
-    (a partial second wave would double the kernel time)."""
+def attention_split_plan(batch: int, nkv: int, max_pages: int, num_sms: int = 148) -> tuple[int, int, bool]:
+    """Split-KV geometry (splits, pages per split, cluster merge).
+
+    As many CTAs over (batch, kv head, split) as fit in ONE wave of resident CTAs (a partial second
+    wave would double the kernel time). When that needs at most 8 splits per pair, or 8 splits leave
+    each CTA a modest number of pages, the splits of a pair form a cluster and merge through
+    distributed shared memory; long contexts with few pairs use more splits and the global merge."""
     pairs = max(1, batch * nkv)
     slots = ATTN_CTAS_PER_SM * num_sms
     splits = max(1, min(max_pages, slots // pairs))
+    if splits > 8 and (max_pages + 7) // 8 <= 32:
+        splits = 8
     pps = min(512, (max_pages + splits - 1) // splits)
     splits = (max_pages + pps - 1) // pps
-    return splits, pps
+    return splits, pps, 1 < splits <= 8
 
 
 class DecodeAttention:
     """Paged GQA decode attention with its own split-KV scratch (allocated once, graph-safe)."""
 
     def __init__(self, batch: int, nq: int, nkv: int, head_dim: int, max_pages: int, device, num_sms: int = 148):
-        self.splits, self.pps = attention_split_plan(batch, nkv, max_pages, num_sms)
+        self.splits, self.pps, self.cluster = attention_split_plan(batch, nkv, max_pages, num_sms)
         self.batch, self.nq, self.nkv, self.head_dim = batch, nq, nkv, head_dim
         nbytes = native().attn_scratch_bytes(batch, nkv, self.splits, nq // nkv, head_dim)
         self.scratch = torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
     def __call__(self, q, k_cache, v_cache, block_tables, seq_lens, out, scale: float):
         native().decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, self.scratch, self.splits,
-                                  self.pps, float(scale))
+                                  self.pps, float(scale), self.cluster)
         return out

@@ -93,10 +93,22 @@ def test_decode_attention(cuda, nq, nkv, dtype):
     q = torch.randn(B, nq, D, device=cuda).to(dtype)
     scale = 1 / math.sqrt(D)
     ref = paged_attention_ref(q, kc, vc, bt, seq, scale)
-    for num_sms in (148, 1):  # many splits (in-kernel combine) and a single split
+    for num_sms in (148, 8, 1):  # global split merge, cluster (DSMEM) merge, single split
         attn = K.DecodeAttention(B, nq, nkv, D, maxb, cuda, num_sms=num_sms)
         out = torch.empty_like(q)
         for _ in range(2):  # second call checks the split counters were reset
             attn(q, kc, vc, bt, seq, out, scale)
             torch.cuda.synchronize()
-            assert rel_err(out, ref) <= 2 ** -7, (num_sms, rel_err(out, ref))
+            assert rel_err(out, ref) <= 2 ** -7, (num_sms, attn.splits, attn.cluster, rel_err(out, ref))
+    for splits, cl in [(2, True), (3, True), (5, True), (8, True), (40, False), (13, False)]:
+        attn = K.DecodeAttention(B, nq, nkv, D, maxb, cuda)  # cluster merge for <= 8 splits, global above
+        attn.splits, attn.pps, attn.cluster = splits, -(-maxb // splits), cl
+        attn.splits = -(-maxb // attn.pps)
+        from comm_opt_b200._ext import native
+
+        attn.scratch = torch.zeros(native().attn_scratch_bytes(B, nkv, attn.splits, nq // nkv, D), dtype=torch.uint8,
+                                   device=cuda)
+        out = torch.empty_like(q)
+        attn(q, kc, vc, bt, seq, out, scale)
+        torch.cuda.synchronize()
+        assert rel_err(out, ref) <= 2 ** -7, (splits, rel_err(out, ref))
