@@ -1,0 +1,127 @@
+"""Experiment runner: independent launches in a randomised, recorded order (the reference's
+exp/lib/ncclrun.py:18-106 - Job, GPU sets, "no other GPU processes" guard, env snapshot, schedule.tsv,
+DRY_RUN), driving this repository's torchrun entry points instead of nccl-tests binaries.
+
+    from comm_opt_b200.harness.runner import Job, run_all
+    jobs = [Job("collectives", 8, rep=r, args=("--colls", "all_reduce")) for r in range(3)]
+    run_all(jobs, "collective_baseline", seed=0)        # DRY_RUN=1 only prints the commands
+"""
+from __future__ import annotations
+
+import os
+import random
+import shlex
+import subprocess
+import sys
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+
+from ..utils.results import ROOT, RunDir, gpu_state
+
+ENTRY = {
+    "collectives": "comm_opt_b200.harness.collectives",
+    "fused_sweep": "comm_opt_b200.harness.fused_sweep",
+    "selftest": "comm_opt_b200.harness.mp_selftest",
+}
+
+GPUSETS = {  # set A: first GPUs; set B: other physical GPUs / rank order (the reference's second set)
+    1: {"A": "0", "B": "7"},
+    2: {"A": "0,1", "B": "6,7"},
+    4: {"A": "0,1,2,3", "B": "4,5,6,7"},
+    8: {"A": "0,1,2,3,4,5,6,7", "B": "0,2,4,6,1,3,5,7"},
+}
+
+
+@dataclass
+class Job:
+    entry: str
+    ngpus: int
+    gpuset: str = "A"
+    rep: int = 0
+    variant: str = "default"
+    env: dict = field(default_factory=dict)
+    args: tuple = ()
+    timeout_s: int = 1500
+
+    @property
+    def tag(self) -> str:
+        return f"{self.entry}_g{self.ngpus}{self.gpuset}_{self.variant}_r{self.rep}"
+
+
+def gpu_processes() -> str:
+    """Compute processes on the GPUs that are not ours (the reference's rule: do not measure next to others)."""
+    try:
+        out = subprocess.run(["nvidia-smi", "--query-compute-apps=pid,process_name,used_memory",
+                              "--format=csv,noheader"], capture_output=True, text=True, timeout=30).stdout
+    except (OSError, subprocess.TimeoutExpired):
+        return ""
+    return "\n".join(l for l in out.splitlines() if l.strip())
+
+
+def command(job: Job, out: Path, port: int) -> tuple[list[str], dict]:
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES=GPUSETS[job.ngpus][job.gpuset], **job.env)
+    cmd = ["timeout", "-k", "60", str(job.timeout_s), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={job.ngpus}", "--master-addr=127.0.0.1", f"--master-port={port}", "-m",
+           ENTRY[job.entry], *job.args]
+    if job.entry == "collectives":
+        cmd += ["--out", str(out / f"{job.tag}.json")]
+    elif job.entry == "fused_sweep":
+        cmd += ["--out-dir", str(out / "runs"), "--ts", job.tag]
+    return cmd, env
+
+
+def run_all(jobs: list[Job], name: str, seed: int, base: Path | None = None) -> Path | None:
+    dry = bool(os.environ.get("DRY_RUN"))
+    jobs = list(jobs)
+    random.Random(seed).shuffle(jobs)
+    if dry:
+        for i, j in enumerate(jobs):
+            cmd, _ = command(j, Path("results") / name / "DRY", 29700 + i)
+            print(shlex.join(cmd))
+        print(f"{len(jobs)} jobs, seed {seed}", file=sys.stderr)
+        return None
+    if procs := gpu_processes():
+        sys.exit(f"GPUs have running processes; not measuring:\n{procs}")
+    run = RunDir(name, base)
+    run.snapshot()
+    (run.path / "seed.txt").write_text(f"{seed}\n")
+    for i, j in enumerate(jobs):
+        if run.done(f"{j.tag}.log"):
+            continue  # resume: this job already ran in this directory
+        if procs := gpu_processes():
+            sys.exit(f"stopped before job {i}: other GPU processes appeared:\n{procs}")
+        state, t0 = gpu_state(), time.time()
+        cmd, env = command(j, run.path, 29700 + i % 100)
+        with open(run.path / f"{j.tag}.log", "w") as log:
+            rc = subprocess.run(cmd, stdout=log, stderr=subprocess.STDOUT, env=env, cwd=ROOT).returncode
+        run.schedule(i, j.tag, t0, time.time() - t0, rc, state, env=j.env, variant=j.variant, ngpus=j.ngpus)
+        print(f"[{i + 1}/{len(jobs)}] {j.tag} rc={rc} {time.time() - t0:.1f}s", file=sys.stderr, flush=True)
+    return run.path
+
+
+def collective_baseline_jobs(gpus=(2, 4, 8), reps: int = 1) -> list[Job]:
+    """The M0 baseline: six collectives x sizes x GPU counts, graph mode as nccl-tests -G 20."""
+    return [Job("collectives", g, rep=r, args=("--begin", "8", "--end", "256M", "--graph", "20")) for g in gpus
+            for r in range(reps)]
+
+
+def nccl_variant_jobs(ngpus: int = 8) -> list[Job]:
+    """The M7 "where slow" idea on NCCL knobs available here: algorithm / protocol / NVLS on and off."""
+    variants = {"default": {}, "nvls_off": {"NCCL_NVLS_ENABLE": "0"}, "ll": {"NCCL_PROTO": "LL"},
+                "ll128": {"NCCL_PROTO": "LL128"}, "ring": {"NCCL_ALGO": "Ring"}, "tree": {"NCCL_ALGO": "Tree"}}
+    return [Job("collectives", ngpus, variant=k, env=v, args=("--colls", "all_reduce", "--begin", "1K", "--end", "8M",
+                                                               "--graph", "20")) for k, v in variants.items()]
+
+
+if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants"])
+    ap.add_argument("--gpus", default="2,4,8")
+    ap.add_argument("--seed", type=int, default=0)
+    a = ap.parse_args()
+    gp = tuple(int(g) for g in a.gpus.split(","))
+    jobs = collective_baseline_jobs(gp) if a.plan == "collective_baseline" else nccl_variant_jobs(max(gp))
+    print(run_all(jobs, a.plan, a.seed))

@@ -1,0 +1,50 @@
+"""Harness pieces on CPU: collective sweep over gloo, runner dry run, loaders and statistics."""
+import json
+import os
+import subprocess
+import sys
+
+from conftest import ROOT, free_port
+
+
+def test_collectives_gloo_two_ranks(tmp_path):
+    out = tmp_path / "c.json"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={free_port()}", "-m", "comm_opt_b200.harness.collectives",
+           "--device", "cpu", "--begin", "64", "--end", "4K", "--iters", "3", "--warmup", "1", "--out", str(out)]
+    p = subprocess.run(["timeout", "-k", "10", "240"] + cmd, cwd=ROOT, capture_output=True, text=True)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    doc = json.loads(out.read_text())
+    colls = {r["coll"] for r in doc["results"]}
+    assert colls == {"all_reduce", "all_gather", "reduce_scatter", "alltoall", "broadcast", "sendrecv"}
+    assert all(r["nwrong"] == 0 for r in doc["results"])
+    ar = [r for r in doc["results"] if r["coll"] == "all_reduce"]
+    assert all(abs(r["busbw"] - r["algbw"] * 2 * (2 - 1) / 2) < 1e-9 for r in ar)
+
+
+def test_runner_dry_run_prints_commands():
+    env = dict(os.environ, DRY_RUN="1")
+    code = ("from comm_opt_b200.harness.runner import *; run_all(collective_baseline_jobs((2, 8)), 'x', 3);"
+            "run_all(nccl_variant_jobs(8), 'y', 4)")
+    p = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True)
+    assert p.returncode == 0, p.stderr
+    lines = [l for l in p.stdout.splitlines() if "torch.distributed.run" in l]
+    assert len(lines) == 2 + 6 and all("127.0.0.1" in l and "timeout" in l for l in lines)
+
+
+def test_collective_loader_and_bound(tmp_path):
+    from comm_opt_b200.harness.collective_analysis import achievable_us, fit_bound, load_run, summarize
+    from comm_opt_b200.utils.stats import disjoint
+
+    for rep in range(3):
+        doc = dict(results=[dict(coll="all_reduce", world=8, size=s, p50_us=5.0 + s / 1e5 + rep, busbw=s / 1e4 + rep,
+                                 time_us=1.0) for s in (1024, 1 << 20)])
+        (tmp_path / f"j{rep}.json").write_text(json.dumps(doc))
+    rows = load_run(tmp_path)
+    assert len(rows) == 6
+    s = summarize(rows, ("coll", "world", "size"), "p50_us")
+    m = s[("all_reduce", 8, 1024)]
+    assert m["n"] == 3 and m["lo"] <= m["med"] <= m["hi"]
+    assert not disjoint(s[("all_reduce", 8, 1024)], s[("all_reduce", 8, 1024)])
+    l0, bw = fit_bound(rows)
+    assert achievable_us(1 << 20, 8, l0, bw) > l0
