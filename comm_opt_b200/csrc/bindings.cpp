@@ -92,7 +92,7 @@ std::vector<int64_t> py_fused_ar(std::vector<int64_t> bases, int64_t mc, std::ve
                                  int64_t rank, int64_t rows, int64_t hidden, double eps, int64_t variant,
                                  int64_t blocks, int64_t threads, int64_t cluster, int64_t emulate, int64_t pdl,
                                  int64_t norm, int64_t timeout_ns, int64_t x_rs, int64_t res_rs, int64_t out_rs,
-                                 bool dry_run) {
+                                 bool dry_run, c10::optional<torch::Tensor> stamps) {
   cob::ARParams p = {};
   COB_CHECK(bases.size() >= 2 && bases.size() <= cob::kMaxWorld, "world must be 2..8");
   for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
@@ -128,6 +128,13 @@ std::vector<int64_t> py_fused_ar(std::vector<int64_t> bases, int64_t mc, std::ve
   p.norm = (int)norm;
   p.dtype = dtype_code(x);
   p.timeout_ns = (unsigned long long)timeout_ns;
+  if (stamps.has_value()) {
+    COB_CHECK(stamps->is_cuda() && stamps->scalar_type() == torch::kInt64 && stamps->dim() == 4 &&
+                  stamps->size(2) == cob::kMaxBlocks && stamps->size(3) == cob::kStampPhases,
+              "stamps must be int64 [ranks, cap, kMaxBlocks, kStampPhases]");
+    p.stamps = reinterpret_cast<long long*>(stamps->data_ptr());
+    p.stamp_cap = (int)stamps->size(1);
+  }
   COB_CHECK(p.L.world == p.world, "layout world ", p.L.world, " != ", p.world);
   COB_CHECK(p.L.esize == (int)x.element_size(), "communicator dtype size ", p.L.esize, " != input ",
               x.element_size());
@@ -171,7 +178,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "comm_opt_b200 native kernels (sm_100a)";
   m.def("plan_layout", &py_plan_layout);
   m.def("init_heap", &py_init_heap);
-  m.def("fused_ar", &py_fused_ar);
+  m.def("fused_ar", &py_fused_ar, pybind11::arg("bases"), pybind11::arg("mc"), pybind11::arg("layout"),
+        pybind11::arg("x"), pybind11::arg("residual"), pybind11::arg("gamma"), pybind11::arg("out"),
+        pybind11::arg("rank"), pybind11::arg("rows"), pybind11::arg("hidden"), pybind11::arg("eps"),
+        pybind11::arg("variant"), pybind11::arg("blocks"), pybind11::arg("threads"), pybind11::arg("cluster"),
+        pybind11::arg("emulate"), pybind11::arg("pdl"), pybind11::arg("norm"), pybind11::arg("timeout_ns"),
+        pybind11::arg("x_rs"), pybind11::arg("res_rs"), pybind11::arg("out_rs"), pybind11::arg("dry_run"),
+        pybind11::arg("stamps") = pybind11::none());
+  m.attr("kStampPhases") = cob::kStampPhases;
   m.def("allgather_u32", &py_allgather_u32);
   m.attr("kMaxBlocks") = cob::kMaxBlocks;
   m.attr("kMaxWorld") = cob::kMaxWorld;

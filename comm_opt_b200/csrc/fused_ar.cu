@@ -73,6 +73,15 @@ __device__ void record_error(RankState* st, uint32_t bit, uint64_t variant_phase
   }
 }
 
+// Phase stamp of this block (thread 0) when stamping is enabled.
+__device__ __forceinline__ void stamp(const ARParams& p, int rank, uint64_t e, int phase) {
+  if (p.stamps != nullptr && threadIdx.x == 0) {
+    const size_t i = (((size_t)rank * p.stamp_cap + (size_t)(e % (uint64_t)p.stamp_cap)) * kMaxBlocks + blockIdx.x) *
+                         kStampPhases + phase;
+    p.stamps[i] = (long long)globaltimer();
+  }
+}
+
 // Last block of this rank's call advances the epoch (M16 rule: every block reads the same epoch at
 // start; the count of finished blocks, not the block index, decides who advances it).
 __device__ __forceinline__ void finish_call(RankState* st, uint64_t e, int blocks_per_rank) {
@@ -197,6 +206,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   const int slot = (int)(e & 1);
   Waiter w(p.timeout_ns, &st->error);
   bool ok = true;
+  stamp(p, rank, e, 0);
 
   if (MODE == kLamport1S) {
     for (int row = cl; row < p.rows; row += ncl) {
@@ -231,7 +241,9 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
       ok = nvls_barrier(p, rank, st, 0, nc, w);
       if (tid == 0) st->nvls_calls[blockIdx.x][0] = nc;
     }
+    stamp(p, rank, e, 2);
   }
+  stamp(p, rank, e, 1);
   pdl_trigger();
 
   int it = 0;
@@ -302,7 +314,9 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
       if (v < v1) store_norm<T>(p, out, res, row, v, h[k], hb[k], rstd);
     }
   }
+  stamp(p, rank, e, 3);
   if (C > 1) cg::this_cluster().sync();  // no CTA leaves while a peer CTA may read its shared memory
+  stamp(p, rank, e, 4);
   finish_call(st, e, gridDim.x);
 }
 
@@ -337,6 +351,7 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
   const uint32_t etag = (uint32_t)e;
   Waiter w(p.timeout_ns, &st->error);
   bool ok = true;
+  stamp(p, rank, e, 0);
 
   // ---- phase 1
   if (MODE == kLamport2S) {
@@ -365,6 +380,7 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
       if (tid == 0) st->nvls_calls[blockIdx.x][0] = nc;
     }
   }
+  stamp(p, rank, e, 1);
   pdl_trigger();
 
   // ---- phase 2: owned slice of this block's rows
@@ -439,6 +455,7 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
     }
   }
 
+  stamp(p, rank, e, 2);
   if (MODE == kNvls2S) {
     __threadfence_system();
     __syncthreads();
@@ -509,6 +526,8 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
       }
     }
   }
+  stamp(p, rank, e, 3);
+  stamp(p, rank, e, 4);
   finish_call(st, e, gridDim.x);
 }
 

@@ -77,7 +77,14 @@ struct ARParams {
   int variant, blocks, threads, cluster;
   int emulate, pdl, dtype, norm;   // norm == 0: plain all-reduce into `out`, residual untouched
   unsigned long long timeout_ns;
+  // Optional phase stamps (%globaltimer, ns): [rank][call % stamp_cap][kMaxBlocks][kStampPhases];
+  // nullptr = off. Phase 0 start, 1 inputs sent / staged, 2 barrier passed or owner slice reduced,
+  // 3 all data received, 4 block done.
+  long long* stamps;
+  int stamp_cap;
 };
+
+constexpr int kStampPhases = 5;
 
 Layout plan_layout(int world, int max_rows, int max_hidden, int esize, int max_gather);
 

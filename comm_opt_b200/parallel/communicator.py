@@ -90,6 +90,7 @@ class TPCommunicator:
             self._init_state()
         self.have_nvls = bool(self.heap and self.heap.mc and allow_nvls)
         self.last_choice: Choice | None = None
+        self.stamps: torch.Tensor | None = None
 
     # ------------------------------------------------------------------ state management
     def _host_barrier(self):
@@ -150,6 +151,34 @@ class TPCommunicator:
             c = Choice(v, blocks, threads, cluster)
         return c
 
+    # ------------------------------------------------------------------ phase stamps
+    PHASES = ("start", "sent", "reduced", "received", "done")
+
+    def enable_stamps(self, cap: int = 2048):
+        """Record %globaltimer at every phase boundary of every block of every call (ring of `cap` calls)."""
+        ranks = self.world if self.emulated else 1
+        self.stamps = torch.zeros(ranks, cap, native().kMaxBlocks, native().kStampPhases, dtype=torch.int64,
+                                  device=self.device)
+
+    def disable_stamps(self):
+        self.stamps = None
+
+    def stamp_summary(self, epochs: list[int], blocks: int) -> dict:
+        """Per phase, mean over the given calls of (latest block's stamp - earliest block's start) in us,
+        per local rank: the critical path of the call split into phases."""
+        st = self.stamps.cpu()
+        cap = st.shape[1]
+        out = {}
+        for r in range(st.shape[0]):
+            acc = {ph: 0.0 for ph in self.PHASES[1:]}
+            for e in epochs:
+                blk = st[r, e % cap, :blocks]
+                t0 = int(blk[:, 0].min())
+                for i, ph in enumerate(self.PHASES[1:], start=1):
+                    acc[ph] += (int(blk[:, i].max()) - t0) / 1000.0 / len(epochs)
+            out[r] = acc
+        return out
+
     # ------------------------------------------------------------------ ops
     def _shape(self, x: torch.Tensor) -> tuple[int, int]:
         hidden = x.shape[-1]
@@ -174,7 +203,7 @@ class TPCommunicator:
                 self.heap.bases, self.heap.mc, self._layout_list, x, residual if norm else x,
                 gamma if norm else x, out, self.rank, rows, hidden, float(eps), c.variant, c.blocks, c.threads,
                 c.cluster, int(self.emulated), int(self.pdl), int(norm), self.timeout_ns, stride, stride, stride,
-                dry_run)
+                dry_run, self.stamps)
         if rc != 0:
             raise TPCommError(f"fused_ar: unsupported configuration {VARIANT_NAMES.get(v, v)} rows={rows} "
                               f"hidden={hidden} world={self.world} blocks={b} threads={t} cluster={cl} "

@@ -170,3 +170,22 @@ def test_allgather_u32_emulated(cuda):
         comm.check()
         for r in range(4):
             assert torch.equal(out[r], inp)
+
+
+def test_phase_stamps_and_overhead(cuda):
+    """Stamped calls record ordered phase times for every block; outputs unchanged."""
+    comm = TPCommunicator(emulate_world=4, device=cuda, dtype=torch.bfloat16, max_rows=16, max_hidden=8192)
+    x, res0, gamma = make_inputs(4, 8, 8192, torch.bfloat16, cuda)
+    for v in EMU_VARIANTS:
+        comm.disable_stamps()
+        out_plain, _ = check(comm, x, res0, gamma, 1e-6, v)
+        comm.enable_stamps(cap=64)
+        out_st, _ = check(comm, x, res0, gamma, 1e-6, v)
+        assert torch.equal(out_plain, out_st)
+        e = comm.epochs()[0]
+        blocks = comm.last_choice.blocks
+        summ = comm.stamp_summary([e], blocks)
+        for r in range(4):
+            ph = summ[r]
+            assert 0 <= ph["sent"] <= ph["done"] and ph["received"] <= ph["done"] + 1e-3, (v, ph)
+    comm.disable_stamps()

@@ -48,3 +48,25 @@ def test_collective_loader_and_bound(tmp_path):
     assert not disjoint(s[("all_reduce", 8, 1024)], s[("all_reduce", 8, 1024)])
     l0, bw = fit_bound(rows)
     assert achievable_us(1 << 20, 8, l0, bw) > l0
+
+
+def test_trace_decomposition(tmp_path):
+    """Synthetic two-rank trace: comm kernel partly overlapped by compute; rank 1 waits longer."""
+    from comm_opt_b200.harness.traces import decompose
+
+    def trace(comm_dur):
+        ev = [dict(cat="gpu_user_annotation", name="decode_step", ts=0, dur=100),
+              dict(cat="kernel", name="k_gemm_streamk<16>", ts=0, dur=40),
+              dict(cat="kernel", name="void k_oneshot<bf16, 8, 1>", ts=30, dur=comm_dur),
+              dict(cat="kernel", name="k_decode_attn", ts=30 + comm_dur, dur=20)]
+        return dict(traceEvents=ev)
+
+    for r, d in enumerate((20, 30)):
+        (tmp_path / f"trace_rank{r}.json").write_text(json.dumps(trace(d)))
+    rows = decompose(sorted(tmp_path.glob("trace_rank*.json")), "decode_step")
+    r0 = next(r for r in rows if r["rank"] == 0)
+    assert abs(r0["overlap_us"] - 10) < 1e-6 and abs(r0["exposed_comm_us"] - 10) < 1e-6
+    assert abs(r0["compute_only_us"] - (40 - 10 + 20)) < 1e-6
+    assert abs(r0["idle_us"] - (100 - 70)) < 1e-6
+    r1 = next(r for r in rows if r["rank"] == 1)
+    assert r1["exposed_wait_us"] > 0 and abs(r1["exposed_transfer_us"] + r1["exposed_wait_us"] - r1["exposed_comm_us"]) < 1e-9
