@@ -8,6 +8,7 @@
 #include "common_host.h"
 #include "gemm.h"
 #include "ops.h"
+#include "probes.h"
 #include "types.h"
 
 namespace {
@@ -202,9 +203,41 @@ std::vector<int64_t> py_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t sms, 
   return {p.bn, p.tiles, p.ctas, (int64_t)cob::gemm_workspace_bytes(p.ctas, p.bn)};
 }
 
+void py_rs_atomic_probe(std::vector<int64_t> bases, int64_t acc_off, int64_t ctr_off, torch::Tensor x, int64_t rank,
+                        int64_t n, int64_t variant, int64_t emulate, int64_t x_rank_bytes, int64_t blocks,
+                        int64_t timeout_ns, torch::Tensor err) {
+  dense(x, "x");
+  COB_CHECK(bases.size() >= 1 && bases.size() <= 8, "world must be 1..8");
+  cob::RsProbeParams p = {};
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
+  p.acc_off = acc_off;
+  p.ctr_off = ctr_off;
+  p.x = x.data_ptr();
+  p.x_rank_bytes = x_rank_bytes;
+  p.rank = (int)rank;
+  p.world = (int)bases.size();
+  p.n = (int)n;
+  p.variant = (int)variant;
+  p.emulate = (int)emulate;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.err = err.data_ptr<int32_t>();
+  const c10::cuda::CUDAGuard g(x.device());
+  ok(cob::rs_atomic_probe(p, (int)blocks, cur()), "rs_atomic_probe");
+}
+
+std::vector<int64_t> py_clock_calibration(int64_t ns, int64_t device) {
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  auto out = torch::zeros({2}, torch::TensorOptions().dtype(torch::kInt64).device(torch::kCUDA, (c10::DeviceIndex)device));
+  ok(cob::clock_calibration((unsigned long long)ns, reinterpret_cast<long long*>(out.data_ptr()), cur()), "clock_calibration");
+  auto h = out.cpu();
+  return {h[0].item<int64_t>(), h[1].item<int64_t>()};
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
+  m.def("rs_atomic_probe", &py_rs_atomic_probe);
+  m.def("clock_calibration", &py_clock_calibration);
   m.def("gemm", &py_gemm);
   m.def("gemm_plan", &py_gemm_plan);
   m.def("rmsnorm", &py_rmsnorm);

@@ -1,0 +1,130 @@
+"""Primitive probes: reduce-scatter by remote atomics (four `red` forms) and SM clock calibration.
+
+    python -m comm_opt_b200.harness.probes --emulate 8                 (all ranks on one GPU)
+    timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 \
+        --master-port 29541 -m comm_opt_b200.harness.probes            (one rank per GPU, NVLink atomics)
+
+For each variant and size: every rank adds its slice for owner d into d's accumulator, owners wait
+for all arrivals (bounded), the accumulator is checked against the fp32 sum (relative error; f32 adds
+are exact up to ordering, bf16x2 adds round on every arrival), and the kernel is timed with CUDA
+events (max over ranks). The reference found 4-byte atomics too slow to build a reduce-scatter on
+A100 (exp/M11_before_prototype/README.md:188); sm_100a adds 16-byte vector forms.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+
+import torch
+import torch.distributed as dist
+
+from .._ext import native
+
+VARIANTS = {0: "red.f32", 1: "red.v4.f32", 2: "red.bf16x2", 3: "red.v4.bf16x2"}
+
+
+def clock_mhz(device: int = 0, ns: int = 20_000_000) -> float:
+    cycles, t = native().clock_calibration(ns, device)
+    return cycles / t * 1000.0
+
+
+def run_rs(world: int, n: int, variant: int, dev, emulate: bool, blocks: int = 64, reps: int = 5,
+           group=None) -> dict:
+    C = native()
+    es = 4 if variant <= 1 else 2
+    dt = torch.float32 if variant <= 1 else torch.bfloat16
+    acc_bytes = (n * es + 4095) // 4096 * 4096
+    region = acc_bytes + 4096
+    rank = 0 if emulate else dist.get_rank(group)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    if emulate:
+        heap = torch.zeros(world * region, dtype=torch.uint8, device=dev)
+        bases = [heap.data_ptr() + r * region for r in range(world)]
+        x = (0.1 * torch.randn(world, world * n, generator=g, device=dev)).to(dt)
+        mine = [heap[r * region: r * region + n * es].view(dt) for r in range(world)]
+        zero = [heap]
+    else:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        heap = symm_mem.empty(region, dtype=torch.uint8, device=dev)
+        hdl = symm_mem.rendezvous(heap, group or dist.group.WORLD)
+        bases = list(hdl.buffer_ptrs)
+        allx = (0.1 * torch.randn(world, world * n, generator=g, device=dev)).to(dt)
+        x = allx[rank].contiguous()
+        mine = [heap[:n * es].view(dt)]
+        zero = [heap]
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    times = []
+    for it in range(reps + 1):
+        for z in zero:
+            z.zero_()
+        torch.cuda.synchronize()
+        if not emulate:
+            dist.barrier(group=group)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        C.rs_atomic_probe(bases, 0, acc_bytes, x, rank, n, variant, int(emulate), world * n * es, blocks,
+                          int(1e9), err)
+        b.record()
+        torch.cuda.synchronize()
+        if it:
+            times.append(a.elapsed_time(b) * 1000.0)
+    src = x if emulate else allx
+    if emulate:
+        rels = []
+        for d in range(world):
+            ref = sum(src[r, d * n:(d + 1) * n].float() for r in range(world))
+            rels.append(float((mine[d].float() - ref).abs().max() / ref.abs().max()))
+        rel = max(rels)
+    else:
+        ref = sum(src[r, rank * n:(rank + 1) * n].float() for r in range(world))
+        rel = float((mine[0].float() - ref).abs().max() / ref.abs().max())
+    t = sorted(times)[len(times) // 2]
+    if not emulate:
+        tt = torch.tensor([t, rel, float(err.item())], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
+        t, rel, e = [float(v) for v in tt.cpu()]
+    else:
+        e = float(err.item())
+    return dict(variant=VARIANTS[variant], world=world, emulated=emulate, slice_bytes=n * es, us=round(t, 2),
+                push_gbs=round((world - 1) * n * es / t / 1e3, 1), rel_err=rel, timeout=bool(e))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--emulate", type=int, default=0, help="run W ranks in one launch on one GPU")
+    ap.add_argument("--sizes", default="10240,81920,655360")
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args()
+    rows = []
+    if a.emulate:
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        world, rank = a.emulate, 0
+    else:
+        local = int(os.environ["LOCAL_RANK"])
+        dev = torch.device("cuda", local)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        world, rank = dist.get_world_size(), dist.get_rank()
+    for n in [int(s) for s in a.sizes.split(",")]:
+        for v in VARIANTS:
+            r = run_rs(world, n, v, dev, bool(a.emulate))
+            rows.append(r)
+            if rank == 0:
+                print(json.dumps(r), flush=True)
+    if rank == 0:
+        mhz = clock_mhz(dev.index)
+        print(json.dumps(dict(clock_mhz=round(mhz, 1))), flush=True)
+        if a.out:
+            with open(a.out, "w") as f:
+                json.dump(dict(rows=rows, clock_mhz=mhz), f, indent=1)
+    if not a.emulate:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -28,6 +28,7 @@ SOURCES = [
     "attention.cu",
     "gemm_sm100.cu",
     "tma_host.cpp",
+    "probes.cu",
 ]
 SOURCES += [s for s in os.environ.get("COB_EXTRA_SOURCES", "").split(",") if s]
 
