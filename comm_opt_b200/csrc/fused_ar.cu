@@ -250,8 +250,17 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   for (int row = cl; row < p.rows; row += ncl, ++it) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
     float h[kVPT][V::N];
-    uint4 hb[kVPT];
+    uint4 hb[kVPT], rv[kVPT], gv[kVPT];
     float ss = 0.f;
+    // residual and gamma do not depend on the peers: request them before waiting for peer data
+#pragma unroll
+    for (int k = 0; k < kVPT; ++k) {
+      const int v = v0 + tid + k * NT;
+      if (v < v1 && p.norm) {
+        rv[k] = reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden)[v];
+        gv[k] = ld_nc_v4(reinterpret_cast<const uint4*>(p.gamma) + v);
+      }
+    }
 #pragma unroll
     for (int k = 0; k < kVPT; ++k) {
       const int v = v0 + tid + k * NT;
@@ -293,7 +302,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
         }
         if (p.norm) {
           float r[V::N];
-          V::to_float(reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden)[v], r);
+          V::to_float(rv[k], r);
 #pragma unroll
           for (int i = 0; i < V::N; ++i) a[i] += r[i];
         }
@@ -311,7 +320,19 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
 #pragma unroll
     for (int k = 0; k < kVPT; ++k) {
       const int v = v0 + tid + k * NT;
-      if (v < v1) store_norm<T>(p, out, res, row, v, h[k], hb[k], rstd);
+      if (v < v1) {
+        uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * p.hidden);
+        if (p.norm) {
+          float g[V::N], o[V::N];
+          V::to_float(gv[k], g);
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) o[i] = h[k][i] * rstd * g[i];
+          orow[v] = V::from_float(o);
+          reinterpret_cast<uint4*>(res + (size_t)row * p.hidden)[v] = hb[k];
+        } else {
+          orow[v] = hb[k];
+        }
+      }
     }
   }
   stamp(p, rank, e, 3);
@@ -322,20 +343,26 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
 
 // ---------------------------------------------------------------------------------------------
 // Two-shot kernels. Rank r owns columns [r*SV, (r+1)*SV) of every row (SV = HV / W vectors).
-//   phase 1 (LAMPORT): push slice d of x to rank d's rs[slot][rank]           (flat over (row, v))
-//   phase 1 (PULL)   : copy x to stage[parity], flag barrier                    (rows of this block)
-//   phase 1 (NVLS)   : copy x to stage[parity], multicast barrier               (rows of this block)
-//   phase 2 (owner)  : sum the owned slice of each row (+ residual) -> h, partial sum of squares;
-//                      LAMPORT/PULL push h + {partial, epoch} to every rank's ag/agp,
-//                      NVLS multimem.st h + partial into every rank's hbuf/hpart then barrier 2
-//   phase 3          : every rank reads all slices of h + all partials -> out, residual
+// Rows are owned by WARPS (global warp gw handles rows gw, gw + total_warps, ...), so every row is in
+// flight at once and the owner phase needs no block-wide barrier; the row -> block mapping is the
+// same on every rank, which is what the per-block barriers of the pull / NVLS forms rely on.
+//   phase 1 (LAMPORT): push slice d of x to rank d's rs[slot][rank]            (flat, 4 vectors / step)
+//   phase 1 (PULL)   : copy this block's rows of x to stage[parity], flag barrier
+//   phase 1 (NVLS)   : copy this block's rows of x to stage[parity], multicast barrier
+//   phase 2 (owner)  : warp sums the owned slice of its row (+ residual) -> h, partial sum of squares
+//                      (warp reduction); LAMPORT/PULL push h + {partial, epoch} to every rank's ag/agp,
+//                      NVLS multimem.st h + partial to every rank's hbuf/hpart, then barrier 2
+//   phase 3          : all slices of h + all partials -> out, residual (flat for LAMPORT/PULL, the
+//                      block's rows for NVLS)
 // ---------------------------------------------------------------------------------------------
+
 template <typename T, int W, int MODE>
-__global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
+__global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   using V = Vec<T>;
   using LP = LamportOf<T>;
+  constexpr int kChunk = 16 / W;  // vectors per lane per owner-phase step: 16 loads in flight per lane
   const int rank = p.emulate ? (int)blockIdx.y : p.rank;
-  const int tid = threadIdx.x, NT = blockDim.x, lane = tid & 31;
+  const int tid = threadIdx.x, NT = blockDim.x, lane = tid & 31, warp = tid >> 5, NW = NT >> 5;
   RankState* st = state_of(p, rank);
   const T* x = reinterpret_cast<const T*>(p.x) + (size_t)rank * p.x_rs;
   T* res = reinterpret_cast<T*>(p.residual) + (size_t)rank * p.res_rs;
@@ -343,7 +370,7 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
   const int hv = p.hidden / V::N, sv = hv / W;
   const long long total = (long long)p.rows * hv;
   const long long gtid = (long long)blockIdx.x * NT + tid, gthreads = (long long)gridDim.x * NT;
-  __shared__ float s_scr[32];
+  const int gw = blockIdx.x * NW + warp, total_warps = gridDim.x * NW;
 
   pdl_wait();
   const uint64_t e = ld_vol_u64(&st->epoch) + 1;
@@ -355,18 +382,30 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
 
   // ---- phase 1
   if (MODE == kLamport2S) {
-    for (long long u = gtid; u < total; u += gthreads) {
-      const int row = (int)(u / hv), v = (int)(u - (long long)row * hv);
-      const int dst = v / sv, i = v - dst * sv;
-      if (dst != rank) {
-        const uint4 d = LP::clean(ld_nc_v4(reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden) + v));
-        st_vol_v4(rs_at(p, dst, slot, rank, row, i), d);
+    for (long long u0 = gtid; u0 < total; u0 += 4 * gthreads) {
+      uint4 d[4];
+      int rows_[4], vs[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const long long u = u0 + k * gthreads;
+        rows_[k] = -1;
+        if (u < total) {
+          rows_[k] = (int)(u / hv);
+          vs[k] = (int)(u - (long long)rows_[k] * hv);
+          d[k] = ld_nc_v4(reinterpret_cast<const uint4*>(x + (size_t)rows_[k] * p.hidden) + vs[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (rows_[k] < 0) continue;
+        const int dst = vs[k] / sv, i = vs[k] - dst * sv;
+        if (dst != rank) st_vol_v4(rs_at(p, dst, slot, rank, rows_[k], i), LP::clean(d[k]));
       }
     }
   } else {
-    for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    for (int row = gw; row < p.rows; row += total_warps) {
       const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
-      for (int v = tid; v < hv; v += NT) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
+      for (int v = lane; v < hv; v += 32) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
     }
     __threadfence();
     __syncthreads();
@@ -383,35 +422,55 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
   stamp(p, rank, e, 1);
   pdl_trigger();
 
-  // ---- phase 2: owned slice of this block's rows
-  for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+  // ---- phase 2: a warp per row, the owned slice in chunks of kChunk vectors per lane
+  for (int row = gw; row < p.rows; row += total_warps) {
     float ss = 0.f;
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
+    const uint4* rr = reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden);
+    for (int c0 = 0; c0 < sv; c0 += 32 * kChunk) {
+      uint4 rv[kChunk];
+      float a[kChunk][V::N];
 #pragma unroll
-    for (int k = 0; k < kVPT; ++k) {
-      const int i = tid + k * NT;
-      if (i < sv) {
-        const int v = rank * sv + i;
-        float a[V::N];
+      for (int k = 0; k < kChunk; ++k) {
+        const int i = c0 + k * 32 + lane;
 #pragma unroll
-        for (int q = 0; q < V::N; ++q) a[q] = 0.f;
-        if (MODE == kNvls2S) {
-          const uint4 s = ok ? mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, v) * 16) : make_uint4(0, 0, 0, 0);
-          V::to_float(s, a);
-        } else {
-          uint4 d[W];
+        for (int q = 0; q < V::N; ++q) a[k][q] = 0.f;
+        if (i < sv && p.norm) rv[k] = rr[rank * sv + i];  // issued before the peer data is awaited
+      }
+      if (MODE == kNvls2S) {
+        uint4 sred[kChunk];
+#pragma unroll
+        for (int k = 0; k < kChunk; ++k) {
+          const int i = c0 + k * 32 + lane;
+          if (i < sv && ok) sred[k] = mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, rank * sv + i) * 16);
+          else sred[k] = make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int k = 0; k < kChunk; ++k) V::to_float(sred[k], a[k]);
+      } else {
+        // every source's vector of every chunk element is requested before any is awaited
+        uint4 d[kChunk][W];
+#pragma unroll
+        for (int k = 0; k < kChunk; ++k) {
+          const int i = c0 + k * 32 + lane;
+          if (i >= sv) continue;
 #pragma unroll
           for (int s = 0; s < W; ++s) {
             if (MODE == kLamport2S)
-              d[s] = (s == rank) ? ld_nc_v4(xr + v) : ld_vol_v4(rs_at(p, rank, slot, s, row, i));
+              d[k][s] = (s == rank) ? ld_nc_v4(xr + rank * sv + i) : ld_vol_v4(rs_at(p, rank, slot, s, row, i));
             else
-              d[s] = ok ? ld_vol_v4(stage_at(p, s, slot, row, v)) : make_uint4(0, 0, 0, 0);
+              d[k][s] = ok ? ld_vol_v4(stage_at(p, s, slot, row, rank * sv + i)) : make_uint4(0, 0, 0, 0);
           }
+        }
+#pragma unroll
+        for (int k = 0; k < kChunk; ++k) {
+          const int i = c0 + k * 32 + lane;
+          if (i >= sv) continue;
           if (MODE == kLamport2S) {
 #pragma unroll
             for (int s = 0; s < W; ++s) {
-              if (s != rank && ok && !poll_vec<T>(rs_at(p, rank, slot, s, row, i), d[s], w)) {
-                record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 2, ((uint64_t)row << 32) | v, s, e);
+              if (s != rank && ok && !poll_vec<T>(rs_at(p, rank, slot, s, row, i), d[k][s], w)) {
+                record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 2, ((uint64_t)row << 32) | i, s, e);
                 ok = false;
               }
             }
@@ -422,62 +481,67 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
 #pragma unroll
           for (int s = 0; s < W; ++s) {
             float f[V::N];
-            V::to_float(d[s], f);
+            V::to_float(d[k][s], f);
 #pragma unroll
-            for (int q = 0; q < V::N; ++q) a[q] += f[q];
+            for (int q = 0; q < V::N; ++q) a[k][q] += f[q];
           }
         }
+      }
+#pragma unroll
+      for (int k = 0; k < kChunk; ++k) {
+        const int i = c0 + k * 32 + lane;
+        if (i >= sv) continue;
         if (p.norm) {
           float r[V::N];
-          V::to_float(reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden)[v], r);
+          V::to_float(rv[k], r);
 #pragma unroll
-          for (int q = 0; q < V::N; ++q) a[q] += r[q];
+          for (int q = 0; q < V::N; ++q) a[k][q] += r[q];
         }
-        const uint4 hb = LP::clean(V::from_float(a));
+        const uint4 hb = LP::clean(V::from_float(a[k]));
         float hf[V::N];
         V::to_float(hb, hf);
 #pragma unroll
         for (int q = 0; q < V::N; ++q) ss += hf[q] * hf[q];
         if (MODE == kNvls2S) {
-          mm_st_v4(p.mc + p.L.hbuf + ((size_t)row * p.L.max_hv + v) * 16, hb);
+          mm_st_v4(p.mc + p.L.hbuf + ((size_t)row * p.L.max_hv + rank * sv + i) * 16, hb);
         } else {
 #pragma unroll
           for (int dd = 0; dd < W; ++dd) st_vol_v4(ag_at(p, (rank + dd) % W, slot, rank, row, i), hb);
         }
       }
     }
-    const float part = p.norm ? block_sum(ss, s_scr) : 0.f;
+    const float part = warp_sum(ss);
     const unsigned long long word = ((unsigned long long)etag << 32) | __float_as_uint(part);
     if (MODE == kNvls2S) {
-      if (tid == 0) mm_st_u64(p.mc + p.L.hpart + ((size_t)row * p.L.world + rank) * 8, word);
-    } else if (tid < W) {
-      st_vol_u64(agp_at(p, tid, slot, rank, row), word);
+      if (lane == 0) mm_st_u64(p.mc + p.L.hpart + ((size_t)row * p.L.world + rank) * 8, word);
+    } else if (lane < W) {
+      st_vol_u64(agp_at(p, lane, slot, rank, row), word);
     }
   }
-
   stamp(p, rank, e, 2);
+
   if (MODE == kNvls2S) {
     __threadfence_system();
     __syncthreads();
     const uint32_t nc = st->nvls_calls[blockIdx.x][1] + 1u;
     ok = nvls_barrier(p, rank, st, 1, nc, w) && ok;
     if (tid == 0) st->nvls_calls[blockIdx.x][1] = nc;
-    // phase 3 (NVLS): rows of this block only (the barrier covered exactly these rows)
-    for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    // phase 3 (NVLS): this block's rows (the barrier covered exactly these rows)
+    for (int row = gw; row < p.rows; row += total_warps) {
       float tot = 0.f;
       if (p.norm) {
-        for (int q = 0; q < W; ++q) {
-          const unsigned long long wd =
-              ld_vol_u64(p.base[rank] + p.L.hpart + ((size_t)row * p.L.world + q) * 8);
-          if ((uint32_t)(wd >> 32) != etag && ok) {
-            if (tid == 0) record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, row, q, e);
-            ok = false;
-          }
-          tot += __uint_as_float((uint32_t)wd);
+        unsigned long long wd = 0ull;
+        if (lane < W) wd = ld_vol_u64(p.base[rank] + p.L.hpart + ((size_t)row * p.L.world + lane) * 8);
+        if (lane < W && (uint32_t)(wd >> 32) != etag && ok) {
+          record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, row, lane, e);
+          ok = false;
         }
+        const float mine = __uint_as_float((uint32_t)wd);
+#pragma unroll
+        for (int q = 0; q < W; ++q) tot += __shfl_sync(0xffffffffu, mine, q);
       }
       const float rstd = rsqrtf(tot / (float)p.hidden + p.eps);
-      for (int v = tid; v < hv; v += NT) {
+      for (int v = lane; v < hv; v += 32) {
         const uint4 hb = ld_vol_v4(p.base[rank] + p.L.hbuf + ((size_t)row * p.L.max_hv + v) * 16);
         float hf[V::N];
         V::to_float(hb, hf);
@@ -485,19 +549,35 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
       }
     }
   } else {
-    // phase 3 (LAMPORT/PULL): flat over (row, v); a warp shares one row (hv % 32 == 0)
-    for (long long u0 = gtid - lane; u0 < total; u0 += gthreads) {
-      const long long u = u0 + lane;
-      const int row = (int)(u0 / hv);
-      float tot = 0.f;
-      if (p.norm) {
+    // phase 3 (LAMPORT/PULL): flat over (row, v), two vectors per lane per step; a warp shares one
+    // row per step (hv % 32 == 0)
+    for (long long u0 = gtid - lane; u0 < total; u0 += 2 * gthreads) {
+      uint4 hb[2];
+      uint4* at[2];
+      int rowk[2], vk[2];
+      float tot[2] = {0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const long long ub = u0 + k * gthreads;
+        rowk[k] = -1;
+        if (ub < total) {
+          rowk[k] = (int)(ub / hv);
+          vk[k] = (int)(ub + lane - (long long)rowk[k] * hv);
+          const int s = vk[k] / sv, i = vk[k] - s * sv;
+          at[k] = ag_at(p, rank, slot, s, rowk[k], i);
+          hb[k] = ld_vol_v4(at[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (rowk[k] < 0 || !p.norm) continue;  // warp-uniform
         unsigned long long wd = 0ull;
         if (lane < W) {
-          const unsigned long long* a = agp_at(p, rank, slot, lane, row);
+          const unsigned long long* a = agp_at(p, rank, slot, lane, rowk[k]);
           wd = ld_vol_u64(a);
           while ((uint32_t)(wd >> 32) != etag && ok) {
             if (w.expired()) {
-              record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, row, lane, e);
+              record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, rowk[k], lane, e);
               ok = false;
               break;
             }
@@ -507,22 +587,20 @@ __global__ void __launch_bounds__(512) k_twoshot(const ARParams p) {
         __syncwarp();
         const float mine = __uint_as_float((uint32_t)wd);
 #pragma unroll
-        for (int q = 0; q < W; ++q) tot += __shfl_sync(0xffffffffu, mine, q);
+        for (int q = 0; q < W; ++q) tot[k] += __shfl_sync(0xffffffffu, mine, q);
       }
-      if (u < total) {
-        const int v = (int)(u - (long long)row * hv);
-        const int s = v / sv, i = v - s * sv;
-        uint4* a = ag_at(p, rank, slot, s, row, i);
-        uint4 hb = ld_vol_v4(a);
-        if (ok && !poll_vec<T>(a, hb, w)) {
-          record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 3, ((uint64_t)row << 32) | v, s, e);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        if (rowk[k] < 0) continue;
+        if (ok && !poll_vec<T>(at[k], hb[k], w)) {
+          record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 3, ((uint64_t)rowk[k] << 32) | vk[k], 0, e);
           ok = false;
         }
-        st_vol_v4(a, LP::fill());
+        st_vol_v4(at[k], LP::fill());
         float hf[V::N];
-        V::to_float(hb, hf);
-        const float rstd = rsqrtf(tot / (float)p.hidden + p.eps);
-        store_norm<T>(p, out, res, row, v, hf, hb, rstd);
+        V::to_float(hb[k], hf);
+        const float rstd = rsqrtf(tot[k] / (float)p.hidden + p.eps);
+        store_norm<T>(p, out, res, rowk[k], vk[k], hf, hb[k], rstd);
       }
     }
   }
@@ -696,16 +774,17 @@ cudaError_t resolve_config(ARParams& p, int num_sms) {
     }
     if (p.blocks % p.cluster != 0) return cudaErrorInvalidValue;
   } else {
-    const int sv = hv / p.world;
-    if (p.threads <= 0) p.threads = sv > 1024 ? 512 : (sv > 256 ? 256 : 128);
+    if (p.threads <= 0) p.threads = 256;
     p.threads = std::max(p.threads, 32);
-    if (sv > p.threads * kVPT) return cudaErrorInvalidValue;
+    if (p.threads > 256) return cudaErrorInvalidValue;
     p.cluster = 1;
     if (p.blocks <= 0) {
-      // enough CTAs for the flat push / gather phases: ~2 vectors per thread, capped by the budget
-      const long long flat = ((long long)p.rows * hv + 2LL * p.threads - 1) / (2LL * p.threads);
-      long long b = std::max<long long>(p.rows, flat);
-      if (p.variant != kLamport2S) b = p.rows;  // barrier variants: one block per row group
+      // rows are owned by warps: enough CTAs that every row has a warp, and enough threads for the
+      // flat push / gather phases (~4 vectors per thread), capped by one resident CTA per SM
+      const int warps = p.threads / 32;
+      const long long by_rows = ((long long)p.rows + warps - 1) / warps;
+      const long long by_flat = ((long long)p.rows * hv + 4LL * p.threads - 1) / (4LL * p.threads);
+      const long long b = p.variant == kLamport2S ? std::max(by_rows, by_flat) : by_rows;
       p.blocks = (int)std::max<long long>(1, std::min<long long>(b, budget));
     }
   }
