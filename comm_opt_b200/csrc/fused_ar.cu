@@ -19,8 +19,9 @@
 //   * thread-block clusters with DSMEM so a single row can be spread over up to 8 SMs,
 //   * every wait bounded by %globaltimer; a timeout sets the rank's error word and the kernel
 //     returns (the reference's spins are unbounded, fused_ar_norm_nf.cu:95-96, 181-183),
-//   * global epoch advanced by the last block (same rule as the reference's M16 fix,
-//     exp/M16_epoch_fix/fused_ar_norm.cu:190-198) so graphs of different grid sizes interleave.
+//   * one epoch for all blocks of a call whatever the grid size, so graphs of different grid sizes
+//     interleave (the property of the reference's M16 fix, exp/M16_epoch_fix/fused_ar_norm.cu:190-198),
+//     without its last-block arrival counter: each block publishes the epoch for its index class.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -82,17 +83,19 @@ __device__ __forceinline__ void stamp(const ARParams& p, int rank, uint64_t e, i
   }
 }
 
-// Last block of this rank's call advances the epoch (M16 rule: every block reads the same epoch at
-// start; the count of finished blocks, not the block index, decides who advances it).
-__device__ __forceinline__ void finish_call(RankState* st, uint64_t e, int blocks_per_rank) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned prev = atomicAdd(&st->done, 1u);
-    if (prev == (unsigned)blocks_per_rank - 1u) {
-      st->done = 0u;
-      *reinterpret_cast<volatile unsigned long long*>(&st->epoch) = e;
-    }
-  }
+// End of a call: publish the epoch to the blocks of the next call (see RankState::blk_epoch). No
+// block waits for another, so there is no arrival counter on the critical path; the next call reads
+// these words after griddepcontrol.wait, which returns once this grid has completed and its writes
+// are visible. Every block of every call reads the same epoch, whatever the grid sizes (the rule
+// of the reference's fix for graphs of mixed grid sizes, exp/M16_epoch_fix/fused_ar_norm.cu:190-198).
+__device__ __forceinline__ uint64_t call_epoch(RankState* st) {
+  return ld_vol_u64(&st->blk_epoch[blockIdx.x]) + 1;
+}
+
+__device__ __forceinline__ void finish_call(RankState* st, uint64_t e) {
+  for (int j = blockIdx.x + threadIdx.x * gridDim.x; j < kMaxBlocks; j += blockDim.x * gridDim.x)
+    st->blk_epoch[j] = e;
+  if (blockIdx.x == 0 && threadIdx.x == 0) st->epoch = e;
 }
 
 // Cluster-wide (or block-wide when C == 1) sum with a fixed order. `it` alternates the shared
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   __shared__ float s_part[2];
 
   pdl_wait();
-  const uint64_t e = ld_vol_u64(&st->epoch) + 1;
+  const uint64_t e = call_epoch(st);
   const int slot = (int)(e & 1);
   Waiter w(p.timeout_ns, &st->error);
   bool ok = true;
@@ -338,7 +341,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   stamp(p, rank, e, 3);
   if (C > 1) cg::this_cluster().sync();  // no CTA leaves while a peer CTA may read its shared memory
   stamp(p, rank, e, 4);
-  finish_call(st, e, gridDim.x);
+  finish_call(st, e);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -373,7 +376,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   const int gw = blockIdx.x * NW + warp, total_warps = gridDim.x * NW;
 
   pdl_wait();
-  const uint64_t e = ld_vol_u64(&st->epoch) + 1;
+  const uint64_t e = call_epoch(st);
   const int slot = (int)(e & 1);
   const uint32_t etag = (uint32_t)e;
   Waiter w(p.timeout_ns, &st->error);
@@ -606,7 +609,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   }
   stamp(p, rank, e, 3);
   stamp(p, rank, e, 4);
-  finish_call(st, e, gridDim.x);
+  finish_call(st, e);
 }
 
 // Fill a region with a 32-bit pattern.

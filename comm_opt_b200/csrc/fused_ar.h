@@ -35,14 +35,18 @@ enum Variant : int {
 // Per-rank control block (in the rank's own heap). Only this rank's kernels write it, except
 // `flags` (separate region) which peers write.
 struct alignas(256) RankState {
-  unsigned long long epoch;          // number of completed fused calls on this rank
-  unsigned int done;                 // blocks of the current call that have finished
+  unsigned long long epoch;          // number of completed fused calls on this rank (written by block 0)
+  unsigned int unused;
   unsigned int error;                // sticky ErrBits (see common.cuh)
   unsigned long long err_detail[4];  // where the first error happened
   unsigned int flag_calls[kMaxBlocks];     // per-block call counter of the flag barrier
   unsigned int nvls_calls[kMaxBlocks][2];  // per-block call counters of the two NVLS barriers
   unsigned int gather_epoch;               // epoch of the small all-gather primitive
   unsigned int pad[3];
+  // Epoch as read by block b of the next call. Block b of a call with G blocks writes entries
+  // b, b + G, b + 2G, ... at its end, so every entry holds the same value whatever the grid size of
+  // the next call; that call reads them only after this one has completed (stream order).
+  unsigned long long blk_epoch[kMaxBlocks];
 };
 
 // Byte offsets of every region inside a heap (identical on all ranks). Sizes in comments use

@@ -29,7 +29,7 @@ FIELDS = ("state", "flags", "nvls", "land1", "rs", "ag", "agp", "stage", "hbuf",
 
 MAX_BLOCKS = 160        # per-block barrier slots (>= 148 SMs)
 MAX_WORLD = 8
-RANK_STATE_BYTES = 2048  # sizeof(cob::RankState)
+RANK_STATE_BYTES = 3328  # sizeof(cob::RankState)
 
 
 @dataclass(frozen=True)
@@ -164,5 +164,5 @@ class SymmetricHeap:
         return [self.tensor]
 
     def state_words(self, heap: torch.Tensor) -> torch.Tensor:
-        """int64 view of the first 48 bytes of a RankState: epoch, (done|error<<32), err_detail[4]."""
+        """int64 view of the first 48 bytes of a RankState: epoch, (unused|error<<32), err_detail[4]."""
         return heap[self.layout.state:self.layout.state + 48].view(torch.int64)
