@@ -1,4 +1,4 @@
-"""Flagship benchmark: Llama-3-70B-shaped tensor-parallel greedy decode.
+"""Flagship benchmark: Llama-3-70B-shaped tensor-parallel greedy decode (the reference's headline TP=8 decode metric).
 
     python bench.py --gpus N --steps K --warmup W          (N > 1: launched by torch.distributed.run)
 
@@ -105,7 +105,7 @@ class ClockSampler:
 def reference_arm(args):
     line = {"impl": "reference",
             "unavailable": "the reference (allennnnnz/comm_opt) is not an installable project: pip install of "
-                           "/root/reference fails with 'Neither setup.py nor pyproject.toml found', and it has no "
+                           "the reference source tree fails with 'Neither setup.py nor pyproject.toml found', and it has no "
                            "decode runner of its own (its decode numbers come from vLLM driver scripts)"}
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(line), flush=True)

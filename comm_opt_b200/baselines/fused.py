@@ -1,4 +1,4 @@
-"""Implementations compared by the fused-op sweep, behind one interface.
+"""Implementations compared by the fused-op sweep (the reference's headline fused-op benchmark), behind one interface.
 
 Every implementation turns (x, residual, gamma, eps) of this rank into a zero-argument callable that
 performs ONE fused all-reduce + residual add + RMSNorm on static buffers, so K calls can be captured

@@ -10,7 +10,9 @@
 #include <vector>
 
 #include "fused_ar.h"
+#include "fused_gemm.h"
 #include "ops.h"
+#include "tma_host.h"
 #include "types.h"
 
 namespace cob {
@@ -169,6 +171,87 @@ void py_allgather_u32(std::vector<int64_t> bases, std::vector<int64_t> layout, t
   check_cuda(cob::launch_allgather_u32(p, at::cuda::getCurrentCUDAStream()), "allgather_u32");
 }
 
+
+// Layer-boundary fused GEMMs. kind 0 = gemm_push (x -> landing buffers of every rank),
+// kind 1 = ar_norm_gemm (landing buffers + residual + gamma -> y). Weights w are [ranks * N, K]
+// (emulate: every rank's weights stacked), x [ranks * M, K]. Returns {bn, tiles, splits, kps}.
+std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std::vector<int64_t> layout,
+                                   torch::Tensor w, c10::optional<torch::Tensor> x,
+                                   c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> gamma,
+                                   c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> act,
+                                   c10::optional<torch::Tensor> flags, c10::optional<torch::Tensor> pss,
+                                   torch::Tensor err, int64_t rank, int64_t M, int64_t N, int64_t K, double eps,
+                                   int64_t emulate, int64_t splits, int64_t pdl, int64_t timeout_ns,
+                                   int64_t res_rs, bool dry_run) {
+  cob::FusedGemmParams p = {};
+  COB_CHECK(bases.size() >= 1 && bases.size() <= cob::kMaxWorld, "world must be 1..8");
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
+  p.L = vec_to_layout(layout);
+  p.world = (int)bases.size();
+  p.rank = (int)rank;
+  p.emulate = (int)emulate;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.eps = (float)eps;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  const int ranks = emulate ? p.world : 1;
+  check_dense(w, "w");
+  check_dense(err, "err");
+  COB_CHECK(w.scalar_type() == torch::kBFloat16, "fused GEMMs take bf16 weights");
+  COB_CHECK(w.numel() == (int64_t)ranks * N * K, "w must hold ranks * N * K elements");
+  COB_CHECK(err.scalar_type() == torch::kInt32, "err must be int32");
+  COB_CHECK(p.L.world == p.world && p.L.esize == 2, "communicator layout must be bf16 with this world");
+  p.err = reinterpret_cast<int*>(err.data_ptr());
+  const c10::cuda::CUDAGuard g(w.device());
+  int sms = 0;
+  check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, w.device().index()), "sm count");
+  const cob::FusedGemmPlan pl = cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, std::max(1, sms / ranks));
+  if (dry_run) return {pl.bn, pl.tiles, pl.splits, pl.kps};
+  CUtensorMap tw, tb;
+  check_cuda(cob::tensor_map_2d(w.data_ptr(), (uint64_t)ranks * N, (uint64_t)K, (uint64_t)K * 2, 128, 64, true, &tw),
+             "weight tensor map");
+  cudaError_t rc;
+  if (kind == 0) {
+    COB_CHECK(x.has_value(), "gemm_push needs x");
+    check_dense(*x, "x");
+    COB_CHECK(x->scalar_type() == torch::kBFloat16 && x->numel() == (int64_t)ranks * M * K, "x must be bf16 [ranks*M, K]");
+    check_cuda(cob::tensor_map_2d(x->data_ptr(), (uint64_t)ranks * M, (uint64_t)K, (uint64_t)K * 2, (uint32_t)pl.bn, 64,
+                                  true, &tb),
+               "x tensor map");
+    rc = cob::launch_gemm_push(p, tw, tb, pl, ranks, pdl != 0, at::cuda::getCurrentCUDAStream());
+  } else {
+    COB_CHECK(residual.has_value() && gamma.has_value() && y.has_value() && act.has_value() && flags.has_value() &&
+                  pss.has_value(),
+              "ar_norm_gemm needs residual, gamma, y, act, flags, pss");
+    for (auto* t : {&*residual, &*gamma, &*y, &*act, &*flags, &*pss}) check_dense(*t, "fused GEMM operand");
+    COB_CHECK(residual->scalar_type() == torch::kBFloat16 && gamma->scalar_type() == torch::kBFloat16 &&
+                  y->scalar_type() == torch::kBFloat16 && act->scalar_type() == torch::kBFloat16,
+              "residual, gamma, y, act must be bf16");
+    COB_CHECK(residual->numel() >= (int64_t)ranks * M * K && gamma->numel() == K && y->numel() >= (int64_t)ranks * M * N,
+              "residual / gamma / y sizes");
+    COB_CHECK(act->dim() == 2 && act->size(1) == K && act->size(0) % ranks == 0, "act must be [ranks * rows, K]");
+    COB_CHECK(flags->scalar_type() == torch::kInt32 && flags->numel() >= (int64_t)ranks * cob::kMaxPieces,
+              "flags must be int32 [ranks, kMaxPieces]");
+    p.act_rows = (int)(act->size(0) / ranks);
+    COB_CHECK(pss->scalar_type() == torch::kFloat && pss->numel() >= (int64_t)ranks * cob::kMaxPieces * p.act_rows,
+              "pss must be float32 [ranks, kMaxPieces, rows]");
+    p.residual = residual->data_ptr();
+    p.gamma = gamma->data_ptr();
+    p.Y = y->data_ptr();
+    p.act = act->data_ptr();
+    p.flags = reinterpret_cast<uint32_t*>(flags->data_ptr());
+    p.pss = reinterpret_cast<float*>(pss->data_ptr());
+    p.res_rs = res_rs;
+    check_cuda(cob::tensor_map_2d(act->data_ptr(), (uint64_t)act->size(0), (uint64_t)K, (uint64_t)K * 2,
+                                  (uint32_t)pl.bn, 64, true, &tb),
+               "act tensor map");
+    rc = cob::launch_ar_norm_gemm(p, tw, tb, pl, ranks, pdl != 0, at::cuda::getCurrentCUDAStream());
+  }
+  check_cuda(rc, kind == 0 ? "gemm_push launch" : "ar_norm_gemm launch");
+  return {pl.bn, pl.tiles, pl.splits, pl.kps};
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m);  // ops_bindings.cpp
@@ -190,6 +273,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("kMaxBlocks") = cob::kMaxBlocks;
   m.attr("kMaxWorld") = cob::kMaxWorld;
   m.attr("kRankStateBytes") = (int64_t)sizeof(cob::RankState);
+  m.def("fused_gemm", &py_fused_gemm, pybind11::arg("kind"), pybind11::arg("bases"), pybind11::arg("layout"),
+        pybind11::arg("w"), pybind11::arg("x") = pybind11::none(), pybind11::arg("residual") = pybind11::none(),
+        pybind11::arg("gamma") = pybind11::none(), pybind11::arg("y") = pybind11::none(),
+        pybind11::arg("act") = pybind11::none(), pybind11::arg("flags") = pybind11::none(),
+        pybind11::arg("pss") = pybind11::none(), pybind11::arg("err"), pybind11::arg("rank"), pybind11::arg("M"),
+        pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("eps"), pybind11::arg("emulate"),
+        pybind11::arg("splits"), pybind11::arg("pdl"), pybind11::arg("timeout_ns"), pybind11::arg("res_rs"),
+        pybind11::arg("dry_run"));
+  m.attr("kMaxPieces") = cob::kMaxPieces;
   register_ops(m);
   register_ipc(m);
 }

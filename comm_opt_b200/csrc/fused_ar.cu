@@ -53,9 +53,15 @@ __device__ __forceinline__ uint4* ag_at(const ARParams& p, int owner, int slot, 
   return reinterpret_cast<uint4*>(p.base[owner] + p.L.ag) +
          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i);
 }
-__device__ __forceinline__ unsigned long long* agp_at(const ARParams& p, int owner, int slot, int src, int row) {
+// Partial sums of squares travel per "unit" of an owner slice (512 / W vectors): units per slice
+// ceil(hv / 512), at most pu_max(L) words per (source rank, row).
+__host__ __device__ __forceinline__ int pu_max(const Layout& L) { return (L.max_hv + 511) / 512; }
+__device__ __forceinline__ unsigned long long* agp_at(const ARParams& p, int owner, int slot, int src, int row, int u) {
   return reinterpret_cast<unsigned long long*>(p.base[owner] + p.L.agp) +
-         (((size_t)slot * p.L.world + src) * p.L.max_rows + row);
+         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * pu_max(p.L) + u);
+}
+__device__ __forceinline__ size_t hpart_idx(const ARParams& p, int row, int src, int u) {
+  return ((size_t)row * p.L.world + src) * pu_max(p.L) + u;
 }
 __device__ __forceinline__ size_t stage_idx(const ARParams& p, int parity, int row, int v) {
   return ((size_t)parity * p.L.max_rows + row) * p.L.max_hv + v;
@@ -345,32 +351,62 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Two-shot kernels. Rank r owns columns [r*SV, (r+1)*SV) of every row (SV = HV / W vectors).
-// Rows are owned by WARPS (global warp gw handles rows gw, gw + total_warps, ...), so every row is in
-// flight at once and the owner phase needs no block-wide barrier; the row -> block mapping is the
-// same on every rank, which is what the per-block barriers of the pull / NVLS forms rely on.
+// Two-shot kernels. Rank r owns columns [r*SV, (r+1)*SV) of every row (SV = HV / W vectors). The owned
+// slice of a row is cut into units of 32 lanes x (16 / W) vectors (ceil(HV / 512) units per slice),
+// so even one row keeps several warps busy and every lane has 16 peer loads in flight; each unit's
+// sum of squares travels as its own {f32, epoch32} word.
 //   phase 1 (LAMPORT): push slice d of x to rank d's rs[slot][rank]            (flat, 4 vectors / step)
 //   phase 1 (PULL)   : copy this block's rows of x to stage[parity], flag barrier
 //   phase 1 (NVLS)   : copy this block's rows of x to stage[parity], multicast barrier
-//   phase 2 (owner)  : warp sums the owned slice of its row (+ residual) -> h, partial sum of squares
-//                      (warp reduction); LAMPORT/PULL push h + {partial, epoch} to every rank's ag/agp,
-//                      NVLS multimem.st h + partial to every rank's hbuf/hpart, then barrier 2
+//   phase 2 (owner)  : a warp per unit: sum over ranks (+ residual) -> h, unit sum of squares (warp
+//                      reduction); LAMPORT/PULL push h + {partial, epoch} to every rank's ag/agp,
+//                      NVLS multimem.st h + partial to every rank's hbuf/hpart, then barrier 2.
+//                      LAMPORT spreads units over all warps of the grid; PULL / NVLS keep a row in
+//                      the block that staged it (their barriers are per block).
 //   phase 3          : all slices of h + all partials -> out, residual (flat for LAMPORT/PULL, the
 //                      block's rows for NVLS)
 // ---------------------------------------------------------------------------------------------
+
+// Sum of the W x U unit partials of a row (epoch-tagged words), warp-wide; false on timeout.
+template <int W>
+__device__ __forceinline__ bool row_partials(const ARParams& p, int rank, int slot, int row, int U, uint32_t etag,
+                                             bool nvls, Waiter& w, RankState* st, uint64_t e, float& tot) {
+  const int lane = threadIdx.x & 31;
+  float acc = 0.f;
+  bool ok = true;
+  for (int j = lane; j < W * U; j += 32) {
+    const int src = j / U, u = j - src * U;
+    const unsigned long long* a =
+        nvls ? reinterpret_cast<const unsigned long long*>(p.base[rank] + p.L.hpart) + hpart_idx(p, row, src, u)
+             : agp_at(p, rank, slot, src, row, u);
+    unsigned long long wd = ld_vol_u64(a);
+    while ((uint32_t)(wd >> 32) != etag) {
+      if (w.expired()) {
+        record_error(st, kErrTimeoutPartial, 3, row, j, e);
+        ok = false;
+        break;
+      }
+      wd = ld_vol_u64(a);
+    }
+    acc += __uint_as_float((uint32_t)wd);
+  }
+  tot = warp_sum(acc);
+  return __all_sync(0xffffffffu, ok);
+}
 
 template <typename T, int W, int MODE>
 __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   using V = Vec<T>;
   using LP = LamportOf<T>;
-  constexpr int kChunk = 16 / W;  // vectors per lane per owner-phase step: 16 loads in flight per lane
+  constexpr int kChunk = 16 / W;  // vectors per lane per unit: 16 loads in flight per lane
+  constexpr int UV = 32 * kChunk;  // vectors per unit
   const int rank = p.emulate ? (int)blockIdx.y : p.rank;
   const int tid = threadIdx.x, NT = blockDim.x, lane = tid & 31, warp = tid >> 5, NW = NT >> 5;
   RankState* st = state_of(p, rank);
   const T* x = reinterpret_cast<const T*>(p.x) + (size_t)rank * p.x_rs;
   T* res = reinterpret_cast<T*>(p.residual) + (size_t)rank * p.res_rs;
   T* out = reinterpret_cast<T*>(p.out) + (size_t)rank * p.out_rs;
-  const int hv = p.hidden / V::N, sv = hv / W;
+  const int hv = p.hidden / V::N, sv = hv / W, U = (sv + UV - 1) / UV;
   const long long total = (long long)p.rows * hv;
   const long long gtid = (long long)blockIdx.x * NT + tid, gthreads = (long long)gridDim.x * NT;
   const int gw = blockIdx.x * NW + warp, total_warps = gridDim.x * NW;
@@ -406,9 +442,9 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
       }
     }
   } else {
-    for (int row = gw; row < p.rows; row += total_warps) {
+    for (int row = blockIdx.x; row < p.rows; row += gridDim.x) {
       const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
-      for (int v = lane; v < hv; v += 32) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
+      for (int v = tid; v < hv; v += NT) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
     }
     __threadfence();
     __syncthreads();
@@ -425,100 +461,102 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   stamp(p, rank, e, 1);
   pdl_trigger();
 
-  // ---- phase 2: a warp per row, the owned slice in chunks of kChunk vectors per lane
-  for (int row = gw; row < p.rows; row += total_warps) {
+  // ---- phase 2: a warp per (row, unit of the owned slice)
+  // LAMPORT: units over all warps of the grid; PULL / NVLS: the block's rows, units over its warps
+  const int nunits = MODE == kLamport2S ? p.rows * U : ((p.rows - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * U;
+  for (int g = (MODE == kLamport2S ? gw : warp); g < nunits; g += (MODE == kLamport2S ? total_warps : NW)) {
+    const int row = MODE == kLamport2S ? g / U : (int)blockIdx.x + (g / U) * (int)gridDim.x;
+    const int c0 = (g % U) * UV;
     float ss = 0.f;
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
     const uint4* rr = reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden);
-    for (int c0 = 0; c0 < sv; c0 += 32 * kChunk) {
-      uint4 rv[kChunk];
-      float a[kChunk][V::N];
+    uint4 rv[kChunk];
+    float a[kChunk][V::N];
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) {
+      const int i = c0 + k * 32 + lane;
+#pragma unroll
+      for (int q = 0; q < V::N; ++q) a[k][q] = 0.f;
+      if (i < sv && p.norm) rv[k] = rr[rank * sv + i];  // issued before the peer data is awaited
+    }
+    if (MODE == kNvls2S) {
+      uint4 sred[kChunk];
 #pragma unroll
       for (int k = 0; k < kChunk; ++k) {
         const int i = c0 + k * 32 + lane;
-#pragma unroll
-        for (int q = 0; q < V::N; ++q) a[k][q] = 0.f;
-        if (i < sv && p.norm) rv[k] = rr[rank * sv + i];  // issued before the peer data is awaited
+        if (i < sv && ok) sred[k] = mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, rank * sv + i) * 16);
+        else sred[k] = make_uint4(0, 0, 0, 0);
       }
-      if (MODE == kNvls2S) {
-        uint4 sred[kChunk];
 #pragma unroll
-        for (int k = 0; k < kChunk; ++k) {
-          const int i = c0 + k * 32 + lane;
-          if (i < sv && ok) sred[k] = mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, rank * sv + i) * 16);
-          else sred[k] = make_uint4(0, 0, 0, 0);
-        }
+      for (int k = 0; k < kChunk; ++k) V::to_float(sred[k], a[k]);
+    } else {
+      // every source's vector of every chunk element is requested before any is awaited
+      uint4 d[kChunk][W];
 #pragma unroll
-        for (int k = 0; k < kChunk; ++k) V::to_float(sred[k], a[k]);
-      } else {
-        // every source's vector of every chunk element is requested before any is awaited
-        uint4 d[kChunk][W];
+      for (int k = 0; k < kChunk; ++k) {
+        const int i = c0 + k * 32 + lane;
+        if (i >= sv) continue;
 #pragma unroll
-        for (int k = 0; k < kChunk; ++k) {
-          const int i = c0 + k * 32 + lane;
-          if (i >= sv) continue;
-#pragma unroll
-          for (int s = 0; s < W; ++s) {
-            if (MODE == kLamport2S)
-              d[k][s] = (s == rank) ? ld_nc_v4(xr + rank * sv + i) : ld_vol_v4(rs_at(p, rank, slot, s, row, i));
-            else
-              d[k][s] = ok ? ld_vol_v4(stage_at(p, s, slot, row, rank * sv + i)) : make_uint4(0, 0, 0, 0);
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < kChunk; ++k) {
-          const int i = c0 + k * 32 + lane;
-          if (i >= sv) continue;
-          if (MODE == kLamport2S) {
-#pragma unroll
-            for (int s = 0; s < W; ++s) {
-              if (s != rank && ok && !poll_vec<T>(rs_at(p, rank, slot, s, row, i), d[k][s], w)) {
-                record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 2, ((uint64_t)row << 32) | i, s, e);
-                ok = false;
-              }
-            }
-#pragma unroll
-            for (int s = 0; s < W; ++s)
-              if (s != rank) st_vol_v4(rs_at(p, rank, slot, s, row, i), LP::fill());
-          }
-#pragma unroll
-          for (int s = 0; s < W; ++s) {
-            float f[V::N];
-            V::to_float(d[k][s], f);
-#pragma unroll
-            for (int q = 0; q < V::N; ++q) a[k][q] += f[q];
-          }
+        for (int s = 0; s < W; ++s) {
+          if (MODE == kLamport2S)
+            d[k][s] = (s == rank) ? ld_nc_v4(xr + rank * sv + i) : ld_vol_v4(rs_at(p, rank, slot, s, row, i));
+          else
+            d[k][s] = ok ? ld_vol_v4(stage_at(p, s, slot, row, rank * sv + i)) : make_uint4(0, 0, 0, 0);
         }
       }
 #pragma unroll
       for (int k = 0; k < kChunk; ++k) {
         const int i = c0 + k * 32 + lane;
         if (i >= sv) continue;
-        if (p.norm) {
-          float r[V::N];
-          V::to_float(rv[k], r);
+        if (MODE == kLamport2S) {
 #pragma unroll
-          for (int q = 0; q < V::N; ++q) a[k][q] += r[q];
+          for (int s = 0; s < W; ++s) {
+            if (s != rank && ok && !poll_vec<T>(rs_at(p, rank, slot, s, row, i), d[k][s], w)) {
+              record_error(st, kErrTimeoutLanding, ((uint64_t)MODE << 32) | 2, ((uint64_t)row << 32) | i, s, e);
+              ok = false;
+            }
+          }
+#pragma unroll
+          for (int s = 0; s < W; ++s)
+            if (s != rank) st_vol_v4(rs_at(p, rank, slot, s, row, i), LP::fill());
         }
-        const uint4 hb = LP::clean(V::from_float(a[k]));
-        float hf[V::N];
-        V::to_float(hb, hf);
 #pragma unroll
-        for (int q = 0; q < V::N; ++q) ss += hf[q] * hf[q];
-        if (MODE == kNvls2S) {
-          mm_st_v4(p.mc + p.L.hbuf + ((size_t)row * p.L.max_hv + rank * sv + i) * 16, hb);
-        } else {
+        for (int s = 0; s < W; ++s) {
+          float f[V::N];
+          V::to_float(d[k][s], f);
 #pragma unroll
-          for (int dd = 0; dd < W; ++dd) st_vol_v4(ag_at(p, (rank + dd) % W, slot, rank, row, i), hb);
+          for (int q = 0; q < V::N; ++q) a[k][q] += f[q];
         }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) {
+      const int i = c0 + k * 32 + lane;
+      if (i >= sv) continue;
+      if (p.norm) {
+        float r[V::N];
+        V::to_float(rv[k], r);
+#pragma unroll
+        for (int q = 0; q < V::N; ++q) a[k][q] += r[q];
+      }
+      const uint4 hb = LP::clean(V::from_float(a[k]));
+      float hf[V::N];
+      V::to_float(hb, hf);
+#pragma unroll
+      for (int q = 0; q < V::N; ++q) ss += hf[q] * hf[q];
+      if (MODE == kNvls2S) {
+        mm_st_v4(p.mc + p.L.hbuf + ((size_t)row * p.L.max_hv + rank * sv + i) * 16, hb);
+      } else {
+#pragma unroll
+        for (int dd = 0; dd < W; ++dd) st_vol_v4(ag_at(p, (rank + dd) % W, slot, rank, row, i), hb);
       }
     }
     const float part = warp_sum(ss);
     const unsigned long long word = ((unsigned long long)etag << 32) | __float_as_uint(part);
     if (MODE == kNvls2S) {
-      if (lane == 0) mm_st_u64(p.mc + p.L.hpart + ((size_t)row * p.L.world + rank) * 8, word);
+      if (lane == 0) mm_st_u64(p.mc + p.L.hpart + hpart_idx(p, row, rank, g % U) * 8, word);
     } else if (lane < W) {
-      st_vol_u64(agp_at(p, lane, slot, rank, row), word);
+      st_vol_u64(agp_at(p, lane, slot, rank, row, g % U), word);
     }
   }
   stamp(p, rank, e, 2);
@@ -529,20 +567,10 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
     const uint32_t nc = st->nvls_calls[blockIdx.x][1] + 1u;
     ok = nvls_barrier(p, rank, st, 1, nc, w) && ok;
     if (tid == 0) st->nvls_calls[blockIdx.x][1] = nc;
-    // phase 3 (NVLS): this block's rows (the barrier covered exactly these rows)
-    for (int row = gw; row < p.rows; row += total_warps) {
+    // phase 3 (NVLS): this block's rows (the barrier covered exactly these rows), a warp per row
+    for (int row = (int)blockIdx.x + warp * (int)gridDim.x; row < p.rows; row += NW * (int)gridDim.x) {
       float tot = 0.f;
-      if (p.norm) {
-        unsigned long long wd = 0ull;
-        if (lane < W) wd = ld_vol_u64(p.base[rank] + p.L.hpart + ((size_t)row * p.L.world + lane) * 8);
-        if (lane < W && (uint32_t)(wd >> 32) != etag && ok) {
-          record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, row, lane, e);
-          ok = false;
-        }
-        const float mine = __uint_as_float((uint32_t)wd);
-#pragma unroll
-        for (int q = 0; q < W; ++q) tot += __shfl_sync(0xffffffffu, mine, q);
-      }
+      if (p.norm && ok && !row_partials<W>(p, rank, slot, row, U, etag, true, w, st, e, tot)) ok = false;
       const float rstd = rsqrtf(tot / (float)p.hidden + p.eps);
       for (int v = lane; v < hv; v += 32) {
         const uint4 hb = ld_vol_v4(p.base[rank] + p.L.hbuf + ((size_t)row * p.L.max_hv + v) * 16);
@@ -574,23 +602,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         if (rowk[k] < 0 || !p.norm) continue;  // warp-uniform
-        unsigned long long wd = 0ull;
-        if (lane < W) {
-          const unsigned long long* a = agp_at(p, rank, slot, lane, rowk[k]);
-          wd = ld_vol_u64(a);
-          while ((uint32_t)(wd >> 32) != etag && ok) {
-            if (w.expired()) {
-              record_error(st, kErrTimeoutPartial, ((uint64_t)MODE << 32) | 3, rowk[k], lane, e);
-              ok = false;
-              break;
-            }
-            wd = ld_vol_u64(a);
-          }
-        }
-        __syncwarp();
-        const float mine = __uint_as_float((uint32_t)wd);
-#pragma unroll
-        for (int q = 0; q < W; ++q) tot[k] += __shfl_sync(0xffffffffu, mine, q);
+        if (ok && !row_partials<W>(p, rank, slot, rowk[k], U, etag, false, w, st, e, tot[k])) ok = false;
       }
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
@@ -726,10 +738,10 @@ Layout plan_layout(int world, int max_rows, int max_hidden, int esize, int max_g
   L.land1 = take(2 * W * R * HV * 16);
   L.rs = take(2 * W * R * SV * 16);
   L.ag = take(2 * W * R * SV * 16);
-  L.agp = take(2 * W * R * 8);
+  L.agp = take(2 * W * R * pu_max(L) * 8);
   L.stage = take(2 * R * HV * 16);
   L.hbuf = take(R * HV * 16);
-  L.hpart = take(R * W * 8);
+  L.hpart = take(R * W * pu_max(L) * 8);
   L.gather = take(2 * W * (long long)max_gather * 8);
   L.total = align_up(off, 2 << 20);
   return L;
@@ -782,12 +794,14 @@ cudaError_t resolve_config(ARParams& p, int num_sms) {
     if (p.threads > 256) return cudaErrorInvalidValue;
     p.cluster = 1;
     if (p.blocks <= 0) {
-      // rows are owned by warps: enough CTAs that every row has a warp, and enough threads for the
-      // flat push / gather phases (~4 vectors per thread), capped by one resident CTA per SM
+      // LAMPORT: enough CTAs that every (row, unit) has a warp and the flat push / gather phases
+      // have ~4 vectors per thread; PULL / NVLS: a CTA per row (their barriers are per CTA); capped
+      // by one resident CTA per SM
       const int warps = p.threads / 32;
-      const long long by_rows = ((long long)p.rows + warps - 1) / warps;
+      const int units = (hv / p.world + 32 * (16 / p.world) - 1) / (32 * (16 / p.world));
+      const long long by_units = ((long long)p.rows * units + warps - 1) / warps;
       const long long by_flat = ((long long)p.rows * hv + 4LL * p.threads - 1) / (4LL * p.threads);
-      const long long b = p.variant == kLamport2S ? std::max(by_rows, by_flat) : by_rows;
+      const long long b = p.variant == kLamport2S ? std::max(by_units, by_flat) : (long long)p.rows;
       p.blocks = (int)std::max<long long>(1, std::min<long long>(b, budget));
     }
   }

@@ -29,7 +29,7 @@ def main():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--steps", type=int, default=8)
-    ap.add_argument("--out-dir", default="gpurun_out/traces")
+    ap.add_argument("--out-dir", default="results/traces")
     a = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

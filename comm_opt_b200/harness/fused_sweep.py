@@ -1,4 +1,4 @@
-"""Fused all-reduce + residual + RMSNorm latency sweep on 2/4/8 GPUs.
+"""Fused all-reduce + residual + RMSNorm latency sweep (the reference's headline fused-op benchmark) on 2/4/8 GPUs.
 
     timeout -k 60 1800 python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \
         --master-addr 127.0.0.1 --master-port 29511 -m comm_opt_b200.harness.fused_sweep \

@@ -23,6 +23,8 @@ ENTRY = {
     "collectives": "comm_opt_b200.harness.collectives",
     "fused_sweep": "comm_opt_b200.harness.fused_sweep",
     "selftest": "comm_opt_b200.harness.mp_selftest",
+    "bakeoff": "comm_opt_b200.harness.allreduce_bakeoff",
+    "phases": "comm_opt_b200.harness.phase_profile",
 }
 
 GPUSETS = {  # set A: first GPUs; set B: other physical GPUs / rank order (the reference's second set)
@@ -68,6 +70,8 @@ def command(job: Job, out: Path, port: int) -> tuple[list[str], dict]:
         cmd += ["--out", str(out / f"{job.tag}.json")]
     elif job.entry == "fused_sweep":
         cmd += ["--out-dir", str(out / "runs"), "--ts", job.tag]
+    elif job.entry in ("bakeoff", "phases"):
+        cmd += ["--out-dir", str(out / "runs")]
     return cmd, env
 
 

@@ -91,6 +91,9 @@ class TPCommunicator:
         self.have_nvls = bool(self.heap and self.heap.mc and allow_nvls)
         self.last_choice: Choice | None = None
         self.stamps: torch.Tensor | None = None
+        self._fg: dict[int, dict] = {}  # layer-boundary fused GEMM workspaces by inner size K
+        self._fg_err_t: torch.Tensor | None = None
+        self.last_fused_gemm: tuple | None = None
 
     # ------------------------------------------------------------------ state management
     def _host_barrier(self):
@@ -113,6 +116,8 @@ class TPCommunicator:
             return
         torch.cuda.synchronize(self.device)
         self._host_barrier()
+        for ws in self._fg.values():
+            ws["flags"].zero_()
         self._init_state()
 
     def error_state(self) -> list[dict]:
@@ -246,6 +251,74 @@ class TPCommunicator:
         with torch.cuda.device(self.device):
             native().allgather_u32(self.heap.bases, self._layout_list, inp, out, self.rank, n, int(self.emulated),
                                    self.timeout_ns, n if self.emulated else 0, self.world * n if self.emulated else 0)
+        return out
+
+    # ------------------------------------------------------------------ layer-boundary fused GEMMs
+    def _fg_workspace(self, K: int) -> dict:
+        ws = self._fg.get(K)
+        if ws is None:
+            ranks = self.world if self.emulated else 1
+            n = native().kMaxPieces
+            ws = dict(act=torch.zeros(ranks * self.max_rows, K, dtype=torch.bfloat16, device=self.device),
+                      flags=torch.zeros(ranks, n, dtype=torch.int32, device=self.device),
+                      pss=torch.zeros(ranks, n, self.max_rows, dtype=torch.float32, device=self.device))
+            self._fg[K] = ws
+        return ws
+
+    def prepare_fused_gemm(self, K: int):
+        """Allocate the workspace of ar_norm_gemm for inner size K (call before CUDA-graph capture)."""
+        self._fg_workspace(K)
+
+    def _fg_dims(self, t: torch.Tensor) -> tuple[int, int]:
+        if self.emulated:
+            assert t.shape[0] == self.world, "emulated operands are [world, rows, cols]"
+            return t[0].numel() // t.shape[-1], t.shape[-1]
+        return t.numel() // t.shape[-1], t.shape[-1]
+
+    def gemm_push(self, x: torch.Tensor, w: torch.Tensor, splits: int = 0, dry_run: bool = False):
+        """Row-parallel GEMM whose epilogue is the first half of the all-reduce: x [M, K] @ w[N, K]^T is
+        pushed (bf16) into every rank's landing buffers; `ar_norm_gemm` (or nothing else) must follow.
+        Emulation: x [W, M, K], w [W, N, K]."""
+        if self.world == 1 or self.dtype != torch.bfloat16:
+            raise TPCommError("fused GEMMs need world > 1 and a bf16 communicator")
+        M, K = self._fg_dims(x)
+        N = w.shape[-2]
+        if M > self.max_rows or N > self.max_hidden:
+            raise TPCommError(f"gemm_push [{M}, {N}] exceeds the communicator capacity")
+        with torch.cuda.device(self.device):
+            plan = native().fused_gemm(0, self.heap.bases, self._layout_list, w, x=x, err=self._fg_err(),
+                                       rank=self.rank, M=M, N=N, K=K, eps=0.0, emulate=int(self.emulated), splits=splits,
+                                       pdl=int(self.pdl), timeout_ns=self.timeout_ns, res_rs=0, dry_run=dry_run)
+        self.last_fused_gemm = ("gemm_push", tuple(plan))
+        return plan
+
+    def _fg_err(self) -> torch.Tensor:
+        if self._fg_err_t is None:
+            self._fg_err_t = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self._fg_err_t
+
+    def ar_norm_gemm(self, residual: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+                     out: torch.Tensor | None = None, splits: int = 0, dry_run: bool = False) -> torch.Tensor:
+        """Second half of the all-reduce fused with RMSNorm and the next column-parallel GEMM:
+        h = residual + sum_ranks(pushed partials) (residual updated in place),
+        out = (RMSNorm(h) * gamma) @ w^T, out [M, N]. Emulation: residual [W, M, K], w [W, N, K]."""
+        if self.world == 1 or self.dtype != torch.bfloat16:
+            raise TPCommError("fused GEMMs need world > 1 and a bf16 communicator")
+        M, K = self._fg_dims(residual)
+        N = w.shape[-2]
+        if M > self.max_rows or K > self.max_hidden:
+            raise TPCommError(f"ar_norm_gemm [{M}, {K}] exceeds the communicator capacity")
+        if out is None:
+            shape = (self.world, M, N) if self.emulated else (M, N)
+            out = torch.empty(shape, dtype=torch.bfloat16, device=residual.device)
+        ws = self._fg_workspace(K)
+        with torch.cuda.device(self.device):
+            plan = native().fused_gemm(1, self.heap.bases, self._layout_list, w, residual=residual, gamma=gamma,
+                                       y=out, act=ws["act"], flags=ws["flags"], pss=ws["pss"], err=self._fg_err(),
+                                       rank=self.rank, M=M, N=N, K=K, eps=float(eps), emulate=int(self.emulated),
+                                       splits=splits, pdl=int(self.pdl), timeout_ns=self.timeout_ns,
+                                       res_rs=M * K if self.emulated else 0, dry_run=dry_run)
+        self.last_fused_gemm = ("ar_norm_gemm", tuple(plan))
         return out
 
     def close(self):

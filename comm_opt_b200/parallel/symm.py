@@ -80,10 +80,11 @@ def plan_layout_py(world: int, max_rows: int, max_hidden: int, esize: int, max_g
     take("land1", 2 * W * R * HV * 16)
     take("rs", 2 * W * R * SV * 16)
     take("ag", 2 * W * R * SV * 16)
-    take("agp", 2 * W * R * 8)
+    pu = (HV + 511) // 512  # partial-sum units per owner slice (kernels: ceil(hv / 512))
+    take("agp", 2 * W * R * pu * 8)
     take("stage", 2 * R * HV * 16)
     take("hbuf", R * HV * 16)
-    take("hpart", R * W * 8)
+    take("hpart", R * W * pu * 8)
     take("gather", 2 * W * max_gather * 8)
     total = _align(off, 2 << 20)
     return HeapLayout(total=total, world=world, max_rows=max_rows, max_hv=max_hv, sv_max=sv_max, esize=esize,

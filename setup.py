@@ -24,6 +24,7 @@ SOURCES = [
     "ops_bindings.cpp",
     "ipc_bindings.cpp",
     "fused_ar.cu",
+    "fused_gemm.cu",
     "decode_ops.cu",
     "attention.cu",
     "gemm_sm100.cu",

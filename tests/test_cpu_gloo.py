@@ -1,6 +1,6 @@
 """CPU/gloo tier: world_size 2 correctness of fused all-reduce + residual add + RMSNorm.
 
-Config: per-rank x [T=4, H=4096] fp32 ~N(0,1) (seed + rank), residual [4, 4096]
+Config (the reference's gloo correctness test): per-rank x [T=4, H=4096] fp32 ~N(0,1) (seed + rank), residual [4, 4096]
 ~N(0,1) (same on every rank), gamma = 1 + 0.1 N(0,1), eps = 1e-6. Output must equal
 RMSNorm(sum_ranks(x) + residual) * gamma and the new residual must be returned.
 """

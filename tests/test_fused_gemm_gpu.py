@@ -1,0 +1,106 @@
+"""Layer-boundary fusion (row-parallel GEMM -> all-reduce + residual + RMSNorm -> column-parallel GEMM)
+with every rank emulated on one GPU.
+
+`gemm_push` runs all ranks' GEMMs in one launch and pushes the partial outputs into the landing
+buffers; `ar_norm_gemm` (one launch, all ranks) waits for them, so the two launches never wait on
+each other. Oracle: fp32 GEMMs, fp32 sum + residual + RMSNorm, fp32 second GEMM; relative error
+max|out - ref| / max|ref| <= 2^-5 (the acceptance rule of the fused op,
+exp/M17_epoch_ab/bench_ab.py:160-164).
+"""
+import pytest
+import torch
+
+from comm_opt_b200.ops.reference import TOL, rel_err
+from comm_opt_b200.parallel import TPCommunicator
+
+pytestmark = pytest.mark.gpu
+
+
+def reference(x, w1, res0, gamma, w2, eps):
+    """x [W, M, K1], w1 [W, H, K1], res0 [M, H], w2 [W, N2, H] -> (h [M, H], out [W, M, N2])."""
+    y = sum(x[r].float() @ w1[r].float().t() for r in range(x.shape[0]))
+    h = res0.float() + y
+    n = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps) * gamma.float()
+    return h, torch.stack([n @ w2[r].float().t() for r in range(x.shape[0])])
+
+
+def layer_boundary(comm, x, w1, res, gamma, w2, eps, splits1=0, splits2=0):
+    comm.gemm_push(x, w1, splits=splits1)
+    return comm.ar_norm_gemm(res, gamma, w2, eps, splits=splits2)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("M", [1, 5, 16, 40])
+def test_layer_boundary_emulated(cuda, world, M):
+    K1, H, N2, eps = 512, 1024, 384, 1e-5
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=64, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(M * 10 + world)
+    w1 = (0.02 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    w2 = (0.02 * torch.randn(world, N2, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res0 = torch.randn(M, H, generator=g, device=cuda).bfloat16()
+    res = res0.unsqueeze(0).repeat(world, 1, 1).contiguous()
+    for it in range(3):  # consecutive calls alternate landing slots and reuse the pieces' flags
+        x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+        before = res[0].clone()
+        out = layer_boundary(comm, x, w1, res, gamma, w2, eps, splits1=2, splits2=2)
+        torch.cuda.synchronize()
+        comm.check()
+        h_ref, out_ref = reference(x, w1, before, gamma, w2, eps)
+        for r in range(world):
+            assert rel_err(res[r], h_ref) <= TOL, (it, r, rel_err(res[r], h_ref))
+            assert rel_err(out[r], out_ref[r]) <= TOL, (it, r, rel_err(out[r], out_ref[r]))
+        for r in range(1, world):
+            assert torch.equal(res[r], res[0])
+    assert comm.epochs() == [3] * world
+
+
+def test_layer_boundary_interleaved_with_fused_ar(cuda):
+    """The fused GEMMs and the standalone fused op share the epoch and the landing slots."""
+    world, M, K1, H, N2, eps = 4, 8, 256, 2048, 256, 1e-6
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=16, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(3)
+    w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    w2 = (0.05 * torch.randn(world, N2, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res = torch.randn(M, H, generator=g, device=cuda).bfloat16().unsqueeze(0).repeat(world, 1, 1).contiguous()
+    for it in range(4):
+        if it % 2:
+            xs = torch.randn(world, M, H, generator=g, device=cuda).bfloat16()
+            before = res[0].clone()
+            out = torch.empty_like(xs)
+            comm.fused_allreduce_add_rmsnorm(xs, res, gamma, eps, out=out, variant="lamport_1s")
+            torch.cuda.synchronize()
+            h_ref = before.float() + xs.float().sum(0)
+            assert rel_err(res[0], h_ref) <= TOL
+        else:
+            x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+            before = res[0].clone()
+            out = layer_boundary(comm, x, w1, res, gamma, w2, eps)
+            torch.cuda.synchronize()
+            h_ref, out_ref = reference(x, w1, before, gamma, w2, eps)
+            assert rel_err(res[0], h_ref) <= TOL and rel_err(out[1], out_ref[1]) <= TOL, it
+    comm.check()
+    assert comm.epochs() == [4] * world
+
+
+@pytest.mark.parametrize("M", [8, 32])
+def test_layer_boundary_70b_tp8_shapes(cuda, M):
+    """Llama-70B TP=8 shapes, 2 emulated ranks: down_proj [M, 3584] x [8192, 3584]^T ->
+    AR + residual + RMSNorm -> QKV [M, 8192] x [1280, 8192]^T (default split plans)."""
+    world, K1, H, N2, eps = 2, 3584, 8192, 1280, 1e-5
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=M, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(M)
+    w1 = (0.02 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    w2 = (0.02 * torch.randn(world, N2, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res0 = torch.randn(M, H, generator=g, device=cuda).bfloat16()
+    res = res0.unsqueeze(0).repeat(world, 1, 1).contiguous()
+    x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+    out = layer_boundary(comm, x, w1, res, gamma, w2, eps)
+    torch.cuda.synchronize()
+    comm.check()
+    h_ref, out_ref = reference(x, w1, res0, gamma, w2, eps)
+    for r in range(world):
+        assert rel_err(res[r], h_ref) <= TOL
+        assert rel_err(out[r], out_ref[r]) <= TOL
