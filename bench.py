@@ -42,6 +42,8 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--gemm", choices=["cob", "torch"], default="cob")
+    p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=0,
+                   help="fuse o_proj/down_proj -> all-reduce + RMSNorm -> next GEMM (TP > 1)")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--layers", type=int, default=None, help="override the layer count (debug only; invalid for bench)")
     p.add_argument("--out", default=None, help="also write the JSON line to this file")
@@ -145,7 +147,7 @@ def main():
     weights = LlamaWeights(cfg, rank, world, dev, seed=0)
     comm = TPCommunicator(group, device=dev, dtype=torch.bfloat16, max_rows=max(B, 8), max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, weights, comm, max_batch=B, max_seq=max_seq, device=dev, gemm=args.gemm,
-                            nccl_group=group)
+                            nccl_group=group, fuse_boundary=bool(args.fuse_boundary))
     prompts = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(1234))
     first = runner.prefill(prompts)
     runner.start(B, first, P)
@@ -220,7 +222,8 @@ def main():
             "data": "synthetic: uniform-random prompt token ids (seed 1234), random-init weights N(0, 0.02)",
             "config": {"model": cfg.name + ("" if args.layers is None else f"-L{cfg.layers}-INVALID"),
                        "global_batch": B, "seq_len": P, "decode_tokens_timed": K, "parallelism": f"tp{world}",
-                       "gemm": args.gemm, "tokens_per_s": round(B * 1000.0 / ms, 1),
+                       "gemm": args.gemm, "fuse_boundary": runner.fuse_boundary,
+                       "tokens_per_s": round(B * 1000.0 / ms, 1),
                        "l2": "no flush: each step streams the full weight set (141 GB / N) >> 126 MB L2",
                        "setup_s": round(setup_s, 1)},
             "e2e": {"value": round(ms_e2e, 4), "unit": "ms/token", "h2d_bytes_per_step": B * 4,

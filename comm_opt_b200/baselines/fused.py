@@ -5,6 +5,8 @@ performs ONE fused all-reduce + residual add + RMSNorm on static buffers, so K c
 in a CUDA graph and replayed (the reference's timing method, exp/M17_epoch_ab/bench_ab.py:167-195).
 
   ours:<variant>     TPCommunicator.fused_allreduce_add_rmsnorm (lamport_1s/2s, pull_1s/2s, nvls_1s/2s, auto)
+  ours_ipc:<variant> the same on a CUDA-IPC heap instead of a multicast-capable symmetric-memory heap
+  ours_pdl:<variant> the same with programmatic dependent launch between consecutive calls
   nccl_norm          NCCL all-reduce (in place) + vLLM fused_add_rms_norm  (reference U_nccl,
                      exp/M9_fused_baselines/bench_fused.py:88-89)
   vllm_car           vLLM custom all-reduce + fused_add_rms_norm           (reference U_vllm,
@@ -65,12 +67,24 @@ class Ours(Impl):
                 return "hidden not divisible for two-shot"
         return ""
 
+    pdl = False
+    owns_comm = False  # close the communicator with this implementation (the IPC-heap one)
+
+    def close(self):
+        if self.owns_comm:
+            self.comm.close()
+
     def make(self, x, residual, gamma, eps):
         out = torch.empty_like(x)
-        comm, v = self.comm, self.variant
+        comm, v, pdl = self.comm, self.variant, self.pdl
 
         def fn():
-            comm.fused_allreduce_add_rmsnorm(x, residual, gamma, eps, out=out, variant=v)
+            old = comm.pdl
+            comm.pdl = pdl or old
+            try:
+                comm.fused_allreduce_add_rmsnorm(x, residual, gamma, eps, out=out, variant=v)
+            finally:
+                comm.pdl = old
             return out
 
         return fn
@@ -235,10 +249,26 @@ class RefProto(Impl):
 def build(names: list[str], *, comm, rank, world, max_rows, hidden, dtype, device, cpu_group) -> tuple[list, dict]:
     """Instantiate the requested implementations; returns (impls, {name: reason} for unavailable ones)."""
     impls, skipped = [], {}
+    comm_ipc = None
     for n in names:
         try:
             if n.startswith("ours:"):
                 impls.append(Ours(comm, n.split(":", 1)[1]))
+            elif n.startswith("ours_ipc:"):
+                # the same kernels on a heap shared by CUDA IPC (no multicast object bound to it)
+                if comm_ipc is None:
+                    from ..parallel import TPCommunicator
+
+                    comm_ipc = TPCommunicator(comm.group, device=device, dtype=dtype, max_rows=max_rows,
+                                              max_hidden=hidden, backend="ipc", pdl=comm.pdl)
+                o = Ours(comm_ipc, n.split(":", 1)[1])
+                o.name = n
+                o.owns_comm = not any(getattr(i, "owns_comm", False) for i in impls)
+                impls.append(o)
+            elif n.startswith("ours_pdl:"):
+                o = Ours(comm, n.split(":", 1)[1])
+                o.name, o.pdl = n, True
+                impls.append(o)
             elif n == "nccl_norm":
                 impls.append(NcclNorm())
             elif n == "vllm_car":

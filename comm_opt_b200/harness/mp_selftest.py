@@ -16,6 +16,8 @@ Parts:
                Uses the CUDA-IPC heap (never bound to a multicast object) and plain peer loads.
   decode     - tiny Llama-shaped model at TP = world vs the unsharded fp32 forward (logits), and
                identical greedy tokens on every rank.
+  decode_fused - the same with the layer boundaries fused (GEMM push epilogue -> all-reduce + RMSNorm
+               inside the next GEMM).
 Rank 0 prints one JSON summary; the exit code is non-zero on any failure.
 """
 from __future__ import annotations
@@ -193,7 +195,7 @@ def fault(C: Checker, dev, world):
     comm.close()
 
 
-def decode_check(C: Checker, dev, world):
+def decode_check(C: Checker, dev, world, fused: bool = False):
     import math
 
     import torch.nn.functional as F
@@ -205,7 +207,9 @@ def decode_check(C: Checker, dev, world):
     full = LlamaWeights.full_random(cfg, device=dev, seed=3)
     w = LlamaWeights(cfg, dist.get_rank(), world, dev, full=full)
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)
-    runner = TPDecodeRunner(cfg, w, comm, max_batch=4, max_seq=96, device=dev, nccl_group=dist.group.WORLD)
+    runner = TPDecodeRunner(cfg, w, comm, max_batch=4, max_seq=96, device=dev, nccl_group=dist.group.WORLD,
+                            fuse_boundary=fused)
+    C.check(runner.fuse_boundary == fused, "layer-boundary fusion engaged as requested")
     prompts = torch.randint(0, cfg.vocab, (3, 29), generator=torch.Generator().manual_seed(1))
     first = runner.prefill(prompts)
     buf = runner.start(3, first, 29)
@@ -244,7 +248,8 @@ def decode_check(C: Checker, dev, world):
         runner.step(3)
         torch.cuda.synchronize()
         ref = ref_logits(toks)[:, r * V:(r + 1) * V]
-        C.check(rel_err(buf["logits"], ref) < 2 ** -5, f"decode step {step} logits err {rel_err(buf['logits'], ref):.3e}")
+        C.check(rel_err(buf["logits"], ref) < 2 ** -5,
+                f"decode step {step} (fused={fused}) logits err {rel_err(buf['logits'], ref):.3e}")
         C.check(same_everywhere(buf["ids"]), f"decode step {step}: ranks disagree on tokens")
         toks = torch.cat([toks, buf["ids"].cpu()[:, None].long()], 1)
     runner.release_graphs()
@@ -267,7 +272,8 @@ def main():
     t0 = time.time()
     try:
         for part in a.parts.split(","):
-            {"functional": functional, "fault": fault, "decode": decode_check}[part](C, dev, world)
+            {"functional": functional, "fault": fault, "decode": decode_check,
+             "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True)}[part](C, dev, world)
     except Exception:
         err = traceback.format_exc()
         C.fails.append(err[-2000:])

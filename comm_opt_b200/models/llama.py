@@ -176,7 +176,7 @@ class TPDecodeRunner:
     """Greedy TP decoding: torch prefill, then graph-captured decode steps built from our kernels."""
 
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
-                 device, gemm: str = "cob", nccl_group=None, pdl: bool = True):
+                 device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -197,6 +197,12 @@ class TPDecodeRunner:
         self.graphs: dict[int, tuple] = {}
         self.kernels_per_step: dict[int, int] = {}
         self.pdl = pdl  # programmatic dependent launch between the kernels of a captured step
+        # layer-boundary fusion: o_proj / down_proj push their partial sums straight into the
+        # all-reduce landing buffers, and the all-reduce + residual + RMSNorm runs inside the next
+        # GEMM (gate_up, the next layer's qkv, the LM head); needs TP > 1, bf16 and this package's GEMMs
+        self.fuse_boundary = bool(fuse_boundary and self.tp > 1 and self.dtype == torch.bfloat16 and gemm == "cob")
+        if self.fuse_boundary:
+            comm.prepare_fused_gemm(cfg.hidden)
 
     # ------------------------------------------------------------------ prefill (plain torch)
     def _ar(self, x: torch.Tensor) -> torch.Tensor:
@@ -286,6 +292,8 @@ class TPDecodeRunner:
         K.rmsnorm(buf["res"], w.layers[0].ln1, cfg.eps, out=buf["h"])
         n += 2
         ours = 1 if self.gemm == "cob" else 0
+        if self.fuse_boundary:
+            return n + self._step_fused(B, buf, bt)
         for i, L in enumerate(w.layers):
             self.lin[(i, "qkv")](buf["h"], out=buf["qkv"])
             K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
@@ -308,6 +316,31 @@ class TPDecodeRunner:
         K.argmax_combine(buf["gathered"] if self.tp > 1 else buf["keys"].view(1, B), self.tp, ids=buf["ids"],
                          positions=buf["pos"], seq_lens=buf["lens"], local_keys=buf["keys"])
         return n + 1
+
+    def _step_fused(self, B: int, buf: dict, bt: torch.Tensor) -> int:
+        """Decode step with the layer boundaries fused (after the embedding and first norm)."""
+        cfg, s, w, comm = self.cfg, self.s, self.w, self.comm
+        n = 0
+        self.lin[(0, "qkv")](buf["h"], out=buf["qkv"])
+        n += 1
+        for i, L in enumerate(w.layers):
+            K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
+                             self.cache.v[i], s["nq"], s["nkv"])
+            buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
+            comm.gemm_push(buf["attn"].view(B, -1), L.wo)
+            comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, cfg.eps, out=buf["gu"])
+            K.silu_mul(buf["gu"], out=buf["act"])
+            comm.gemm_push(buf["act"], L.wdown)
+            if i + 1 < len(w.layers):
+                comm.ar_norm_gemm(buf["res"], w.layers[i + 1].ln1, w.layers[i + 1].wqkv, cfg.eps, out=buf["qkv"])
+            else:
+                comm.ar_norm_gemm(buf["res"], w.final_norm, w.lm_head, cfg.eps, out=buf["logits"])
+            n += 7
+        K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
+        comm.all_gather_u32(buf["keys"].view(torch.int32), out=buf["gathered"].view(torch.int32).view(self.tp, 2 * B))
+        K.argmax_combine(buf["gathered"], self.tp, ids=buf["ids"], positions=buf["pos"], seq_lens=buf["lens"],
+                         local_keys=buf["keys"])
+        return n + 3
 
     def start(self, B: int, first_ids: torch.Tensor, prompt_len: int):
         """Set up decoding of B sequences whose prompts (length prompt_len) are in the cache."""
