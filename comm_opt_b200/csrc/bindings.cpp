@@ -174,7 +174,7 @@ void py_allgather_u32(std::vector<int64_t> bases, std::vector<int64_t> layout, t
 
 // Layer-boundary fused GEMMs. kind 0 = gemm_push (x -> landing buffers of every rank),
 // kind 1 = ar_norm_gemm (landing buffers + residual + gamma -> y). Weights w are [ranks * N, K]
-// (emulate: every rank's weights stacked), x [ranks * M, K]. Returns {bn, tiles, splits, kps}.
+// (emulate: every rank's weights stacked), x [ranks * M, K]. Returns {bn, tiles, splits, kps, xctas}.
 std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std::vector<int64_t> layout,
                                    torch::Tensor w, c10::optional<torch::Tensor> x,
                                    c10::optional<torch::Tensor> residual, c10::optional<torch::Tensor> gamma,
@@ -206,8 +206,9 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
   const c10::cuda::CUDAGuard g(w.device());
   int sms = 0;
   check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, w.device().index()), "sm count");
-  const cob::FusedGemmPlan pl = cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, std::max(1, sms / ranks));
-  if (dry_run) return {pl.bn, pl.tiles, pl.splits, pl.kps};
+  const cob::FusedGemmPlan pl =
+      cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, std::max(1, sms / ranks), kind == 1);
+  if (dry_run) return {pl.bn, pl.tiles, pl.splits, pl.kps, pl.xctas};
   CUtensorMap tw, tb;
   check_cuda(cob::tensor_map_2d(w.data_ptr(), (uint64_t)ranks * N, (uint64_t)K, (uint64_t)K * 2, 128, 64, true, &tw),
              "weight tensor map");
@@ -249,7 +250,7 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
     rc = cob::launch_ar_norm_gemm(p, tw, tb, pl, ranks, pdl != 0, at::cuda::getCurrentCUDAStream());
   }
   check_cuda(rc, kind == 0 ? "gemm_push launch" : "ar_norm_gemm launch");
-  return {pl.bn, pl.tiles, pl.splits, pl.kps};
+  return {pl.bn, pl.tiles, pl.splits, pl.kps, pl.xctas};
 }
 
 }  // namespace

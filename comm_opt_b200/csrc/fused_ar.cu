@@ -53,9 +53,9 @@ __device__ __forceinline__ uint4* ag_at(const ARParams& p, int owner, int slot, 
   return reinterpret_cast<uint4*>(p.base[owner] + p.L.ag) +
          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i);
 }
-// Partial sums of squares travel per "unit" of an owner slice (512 / W vectors): units per slice
-// ceil(hv / 512), at most pu_max(L) words per (source rank, row).
-__host__ __device__ __forceinline__ int pu_max(const Layout& L) { return (L.max_hv + 511) / 512; }
+// Partial sums of squares travel per "unit" of an owner slice (32 vectors, one per lane): units per
+// slice ceil(sv / 32), at most pu_max(L) words per (source rank, row).
+__host__ __device__ __forceinline__ int pu_max(const Layout& L) { return (L.sv_max + 31) / 32; }
 __device__ __forceinline__ unsigned long long* agp_at(const ARParams& p, int owner, int slot, int src, int row, int u) {
   return reinterpret_cast<unsigned long long*>(p.base[owner] + p.L.agp) +
          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * pu_max(p.L) + u);
@@ -119,12 +119,12 @@ __device__ __forceinline__ float row_sum(float v, float* scratch, float* s_part,
 
 template <typename T>
 __device__ __forceinline__ void store_norm(const ARParams& p, T* out, T* res, int row, int v, const float* h,
-                                           const uint4& hbits, float rstd) {
+                                           const uint4& hbits, float rstd, const uint4* gamma_v = nullptr) {
   using V = Vec<T>;
   uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * p.hidden);
   if (p.norm) {
     float g[V::N], o[V::N];
-    V::to_float(ld_nc_v4(reinterpret_cast<const uint4*>(p.gamma) + v), g);
+    V::to_float(gamma_v ? *gamma_v : ld_nc_v4(reinterpret_cast<const uint4*>(p.gamma) + v), g);
 #pragma unroll
     for (int i = 0; i < V::N; ++i) o[i] = h[i] * rstd * g[i];
     orow[v] = V::from_float(o);
@@ -352,9 +352,9 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
 
 // ---------------------------------------------------------------------------------------------
 // Two-shot kernels. Rank r owns columns [r*SV, (r+1)*SV) of every row (SV = HV / W vectors). The owned
-// slice of a row is cut into units of 32 lanes x (16 / W) vectors (ceil(HV / 512) units per slice),
-// so even one row keeps several warps busy and every lane has 16 peer loads in flight; each unit's
-// sum of squares travels as its own {f32, epoch32} word.
+// slice of a row is cut into units of 32 vectors (one per lane, ceil(SV / 32) units per slice), so
+// even one row keeps several warps busy; each unit's sum of squares travels as its own
+// {f32, epoch32} word and a row's W x units words are summed by one warp in phase 3.
 //   phase 1 (LAMPORT): push slice d of x to rank d's rs[slot][rank]            (flat, 4 vectors / step)
 //   phase 1 (PULL)   : copy this block's rows of x to stage[parity], flag barrier
 //   phase 1 (NVLS)   : copy this block's rows of x to stage[parity], multicast barrier
@@ -398,7 +398,7 @@ template <typename T, int W, int MODE>
 __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   using V = Vec<T>;
   using LP = LamportOf<T>;
-  constexpr int kChunk = 16 / W;  // vectors per lane per unit: 16 loads in flight per lane
+  constexpr int kChunk = 1;       // vectors per lane per unit
   constexpr int UV = 32 * kChunk;  // vectors per unit
   const int rank = p.emulate ? (int)blockIdx.y : p.rank;
   const int tid = threadIdx.x, NT = blockDim.x, lane = tid & 31, warp = tid >> 5, NW = NT >> 5;
@@ -583,7 +583,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
     // phase 3 (LAMPORT/PULL): flat over (row, v), two vectors per lane per step; a warp shares one
     // row per step (hv % 32 == 0)
     for (long long u0 = gtid - lane; u0 < total; u0 += 2 * gthreads) {
-      uint4 hb[2];
+      uint4 hb[2], gv[2];
       uint4* at[2];
       int rowk[2], vk[2];
       float tot[2] = {0.f, 0.f};
@@ -597,6 +597,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
           const int s = vk[k] / sv, i = vk[k] - s * sv;
           at[k] = ag_at(p, rank, slot, s, rowk[k], i);
           hb[k] = ld_vol_v4(at[k]);
+          if (p.norm) gv[k] = ld_nc_v4(reinterpret_cast<const uint4*>(p.gamma) + vk[k]);  // before any wait
         }
       }
 #pragma unroll
@@ -615,7 +616,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
         float hf[V::N];
         V::to_float(hb[k], hf);
         const float rstd = rsqrtf(tot[k] / (float)p.hidden + p.eps);
-        store_norm<T>(p, out, res, rowk[k], vk[k], hf, hb[k], rstd);
+        store_norm<T>(p, out, res, rowk[k], vk[k], hf, hb[k], rstd, &gv[k]);
       }
     }
   }
@@ -795,12 +796,12 @@ cudaError_t resolve_config(ARParams& p, int num_sms) {
     p.cluster = 1;
     if (p.blocks <= 0) {
       // LAMPORT: enough CTAs that every (row, unit) has a warp and the flat push / gather phases
-      // have ~4 vectors per thread; PULL / NVLS: a CTA per row (their barriers are per CTA); capped
+      // have ~1 vector per thread; PULL / NVLS: a CTA per row (their barriers are per CTA); capped
       // by one resident CTA per SM
       const int warps = p.threads / 32;
-      const int units = (hv / p.world + 32 * (16 / p.world) - 1) / (32 * (16 / p.world));
+      const int units = (hv / p.world + 31) / 32;
       const long long by_units = ((long long)p.rows * units + warps - 1) / warps;
-      const long long by_flat = ((long long)p.rows * hv + 4LL * p.threads - 1) / (4LL * p.threads);
+      const long long by_flat = ((long long)p.rows * hv + p.threads - 1) / p.threads;
       const long long b = p.variant == kLamport2S ? std::max(by_units, by_flat) : (long long)p.rows;
       p.blocks = (int)std::max<long long>(1, std::min<long long>(b, budget));
     }

@@ -60,7 +60,7 @@ struct FCfg {
   static constexpr int PIPE = RING > PART ? RING : PART;
   static constexpr int CTRL = 1024 + BN * 8;  // barriers, flags, per-row sums / rstd
   static constexpr int SMEM = PIPE + 1024 + CTRL + kQCap * 4;
-  static constexpr int TC = BN < 32 ? 32 : BN;
+  static constexpr int TC = BN < 32 ? 32 : BN;  // TMEM columns per accumulator (two are allocated)
   // SMALL: two CTAs per SM (228 KB per SM, 1 KB reserved per CTA)
   static_assert(!SMALL || SMEM <= 113 * 1024, "two CTAs per SM");
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
@@ -69,7 +69,8 @@ struct FCfg {
 struct Ctrl {
   uint64_t* full;
   uint64_t* empty;
-  uint64_t* tfull;
+  uint64_t* tfull;   // [2]
+  uint64_t* tempty;  // [2]
   uint32_t* tmem_slot;
   volatile int* fail;
   int* issued;
@@ -87,7 +88,8 @@ __device__ __forceinline__ Ctrl carve(uint8_t* smem) {
   c.full = reinterpret_cast<uint64_t*>(ctrl);
   c.empty = c.full + C::STAGES;
   c.tfull = c.empty + C::STAGES;
-  c.tmem_slot = reinterpret_cast<uint32_t*>(c.tfull + 1);
+  c.tempty = c.tfull + 2;
+  c.tmem_slot = reinterpret_cast<uint32_t*>(c.tempty + 2);
   c.fail = reinterpret_cast<volatile int*>(c.tmem_slot + 1);
   c.issued = const_cast<int*>(c.fail) + 1;
   c.consumed = c.issued + 1;
@@ -156,23 +158,29 @@ __device__ bool wait_flags(const uint32_t* flags, int n, uint32_t tag, uint64_t 
 }
 
 // ---------------------------------------------------------------------------------------------
-// Main loop shared by both kernels: warp 0 producer, warp 1 MMA issuer, one accumulator tile.
+// Main loop shared by both kernels: warp 0 producer, warp 1 MMA issuer. The CTA computes `nt` output
+// tiles (rows wrow + i * wstride, i < nt) over the same k-range; accumulators alternate between two
+// TMEM buffers so the epilogue of one tile overlaps the MMAs of the next.
 // WAIT_ACT: the activation loads wait for the pieces of this split (ar_norm_gemm).
 // ---------------------------------------------------------------------------------------------
 template <int BN, bool SMALL, bool WAIT_ACT>
 __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtensorMap* tmW, const CUtensorMap* tmB,
                                          uint8_t* smem, const Ctrl& c, uint32_t tmem, int k0, int nsteps, int wrow,
-                                         int brow, const uint32_t* split_flags, int nflags, uint32_t tag) {
+                                         int wstride, int nt, int brow, const uint32_t* split_flags, int nflags,
+                                         uint32_t tag) {
   using C = FCfg<BN, SMALL>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  const int total = nt * nsteps;
   if (warp == 0) {
-    const int pre = min(C::STAGES, nsteps);
+    const int pre = min(C::STAGES, total);
+    auto wr = [&](int i) { return wrow + (i / nsteps) * wstride; };
+    auto kx = [&](int i) { return (k0 + i % nsteps) * BK; };
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&c.full[i], C::STAGE);
-        tma_load_2d(sA + i * C::A_BYTES, tmW, &c.full[i], (k0 + i) * BK, wrow);
+        tma_load_2d(sA + i * C::A_BYTES, tmW, &c.full[i], kx(i), wr(i));
       }
       if (!WAIT_ACT) pdl_wait();
     }
@@ -184,23 +192,21 @@ __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtenso
     }
     if (lane == 0) {
       int issued = pre;
+      // the ring's first stages expect activation bytes too: on failure they are loaded anyway
+      // (contents unused, the CTA reports failure) so every issued stage completes and can be drained
+      for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * C::B_BYTES, tmB, &c.full[i], kx(i), brow);
       if (ok) {
-        for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * C::B_BYTES, tmB, &c.full[i], (k0 + i) * BK, brow);
-        for (int i = pre; i < nsteps; ++i) {
+        for (int i = pre; i < total; ++i) {
           const int s = i % C::STAGES;
           if (!mbar_wait(&c.empty[s], ((i / C::STAGES) & 1) ^ 1, p.timeout_ns) || *c.fail) {
             *c.fail = 1;
             break;
           }
           mbar_arrive_expect_tx(&c.full[s], C::STAGE);
-          tma_load_2d(sA + s * C::A_BYTES, tmW, &c.full[s], (k0 + i) * BK, wrow);
-          tma_load_2d(sB + s * C::B_BYTES, tmB, &c.full[s], (k0 + i) * BK, brow);
+          tma_load_2d(sA + s * C::A_BYTES, tmW, &c.full[s], kx(i), wr(i));
+          tma_load_2d(sB + s * C::B_BYTES, tmB, &c.full[s], kx(i), brow);
           issued = i + 1;
         }
-      } else {
-        // the ring's first stages expect activation bytes too: load them anyway (contents unused,
-        // the CTA reports failure) so every issued stage completes and can be drained
-        for (int i = 0; i < pre; ++i) tma_load_2d(sB + i * C::B_BYTES, tmB, &c.full[i], (k0 + i) * BK, brow);
       }
       *c.issued = issued;
       if (!WAIT_ACT) pdl_trigger();
@@ -209,21 +215,32 @@ __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtenso
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16(BM, BN, true);
       int i = 0;
-      for (; i < nsteps; ++i) {
-        const int s = i % C::STAGES;
-        if (!mbar_wait(&c.full[s], (i / C::STAGES) & 1, p.timeout_ns) || *c.fail) {
+      bool ok = true;
+      for (int tile = 0; tile < nt && ok; ++tile) {
+        const int acc = tile & 1;
+        if (!mbar_wait(&c.tempty[acc], ((tile >> 1) & 1) ^ 1, p.timeout_ns)) {
           *c.fail = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t a = smem_addr(sA + s * C::A_BYTES), b = smem_addr(sB + s * C::B_BYTES);
+        const uint32_t d = tmem + acc * C::TC;
+        for (int k = 0; k < nsteps; ++k, ++i) {
+          const int s = i % C::STAGES;
+          if (!mbar_wait(&c.full[s], (i / C::STAGES) & 1, p.timeout_ns) || *c.fail) {
+            *c.fail = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = smem_addr(sA + s * C::A_BYTES), b = smem_addr(sB + s * C::B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          mma_f16(tmem, desc_k_sw128(a + kk * 32), desc_k_sw128(b + kk * 32), idesc, (i > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&c.empty[s]);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16(d, desc_k_sw128(a + kk * 32), desc_k_sw128(b + kk * 32), idesc, (k > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&c.empty[s]);
+        }
+        mma_commit(&c.tfull[acc]);
       }
       *c.consumed = i;
-      mma_commit(&c.tfull[0]);
     }
   }
 }
@@ -237,7 +254,7 @@ __device__ __forceinline__ void tile_to_smem(const FusedGemmParams& p, uint8_t* 
   if (!mbar_wait(&c.tfull[0], 0, p.timeout_ns)) *c.fail = 1;
   __syncwarp();
   tc_fence_after();
-  float* part = reinterpret_cast<float*>(smem);
+  float* part = reinterpret_cast<float*>(smem);  // single tile per CTA: the drained ring holds it
   const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
   const int mcols = min(M, BN);
   for (int c0 = 0; c0 < mcols; c0 += 16) {
@@ -291,7 +308,7 @@ __device__ __forceinline__ void teardown(const FusedGemmParams& p, const Ctrl& c
   }
   tc_fence_before();
   __syncthreads();
-  if ((threadIdx.x >> 5) == 1) tmem_dealloc(tmem, C::TC);
+  if ((threadIdx.x >> 5) == 1) tmem_dealloc(tmem, 2 * C::TC);
 }
 
 template <int BN, bool SMALL>
@@ -305,13 +322,16 @@ __device__ __forceinline__ uint32_t setup(uint8_t* smem, const Ctrl& c, int full
       mbar_init(&c.full[s], full_count);
       mbar_init(&c.empty[s], 1);
     }
-    mbar_init(&c.tfull[0], 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&c.tfull[a], 1);
+      mbar_init(&c.tempty[a], 4);  // one arrival per epilogue warp
+    }
     *c.fail = 0;
     *c.issued = 0;
     *c.consumed = 0;
     fence_barrier_init();
   }
-  if ((threadIdx.x >> 5) == 1) tmem_alloc(c.tmem_slot, C::TC);
+  if ((threadIdx.x >> 5) == 1) tmem_alloc(c.tmem_slot, 2 * C::TC);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -335,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   const int k0 = r * p.kps, nsteps = min(KT, k0 + p.kps) - k0;
   const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, &tmW, &tmX);
 
-  mainloop<BN, SMALL, false>(p, &tmW, &tmX, smem, c, tmem, k0, nsteps, (p.emulate ? rank * p.N : 0) + t * BM,
+  mainloop<BN, SMALL, false>(p, &tmW, &tmX, smem, c, tmem, k0, nsteps, (p.emulate ? rank * p.N : 0) + t * BM, 0, 1,
                              p.emulate ? rank * p.M : 0, nullptr, 0, 0u);
   if (threadIdx.x >= 64) tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
   pdl_wait();  // every thread: the epoch below was written by an earlier kernel of the stream
@@ -377,12 +397,15 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const Ctrl c = carve<BN, SMALL>(smem);
   const int rank = p.emulate ? (int)blockIdx.z : p.rank;
+  const int wsr = p.emulate ? rank : 0;  // workspace index of this rank (one set per process otherwise)
+  // X CTAs along x; CTA x computes tiles x, x + X, ... (several only when splits == 1)
   const int t = blockIdx.x, r = blockIdx.y, cs = gridDim.y, tiles = gridDim.x;
+  const int ntiles = (p.N + BM - 1) / BM, nt = (ntiles - t + tiles - 1) / tiles;
   const int KT = p.K / BK, KV = p.K / 8;
   const int k0 = r * p.kps, nsteps = min(KT, k0 + p.kps) - k0;
   const int piece = r * tiles + t;
-  uint32_t* flags = p.flags + (size_t)rank * kMaxPieces;
-  float* pss = p.pss + (size_t)rank * kMaxPieces * p.act_rows;
+  uint32_t* flags = p.flags + (size_t)wsr * kMaxPieces;
+  float* pss = p.pss + (size_t)wsr * kMaxPieces * p.act_rows;
   const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, &tmW, &tmA);
   // No griddepcontrol.wait: nothing read here is written by the immediately preceding kernel
   // (partials arrive through Lamport landing buffers, the epoch / residual / pieces were written by
@@ -392,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   const int slot = (int)(e & 1);
 
   mainloop<BN, SMALL, true>(p, &tmW, &tmA, smem, c, tmem, k0, nsteps, (p.emulate ? rank * p.N : 0) + t * BM,
-                            rank * p.act_rows * (p.emulate ? 1 : 0), flags + (size_t)r * tiles, tiles, tag);
+                            tiles * BM, nt, wsr * p.act_rows, flags + (size_t)r * tiles, tiles, tag);
 
   if (threadIdx.x >= 64) {
     const int tid = threadIdx.x - 64;
@@ -473,28 +496,61 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
     if (tid == 0 && !*c.fail) st_release_u32(flags + piece, tag);
 
     // ---------------- epilogue
-    tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
-    // this split's per-row sum of squares over its `tiles` pieces: lanes stride the pieces, warp tree
+    // this split's per-row sum of squares over its pieces: lanes stride the pieces, warp tree
     const int warp = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
     if (!wait_flags(flags + (size_t)r * tiles, tiles, tag, p.timeout_ns, c.fail)) *c.fail = 1;
     for (int b = warp; b < p.M; b += 4) {
       float s = 0.f;
       for (int j = lane; j < tiles; j += 32) s += __ldcg(pss + (size_t)(r * tiles + j) * p.act_rows + b);
       s = warp_sum(s);
-      if (lane == 0) c.ss[b] = s;
+      if (lane == 0) {
+        c.ss[b] = s;
+        c.rstd[b] = rsqrtf(s / (float)p.K + p.eps);  // final when splits == 1
+      }
+    }
+    if (cs == 1) {
+      // several tiles per CTA: accumulator -> registers -> scaled bf16 stores, row-major Y
+      epi_sync();
+      const int q = warp & 3;
+      __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(p.Y) + (p.emulate ? (size_t)rank * p.M * p.N : 0);
+      using C = FCfg<BN, SMALL>;
+      for (int i = 0; i < nt; ++i) {
+        const int acc = i & 1;
+        if (!mbar_wait(&c.tfull[acc], (i >> 1) & 1, p.timeout_ns)) *c.fail = 1;
+        __syncwarp();
+        tc_fence_after();
+        const int n = (t + i * tiles) * BM + q * 32 + lane;
+        const uint32_t taddr = tmem + acc * C::TC + ((uint32_t)(q * 32) << 16);
+        for (int c0 = 0; c0 < min(p.M, BN); c0 += 16) {
+          float v[16];
+          tmem_ld16(taddr + c0, v);
+          if (n < p.N && !*c.fail) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (c0 + j < p.M) Y[(size_t)(c0 + j) * p.N + n] = __float2bfloat16_rn(v[j] * c.rstd[c0 + j]);
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&c.tempty[acc])) : "memory");
+      }
+    } else {
+      tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
     }
   }
   __syncthreads();
   cg::cluster_group cluster = cg::this_cluster();
-  if (cs > 1) cluster.sync();
-  for (int b = threadIdx.x; b < p.M; b += kThreads) {
-    float s = 0.f;
-    for (int cc = 0; cc < cs; ++cc) s += cs > 1 ? *cluster.map_shared_rank(c.ss + b, cc) : c.ss[b];
-    c.rstd[b] = rsqrtf(s / (float)p.K + p.eps);
+  if (cs > 1) {
+    cluster.sync();
+    for (int b = threadIdx.x; b < p.M; b += kThreads) {
+      float s = 0.f;
+      for (int cc = 0; cc < cs; ++cc) s += *cluster.map_shared_rank(c.ss + b, cc);
+      c.rstd[b] = rsqrtf(s / (float)p.K + p.eps);
+    }
+    __syncthreads();
   }
-  __syncthreads();
   const int per = BM / cs, f0 = r * per, groups = per / 8;
-  if (!*c.fail) {
+  if (cs > 1 && !*c.fail) {
     float* part = reinterpret_cast<float*>(smem);
     __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(p.Y) + (p.emulate ? (size_t)rank * p.M * p.N : 0);
     for (int idx = threadIdx.x; idx < p.M * groups; idx += kThreads) {
@@ -530,7 +586,7 @@ cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUte
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.tiles, pl.splits, ranks);
+  cfg.gridDim = dim3(pl.xctas, pl.splits, ranks);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
@@ -581,18 +637,22 @@ cudaError_t check_common(const FusedGemmParams& p, const FusedGemmPlan& pl, int 
     return cudaErrorInvalidValue;
   if (pl.splits < 1 || pl.splits > 8 || BM % (8 * pl.splits) || pl.tiles != (p.N + BM - 1) / BM)
     return cudaErrorInvalidValue;
+  // several tiles per CTA only without split-K (the cluster epilogue holds one tile)
+  if (pl.xctas < 1 || pl.xctas > pl.tiles || (pl.splits > 1 && pl.xctas != pl.tiles)) return cudaErrorInvalidValue;
   if ((long long)pl.kps * (pl.splits - 1) >= p.K / BK) return cudaErrorInvalidValue;  // every split non-empty
   return cudaSuccess;
 }
 
 }  // namespace
 
-FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms) {
+FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer) {
   FusedGemmPlan pl = {};
   pl.bn = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
   pl.tiles = (N + BM - 1) / BM;
   const int KT = K / BK;
   const int per_sm = pl.bn <= 64 ? 2 : 1;
+  // ar_norm_gemm: the whole grid resident at once and one epoch word per CTA
+  const int cap = std::min(num_sms * per_sm, kMaxBlocks);
   if (splits <= 0) {
     // enough CTAs to keep every SM streaming weights, within one resident wave
     splits = 1;
@@ -602,8 +662,15 @@ FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms) {
   pl.splits = (KT + pl.kps - 1) / pl.kps;
   while (BM % (8 * pl.splits)) --pl.splits;
   pl.kps = (KT + pl.splits - 1) / pl.splits;
+  pl.xctas = pl.tiles;
+  if (consumer && pl.tiles * pl.splits > cap) {
+    // too many tiles for one resident wave: no split-K, each CTA loops over several tiles
+    pl.splits = 1;
+    pl.kps = KT;
+    pl.xctas = std::min(pl.tiles, cap);
+  }
   pl.smem = smem_of(pl.bn);
-  pl.ctas = pl.tiles * pl.splits;
+  pl.ctas = pl.xctas * pl.splits;
   return pl;
 }
 
@@ -611,6 +678,7 @@ cudaError_t launch_gemm_push(const FusedGemmParams& p, const CUtensorMap& tmW, c
                              const FusedGemmPlan& pl, int ranks, bool pdl, cudaStream_t stream) {
   cudaError_t e = check_common(p, pl, ranks);
   if (e != cudaSuccess) return e;
+  if (pl.xctas != pl.tiles) return cudaErrorInvalidValue;
   if (p.M > p.L.max_rows || p.N / 8 > p.L.max_hv || p.L.world != p.world) return cudaErrorInvalidValue;
   return launch_sel<true>(p, tmW, tmX, pl, ranks, pdl, stream);
 }
@@ -621,15 +689,15 @@ cudaError_t launch_ar_norm_gemm(const FusedGemmParams& p, const CUtensorMap& tmW
   if (e != cudaSuccess) return e;
   if (p.M > p.L.max_rows || p.K / 8 > p.L.max_hv || p.L.world != p.world || p.M > p.act_rows) return cudaErrorInvalidValue;
   // pieces per launch, and per-block epoch words written by every block (no two blocks share one)
-  if (pl.tiles * pl.splits > kMaxPieces || pl.tiles * pl.splits > kMaxBlocks) return cudaErrorInvalidValue;
+  if (pl.ctas > kMaxPieces || pl.ctas > kMaxBlocks) return cudaErrorInvalidValue;
   // every piece's per-item sums of squares fit in shared memory
   const int KV = p.K / 8, slen = std::min(KV, pl.kps * 8);
-  if ((long long)p.M * ((slen + pl.tiles - 1) / pl.tiles + 1) > kQCap) return cudaErrorInvalidValue;
+  if ((long long)p.M * ((slen + pl.xctas - 1) / pl.xctas + 1) > kQCap) return cudaErrorInvalidValue;
   // CTAs wait for pieces of other CTAs of the launch: the whole grid must be resident at once
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if ((long long)pl.tiles * pl.splits * ranks > (long long)sms * (pl.bn <= 64 ? 2 : 1)) return cudaErrorInvalidValue;
+  if ((long long)pl.ctas * ranks > (long long)sms * (pl.bn <= 64 ? 2 : 1)) return cudaErrorInvalidValue;
   return launch_sel<false>(p, tmW, tmA, pl, ranks, pdl, stream);
 }
 

@@ -44,10 +44,12 @@ struct FusedGemmParams {
 
 struct FusedGemmPlan {
   int bn, tiles, splits, kps, smem, ctas;
+  int xctas;  // CTAs along the output dimension (== tiles, or fewer looping over tiles when splits == 1)
 };
 
-// Geometry for M rows, N outputs, K inner: BN (MMA N) and the split count (0 = choose).
-FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms);
+// Geometry for M rows, N outputs, K inner: BN (MMA N) and the split count (0 = choose). `consumer`:
+// plan for ar_norm_gemm (whole grid resident, at most kMaxBlocks CTAs).
+FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer);
 
 // tmW: [ranks * N, K] weights, box 64 x 128; tmX: [rows, K] activations, box 64 x BN.
 cudaError_t launch_gemm_push(const FusedGemmParams& p, const CUtensorMap& tmW, const CUtensorMap& tmX,

@@ -9,8 +9,9 @@ per-rank mean over calls:
   sent / reduced / received / done : latest block's stamp - earliest block's start of the same call
   gap                              : next call's earliest start - this call's latest done, for calls
                                      back to back in one CUDA graph (launch + epoch hand-over cost)
-  skew                             : spread of the calls' start stamps across ranks (the timers of
-                                     different GPUs are not synchronised exactly; read as indicative)
+  skew                             : spread of the calls' start stamps across ranks, reported only when
+                                     the GPUs' %globaltimer clocks agree to within 1 ms (they are not
+                                     synchronised across GPUs in general)
   op_us / op_us_stamped            : graph time per call without and with stamps (stamping overhead)
 
     timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 \
@@ -141,7 +142,8 @@ def main():
                         row[k] = max(vals) if vals else None
                     n = min(len(r[3]) for r in allr)
                     skews = [max(r[3][i] for r in allr) - min(r[3][i] for r in allr) for i in range(n)]
-                    row["skew"] = summary([s / 1000.0 for s in skews])["p50"] if skews else None
+                    sk = summary([s / 1000.0 for s in skews])["p50"] if skews else None
+                    row["skew"] = sk if sk is not None and sk < 1000.0 else None
                 rows.append(row)
                 fmt = lambda k: "   -  " if row.get(k) is None else f"{row[k]:6.2f}"  # noqa: E731
                 print(f"{v:11s} T{T:4d} op {fmt('op_us')} (stamped {fmt('op_us_stamped')})  sent {fmt('sent')} "

@@ -80,7 +80,7 @@ def plan_layout_py(world: int, max_rows: int, max_hidden: int, esize: int, max_g
     take("land1", 2 * W * R * HV * 16)
     take("rs", 2 * W * R * SV * 16)
     take("ag", 2 * W * R * SV * 16)
-    pu = (HV + 511) // 512  # partial-sum units per owner slice (kernels: ceil(hv / 512))
+    pu = (SV + 31) // 32  # partial-sum units per owner slice (32 vectors each)
     take("agp", 2 * W * R * pu * 8)
     take("stage", 2 * R * HV * 16)
     take("hbuf", R * HV * 16)

@@ -104,3 +104,28 @@ def test_layer_boundary_70b_tp8_shapes(cuda, M):
     for r in range(world):
         assert rel_err(res[r], h_ref) <= TOL
         assert rel_err(out[r], out_ref[r]) <= TOL
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_layer_boundary_many_tiles(cuda, world):
+    """More output tiles than resident CTAs: ar_norm_gemm drops split-K and loops over tiles per CTA
+    (double-buffered accumulators), as for gate_up / the LM head at TP <= 4."""
+    M, K1, H, N2, eps = 8, 256, 1024, 8192, 1e-5
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=16, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(world)
+    w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    w2 = (0.05 * torch.randn(world, N2, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res = torch.randn(M, H, generator=g, device=cuda).bfloat16().unsqueeze(0).repeat(world, 1, 1).contiguous()
+    for it in range(2):
+        x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+        before = res[0].clone()
+        out = layer_boundary(comm, x, w1, res, gamma, w2, eps)
+        torch.cuda.synchronize()
+        comm.check()
+        kind, plan = comm.last_fused_gemm
+        assert plan[2] == 1 and plan[4] < plan[1], plan  # no split-K, fewer CTAs than tiles
+        h_ref, out_ref = reference(x, w1, before, gamma, w2, eps)
+        for r in range(world):
+            assert rel_err(res[r], h_ref) <= TOL
+            assert rel_err(out[r], out_ref[r]) <= TOL, (it, r, rel_err(out[r], out_ref[r]))
