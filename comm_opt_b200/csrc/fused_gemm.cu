@@ -511,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
     if (cs == 1) {
       // several tiles per CTA: accumulator -> registers -> scaled bf16 stores, row-major Y
       epi_sync();
-      const int q = warp & 3;
+      const int q = (threadIdx.x >> 5) & 3;  // TMEM lane quarter a warp may access: warp id % 4
       __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(p.Y) + (p.emulate ? (size_t)rank * p.M * p.N : 0);
       using C = FCfg<BN, SMALL>;
       for (int i = 0; i < nt; ++i) {

@@ -110,7 +110,7 @@ def test_layer_boundary_70b_tp8_shapes(cuda, M):
 def test_layer_boundary_many_tiles(cuda, world):
     """More output tiles than resident CTAs: ar_norm_gemm drops split-K and loops over tiles per CTA
     (double-buffered accumulators), as for gate_up / the LM head at TP <= 4."""
-    M, K1, H, N2, eps = 8, 256, 1024, 8192, 1e-5
+    M, K1, H, N2, eps = 8, 256, 1024, 24576, 1e-5  # 192 output tiles > resident CTAs per rank
     comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=16, max_hidden=H)
     g = torch.Generator(device=cuda).manual_seed(world)
     w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
