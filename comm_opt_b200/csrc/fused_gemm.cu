@@ -583,6 +583,9 @@ cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUte
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
+    // clusters of 16 CTAs (split-K 16 for narrow outputs such as QKV at TP=8) are non-portable
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
     attr = true;
   }
   cudaLaunchConfig_t cfg = {};
@@ -635,7 +638,7 @@ cudaError_t check_common(const FusedGemmParams& p, const FusedGemmPlan& pl, int 
   if (p.M <= 0 || p.M > 128 || p.N % 8 || p.K % BK || p.N <= 0 || p.K <= 0) return cudaErrorInvalidValue;
   if (p.world < 1 || p.world > kMaxWorld || ranks < 1 || (p.emulate ? ranks != p.world : ranks != 1))
     return cudaErrorInvalidValue;
-  if (pl.splits < 1 || pl.splits > 8 || BM % (8 * pl.splits) || pl.tiles != (p.N + BM - 1) / BM)
+  if (pl.splits < 1 || pl.splits > 16 || BM % (8 * pl.splits) || pl.tiles != (p.N + BM - 1) / BM)
     return cudaErrorInvalidValue;
   // several tiles per CTA only without split-K (the cluster epilogue holds one tile)
   if (pl.xctas < 1 || pl.xctas > pl.tiles || (pl.splits > 1 && pl.xctas != pl.tiles)) return cudaErrorInvalidValue;
@@ -656,7 +659,10 @@ FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool
   if (splits <= 0) {
     // enough CTAs to keep every SM streaming weights, within one resident wave
     splits = 1;
-    while (splits < 8 && pl.tiles * splits * 2 <= num_sms * per_sm && KT / (splits * 2) >= 2) splits *= 2;
+    // (up to 16: a non-portable cluster size, co-scheduled as 8 SMs x 2 CTAs)
+    const int smax = per_sm == 2 ? 16 : 8;
+    const int lim = consumer ? cap : num_sms * per_sm;
+    while (splits < smax && pl.tiles * splits * 2 <= lim && KT / (splits * 2) >= 2) splits *= 2;
   }
   pl.kps = (KT + splits - 1) / splits;
   pl.splits = (KT + pl.kps - 1) / pl.kps;

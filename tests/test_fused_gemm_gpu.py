@@ -129,3 +129,24 @@ def test_layer_boundary_many_tiles(cuda, world):
         for r in range(world):
             assert rel_err(res[r], h_ref) <= TOL
             assert rel_err(out[r], out_ref[r]) <= TOL, (it, r, rel_err(out[r], out_ref[r]))
+
+
+def test_layer_boundary_split16(cuda):
+    """Split-K over a 16-CTA (non-portable) cluster, the plan for narrow outputs such as QKV at TP=8."""
+    world, M, K1, H, N2, eps = 2, 8, 512, 2048, 1280, 1e-5
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=8, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(16)
+    w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    w2 = (0.05 * torch.randn(world, N2, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res0 = torch.randn(M, H, generator=g, device=cuda).bfloat16()
+    res = res0.unsqueeze(0).repeat(world, 1, 1).contiguous()
+    x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+    out = layer_boundary(comm, x, w1, res, gamma, w2, eps, splits2=16)
+    torch.cuda.synchronize()
+    comm.check()
+    assert comm.last_fused_gemm[1][2] == 16
+    h_ref, out_ref = reference(x, w1, res0, gamma, w2, eps)
+    for r in range(world):
+        assert rel_err(res[r], h_ref) <= TOL
+        assert rel_err(out[r], out_ref[r]) <= TOL
