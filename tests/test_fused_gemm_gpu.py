@@ -133,7 +133,7 @@ def test_layer_boundary_many_tiles(cuda, world):
 
 def test_layer_boundary_split16(cuda):
     """Split-K over a 16-CTA (non-portable) cluster, the plan for narrow outputs such as QKV at TP=8."""
-    world, M, K1, H, N2, eps = 2, 8, 512, 2048, 1280, 1e-5
+    world, M, K1, H, N2, eps = 2, 8, 512, 2048, 640, 1e-5
     comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=8, max_hidden=H)
     g = torch.Generator(device=cuda).manual_seed(16)
     w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
