@@ -42,8 +42,9 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--gemm", choices=["cob", "torch"], default="cob")
-    p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=0,
-                   help="fuse o_proj/down_proj -> all-reduce + RMSNorm -> next GEMM (TP > 1)")
+    p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=1,
+                   help="fuse o_proj/down_proj -> all-reduce + RMSNorm -> next GEMM (TP > 1; 0 = separate "
+                        "GEMM, fused all-reduce + RMSNorm kernel, GEMM)")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--layers", type=int, default=None, help="override the layer count (debug only; invalid for bench)")
     p.add_argument("--out", default=None, help="also write the JSON line to this file")
@@ -223,6 +224,7 @@ def main():
             "config": {"model": cfg.name + ("" if args.layers is None else f"-L{cfg.layers}-INVALID"),
                        "global_batch": B, "seq_len": P, "decode_tokens_timed": K, "parallelism": f"tp{world}",
                        "gemm": args.gemm, "fuse_boundary": runner.fuse_boundary,
+                       "fuse_fallback": runner.fuse_error[:200] or None,
                        "tokens_per_s": round(B * 1000.0 / ms, 1),
                        "l2": "no flush: each step streams the full weight set (141 GB / N) >> 126 MB L2",
                        "setup_s": round(setup_s, 1)},

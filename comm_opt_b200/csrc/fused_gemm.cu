@@ -16,6 +16,8 @@
 // ar_norm_gemm (all-reduce + residual + RMSNorm -> column-parallel GEMM)
 //   warp 0 : weight tiles for the first ring slots at once (they do not depend on anything), then
 //            waits for the activation pieces of its split and streams activation + weight tiles.
+//            Launched with programmatic dependent launch, the weight stream overlaps the tail of the
+//            preceding gemm_push; the pieces wait for it to complete (griddepcontrol.wait) first.
 //   warp 1 : tcgen05.mma issuer.
 //   warps 2-5 : first the "piece" of the all-reduce this CTA owns: a [M, ~K / CTAs] block of the
 //            landing buffers, polled per 16-byte vector (Lamport), summed over ranks with the
@@ -209,7 +211,7 @@ __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtenso
         }
       }
       *c.issued = issued;
-      if (!WAIT_ACT) pdl_trigger();
+      pdl_trigger();  // every load is issued: the next kernel may start its prologue
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -407,9 +409,11 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   uint32_t* flags = p.flags + (size_t)wsr * kMaxPieces;
   float* pss = p.pss + (size_t)wsr * kMaxPieces * p.act_rows;
   const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, &tmW, &tmA);
-  // No griddepcontrol.wait: nothing read here is written by the immediately preceding kernel
-  // (partials arrive through Lamport landing buffers, the epoch / residual / pieces were written by
-  // kernels that completed before the preceding one passed its own wait).
+  // The weight stream needs nothing from earlier kernels and starts at once (warp 0). The pieces
+  // (warps 2-5) first wait, in hardware, for the preceding kernel - this rank's gemm_push - to
+  // complete, so on this GPU nothing spins on a kernel that runs concurrently; the polls that
+  // follow only wait for the other ranks' pushes. The epoch was written by a kernel that completed
+  // before the preceding one passed its own wait.
   const uint64_t e = fg_epoch(p, rank);
   const uint32_t tag = (uint32_t)e;
   const int slot = (int)(e & 1);
@@ -419,6 +423,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
 
   if (threadIdx.x >= 64) {
     const int tid = threadIdx.x - 64;
+    pdl_wait();
     // ---------------- this CTA's piece of the all-reduce: vectors [vb, ve) of every row
     const int s0 = k0 * 8, slen = min(KV, (k0 + p.kps) * 8) - s0;
     const int vb = s0 + (int)((long long)slen * t / tiles), ve = s0 + (int)((long long)slen * (t + 1) / tiles);

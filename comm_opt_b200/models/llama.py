@@ -201,6 +201,7 @@ class TPDecodeRunner:
         # all-reduce landing buffers, and the all-reduce + residual + RMSNorm runs inside the next
         # GEMM (gate_up, the next layer's qkv, the LM head); needs TP > 1, bf16 and this package's GEMMs
         self.fuse_boundary = bool(fuse_boundary and self.tp > 1 and self.dtype == torch.bfloat16 and gemm == "cob")
+        self.fuse_error = ""
         if self.fuse_boundary:
             comm.prepare_fused_gemm(cfg.hidden)
 
@@ -365,8 +366,22 @@ class TPDecodeRunner:
         saved = {k: v.clone() for k, v in buf.items() if k in ("ids", "pos", "lens")}
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(s):
-            self._step(B, buf)  # warm-up outside the graph (also compiles lazy modules)
+        try:
+            with torch.cuda.stream(s):
+                self._step(B, buf)  # warm-up outside the graph (also compiles lazy modules)
+        except RuntimeError as e:
+            if not self.fuse_boundary:
+                raise
+            # a fused layer boundary rejected this geometry (the launcher's residency / capacity
+            # checks, identical on every rank): re-initialise the collective state and run unfused
+            torch.cuda.synchronize(self.device)
+            self.comm.reset()
+            self.fuse_boundary = False
+            self.fuse_error = str(e)
+            for k, v in saved.items():
+                buf[k].copy_(v)
+            with torch.cuda.stream(s):
+                self._step(B, buf)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         for k, v in saved.items():

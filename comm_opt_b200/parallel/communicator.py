@@ -55,7 +55,7 @@ def default_timeout_ms() -> float:
 class TPCommunicator:
     def __init__(self, group=None, *, emulate_world: int | None = None, device=None, dtype=torch.bfloat16,
                  max_rows: int = 512, max_hidden: int = 8192, max_gather: int = 4096,
-                 timeout_ms: float | None = None, pdl: bool = False, table: VariantTable | None = None,
+                 timeout_ms: float | None = None, pdl: bool = True, table: VariantTable | None = None,
                  allow_nvls: bool = True, backend: str = "symm_mem"):
         import torch.distributed as dist
 
