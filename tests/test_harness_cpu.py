@@ -70,3 +70,34 @@ def test_trace_decomposition(tmp_path):
     assert abs(r0["idle_us"] - (100 - 70)) < 1e-6
     r1 = next(r for r in rows if r["rank"] == 1)
     assert r1["exposed_wait_us"] > 0 and abs(r1["exposed_transfer_us"] + r1["exposed_wait_us"] - r1["exposed_comm_us"]) < 1e-9
+
+
+def test_phase_decomposition_from_stamps():
+    """Synthetic stamps of 2 graph replays x 3 calls, 2 blocks: phases, inter-call gap within a replay."""
+    import torch
+
+    from comm_opt_b200.harness.phase_profile import decompose
+
+    cap, blocks, ops = 16, 2, 3
+    st = torch.zeros(cap, 160, 5, dtype=torch.int64)
+    t = 1_000_000
+    epochs = list(range(5, 11))
+    for e in epochs:
+        for b in range(blocks):
+            st[e % cap, b] = torch.tensor([t + 100 * b, t + 500, 0, t + 3000, t + 4000 + 100 * b])
+        t += 4100 + 900  # 0.9 us gap to the next call
+    ph, starts = decompose(st, epochs, blocks, ops)
+    assert abs(ph["sent"] - 0.5) < 1e-9 and abs(ph["received"] - 3.0) < 1e-9 and abs(ph["done"] - 4.1) < 1e-9
+    assert ph["reduced"] is None  # phase not stamped by this variant
+    assert abs(ph["gap"] - 0.9) < 1e-9 and len(starts) == 6
+
+
+def test_bakeoff_shapes_and_runner_entries():
+    from comm_opt_b200.harness.allreduce_bakeoff import shape_of
+    from comm_opt_b200.harness.runner import ENTRY, Job, command
+
+    assert shape_of(1024, 2) == (1, 512) and shape_of(8 << 20, 2) == (512, 8192) and shape_of(48 << 10, 2) == (3, 8192)
+    for e in ("bakeoff", "phases", "collectives", "fused_sweep", "selftest"):
+        assert e in ENTRY
+    cmd, env = command(Job("bakeoff", 8), ROOT / "results" / "x", 29999)
+    assert "--out-dir" in cmd and env["CUDA_VISIBLE_DEVICES"] == "0,1,2,3,4,5,6,7"
