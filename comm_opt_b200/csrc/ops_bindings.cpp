@@ -233,9 +233,41 @@ std::vector<int64_t> py_clock_calibration(int64_t ns, int64_t device) {
   return {h[0].item<int64_t>(), h[1].item<int64_t>()};
 }
 
+std::vector<int64_t> py_prim_layout(int64_t world, int64_t n) {
+  long long f = 0, st = 0, l = 0;
+  const size_t total = cob::prim_heap_bytes((int)world, (int)n, &f, &st, &l);
+  return {(int64_t)total, f, st, l};
+}
+
+void py_prim_probe(std::vector<int64_t> bases, std::vector<int64_t> offs, int64_t rank, int64_t n, int64_t mode,
+                   int64_t emulate, int64_t blocks, int64_t threads, int64_t timeout_ns, torch::Tensor bad,
+                   torch::Tensor err) {
+  COB_CHECK(bases.size() >= 1 && bases.size() <= 8 && offs.size() == 3, "world 1..8, offsets {flags, stage, land}");
+  COB_CHECK(bad.is_cuda() && bad.scalar_type() == torch::kInt32 && err.is_cuda() && err.scalar_type() == torch::kInt32,
+            "bad / err must be CUDA int32");
+  cob::PrimParams p = {};
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
+  p.flags_off = offs[0];
+  p.stage_off = offs[1];
+  p.land_off = offs[2];
+  p.rank = (int)rank;
+  p.world = (int)bases.size();
+  p.n = (int)n;
+  p.mode = (int)mode;
+  p.emulate = (int)emulate;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.bad = reinterpret_cast<unsigned int*>(bad.data_ptr());
+  p.err = err.data_ptr<int32_t>();
+  COB_CHECK(bad.numel() >= (emulate ? p.world : 1), "bad must hold one word per local rank");
+  const c10::cuda::CUDAGuard g(bad.device());
+  ok(cob::prim_probe(p, (int)blocks, (int)threads, cur()), "prim_probe");
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
+  m.def("prim_layout", &py_prim_layout);
+  m.def("prim_probe", &py_prim_probe);
   m.def("rs_atomic_probe", &py_rs_atomic_probe);
   m.def("clock_calibration", &py_clock_calibration);
   m.def("gemm", &py_gemm);

@@ -17,6 +17,26 @@ struct RsProbeParams {
 };
 
 cudaError_t rs_atomic_probe(const RsProbeParams& p, int blocks, cudaStream_t s);
+
+// Push-vs-pull primitives over NVLink (all-gather and reduce-scatter of n 32-bit words per rank).
+// Probe heap per rank (same offsets on every rank):
+//   [0, 8 * kPrimMaxBlocks)                   u64 per-block epoch words (this rank only)
+//   flags: u64 [kPrimMaxBlocks][8]            flag-barrier slots written by peers (pull forms)
+//   stage: u32 [2][n]                         staged input for the pull forms (by epoch parity)
+//   land : u32 [2][8][n / world]              Lamport landing for the push forms (sentinel 0x80000000)
+// Payload words are a hash of (source rank, index, epoch) so data of an earlier call is detected.
+constexpr int kPrimMaxBlocks = 256;
+enum PrimMode : int { kAgPull = 0, kAgPush = 1, kRsPull = 2, kRsPush = 3 };
+struct PrimParams {
+  char* base[8];
+  long long flags_off, stage_off, land_off;  // byte offsets in every heap
+  int rank, world, n, mode, emulate;
+  unsigned long long timeout_ns;
+  unsigned int* bad;  // [ranks] words whose value did not match the expected payload
+  int* err;           // set on a timed-out wait
+};
+size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off);
+cudaError_t prim_probe(const PrimParams& p, int blocks, int threads, cudaStream_t s);
 // out[0] = SM cycles, out[1] = %globaltimer nanoseconds over a spin of `ns` nanoseconds
 cudaError_t clock_calibration(unsigned long long ns, long long* out, cudaStream_t s);
 

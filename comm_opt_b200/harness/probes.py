@@ -1,4 +1,5 @@
-"""Primitive probes: reduce-scatter by remote atomics (four `red` forms) and SM clock calibration.
+"""Primitive probes: reduce-scatter by remote atomics (four `red` forms), push vs pull all-gather /
+reduce-scatter primitives in steady state, and SM clock calibration.
 
     python -m comm_opt_b200.harness.probes --emulate 8                 (all ranks on one GPU)
     timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 \
@@ -92,10 +93,79 @@ def run_rs(world: int, n: int, variant: int, dev, emulate: bool, blocks: int = 6
                 push_gbs=round((world - 1) * n * es / t / 1e3, 1), rel_err=rel, timeout=bool(e))
 
 
+PRIM_MODES = {0: "ag_pull", 1: "ag_push", 2: "rs_pull", 3: "rs_push"}
+
+
+def run_prim(world: int, n: int, mode: int, dev, emulate: bool, blocks: int = 64, threads: int = 256,
+             graph_ops: int = 20, replays: int = 10, group=None, timeout_ms: float = 1000.0) -> dict:
+    """Steady state (the reference's M13 'steady' mode): `graph_ops` launches per CUDA graph on buffers
+    that are never cleared between launches; every word is checked against its (rank, index, epoch)
+    hash inside the kernel. n = 32-bit words per rank (AG: n / world contributed, n gathered; RS: n
+    contributed, n / world reduced). Returns per-op p50 us (max over ranks) and the mismatch count."""
+    C = native()
+    total, f_off, st_off, l_off = C.prim_layout(world, n)
+    rank = 0 if emulate else dist.get_rank(group)
+    S = n // world
+    if emulate:
+        heap = torch.zeros(world * total, dtype=torch.uint8, device=dev)
+        bases = [heap.data_ptr() + r * total for r in range(world)]
+        for r in range(world):
+            heap[r * total + l_off: (r + 1) * total].view(torch.int32).fill_(-2 ** 31)
+    else:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        heap = symm_mem.empty(total, dtype=torch.uint8, device=dev)
+        heap.zero_()
+        heap[l_off:].view(torch.int32).fill_(-2 ** 31)
+        bases = list(symm_mem.rendezvous(heap, group or dist.group.WORLD).buffer_ptrs)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+    bad = torch.zeros(world if emulate else 1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def call():
+        C.prim_probe(bases, [f_off, st_off, l_off], rank, n, mode, int(emulate), blocks, threads,
+                     int(timeout_ms * 1e6), bad, err)
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    if not emulate:
+        dist.barrier(group=group)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(graph_ops):
+            call()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(replays + 1)]
+    g.replay()
+    torch.cuda.synchronize()
+    if not emulate:
+        dist.barrier(group=group)
+    ev[0].record()
+    for i in range(replays):
+        g.replay()
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    times = sorted(ev[i].elapsed_time(ev[i + 1]) * 1000.0 / graph_ops for i in range(replays))
+    t = times[len(times) // 2]
+    nbad, nerr = float(bad.sum().item()), float(err.item())
+    del g
+    if not emulate:
+        tt = torch.tensor([t, nbad, nerr], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
+        t, nbad, nerr = [float(v) for v in tt.cpu()]
+        dist.barrier(group=group)
+    moved = (world - 1) * S * 4  # bytes each rank sends over NVLink per call
+    return dict(mode=PRIM_MODES[mode], world=world, emulated=emulate, words=n, us=round(t, 2),
+                link_gbs=round(moved / t / 1e3, 1), bad_words=int(nbad), timeout=bool(nerr),
+                calls=3 + graph_ops * (replays + 1))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--emulate", type=int, default=0, help="run W ranks in one launch on one GPU")
     ap.add_argument("--sizes", default="10240,81920,655360")
+    ap.add_argument("--prim", action="store_true", help="push vs pull primitives instead of the atomic RS probe")
     ap.add_argument("--out", default=None)
     a = ap.parse_args()
     rows = []
@@ -110,8 +180,9 @@ def main():
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         world, rank = dist.get_world_size(), dist.get_rank()
     for n in [int(s) for s in a.sizes.split(",")]:
-        for v in VARIANTS:
-            r = run_rs(world, n, v, dev, bool(a.emulate))
+        for v in (PRIM_MODES if a.prim else VARIANTS):
+            n_w = n // (4 * world) * 4 * world if a.prim else n
+            r = run_prim(world, n_w, v, dev, bool(a.emulate)) if a.prim else run_rs(world, n, v, dev, bool(a.emulate))
             rows.append(r)
             if rank == 0:
                 print(json.dumps(r), flush=True)

@@ -18,3 +18,16 @@ def test_rs_atomic_emulated(cuda, world, variant):
 def test_clock_calibration(cuda):
     mhz = clock_mhz(0, ns=5_000_000)
     assert 100 < mhz < 3000
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
+def test_push_pull_primitives_steady_state(cuda, world, mode):
+    """All-gather / reduce-scatter in pull and push form, K launches per graph on never-cleared buffers:
+    every word matches its (rank, index, epoch) hash, no wait times out."""
+    from comm_opt_b200.harness.probes import run_prim
+
+    r = run_prim(world, 4096 * world, mode, cuda, emulate=True, blocks=8, threads=128, graph_ops=8, replays=3,
+                 timeout_ms=100)
+    assert r["bad_words"] == 0 and not r["timeout"], r
+    assert r["us"] > 0
