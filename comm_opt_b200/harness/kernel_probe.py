@@ -1,0 +1,115 @@
+"""Single-kernel drivers on one GPU: a fixed, small workload per hot kernel, timed with CUDA events
+(warm-up, then `--iters` launches, p50), and the command a profiler capture of that kernel runs.
+
+    python -m comm_opt_b200.harness.kernel_probe fused_ar --variant lamport_1s --world 2 --rows 8
+    python -m comm_opt_b200.harness.kernel_probe attention --batch 8 --ctx 2048
+    python -m comm_opt_b200.harness.kernel_probe decode_ops --batch 8
+    ncu --set full --clock-control none -k regex:k_oneshot -s 3 -c 1 -o oneshot \
+        python -m comm_opt_b200.harness.kernel_probe fused_ar --variant lamport_1s --world 2 --rows 8 --iters 4
+
+Shapes default to one Llama-70B TP=8 rank: hidden 8192, 8 query heads / 1 KV head of 128, SwiGLU
+shard 3584. Fused-op ranks are emulated in one launch (see TPCommunicator(emulate_world=...)).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import torch
+
+from ..ops import kernels as K
+from ..ops.reference import rope_tables
+from ..parallel import TPCommunicator
+
+
+def timed(fn, iters: int) -> dict:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(iters + 1)]
+    ev[0].record()
+    for i in range(iters):
+        fn()
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    us = sorted(ev[i].elapsed_time(ev[i + 1]) * 1000.0 for i in range(iters))
+    return dict(p50_us=round(us[len(us) // 2], 3), min_us=round(us[0], 3), iters=iters)
+
+
+def fused_ar(a, dev) -> dict:
+    comm = TPCommunicator(emulate_world=a.world, device=dev, dtype=torch.bfloat16, max_rows=a.rows, max_hidden=a.hidden)
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(a.world, a.rows, a.hidden, generator=g, device=dev).bfloat16()
+    res = torch.randn(a.world, a.rows, a.hidden, generator=g, device=dev).bfloat16()
+    gamma = torch.ones(a.hidden, device=dev).bfloat16()
+    out = torch.empty_like(x)
+    r = timed(lambda: comm.fused_allreduce_add_rmsnorm(x, res, gamma, 1e-6, out=out, variant=a.variant), a.iters)
+    comm.check()
+    return dict(r, variant=a.variant, world=a.world, rows=a.rows, hidden=a.hidden, choice=comm.last_choice.__dict__,
+                bytes_per_rank=a.rows * a.hidden * 2)
+
+
+def attention(a, dev) -> dict:
+    B, nq, nkv, D, blk = a.batch, a.heads, a.kv_heads, 128, 16
+    pages = (a.ctx + blk - 1) // blk
+    nblocks = B * pages + 16
+    g = torch.Generator(device=dev).manual_seed(0)
+    kc = torch.randn(nblocks, nkv, blk, D, generator=g, device=dev).bfloat16()
+    vc = torch.randn(nblocks, nkv, blk, D, generator=g, device=dev).bfloat16()
+    perm = torch.randperm(nblocks, generator=torch.Generator().manual_seed(1))[:B * pages]
+    bt = perm.view(B, pages).to(torch.int32).to(dev)
+    lens = torch.full((B,), a.ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, nq, D, generator=g, device=dev).bfloat16()
+    out = torch.empty_like(q)
+    op = K.DecodeAttention(B, nq, nkv, D, pages, dev, torch.cuda.get_device_properties(dev).multi_processor_count)
+    r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5), a.iters)
+    kv_bytes = 2 * B * nkv * a.ctx * D * 2
+    return dict(r, batch=B, ctx=a.ctx, heads=nq, kv_heads=nkv, splits=op.splits, pages_per_split=op.pps,
+                cluster=op.cluster, kv_bytes=kv_bytes)
+
+
+def decode_ops(a, dev) -> dict:
+    B, H, nq, nkv, D, inter = a.batch, a.hidden, a.heads, a.kv_heads, 128, a.inter
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(B, H, generator=g, device=dev).bfloat16()
+    gamma = torch.ones(H, device=dev).bfloat16()
+    h = torch.empty_like(x)
+    qkv = torch.randn(B, (nq + 2 * nkv) * D, generator=g, device=dev).bfloat16()
+    pages = 8
+    kc = torch.zeros(B * pages, nkv, 16, D, device=dev).bfloat16()
+    vc = torch.zeros_like(kc)
+    bt = torch.arange(B * pages, dtype=torch.int32, device=dev).view(B, pages)
+    pos = torch.full((B,), 100, dtype=torch.int32, device=dev)
+    cos, sin = rope_tables(256, D, 5e5, dev)
+    q = torch.empty(B, nq, D, device=dev).bfloat16()
+    gu = torch.randn(B, 2 * inter, generator=g, device=dev).bfloat16()
+    act = torch.empty(B, inter, device=dev).bfloat16()
+    out = {}
+    out["rmsnorm"] = timed(lambda: K.rmsnorm(x, gamma, 1e-5, out=h), a.iters)
+    out["rope_append"] = timed(lambda: K.rope_append_kv(qkv, pos, cos, sin, bt, q, kc, vc, nq, nkv), a.iters)
+    out["silu_mul"] = timed(lambda: K.silu_mul(gu, out=act), a.iters)
+    return dict(batch=B, hidden=H, inter=inter, **out)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["fused_ar", "attention", "decode_ops"])
+    ap.add_argument("--variant", default="lamport_1s")
+    ap.add_argument("--world", type=int, default=2)
+    ap.add_argument("--rows", type=int, default=8)
+    ap.add_argument("--hidden", type=int, default=8192)
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--heads", type=int, default=8)
+    ap.add_argument("--kv-heads", type=int, default=1)
+    ap.add_argument("--inter", type=int, default=3584)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    r = {"fused_ar": fused_ar, "attention": attention, "decode_ops": decode_ops}[a.kernel](a, dev)
+    print(json.dumps(dict(kernel=a.kernel, **r)))
+
+
+if __name__ == "__main__":
+    main()
