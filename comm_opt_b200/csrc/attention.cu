@@ -105,7 +105,7 @@ __host__ __device__ constexpr size_t attn_smem_bytes() {
          (size_t)kWarps * kStages * 8 + kMaxPagesPerSplit * 4 + 64;
 }
 
-// CLUSTER: the splits of one (sequence, kv head) pair form a thread-block cluster (splits <= 8) and
+// CLUSTER: the splits of one (sequence, kv head) pair form a thread-block cluster (splits <= 16) and
 // are merged through distributed shared memory; otherwise they are merged through the global
 // scratch by the last split to finish.
 template <typename T, bool CLUSTER>
@@ -135,20 +135,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   const int pg0 = split * p.pages_per_split, pg1 = min(npages, pg0 + p.pages_per_split);
   for (int i = threadIdx.x; i < pg1 - pg0; i += blockDim.x)
     s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
-  const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
-  for (int c = threadIdx.x; c < kRows * CH; c += blockDim.x) {
-    const int r = c / CH, ch = c % CH;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < G) v = reinterpret_cast<const uint4*>(q + (size_t)r * kD)[ch];
-    *reinterpret_cast<uint4*>(sQ + swz(r, ch)) = v;
-  }
-  __syncthreads();
-  uint32_t qa[kD / 16][4];
-#pragma unroll
-  for (int ks = 0; ks < kD / 16; ++ks) {
-    const int r = lane & 15, ch = ks * 2 + (lane >> 4);
-    ldsm_x4(qa[ks], sQ + swz(r, ch));
-  }
+  __syncthreads();  // page list (and the barrier initialisation) visible to every warp
 
   T* myKV = sKV + (size_t)warp * kStages * 2 * kPageElems;
   uint64_t* mybar = bars + warp * kStages;
@@ -169,6 +156,21 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   };
 #pragma unroll
   for (int i = 0; i < kStages; ++i) issue(i);
+  // the query tile is staged while the first pages are in flight
+  const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
+  for (int c = threadIdx.x; c < kRows * CH; c += blockDim.x) {
+    const int r = c / CH, ch = c % CH;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < G) v = reinterpret_cast<const uint4*>(q + (size_t)r * kD)[ch];
+    *reinterpret_cast<uint4*>(sQ + swz(r, ch)) = v;
+  }
+  __syncthreads();
+  uint32_t qa[kD / 16][4];
+#pragma unroll
+  for (int ks = 0; ks < kD / 16; ++ks) {
+    const int r = lane & 15, ch = ks * 2 + (lane >> 4);
+    ldsm_x4(qa[ks], sQ + swz(r, ch));
+  }
 
   const float sl2 = p.scale * kLog2e;
   float o[kD / 8][4];
@@ -409,11 +411,15 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const size_t smem = attn_smem_bytes();
   const dim3 grid(p.splits, p.nkv, p.batch);
-  const bool cluster = p.cluster && p.splits > 1 && p.splits <= 8;
+  const bool cluster = p.cluster && p.splits > 1 && p.splits <= 16;
   auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true> : k_decode_attn<__nv_bfloat16, false>)
                  : (cluster ? k_decode_attn<__half, true> : k_decode_attn<__half, false>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
+  if (cluster && p.splits > 8) {  // clusters of 9..16 CTAs are non-portable (two CTAs per SM here)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
   if (!cluster) return launch_k(fn, grid, dim3(kWarps * 32), smem, s, a);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;

@@ -100,8 +100,9 @@ def test_decode_attention(cuda, nq, nkv, dtype):
             attn(q, kc, vc, bt, seq, out, scale)
             torch.cuda.synchronize()
             assert rel_err(out, ref) <= 2 ** -7, (num_sms, attn.splits, attn.cluster, rel_err(out, ref))
-    for splits, cl in [(2, True), (3, True), (5, True), (8, True), (40, False), (13, False)]:
-        attn = K.DecodeAttention(B, nq, nkv, D, maxb, cuda)  # cluster merge for <= 8 splits, global above
+    # cluster merge up to 16 splits (9..16: non-portable cluster sizes), global merge otherwise
+    for splits, cl in [(2, True), (3, True), (5, True), (8, True), (10, True), (16, True), (40, False), (13, False)]:
+        attn = K.DecodeAttention(B, nq, nkv, D, maxb, cuda)
         attn.splits, attn.pps, attn.cluster = splits, -(-maxb // splits), cl
         attn.splits = -(-maxb // attn.pps)
         from comm_opt_b200._ext import native
