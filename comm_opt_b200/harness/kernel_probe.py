@@ -1,5 +1,6 @@
 """Single-kernel drivers on one GPU: a fixed, small workload per hot kernel, timed with CUDA events
-(warm-up, then `--iters` launches, p50), and the command a profiler capture of that kernel runs.
+(warm-up, then `--iters` launches, p50; `--graph K` times graphs of K back-to-back launches, which
+removes the host launch interval), and the command a profiler capture of that kernel runs.
 
     python -m comm_opt_b200.harness.kernel_probe fused_ar --variant lamport_1s --world 2 --rows 8
     python -m comm_opt_b200.harness.kernel_probe attention --batch 8 --ctx 2048
@@ -22,18 +23,29 @@ from ..ops.reference import rope_tables
 from ..parallel import TPCommunicator
 
 
+GRAPH_OPS = 0  # > 0: time graphs of this many back-to-back launches (device time per launch)
+
+
 def timed(fn, iters: int) -> dict:
     for _ in range(3):
         fn()
     torch.cuda.synchronize()
+    per, g = 1, None
+    if GRAPH_OPS > 0:
+        per, g = GRAPH_OPS, torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(per):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(iters + 1)]
     ev[0].record()
     for i in range(iters):
-        fn()
+        g.replay() if g is not None else fn()
         ev[i + 1].record()
     torch.cuda.synchronize()
-    us = sorted(ev[i].elapsed_time(ev[i + 1]) * 1000.0 for i in range(iters))
-    return dict(p50_us=round(us[len(us) // 2], 3), min_us=round(us[0], 3), iters=iters)
+    us = sorted(ev[i].elapsed_time(ev[i + 1]) * 1000.0 / per for i in range(iters))
+    return dict(p50_us=round(us[len(us) // 2], 3), min_us=round(us[0], 3), iters=iters, per_graph=per)
 
 
 def fused_ar(a, dev) -> dict:
@@ -62,6 +74,14 @@ def attention(a, dev) -> dict:
     q = torch.randn(B, nq, D, generator=g, device=dev).bfloat16()
     out = torch.empty_like(q)
     op = K.DecodeAttention(B, nq, nkv, D, pages, dev, torch.cuda.get_device_properties(dev).multi_processor_count)
+    if a.splits:  # explicit split count (cluster merge up to 16)
+        from .._ext import native
+
+        op.pps = -(-pages // a.splits)
+        op.splits = -(-pages // op.pps)
+        op.cluster = op.splits <= 16
+        op.scratch = torch.zeros(native().attn_scratch_bytes(B, nkv, op.splits, nq // nkv, D), dtype=torch.uint8,
+                                 device=dev)
     r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5), a.iters)
     kv_bytes = 2 * B * nkv * a.ctx * D * 2
     return dict(r, batch=B, ctx=a.ctx, heads=nq, kv_heads=nkv, splits=op.splits, pages_per_split=op.pps,
@@ -104,7 +124,11 @@ def main():
     ap.add_argument("--kv-heads", type=int, default=1)
     ap.add_argument("--inter", type=int, default=3584)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--splits", type=int, default=0, help="attention: override the split plan")
+    ap.add_argument("--graph", type=int, default=0, help="time CUDA graphs of this many launches")
     a = ap.parse_args()
+    global GRAPH_OPS
+    GRAPH_OPS = a.graph
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     r = {"fused_ar": fused_ar, "attention": attention, "decode_ops": decode_ops}[a.kernel](a, dev)
