@@ -68,23 +68,20 @@ def attention_split_plan(batch: int, nkv: int, max_pages: int, num_sms: int = 14
     """Split-KV geometry (splits, pages per split, cluster merge).
 
     As many CTAs over (batch, kv head, split) as fit in ONE wave of resident CTAs (a partial second
-    wave would double the kernel time). When that needs at most 16 splits per pair, or 16 splits leave
-    each CTA at most 16 pages (else 8 splits at most 32), the splits of a pair form a cluster and merge
-    through distributed shared memory; long contexts with few pairs use more splits and the global
-    merge."""
+    wave would double the kernel time). When that needs at most 8 splits per pair, or 8 splits leave
+    each CTA at most 32 pages, the splits of a pair form a cluster and merge through distributed
+    shared memory; long contexts with few pairs use more splits and the global merge."""
     pairs = max(1, batch * nkv)
     slots = ATTN_CTAS_PER_SM * num_sms
     splits = max(1, min(max_pages, slots // pairs))
-    if splits > 8:
-        # a cluster merge (DSMEM) when it leaves each CTA a modest page chain: 16 CTAs (non-portable
-        # cluster, 8 SMs x 2) when they still fit one wave, else 8
-        if splits >= 16 and (max_pages + 15) // 16 <= 16:
-            splits = 16
-        elif (max_pages + 7) // 8 <= 32:
-            splits = 8
+    if splits > 8 and (max_pages + 7) // 8 <= 32:
+        # a cluster merge (DSMEM) of 8 splits when each CTA keeps a modest page chain. Measured at
+        # batch 8, one KV head, 2048 tokens (CUDA graphs, one B200): 8 splits 8.8 us, 16 (a
+        # non-portable cluster, which the kernel supports) 9.9 us, 32 with the global merge 26.2 us.
+        splits = 8
     pps = min(512, (max_pages + splits - 1) // splits)
     splits = (max_pages + pps - 1) // pps
-    return splits, pps, 1 < splits <= 16
+    return splits, pps, 1 < splits <= 8
 
 
 class DecodeAttention:
