@@ -12,6 +12,14 @@ schedules, with the invariants checked on every memory operation:
 * every rank finishes every call (no deadlock), with different grid sizes per call and any mix of
   variants (one CUDA graph per batch size, replayed in any order).
 
+The layer-boundary pair of csrc/fused_gemm.cu is modelled as one call of two kernels per rank
+(variant FG): the push GEMM's CTAs store column groups of every row into land1 of every rank (its
+own included) under the call's epoch without advancing it; after that kernel completes, the consumer
+GEMM's CTAs each take one piece of columns from all sources (clearing the cells), stage it, publish a
+flag tagged with the epoch, and the CTAs of a split wait for all pieces of their split (and, for the
+row norms, of every split) before reading the staged activation; the epoch advances when the
+consumer kernel completes.
+
 Each simulated memory cell stores (epoch, payload) or FILL, standing for the Lamport -0 sentinel.
 The unit of interleaving is one memory operation; blocks of one rank are modelled for the
 barrier-based variants because their barriers are per block.
@@ -24,6 +32,8 @@ from dataclasses import dataclass, field
 FILL = None
 
 L1S, L2S, P1S, P2S = 1, 2, 5, 6
+FG = 7  # gemm_push + ar_norm_gemm (layer-boundary fusion)
+FG_COLS = 12  # modelled column groups of the pushed rows
 
 
 class ProtocolViolation(AssertionError):
@@ -35,6 +45,7 @@ class Call:
     variant: int
     blocks: int
     rows: int
+    splits: int = 1  # FG: split-K count of the consumer (its CTAs = blocks x splits pieces)
 
 
 @dataclass
@@ -47,6 +58,9 @@ class Memory:
     agp: dict = field(default_factory=dict)     # (owner, slot, src, row) -> epoch tag (never cleared)
     stage: dict = field(default_factory=dict)   # (owner, parity, row) -> epoch
     flags: dict = field(default_factory=dict)   # (owner, block, src) -> count
+    fg_land: dict = field(default_factory=dict)  # (owner, slot, src, row, col) -> (epoch, value) | FILL
+    act: dict = field(default_factory=dict)      # (owner, col) -> epoch of the staged activation
+    pflags: dict = field(default_factory=dict)   # (owner, piece) -> epoch tag
 
 
 def value(rank: int, epoch: int, row: int) -> int:
@@ -86,7 +100,7 @@ class Rank:
         for call in self.calls:
             e = self.epoch + 1  # every block reads the same epoch; the last block advances it
             got: dict = {}
-            blocks = [self._block(call, e, b, got) for b in range(call.blocks)]
+            blocks = [] if call.variant == FG else [self._block(call, e, b, got) for b in range(call.blocks)]
             live = list(blocks)
             while live:
                 g = self.rng.choice(live)
@@ -94,11 +108,15 @@ class Rank:
                     yield next(g)
                 except StopIteration:
                     live.remove(g)
-            expect = call.rows * self.mem.world
+            if call.variant == FG:
+                yield from self._fused_boundary(call, e, got)
+            expect = call.rows * self.mem.world * (FG_COLS if call.variant == FG else 1)
             if len(got) != expect:
                 raise ProtocolViolation(f"rank {self.rank} call {e}: {len(got)} of {expect} row pieces")
-            for (src, row), v in got.items():
-                if v != value(src, e, row):
+            for key, v in got.items():
+                src, row = key[0], key[1]
+                if v != value(src, e, row * FG_COLS + (key[2] if len(key) > 2 else 0) if call.variant == FG
+                              else row):
                     raise ProtocolViolation(f"rank {self.rank} call {e}: wrong payload from {src} row {row}")
             self.results.append(dict(epoch=e, n=len(got)))
             self.epoch = e
@@ -166,6 +184,58 @@ class Rank:
         else:
             raise ValueError(call.variant)
 
+    def _interleave(self, gens):
+        live = list(gens)
+        while live:
+            g = self.rng.choice(live)
+            try:
+                yield next(g)
+            except StopIteration:
+                live.remove(g)
+
+    def _fused_boundary(self, call: Call, e: int, got: dict):
+        """gemm_push (call.blocks CTAs) then, after it completes, ar_norm_gemm (blocks x splits CTAs)."""
+        W, slot, C = self.mem.world, e % self.mem.nslots, FG_COLS
+
+        def push(b):
+            for row in range(call.rows):
+                for col in range(b, C, call.blocks):
+                    for i in range(W):  # own heap first, then the peers
+                        self._put(self.mem.fg_land, ((self.rank + i) % W, slot, self.rank, row, col),
+                                  (e, value(self.rank, e, row * C + col)))
+                        yield True
+
+        yield from self._interleave(push(b) for b in range(call.blocks))
+        tiles, S = call.blocks, call.splits
+        span = [(r * C // S, (r + 1) * C // S) for r in range(S)]
+
+        def consumer(t, r):
+            c0, c1 = span[r]
+            lo, hi = c0 + (c1 - c0) * t // tiles, c0 + (c1 - c0) * (t + 1) // tiles
+            for row in range(call.rows):  # this CTA's piece: columns [lo, hi) of every row
+                for col in range(lo, hi):
+                    for src in range(W):
+                        while (v := self._take(self.mem.fg_land, (self.rank, slot, src, row, col), e)) is None:
+                            yield False
+                        got[(src, row, col)] = v[1]
+                        yield True
+            for col in range(lo, hi):
+                self.mem.act[(self.rank, col)] = e
+                yield True
+            self.mem.pflags[(self.rank, r * tiles + t)] = e
+            yield True
+            # TMA producer of split r: all pieces of the split, then the staged activation
+            for tt in range(tiles):
+                while self.mem.pflags.get((self.rank, r * tiles + tt)) != e:
+                    yield False
+            for col in range(c0, c1):
+                if self.mem.act.get((self.rank, col)) != e:
+                    raise ProtocolViolation(f"rank {self.rank} call {e} split {r} reads activation col {col} "
+                                            f"of call {self.mem.act.get((self.rank, col))}")
+                yield True
+
+        yield from self._interleave(consumer(t, r) for t in range(tiles) for r in range(S))
+
     def _stage_and_barrier(self, e: int, b: int, rows):
         """Copy this block's rows into stage[parity], then block b's flag barrier."""
         W = self.mem.world
@@ -215,12 +285,13 @@ def simulate(world: int, calls: list[Call], seed: int = 0, max_steps: int = 2_00
             raise ProtocolViolation(f"deadlock: epochs {[x.epoch for x in ranks]}")
         if steps > max_steps:
             raise ProtocolViolation("step budget exhausted")
-    leftovers = [k for t in (mem.land1, mem.rs, mem.ag) for k, v in t.items() if v is not FILL]
+    leftovers = [k for t in (mem.land1, mem.rs, mem.ag, mem.fg_land) for k, v in t.items() if v is not FILL]
     if leftovers:
         raise ProtocolViolation(f"landing cells not restored to the sentinel: {leftovers[:4]}")
     return dict(steps=steps, epochs=[r.epoch for r in ranks])
 
 
-def random_calls(n: int, seed: int, variants=(L1S, L2S, P1S, P2S), rows=(1, 3, 8), blocks=(1, 2, 4)) -> list[Call]:
+def random_calls(n: int, seed: int, variants=(L1S, L2S, P1S, P2S), rows=(1, 3, 8), blocks=(1, 2, 4),
+                 splits=(1, 2, 3)) -> list[Call]:
     rng = random.Random(seed)
-    return [Call(rng.choice(variants), rng.choice(blocks), rng.choice(rows)) for _ in range(n)]
+    return [Call(rng.choice(variants), rng.choice(blocks), rng.choice(rows), rng.choice(splits)) for _ in range(n)]

@@ -33,3 +33,26 @@ def test_checker_detects_single_slot_protocol():
         except ProtocolViolation:
             caught += 1
     assert caught == 6
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_boundary_mixed_with_fused_ar(world):
+    """gemm_push + ar_norm_gemm calls share the epoch and land1 with the standalone one-shot calls."""
+    from comm_opt_b200.parallel.protocol_sim import FG
+
+    for seed in range(3):
+        calls = random_calls(16, seed + 100 * world, variants=(L1S, FG, L2S, FG))
+        res = simulate(world, calls, seed=seed, slow_rank=seed % world)
+        assert res["epochs"] == [16] * world
+
+
+def test_checker_detects_single_slot_fused_boundary():
+    from comm_opt_b200.parallel.protocol_sim import FG
+
+    caught = 0
+    for seed in range(6):
+        try:
+            simulate(4, [Call(FG, 2, 2, 2)] * 12, seed=seed, slow_rank=seed % 4, slow_factor=40, nslots=1)
+        except ProtocolViolation:
+            caught += 1
+    assert caught >= 5
