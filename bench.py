@@ -107,9 +107,11 @@ class ClockSampler:
 
 def reference_arm(args):
     line = {"impl": "reference",
-            "unavailable": "the reference (allennnnnz/comm_opt) is not an installable project: pip install of "
-                           "the reference source tree fails with 'Neither setup.py nor pyproject.toml found', and it has no "
-                           "decode runner of its own (its decode numbers come from vLLM driver scripts)"}
+            "unavailable": "the reference (allennnnnz/comm_opt) is not an installable project (pip install of its "
+                           "source tree fails: 'Neither setup.py nor pyproject.toml found') and has no decode runner "
+                           "of its own: its only decode path, exp/M5_e2e_comm_share/infer.py, drives the vLLM engine "
+                           "on a Hugging Face checkpoint and tokenizer from the hub cache, which this offline box "
+                           "does not have; its fused kernel is compared in harness/fused_sweep.py (ref_m16nf)"}
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(line), flush=True)
 
