@@ -182,7 +182,11 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
                                    c10::optional<torch::Tensor> flags, c10::optional<torch::Tensor> pss,
                                    torch::Tensor err, int64_t rank, int64_t M, int64_t N, int64_t K, double eps,
                                    int64_t emulate, int64_t splits, int64_t pdl, int64_t timeout_ns,
-                                   int64_t res_rs, bool dry_run) {
+                                   int64_t res_rs, bool dry_run, int64_t epi,
+                                   c10::optional<torch::Tensor> positions, c10::optional<torch::Tensor> cos_t,
+                                   c10::optional<torch::Tensor> sin_t, c10::optional<torch::Tensor> block_tables,
+                                   c10::optional<torch::Tensor> k_cache, c10::optional<torch::Tensor> v_cache,
+                                   int64_t nq, int64_t nkv) {
   cob::FusedGemmParams p = {};
   COB_CHECK(bases.size() >= 1 && bases.size() <= cob::kMaxWorld, "world must be 1..8");
   for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
@@ -206,9 +210,34 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
   const c10::cuda::CUDAGuard g(w.device());
   int sms = 0;
   check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, w.device().index()), "sm count");
+  COB_CHECK(epi >= 0 && epi <= 2 && (kind == 1 || epi == 0), "epilogue 0 plain, 1 swiglu, 2 rope_kv (consumer only)");
+  p.epi = (int)epi;
   const cob::FusedGemmPlan pl =
-      cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, std::max(1, sms / ranks), kind == 1);
+      cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, std::max(1, sms / ranks), kind == 1, (int)epi);
   if (dry_run) return {pl.bn, pl.tiles, pl.splits, pl.kps, pl.xctas};
+  COB_CHECK(pl.splits > 0, "no launch geometry supports this epilogue for [", M, ", ", N, ", ", K, "]");
+  if (epi == cob::kEpiRopeKv) {
+    COB_CHECK(positions.has_value() && cos_t.has_value() && sin_t.has_value() && block_tables.has_value() &&
+                  k_cache.has_value() && v_cache.has_value(),
+              "rope_kv epilogue needs positions, cos, sin, block_tables, k_cache, v_cache");
+    COB_CHECK(positions->scalar_type() == torch::kInt32 && block_tables->scalar_type() == torch::kInt32 &&
+                  cos_t->scalar_type() == torch::kFloat && sin_t->scalar_type() == torch::kFloat &&
+                  cos_t->size(-1) == 64 && k_cache->scalar_type() == torch::kBFloat16 &&
+                  v_cache->scalar_type() == torch::kBFloat16 && k_cache->size(-1) == 128,
+              "rope_kv operand types / shapes (head_dim 128, bf16 caches [blocks, nkv, bs, 128])");
+    for (auto* t : {&*positions, &*cos_t, &*sin_t, &*block_tables, &*k_cache, &*v_cache}) check_dense(*t, "rope_kv operand");
+    p.positions = positions->data_ptr<int32_t>();
+    p.cos_t = cos_t->data_ptr<float>();
+    p.sin_t = sin_t->data_ptr<float>();
+    p.block_tables = block_tables->data_ptr<int32_t>();
+    p.max_blocks = (int)block_tables->size(-1);
+    p.k_cache = k_cache->data_ptr();
+    p.v_cache = v_cache->data_ptr();
+    p.nq = (int)nq;
+    p.nkv = (int)nkv;
+    p.bs = (int)k_cache->size(-2);
+    p.cache_rs = emulate ? k_cache->numel() / ranks : 0;
+  }
   CUtensorMap tw, tb;
   check_cuda(cob::tensor_map_2d(w.data_ptr(), (uint64_t)ranks * N, (uint64_t)K, (uint64_t)K * 2, 128, 64, true, &tw),
              "weight tensor map");
@@ -229,7 +258,9 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
     COB_CHECK(residual->scalar_type() == torch::kBFloat16 && gamma->scalar_type() == torch::kBFloat16 &&
                   y->scalar_type() == torch::kBFloat16 && act->scalar_type() == torch::kBFloat16,
               "residual, gamma, y, act must be bf16");
-    COB_CHECK(residual->numel() >= (int64_t)ranks * M * K && gamma->numel() == K && y->numel() >= (int64_t)ranks * M * N,
+    const int64_t ycols = epi == cob::kEpiSwiglu ? N / 2 : (epi == cob::kEpiRopeKv ? nq * 128 : N);
+    COB_CHECK(residual->numel() >= (int64_t)ranks * M * K && gamma->numel() == K &&
+                  y->numel() >= (int64_t)ranks * M * ycols,
               "residual / gamma / y sizes");
     COB_CHECK(act->dim() == 2 && act->size(1) == K && act->size(0) % ranks == 0, "act must be [ranks * rows, K]");
     COB_CHECK(flags->scalar_type() == torch::kInt32 && flags->numel() >= (int64_t)ranks * cob::kMaxPieces,
@@ -281,7 +312,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("pss") = pybind11::none(), pybind11::arg("err"), pybind11::arg("rank"), pybind11::arg("M"),
         pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("eps"), pybind11::arg("emulate"),
         pybind11::arg("splits"), pybind11::arg("pdl"), pybind11::arg("timeout_ns"), pybind11::arg("res_rs"),
-        pybind11::arg("dry_run"));
+        pybind11::arg("dry_run"), pybind11::arg("epi") = 0, pybind11::arg("positions") = pybind11::none(),
+        pybind11::arg("cos") = pybind11::none(), pybind11::arg("sin") = pybind11::none(),
+        pybind11::arg("block_tables") = pybind11::none(), pybind11::arg("k_cache") = pybind11::none(),
+        pybind11::arg("v_cache") = pybind11::none(), pybind11::arg("nq") = 0, pybind11::arg("nkv") = 0);
   m.attr("kMaxPieces") = cob::kMaxPieces;
   register_ops(m);
   register_ipc(m);

@@ -26,7 +26,10 @@
 //            stored, the landing vectors restored to -0, then a per-piece flag = epoch (release).
 //            Then the epilogue: rstd per row from all pieces' sums (per split with a warp tree, then
 //            across the cluster through DSMEM, fixed order: deterministic), partial tiles summed
-//            over the cluster, scaled by rstd, stored as bf16.
+//            over the cluster, scaled by rstd, stored as bf16 - or, with a paired epilogue, each CTA
+//            finishes row pairs (f, 64 + f) of its tile: SiLU(gate) * up (the gate_up projection,
+//            weights interleaved per tile) or RoPE + paged-KV append (the QKV projection, one head
+//            per tile), which removes the separate SiLU and RoPE kernels from the decode step.
 //   RMSNorm folds into the GEMM: Z = (h * gamma * rstd) W^T = rstd * ((h * gamma) W^T) per row.
 //
 // CTAs of ar_norm_gemm wait for pieces written by other CTAs of the same launch, so the host only
@@ -554,8 +557,61 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
     }
     __syncthreads();
   }
+  if (cs > 1 && !*c.fail && p.epi != kEpiPlain) {
+    // paired epilogue: this CTA finishes half-rows [r * ph, (r + 1) * ph) of both tile halves
+    float* part = reinterpret_cast<float*>(smem);
+    const int ph = (BM / 2) / cs, hgroups = ph / 8;
+    for (int idx = threadIdx.x; idx < p.M * hgroups; idx += kThreads) {
+      const int b = idx / hgroups, f = r * ph + (idx % hgroups) * 8;
+      float lo[8], hi[8];
+      cluster_sum8(part, cs, b, f, lo);
+      cluster_sum8(part, cs, b, BM / 2 + f, hi);
+      const float rs = c.rstd[b];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // the values a plain epilogue would have stored (bf16)
+        lo[j] = __bfloat162float(__float2bfloat16_rn(lo[j] * rs));
+        hi[j] = __bfloat162float(__float2bfloat16_rn(hi[j] * rs));
+      }
+      if (p.epi == kEpiSwiglu) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = lo[j] / (1.f + __expf(-lo[j])) * hi[j];
+        __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(p.Y) + (p.emulate ? (size_t)rank * p.M * (p.N / 2) : 0);
+        *reinterpret_cast<uint4*>(Y + (size_t)b * (p.N / 2) + t * (BM / 2) + f) = pack_bf16x8(o);
+      } else {  // kEpiRopeKv: tile t is head t
+        const int head = t, pos = p.positions[b];
+        if (head < p.nq + p.nkv) {
+          float o1[8], o2[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float cs_ = p.cos_t[(size_t)pos * (BM / 2) + f + j], sn = p.sin_t[(size_t)pos * (BM / 2) + f + j];
+            o1[j] = lo[j] * cs_ - hi[j] * sn;
+            o2[j] = hi[j] * cs_ + lo[j] * sn;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            lo[j] = o1[j];
+            hi[j] = o2[j];
+          }
+        }
+        __nv_bfloat16* dst;
+        if (head < p.nq) {
+          dst = reinterpret_cast<__nv_bfloat16*>(p.Y) + (p.emulate ? (size_t)rank * p.M * p.nq * BM : 0) +
+                ((size_t)b * p.nq + head) * BM;
+        } else {
+          const int blk = p.block_tables[(size_t)b * p.max_blocks + pos / p.bs], off = pos % p.bs;
+          const int kv = head < p.nq + p.nkv ? head - p.nq : head - p.nq - p.nkv;
+          __nv_bfloat16* cache = reinterpret_cast<__nv_bfloat16*>(head < p.nq + p.nkv ? p.k_cache : p.v_cache) +
+                                 (p.emulate ? (size_t)rank * p.cache_rs : 0);
+          dst = cache + (((size_t)blk * p.nkv + kv) * p.bs + off) * BM;
+        }
+        *reinterpret_cast<uint4*>(dst + f) = pack_bf16x8(lo);
+        *reinterpret_cast<uint4*>(dst + BM / 2 + f) = pack_bf16x8(hi);
+      }
+    }
+  }
   const int per = BM / cs, f0 = r * per, groups = per / 8;
-  if (cs > 1 && !*c.fail) {
+  if (cs > 1 && !*c.fail && p.epi == kEpiPlain) {
     float* part = reinterpret_cast<float*>(smem);
     __nv_bfloat16* Y = reinterpret_cast<__nv_bfloat16*>(p.Y) + (p.emulate ? (size_t)rank * p.M * p.N : 0);
     for (int idx = threadIdx.x; idx < p.M * groups; idx += kThreads) {
@@ -647,13 +703,19 @@ cudaError_t check_common(const FusedGemmParams& p, const FusedGemmPlan& pl, int 
     return cudaErrorInvalidValue;
   // several tiles per CTA only without split-K (the cluster epilogue holds one tile)
   if (pl.xctas < 1 || pl.xctas > pl.tiles || (pl.splits > 1 && pl.xctas != pl.tiles)) return cudaErrorInvalidValue;
+  if (p.epi != kEpiPlain) {
+    if (pl.splits < 2 || pl.splits > 8 || p.N % BM) return cudaErrorInvalidValue;
+    if (p.epi == kEpiRopeKv && (p.N != (p.nq + 2 * p.nkv) * BM || p.bs <= 0 || !p.positions || !p.cos_t ||
+                                !p.sin_t || !p.block_tables || !p.k_cache || !p.v_cache))
+      return cudaErrorInvalidValue;
+  }
   if ((long long)pl.kps * (pl.splits - 1) >= p.K / BK) return cudaErrorInvalidValue;  // every split non-empty
   return cudaSuccess;
 }
 
 }  // namespace
 
-FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer) {
+FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer, int epi) {
   FusedGemmPlan pl = {};
   pl.bn = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
   pl.tiles = (N + BM - 1) / BM;
@@ -665,7 +727,7 @@ FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool
     // enough CTAs to keep every SM streaming weights, within one resident wave
     splits = 1;
     // (up to 16: a non-portable cluster size, co-scheduled as 8 SMs x 2 CTAs)
-    const int smax = per_sm == 2 ? 16 : 8;
+    const int smax = epi != kEpiPlain ? 8 : (per_sm == 2 ? 16 : 8);
     const int lim = consumer ? cap : num_sms * per_sm;
     while (splits < smax && pl.tiles * splits * 2 <= lim && KT / (splits * 2) >= 2) splits *= 2;
   }
@@ -674,7 +736,16 @@ FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool
   while (BM % (8 * pl.splits)) --pl.splits;
   pl.kps = (KT + pl.splits - 1) / pl.splits;
   pl.xctas = pl.tiles;
-  if (consumer && pl.tiles * pl.splits > cap) {
+  if (epi != kEpiPlain) {
+    // paired epilogues finish whole tiles inside a cluster of 2..8 splits, one tile per CTA
+    if (pl.splits < 2 && KT >= 2 && pl.tiles * 2 <= cap) {
+      pl.splits = 2;
+      pl.kps = (KT + 1) / 2;
+      pl.splits = (KT + pl.kps - 1) / pl.kps;
+    }
+    if (pl.splits < 2 || pl.splits > 8 || pl.tiles * pl.splits > cap) pl.splits = 0;  // unsupported
+  }
+  if (consumer && pl.splits > 0 && pl.tiles * pl.splits > cap) {
     // too many tiles for one resident wave: no split-K, each CTA loops over several tiles
     pl.splits = 1;
     pl.kps = KT;
@@ -689,7 +760,7 @@ cudaError_t launch_gemm_push(const FusedGemmParams& p, const CUtensorMap& tmW, c
                              const FusedGemmPlan& pl, int ranks, bool pdl, cudaStream_t stream) {
   cudaError_t e = check_common(p, pl, ranks);
   if (e != cudaSuccess) return e;
-  if (pl.xctas != pl.tiles) return cudaErrorInvalidValue;
+  if (pl.xctas != pl.tiles || p.epi != kEpiPlain) return cudaErrorInvalidValue;
   if (p.M > p.L.max_rows || p.N / 8 > p.L.max_hv || p.L.world != p.world) return cudaErrorInvalidValue;
   return launch_sel<true>(p, tmW, tmX, pl, ranks, pdl, stream);
 }

@@ -40,7 +40,25 @@ struct FusedGemmParams {
   float* pss;                // [ranks][kMaxPieces][M_max] per-piece partial sums of squares
   void* Y;                   // [M, N] output (ldy = N); emulate: rank r at Y + r * M * N
   long long x_rs, res_rs;    // emulate element strides between ranks' X / residual
+  // ar_norm_gemm epilogue applied to each 128-row output tile as two halves (rows f and 64 + f):
+  //   kEpiPlain  : Y[M, N]
+  //   kEpiSwiglu : Y[M, N / 2] = silu(gate) * up, weights tile-interleaved (tile t = 64 gate rows
+  //                t*64.. then the 64 matching up rows)
+  //   kEpiRopeKv : tile t = head t of [q heads | k heads | v heads] (head_dim 128): q heads rotated
+  //                (RoPE at positions[b]) into Y = q_out [M, nq, 128]; k heads rotated and v heads copied
+  //                into the paged caches [blocks, nkv, bs, 128] at slot positions[b]
+  int epi;
+  const int* positions;      // [M]
+  const float* cos_t;        // [max_pos, 64]
+  const float* sin_t;
+  const int* block_tables;   // [M, max_blocks]
+  int max_blocks, nq, nkv, bs;
+  void* k_cache;
+  void* v_cache;
+  long long cache_rs;        // emulate element stride between ranks' caches
 };
+
+enum FusedEpi : int { kEpiPlain = 0, kEpiSwiglu = 1, kEpiRopeKv = 2 };
 
 struct FusedGemmPlan {
   int bn, tiles, splits, kps, smem, ctas;
@@ -48,8 +66,10 @@ struct FusedGemmPlan {
 };
 
 // Geometry for M rows, N outputs, K inner: BN (MMA N) and the split count (0 = choose). `consumer`:
-// plan for ar_norm_gemm (whole grid resident, at most kMaxBlocks CTAs).
-FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer);
+// plan for ar_norm_gemm (whole grid resident, at most kMaxBlocks CTAs). The paired epilogues
+// (swiglu, rope) need 2..8 splits per tile (each CTA of a cluster finishes whole row pairs); a plan
+// that cannot meet that returns splits == 0.
+FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer, int epi = kEpiPlain);
 
 // tmW: [ranks * N, K] weights, box 64 x 128; tmX: [rows, K] activations, box 64 x BN.
 cudaError_t launch_gemm_push(const FusedGemmParams& p, const CUtensorMap& tmW, const CUtensorMap& tmX,

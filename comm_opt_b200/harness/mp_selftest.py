@@ -17,7 +17,8 @@ Parts:
   decode     - tiny Llama-shaped model at TP = world vs the unsharded fp32 forward (logits), and
                identical greedy tokens on every rank.
   decode_fused - the same with the layer boundaries fused (GEMM push epilogue -> all-reduce + RMSNorm
-               inside the next GEMM).
+               inside the next GEMM); decode_fused_epi also moves SiLU * up and RoPE + KV append
+               into the consumer GEMMs' epilogues.
 Rank 0 prints one JSON summary; the exit code is non-zero on any failure.
 """
 from __future__ import annotations
@@ -195,7 +196,7 @@ def fault(C: Checker, dev, world):
     comm.close()
 
 
-def decode_check(C: Checker, dev, world, fused: bool = False):
+def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False):
     import math
 
     import torch.nn.functional as F
@@ -208,7 +209,7 @@ def decode_check(C: Checker, dev, world, fused: bool = False):
     w = LlamaWeights(cfg, dist.get_rank(), world, dev, full=full)
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, w, comm, max_batch=4, max_seq=96, device=dev, nccl_group=dist.group.WORLD,
-                            fuse_boundary=fused)
+                            fuse_boundary=fused, fuse_epilogues=epilogues)
     C.check(runner.fuse_boundary == fused, "layer-boundary fusion engaged as requested")
     prompts = torch.randint(0, cfg.vocab, (3, 29), generator=torch.Generator().manual_seed(1))
     first = runner.prefill(prompts)
@@ -273,7 +274,9 @@ def main():
     try:
         for part in a.parts.split(","):
             {"functional": functional, "fault": fault, "decode": decode_check,
-             "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True)}[part](C, dev, world)
+             "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True),
+             "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True)
+             }[part](C, dev, world)
     except Exception:
         err = traceback.format_exc()
         C.fails.append(err[-2000:])

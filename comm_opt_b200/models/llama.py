@@ -176,7 +176,8 @@ class TPDecodeRunner:
     """Greedy TP decoding: torch prefill, then graph-captured decode steps built from our kernels."""
 
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
-                 device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False):
+                 device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
+                 fuse_epilogues: bool = False):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -202,6 +203,10 @@ class TPDecodeRunner:
         # GEMM (gate_up, the next layer's qkv, the LM head); needs TP > 1, bf16 and this package's GEMMs
         self.fuse_boundary = bool(fuse_boundary and self.tp > 1 and self.dtype == torch.bfloat16 and gemm == "cob")
         self.fuse_error = ""
+        # with fuse_boundary: SiLU * up and RoPE + KV append inside the consumer GEMMs' epilogues
+        self.fuse_epilogues = bool(fuse_epilogues)
+        self._fuse_epi: dict[int, tuple[bool, bool]] = {}
+        self._wgu_il: list | None = None
         if self.fuse_boundary:
             comm.prepare_fused_gemm(cfg.hidden)
 
@@ -318,25 +323,57 @@ class TPDecodeRunner:
                          positions=buf["pos"], seq_lens=buf["lens"], local_keys=buf["keys"])
         return n + 1
 
+    def _fused_epilogues(self, B: int, buf: dict) -> tuple[bool, bool]:
+        """(swiglu in the gate_up GEMM, RoPE + KV append in the QKV GEMM) for batch B: used when the
+        consumer GEMM has a launch geometry for them (2..8 K-splits per output tile)."""
+        if not self.fuse_epilogues:
+            return False, False
+        if B not in self._fuse_epi:
+            cfg, s, L, comm = self.cfg, self.s, self.w.layers[0], self.comm
+            comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, dry_run=True, epilogue="swiglu")
+            sw = comm.last_fused_gemm[1][2] > 0 and s["inter"] % 64 == 0
+            comm.ar_norm_gemm(buf["res"], L.ln1, L.wqkv, dry_run=True, epilogue="rope_kv")
+            rp = comm.last_fused_gemm[1][2] > 0 and cfg.head_dim == 128
+            if sw and self._wgu_il is None:  # tile-interleaved gate/up copies (allocated outside capture)
+                self._wgu_il = [comm.interleave_gate_up(Lw.wgu) for Lw in self.w.layers]
+            self._fuse_epi[B] = (sw, rp)
+        return self._fuse_epi[B]
+
     def _step_fused(self, B: int, buf: dict, bt: torch.Tensor) -> int:
-        """Decode step with the layer boundaries fused (after the embedding and first norm)."""
+        """Decode step with the layer boundaries fused (after the embedding and first norm). Where the
+        consumer GEMM supports it, SiLU * up runs in the gate_up epilogue and RoPE + the paged-KV append
+        in the QKV epilogue (5 kernels per layer instead of 7)."""
         cfg, s, w, comm = self.cfg, self.s, self.w, self.comm
+        sw, rp = self._fused_epilogues(B, buf)
         n = 0
         self.lin[(0, "qkv")](buf["h"], out=buf["qkv"])
         n += 1
         for i, L in enumerate(w.layers):
-            K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
-                             self.cache.v[i], s["nq"], s["nkv"])
+            if i == 0 or not rp:
+                K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
+                                 self.cache.v[i], s["nq"], s["nkv"])
+                n += 1
             buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
             comm.gemm_push(buf["attn"].view(B, -1), L.wo)
-            comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, cfg.eps, out=buf["gu"])
-            K.silu_mul(buf["gu"], out=buf["act"])
+            if sw:
+                comm.ar_norm_gemm(buf["res"], L.ln2, self._wgu_il[i], cfg.eps, out=buf["act"], epilogue="swiglu")
+            else:
+                comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, cfg.eps, out=buf["gu"])
+                K.silu_mul(buf["gu"], out=buf["act"])
+                n += 1
             comm.gemm_push(buf["act"], L.wdown)
             if i + 1 < len(w.layers):
-                comm.ar_norm_gemm(buf["res"], w.layers[i + 1].ln1, w.layers[i + 1].wqkv, cfg.eps, out=buf["qkv"])
+                nxt = w.layers[i + 1]
+                if rp:
+                    comm.ar_norm_gemm(buf["res"], nxt.ln1, nxt.wqkv, cfg.eps, out=buf["q"], epilogue="rope_kv",
+                                      rope=dict(positions=buf["pos"], cos=self.cos, sin=self.sin, block_tables=bt,
+                                                k_cache=self.cache.k[i + 1], v_cache=self.cache.v[i + 1],
+                                                nq=s["nq"], nkv=s["nkv"]))
+                else:
+                    comm.ar_norm_gemm(buf["res"], nxt.ln1, nxt.wqkv, cfg.eps, out=buf["qkv"])
             else:
                 comm.ar_norm_gemm(buf["res"], w.final_norm, w.lm_head, cfg.eps, out=buf["logits"])
-            n += 7
+            n += 5
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         comm.all_gather_u32(buf["keys"].view(torch.int32), out=buf["gathered"].view(torch.int32).view(self.tp, 2 * B))
         K.argmax_combine(buf["gathered"], self.tp, ids=buf["ids"], positions=buf["pos"], seq_lens=buf["lens"],

@@ -297,29 +297,62 @@ class TPCommunicator:
             self._fg_err_t = torch.zeros(1, dtype=torch.int32, device=self.device)
         return self._fg_err_t
 
+    EPILOGUES = {"plain": 0, "swiglu": 1, "rope_kv": 2}
+
+    @staticmethod
+    def interleave_gate_up(w: torch.Tensor) -> torch.Tensor:
+        """[..., 2I, K] = [gate rows; up rows] -> the swiglu epilogue's layout: output tile t (128 rows)
+        holds gate rows 64t..64t+63 then the matching up rows (I % 64 == 0)."""
+        I2, K = w.shape[-2], w.shape[-1]
+        I = I2 // 2
+        assert I % 64 == 0, "intermediate size must be a multiple of 64"
+        lead = w.shape[:-2]
+        g = w[..., :I, :].reshape(*lead, I // 64, 64, K)
+        u = w[..., I:, :].reshape(*lead, I // 64, 64, K)
+        return torch.stack([g, u], dim=-3).reshape(*lead, I2, K).contiguous()
+
     def ar_norm_gemm(self, residual: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
-                     out: torch.Tensor | None = None, splits: int = 0, dry_run: bool = False) -> torch.Tensor:
+                     out: torch.Tensor | None = None, splits: int = 0, dry_run: bool = False,
+                     epilogue: str = "plain", rope: dict | None = None) -> torch.Tensor:
         """Second half of the all-reduce fused with RMSNorm and the next column-parallel GEMM:
-        h = residual + sum_ranks(pushed partials) (residual updated in place),
-        out = (RMSNorm(h) * gamma) @ w^T, out [M, N]. Emulation: residual [W, M, K], w [W, N, K]."""
+        h = residual + sum_ranks(pushed partials) (residual updated in place), z = (RMSNorm(h) * gamma) @ w^T.
+        epilogue "plain": out = z [M, N]. "swiglu": w tile-interleaved (`interleave_gate_up`), out = silu(gate)
+        * up [M, N / 2]. "rope_kv": z holds [q heads | k heads | v heads] of 128; out = RoPE(q) [M, nq, 128],
+        RoPE(k) and v written into the paged caches at rope["positions"] (keys: positions, cos, sin,
+        block_tables, k_cache, v_cache, nq, nkv). Emulation: residual [W, M, K], w [W, N, K]."""
         if self.world == 1 or self.dtype != torch.bfloat16:
             raise TPCommError("fused GEMMs need world > 1 and a bf16 communicator")
         M, K = self._fg_dims(residual)
         N = w.shape[-2]
+        epi = self.EPILOGUES[epilogue]
         if M > self.max_rows or K > self.max_hidden:
             raise TPCommError(f"ar_norm_gemm [{M}, {K}] exceeds the communicator capacity")
-        if out is None:
-            shape = (self.world, M, N) if self.emulated else (M, N)
+        if out is None and not dry_run:
+            cols = N // 2 if epi == 1 else (rope["nq"] * 128 if epi == 2 else N)
+            shape = (self.world, M, cols) if self.emulated else (M, cols)
             out = torch.empty(shape, dtype=torch.bfloat16, device=residual.device)
         ws = self._fg_workspace(K)
+        r = rope or {}
         with torch.cuda.device(self.device):
             plan = native().fused_gemm(1, self.heap.bases, self._layout_list, w, residual=residual, gamma=gamma,
-                                       y=out, act=ws["act"], flags=ws["flags"], pss=ws["pss"], err=self._fg_err(),
-                                       rank=self.rank, M=M, N=N, K=K, eps=float(eps), emulate=int(self.emulated),
-                                       splits=splits, pdl=int(self.pdl), timeout_ns=self.timeout_ns,
-                                       res_rs=M * K if self.emulated else 0, dry_run=dry_run)
+                                       y=out if out is not None else residual, act=ws["act"], flags=ws["flags"],
+                                       pss=ws["pss"], err=self._fg_err(), rank=self.rank, M=M, N=N, K=K,
+                                       eps=float(eps), emulate=int(self.emulated), splits=splits,
+                                       pdl=int(self.pdl), timeout_ns=self.timeout_ns,
+                                       res_rs=M * K if self.emulated else 0, dry_run=dry_run, epi=epi,
+                                       positions=r.get("positions"), cos=r.get("cos"), sin=r.get("sin"),
+                                       block_tables=r.get("block_tables"), k_cache=r.get("k_cache"),
+                                       v_cache=r.get("v_cache"), nq=r.get("nq", 0), nkv=r.get("nkv", 0))
         self.last_fused_gemm = ("ar_norm_gemm", tuple(plan))
         return out
+
+    def fused_epilogue_supported(self, M: int, N: int, K: int, epilogue: str) -> bool:
+        """Whether ar_norm_gemm can run this epilogue for [M, K] x [N, K]^T (a plan with 2..8 splits)."""
+        ranks = self.world if self.emulated else 1
+        dummy_w = torch.empty(ranks * N, K, dtype=torch.bfloat16, device=self.device)
+        dummy_r = torch.empty((ranks, M, K) if self.emulated else (M, K), dtype=torch.bfloat16, device=self.device)
+        self.ar_norm_gemm(dummy_r, dummy_r.new_empty(K), dummy_w, dry_run=True, epilogue=epilogue)
+        return self.last_fused_gemm[1][2] > 0
 
     def close(self):
         """Collective teardown: every rank unmaps its peers' heaps before any heap is freed."""

@@ -150,3 +150,73 @@ def test_layer_boundary_split16(cuda):
     for r in range(world):
         assert rel_err(res[r], h_ref) <= TOL
         assert rel_err(out[r], out_ref[r]) <= TOL
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_layer_boundary_swiglu_epilogue(cuda, world):
+    """down_proj push -> AR + residual + RMSNorm -> gate_up with SiLU(gate) * up in the epilogue."""
+    M, K1, H, I, eps = 8, 512, 1024, 448, 1e-5  # I = 7 tiles of 64
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=8, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(world + 40)
+    w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    wgu = (0.05 * torch.randn(world, 2 * I, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res0 = torch.randn(M, H, generator=g, device=cuda).bfloat16()
+    res = res0.unsqueeze(0).repeat(world, 1, 1).contiguous()
+    x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+    comm.gemm_push(x, w1)
+    act = comm.ar_norm_gemm(res, gamma, TPCommunicator.interleave_gate_up(wgu), eps, epilogue="swiglu")
+    torch.cuda.synchronize()
+    comm.check()
+    assert act.shape == (world, M, I) and 2 <= comm.last_fused_gemm[1][2] <= 8
+    h_ref, gu_ref = reference(x, w1, res0, gamma, wgu, eps)
+    for r in range(world):
+        gg, uu = gu_ref[r].bfloat16().float().chunk(2, -1)
+        ref = torch.nn.functional.silu(gg) * uu
+        assert rel_err(res[r], h_ref) <= TOL
+        assert rel_err(act[r], ref) <= TOL, (r, rel_err(act[r], ref))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_layer_boundary_rope_kv_epilogue(cuda, world):
+    """AR + RMSNorm -> QKV with RoPE on q/k and the paged KV append in the epilogue."""
+    from comm_opt_b200.ops.reference import rope_tables
+
+    M, K1, H, nq, nkv, D, bs, eps = 6, 256, 1024, 4, 2, 128, 16, 1e-5
+    N = (nq + 2 * nkv) * D
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=8, max_hidden=H)
+    g = torch.Generator(device=cuda).manual_seed(world + 50)
+    w1 = (0.05 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    wqkv = (0.05 * torch.randn(world, N, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res0 = torch.randn(M, H, generator=g, device=cuda).bfloat16()
+    res = res0.unsqueeze(0).repeat(world, 1, 1).contiguous()
+    x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+    maxb, nblocks = 4, 40
+    pos = torch.tensor([0, 5, 16, 17, 40, 63], dtype=torch.int32, device=cuda)
+    bt = torch.randperm(nblocks, generator=torch.Generator().manual_seed(2))[:M * maxb].view(M, maxb)
+    bt = bt.to(torch.int32).to(cuda)
+    kc = torch.zeros(world, nblocks, nkv, bs, D, dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros_like(kc)
+    cos, sin = rope_tables(128, D, 5e5, cuda)
+    comm.gemm_push(x, w1)
+    q = comm.ar_norm_gemm(res, gamma, wqkv, eps, epilogue="rope_kv",
+                          rope=dict(positions=pos, cos=cos, sin=sin, block_tables=bt, k_cache=kc, v_cache=vc,
+                                    nq=nq, nkv=nkv))
+    torch.cuda.synchronize()
+    comm.check()
+    h_ref, z_ref = reference(x, w1, res0, gamma, wqkv, eps)
+    half = D // 2
+    for r in range(world):
+        z = z_ref[r].bfloat16().float().view(M, nq + 2 * nkv, D)
+        c, s = cos[pos.long()][:, None, :], sin[pos.long()][:, None, :]
+
+        def rot(t):
+            return torch.cat([t[..., :half] * c - t[..., half:] * s, t[..., half:] * c + t[..., :half] * s], -1)
+
+        assert rel_err(q[r].view(M, nq, D), rot(z[:, :nq])) <= TOL
+        for b in range(M):
+            blk, off = int(bt[b, int(pos[b]) // bs]), int(pos[b]) % bs
+            kref, vref = rot(z[b:b + 1, nq:nq + nkv])[0], z[b, nq + nkv:]
+            assert rel_err(kc[r, blk, :, off], kref) <= TOL, (r, b)
+            assert rel_err(vc[r, blk, :, off], vref) <= TOL, (r, b)
