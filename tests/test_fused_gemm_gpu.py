@@ -207,16 +207,16 @@ def test_layer_boundary_rope_kv_epilogue(cuda, world):
     comm.check()
     h_ref, z_ref = reference(x, w1, res0, gamma, wqkv, eps)
     half = D // 2
+    c, s = cos[pos.long()][:, None, :], sin[pos.long()][:, None, :]  # [M, 1, 64]: row b at position pos[b]
+
+    def rot(t):  # t [M, heads, D]
+        return torch.cat([t[..., :half] * c - t[..., half:] * s, t[..., half:] * c + t[..., :half] * s], -1)
+
     for r in range(world):
         z = z_ref[r].bfloat16().float().view(M, nq + 2 * nkv, D)
-        c, s = cos[pos.long()][:, None, :], sin[pos.long()][:, None, :]
-
-        def rot(t):
-            return torch.cat([t[..., :half] * c - t[..., half:] * s, t[..., half:] * c + t[..., :half] * s], -1)
-
-        assert rel_err(q[r].view(M, nq, D), rot(z[:, :nq])) <= TOL
+        qref, kref, vref = rot(z[:, :nq]), rot(z[:, nq:nq + nkv]), z[:, nq + nkv:]
+        assert rel_err(q[r].view(M, nq, D), qref) <= TOL
         for b in range(M):
             blk, off = int(bt[b, int(pos[b]) // bs]), int(pos[b]) % bs
-            kref, vref = rot(z[b:b + 1, nq:nq + nkv])[0], z[b, nq + nkv:]
-            assert rel_err(kc[r, blk, :, off], kref) <= TOL, (r, b)
-            assert rel_err(vc[r, blk, :, off], vref) <= TOL, (r, b)
+            assert rel_err(kc[r, blk, :, off], kref[b]) <= TOL, (r, b)
+            assert rel_err(vc[r, blk, :, off], vref[b]) <= TOL, (r, b)
