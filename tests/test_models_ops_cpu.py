@@ -1,0 +1,107 @@
+"""CPU tier for the model description, the fp32 oracles and the analyzers (no GPU, no native code)."""
+import json
+
+import torch
+
+from comm_opt_b200.harness.analyze_sweep import calibrate, table
+from comm_opt_b200.harness.launch_table import load as load_launches
+from comm_opt_b200.harness.launch_table import summarize
+from comm_opt_b200.models.llama import LLAMA3_70B, LLAMA3_8B, BlockAllocator, LlamaWeights, tiny_config
+from comm_opt_b200.ops.reference import paged_attention_ref, rope_ref, rope_tables
+from comm_opt_b200.parallel.communicator import TPCommunicator
+from comm_opt_b200.parallel.variant_table import VARIANTS, VariantTable
+
+
+def test_llama_presets_and_sharding():
+    assert abs(LLAMA3_70B.params / 1e9 - 70.6) < 0.2  # Llama-3-70B: 70.6 B parameters
+    assert abs(LLAMA3_8B.params / 1e9 - 8.03) < 0.05
+    s = LLAMA3_70B.shard(8)
+    assert s == dict(nq=8, nkv=1, inter=3584, vocab=16032)
+    # the TP=8 decode GEMM shapes the kernels and benches are tuned for
+    D = LLAMA3_70B.head_dim
+    assert (s["nq"] + 2 * s["nkv"]) * D == 1280 and 2 * s["inter"] == 7168
+
+
+def test_sharded_weights_slice_the_full_model():
+    cfg = tiny_config(layers=1)
+    full = LlamaWeights.full_random(cfg, device="cpu", seed=1)
+    parts = [LlamaWeights(cfg, r, 2, "cpu", full=full) for r in range(2)]
+    # row-parallel o_proj: the ranks' column blocks concatenate to the full matrix
+    wo = torch.cat([p.layers[0].wo for p in parts], 1)
+    assert torch.equal(wo, full["layers"][0]["wo"])
+    # column-parallel gate_up: gate and up halves sharded separately, then stacked per rank
+    I = cfg.inter // 2
+    g = torch.cat([p.layers[0].wgu[:I] for p in parts], 0)
+    assert torch.equal(g, full["layers"][0]["wgu"][:cfg.inter])
+
+
+def test_block_allocator_reuses_pages():
+    a = BlockAllocator(8)
+    p1 = a.alloc(5)
+    assert len(set(p1)) == 5
+    a.release(p1[:3])
+    p2 = a.alloc(6)
+    assert len(set(p2)) == 6 and not set(p2) & set(p1[3:])
+
+
+def test_paged_attention_oracle_matches_dense():
+    torch.manual_seed(0)
+    B, nq, nkv, D, bs, pages = 2, 4, 2, 16, 4, 5
+    seq = torch.tensor([7, 17])
+    kc = torch.randn(B * pages, nkv, bs, D)
+    vc = torch.randn(B * pages, nkv, bs, D)
+    bt = torch.randperm(B * pages).view(B, pages).int()
+    q = torch.randn(B, nq, D)
+    out = paged_attention_ref(q, kc, vc, bt, seq, 0.25)
+    for b in range(B):
+        k = kc[bt[b].long()].permute(1, 0, 2, 3).reshape(nkv, pages * bs, D)[:, :seq[b]]
+        v = vc[bt[b].long()].permute(1, 0, 2, 3).reshape(nkv, pages * bs, D)[:, :seq[b]]
+        k, v = k.repeat_interleave(nq // nkv, 0), v.repeat_interleave(nq // nkv, 0)
+        ref = torch.softmax(q[b][:, None, :] @ k.transpose(1, 2) * 0.25, -1) @ v
+        assert torch.allclose(out[b].float(), ref[:, 0], atol=1e-5)
+
+
+def test_rope_is_a_rotation():
+    cos, sin = rope_tables(64, 32, 1e4)
+    x = torch.randn(3, 2, 32)
+    pos = torch.tensor([0, 5, 63])
+    y = rope_ref(x, pos, cos, sin)
+    assert torch.allclose(y[0], x[0].float())                        # position 0: identity
+    assert torch.allclose(y.norm(dim=-1), x.float().norm(dim=-1), atol=1e-5)  # norm preserved
+
+
+def test_interleave_gate_up_roundtrip():
+    w = torch.randn(2, 256, 8)
+    il = TPCommunicator.interleave_gate_up(w)
+    g, u = w[:, :128], w[:, 128:]
+    assert torch.equal(il[:, :64], g[:, :64]) and torch.equal(il[:, 64:128], u[:, :64])
+    assert torch.equal(il[:, 128:192], g[:, 64:]) and torch.equal(il[:, 192:], u[:, 64:])
+
+
+def test_launch_table_summary(tmp_path):
+    p = tmp_path / "l.csv"
+    rows = ['"ID","Kernel Name","Metric Name","Metric Unit","Metric Value"']
+    for i, (k, v) in enumerate([("void k_gemm<16>(int)", "10,000"), ("k_attn(x)", "5000"), ("void k_gemm<16>(int)", "10000")]):
+        rows.append(f'"{i}","{k}","gpu__time_duration.sum","nsecond","{v}"')
+    p.write_text("\n".join(rows) + "\n")
+    out = summarize(load_launches(str(p)), steps=1)
+    assert out[0][0].startswith("void k_gemm") and out[0][1] == 2 and abs(out[0][2] - 20.0) < 1e-9
+    assert abs(sum(r[3] for r in out) - 1.0) < 1e-9
+
+
+def test_analyze_and_calibrate_synthetic_sweep(tmp_path):
+    rows = []
+    for T, (a1, a2, b) in {1: (5.0, 9.0, 10.0), 64: (20.0, 12.0, 30.0)}.items():
+        for impl, us in (("ours:lamport_1s", a1), ("ours:lamport_2s", a2), ("vllm_car", b)):
+            rows.append(dict(impl=impl, world=8, dtype="bfloat16", hidden=8192, tokens=T, bytes=T * 16384,
+                             p50_us=us, correct=True, skip="", variant=dict(blocks=8, threads=128, cluster=1)))
+    text, summary = table(rows)
+    assert "speedup" in text and len(summary) == 2
+    t = calibrate(rows, tmp_path / "vt.json")
+    c1 = t.lookup(8, torch.bfloat16, 2, 8192, 1, False)
+    c64 = t.lookup(8, torch.bfloat16, 2, 8192, 64, False)
+    assert c1.variant == VARIANTS["lamport_1s"] and c64.variant == VARIANTS["lamport_2s"]
+    t.save(tmp_path / "vt.json")
+    again = VariantTable.load(tmp_path / "vt.json")
+    assert again.lookup(8, torch.bfloat16, 2, 8192, 64, False).variant == VARIANTS["lamport_2s"]
+    json.loads((tmp_path / "vt.json").read_text())
