@@ -286,6 +286,15 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
 
 }  // namespace
 
+namespace {
+// Host planner of the layer-boundary GEMMs (no device work): {bn, tiles, splits, kps, xctas, ctas, smem}.
+std::vector<int64_t> py_fused_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t splits, int64_t sms,
+                                        bool consumer, int64_t epi) {
+  const cob::FusedGemmPlan p = cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, (int)sms, consumer, (int)epi);
+  return {p.bn, p.tiles, p.splits, p.kps, p.xctas, p.ctas, p.smem};
+}
+}  // namespace
+
 void register_ops(pybind11::module& m);  // ops_bindings.cpp
 void register_ipc(pybind11::module& m);  // ipc_bindings.cpp
 
@@ -317,6 +326,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("block_tables") = pybind11::none(), pybind11::arg("k_cache") = pybind11::none(),
         pybind11::arg("v_cache") = pybind11::none(), pybind11::arg("nq") = 0, pybind11::arg("nkv") = 0);
   m.attr("kMaxPieces") = cob::kMaxPieces;
+  m.def("fused_gemm_plan", &py_fused_gemm_plan);
   register_ops(m);
   register_ipc(m);
 }

@@ -42,3 +42,38 @@ def test_variant_rule_and_roundtrip(tmp_path):
     t2 = VariantTable.load(p)
     assert t2.entries == t.entries and json.loads(p.read_text())
     assert [rows_bucket(r) for r in (1, 2, 3, 5, 64, 65)] == [1, 2, 4, 8, 64, 128]
+
+
+@pytest.mark.skipif(not available(), reason="native extension not built")
+@pytest.mark.parametrize("model", ["70b", "8b"])
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_fused_gemm_plans_for_decode_shapes(model, tp):
+    """Every layer-boundary GEMM of a TP decode step gets a launchable plan: consumer grids resident at
+    once (<= SMs x CTAs per SM) and within the per-block epoch words, split-K only with one tile per
+    CTA, the per-piece sum-of-squares buffer within shared memory, paired epilogues 2..8 splits or none."""
+    from comm_opt_b200._ext import native
+    from comm_opt_b200.models.llama import PRESETS
+
+    C = native()
+    cfg = PRESETS[model]
+    s = cfg.shard(tp)
+    D, H = cfg.head_dim, cfg.hidden
+    sms = 148
+    for B in (1, 8, 32, 64, 128):
+        for N, K in ((H, s["nq"] * D), (H, s["inter"])):  # o_proj, down_proj: push GEMMs
+            bn, tiles, splits, kps, xctas, ctas, smem = C.fused_gemm_plan(B, N, K, 0, sms, False, 0)
+            assert splits >= 1 and xctas == tiles and ctas == tiles * splits and 128 % (8 * splits) == 0
+            assert kps * (splits - 1) < K // 64 and smem <= 227 * 1024
+        for N, epi in ((2 * s["inter"], 1), ((s["nq"] + 2 * s["nkv"]) * D, 2), (s["vocab"], 0)):
+            for e in {0, epi}:
+                bn, tiles, splits, kps, xctas, ctas, smem = C.fused_gemm_plan(B, N, H, 0, sms, True, e)
+                cap = min(sms * (2 if bn <= 64 else 1), C.kMaxBlocks)
+                if e and splits == 0:
+                    continue  # the paired epilogue is not offered for this shape: separate kernels run
+                assert 1 <= splits <= (8 if e else 16) and ctas == xctas * splits <= cap
+                assert ctas <= C.kMaxPieces and (splits == 1 or xctas == tiles)
+                if e:
+                    assert splits >= 2 and xctas == tiles
+                KV = H // 8
+                slen = min(KV, kps * 8)
+                assert B * (-(-slen // xctas) + 1) <= 2048, (B, N, splits, xctas)
