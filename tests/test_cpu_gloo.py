@@ -53,3 +53,34 @@ def test_fused_oracle_gloo_world2():
 
 def test_fused_oracle_gloo_world4():
     run_gloo(_check_oracle, 4)
+
+
+def _check_layer_boundary(rank, world):
+    import torch.distributed as dist
+
+    from comm_opt_b200.ops.reference import rel_err
+    from comm_opt_b200.parallel.cpu_collective import layer_boundary_cpu
+
+    g = torch.Generator().manual_seed(100 + rank)
+    M, K1, H, N, eps = 4, 64, 256, 96, 1e-5
+    x = torch.randn(M, K1, generator=g).bfloat16()
+    w_row = (0.1 * torch.randn(H, K1, generator=g)).bfloat16()
+    w_col = (0.1 * torch.randn(N, H, generator=g)).bfloat16()
+    shared = torch.Generator().manual_seed(5)
+    residual = torch.randn(M, H, generator=shared).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=shared)).bfloat16()
+    z, h = layer_boundary_cpu(x, w_row, residual, gamma, w_col, eps)
+    # unfused statement: all-reduce of fp32 GEMM outputs, residual, RMSNorm, then the next GEMM
+    y = x.double() @ w_row.double().t()
+    dist.all_reduce(y)
+    h_ref = residual.double() + y
+    n_ref = h_ref * torch.rsqrt(h_ref.pow(2).mean(-1, keepdim=True) + eps) * gamma.double()
+    z_ref = n_ref @ w_col.double().t()
+    assert rel_err(h, h_ref) <= 2 ** -5 and rel_err(z, z_ref) <= 2 ** -5
+    hs = [torch.empty_like(h) for _ in range(world)]
+    dist.all_gather(hs, h)
+    assert all(torch.equal(t, hs[0]) for t in hs)  # the new residual is identical on every rank
+
+
+def test_layer_boundary_statement_gloo_world2():
+    run_gloo(_check_layer_boundary, 2)
