@@ -40,6 +40,27 @@ ERR_BITS = {
 }
 
 
+def decode_state(words: list[int], rank: int) -> dict:
+    """One rank's control words (int64: epoch, unused | error << 32, err_detail[4]) -> readable state.
+    err_detail: [0] = kernel family and phase ((variant << 32) | phase for the fused all-reduce kernels,
+    0xF6 << 32 for the fused GEMMs), [1] = where (row << 32 | vector, or the rank's block), [2] = peer
+    or block, [3] = the call's epoch."""
+    err = (words[1] >> 32) & 0xFFFFFFFF
+    d = [w & 0xFFFFFFFFFFFFFFFF for w in words[2:6]]
+    fam = d[0] >> 32
+    where = dict(kernel="fused_gemm" if fam == 0xF6 else VARIANT_NAMES.get(fam, f"variant {fam}"),
+                 phase=d[0] & 0xFFFFFFFF, row=d[1] >> 32, vector=d[1] & 0xFFFFFFFF, peer_or_block=d[2], call=d[3])
+    return dict(rank=rank, epoch=words[0], error=err, detail=d, where=where,
+                reasons=[m for b, m in ERR_BITS.items() if err & b])
+
+
+def describe_error(state: dict) -> str:
+    w = state["where"]
+    return (f"rank {state['rank']}: {', '.join(state['reasons']) or 'no error'} in {w['kernel']} phase {w['phase']} "
+            f"(row {w['row']}, vector {w['vector']}, peer/block {w['peer_or_block']}, call {w['call']}; "
+            f"epoch now {state['epoch']})")
+
+
 class TPCommError(RuntimeError):
     pass
 
@@ -125,13 +146,8 @@ class TPCommunicator:
         if self.world == 1:
             return []
         torch.cuda.synchronize(self.device)
-        out = []
-        for r, h in enumerate(self.heap.local_heaps()):
-            w = self.heap.state_words(h).cpu().tolist()
-            err = (w[1] >> 32) & 0xFFFFFFFF
-            out.append(dict(rank=r if self.emulated else self.rank, epoch=w[0], error=err,
-                            detail=w[2:6], reasons=[m for b, m in ERR_BITS.items() if err & b]))
-        return out
+        return [decode_state(self.heap.state_words(h).cpu().tolist(), r if self.emulated else self.rank)
+                for r, h in enumerate(self.heap.local_heaps())]
 
     def epochs(self) -> list[int]:
         return [s["epoch"] for s in self.error_state()]
@@ -140,9 +156,7 @@ class TPCommunicator:
         """Raise TPCommTimeout if any local rank recorded a bounded-wait timeout."""
         for s in self.error_state():
             if s["error"]:
-                raise TPCommTimeout(f"rank {s['rank']}: {', '.join(s['reasons'])} "
-                                    f"(detail {[hex(d) for d in s['detail']]}, epoch {s['epoch']}); "
-                                    "call reset() on every rank before reuse")
+                raise TPCommTimeout(describe_error(s) + "; call reset() on every rank before reuse")
 
     # ------------------------------------------------------------------ variant choice
     def choose(self, rows: int, hidden: int, variant="auto", blocks=0, threads=0, cluster=0) -> Choice:

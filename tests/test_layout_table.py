@@ -77,3 +77,20 @@ def test_fused_gemm_plans_for_decode_shapes(model, tp):
                 KV = H // 8
                 slen = min(KV, kps * 8)
                 assert B * (-(-slen // xctas) + 1) <= 2048, (B, N, splits, xctas)
+
+
+def test_error_word_decoding():
+    from comm_opt_b200.parallel.communicator import decode_state, describe_error
+
+    # lamport_1s (variant 1) phase 2 timed out on row 3, vector 17, waiting for peer 5 in call 42
+    words = [41, (1 << 32) | 0, (1 << 32) | 2, (3 << 32) | 17, 5, 42]
+    st = decode_state(words, 0)
+    assert st["error"] == 1 and st["reasons"] == ["timeout waiting for landing data"]
+    assert st["where"]["kernel"] == "lamport_1s" and st["where"]["row"] == 3 and st["where"]["vector"] == 17
+    msg = describe_error(st)
+    assert "lamport_1s phase 2" in msg and "peer/block 5" in msg and "call 42" in msg
+    # fused GEMM family, error bits combined, a negative int64 word (bit 63 set) decodes unsigned
+    st = decode_state([7, (9 << 32) | 0, 0xF6 << 32, -1, 3, 8], 2)
+    assert st["where"]["kernel"] == "fused_gemm" and st["error"] == 9 and len(st["reasons"]) == 2
+    assert st["where"]["row"] == 0xFFFFFFFF
+    assert decode_state([0, 0, 0, 0, 0, 0], 1)["reasons"] == []
