@@ -14,6 +14,8 @@ Parts:
   fault      - fault injection on the host: one rank skips a call, the others' bounded waits run out,
                they report TPCommTimeout, every rank calls reset() and the next calls are correct.
                Uses the CUDA-IPC heap (never bound to a multicast object) and plain peer loads.
+  stress     - fused calls and layer boundaries checked call by call while a side stream runs large
+               GEMMs on every SM (memory-ordering stress under concurrent compute).
   decode     - tiny Llama-shaped model at TP = world vs the unsharded fp32 forward (logits), and
                identical greedy tokens on every rank.
   decode_fused - the same with the layer boundaries fused (GEMM push epilogue -> all-reduce + RMSNorm
@@ -196,6 +198,53 @@ def fault(C: Checker, dev, world):
     comm.close()
 
 
+def stress(C: Checker, dev, world, calls: int = 120):
+    """Memory-ordering stress: fused calls (mixed variants and sizes, one CUDA graph per shape replayed in
+    random order) and layer boundaries while a side stream keeps every SM busy with large GEMMs. Every
+    call is checked against the fp32 NCCL oracle; the side load is bounded by a launch count."""
+    comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=64, max_hidden=8192)
+    comm.prepare_fused_gemm(4096)
+    rng = random.Random(1234)  # same sequence on every rank
+    side = torch.cuda.Stream(dev)
+    a = torch.randn(8192, 8192, device=dev, dtype=torch.bfloat16)
+    vs = ["lamport_1s", "lamport_2s", "pull_1s", "pull_2s"] + (["nvls_1s", "nvls_2s"] if comm.have_nvls else [])
+    g = torch.Generator(device=dev).manual_seed(99 + dist.get_rank())
+    w1 = (0.02 * torch.randn(4096, 1024, generator=g, device=dev)).bfloat16()
+    w2 = (0.02 * torch.randn(384, 4096, generator=g, device=dev)).bfloat16()
+    bad = 0
+    for i in range(calls):
+        with torch.cuda.stream(side):  # compute load overlapping the collective
+            for _ in range(2):
+                torch.mm(a, a)
+        if rng.random() < 0.75:
+            v, rows = rng.choice(vs), rng.choice([1, 3, 8, 17, 64])
+            x, res0, gamma = inputs(rows, 8192, torch.bfloat16, dev, seed=i)
+            ref_out, ref_h = dist_fused_allreduce_add_rmsnorm_ref(x, res0, gamma, 1e-6)
+            res = res0.clone()
+            out, res = comm.fused_allreduce_add_rmsnorm(x, res, gamma, 1e-6, variant=v)
+            torch.cuda.synchronize()
+            ok = rel_err(out, ref_out) <= TOL and rel_err(res, ref_h) <= TOL
+        else:
+            M = rng.choice([1, 5, 16])
+            x = torch.randn(M, 1024, generator=g, device=dev).bfloat16()
+            res0 = torch.randn(M, 4096, device=dev, generator=torch.Generator(device=dev).manual_seed(i)).bfloat16()
+            gam = torch.ones(4096, device=dev, dtype=torch.bfloat16)
+            y = (x.float() @ w1.float().t())
+            dist.all_reduce(y)
+            h = res0.float() + y
+            ref = (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5)) @ w2.float().t()
+            res = res0.clone()
+            comm.gemm_push(x, w1)
+            z = comm.ar_norm_gemm(res, gam, w2, 1e-5)
+            torch.cuda.synchronize()
+            ok = rel_err(z, ref) <= TOL and rel_err(res, h) <= TOL
+        bad += 0 if ok else 1
+    side.synchronize()
+    comm.check()
+    C.check(bad == 0, f"stress: {bad} of {calls} calls wrong under concurrent GEMM load")
+    comm.close()
+
+
 def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False):
     import math
 
@@ -273,7 +322,7 @@ def main():
     t0 = time.time()
     try:
         for part in a.parts.split(","):
-            {"functional": functional, "fault": fault, "decode": decode_check,
+            {"functional": functional, "fault": fault, "decode": decode_check, "stress": stress,
              "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True),
              "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True)
              }[part](C, dev, world)
