@@ -199,9 +199,9 @@ def fault(C: Checker, dev, world):
 
 
 def stress(C: Checker, dev, world, calls: int = 120):
-    """Memory-ordering stress: fused calls (mixed variants and sizes, one CUDA graph per shape replayed in
-    random order) and layer boundaries while a side stream keeps every SM busy with large GEMMs. Every
-    call is checked against the fp32 NCCL oracle; the side load is bounded by a launch count."""
+    """Memory-ordering stress: fused calls (variants and sizes in a seeded random order, the same on
+    every rank) and layer boundaries while a side stream keeps the SMs busy with large GEMMs. Every call
+    is checked against the fp32 NCCL oracle; the side load is bounded by a launch count."""
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=64, max_hidden=8192)
     comm.prepare_fused_gemm(4096)
     rng = random.Random(1234)  # same sequence on every rank
