@@ -310,6 +310,20 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
 // ---------------------------------------------------------------------------------------------
 // Error bits in RankState::error. A kernel that gives up on a wait sets a bit, records where in
 // err_detail, and returns; the host reads the word and raises.
+// Checked build (COB_CHECKED=1 at build time): every heap address the collective kernels form is
+// range-checked; an out-of-range index sets kErrBounds in the rank's error word and the access goes to
+// a private scratch line instead of faulting the GPU. Off by default (no code in the hot path).
+#ifdef COB_CHECKED
+static __device__ __align__(16) unsigned char g_cob_oob_scratch[256];  // one per translation unit
+static __device__ unsigned int g_cob_oob_count;
+#define COB_IN_RANGE(ptr_expr, ok_expr, err_word)                                        \
+  ((ok_expr) ? (ptr_expr)                                                                \
+             : (atomicOr((err_word), (unsigned int)cob::kErrBounds), atomicAdd(&g_cob_oob_count, 1u), \
+                reinterpret_cast<decltype(ptr_expr)>(g_cob_oob_scratch)))
+#else
+#define COB_IN_RANGE(ptr_expr, ok_expr, err_word) (ptr_expr)
+#endif
+
 enum ErrBits : uint32_t {
   kErrTimeoutLanding = 1u << 0,
   kErrTimeoutFlag = 1u << 1,
@@ -318,6 +332,7 @@ enum ErrBits : uint32_t {
   kErrBadArgs = 1u << 4,
   kErrTimeoutGather = 1u << 5,
   kErrTimeoutGrid = 1u << 6,
+  kErrBounds = 1u << 7,  // checked build only: an index was out of range (the access was skipped)
 };
 
 // Per-thread wait budget: cheap spin count, then a %globaltimer deadline. Also gives up early when

@@ -41,17 +41,28 @@ __host__ __device__ __forceinline__ long long align_up(long long v, long long a)
 __device__ __forceinline__ RankState* state_of(const ARParams& p, int r) {
   return reinterpret_cast<RankState*>(p.base[r] + p.L.state);
 }
+// index ranges of the heap regions (checked builds record a violation instead of accessing)
+__device__ __forceinline__ bool heap_ok(const ARParams& p, int owner, int slot, int src, int row, int v, int vmax) {
+  return (unsigned)owner < (unsigned)p.L.world && (unsigned)slot < 2u && (unsigned)src < (unsigned)p.L.world &&
+         (unsigned)row < (unsigned)p.L.max_rows && (unsigned)v < (unsigned)vmax;
+}
+__device__ __forceinline__ unsigned int* err_word_of(const ARParams& p) {
+  return &reinterpret_cast<RankState*>(p.base[p.emulate ? blockIdx.y : p.rank] + p.L.state)->error;
+}
 __device__ __forceinline__ uint4* land1_at(const ARParams& p, int owner, int slot, int src, int row, int v) {
-  return reinterpret_cast<uint4*>(p.base[owner] + p.L.land1) +
-         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.max_hv + v);
+  return COB_IN_RANGE(reinterpret_cast<uint4*>(p.base[owner] + p.L.land1) +
+                          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.max_hv + v),
+                      heap_ok(p, owner, slot, src, row, v, p.L.max_hv), err_word_of(p));
 }
 __device__ __forceinline__ uint4* rs_at(const ARParams& p, int owner, int slot, int src, int row, int i) {
-  return reinterpret_cast<uint4*>(p.base[owner] + p.L.rs) +
-         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i);
+  return COB_IN_RANGE(reinterpret_cast<uint4*>(p.base[owner] + p.L.rs) +
+                          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i),
+                      heap_ok(p, owner, slot, src, row, i, p.L.sv_max), err_word_of(p));
 }
 __device__ __forceinline__ uint4* ag_at(const ARParams& p, int owner, int slot, int src, int row, int i) {
-  return reinterpret_cast<uint4*>(p.base[owner] + p.L.ag) +
-         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i);
+  return COB_IN_RANGE(reinterpret_cast<uint4*>(p.base[owner] + p.L.ag) +
+                          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.sv_max + i),
+                      heap_ok(p, owner, slot, src, row, i, p.L.sv_max), err_word_of(p));
 }
 // Partial sums of squares travel per "unit" of an owner slice (32 vectors, one per lane): units per
 // slice ceil(sv / 32), at most pu_max(L) words per (source rank, row).
@@ -67,7 +78,8 @@ __device__ __forceinline__ size_t stage_idx(const ARParams& p, int parity, int r
   return ((size_t)parity * p.L.max_rows + row) * p.L.max_hv + v;
 }
 __device__ __forceinline__ uint4* stage_at(const ARParams& p, int owner, int parity, int row, int v) {
-  return reinterpret_cast<uint4*>(p.base[owner] + p.L.stage) + stage_idx(p, parity, row, v);
+  return COB_IN_RANGE(reinterpret_cast<uint4*>(p.base[owner] + p.L.stage) + stage_idx(p, parity, row, v),
+                      heap_ok(p, owner, parity, 0, row, v, p.L.max_hv), err_word_of(p));
 }
 
 __device__ void record_error(RankState* st, uint32_t bit, uint64_t variant_phase, uint64_t where,

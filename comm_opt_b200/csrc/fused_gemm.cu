@@ -108,8 +108,12 @@ __device__ __forceinline__ RankState* fg_state(const FusedGemmParams& p, int r) 
   return reinterpret_cast<RankState*>(p.base[r] + p.L.state);
 }
 __device__ __forceinline__ uint4* fg_land(const FusedGemmParams& p, int owner, int slot, int src, int row, int v) {
-  return reinterpret_cast<uint4*>(p.base[owner] + p.L.land1) +
-         ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.max_hv + v);
+  return COB_IN_RANGE(
+      reinterpret_cast<uint4*>(p.base[owner] + p.L.land1) +
+          ((((size_t)slot * p.L.world + src) * p.L.max_rows + row) * p.L.max_hv + v),
+      (unsigned)owner < (unsigned)p.L.world && (unsigned)slot < 2u && (unsigned)src < (unsigned)p.L.world &&
+          (unsigned)row < (unsigned)p.L.max_rows && (unsigned)v < (unsigned)p.L.max_hv,
+      &reinterpret_cast<RankState*>(p.base[p.emulate ? blockIdx.z : p.rank] + p.L.state)->error);
 }
 __device__ __forceinline__ int lin_block() { return blockIdx.x + gridDim.x * blockIdx.y; }
 __device__ __forceinline__ uint64_t fg_epoch(const FusedGemmParams& p, int rank) {

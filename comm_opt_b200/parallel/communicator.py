@@ -37,6 +37,7 @@ ERR_BITS = {
     16: "bad arguments",
     32: "timeout in all-gather",
     64: "timeout in grid barrier",
+    128: "index out of range (checked build; access skipped)",
 }
 
 

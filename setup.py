@@ -17,6 +17,8 @@ CSRC = ROOT / "comm_opt_b200" / "csrc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v" if os.environ.get(
     "COB_PTXAS_VERBOSE") else "-Xptxas=-O3"]
+if os.environ.get("COB_CHECKED"):  # range-checked heap accesses in the collective kernels (debug builds)
+    NVCC.append("-DCOB_CHECKED")
 CXX = ["-O3", "-std=c++17"]
 
 SOURCES = [
