@@ -287,6 +287,26 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
 }  // namespace
 
 namespace {
+// Host geometry of one fused all-reduce call (no device work): {status, variant, blocks, threads, cluster}.
+std::vector<int64_t> py_fused_ar_config(std::vector<int64_t> layout, int64_t world, int64_t rows, int64_t hidden,
+                                        int64_t dtype, int64_t variant, int64_t blocks, int64_t threads,
+                                        int64_t cluster, int64_t emulate, int64_t sms, bool have_mc) {
+  cob::ARParams p = {};
+  p.L = vec_to_layout(layout);
+  p.world = (int)world;
+  p.rows = (int)rows;
+  p.hidden = (int)hidden;
+  p.dtype = (int)dtype;
+  p.variant = (int)variant;
+  p.blocks = (int)blocks;
+  p.threads = (int)threads;
+  p.cluster = (int)cluster;
+  p.emulate = (int)emulate;
+  p.mc = have_mc ? reinterpret_cast<char*>(1) : nullptr;  // only tested for null
+  const cudaError_t rc = cob::resolve_config(p, (int)sms);
+  return {(int64_t)rc, p.variant, p.blocks, p.threads, p.cluster};
+}
+
 // Host planner of the layer-boundary GEMMs (no device work): {bn, tiles, splits, kps, xctas, ctas, smem}.
 std::vector<int64_t> py_fused_gemm_plan(int64_t M, int64_t N, int64_t K, int64_t splits, int64_t sms,
                                         bool consumer, int64_t epi) {
@@ -327,6 +347,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("v_cache") = pybind11::none(), pybind11::arg("nq") = 0, pybind11::arg("nkv") = 0);
   m.attr("kMaxPieces") = cob::kMaxPieces;
   m.def("fused_gemm_plan", &py_fused_gemm_plan);
+  m.def("fused_ar_config", &py_fused_ar_config);
   register_ops(m);
   register_ipc(m);
 }

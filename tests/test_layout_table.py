@@ -94,3 +94,63 @@ def test_error_word_decoding():
     assert st["where"]["kernel"] == "fused_gemm" and st["error"] == 9 and len(st["reasons"]) == 2
     assert st["where"]["row"] == 0xFFFFFFFF
     assert decode_state([0, 0, 0, 0, 0, 0], 1)["reasons"] == []
+
+
+@pytest.mark.skipif(not available(), reason="native extension not built")
+def test_fused_ar_geometry_rules():
+    """resolve_config (host C++) over worlds, dtypes, sizes and variants: every accepted geometry is
+    launchable (blocks within the per-rank SM budget and the barrier slots, cluster divides the grid,
+    a row chunk fits the threads); rejections only where a variant cannot run."""
+    from comm_opt_b200._ext import native
+
+    C = native()
+    esz = {0: 4, 1: 2, 2: 2}
+    for world in (2, 4, 8):
+        for dtype in (0, 1, 2):
+            L = C.plan_layout(world, 512, 8192 if dtype else 4096, esz[dtype], 4096)
+            for emulate in (0, 1):
+                budget = 148 // (world if emulate else 1)
+                for hidden in (1024, 2048, 4096, 5120, 8192):
+                    hv = hidden * esz[dtype] // 16
+                    if hv > L[14]:
+                        continue
+                    for rows in (1, 3, 8, 17, 64, 512):
+                        for v in range(1, 7):
+                            for mc in (False, True):
+                                rc, var, b, t, cl = C.fused_ar_config(L, world, rows, hidden, dtype, v, 0, 0, 0,
+                                                                      emulate, 148, mc)
+                                nvls = v in (3, 4)
+                                two = v in (2, 4, 6)
+                                if nvls and not mc:
+                                    assert rc != 0
+                                    continue
+                                if two and (hv % world or hv % 32):
+                                    assert rc != 0
+                                    continue
+                                assert rc == 0, (world, dtype, emulate, hidden, rows, v)
+                                assert 1 <= b <= min(budget, C.kMaxBlocks) and t % 32 == 0 and t <= 512
+                                if two:
+                                    assert cl == 1 and t <= 256
+                                else:
+                                    assert cl in (1, 2, 4, 8) and b % cl == 0
+                                    assert -(-hv // cl) <= t * 4
+
+
+@pytest.mark.skipif(not available(), reason="native extension not built")
+def test_committed_variant_table_geometries_resolve():
+    """Every entry of the committed, measured variant table is accepted by the current kernels."""
+    from comm_opt_b200._ext import native
+    from comm_opt_b200.parallel.variant_table import VariantTable
+
+    C = native()
+    t = VariantTable.load()
+    for key, ch in t.entries.items():
+        w, dt, h, tb = key.split("/")
+        world, hidden = int(w[1:]), int(h[1:])
+        dtype = {"float32": 0, "float16": 1, "bfloat16": 2}[dt]
+        rows = int(tb[1:])
+        esize = 4 if dtype == 0 else 2
+        L = C.plan_layout(world, 512, hidden, esize, 4096)
+        rc, *_ = C.fused_ar_config(L, world, rows, hidden, dtype, ch.variant, ch.blocks, ch.threads, ch.cluster,
+                                   0, 148, True)
+        assert rc == 0, (key, ch)
