@@ -3,7 +3,8 @@ decode engine could use instead, timed identically inside CUDA graphs.
 
 Capability of the reference's M6 bench (exp/M6_allreduce_bakeoff/bench_torch.py:21-122: torch NCCL,
 vLLM custom all-reduce, PyTorch SymmetricMemory one-shot / two-shot; 1 KB - 8 MB; K all-reduces per
-graph; error against an fp32 all-reduce of the same inputs). Per (implementation, size): one eager call
+graph; error against an fp32 all-reduce of the same inputs), plus SymmetricMemory's NVSwitch multicast
+forms (multimem one-shot and multimem all-reduce), which the reference's A100 system could not run. Per (implementation, size): one eager call
 on seeded inputs checked against the fp32 sum, then 5 eager calls, K calls captured in one graph,
 3 warm replays and R timed replays; the per-op time of a replay is its time / K, the MAX over ranks is
 taken per replay, and p50 / p99 / mean over replays are reported (the reference reported the mean of
@@ -30,7 +31,8 @@ from ..parallel import TPCommunicator
 from ..utils.results import RunDir, gpu_state
 from ..utils.stats import summary
 
-DEFAULT_IMPLS = "ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_2s,torch_nccl,vllm_car,symm_one_shot,symm_two_shot"
+DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_2s,torch_nccl,vllm_car,symm_one_shot,"
+                 "symm_two_shot,symm_multimem,symm_multimem_one_shot")
 HIDDEN = 8192
 
 
@@ -107,6 +109,16 @@ class Bakeoff:
         s.copy_(x)
         if impl == "symm_one_shot":
             return (lambda: torch.ops.symm_mem.one_shot_all_reduce(s, "sum", self.group_name)), contextlib.nullcontext
+        if impl == "symm_multimem_one_shot":  # NVSwitch multicast load-reduce (NVLS), one shot
+            return (lambda: torch.ops.symm_mem.multimem_one_shot_all_reduce(s, "sum", self.group_name)), \
+                contextlib.nullcontext
+        if impl == "symm_multimem":  # NVLS reduce-scatter + multicast store, in place
+
+            def mm():
+                s.copy_(x)
+                torch.ops.symm_mem.multimem_all_reduce_(s, "sum", self.group_name)
+                return s
+            return mm, contextlib.nullcontext
 
         def two():
             s.copy_(x)
