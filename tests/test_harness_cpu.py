@@ -101,3 +101,21 @@ def test_bakeoff_shapes_and_runner_entries():
         assert e in ENTRY
     cmd, env = command(Job("bakeoff", 8), ROOT / "results" / "x", 29999)
     assert "--out-dir" in cmd and env["CUDA_VISIBLE_DEVICES"] == "0,1,2,3,4,5,6,7"
+
+
+def test_report_tables(tmp_path):
+    from comm_opt_b200.harness.report import render
+
+    d = tmp_path / "b"
+    d.mkdir()
+    rows = [dict(impl=i, batch=B, p50_us=v, correct=True, error="", roofline_us=12.2, frac_of_roofline=12.2 / v)
+            for B in (1, 8) for i, v in (("fused", 27.0), ("ours_split", 34.0))]
+    (d / "boundary.json").write_text(json.dumps(dict(world=8, rows=rows)))
+    t = render(d)
+    assert "| 1 | 27.00 | 34.00 | 12.20 | 0.452 |" in t
+    f = tmp_path / "bench.json"
+    f.write_text(json.dumps(dict(metric="m", n_gpus=8, value=7.7, e2e=dict(value=7.74), kernels_per_step=566,
+                                 config=dict(parallelism="tp8"))) + "\n" +
+                 json.dumps(dict(impl="reference", unavailable="not installable")) + "\n")
+    t = render(f)
+    assert "| m | 8 | 7.700 | 7.740 | 566 | parallelism=tp8 |" in t and "unavailable: not installable" in t
