@@ -12,6 +12,9 @@ schedules, with the invariants checked on every memory operation:
 * every rank finishes every call (no deadlock), with different grid sizes per call and any mix of
   variants (one CUDA graph per batch size, replayed in any order).
 
+The NVSwitch multicast variants are modelled with their multicast barriers (one add into every rank's
+counter per block, a wait for world x calls on the local copy) and, for the two-shot form, the
+multicast store of h into every rank's buffer, which must not overwrite a slice a rank has not read.
 The layer-boundary pair of csrc/fused_gemm.cu is modelled as one call of two kernels per rank
 (variant FG): the push GEMM's CTAs store column groups of every row into land1 of every rank (its
 own included) under the call's epoch without advancing it; after that kernel completes, the consumer
@@ -32,6 +35,7 @@ from dataclasses import dataclass, field
 FILL = None
 
 L1S, L2S, P1S, P2S = 1, 2, 5, 6
+NV1S, NV2S = 3, 4  # NVSwitch multicast: stage + multicast barrier, in-switch reduce (+ multicast store)
 FG = 7  # gemm_push + ar_norm_gemm (layer-boundary fusion)
 FG_COLS = 12  # modelled column groups of the pushed rows
 
@@ -61,6 +65,8 @@ class Memory:
     fg_land: dict = field(default_factory=dict)  # (owner, slot, src, row, col) -> (epoch, value) | FILL
     act: dict = field(default_factory=dict)      # (owner, col) -> epoch of the staged activation
     pflags: dict = field(default_factory=dict)   # (owner, piece) -> epoch tag
+    nvcnt: dict = field(default_factory=dict)    # (owner, block, k) -> multicast barrier counter
+    hbuf: dict = field(default_factory=dict)     # (owner, row, slice) -> (epoch, value) | FILL (multicast h)
 
 
 def value(rank: int, epoch: int, row: int) -> int:
@@ -76,6 +82,7 @@ class Rank:
         self.rng = random.Random(seed * 131 + rank)
         self.epoch = 0
         self.flag_calls: dict[int, int] = {}
+        self.nv_calls: dict[tuple, int] = {}
         self.done = False
         self.gen = self._run()
         self.results: list[dict] = []
@@ -181,6 +188,30 @@ class Rank:
                     self._read_stage(src, e, row)
                     got[(src, row)] = value(src, e, row)
                     yield True
+        elif call.variant == NV1S:
+            yield from self._stage_and_nv_barrier(e, b, rows, 0)
+            for row in rows:  # multimem.ld_reduce: every rank's staged row, summed in the switch
+                for src in range(W):
+                    self._read_stage(src, e, row)
+                    got[(src, row)] = value(src, e, row)
+                yield True
+        elif call.variant == NV2S:
+            yield from self._stage_and_nv_barrier(e, b, rows, 0)
+            for row in rows:  # owned slice: reduce in the switch, multicast-store h to every rank
+                for src in range(W):
+                    self._read_stage(src, e, row)
+                for owner in range(W):
+                    self._put(self.mem.hbuf, (owner, row, self.rank), (e, value(self.rank, e, row)))
+                yield True
+            yield from self._nv_barrier(b, 1)
+            for row in rows:
+                for sl in range(W):
+                    v = self._take(self.mem.hbuf, (self.rank, row, sl), e)
+                    if v is None:
+                        raise ProtocolViolation(f"rank {self.rank} call {e}: h slice {sl} of row {row} missing "
+                                                "after the second barrier")
+                    got[(sl, row)] = v[1]
+                    yield True
         else:
             raise ValueError(call.variant)
 
@@ -251,6 +282,23 @@ class Rank:
             while self.mem.flags.get((self.rank, b, peer), 0) < bc:
                 yield False
 
+    def _nv_barrier(self, b: int, k: int):
+        """Multicast barrier k of block b: one add to every rank's counter, wait for world x calls locally."""
+        W = self.mem.world
+        calls = self.nv_calls.get((b, k), 0) + 1
+        self.nv_calls[(b, k)] = calls
+        for owner in range(W):  # multimem.red: the switch adds to every rank's copy
+            self.mem.nvcnt[(owner, b, k)] = self.mem.nvcnt.get((owner, b, k), 0) + 1
+        yield True
+        while self.mem.nvcnt.get((self.rank, b, k), 0) < calls * W:
+            yield False
+
+    def _stage_and_nv_barrier(self, e: int, b: int, rows, k: int):
+        for row in rows:
+            self.mem.stage[(self.rank, e % self.mem.nslots, row)] = e
+            yield True
+        yield from self._nv_barrier(b, k)
+
     def _read_stage(self, src: int, e: int, row: int):
         got = self.mem.stage.get((src, e % self.mem.nslots, row))
         if got != e:
@@ -285,7 +333,7 @@ def simulate(world: int, calls: list[Call], seed: int = 0, max_steps: int = 2_00
             raise ProtocolViolation(f"deadlock: epochs {[x.epoch for x in ranks]}")
         if steps > max_steps:
             raise ProtocolViolation("step budget exhausted")
-    leftovers = [k for t in (mem.land1, mem.rs, mem.ag, mem.fg_land) for k, v in t.items() if v is not FILL]
+    leftovers = [k for t in (mem.land1, mem.rs, mem.ag, mem.fg_land, mem.hbuf) for k, v in t.items() if v is not FILL]
     if leftovers:
         raise ProtocolViolation(f"landing cells not restored to the sentinel: {leftovers[:4]}")
     return dict(steps=steps, epochs=[r.epoch for r in ranks])

@@ -56,3 +56,28 @@ def test_checker_detects_single_slot_fused_boundary():
         except ProtocolViolation:
             caught += 1
     assert caught >= 5
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_nvls_variants_mixed(world):
+    """Multicast-barrier variants (in-switch reduce, multicast store of h) mixed with every other
+    variant, different grid sizes per call, a slow rank."""
+    from comm_opt_b200.parallel.protocol_sim import NV1S, NV2S
+
+    for seed in range(2):
+        calls = random_calls(12, seed + 7 * world, variants=(NV1S, NV2S, L1S, P2S, NV2S), rows=(1, 3, 8),
+                             blocks=(1, 2, 3))
+        res = simulate(world, calls, seed=seed, slow_rank=(seed + 1) % world, slow_factor=30)
+        assert res["epochs"] == [12] * world
+
+
+def test_checker_detects_single_stage_slot_nvls():
+    from comm_opt_b200.parallel.protocol_sim import NV1S, NV2S
+
+    caught = 0
+    for seed in range(4):
+        try:
+            simulate(4, [Call(NV1S, 2, 3), Call(NV2S, 1, 3)] * 6, seed=seed, slow_rank=seed, slow_factor=40, nslots=1)
+        except ProtocolViolation:
+            caught += 1
+    assert caught >= 3
