@@ -154,3 +154,29 @@ def test_committed_variant_table_geometries_resolve():
         rc, *_ = C.fused_ar_config(L, world, rows, hidden, dtype, ch.variant, ch.blocks, ch.threads, ch.cluster,
                                    0, 148, True)
         assert rc == 0, (key, ch)
+
+
+@pytest.mark.skipif(not available(), reason="native extension not built")
+def test_streamk_gemm_plans():
+    """Stream-K partition of every decode projection (70B / 8B, TP 1/2/4/8, batch 1..256): CTAs within
+    the SMs and the flattened work, at most 48 contributors per split tile, batch tile covering M."""
+    from comm_opt_b200._ext import native
+    from comm_opt_b200.models.llama import PRESETS
+
+    C = native()
+    for model in ("70b", "8b"):
+        cfg = PRESETS[model]
+        for tp in (1, 2, 4, 8):
+            s = cfg.shard(tp)
+            D, H = cfg.head_dim, cfg.hidden
+            shapes = [((s["nq"] + 2 * s["nkv"]) * D, H), (H, s["nq"] * D), (2 * s["inter"], H), (H, s["inter"]),
+                      (s["vocab"], H)]
+            for M in (1, 8, 32, 64, 128, 256):
+                for N, K in shapes:
+                    bn, tiles, ctas, ws = C.gemm_plan(M, N, K, 148, 0)
+                    KT = -(-K // 64)
+                    total = tiles * KT
+                    assert bn >= M and bn in (16, 32, 64, 128, 256)
+                    assert tiles == -(-N // 128) and 1 <= ctas <= min(148, total)
+                    assert -(-KT * ctas // total) + 1 <= 48
+                    assert ws == ctas * 2 * 128 * bn * 4
