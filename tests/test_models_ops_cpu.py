@@ -105,3 +105,18 @@ def test_analyze_and_calibrate_synthetic_sweep(tmp_path):
     again = VariantTable.load(tmp_path / "vt.json")
     assert again.lookup(8, torch.bfloat16, 2, 8192, 64, False).variant == VARIANTS["lamport_2s"]
     json.loads((tmp_path / "vt.json").read_text())
+
+
+def test_attention_split_plans():
+    """Split-KV geometry: covers every page, at most 512 pages per split (the kernel's page list),
+    one wave of resident CTAs, cluster merge only for 2..8 splits."""
+    from comm_opt_b200.ops.kernels import ATTN_CTAS_PER_SM, attention_split_plan
+
+    for batch in (1, 2, 8, 32, 128):
+        for nkv in (1, 2, 8):
+            for pages in (1, 7, 64, 136, 512, 2048):
+                splits, pps, cluster = attention_split_plan(batch, nkv, pages, 148)
+                assert splits >= 1 and 1 <= pps <= 512 and splits * pps >= pages and (splits - 1) * pps < pages
+                assert cluster == (1 < splits <= 8)
+                if splits > 1:
+                    assert batch * nkv * splits <= ATTN_CTAS_PER_SM * 148 or pps == 512
