@@ -118,14 +118,25 @@ def nccl_variant_jobs(ngpus: int = 8) -> list[Job]:
                                                                "--graph", "20")) for k, v in variants.items()]
 
 
+def fused_hidden_jobs(ngpus: int = 8, impls: str = "ours:auto,vllm_car,trt_oneshot") -> list[Job]:
+    """The reference's M10 question (exp/M10_why_fused_slow/run.py:24-42): the same message bytes at
+    narrower rows. Hidden 8192 / 4096 / 2048 / 1024 with 1x / 2x / 4x / 8x the tokens."""
+    base = (1, 2, 4, 8, 16, 32, 64)
+    return [Job("fused_sweep", ngpus, variant=f"h{8192 // k}",
+                args=("--hidden", str(8192 // k), "--tokens", ",".join(str(t * k) for t in base), "--impls", impls,
+                      "--replays", "20"))
+            for k in (1, 2, 4, 8)]
+
+
 if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants"])
+    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden"])
     ap.add_argument("--gpus", default="2,4,8")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args()
     gp = tuple(int(g) for g in a.gpus.split(","))
-    jobs = collective_baseline_jobs(gp) if a.plan == "collective_baseline" else nccl_variant_jobs(max(gp))
+    jobs = {"collective_baseline": lambda: collective_baseline_jobs(gp), "nccl_variants": lambda: nccl_variant_jobs(max(gp)),
+            "fused_hidden": lambda: fused_hidden_jobs(max(gp))}[a.plan]()
     print(run_all(jobs, a.plan, a.seed))

@@ -25,11 +25,12 @@ def test_collectives_gloo_two_ranks(tmp_path):
 def test_runner_dry_run_prints_commands():
     env = dict(os.environ, DRY_RUN="1")
     code = ("from comm_opt_b200.harness.runner import *; run_all(collective_baseline_jobs((2, 8)), 'x', 3);"
-            "run_all(nccl_variant_jobs(8), 'y', 4)")
+            "run_all(nccl_variant_jobs(8), 'y', 4); run_all(fused_hidden_jobs(8), 'z', 5)")
     p = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stderr
     lines = [l for l in p.stdout.splitlines() if "torch.distributed.run" in l]
-    assert len(lines) == 2 + 6 and all("127.0.0.1" in l and "timeout" in l for l in lines)
+    assert len(lines) == 2 + 6 + 4 and all("127.0.0.1" in l and "timeout" in l for l in lines)
+    assert sum("--hidden 1024" in l and "--tokens 8,16,32" in l for l in lines) == 1
 
 
 def test_collective_loader_and_bound(tmp_path):
