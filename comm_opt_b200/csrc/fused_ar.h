@@ -58,10 +58,11 @@ struct Layout {
   long long land1;   // vec [2][W][R][HV]     one-shot push landing (Lamport fill)
   long long rs;      // vec [2][W][R][SV]     two-shot reduce-scatter landing (Lamport fill)
   long long ag;      // vec [2][W][R][SV]     two-shot all-gather landing (Lamport fill)
-  long long agp;     // u64 [2][W][R]         per-row partial sum of squares {f32, epoch32}
+  long long agp;     // u64 [2][W][R][PU]     per-unit partial sums of squares {f32, epoch32},
+                     //                       PU = ceil(SV / 32) units of 32 vectors per owner slice
   long long stage;   // vec [2][R][HV]        staged copy of x for pull / NVLS variants
   long long hbuf;    // vec [R][HV]           NVLS two-shot all-gathered h
-  long long hpart;   // u64 [R][W]            NVLS two-shot partials {f32, epoch32}
+  long long hpart;   // u64 [R][W][PU]        NVLS two-shot per-unit partials {f32, epoch32}
   long long gather;  // u64 [2][W][G]         small all-gather (LL words {u32 data, u32 epoch})
   long long total;   // heap size in bytes
   int world, max_rows, max_hv, sv_max, esize, max_gather;
