@@ -1,7 +1,9 @@
 """Where the time of one fused call goes, from the kernels' own phase stamps (%globaltimer, ns).
 
 The reference splits a decode step into compute / exposed communication / waiting from profiler traces
-(exp/M5_e2e_comm_share/traces.py:87-167); this tool goes one level down, inside the fused collective:
+(exp/M5_e2e_comm_share/traces.py:87-167) and restated vLLM's custom all-reduce with phase stamps
+(exp/M11_before_prototype/car_timed.cu:34-47); this tool goes one level down, inside the fused collective
+(with `--allreduce`, inside the plain all-reduce, whose pull variants share vLLM's phase structure):
 every block of every call records start, inputs sent (or staged), barrier passed / owner slice reduced,
 all peer data received and done. Per variant and token count it reports, as the max over ranks of the
 per-rank mean over calls:
@@ -86,6 +88,9 @@ def main():
     ap.add_argument("--graph-ops", type=int, default=20)
     ap.add_argument("--replays", type=int, default=10)
     ap.add_argument("--out-dir", default=None)
+    ap.add_argument("--allreduce", action="store_true",
+                    help="plain all-reduce (norm epilogue off): pull_1s / pull_2s then have the phase structure of "
+                         "vLLM's one-stage / two-stage custom all-reduce (barrier, peer loads, barrier)")
     a = ap.parse_args()
     local = int(os.environ["LOCAL_RANK"])
     dev = torch.device("cuda", local)
@@ -96,7 +101,8 @@ def main():
     DT, H = getattr(torch, a.dtype), a.hidden
     tokens = [int(t) for t in a.tokens.split(",")]
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=DT, max_rows=max(tokens), max_hidden=H)
-    run = RunDir("phase_profile", Path(a.out_dir) if a.out_dir else None) if rank == 0 else None
+    run = RunDir("phase_profile_ar" if a.allreduce else "phase_profile", Path(a.out_dir) if a.out_dir else None) \
+        if rank == 0 else None
     if run:
         run.snapshot()
     cap = a.graph_ops * a.replays + 8
@@ -109,7 +115,10 @@ def main():
             out = torch.empty_like(x)
 
             def fn():
-                comm.fused_allreduce_add_rmsnorm(x, res, gamma, 1e-6, out=out, variant=v)
+                if a.allreduce:
+                    comm.all_reduce(x, out, variant=v)
+                else:
+                    comm.fused_allreduce_add_rmsnorm(x, res, gamma, 1e-6, out=out, variant=v)
 
             err = ""
             try:
