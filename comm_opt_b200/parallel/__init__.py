@@ -1,7 +1,8 @@
 """Communication substrate: symmetric heap, tensor-parallel communicator, variant table."""
 from .communicator import TPCommError, TPCommTimeout, TPCommunicator
+from .config import CommConfig
 from .symm import HeapLayout, SymmetricHeap, plan_layout
 from .variant_table import VARIANT_NAMES, VARIANTS, Choice, VariantTable
 
-__all__ = ["TPCommunicator", "TPCommError", "TPCommTimeout", "SymmetricHeap", "HeapLayout", "plan_layout",
+__all__ = ["TPCommunicator", "CommConfig", "TPCommError", "TPCommTimeout", "SymmetricHeap", "HeapLayout", "plan_layout",
            "VariantTable", "Choice", "VARIANTS", "VARIANT_NAMES"]

@@ -117,6 +117,14 @@ class TPCommunicator:
         self._fg_err_t: torch.Tensor | None = None
         self.last_fused_gemm: tuple | None = None
 
+    @classmethod
+    def from_config(cls, group=None, config=None, **kw) -> "TPCommunicator":
+        """Build from a CommConfig (defaults + COB_* environment overrides when `config` is None)."""
+        from .config import CommConfig
+
+        cfg = config if config is not None else CommConfig.from_env()
+        return cls(group, **cfg.kwargs(), **kw)
+
     # ------------------------------------------------------------------ state management
     def _host_barrier(self):
         if not self.emulated and self.world > 1:

@@ -84,3 +84,75 @@ def _check_layer_boundary(rank, world):
 
 def test_layer_boundary_statement_gloo_world2():
     run_gloo(_check_layer_boundary, 2)
+
+
+def _check_functional_api(rank, world):
+    import torch.distributed as dist
+
+    import comm_opt_b200
+    from comm_opt_b200.ops.reference import rel_err
+
+    x, residual, gamma = _inputs(rank)
+    res = residual.clone()
+    out, new_res = comm_opt_b200.fused_allreduce_add_rmsnorm(x, res, gamma, 1e-6)
+    assert new_res is res  # updated in place and returned
+    xs = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(xs, x)
+    h_ref = residual.double() + sum(t.double() for t in xs)
+    out_ref = h_ref * torch.rsqrt(h_ref.pow(2).mean(-1, keepdim=True) + 1e-6) * gamma.double()
+    assert rel_err(res, h_ref) < 1e-6 and rel_err(out, out_ref) < 1e-5
+    g = torch.Generator().manual_seed(50 + rank)
+    xb = torch.randn(4, 32, generator=g)
+    w_row = 0.1 * torch.randn(4096, 32, generator=g)
+    w_col = 0.1 * torch.randn(64, 4096, generator=g)
+    res = residual.clone()
+    z, _ = comm_opt_b200.layer_boundary(xb, w_row, res, gamma, w_col, 1e-6)
+    y = xb.double() @ w_row.double().t()
+    dist.all_reduce(y)
+    h = residual.double() + y
+    zr = (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6) * gamma.double()) @ w_col.double().t()
+    assert rel_err(z, zr) < 1e-5 and rel_err(res, h) < 1e-6
+
+
+def test_functional_api_gloo_world2():
+    run_gloo(_check_functional_api, 2)
+
+
+def test_functional_api_communicator_cache():
+    """Capacity growth: a call beyond the cached communicator's capacity closes it and builds a larger one."""
+    from comm_opt_b200 import api
+    from comm_opt_b200.parallel.config import CommConfig
+
+    made, closed = [], []
+
+    class Fake:
+        def __init__(self, group, cfg, device=None, dtype=None):
+            self.max_rows, self.max_hidden = cfg.max_rows, cfg.max_hidden
+            made.append((cfg.max_rows, cfg.max_hidden))
+
+        def close(self):
+            closed.append(1)
+
+    api._COMMS.clear()
+    x = torch.zeros(2, 8)
+    cfg = CommConfig(max_rows=4, max_hidden=1024)
+    c1 = api.communicator(x, 1024, 3, None, cfg, factory=Fake)
+    assert api.communicator(x, 1024, 4, None, cfg, factory=Fake) is c1
+    c2 = api.communicator(x, 2048, 9, None, cfg, factory=Fake)
+    assert c2 is not c1 and closed == [1] and made == [(4, 1024), (9, 2048)]
+    api._COMMS.clear()
+
+
+def test_comm_config_env_and_dict():
+    import pytest
+
+    from comm_opt_b200.parallel.config import CommConfig
+
+    c = CommConfig.from_env(env={"COB_MAX_ROWS": "64", "COB_PDL": "0", "COB_WAIT_TIMEOUT_MS": "250",
+                                 "COB_HEAP_BACKEND": "ipc"})
+    assert (c.max_rows, c.pdl, c.timeout_ms, c.backend) == (64, False, 250.0, "ipc")
+    assert CommConfig.from_dict(c.kwargs()) == c
+    with pytest.raises(ValueError):
+        CommConfig.from_dict({"max_rowz": 3})
+    with pytest.raises(ValueError):
+        CommConfig(backend="nccl")
