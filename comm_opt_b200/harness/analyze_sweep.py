@@ -51,6 +51,29 @@ def table(rows: list[dict]) -> tuple[str, list[dict]]:
     return "\n".join(out), summary
 
 
+def repeats(rows: list[dict], ours: str, base: str) -> list[dict]:
+    """Independent launches of the same configuration (several sweeps): per (world, tokens) the median
+    and [min, max] of the per-launch p50 for `ours` and `base`, and whether the difference is
+    "effective" by the reference's rule (>= 3 % and disjoint [min, max] intervals,
+    exp/M18_incremental/README.md:34-40)."""
+    from ..utils.stats import disjoint, median_minmax
+
+    out = []
+    keys = sorted({(r["world"], r["tokens"]) for r in rows})
+    for w, T in keys:
+        a = [r["p50_us"] for r in rows if (r["world"], r["tokens"], r["impl"]) == (w, T, ours) and r["correct"]
+             and r["p50_us"]]
+        b = [r["p50_us"] for r in rows if (r["world"], r["tokens"], r["impl"]) == (w, T, base) and r["correct"]
+             and r["p50_us"]]
+        if not a or not b:
+            continue
+        ma, mb = median_minmax(a), median_minmax(b)
+        gain = mb["med"] / ma["med"] - 1.0
+        out.append(dict(world=w, tokens=T, ours=ma, base=mb, gain=gain,
+                        effective=abs(gain) >= 0.03 and disjoint(ma, mb) and len(a) >= 3 and len(b) >= 3))
+    return out
+
+
 def calibrate(rows: list[dict], table_path: Path | None = None) -> VariantTable:
     """Fastest correct variant (with its geometry) per (world, dtype, hidden, rows bucket)."""
     import torch
@@ -74,8 +97,19 @@ def main():
     ap.add_argument("sweeps", nargs="+")
     ap.add_argument("--calibrate", action="store_true", help="update the committed variant table")
     ap.add_argument("--table", default=None)
+    ap.add_argument("--repeats", nargs=2, metavar=("OURS", "BASELINE"),
+                    help="median [min, max] over the given sweeps (independent launches) and the effectiveness rule")
     a = ap.parse_args()
     rows = load(a.sweeps)
+    if a.repeats:
+        print(f"| world | tokens | {a.repeats[0]} med [min, max] | {a.repeats[1]} med [min, max] | gain | effective |")
+        print("|---|---|---|---|---|---|")
+        for r in repeats(rows, *a.repeats):
+            o, b = r["ours"], r["base"]
+            print(f"| {r['world']} | {r['tokens']} | {o['med']:.2f} [{o['lo']:.2f}, {o['hi']:.2f}] (n={o['n']}) | "
+                  f"{b['med']:.2f} [{b['lo']:.2f}, {b['hi']:.2f}] (n={b['n']}) | {100 * r['gain']:+.1f}% | "
+                  f"{'yes' if r['effective'] else 'no'} |")
+        return
     text, _ = table(rows)
     print(text)
     if a.calibrate:

@@ -120,3 +120,16 @@ def test_attention_split_plans():
                 assert cluster == (1 < splits <= 8)
                 if splits > 1:
                     assert batch * nkv * splits <= ATTN_CTAS_PER_SM * 148 or pps == 512
+
+
+def test_repeat_statistics_effectiveness_rule():
+    from comm_opt_b200.harness.analyze_sweep import repeats
+
+    rows = []
+    for rep, (a, b) in enumerate([(10.0, 12.0), (10.2, 12.5), (10.1, 12.2)]):
+        for impl, v in (("ours:x", a), ("base", b)):
+            rows.append(dict(world=8, tokens=1, impl=impl, p50_us=v, correct=True))
+            rows.append(dict(world=8, tokens=2, impl=impl, p50_us=v + (rep == 0) * 3.0, correct=True))
+    out = {r["tokens"]: r for r in repeats(rows, "ours:x", "base")}
+    assert out[1]["effective"] and abs(out[1]["ours"]["med"] - 10.1) < 1e-9 and out[1]["ours"]["n"] == 3
+    assert not out[2]["effective"]  # the first launch's outlier makes the intervals overlap
