@@ -30,6 +30,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=2048)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--out-dir", default="results/traces")
+    ap.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=1)
     a = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -44,7 +45,7 @@ def main():
     w = LlamaWeights(cfg, rank, world, dev, seed=0)
     comm = TPCommunicator(group, device=dev, dtype=torch.bfloat16, max_rows=max(8, a.batch), max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, w, comm, max_batch=a.batch, max_seq=a.prompt + a.steps + 64, device=dev,
-                            nccl_group=group)
+                            nccl_group=group, fuse_boundary=bool(a.fuse_boundary))
     prompts = torch.randint(0, cfg.vocab, (a.batch, a.prompt), generator=torch.Generator().manual_seed(0))
     first = runner.prefill(prompts)
     runner.start(a.batch, first, a.prompt)
@@ -67,8 +68,10 @@ def main():
     if rank == 0:
         rows = decompose(sorted(out.glob("trace_rank*.json")), "decode_step")
         share = sum(r["exposed_comm_us"] for r in rows) / max(1e-9, sum(r["wall_us"] for r in rows))
+        fused = sum(r.get("fused_us", 0.0) for r in rows) / max(1e-9, sum(r["wall_us"] for r in rows))
         print(json.dumps(dict(model=cfg.name, layers=cfg.layers, tp=world, batch=a.batch, steps=a.steps,
-                              exposed_comm_share=round(share, 4),
+                              fuse_boundary=runner.fuse_boundary, exposed_comm_share=round(share, 4),
+                              fused_gemm_collective_share=round(fused, 4),
                               mean_wall_us=sum(r["wall_us"] for r in rows) / max(1, len(rows)))), flush=True)
     runner.release_graphs()
     if world > 1:

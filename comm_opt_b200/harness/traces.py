@@ -18,6 +18,9 @@ from pathlib import Path
 
 COMM_RE = re.compile(r"k_oneshot|k_twoshot|k_allgather|nccl|cross_device_reduce|custom_?all_?reduce|allreduce_fusion|"
                      r"one_shot_all_reduce|two_shot_all_reduce|multimem", re.I)
+# kernels that do a GEMM and the collective together (layer-boundary fusion): counted as compute in the
+# split above, and reported on their own as fused_us
+FUSED_RE = re.compile(r"k_gemm_push|k_ar_norm_gemm", re.I)
 GPU_CATS = {"kernel", "gpu_memcpy", "gpu_memset"}
 
 
@@ -64,6 +67,7 @@ def decompose_rank(events: list[dict], step_re: str) -> tuple[list[dict], list[f
     work = [e for e in events if e.get("cat") in GPU_CATS and e.get("dur", 0) > 0]
     comm = union([(e["ts"], e["ts"] + e["dur"]) for e in work if COMM_RE.search(e.get("name", ""))])
     comp = union([(e["ts"], e["ts"] + e["dur"]) for e in work if not COMM_RE.search(e.get("name", ""))])
+    fused = union([(e["ts"], e["ts"] + e["dur"]) for e in work if FUSED_RE.search(e.get("name", ""))])
     marks = sorted((e["ts"], e["ts"] + e.get("dur", 0)) for e in events
                    if e.get("cat") in ("gpu_user_annotation", "user_annotation") and re.search(step_re, e.get("name", "")))
     steps = []
@@ -73,7 +77,7 @@ def decompose_rank(events: list[dict], step_re: str) -> tuple[list[dict], list[f
         busy = length(union(c + k))
         steps.append(dict(wall_us=e - s, compute_only_us=length(k) - length(both),
                           exposed_comm_us=length(c) - length(both), overlap_us=length(both), idle_us=e - s - busy,
-                          comm_total_us=length(c)))
+                          comm_total_us=length(c), fused_us=length(union(clip(fused, s, e)))))
     comm_durs = [e["dur"] for e in sorted(work, key=lambda x: x["ts"]) if COMM_RE.search(e.get("name", ""))]
     return steps, comm_durs
 
