@@ -42,6 +42,8 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--gemm", choices=["cob", "torch"], default="cob")
+    p.add_argument("--collective", choices=["ours", "nccl"], default="ours",
+                   help="nccl: the same runner with NCCL all-reduce + add/RMSNorm kernel (baseline decode step)")
     p.add_argument("--fuse-epilogues", type=int, choices=[0, 1], default=0,
                    help="with fused boundaries: SiLU * up and RoPE + KV append in the consumer GEMMs")
     p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=1,
@@ -153,7 +155,7 @@ def main():
     comm = TPCommunicator(group, device=dev, dtype=torch.bfloat16, max_rows=max(B, 8), max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, weights, comm, max_batch=B, max_seq=max_seq, device=dev, gemm=args.gemm,
                             nccl_group=group, fuse_boundary=bool(args.fuse_boundary),
-                            fuse_epilogues=bool(args.fuse_epilogues))
+                            fuse_epilogues=bool(args.fuse_epilogues), collective=args.collective)
     prompts = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(1234))
     first = runner.prefill(prompts)
     runner.start(B, first, P)
@@ -228,7 +230,7 @@ def main():
             "data": "synthetic: uniform-random prompt token ids (seed 1234), random-init weights N(0, 0.02)",
             "config": {"model": cfg.name + ("" if args.layers is None else f"-L{cfg.layers}-INVALID"),
                        "global_batch": B, "seq_len": P, "decode_tokens_timed": K, "parallelism": f"tp{world}",
-                       "gemm": args.gemm, "fuse_boundary": runner.fuse_boundary,
+                       "gemm": args.gemm, "collective": args.collective, "fuse_boundary": runner.fuse_boundary,
                        "fuse_epilogues": runner.fuse_boundary and runner.fuse_epilogues,
                        "fuse_fallback": runner.fuse_error[:200] or None,
                        "tokens_per_s": round(B * 1000.0 / ms, 1),

@@ -20,7 +20,8 @@ Parts:
                identical greedy tokens on every rank.
   decode_fused - the same with the layer boundaries fused (GEMM push epilogue -> all-reduce + RMSNorm
                inside the next GEMM); decode_fused_epi also moves SiLU * up and RoPE + KV append
-               into the consumer GEMMs' epilogues.
+               into the consumer GEMMs' epilogues; decode_nccl runs the baseline step (NCCL all-reduce +
+               add/RMSNorm kernel) through the same runner.
 Rank 0 prints one JSON summary; the exit code is non-zero on any failure.
 """
 from __future__ import annotations
@@ -245,7 +246,7 @@ def stress(C: Checker, dev, world, calls: int = 120):
     comm.close()
 
 
-def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False):
+def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False, collective: str = "ours"):
     import math
 
     import torch.nn.functional as F
@@ -258,7 +259,7 @@ def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = 
     w = LlamaWeights(cfg, dist.get_rank(), world, dev, full=full)
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, w, comm, max_batch=4, max_seq=96, device=dev, nccl_group=dist.group.WORLD,
-                            fuse_boundary=fused, fuse_epilogues=epilogues)
+                            fuse_boundary=fused, fuse_epilogues=epilogues, collective=collective)
     C.check(runner.fuse_boundary == fused, "layer-boundary fusion engaged as requested")
     prompts = torch.randint(0, cfg.vocab, (3, 29), generator=torch.Generator().manual_seed(1))
     first = runner.prefill(prompts)
@@ -324,7 +325,8 @@ def main():
         for part in a.parts.split(","):
             {"functional": functional, "fault": fault, "decode": decode_check, "stress": stress,
              "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True),
-             "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True)
+             "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True),
+             "decode_nccl": lambda C, dev, world: decode_check(C, dev, world, collective="nccl")
              }[part](C, dev, world)
     except Exception:
         err = traceback.format_exc()

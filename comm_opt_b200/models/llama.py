@@ -177,7 +177,7 @@ class TPDecodeRunner:
 
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
                  device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
-                 fuse_epilogues: bool = False):
+                 fuse_epilogues: bool = False, collective: str = "ours"):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -201,7 +201,12 @@ class TPDecodeRunner:
         # layer-boundary fusion: o_proj / down_proj push their partial sums straight into the
         # all-reduce landing buffers, and the all-reduce + residual + RMSNorm runs inside the next
         # GEMM (gate_up, the next layer's qkv, the LM head); needs TP > 1, bf16 and this package's GEMMs
-        self.fuse_boundary = bool(fuse_boundary and self.tp > 1 and self.dtype == torch.bfloat16 and gemm == "cob")
+        # "ours": the fused all-reduce + residual + RMSNorm kernel; "nccl": the baseline decode step, NCCL
+        # all-reduce (captured in the graph) followed by this package's add + RMSNorm kernel
+        assert collective in ("ours", "nccl")
+        self.collective = collective
+        self.fuse_boundary = bool(fuse_boundary and self.tp > 1 and self.dtype == torch.bfloat16 and gemm == "cob"
+                                  and collective == "ours")
         self.fuse_error = ""
         # with fuse_boundary: SiLU * up and RoPE + KV append inside the consumer GEMMs' epilogues
         self.fuse_epilogues = bool(fuse_epilogues)
@@ -306,12 +311,12 @@ class TPDecodeRunner:
                              self.cache.v[i], s["nq"], s["nkv"])
             buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
             self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
-            comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], L.ln2, cfg.eps, out=buf["h"])
+            self._allreduce_add_rmsnorm(buf, L.ln2)
             self.lin[(i, "gu")](buf["h"], out=buf["gu"])
             K.silu_mul(buf["gu"], out=buf["act"])
             self.lin[(i, "down")](buf["act"], out=buf["part"])
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
-            comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], nxt, cfg.eps, out=buf["h"])
+            self._allreduce_add_rmsnorm(buf, nxt)
             n += 5 + 4 * ours
         self.lin["head"](buf["h"], out=buf["logits"])
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
@@ -322,6 +327,16 @@ class TPDecodeRunner:
         K.argmax_combine(buf["gathered"] if self.tp > 1 else buf["keys"].view(1, B), self.tp, ids=buf["ids"],
                          positions=buf["pos"], seq_lens=buf["lens"], local_keys=buf["keys"])
         return n + 1
+
+    def _allreduce_add_rmsnorm(self, buf: dict, gamma: torch.Tensor):
+        """h = RMSNorm(residual + sum_ranks(part)) * gamma, residual updated (one or two kernels)."""
+        if self.collective == "nccl" and self.tp > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(buf["part"], group=self.nccl_group)
+            K.add_rmsnorm(buf["part"], buf["res"], gamma, self.cfg.eps, out=buf["h"])
+        else:
+            self.comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], gamma, self.cfg.eps, out=buf["h"])
 
     def _fused_epilogues(self, B: int, buf: dict) -> tuple[bool, bool]:
         """(swiglu in the gate_up GEMM, RoPE + KV append in the QKV GEMM) for batch B: used when the
