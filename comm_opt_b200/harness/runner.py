@@ -25,6 +25,8 @@ ENTRY = {
     "selftest": "comm_opt_b200.harness.mp_selftest",
     "bakeoff": "comm_opt_b200.harness.allreduce_bakeoff",
     "phases": "comm_opt_b200.harness.phase_profile",
+    "boundary": "comm_opt_b200.harness.boundary_bench",
+    "bench": "bench.py",  # a script at the repository root, not a module
 }
 
 GPUSETS = {  # set A: first GPUs; set B: other physical GPUs / rank order (the reference's second set)
@@ -63,15 +65,17 @@ def gpu_processes() -> str:
 
 def command(job: Job, out: Path, port: int) -> tuple[list[str], dict]:
     env = dict(os.environ, CUDA_VISIBLE_DEVICES=GPUSETS[job.ngpus][job.gpuset], **job.env)
+    target = [ENTRY[job.entry]] if ENTRY[job.entry].endswith(".py") else ["-m", ENTRY[job.entry]]
     cmd = ["timeout", "-k", "60", str(job.timeout_s), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={job.ngpus}", "--master-addr=127.0.0.1", f"--master-port={port}", "-m",
-           ENTRY[job.entry], *job.args]
+           f"--nproc-per-node={job.ngpus}", "--master-addr=127.0.0.1", f"--master-port={port}", *target, *job.args]
     if job.entry == "collectives":
         cmd += ["--out", str(out / f"{job.tag}.json")]
     elif job.entry == "fused_sweep":
         cmd += ["--out-dir", str(out / "runs"), "--ts", job.tag]
-    elif job.entry in ("bakeoff", "phases"):
+    elif job.entry in ("bakeoff", "phases", "boundary"):
         cmd += ["--out-dir", str(out / "runs")]
+    elif job.entry == "bench":
+        cmd += ["--gpus", str(job.ngpus), "--out", str(out / f"{job.tag}.json")]
     return cmd, env
 
 
@@ -118,6 +122,27 @@ def nccl_variant_jobs(ngpus: int = 8) -> list[Job]:
                                                                "--graph", "20")) for k, v in variants.items()]
 
 
+def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
+    """Every headline measurement of the project as independent jobs: the fused-op sweep against all
+    baselines, the layer-boundary bench, and the TP decode (fused / separate boundaries / NCCL baseline
+    step) at each GPU count, plus the 70B decode batch sweep at 8 GPUs."""
+    sweep_impls = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_1s,ours:nvls_2s,nccl_norm,vllm_car,"
+                   "trt_oneshot,trt_twoshot")
+    jobs = []
+    for g in gpus:
+        jobs.append(Job("fused_sweep", g, args=("--impls", sweep_impls + (",ref_m16nf" if g == 8 else ""),
+                                                "--replays", "20")))
+        jobs.append(Job("boundary", g))
+        for variant, extra in (("fused", ()), ("separate", ("--fuse-boundary", "0")),
+                               ("nccl", ("--collective", "nccl"))):
+            jobs.append(Job("bench", g, variant=variant, args=("--steps", "64", "--warmup", "4", *extra)))
+    for B in batches:
+        if B != 8:
+            jobs.append(Job("bench", max(gpus), variant=f"b{B}", args=("--steps", "32", "--warmup", "3",
+                                                                       "--batch", str(B))))
+    return jobs
+
+
 def fused_hidden_jobs(ngpus: int = 8, impls: str = "ours:auto,vllm_car,trt_oneshot") -> list[Job]:
     """The reference's M10 question (exp/M10_why_fused_slow/run.py:24-42): the same message bytes at
     narrower rows. Hidden 8192 / 4096 / 2048 / 1024 with 1x / 2x / 4x / 8x the tokens."""
@@ -132,11 +157,11 @@ if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden"])
+    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden", "headline"])
     ap.add_argument("--gpus", default="2,4,8")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args()
     gp = tuple(int(g) for g in a.gpus.split(","))
     jobs = {"collective_baseline": lambda: collective_baseline_jobs(gp), "nccl_variants": lambda: nccl_variant_jobs(max(gp)),
-            "fused_hidden": lambda: fused_hidden_jobs(max(gp))}[a.plan]()
+            "fused_hidden": lambda: fused_hidden_jobs(max(gp)), "headline": lambda: headline_jobs(gp)}[a.plan]()
     print(run_all(jobs, a.plan, a.seed))

@@ -33,6 +33,17 @@ def test_runner_dry_run_prints_commands():
     assert sum("--hidden 1024" in l and "--tokens 8,16,32" in l for l in lines) == 1
 
 
+def test_runner_headline_plan():
+    from comm_opt_b200.harness.runner import command, headline_jobs
+
+    jobs = headline_jobs((2, 4, 8))
+    assert len(jobs) == 3 * 5 + 3  # per GPU count: sweep, boundary, 3 decode forms; 3 extra batches at 8
+    cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
+    assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3
+    assert all(("bench.py" in c) != (" -m comm_opt_b200" in c.split("torch.distributed.run")[1]) for c in cmds)
+    assert sum("ref_m16nf" in c for c in cmds) == 1
+
+
 def test_collective_loader_and_bound(tmp_path):
     from comm_opt_b200.harness.collective_analysis import achievable_us, fit_bound, load_run, summarize
     from comm_opt_b200.utils.stats import disjoint
