@@ -26,6 +26,8 @@ ENTRY = {
     "bakeoff": "comm_opt_b200.harness.allreduce_bakeoff",
     "phases": "comm_opt_b200.harness.phase_profile",
     "boundary": "comm_opt_b200.harness.boundary_bench",
+    "comm_share": "comm_opt_b200.harness.comm_share",
+    "train_share": "comm_opt_b200.harness.train_share",
     "bench": "bench.py",  # a script at the repository root, not a module
 }
 
@@ -74,6 +76,8 @@ def command(job: Job, out: Path, port: int) -> tuple[list[str], dict]:
         cmd += ["--out-dir", str(out / "runs"), "--ts", job.tag]
     elif job.entry in ("bakeoff", "phases", "boundary"):
         cmd += ["--out-dir", str(out / "runs")]
+    elif job.entry in ("comm_share", "train_share"):
+        cmd += ["--out-dir", str(out / "runs" / job.tag)]  # one trace set per job
     elif job.entry == "bench":
         cmd += ["--gpus", str(job.ngpus), "--out", str(out / f"{job.tag}.json")]
     return cmd, env
@@ -143,6 +147,21 @@ def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
     return jobs
 
 
+def e2e_share_jobs(ngpus: int = 8, reps: int = 3) -> list[Job]:
+    """The reference's M5 matrix (exp/M5_e2e_comm_share/run_train.py:14-16 and run_infer.py): training of
+    Llama-3 1B / 8B at TP 8 / 4 / 2 x FSDP ngpus / TP, 8 x 2048 tokens per step, `reps` launches each; and
+    the communication share of TP decode (70B, batch 1 / 8 / 128, fused and separate layer boundaries)."""
+    jobs = [Job("train_share", ngpus, variant=f"{m}_tp{tp}", rep=r, timeout_s=1800,
+                args=("--model", m, "--tp", str(tp), "--seq", "2048", "--global-seqs", "8", "--steps", "10",
+                      "--profile", "5"))
+            for m in ("1b", "8b") for tp in (8, 4, 2) if tp <= ngpus for r in range(reps)]
+    for B in (1, 8, 128):
+        for fb in (1, 0):
+            jobs.append(Job("comm_share", ngpus, variant=f"70b_b{B}_fb{fb}",
+                            args=("--model", "70b", "--batch", str(B), "--fuse-boundary", str(fb))))
+    return jobs
+
+
 def fused_hidden_jobs(ngpus: int = 8, impls: str = "ours:auto,vllm_car,trt_oneshot") -> list[Job]:
     """The reference's M10 question (exp/M10_why_fused_slow/run.py:24-42): the same message bytes at
     narrower rows. Hidden 8192 / 4096 / 2048 / 1024 with 1x / 2x / 4x / 8x the tokens."""
@@ -157,11 +176,12 @@ if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden", "headline"])
+    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden", "headline", "e2e_share"])
     ap.add_argument("--gpus", default="2,4,8")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args()
     gp = tuple(int(g) for g in a.gpus.split(","))
     jobs = {"collective_baseline": lambda: collective_baseline_jobs(gp), "nccl_variants": lambda: nccl_variant_jobs(max(gp)),
-            "fused_hidden": lambda: fused_hidden_jobs(max(gp)), "headline": lambda: headline_jobs(gp)}[a.plan]()
+            "fused_hidden": lambda: fused_hidden_jobs(max(gp)), "headline": lambda: headline_jobs(gp),
+            "e2e_share": lambda: e2e_share_jobs(max(gp))}[a.plan]()
     print(run_all(jobs, a.plan, a.seed))

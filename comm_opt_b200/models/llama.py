@@ -55,8 +55,9 @@ class LlamaConfig:
 
 LLAMA3_8B = LlamaConfig("llama3-8b", 4096, 32, 32, 8, 128, 14336, 128256)
 LLAMA3_70B = LlamaConfig("llama3-70b", 8192, 80, 64, 8, 128, 28672, 128256)
+LLAMA3_1B = LlamaConfig("llama3-1b", 2048, 16, 32, 8, 64, 8192, 128256)
 TINY = LlamaConfig("tiny", 1024, 2, 16, 8, 128, 2048, 4096)
-PRESETS = {"llama3-8b": LLAMA3_8B, "8b": LLAMA3_8B, "llama3-70b": LLAMA3_70B, "70b": LLAMA3_70B, "tiny": TINY}
+PRESETS = {"llama3-1b": LLAMA3_1B, "1b": LLAMA3_1B, "llama3-8b": LLAMA3_8B, "8b": LLAMA3_8B, "llama3-70b": LLAMA3_70B, "70b": LLAMA3_70B, "tiny": TINY}
 
 
 class LayerWeights:

@@ -131,3 +131,17 @@ def test_report_tables(tmp_path):
                  json.dumps(dict(impl="reference", unavailable="not installable")) + "\n")
     t = render(f)
     assert "| m | 8 | 7.700 | 7.740 | 566 | parallelism=tp8 |" in t and "unavailable: not installable" in t
+
+
+def test_e2e_share_plan():
+    """The M5 matrix: 1B / 8B x TP 8 / 4 / 2 x 3 launches of training, plus the decode comm-share jobs; each
+    job writes its traces into its own directory."""
+    from comm_opt_b200.harness.runner import Job, command, e2e_share_jobs
+
+    jobs = e2e_share_jobs(8)
+    train = [j for j in jobs if j.entry == "train_share"]
+    assert len(train) == 18 and {j.variant for j in train} == {f"{m}_tp{t}" for m in ("1b", "8b") for t in (8, 4, 2)}
+    assert len([j for j in jobs if j.entry == "comm_share"]) == 6
+    cmd, _ = command(Job("train_share", 8, variant="8b_tp4"), ROOT / "results" / "x", 29999)
+    assert cmd[-1].endswith("runs/train_share_g8A_8b_tp4_r0") and "comm_opt_b200.harness.train_share" in cmd
+    assert len(e2e_share_jobs(4, reps=1)) == 4 + 6  # TP 8 needs 8 GPUs
