@@ -263,9 +263,49 @@ void py_prim_probe(std::vector<int64_t> bases, std::vector<int64_t> offs, int64_
   ok(cob::prim_probe(p, (int)blocks, (int)threads, cur()), "prim_probe");
 }
 
+cob::LineProbeParams line_params(const std::vector<int64_t>& bases, int64_t heap_bytes, int64_t lines_off,
+                                 int64_t n_lines, int64_t rank, int64_t target, int64_t mode, int64_t emulate,
+                                 int64_t observer_blocks, int64_t writer_blocks, int64_t epoch, int64_t timeout_ns,
+                                 const torch::Tensor& counters) {
+  COB_CHECK(bases.size() >= 2 && bases.size() <= 8, "world must be 2..8");
+  COB_CHECK(counters.is_cuda() && counters.scalar_type() == torch::kInt64 && counters.numel() >= 5,
+            "counters must be a CUDA int64 tensor of 5 words");
+  COB_CHECK(target >= 0 && target < (int64_t)bases.size(), "target rank out of range");
+  COB_CHECK(lines_off >= 0 && lines_off % 128 == 0 && n_lines >= 1 && lines_off + n_lines * 128 <= heap_bytes,
+            "lines [", lines_off, ", +", n_lines * 128, ") do not fit the ", heap_bytes, "-byte heap (or misaligned)");
+  cob::LineProbeParams p = {};
+  for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
+  p.lines_off = lines_off;
+  p.n_lines = n_lines;
+  p.rank = (int)rank;
+  p.world = (int)bases.size();
+  p.target = (int)target;
+  p.mode = (int)mode;
+  p.emulate = (int)emulate;
+  p.observer_blocks = (int)observer_blocks;
+  p.writer_blocks = (int)writer_blocks;
+  p.epoch = (unsigned int)epoch;
+  p.timeout_ns = (unsigned long long)timeout_ns;
+  p.counters = reinterpret_cast<unsigned long long*>(counters.data_ptr());
+  return p;
+}
+
+void py_line_probe(std::vector<int64_t> bases, int64_t heap_bytes, int64_t lines_off, int64_t n_lines, int64_t rank,
+                   int64_t target, int64_t mode, int64_t emulate, int64_t observer_blocks, int64_t writer_blocks,
+                   int64_t epoch, int64_t timeout_ns, torch::Tensor counters, bool check) {
+  const cob::LineProbeParams p = line_params(bases, heap_bytes, lines_off, n_lines, rank, target, mode, emulate,
+                                             observer_blocks, writer_blocks, epoch, timeout_ns, counters);
+  const c10::cuda::CUDAGuard g(counters.device());
+  if (check)
+    ok(cob::line_check(p, cur()), "line_check");
+  else
+    ok(cob::line_probe(p, cur()), "line_probe");
+}
+
 }  // namespace
 
 void register_ops(pybind11::module& m) {
+  m.def("line_probe", &py_line_probe);
   m.def("prim_layout", &py_prim_layout);
   m.def("prim_probe", &py_prim_probe);
   m.def("rs_atomic_probe", &py_rs_atomic_probe);

@@ -11,7 +11,9 @@
 //     into the peers' landing words, poll own landing). Arrival is per 32-bit word (Lamport sentinel),
 //     not per 128-byte line; launches reuse the buffers without clearing (epoch-parity slots, cleared
 //     on consumption) and the payload is a hash of (rank, index, epoch), so any stale or torn word is
-//     counted.
+//     counted;
+//   * line atomicity (the reference's M8 premise test, exp/M8_ll128_atomic_a100/test_ll128_atomic.cu:24-50,
+//     extended to the store forms that LL128-style protocols rely on), bounded by one deadline.
 #include "common.cuh"
 #include "probes.h"
 
@@ -217,7 +219,190 @@ __global__ void __launch_bounds__(1024) k_prim(const PrimParams p) {
     ep[j] = e;
 }
 
+// ----------------------------------------------------------------------------- line atomicity
+constexpr int kLineThreads = 256;
+
+__device__ __forceinline__ void red_sys_add_u32(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_sys_v4(uint32_t* p, const uint4& v) {
+  asm volatile("st.relaxed.sys.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t ld_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_sys_v4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
+               : "memory");
+  return v;
+}
+
+// expected final word w of line l (store modes: epoch e; atomic mode: W - 1 writers other than target)
+__device__ __forceinline__ uint32_t line_expect(const LineProbeParams& p, long long l, int w) {
+  if (p.mode == kLineAtomic)
+    return w == 31 ? (uint32_t)(p.world - 1) : (uint32_t)(p.world * (p.world + 1) / 2 - (p.target + 1));
+  return w == 31 ? p.epoch : prim_word(w, (int)l, p.epoch);
+}
+
+// writer `widx` (0 .. W-2, the ranks other than the target in order) with `nwb` blocks, this block `wb`
+template <int MODE>
+__device__ void line_write(const LineProbeParams& p, int widx, int wb, int nwb) {
+  uint32_t* lines = reinterpret_cast<uint32_t*>(p.base[p.target] + p.lines_off);
+  const int lane = threadIdx.x & 31;
+  const long long warp = (long long)wb * (kLineThreads / 32) + (threadIdx.x >> 5);
+  const long long nwarps = (long long)nwb * (kLineThreads / 32);
+  const int wrank = widx < p.target ? widx : widx + 1;
+  const int nw = p.world - 1;
+  if (MODE == kLineAtomic) {
+    const uint32_t add = lane == 31 ? 1u : (uint32_t)(wrank + 1);
+    for (long long l = warp; l < p.n_lines; l += nwarps) red_sys_add_u32(lines + l * 32 + lane, add);
+  } else if (MODE == kLineStore4) {
+    // this writer's lines: widx, widx + nw, widx + 2 nw, ...
+    for (long long j = warp;; j += nwarps) {
+      const long long l = widx + j * nw;
+      if (l >= p.n_lines) break;
+      st_sys_u32(lines + l * 32 + lane, line_expect(p, l, lane));
+    }
+  } else {
+    // 8 lanes per line, 4 lines per warp instruction
+    const int sub = lane >> 3, q = lane & 7;
+    for (long long j0 = warp * 4;; j0 += nwarps * 4) {
+      if (widx + j0 * nw >= p.n_lines) break;  // uniform across the warp
+      const long long l = widx + (j0 + sub) * nw;
+      if (l < p.n_lines)
+        st_sys_v4(lines + l * 32 + 4 * q, make_uint4(line_expect(p, l, 4 * q), line_expect(p, l, 4 * q + 1),
+                                                      line_expect(p, l, 4 * q + 2), line_expect(p, l, 4 * q + 3)));
+    }
+  }
+}
+
+template <int MODE>
+__device__ void line_observe(const LineProbeParams& p, int ob, int nob) {
+  const uint32_t* lines = reinterpret_cast<const uint32_t*>(p.base[p.target] + p.lines_off);
+  const int lane = threadIdx.x & 31;
+  const long long warp = (long long)ob * (kLineThreads / 32) + (threadIdx.x >> 5);
+  const long long nwarps = (long long)nob * (kLineThreads / 32);
+  const uint32_t want_flag = line_expect(p, 0, 31);
+  unsigned long long viol = 0, raced = 0, tmo = 0, seen = 0;
+  const uint64_t t0 = globaltimer();
+  bool expired = false;
+  for (long long l = warp; l < p.n_lines; l += nwarps) {
+    if (expired) {
+      ++tmo;  // not read: the deadline passed
+      continue;
+    }
+    for (uint32_t spin = 0;; ++spin) {
+      bool bad = false;
+      uint32_t flag;
+      if (MODE == kLineStore16) {
+        // one 16-byte load per lane covers the line with lanes 0..7 (lanes 8..31 re-read it)
+        const uint4 v = ld_sys_v4(lines + l * 32 + 4 * (lane & 7));
+        flag = __shfl_sync(0xffffffffu, v.w, 7);
+        const int w = 4 * (lane & 7);
+        bad = v.x != line_expect(p, l, w) || v.y != line_expect(p, l, w + 1) || v.z != line_expect(p, l, w + 2) ||
+              (w + 3 != 31 && v.w != line_expect(p, l, w + 3));
+      } else {
+        const uint32_t v = ld_sys_u32(lines + l * 32 + lane);
+        flag = __shfl_sync(0xffffffffu, v, 31);
+        bad = lane != 31 && v != line_expect(p, l, lane);
+      }
+      if (flag == want_flag) {  // flag comes from one lane: the branch is uniform
+        if (__any_sync(0xffffffffu, bad)) ++viol;
+        if (spin) ++raced;
+        ++seen;
+        break;
+      }
+      if ((spin & 63u) == 63u) {
+        const int late = (lane == 0) && (globaltimer() - t0 > p.timeout_ns);
+        if (__shfl_sync(0xffffffffu, late, 0)) {
+          expired = true;
+          ++tmo;
+          break;
+        }
+      }
+    }
+  }
+  if (lane == 0) {
+    if (viol) atomicAdd(p.counters + 0, viol);
+    if (raced) atomicAdd(p.counters + 1, raced);
+    if (tmo) atomicAdd(p.counters + 2, tmo);
+    if (seen) atomicAdd(p.counters + 3, seen);
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kLineThreads) k_line(const LineProbeParams p) {
+  int b = blockIdx.x;
+  if (p.emulate) {
+    if (b < p.observer_blocks) {
+      line_observe<MODE>(p, b, p.observer_blocks);
+    } else {
+      b -= p.observer_blocks;
+      line_write<MODE>(p, b / p.writer_blocks, b % p.writer_blocks, p.writer_blocks);
+    }
+  } else if (p.rank == p.target) {
+    line_observe<MODE>(p, b, p.observer_blocks);
+  } else {
+    line_write<MODE>(p, p.rank < p.target ? p.rank : p.rank - 1, b, p.writer_blocks);
+  }
+}
+
+__global__ void __launch_bounds__(kLineThreads) k_line_check(const LineProbeParams p) {
+  const uint32_t* lines = reinterpret_cast<const uint32_t*>(p.base[p.target] + p.lines_off);
+  const int lane = threadIdx.x & 31;
+  const long long warp = (long long)blockIdx.x * (kLineThreads / 32) + (threadIdx.x >> 5);
+  const long long nwarps = (long long)gridDim.x * (kLineThreads / 32);
+  unsigned long long bad = 0;
+  for (long long l = warp; l < p.n_lines; l += nwarps)
+    bad += __any_sync(0xffffffffu, ld_sys_u32(lines + l * 32 + lane) != line_expect(p, l, lane)) ? 1 : 0;
+  if (lane == 0 && bad) atomicAdd(p.counters + 4, bad);
+}
+
 }  // namespace
+
+cudaError_t line_probe(const LineProbeParams& p, cudaStream_t s) {
+  if (p.world < 2 || p.world > 8 || p.target < 0 || p.target >= p.world || p.mode < 0 || p.mode > 2)
+    return cudaErrorInvalidValue;
+  if (p.n_lines < 1 || p.n_lines > (1LL << 24) || p.lines_off < 0 || p.lines_off % 128) return cudaErrorInvalidValue;
+  if (p.observer_blocks < 1 || p.observer_blocks > 1024 || p.writer_blocks < 1 || p.writer_blocks > 4096)
+    return cudaErrorInvalidValue;
+  if (p.mode != kLineAtomic && p.epoch == 0) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(p.base[p.target]) % 16 || !p.counters) return cudaErrorInvalidValue;
+  if (!p.emulate && (p.rank < 0 || p.rank >= p.world)) return cudaErrorInvalidValue;
+  void (*k)(const LineProbeParams) = p.mode == kLineAtomic ? k_line<kLineAtomic>
+                                     : p.mode == kLineStore4 ? k_line<kLineStore4> : k_line<kLineStore16>;
+  int blocks = 0;
+  if (p.emulate) {
+    blocks = p.observer_blocks + (p.world - 1) * p.writer_blocks;
+    // the observer spins on lines written by other blocks of this launch: all must be resident
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kLineThreads, 0);
+    if (e != cudaSuccess) return e;
+    if ((long long)blocks > (long long)sms * per_sm) return cudaErrorInvalidValue;
+  } else {
+    blocks = p.rank == p.target ? p.observer_blocks : p.writer_blocks;
+  }
+  k<<<blocks, kLineThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t line_check(const LineProbeParams& p, cudaStream_t s) {
+  if (p.world < 2 || p.world > 8 || p.target < 0 || p.target >= p.world || p.n_lines < 1 || p.n_lines > (1LL << 24) ||
+      p.lines_off % 128 || !p.counters || (p.mode != kLineAtomic && p.epoch == 0))
+    return cudaErrorInvalidValue;
+  const long long want = (p.n_lines + kLineThreads / 32 - 1) / (kLineThreads / 32);
+  k_line_check<<<(int)(want < 1184 ? want : 1184), kLineThreads, 0, s>>>(p);
+  return cudaGetLastError();
+}
 
 size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off) {
   auto up = [](long long v) { return (v + 4095) / 4096 * 4096; };

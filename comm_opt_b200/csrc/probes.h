@@ -37,6 +37,34 @@ struct PrimParams {
 };
 size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off);
 cudaError_t prim_probe(const PrimParams& p, int blocks, int threads, cudaStream_t s);
+// Line-atomicity probe (the premise behind LL128-style flag-in-line protocols): writer ranks hit every
+// 128-byte line (32 u32 words; word 31 is the line's flag) of the target rank's buffer with one warp-wide
+// operation per line while the target's observer warps read each line with one warp-wide load and
+// count lines whose flag says "complete" but whose other words do not.
+//   mode 0: every writer adds to all 32 words (red.relaxed.sys.add.u32; flag += 1, data += rank + 1);
+//           complete = flag == number of writers, data must then equal the sum of (rank + 1).
+//   mode 1: one writer per line stores 32 x 4 bytes (flag = epoch, data = hash(word, line, epoch)).
+//   mode 2: one writer per line stores 8 x 16 bytes (4 lines per warp instruction), same contents.
+// Store modes run in steady state (the buffer is never cleared; the epoch grows per launch), so data
+// of the previous launch under a new flag is a violation. Writers never wait; the observer gives up
+// at one deadline for the whole launch and counts the lines it did not reach as timeouts.
+// counters (u64, target rank's device memory): [0] violations [1] lines seen in progress before they
+// completed [2] timeouts [3] lines observed complete [4] lines wrong after the launch (check kernel).
+enum LineMode : int { kLineAtomic = 0, kLineStore4 = 1, kLineStore16 = 2 };
+struct LineProbeParams {
+  char* base[8];
+  long long lines_off;  // byte offset of the lines in the target's heap (multiple of 128)
+  long long n_lines;
+  int rank, world, target, mode, emulate;
+  int observer_blocks, writer_blocks;  // blocks of the target's observer / of every writer rank
+  unsigned int epoch;                  // store modes: this launch's flag value (>= 1)
+  unsigned long long timeout_ns;
+  unsigned long long* counters;
+};
+// Runs this rank's role (emulate: every role in one launch, which must be co-resident on this GPU).
+cudaError_t line_probe(const LineProbeParams& p, cudaStream_t s);
+// Counts lines of the target's buffer that differ from their final expected contents into counters[4].
+cudaError_t line_check(const LineProbeParams& p, cudaStream_t s);
 // out[0] = SM cycles, out[1] = %globaltimer nanoseconds over a spin of `ns` nanoseconds
 cudaError_t clock_calibration(unsigned long long ns, long long* out, cudaStream_t s);
 

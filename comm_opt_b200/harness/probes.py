@@ -1,5 +1,6 @@
 """Primitive probes: reduce-scatter by remote atomics (four `red` forms), push vs pull all-gather /
-reduce-scatter primitives in steady state, and SM clock calibration.
+reduce-scatter primitives in steady state, the 128-byte line-atomicity premise test (`--line`), and SM
+clock calibration.
 
     python -m comm_opt_b200.harness.probes --emulate 8                 (all ranks on one GPU)
     timeout -k 60 600 python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 \
@@ -161,11 +162,82 @@ def run_prim(world: int, n: int, mode: int, dev, emulate: bool, blocks: int = 64
                 calls=3 + graph_ops * (replays + 1))
 
 
+LINE_MODES = {0: "atomic_add", 1: "store_4B", 2: "store_16B"}
+
+
+def run_line(world: int, n_lines: int, mode: int, dev, emulate: bool, runs: int = 3, observer_blocks: int = 0,
+             writer_blocks: int = 0, group=None, cpu_group=None, timeout_ms: float = 2000.0) -> dict:
+    """Line-atomicity premise test (the reference's M8, exp/M8_ll128_atomic_a100/test_ll128_atomic.cu): rank 0
+    observes its own buffer of n_lines 128-byte lines while ranks 1..W-1 write them over NVLink (emulate:
+    every role as blocks of one launch on one GPU, L2 instead of NVLink). A violation is a line whose flag
+    word says complete while another word does not match; `raced` counts lines the observer saw before they
+    completed (with none, the run shows nothing either way). Store modes run `runs` launches on the same
+    buffer with growing epochs; the atomic mode clears it before each launch."""
+    C = native()
+    target = 0
+    rank = 0 if emulate else dist.get_rank(group)
+    nbytes = n_lines * 128
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    if emulate:
+        ob = observer_blocks or 16
+        wb = writer_blocks or max(1, (sms - ob) // (world - 1))
+        heap = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        bases = [heap.data_ptr()] * world
+    else:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        ob, wb = observer_blocks or sms, writer_blocks or 2 * sms
+        heap = symm_mem.empty(nbytes, dtype=torch.uint8, device=dev)
+        heap.zero_()
+        bases = list(symm_mem.rendezvous(heap, group or dist.group.WORLD).buffer_ptrs)
+    counters = torch.zeros(5, dtype=torch.int64, device=dev)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if not emulate:
+            dist.barrier(group=cpu_group)  # host-only: an NCCL barrier would queue behind the observer
+
+    rows = []
+    for r in range(1, runs + 1):
+        if mode == 0 and rank == target:
+            heap.zero_()
+        counters.zero_()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        C.line_probe(bases, nbytes, 0, n_lines, rank, target, mode, int(emulate), ob, wb, r, int(timeout_ms * 1e6),
+                     counters, False)
+        b.record()
+        barrier()
+        if rank == target:
+            C.line_probe(bases, nbytes, 0, n_lines, rank, target, mode, int(emulate), ob, wb, r, 0, counters, True)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) if (emulate or rank != target) else 0.0
+        vals = counters.cpu().tolist() + [ms]
+        if not emulate:
+            t = torch.tensor(vals, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=cpu_group)  # counters live on the target only
+            vals = t.tolist()
+        viol, raced, tmo, seen, final_bad, ms = vals
+        per_writer = nbytes if mode == 0 else nbytes / (world - 1)
+        rows.append(dict(run=r, violations=int(viol), raced_lines=int(raced), timeouts=int(tmo), observed=int(seen),
+                         final_bad_lines=int(final_bad), writer_ms=round(ms, 3),
+                         gbs_per_writer=round(per_writer / (ms * 1e-3) / 1e9, 1) if ms > 0 else None))
+    del heap
+    return dict(mode=LINE_MODES[mode], world=world, emulated=emulate, lines=n_lines, observer_blocks=ob,
+                writer_blocks=wb, runs=rows, violations=sum(x["violations"] for x in rows),
+                raced_lines=sum(x["raced_lines"] for x in rows), timeouts=sum(x["timeouts"] for x in rows),
+                final_bad_lines=sum(x["final_bad_lines"] for x in rows))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--emulate", type=int, default=0, help="run W ranks in one launch on one GPU")
     ap.add_argument("--sizes", default="10240,81920,655360")
     ap.add_argument("--prim", action="store_true", help="push vs pull primitives instead of the atomic RS probe")
+    ap.add_argument("--line", action="store_true", help="line-atomicity premise test instead of the atomic RS probe")
+    ap.add_argument("--lines", type=int, default=1 << 20, help="--line: 128-byte lines in the observed buffer")
+    ap.add_argument("--runs", type=int, default=3)
     ap.add_argument("--out", default=None)
     a = ap.parse_args()
     rows = []
@@ -179,7 +251,14 @@ def main():
         torch.cuda.set_device(dev)
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         world, rank = dist.get_world_size(), dist.get_rank()
-    for n in [int(s) for s in a.sizes.split(",")]:
+    if a.line:
+        cpu_group = None if a.emulate else dist.new_group(backend="gloo")
+        for mode in LINE_MODES:
+            r = run_line(world, a.lines, mode, dev, bool(a.emulate), runs=a.runs, cpu_group=cpu_group)
+            rows.append(r)
+            if rank == 0:
+                print(json.dumps(r), flush=True)
+    for n in ([] if a.line else [int(s) for s in a.sizes.split(",")]):
         for v in (PRIM_MODES if a.prim else VARIANTS):
             n_w = n // (4 * world) * 4 * world if a.prim else n
             r = run_prim(world, n_w, v, dev, bool(a.emulate)) if a.prim else run_rs(world, n, v, dev, bool(a.emulate))

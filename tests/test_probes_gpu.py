@@ -31,3 +31,16 @@ def test_push_pull_primitives_steady_state(cuda, world, mode):
                  timeout_ms=100)
     assert r["bad_words"] == 0 and not r["timeout"], r
     assert r["us"] > 0
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_line_atomicity_probe_emulated(cuda, world, mode):
+    """Observer and writers as blocks of one launch: every line observed complete, none timed out, and the
+    buffer holds exactly the expected final contents after each launch (store modes: two launches on the
+    same buffer, the second under a new epoch). Violations are a measurement, not asserted."""
+    from comm_opt_b200.harness.probes import run_line
+
+    r = run_line(world, 1 << 14, mode, cuda, emulate=True, runs=2, timeout_ms=1000)
+    assert r["timeouts"] == 0 and r["final_bad_lines"] == 0, r
+    assert all(x["observed"] == 1 << 14 for x in r["runs"]), r
