@@ -10,7 +10,9 @@ Per implementation and token count (message = tokens x hidden x 2 bytes, 16 KB -
   2. timing: 5 eager calls, K calls captured in one CUDA graph, 3 warm replays, then R replays each
      bracketed by CUDA events; per-op time = replay time / K; for every replay the MAX over ranks
      is taken; p50 / p99 / mean over replays are reported (the reference kept only means).
-Implementation order is shuffled with a recorded seed; a 2 s matmul warm-up brings clocks up first.
+Implementation order is shuffled with a recorded seed; a 2 s matmul warm-up brings clocks up first, and
+the first (implementation, size) pair is measured twice with the first copy dropped (the reference's
+discard-first rule, exp/M19_small_batch/bench_m19.py:249-252; `--discard-first 0` turns it off).
 Results: results/<exp>/<timestamp>/ with env.txt, schedule.tsv, sweep.json (rank 0).
 """
 from __future__ import annotations
@@ -65,6 +67,8 @@ def main():
     ap.add_argument("--eps", type=float, default=1e-6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--warm-s", type=float, default=2.0)
+    ap.add_argument("--discard-first", type=int, choices=[0, 1], default=1,
+                    help="measure the first (impl, tokens) config twice and drop the first copy")
     ap.add_argument("--exp", default="fused_sweep")
     ap.add_argument("--out-dir", default=None, help="base directory of results/ (default: repo results/)")
     ap.add_argument("--ts", default=None)
@@ -93,79 +97,84 @@ def main():
     random.Random(a.seed).shuffle(order)
     warm_gpu(a.warm_s, dev)
     rows, n = [], 0
-    for impl in order:
-        for T in tokens:
-            t_start, state = time.time(), gpu_state() if rank == 0 else ""
-            reason = impl.available(T, H)
-            reasons = [None] * world
-            dist.all_gather_object(reasons, reason, group=cpu_group)
-            reason = next((r for r in reasons if r), "")
-            err, rel, times = "", float("nan"), []
-            if not reason:
-                try:
-                    # ---- correctness on fresh inputs
-                    x, res0 = inputs(T, H, DT, dev, a.seed + T, rank)
-                    ref_out, ref_h = dist_fused_allreduce_add_rmsnorm_ref(x, res0, gamma, a.eps)
-                    res = res0.clone()
-                    fn = impl.make(x.clone(), res, gamma, a.eps)
-                    torch.cuda.synchronize()
-                    dist.barrier(group=cpu_group)
-                    out = fn()
-                    torch.cuda.synchronize()
-                    rel = rel_err(out, ref_out)
-                    if impl.residual_rows == "all":
-                        rel = max(rel, rel_err(res, ref_h))
-                    else:  # rows owned by this rank (the reference keeps the residual sharded)
-                        rp = -(-T // world)
-                        r0, r1 = min(T, rank * rp), min(T, (rank + 1) * rp)
-                        if r1 > r0:
-                            rel = max(rel, rel_err(res[r0:r1], ref_h[r0:r1]))
-                    # ---- timing under graph replay
-                    x, res = inputs(T, H, DT, dev, a.seed + T + 1, rank)
-                    fn = impl.make(x, res, gamma, a.eps)
-                    for _ in range(5):
-                        fn()
-                    torch.cuda.synchronize()
-                    dist.barrier(group=cpu_group)
-                    g = torch.cuda.CUDAGraph()
-                    with impl.capture_ctx():
-                        with torch.cuda.graph(g):
-                            for _ in range(a.graph_ops):
-                                fn()
-                    for _ in range(3):
-                        g.replay()
-                    torch.cuda.synchronize()
-                    dist.barrier(group=cpu_group)
-                    ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.replays + 1)]
-                    ev[0].record()
-                    for i in range(a.replays):
-                        g.replay()
-                        ev[i + 1].record()
-                    torch.cuda.synchronize()
-                    times = [ev[i].elapsed_time(ev[i + 1]) * 1000.0 / a.graph_ops for i in range(a.replays)]
-                    del g
-                    if hasattr(comm, "check") and impl.name.startswith("ours"):
-                        comm.check()
-                except Exception as e:  # recorded per row; other rows continue
-                    err = f"{type(e).__name__}: {str(e)[:200]}"
-            gathered = [None] * world
-            dist.all_gather_object(gathered, (times, rel, err), group=cpu_group)
-            if rank == 0:
-                per_replay = [max(g[0][i] for g in gathered) for i in range(a.replays)] if all(
-                    len(g[0]) == a.replays for g in gathered) else []
-                worst = max((g[1] for g in gathered if g[1] == g[1]), default=float("nan"))
-                errs = next((g[2] for g in gathered if g[2]), "")
-                s = summary(per_replay) if per_replay else {}
-                row = dict(impl=impl.name, world=world, dtype=a.dtype, hidden=H, tokens=T, bytes=T * H * DT.itemsize,
-                           p50_us=s.get("p50"), p99_us=s.get("p99"), mean_us=s.get("mean"),
-                           per_rank_p50=[summary(g[0])["p50"] if g[0] else None for g in gathered],
-                           max_rel_err=worst, correct=bool(worst == worst and worst <= TOL), skip=reason, error=errs,
-                           variant=(comm.last_choice.__dict__ if impl.name.startswith("ours") and comm.last_choice else None))
+    plan = [(impl, T, False) for impl in order for T in tokens]
+    if a.discard_first and plan:
+        plan.insert(0, (plan[0][0], plan[0][1], True))  # first config measured twice, first copy dropped
+    for impl, T, discard in plan:
+        t_start, state = time.time(), gpu_state() if rank == 0 else ""
+        reason = impl.available(T, H)
+        reasons = [None] * world
+        dist.all_gather_object(reasons, reason, group=cpu_group)
+        reason = next((r for r in reasons if r), "")
+        err, rel, times = "", float("nan"), []
+        if not reason:
+            try:
+                # ---- correctness on fresh inputs
+                x, res0 = inputs(T, H, DT, dev, a.seed + T, rank)
+                ref_out, ref_h = dist_fused_allreduce_add_rmsnorm_ref(x, res0, gamma, a.eps)
+                res = res0.clone()
+                fn = impl.make(x.clone(), res, gamma, a.eps)
+                torch.cuda.synchronize()
+                dist.barrier(group=cpu_group)
+                out = fn()
+                torch.cuda.synchronize()
+                rel = rel_err(out, ref_out)
+                if impl.residual_rows == "all":
+                    rel = max(rel, rel_err(res, ref_h))
+                else:  # rows owned by this rank (the reference keeps the residual sharded)
+                    rp = -(-T // world)
+                    r0, r1 = min(T, rank * rp), min(T, (rank + 1) * rp)
+                    if r1 > r0:
+                        rel = max(rel, rel_err(res[r0:r1], ref_h[r0:r1]))
+                # ---- timing under graph replay
+                x, res = inputs(T, H, DT, dev, a.seed + T + 1, rank)
+                fn = impl.make(x, res, gamma, a.eps)
+                for _ in range(5):
+                    fn()
+                torch.cuda.synchronize()
+                dist.barrier(group=cpu_group)
+                g = torch.cuda.CUDAGraph()
+                with impl.capture_ctx():
+                    with torch.cuda.graph(g):
+                        for _ in range(a.graph_ops):
+                            fn()
+                for _ in range(3):
+                    g.replay()
+                torch.cuda.synchronize()
+                dist.barrier(group=cpu_group)
+                ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.replays + 1)]
+                ev[0].record()
+                for i in range(a.replays):
+                    g.replay()
+                    ev[i + 1].record()
+                torch.cuda.synchronize()
+                times = [ev[i].elapsed_time(ev[i + 1]) * 1000.0 / a.graph_ops for i in range(a.replays)]
+                del g
+                if hasattr(comm, "check") and impl.name.startswith("ours"):
+                    comm.check()
+            except Exception as e:  # recorded per row; other rows continue
+                err = f"{type(e).__name__}: {str(e)[:200]}"
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (times, rel, err), group=cpu_group)
+        if rank == 0:
+            per_replay = [max(g[0][i] for g in gathered) for i in range(a.replays)] if all(
+                len(g[0]) == a.replays for g in gathered) else []
+            worst = max((g[1] for g in gathered if g[1] == g[1]), default=float("nan"))
+            errs = next((g[2] for g in gathered if g[2]), "")
+            s = summary(per_replay) if per_replay else {}
+            row = dict(impl=impl.name, world=world, dtype=a.dtype, hidden=H, tokens=T, bytes=T * H * DT.itemsize,
+                       p50_us=s.get("p50"), p99_us=s.get("p99"), mean_us=s.get("mean"),
+                       per_rank_p50=[summary(g[0])["p50"] if g[0] else None for g in gathered],
+                       max_rel_err=worst, correct=bool(worst == worst and worst <= TOL), skip=reason, error=errs,
+                       variant=(comm.last_choice.__dict__ if impl.name.startswith("ours") and comm.last_choice else None))
+            if not discard:
                 rows.append(row)
-                print(f"{impl.name:16s} w{world} T{T:4d} {row['bytes'] >> 10:6d}KB p50 {row['p50_us'] or float('nan'):8.2f} us "
-                      f"p99 {row['p99_us'] or float('nan'):8.2f} err {worst:.1e} {reason or errs}", flush=True)
-                run.schedule(n, f"{impl.name}_T{T}", t_start, time.time() - t_start, 0 if not errs else 1, state)
-                n += 1
+            print(f"{impl.name:16s} w{world} T{T:4d} {row['bytes'] >> 10:6d}KB p50 {row['p50_us'] or float('nan'):8.2f} us "
+                  f"p99 {row['p99_us'] or float('nan'):8.2f} err {worst:.1e} {reason or errs}"
+                  f"{' (discarded)' if discard else ''}", flush=True)
+            run.schedule(n, f"{impl.name}_T{T}" + ("_discard" if discard else ""), t_start, time.time() - t_start,
+                         0 if not errs else 1, state)
+            n += 1
     if rank == 0:
         run.write_json("sweep.json", dict(args=vars(a), world=world, order=[i.name for i in order], skipped=skipped,
                                           comm=comm.describe(), rows=rows))
