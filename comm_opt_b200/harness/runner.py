@@ -128,7 +128,7 @@ def nccl_variant_jobs(ngpus: int = 8) -> list[Job]:
 
 def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
     """Every headline measurement of the project as independent jobs: the fused-op sweep against all
-    baselines, the layer-boundary bench, and the TP decode (fused / separate boundaries / NCCL baseline
+    baselines (hidden 8192 bf16, and the reference's fp16 hidden 5120), the layer-boundary bench, and the TP decode (fused / separate boundaries / NCCL baseline
     step) at each GPU count, plus the 70B decode batch sweep at 8 GPUs."""
     sweep_impls = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_1s,ours:nvls_2s,nccl_norm,vllm_car,"
                    "trt_oneshot,trt_twoshot")
@@ -136,6 +136,10 @@ def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
     for g in gpus:
         jobs.append(Job("fused_sweep", g, args=("--impls", sweep_impls + (",ref_m16nf" if g == 8 else ""),
                                                 "--replays", "20")))
+        # the reference's own quoting configuration: fp16, hidden 5120, 10 KB - 1.25 MB
+        jobs.append(Job("fused_sweep", g, variant="h5120_fp16",
+                        args=("--impls", sweep_impls + (",ref_m16nf" if g == 8 else ""), "--hidden", "5120",
+                              "--dtype", "float16", "--tokens", "1,2,4,8,16,32,64,128", "--replays", "20")))
         jobs.append(Job("boundary", g))
         for variant, extra in (("fused", ()), ("separate", ("--fuse-boundary", "0")),
                                ("nccl", ("--collective", "nccl"))):

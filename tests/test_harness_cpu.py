@@ -37,11 +37,12 @@ def test_runner_headline_plan():
     from comm_opt_b200.harness.runner import command, headline_jobs
 
     jobs = headline_jobs((2, 4, 8))
-    assert len(jobs) == 3 * 5 + 3  # per GPU count: sweep, boundary, 3 decode forms; 3 extra batches at 8
+    assert len(jobs) == 3 * 6 + 3  # per GPU count: 2 sweeps, boundary, 3 decode forms; 3 extra batches at 8
     cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
     assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3
     assert all(("bench.py" in c) != (" -m comm_opt_b200" in c.split("torch.distributed.run")[1]) for c in cmds)
-    assert sum("ref_m16nf" in c for c in cmds) == 1
+    assert sum("ref_m16nf" in c for c in cmds) == 2  # both sweeps at 8 GPUs
+    assert sum("--hidden 5120 --dtype float16" in c for c in cmds) == 3
 
 
 def test_collective_loader_and_bound(tmp_path):
