@@ -72,6 +72,10 @@ def command(job: Job, out: Path, port: int) -> tuple[list[str], dict]:
            f"--nproc-per-node={job.ngpus}", "--master-addr=127.0.0.1", f"--master-port={port}", *target, *job.args]
     if job.entry == "collectives":
         cmd += ["--out", str(out / f"{job.tag}.json")]
+        # NCCL's set-up (version, channels, NVLS, rings) per job, init-time only (no per-call logging)
+        for k, v in (("NCCL_DEBUG", "INFO"), ("NCCL_DEBUG_SUBSYS", "INIT,ENV,GRAPH"),
+                     ("NCCL_DEBUG_FILE", str(out / f"{job.tag}.nccl.%h.%p.log"))):
+            env.setdefault(k, v)  # a job's own setting (or the caller's environment) wins
     elif job.entry == "fused_sweep":
         cmd += ["--out-dir", str(out / "runs"), "--ts", job.tag]
     elif job.entry in ("bakeoff", "phases", "boundary"):
@@ -107,7 +111,8 @@ def run_all(jobs: list[Job], name: str, seed: int, base: Path | None = None) -> 
         cmd, env = command(j, run.path, 29700 + i % 100)
         with open(run.path / f"{j.tag}.log", "w") as log:
             rc = subprocess.run(cmd, stdout=log, stderr=subprocess.STDOUT, env=env, cwd=ROOT).returncode
-        run.schedule(i, j.tag, t0, time.time() - t0, rc, state, env=j.env, variant=j.variant, ngpus=j.ngpus)
+        run.schedule(i, j.tag, t0, time.time() - t0, rc, state, env=j.env, variant=j.variant, ngpus=j.ngpus,
+                     gpuset=j.gpuset, rep=j.rep)
         print(f"[{i + 1}/{len(jobs)}] {j.tag} rc={rc} {time.time() - t0:.1f}s", file=sys.stderr, flush=True)
     return run.path
 
@@ -124,6 +129,33 @@ def nccl_variant_jobs(ngpus: int = 8) -> list[Job]:
                 "ll128": {"NCCL_PROTO": "LL128"}, "ring": {"NCCL_ALGO": "Ring"}, "tree": {"NCCL_ALGO": "Tree"}}
     return [Job("collectives", ngpus, variant=k, env=v, args=("--colls", "all_reduce", "--begin", "1K", "--end", "8M",
                                                                "--graph", "20")) for k, v in variants.items()]
+
+
+def repeat_jobs(reps: int = 5) -> list[Job]:
+    """The reference's M4 study (exp/M4_repeat/run.py:14-26): the collective baseline's notable points
+    repeated in independent launches on two GPU sets, so that a phenomenon counts only when the [min, max]
+    intervals of both sets agree. (collective, GPU counts, size range)."""
+    plan = [("sendrecv", (2, 4, 8), "4M", "256M"), ("alltoall", (2, 8), "64M", "4G"),
+            ("all_gather", (2, 8), "1M", "4G"), ("reduce_scatter", (2, 8), "1M", "4G"),
+            ("all_reduce", (2, 8), "1M", "4G"), ("broadcast", (2, 8), "1M", "2G")]
+    return [Job("collectives", g, gpuset=gs, rep=r, variant=c,
+                args=("--colls", c, "--begin", lo, "--end", hi))
+            for c, gs_counts, lo, hi in plan for g in gs_counts for gs in ("A", "B") for r in range(reps)]
+
+
+def p2p_channel_jobs(reps: int = 5) -> list[Job]:
+    """The reference's M2 study (exp/M2_p2p_channels/run.py:14-30) on NCCL's P2P knobs: point-to-point and
+    all-to-all from 1 MB to 1 GB at 8 GPUs with more P2P channels and smaller NVLink chunks, and the same
+    chunk sizes at 2 GPUs (does a smaller chunk hurt the 2-GPU case)."""
+    variants = {"default": {}, "minp2p64": {"NCCL_MIN_P2P_NCHANNELS": "64"},
+                "chunk128k": {"NCCL_P2P_NVL_CHUNKSIZE": "131072"}, "chunk64k": {"NCCL_P2P_NVL_CHUNKSIZE": "65536"},
+                "minp2p64_chunk128k": {"NCCL_MIN_P2P_NCHANNELS": "64", "NCCL_P2P_NVL_CHUNKSIZE": "131072"}}
+    jobs = [Job("collectives", 8, rep=r, variant=f"{c}_{v}", env=e, args=("--colls", c, "--begin", "1M", "--end", "1G"))
+            for v, e in variants.items() for c in ("sendrecv", "alltoall") for r in range(reps)]
+    jobs += [Job("collectives", 2, rep=r, variant=f"sendrecv_{v}", env=variants[v],
+                 args=("--colls", "sendrecv", "--begin", "1M", "--end", "1G"))
+             for v in ("default", "chunk128k", "chunk64k") for r in range(reps)]
+    return jobs
 
 
 def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
@@ -180,12 +212,14 @@ if __name__ == "__main__":
     import argparse
 
     ap = argparse.ArgumentParser()
-    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden", "headline", "e2e_share"])
+    ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden", "headline", "e2e_share",
+                                     "repeat", "p2p_channels"])
     ap.add_argument("--gpus", default="2,4,8")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args()
     gp = tuple(int(g) for g in a.gpus.split(","))
     jobs = {"collective_baseline": lambda: collective_baseline_jobs(gp), "nccl_variants": lambda: nccl_variant_jobs(max(gp)),
             "fused_hidden": lambda: fused_hidden_jobs(max(gp)), "headline": lambda: headline_jobs(gp),
-            "e2e_share": lambda: e2e_share_jobs(max(gp))}[a.plan]()
+            "e2e_share": lambda: e2e_share_jobs(max(gp)), "repeat": repeat_jobs,
+            "p2p_channels": p2p_channel_jobs}[a.plan]()
     print(run_all(jobs, a.plan, a.seed))

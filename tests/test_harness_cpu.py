@@ -146,3 +146,49 @@ def test_e2e_share_plan():
     cmd, _ = command(Job("train_share", 8, variant="8b_tp4"), ROOT / "results" / "x", 29999)
     assert cmd[-1].endswith("runs/train_share_g8A_8b_tp4_r0") and "comm_opt_b200.harness.train_share" in cmd
     assert len(e2e_share_jobs(4, reps=1)) == 4 + 6  # TP 8 needs 8 GPUs
+
+
+def test_nccl_log_summary_and_gpuset_comparison(tmp_path):
+    """NCCL's set-up read from an INIT / ENV / GRAPH log, attached to every row of the job; sets A and B
+    compared per point over repeated launches."""
+    from comm_opt_b200.harness.collective_analysis import compare_gpusets, load_run, nccl_log_summary
+
+    log = ("h:1:1 [0] NCCL INFO NCCL version 2.28.9+cuda12.9\n"
+           "h:1:1 [0] NCCL INFO NCCL_P2P_NVL_CHUNKSIZE set by environment to 131072\n"
+           "h:1:1 [0] NCCL INFO comm 0x1 rank 0 nRanks 8 nNodes 1 localRanks 8 localRank 0 MNNVL 0\n"
+           + "".join(f"h:1:1 [0] NCCL INFO Channel {c:02d}/24 :    0   1   2   3   4   5   6   7\n" for c in range(24))
+           + "h:1:1 [0] NCCL INFO NVLS multicast support is available on dev 0 (NVLS_NCHANNELS 16)\n"
+           "h:1:1 [0] NCCL INFO 24 coll channels, 24 collnet channels, 16 nvls channels, 32 p2p channels, "
+           "32 p2p channels per peer\n")
+    s = nccl_log_summary(log)
+    assert s == dict(nccl_version="2.28.9+cuda12.9", nranks=8, coll_channels=24, nvls_channels=16, p2p_channels=32,
+                     p2p_channels_per_peer=32, rings=24, nvls=True, env={"NCCL_P2P_NVL_CHUNKSIZE": "131072"})
+    assert nccl_log_summary("nothing here") == {}
+    from comm_opt_b200.utils.results import RunDir
+
+    run = RunDir("repeat", tmp_path, "t")
+    for i, (gs, rep) in enumerate((g, r) for g in "AB" for r in range(3)):
+        tag = f"collectives_g8{gs}_all_reduce_r{rep}"
+        bw = (100.0 if gs == "A" else 104.0) + rep
+        (run.path / f"{tag}.json").write_text(json.dumps(dict(results=[
+            dict(coll="all_reduce", world=8, size=1 << 20, busbw=bw, p50_us=10.0)])))
+        run.schedule(i, tag, 0.0, 1.0, 0, "", variant="all_reduce", gpuset=gs, rep=rep)
+        if i == 0:
+            (run.path / f"{tag}.nccl.h.1.log").write_text(log)
+    rows = load_run(run.path)
+    assert len(rows) == 6 and rows[0]["nccl"]["coll_channels"] == 24 and rows[1]["nccl"] == {}
+    (c,) = compare_gpusets(rows)
+    assert c["a"]["med"] == 101.0 and c["b"]["med"] == 105.0 and c["disjoint"] and abs(c["rel_diff"] - 4 / 101) < 1e-12
+
+
+def test_repeat_and_p2p_channel_plans():
+    from comm_opt_b200.harness.runner import Job, command, p2p_channel_jobs, repeat_jobs
+
+    rj = repeat_jobs(5)
+    assert len(rj) == (3 + 2 * 5) * 2 * 5 and {j.gpuset for j in rj} == {"A", "B"}
+    pj = p2p_channel_jobs(5)
+    assert len(pj) == 5 * 2 * 5 + 3 * 5
+    assert any(j.env.get("NCCL_MIN_P2P_NCHANNELS") == "64" for j in pj)
+    cmd, env = command(Job("collectives", 8, env={"NCCL_DEBUG": "WARN"}), ROOT / "results" / "x", 29999)
+    assert env["NCCL_DEBUG"] == "WARN" and env["NCCL_DEBUG_SUBSYS"] == "INIT,ENV,GRAPH"
+    assert env["NCCL_DEBUG_FILE"].endswith("collectives_g8A_default_r0.nccl.%h.%p.log")
