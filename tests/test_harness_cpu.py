@@ -192,3 +192,33 @@ def test_repeat_and_p2p_channel_plans():
     cmd, env = command(Job("collectives", 8, env={"NCCL_DEBUG": "WARN"}), ROOT / "results" / "x", 29999)
     assert env["NCCL_DEBUG"] == "WARN" and env["NCCL_DEBUG_SUBSYS"] == "INIT,ENV,GRAPH"
     assert env["NCCL_DEBUG_FILE"].endswith("collectives_g8A_default_r0.nccl.%h.%p.log")
+
+
+def test_figures_from_runs(tmp_path):
+    """SVG + CSV figures of a fused sweep, a layer-boundary run and a training share summary land in
+    figures/<exp>/<ts>/ and are well-formed XML."""
+    import xml.dom.minidom
+
+    from comm_opt_b200.harness.figures import render
+
+    def run(exp, name, doc):
+        d = tmp_path / "results" / exp / "20260101_000000"
+        d.mkdir(parents=True)
+        (d / name).write_text(json.dumps(doc))
+        return d
+
+    sweep = dict(world=8, rows=[dict(impl=i, world=8, dtype="bfloat16", hidden=8192, tokens=t, bytes=t * 16384,
+                                     p50_us=v * t ** 0.5, correct=True) for i, v in (("ours", 8.0), ("nccl", 29.0))
+                                for t in (1, 4, 16, 64)])
+    bnd = dict(world=8, rows=[dict(impl=i, batch=B, p50_us=v, correct=True, error="", roofline_us=12.2)
+                              for B in (1, 8) for i, v in (("fused", 27.0), ("split", 34.0))])
+    share = dict(model="llama3-8b", world=8, tp=4, dp=2, step_ms=700.0, tokens_per_s=23000.0,
+                 breakdown=dict(compute_pct=68.0, hidden_cost_pct=3.0, transfer_pct=14.0, other_pct=15.0))
+    for exp, name, doc, files in (("fused_sweep", "sweep.json", sweep, ("per_op.csv", "latency.svg")),
+                                  ("boundary_bench", "boundary.json", bnd, ("boundary.csv", "boundary.svg")),
+                                  ("train_share", "summary.json", share, ("share.csv", "share.svg"))):
+        out = render(run(exp, name, doc), base=tmp_path)
+        assert [p.name for p in out] == list(files)
+        assert out[0].parent == tmp_path / "figures" / exp / "20260101_000000"
+        xml.dom.minidom.parse(str(out[1]))
+        assert len(out[0].read_text().splitlines()) >= 2
