@@ -200,12 +200,17 @@ def e2e_share_jobs(ngpus: int = 8, reps: int = 3) -> list[Job]:
 
 def fused_hidden_jobs(ngpus: int = 8, impls: str = "ours:auto,vllm_car,trt_oneshot") -> list[Job]:
     """The reference's M10 question (exp/M10_why_fused_slow/run.py:24-42): the same message bytes at
-    narrower rows. Hidden 8192 / 4096 / 2048 / 1024 with 1x / 2x / 4x / 8x the tokens."""
+    narrower rows (hidden 8192 / 4096 / 2048 / 1024 with 1x / 2x / 4x / 8x the tokens), and its register-limit
+    check: hidden 6400 / 6656, where the TRT-LLM fused kernel stopped launching on A100."""
     base = (1, 2, 4, 8, 16, 32, 64)
-    return [Job("fused_sweep", ngpus, variant=f"h{8192 // k}",
+    jobs = [Job("fused_sweep", ngpus, variant=f"h{8192 // k}",
                 args=("--hidden", str(8192 // k), "--tokens", ",".join(str(t * k) for t in base), "--impls", impls,
                       "--replays", "20"))
             for k in (1, 2, 4, 8)]
+    jobs += [Job("fused_sweep", ngpus, variant=f"h{h}", args=("--hidden", str(h), "--tokens", ",".join(map(str, base)),
+                                                              "--impls", impls, "--replays", "20"))
+             for h in (6400, 6656)]
+    return jobs
 
 
 if __name__ == "__main__":
