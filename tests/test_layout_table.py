@@ -110,7 +110,7 @@ def test_fused_ar_geometry_rules():
             L = C.plan_layout(world, 512, 8192 if dtype else 4096, esz[dtype], 4096)
             for emulate in (0, 1):
                 budget = 148 // (world if emulate else 1)
-                for hidden in (1024, 2048, 4096, 5120, 8192):
+                for hidden in (1024, 2048, 4096, 5120, 6400, 6656, 8192):
                     hv = hidden * esz[dtype] // 16
                     if hv > L[14]:
                         continue
