@@ -129,7 +129,8 @@ def run(a, rank: int, world: int, device: torch.device) -> dict | None:
                    global_seqs=a.global_seqs, tokens_per_step=tokens, step_ms=step_ms,
                    tokens_per_s=tokens / (step_ms * 1e-3), tflops_per_gpu=flops / world / 1e12,
                    mfu_of_measured=(flops / world / 1e12 / peak) if (peak and cuda) else None,
-                   loss_first=losses[0], loss_last=losses[-1], remat=bool(a.remat), device=device.type,
+                   loss_first=losses[0], loss_last=losses[-1], tokens_seen=tr.tokens_seen, remat=bool(a.remat),
+                   device=device.type,
                    peak_mem_gb=(torch.cuda.max_memory_allocated(device) / 2**30) if cuda else None,
                    data="synthetic (random token ids, random init)")
     if a.profile > 0:

@@ -15,6 +15,7 @@ Layout per rank: dp = world / tp data-parallel groups of tp ranks; mesh dims ("d
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 
@@ -173,12 +174,13 @@ class TrainConfig:
 class Trainer:
     """One optimizer step per `step(tokens, labels)`: forward, loss, backward, gradient-norm clip, AdamW."""
 
-    def __init__(self, cfg: LlamaConfig, tc: TrainConfig, device: torch.device, group=None):
+    def __init__(self, cfg: LlamaConfig, tc: TrainConfig, device: torch.device):
+        """Builds the (dp, tp) mesh over the default process group (or runs unsharded without one)."""
         import torch.distributed as dist
 
         self.cfg, self.tc, self.device = cfg, tc, torch.device(device)
-        world = dist.get_world_size(group) if dist.is_initialized() else 1
-        rank = dist.get_rank(group) if dist.is_initialized() else 0
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        rank = dist.get_rank() if dist.is_initialized() else 0
         assert world % tc.tp == 0, f"world {world} not divisible by tp {tc.tp}"
         self.world, self.rank, self.tp, self.dp = world, rank, tc.tp, world // tc.tp
         cfg.shard(tc.tp)  # raises when heads / kv heads / intermediate / vocab do not split tp ways
@@ -226,7 +228,7 @@ class Trainer:
         self.model = model
         self.opt = torch.optim.AdamW(model.parameters(), lr=tc.lr, betas=(0.9, 0.95), weight_decay=0.1,
                                      foreach=True)
-        self.tokens_seen = 0
+        self._tokens = torch.zeros((), dtype=torch.int64, device=self.device)
 
     def clip_(self) -> torch.Tensor:
         params = [p for p in self.model.parameters() if p.grad is not None]
@@ -241,11 +243,14 @@ class Trainer:
         Returns the (rank-local) loss as a device tensor; nothing here synchronizes with the host."""
         import torch.distributed as dist
 
-        if self.tc.count_tokens and self.world > 1:
-            n = torch.tensor([labels.numel()], dtype=torch.int64, device=self.device)
-            dist.all_reduce(n)
-            self._ntok = n  # read lazily: no host sync inside the step
-        ctx = torch.autocast("cuda", dtype=torch.bfloat16) if (self.mp and self.dp == 1) else _null()
+        if self.tc.count_tokens:
+            n = torch.full((), labels.numel(), dtype=torch.int64, device=self.device)
+            if self.world > 1:
+                dist.all_reduce(n)  # every data-parallel group's tokens, once per TP rank of the group
+                n = n // self.tp
+            self._tokens += n  # stays on the device: no host sync inside the step
+        # without FSDP's mixed-precision policy (dp == 1) bf16 compute comes from autocast
+        ctx = torch.autocast("cuda", dtype=torch.bfloat16) if (self.mp and self.dp == 1) else contextlib.nullcontext()
         with ctx:
             logits = self.model(tokens)
         if self.loss_parallel:
@@ -262,16 +267,13 @@ class Trainer:
         self.opt.zero_grad(set_to_none=True)
         return loss.detach()
 
+    @property
+    def tokens_seen(self) -> int:
+        """Tokens trained on so far over all data-parallel ranks (reads the device counter)."""
+        return int(self._tokens)
+
     def local_shapes(self) -> dict:
         return {n: tuple((p.to_local() if hasattr(p, "to_local") else p).shape) for n, p in self.model.named_parameters()}
-
-
-class _null:
-    def __enter__(self):
-        return None
-
-    def __exit__(self, *a):
-        return False
 
 
 def synthetic_batch(cfg: LlamaConfig, batch: int, seq: int, step: int, dp_rank: int, pin: bool = False):

@@ -67,6 +67,7 @@ def _share(rank, world, out_dir):
     if rank == 0:
         assert s["tp"] == 2 and s["dp"] == 1 and s["step_ms"] > 0 and s["tokens_per_step"] == 64
         assert s["breakdown"]["n_steps"] == 1 and torch.isfinite(torch.tensor(s["loss_last"]))
+        assert s["tokens_seen"] == 3 * 2 * 32  # warm-up + timed + profiled steps x 2 sequences x 32 tokens
 
 
 def test_train_share_driver_gloo(tmp_path):
