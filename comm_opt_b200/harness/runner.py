@@ -161,7 +161,8 @@ def p2p_channel_jobs(reps: int = 5) -> list[Job]:
 def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
     """Every headline measurement of the project as independent jobs: the fused-op sweep against all
     baselines (hidden 8192 bf16, and the reference's fp16 hidden 5120), the layer-boundary bench, and the TP decode (fused / separate boundaries / NCCL baseline
-    step) at each GPU count, plus the 70B decode batch sweep at 8 GPUs."""
+    step) at each GPU count, the 70B decode batch sweep at 8 GPUs, and the 8B decode (prompt 1024, batch
+    1 / 8 / 64) against the NCCL step at each GPU count."""
     sweep_impls = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_1s,ours:nvls_2s,nccl_norm,vllm_car,"
                    "trt_oneshot,trt_twoshot")
     jobs = []
@@ -180,6 +181,13 @@ def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
         if B != 8:
             jobs.append(Job("bench", max(gpus), variant=f"b{B}", args=("--steps", "32", "--warmup", "3",
                                                                        "--batch", str(B))))
+    # Llama-3-8B shapes at every GPU count: prompt 1024, batch 1 / 8 / 64, ours and the NCCL step
+    for g in gpus:
+        for B in (1, 8, 64):
+            for variant, extra in (("8b", ()), ("8b_nccl", ("--collective", "nccl"))):
+                jobs.append(Job("bench", g, variant=f"{variant}_b{B}",
+                                args=("--model", "8b", "--prompt", "1024", "--batch", str(B), "--steps", "64",
+                                      "--warmup", "4", *extra)))
     return jobs
 
 

@@ -29,7 +29,7 @@ def test_runner_dry_run_prints_commands():
     p = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stderr
     lines = [l for l in p.stdout.splitlines() if "torch.distributed.run" in l]
-    assert len(lines) == 2 + 6 + 4 and all("127.0.0.1" in l and "timeout" in l for l in lines)
+    assert len(lines) == 2 + 6 + 6 and all("127.0.0.1" in l and "timeout" in l for l in lines)
     assert sum("--hidden 1024" in l and "--tokens 8,16,32" in l for l in lines) == 1
 
 
@@ -37,9 +37,11 @@ def test_runner_headline_plan():
     from comm_opt_b200.harness.runner import command, headline_jobs
 
     jobs = headline_jobs((2, 4, 8))
-    assert len(jobs) == 3 * 6 + 3  # per GPU count: 2 sweeps, boundary, 3 decode forms; 3 extra batches at 8
+    # per GPU count: 2 sweeps, boundary, 3 decode forms, 8B x 3 batches x 2 collectives; 3 extra 70B batches at 8
+    assert len(jobs) == 3 * (6 + 6) + 3
     cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
-    assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3
+    assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3 + 9
+    assert sum("--model 8b --prompt 1024" in c for c in cmds) == 18
     assert all(("bench.py" in c) != (" -m comm_opt_b200" in c.split("torch.distributed.run")[1]) for c in cmds)
     assert sum("ref_m16nf" in c for c in cmds) == 2  # both sweeps at 8 GPUs
     assert sum("--hidden 5120 --dtype float16" in c for c in cmds) == 3
