@@ -14,6 +14,9 @@ Parts:
   fault      - fault injection on the host: one rank skips a call, the others' bounded waits run out,
                they report TPCommTimeout, every rank calls reset() and the next calls are correct.
                Uses the CUDA-IPC heap (never bound to a multicast object) and plain peer loads.
+  leave      - a rank leaves between steps (nothing in flight) and posts it in the store; the others stop
+               before their next launch (RankMonitor.sync), no bounded wait runs out. Use the CUDA-IPC
+               heap's environment (NCCL_NVLS_ENABLE=0), as for `fault`.
   stress     - fused calls and layer boundaries checked call by call while a side stream runs large
                GEMMs on every SM (memory-ordering stress under concurrent compute).
   decode     - tiny Llama-shaped model at TP = world vs the unsharded fp32 forward (logits), and
@@ -199,6 +202,41 @@ def fault(C: Checker, dev, world):
     comm.close()
 
 
+def leave(C: Checker, dev, world, steps: int = 6, leave_at: int = 2):
+    """A rank leaves the TP group between steps, with none of its kernels in flight: it posts its departure
+    in the store instead of reaching the next step; the others learn of it in RankMonitor.sync() before
+    they launch that step, so no kernel waits on the departed rank. Every rank then stays for the final
+    host-side result exchange. CUDA-IPC heap, plain peer loads (no multicast object involved)."""
+    from ..parallel.health import RankFailure, RankMonitor
+
+    comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=16, max_hidden=4096,
+                          timeout_ms=1000, backend="ipc")
+    mon = RankMonitor.from_default_group(prefix="selftest/leave", stale_s=60)
+    mon.wait_joined(60)
+    x, res0, gamma = inputs(4, 4096, torch.bfloat16, dev, seed=11)
+    ref_out, _ = dist_fused_allreduce_add_rmsnorm_ref(x, res0, gamma, 1e-6)
+    leaver, done, reason = world - 1, 0, ""
+    for step in range(steps):
+        if dist.get_rank() == leaver and step == leave_at:
+            torch.cuda.synchronize()
+            mon.leave()
+            break
+        try:
+            mon.sync(60)
+        except RankFailure as e:
+            reason = str(e)
+            break
+        out, _ = comm.fused_allreduce_add_rmsnorm(x, res0.clone(), gamma, 1e-6, variant="lamport_1s")
+        torch.cuda.synchronize()
+        C.check(rel_err(out, ref_out) <= TOL, f"leave: step {step} result")
+        done += 1
+    C.check(done == leave_at, f"leave: rank stopped after {done} steps, expected {leave_at}")
+    if dist.get_rank() != leaver:
+        C.check("left the group" in reason, f"leave: departure not reported ({reason!r})")
+    comm.check()  # no bounded wait ran out: nobody launched a call the leaver would not join
+    comm.close()  # host-side teardown; every process, the leaver's too, is still alive
+
+
 def stress(C: Checker, dev, world, calls: int = 120):
     """Memory-ordering stress: fused calls (variants and sizes in a seeded random order, the same on
     every rank) and layer boundaries while a side stream keeps the SMs busy with large GEMMs. Every call
@@ -323,7 +361,7 @@ def main():
     t0 = time.time()
     try:
         for part in a.parts.split(","):
-            {"functional": functional, "fault": fault, "decode": decode_check, "stress": stress,
+            {"functional": functional, "fault": fault, "leave": leave, "decode": decode_check, "stress": stress,
              "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True),
              "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True),
              "decode_nccl": lambda C, dev, world: decode_check(C, dev, world, collective="nccl")
