@@ -461,9 +461,15 @@ class TPDecodeRunner:
             self._step(B, buf)
         return buf["ids"]
 
-    def decode(self, B: int, host_ids: torch.Tensor, host_out: torch.Tensor) -> torch.Tensor:
+    def decode(self, B: int, host_ids: torch.Tensor, host_out: torch.Tensor, monitor=None,
+               sync_timeout_s: float = 60.0) -> torch.Tensor:
         """One end-to-end greedy step through the public API: copy this step's input token ids from
-        pinned host memory, run the captured step, read the next ids back into pinned host memory."""
+        pinned host memory, run the captured step, read the next ids back into pinned host memory.
+        With a `parallel.health.RankMonitor`, every rank first meets the others at the step boundary on
+        the host (RankFailure if a peer failed, left or is late), so no kernel is launched that waits for
+        a rank that is gone; without one, nothing is added to the step."""
+        if monitor is not None:
+            monitor.sync(sync_timeout_s)
         g, buf = self.graphs[B]
         buf["ids"].copy_(host_ids, non_blocking=True)
         if g is not None:
