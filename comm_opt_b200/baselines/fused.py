@@ -105,6 +105,7 @@ class NcclNorm(Impl):
             self.C = _vllm_ops()
         except Exception:  # pragma: no cover - vLLM missing: the norm falls back to this package's kernel
             self.C = None
+            self.name = "nccl_cobnorm"  # rows say which norm kernel the baseline ran
 
     def make(self, x, residual, gamma, eps):
         C, group = self.C, self.group

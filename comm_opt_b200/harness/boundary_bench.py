@@ -207,7 +207,9 @@ def main():
                 n_job += 1
     if rank == 0:
         run.write_json("boundary.json", dict(args=vars(a), world=world, hbm_gbs=hbm_gbs(), peer_gbs=PEER_GBS,
-                                             comm=comm.describe(), rows=rows))
+                                             comm=comm.describe(), rows=rows,
+                                             baseline_norm="vllm fused_add_rms_norm" if vops is not None
+                                             else "torch add + rms_norm (vLLM missing)"))
         print(json.dumps(dict(results=str(run.path))), flush=True)
     if car is not None:
         car.close()
