@@ -74,6 +74,35 @@ def repeats(rows: list[dict], ours: str, base: str) -> list[dict]:
     return out
 
 
+def expected_tx_bytes(impl: str, msg: int, world: int) -> float | None:
+    """Bytes one rank sends over NVLink per call, by algorithm (flags and row sums left out):
+    one-shot push or pull, (W - 1) S (every peer gets, or reads, the whole message); two-shot
+    reduce-scatter + all-gather, 2 (W - 1) / W S; NVSwitch multicast one-shot, W S (every rank's
+    ld_reduce reads every GPU's copy through the switch); multicast two-shot, S + S / W (each slice read
+    once, the reduced slice stored once for the switch to replicate). None for an unknown algorithm
+    (NCCL picks its own)."""
+    name = impl.split(":", 1)[-1]
+    one, two = (world - 1) * msg, 2 * (world - 1) / world * msg
+    return {"lamport_1s": one, "pull_1s": one, "trt_oneshot": one, "lamport_2s": two, "pull_2s": two,
+            "trt_twoshot": two, "ref_m16nf": two, "nvls_1s": world * msg, "nvls_2s": msg + msg / world}.get(name)
+
+
+def link_table(rows: list[dict]) -> str:
+    """Measured NVLink bytes sent per call (max over ranks, NVML counters) against the algorithm's bytes."""
+    out = ["| impl | world | tokens | KB | measured tx KB/op | expected KB/op | ratio |", "|---|---|---|---|---|---|---|"]
+    for r in sorted(rows, key=lambda r: (r["impl"], r["world"], r["tokens"])):
+        got = r.get("nvlink_tx_bytes_per_op")
+        if got is None or not r.get("correct"):
+            continue
+        exp = expected_tx_bytes(r["impl"] if r["impl"] != "ours:auto" else
+                                "ours:" + next((k for k, v in VARIANTS.items()
+                                                if v == (r.get("variant") or {}).get("variant")), "?"),
+                                r["bytes"], r["world"])
+        out.append(f"| {r['impl']} | {r['world']} | {r['tokens']} | {r['bytes'] >> 10} | {got / 1024:.1f} | "
+                   + (f"{exp / 1024:.1f} | {got / exp:.2f} |" if exp else "- | - |"))
+    return "\n".join(out)
+
+
 def calibrate(rows: list[dict], table_path: Path | None = None) -> VariantTable:
     """Fastest correct variant (with its geometry) per (world, dtype, hidden, rows bucket)."""
     import torch
@@ -97,6 +126,7 @@ def main():
     ap.add_argument("sweeps", nargs="+")
     ap.add_argument("--calibrate", action="store_true", help="update the committed variant table")
     ap.add_argument("--table", default=None)
+    ap.add_argument("--nvlink", action="store_true", help="measured vs expected NVLink bytes per call")
     ap.add_argument("--repeats", nargs=2, metavar=("OURS", "BASELINE"),
                     help="median [min, max] over the given sweeps (independent launches) and the effectiveness rule")
     a = ap.parse_args()
@@ -109,6 +139,9 @@ def main():
             print(f"| {r['world']} | {r['tokens']} | {o['med']:.2f} [{o['lo']:.2f}, {o['hi']:.2f}] (n={o['n']}) | "
                   f"{b['med']:.2f} [{b['lo']:.2f}, {b['hi']:.2f}] (n={b['n']}) | {100 * r['gain']:+.1f}% | "
                   f"{'yes' if r['effective'] else 'no'} |")
+        return
+    if a.nvlink:
+        print(link_table(rows))
         return
     text, _ = table(rows)
     print(text)

@@ -18,6 +18,7 @@ Results: results/<exp>/<timestamp>/ with env.txt, schedule.tsv, sweep.json (rank
 from __future__ import annotations
 
 import argparse
+import contextlib
 import datetime
 import json
 import os
@@ -67,6 +68,8 @@ def main():
     ap.add_argument("--eps", type=float, default=1e-6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--warm-s", type=float, default=2.0)
+    ap.add_argument("--nvlink", type=int, choices=[0, 1], default=1,
+                    help="NVLink bytes per op from NVML's throughput counters around the timed replays")
     ap.add_argument("--discard-first", type=int, choices=[0, 1], default=1,
                     help="measure the first (impl, tokens) config twice and drop the first copy")
     ap.add_argument("--exp", default="fused_sweep")
@@ -95,6 +98,16 @@ def main():
     gamma = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(7))).to(DT).to(dev)
     order = list(impls)
     random.Random(a.seed).shuffle(order)
+    ctr = None
+    if a.nvlink:
+        try:
+            from ..utils.nvlink import NvlinkCounters
+
+            ctr = NvlinkCounters(torch.cuda.current_device())
+            ctr = ctr if ctr.available else None
+        except Exception as e:  # NVML missing or no NVLink: rows carry no byte counts
+            print(f"rank {rank}: NVLink counters unavailable ({type(e).__name__}: {e})", flush=True)
+            ctr = None
     warm_gpu(a.warm_s, dev)
     rows, n = [], 0
     plan = [(impl, T, False) for impl in order for T in tokens]
@@ -106,7 +119,7 @@ def main():
         reasons = [None] * world
         dist.all_gather_object(reasons, reason, group=cpu_group)
         reason = next((r for r in reasons if r), "")
-        err, rel, times = "", float("nan"), []
+        err, rel, times, link = "", float("nan"), [], {}
         if not reason:
             try:
                 # ---- correctness on fresh inputs
@@ -143,11 +156,12 @@ def main():
                 torch.cuda.synchronize()
                 dist.barrier(group=cpu_group)
                 ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.replays + 1)]
-                ev[0].record()
-                for i in range(a.replays):
-                    g.replay()
-                    ev[i + 1].record()
-                torch.cuda.synchronize()
+                with (ctr.measure() if ctr else contextlib.nullcontext({})) as link:
+                    ev[0].record()
+                    for i in range(a.replays):
+                        g.replay()
+                        ev[i + 1].record()
+                    torch.cuda.synchronize()
                 times = [ev[i].elapsed_time(ev[i + 1]) * 1000.0 / a.graph_ops for i in range(a.replays)]
                 del g
                 if hasattr(comm, "check") and impl.name.startswith("ours"):
@@ -155,7 +169,7 @@ def main():
             except Exception as e:  # recorded per row; other rows continue
                 err = f"{type(e).__name__}: {str(e)[:200]}"
         gathered = [None] * world
-        dist.all_gather_object(gathered, (times, rel, err), group=cpu_group)
+        dist.all_gather_object(gathered, (times, rel, err, link), group=cpu_group)
         if rank == 0:
             per_replay = [max(g[0][i] for g in gathered) for i in range(a.replays)] if all(
                 len(g[0]) == a.replays for g in gathered) else []
@@ -167,6 +181,10 @@ def main():
                        per_rank_p50=[summary(g[0])["p50"] if g[0] else None for g in gathered],
                        max_rel_err=worst, correct=bool(worst == worst and worst <= TOL), skip=reason, error=errs,
                        variant=(comm.last_choice.__dict__ if impl.name.startswith("ours") and comm.last_choice else None))
+            ops = a.replays * a.graph_ops
+            if all(g[3].get("tx_bytes") is not None for g in gathered):
+                row["nvlink_tx_bytes_per_op"] = max(g[3]["tx_bytes"] for g in gathered) / ops
+                row["nvlink_rx_bytes_per_op"] = max(g[3]["rx_bytes"] for g in gathered) / ops
             if not discard:
                 rows.append(row)
             print(f"{impl.name:16s} w{world} T{T:4d} {row['bytes'] >> 10:6d}KB p50 {row['p50_us'] or float('nan'):8.2f} us "

@@ -224,3 +224,68 @@ def test_figures_from_runs(tmp_path):
         assert out[0].parent == tmp_path / "figures" / exp / "20260101_000000"
         xml.dom.minidom.parse(str(out[1]))
         assert len(out[0].read_text().splitlines()) >= 2
+
+
+def test_nvlink_counters_against_fake_nvml():
+    """NVLink byte deltas from NVML's per-link throughput counters (KiB), read-only, on a fake NVML:
+    absent links skipped, a link whose read fails reported, only enabled links summed."""
+    import types
+
+    from comm_opt_b200.utils.nvlink import NvlinkCounters
+
+    class FakeNVML:
+        NVML_NVLINK_MAX_LINKS = 4
+        NVML_FEATURE_ENABLED = 1
+        NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_TX = 138
+        NVML_FI_DEV_NVLINK_THROUGHPUT_DATA_RX = 139
+
+        class NVMLError(Exception):
+            pass
+
+        def __init__(self):
+            self.kib = {0: [100, 50], 1: [200, 70], 2: [0, 0]}  # link -> [tx, rx]
+            self.calls = []
+
+        def nvmlInit(self):
+            pass
+
+        def nvmlDeviceGetHandleByIndex(self, i):
+            return ("gpu", i)
+
+        def nvmlDeviceGetNvLinkState(self, h, link):
+            if link == 3:
+                raise self.NVMLError("not present")
+            return 1 if link in (0, 1, 2) else 0
+
+        def nvmlDeviceGetFieldValues(self, h, req):
+            self.calls.append(list(req))
+            out = []
+            for f, link in req:
+                ok = 0 if link != 2 else 3  # link 2's counter cannot be read
+                val = self.kib[link][0 if f == 138 else 1]
+                out.append(types.SimpleNamespace(nvmlReturn=ok, value=types.SimpleNamespace(ullVal=val)))
+            return out
+
+    nv = FakeNVML()
+    ctr = NvlinkCounters(0, nvml=nv)
+    assert ctr.links == [0, 1, 2] and ctr.available
+    assert ctr.read() == dict(tx_kib=300, rx_kib=120, failed_links=[2])
+    with ctr.measure(settle_s=0) as m:
+        nv.kib[0][0] += 7 * 16  # 7 peers x 16 KiB sent on link 0
+        nv.kib[1][1] += 3
+    assert m["tx_bytes"] == 112 * 1024 and m["rx_bytes"] == 3 * 1024 and m["links"] == 3 and m["failed_links"] == [2]
+    assert all(f in (138, 139) for f, _ in nv.calls[0])  # only counter reads were issued
+
+
+def test_expected_nvlink_bytes_and_link_table():
+    from comm_opt_b200.harness.analyze_sweep import expected_tx_bytes, link_table
+
+    S = 16384
+    assert expected_tx_bytes("ours:lamport_1s", S, 8) == 7 * S
+    assert expected_tx_bytes("ours:lamport_2s", S, 8) == 2 * 7 / 8 * S
+    assert expected_tx_bytes("trt_oneshot", S, 4) == 3 * S and expected_tx_bytes("nccl_norm", S, 8) is None
+    rows = [dict(impl="ours:auto", world=8, tokens=1, bytes=S, correct=True, nvlink_tx_bytes_per_op=7.1 * S,
+                 variant=dict(variant=1)),
+            dict(impl="nccl_norm", world=8, tokens=1, bytes=S, correct=True, nvlink_tx_bytes_per_op=2.0 * S)]
+    t = link_table(rows)
+    assert "| ours:auto | 8 | 1 | 16 | 113.6 | 112.0 | 1.01 |" in t and "| nccl_norm | 8 | 1 | 16 | 32.0 | - | - |" in t
