@@ -4,7 +4,9 @@ decode engine could use instead, timed identically inside CUDA graphs.
 Capability of the reference's M6 bench (exp/M6_allreduce_bakeoff/bench_torch.py:21-122: torch NCCL,
 vLLM custom all-reduce, PyTorch SymmetricMemory one-shot / two-shot; 1 KB - 8 MB; K all-reduces per
 graph; error against an fp32 all-reduce of the same inputs), plus SymmetricMemory's NVSwitch multicast
-forms (multimem one-shot and multimem all-reduce), which the reference's A100 system could not run. Per (implementation, size): one eager call
+forms (multimem one-shot and multimem all-reduce), which the reference's A100 system could not run, and
+NCCL timed eagerly as well as in graphs (`torch_nccl@eager`; the reference's "NCCL eager" column,
+exp/M6_allreduce_bakeoff/README.md:93-101). Per (implementation, size): one eager call
 on seeded inputs checked against the fp32 sum, then 5 eager calls, K calls captured in one graph,
 3 warm replays and R timed replays; the per-op time of a replay is its time / K, the MAX over ranks is
 taken per replay, and p50 / p99 / mean over replays are reported (the reference reported the mean of
@@ -31,8 +33,9 @@ from ..parallel import TPCommunicator
 from ..utils.results import RunDir, gpu_state
 from ..utils.stats import summary
 
-DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_2s,torch_nccl,vllm_car,symm_one_shot,"
-                 "symm_two_shot,symm_multimem,symm_multimem_one_shot")
+DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:nvls_2s,torch_nccl,torch_nccl@eager,vllm_car,"
+                 "symm_one_shot,symm_two_shot,symm_multimem,symm_multimem_one_shot")
+EAGER = "@eager"  # suffix: time K eager calls per replay instead of a graph (the reference's "NCCL eager")
 HIDDEN = 8192
 
 
@@ -71,6 +74,7 @@ class Bakeoff:
                         self.skipped[i] = f"{type(e).__name__}: {str(e)[:200]}"
 
     def available(self, impl: str, nbytes: int) -> str:
+        impl = impl.removesuffix(EAGER)
         if impl in self.skipped:
             return self.skipped[impl]
         if impl == "vllm_car" and not self.car.should_custom_ar(torch.empty(nbytes // self.dt.itemsize, dtype=self.dt,
@@ -90,6 +94,7 @@ class Bakeoff:
 
     def make(self, impl: str, x: torch.Tensor):
         """x: this rank's input (flat). Returns (fn -> result tensor, capture context factory)."""
+        impl = impl.removesuffix(EAGER)
         n = x.numel()
         if impl.startswith("ours:"):
             rows, h = shape_of(n * x.element_size(), x.element_size())
@@ -186,19 +191,26 @@ def main():
                         fn()
                     torch.cuda.synchronize()
                     dist.barrier(group=cpu)
-                    graph = torch.cuda.CUDAGraph()
-                    with ctx():
-                        with torch.cuda.graph(graph):
+                    if impl.endswith(EAGER):  # K eager calls stand in for one graph replay
+                        def replay():
                             for _ in range(a.graph_ops):
                                 fn()
+                        graph = None
+                    else:
+                        graph = torch.cuda.CUDAGraph()
+                        with ctx():
+                            with torch.cuda.graph(graph):
+                                for _ in range(a.graph_ops):
+                                    fn()
+                        replay = graph.replay
                     for _ in range(3):
-                        graph.replay()
+                        replay()
                     torch.cuda.synchronize()
                     dist.barrier(group=cpu)
                     ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.replays + 1)]
                     ev[0].record()
                     for i in range(a.replays):
-                        graph.replay()
+                        replay()
                         ev[i + 1].record()
                     torch.cuda.synchronize()
                     times = [ev[i].elapsed_time(ev[i + 1]) * 1000.0 / a.graph_ops for i in range(a.replays)]
