@@ -5,8 +5,8 @@ The reference has none: its product kernel spins without bound (exp/M17_epoch_ab
 181-183), launches run under a wall-clock `timeout` (exp/M17_epoch_ab/run.py:52), and a mismatched warm-up
 was only caught by NCCL's watchdog (exp/M18_incremental/README.md:52). Here every device wait is already
 bounded (the kernels set an error word that `TPCommunicator.check()` turns into `TPCommTimeout`); this
-module covers what a kernel cannot see: a rank that raised, exited, left or never joined. Such a rank must not leave its peers inside a
-collective or a peer-memory wait, so each rank
+module covers what a kernel cannot see: a rank that raised, exited, left or never joined. Such a rank
+must not leave its peers inside a collective or a peer-memory wait, so each rank
 
   * beats (`beat()`): increments its counter key - no clocks are compared across processes; a peer is
     stale when its counter has not moved for `stale_s` seconds of the observer's own clock;
