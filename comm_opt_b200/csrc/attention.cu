@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     for (int i = 0; i < kWarps * kStages; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
   }
-  pdl_wait();
+  pdl_wait_then_trigger();  // the next kernel (the o_proj GEMM) may start streaming its weights
   const int seq = p.seq_lens[b];
   const int npages = (seq + kBS - 1) / kBS;
   const int pg0 = split * p.pages_per_split, pg1 = min(npages, pg0 + p.pages_per_split);

@@ -253,6 +253,16 @@ __device__ __forceinline__ void mm_red_add_u32(void* mc, uint32_t v) {
 // Programmatic dependent launch. Both are no-ops when the kernel was not launched with PDL.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Wait for the predecessor, then let the successor launch at once. The successor's CTAs become
+// resident beside this kernel's (where resources allow) and run their prologue - barrier set-up,
+// tensor-map prefetch, the first weight tiles of a GEMM - while this kernel works; they touch
+// nothing this kernel reads or writes before their own pdl_wait(), which returns only after this
+// grid has completed. Triggering after (never before) the wait keeps at most two kernels of a
+// stream in flight: when a kernel starts, every kernel before its predecessor has completed.
+__device__ __forceinline__ void pdl_wait_then_trigger() {
+  pdl_wait();
+  pdl_trigger();
+}
 
 // Process-wide switch: launch every kernel with programmatic stream serialization, so consecutive
 // kernels in a stream or CUDA graph overlap launch latency and prologue. Every kernel of this
@@ -289,6 +299,35 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------------------------
+// thread-block cluster primitives (distributed shared memory)
+// ---------------------------------------------------------------------------------------------
+// Cluster barrier split into arrive and wait. The release form orders every earlier memory access of
+// the thread, remote NVLink stores included, so it waits until they are acknowledged; the relaxed
+// form orders nothing and costs only the barrier itself.
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+// Shared-memory address of `p` (this CTA) as seen in CTA `cta` of the cluster.
+__device__ __forceinline__ uint32_t cluster_map(const void* p, int cta) {
+  uint32_t out;
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(a), "r"(cta));
+  return out;
+}
+// 64-bit words of this CTA's shared memory that other CTAs of the cluster poll: relaxed at cluster
+// scope, so a word is seen whole (single-copy atomic) and eventually, without ordering anything else.
+__device__ __forceinline__ void st_cluster_word(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.cluster.shared::cta.u64 [%0], %1;" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))),
+               "l"(v)
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_cluster_word(uint32_t cluster_addr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.cluster.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(cluster_addr) : "memory");
   return v;
 }
 

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(512) k_rmsnorm(const T* __restrict__ x, T* __r
 template <typename T>
 __global__ void k_embedding(const int32_t* __restrict__ ids, const T* __restrict__ table, T* __restrict__ out,
                             int hidden) {
-  pdl_wait();
+  pdl_wait_then_trigger();
   const int row = blockIdx.x;
   const uint4* src = reinterpret_cast<const uint4*>(table + (size_t)ids[row] * hidden);
   uint4* dst = reinterpret_cast<uint4*>(out + (size_t)row * hidden);
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, c
                                                     const int32_t* __restrict__ block_tables, int max_blocks,
                                                     T* __restrict__ q_out, T* __restrict__ k_cache,
                                                     T* __restrict__ v_cache, int nq, int nkv, int D, int bs) {
-  pdl_wait();
+  pdl_wait_then_trigger();
   const int b = blockIdx.x, head = blockIdx.y;
   const int pos = positions[b];
   const int half = D / 2;
@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, c
 template <typename T>
 __global__ void k_silu_mul(const T* __restrict__ gu, T* __restrict__ out, int inter) {
   using V = Vec<T>;
-  pdl_wait();
+  pdl_wait_then_trigger();
   const int b = blockIdx.y;
   const int iv = inter / V::N;
   const uint4* g = reinterpret_cast<const uint4*>(gu + (size_t)b * 2 * inter);
@@ -149,7 +149,7 @@ constexpr int kArgmaxChunk = 2048;
 template <typename T>
 __global__ void __launch_bounds__(256) k_argmax_local(const T* __restrict__ logits, unsigned long long* keys,
                                                       int vocab, int vocab_offset) {
-  pdl_wait();
+  pdl_wait_then_trigger();
   const int row = blockIdx.x;
   const int i0 = blockIdx.y * kArgmaxChunk, i1 = min(vocab, i0 + kArgmaxChunk);
   const T* lr = logits + (size_t)row * vocab;
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(256) k_argmax_local(const T* __restrict__ logi
 __global__ void k_argmax_combine(const unsigned long long* __restrict__ gathered, int32_t* __restrict__ ids, int rows,
                                  int world, int32_t* __restrict__ positions, int32_t* __restrict__ seq_lens,
                                  unsigned long long* __restrict__ local_keys) {
-  pdl_wait();
+  pdl_wait_then_trigger();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
   unsigned long long best = 0ull;

@@ -129,6 +129,48 @@ __device__ __forceinline__ float row_sum(float v, float* scratch, float* s_part,
   return tot;
 }
 
+// Cluster-wide sum with no release-ordered barrier (variant kLamport1SX). Each CTA publishes its
+// block sum as one {f32, tag} word in its own shared memory (slot it % 2, tag it + 1); lane c of warp 0
+// polls CTA c's word with relaxed cluster-scope loads, and the C values are added in CTA order from
+// zero, the same order as row_sum(), so every CTA of the cluster (and every rank) gets bitwise the
+// same total. Nothing here orders the CTA's earlier NVLink pushes or landing restores, so the row
+// sum never waits for them to be acknowledged (a release-ordered cluster barrier does).
+// Slot reuse: a CTA writes row it + 2 into slot it % 2 only after it has read every CTA's row it + 1
+// word, which each CTA publishes only after it has consumed all row-it words; two slots suffice. The
+// words are zeroed (tag 0 = none) before a cluster barrier that every CTA passes before its first
+// poll, so stale shared memory is never accepted. A CTA stops reading its peers' shared memory
+// before it arrives at the final cluster barrier, which its peers pass before they exit.
+__device__ __forceinline__ float row_sum_xch(float v, float* scratch, unsigned long long* s_word, float* s_tot, int it,
+                                             int C, int crank, Waiter& w, RankState* st, uint64_t e, int row) {
+  const float part = block_sum(v, scratch);
+  if (C == 1) return part;
+  const uint32_t tag = (uint32_t)it + 1u;
+  if (threadIdx.x == 0) st_cluster_word(&s_word[it & 1], ((unsigned long long)tag << 32) | __float_as_uint(part));
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float pc = part;
+    if (lane < C && lane != crank) {
+      const uint32_t a = cluster_map(&s_word[it & 1], lane);
+      unsigned long long wd = ld_cluster_word(a);
+      while ((uint32_t)(wd >> 32) != tag) {
+        if (w.expired()) {
+          // phase 4: the row partial of cluster CTA `lane` did not arrive
+          record_error(st, kErrTimeoutPartial, ((uint64_t)kLamport1SX << 32) | 4, (uint64_t)row << 32, lane, e);
+          wd = 0ull;
+          break;
+        }
+        wd = ld_cluster_word(a);
+      }
+      pc = __uint_as_float((uint32_t)wd);
+    }
+    float tot = 0.f;
+    for (int c = 0; c < C; ++c) tot += __shfl_sync(0xffffffffu, pc, c);
+    if (lane == 0) *s_tot = tot;
+  }
+  __syncthreads();
+  return *s_tot;
+}
+
 template <typename T>
 __device__ __forceinline__ void store_norm(const ARParams& p, T* out, T* res, int row, int v, const float* h,
                                            const uint4& hbits, float rstd, const uint4* gamma_v = nullptr) {
@@ -204,7 +246,13 @@ __device__ __forceinline__ bool nvls_barrier(const ARParams& p, int rank, RankSt
 //   PULL   : copy x to stage[parity] -> flag barrier -> read every peer's stage -> sum
 //   NVLS   : copy x to stage[parity] -> multicast barrier -> multimem.ld_reduce -> sum
 // ---------------------------------------------------------------------------------------------
-template <typename T, int W, int MODE>
+// VPT: 16-byte vectors per thread per row chunk (1 when the chunk fits the block, else kVPT), so the
+// common geometries (a row spread over a cluster, one vector per thread) hold one vector's state in
+// registers instead of four.
+// XCH (variant kLamport1SX, MODE == kLamport1S): the row sum crosses the cluster through
+// row_sum_xch(), the landing cells get their sentinel back after the row's outputs are stored, and the
+// final cluster barrier is relaxed; the arithmetic and the result are those of kLamport1S.
+template <typename T, int W, int MODE, int VPT, bool XCH>
 __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   using V = Vec<T>;
   using LP = LamportOf<T>;
@@ -221,6 +269,13 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   const int v0 = crank * chunk, v1 = min(hv, v0 + chunk);
   __shared__ float s_scr[32];
   __shared__ float s_part[2];
+  __shared__ unsigned long long s_word[2];  // XCH: this CTA's {row partial, tag} by row parity
+  __shared__ float s_tot;
+  const bool xcl = XCH && C > 1;
+  if (xcl) {
+    if (tid < 2) s_word[tid] = 0ull;
+    cluster_arrive_release();  // nothing of this kernel is in flight yet; waited for before the first poll
+  }
 
   pdl_wait();
   const uint64_t e = call_epoch(st);
@@ -233,7 +288,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
     for (int row = cl; row < p.rows; row += ncl) {
       const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
 #pragma unroll
-      for (int k = 0; k < kVPT; ++k) {
+      for (int k = 0; k < VPT; ++k) {
         const int v = v0 + tid + k * NT;
         if (v < v1) {
           const uint4 d = LP::clean(ld_nc_v4(xr + v));
@@ -246,7 +301,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
     for (int row = cl; row < p.rows; row += ncl) {
       const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
 #pragma unroll
-      for (int k = 0; k < kVPT; ++k) {
+      for (int k = 0; k < VPT; ++k) {
         const int v = v0 + tid + k * NT;
         if (v < v1) *stage_at(p, rank, slot, row, v) = ld_nc_v4(xr + v);
       }
@@ -266,16 +321,18 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
   }
   stamp(p, rank, e, 1);
   pdl_trigger();
+  if (xcl) cluster_wait();
 
   int it = 0;
+  bool arrived = false;
   for (int row = cl; row < p.rows; row += ncl, ++it) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * p.hidden);
-    float h[kVPT][V::N];
-    uint4 hb[kVPT], rv[kVPT], gv[kVPT];
+    float h[VPT][V::N];
+    uint4 hb[VPT], rv[VPT], gv[VPT];
     float ss = 0.f;
     // residual and gamma do not depend on the peers: request them before waiting for peer data
 #pragma unroll
-    for (int k = 0; k < kVPT; ++k) {
+    for (int k = 0; k < VPT; ++k) {
       const int v = v0 + tid + k * NT;
       if (v < v1 && p.norm) {
         rv[k] = reinterpret_cast<const uint4*>(res + (size_t)row * p.hidden)[v];
@@ -283,7 +340,7 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
       }
     }
 #pragma unroll
-    for (int k = 0; k < kVPT; ++k) {
+    for (int k = 0; k < VPT; ++k) {
       const int v = v0 + tid + k * NT;
       if (v < v1) {
         float a[V::N];
@@ -309,9 +366,11 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
                 ok = false;
               }
             }
+            if (!XCH) {
 #pragma unroll
-            for (int s = 0; s < W; ++s)
-              if (s != rank) st_vol_v4(land1_at(p, rank, slot, s, row, v), LP::fill());
+              for (int s = 0; s < W; ++s)
+                if (s != rank) st_vol_v4(land1_at(p, rank, slot, s, row, v), LP::fill());
+            }
           }
 #pragma unroll
           for (int s = 0; s < W; ++s) {
@@ -335,11 +394,16 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
     }
     float rstd = 0.f;
     if (p.norm) {
-      const float tot = row_sum(ss, s_scr, s_part, it, C);
+      const float tot = XCH ? row_sum_xch(ss, s_scr, s_word, &s_tot, it, C, crank, w, st, e, row)
+                            : row_sum(ss, s_scr, s_part, it, C);
       rstd = rsqrtf(tot / (float)p.hidden + p.eps);
     }
+    if (xcl && row + ncl >= p.rows) {  // last row: this CTA reads no more peer shared memory
+      cluster_arrive_relaxed();
+      arrived = true;
+    }
 #pragma unroll
-    for (int k = 0; k < kVPT; ++k) {
+    for (int k = 0; k < VPT; ++k) {
       const int v = v0 + tid + k * NT;
       if (v < v1) {
         uint4* orow = reinterpret_cast<uint4*>(out + (size_t)row * p.hidden);
@@ -355,9 +419,25 @@ __global__ void __launch_bounds__(512) k_oneshot(const ARParams p) {
         }
       }
     }
+    if (XCH && MODE == kLamport1S) {  // the row's landing cells get their sentinel back
+#pragma unroll
+      for (int k = 0; k < VPT; ++k) {
+        const int v = v0 + tid + k * NT;
+        if (v < v1) {
+#pragma unroll
+          for (int s = 0; s < W; ++s)
+            if (s != rank) st_vol_v4(land1_at(p, rank, slot, s, row, v), LP::fill());
+        }
+      }
+    }
   }
   stamp(p, rank, e, 3);
-  if (C > 1) cg::this_cluster().sync();  // no CTA leaves while a peer CTA may read its shared memory
+  if (xcl) {
+    if (!arrived) cluster_arrive_relaxed();
+    cluster_wait();  // no CTA leaves while a peer CTA may still read its shared memory
+  } else if (C > 1) {
+    cg::this_cluster().sync();  // no CTA leaves while a peer CTA may read its shared memory
+  }
   stamp(p, rank, e, 4);
   finish_call(st, e);
 }
@@ -649,7 +729,7 @@ __global__ void __launch_bounds__(1024) k_allgather_u32(const GatherParams p) {
   RankState* st = reinterpret_cast<RankState*>(p.base[rank] + p.L.state);
   const uint32_t* in = p.in + (size_t)rank * p.in_rs;
   uint32_t* out = p.out + (size_t)rank * p.out_rs;
-  pdl_wait();
+  pdl_wait_then_trigger();
   const uint32_t e = *reinterpret_cast<volatile uint32_t*>(&st->gather_epoch) + 1u;
   const int slot = (int)(e & 1u);
   auto at = [&](int owner, int src, int i) {
@@ -683,10 +763,14 @@ __global__ void __launch_bounds__(1024) k_allgather_u32(const GatherParams p) {
 template <typename T, int W>
 cudaError_t launch_typed(const ARParams& p, cudaStream_t stream) {
   void (*fn)(const ARParams);
+  // one-shot: a thread holds one vector of its CTA's row chunk when the chunk fits the block
+  const int hv = p.hidden / Vec<T>::N, chunk = (hv + std::max(p.cluster, 1) - 1) / std::max(p.cluster, 1);
+  const bool one = chunk <= p.threads;
   switch (p.variant) {
-    case kLamport1S: fn = k_oneshot<T, W, kLamport1S>; break;
-    case kPull1S: fn = k_oneshot<T, W, kPull1S>; break;
-    case kNvls1S: fn = k_oneshot<T, W, kNvls1S>; break;
+    case kLamport1S: fn = one ? k_oneshot<T, W, kLamport1S, 1, false> : k_oneshot<T, W, kLamport1S, kVPT, false>; break;
+    case kLamport1SX: fn = one ? k_oneshot<T, W, kLamport1S, 1, true> : k_oneshot<T, W, kLamport1S, kVPT, true>; break;
+    case kPull1S: fn = one ? k_oneshot<T, W, kPull1S, 1, false> : k_oneshot<T, W, kPull1S, kVPT, false>; break;
+    case kNvls1S: fn = one ? k_oneshot<T, W, kNvls1S, 1, false> : k_oneshot<T, W, kNvls1S, kVPT, false>; break;
     case kLamport2S: fn = k_twoshot<T, W, kLamport2S>; break;
     case kPull2S: fn = k_twoshot<T, W, kPull2S>; break;
     case kNvls2S: fn = k_twoshot<T, W, kNvls2S>; break;

@@ -29,7 +29,8 @@ enum Variant : int {
   kNvls2S = 4,     // two-shot: multimem.ld_reduce of the owned slice -> multimem.st of h
   kPull1S = 5,     // one-shot pull: start barrier, every rank reads every peer's x
   kPull2S = 6,     // two-shot: pull reduce-scatter (start barrier) -> all-gather push of h
-  kNumVariants = 7,
+  kLamport1SX = 7, // kLamport1S whose row sums cross the cluster without a release-ordered barrier
+  kNumVariants = 8,
 };
 
 // Per-rank control block (in the rank's own heap). Only this rank's kernels write it, except

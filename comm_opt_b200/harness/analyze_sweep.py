@@ -83,7 +83,7 @@ def expected_tx_bytes(impl: str, msg: int, world: int) -> float | None:
     (NCCL picks its own)."""
     name = impl.split(":", 1)[-1]
     one, two = (world - 1) * msg, 2 * (world - 1) / world * msg
-    return {"lamport_1s": one, "pull_1s": one, "trt_oneshot": one, "lamport_2s": two, "pull_2s": two,
+    return {"lamport_1s": one, "lamport_1sx": one, "pull_1s": one, "trt_oneshot": one, "lamport_2s": two, "pull_2s": two,
             "trt_twoshot": two, "ref_m16nf": two, "nvls_1s": world * msg, "nvls_2s": msg + msg / world}.get(name)
 
 

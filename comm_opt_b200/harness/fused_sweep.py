@@ -34,7 +34,7 @@ from ..parallel import TPCommunicator
 from ..utils.results import RunDir, gpu_state
 from ..utils.stats import summary
 
-DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,ours:nvls_2s,"
+DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_1sx,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,ours:nvls_2s,"
                  "nccl_norm,vllm_car,trt_oneshot,trt_twoshot")
 
 

@@ -36,7 +36,8 @@ FILL = None
 
 L1S, L2S, P1S, P2S = 1, 2, 5, 6
 NV1S, NV2S = 3, 4  # NVSwitch multicast: stage + multicast barrier, in-switch reduce (+ multicast store)
-FG = 7  # gemm_push + ar_norm_gemm (layer-boundary fusion)
+L1SX = 7  # one-shot push whose landing cells get their sentinel back only after the row is finished
+FG = 100  # gemm_push + ar_norm_gemm (layer-boundary fusion)
 FG_COLS = 12  # modelled column groups of the pushed rows
 
 
@@ -92,6 +93,21 @@ class Rank:
         if table.get(key, FILL) is not FILL:
             raise ProtocolViolation(f"rank {self.rank} overwrites unconsumed cell {key}: {table[key]}")
         table[key] = val
+
+    def _peek(self, table: dict, key, epoch: int):
+        """Read a landing cell without giving it back (the restore comes later in the same call)."""
+        v = table.get(key, FILL)
+        if v is FILL:
+            return None
+        if v[0] != epoch:
+            raise ProtocolViolation(f"rank {self.rank} call {epoch} reads stale cell {key}: {v}")
+        return v
+
+    def _restore(self, table: dict, key, epoch: int):
+        v = table.get(key, FILL)
+        if v is FILL or v[0] != epoch:
+            raise ProtocolViolation(f"rank {self.rank} call {epoch} restores cell {key} holding {v}")
+        table[key] = FILL
 
     def _take(self, table: dict, key, epoch: int):
         v = table.get(key, FILL)
@@ -150,6 +166,26 @@ class Rank:
                         yield False
                     got[(src, row)] = v[1]
                     yield True
+        elif call.variant == L1SX:
+            for row in rows:
+                for i in range(1, W):
+                    self._put(self.mem.land1, ((self.rank + i) % W, slot, self.rank, row),
+                              (e, value(self.rank, e, row)))
+                    yield True
+            for row in rows:
+                for src in range(W):
+                    if src == self.rank:
+                        got[(src, row)] = value(src, e, row)
+                        continue
+                    while (v := self._peek(self.mem.land1, (self.rank, slot, src, row), e)) is None:
+                        yield False
+                    got[(src, row)] = v[1]
+                    yield True
+                yield True  # the row sum, the outputs; then the row's cells get their sentinel back
+                for src in range(W):
+                    if src != self.rank:
+                        self._restore(self.mem.land1, (self.rank, slot, src, row), e)
+                        yield True
         elif call.variant in (L2S, P2S):
             if call.variant == L2S:
                 for row in rows:
@@ -339,7 +375,73 @@ def simulate(world: int, calls: list[Call], seed: int = 0, max_steps: int = 2_00
     return dict(steps=steps, epochs=[r.epoch for r in ranks])
 
 
-def random_calls(n: int, seed: int, variants=(L1S, L2S, P1S, P2S), rows=(1, 3, 8), blocks=(1, 2, 4),
+def random_calls(n: int, seed: int, variants=(L1S, L2S, P1S, P2S, L1SX), rows=(1, 3, 8), blocks=(1, 2, 4),
                  splits=(1, 2, 3)) -> list[Call]:
     rng = random.Random(seed)
     return [Call(rng.choice(variants), rng.choice(blocks), rng.choice(rows), rng.choice(splits)) for _ in range(n)]
+
+
+# ---------------------------------------------------------------------------------------------------
+# Row sums across a thread-block cluster without a release-ordered barrier (csrc/fused_ar.cu,
+# row_sum_xch): C CTAs each own one word slot per row parity in their shared memory. For row `it` a
+# CTA stores (tag it + 1, its partial) into its own slot it % 2, then polls every peer's slot it % 2
+# until the tag matches and adds the C partials in CTA order. The words start at tag 0 (cleared before
+# a barrier that every CTA passes before its first poll). The model checks, under random schedules and
+# slow CTAs, that a CTA never overwrites a slot that a peer has not yet read for the older row, that
+# every read returns the partial of the right CTA and row, and that all CTAs compute the same sums.
+
+
+def cluster_partial(cta: int, it: int) -> int:
+    return cta * 1000 + it
+
+
+def simulate_cluster_exchange(C: int, rows: int, seed: int = 0, slow: int | None = None, slow_factor: int = 20,
+                              nslots: int = 2, max_steps: int = 1_000_000) -> dict:
+    rng = random.Random(seed)
+    words = {(c, s): (0, None) for c in range(C) for s in range(nslots)}   # (cta, slot) -> (tag, value)
+    read_upto = {(r, c): -1 for r in range(C) for c in range(C)}          # last row r read from c
+    sums: dict[int, list[int]] = {r: [] for r in range(C)}
+
+    def cta(r: int):
+        for it in range(rows):
+            slot = it % nslots
+            for peer in range(C):  # overwriting slot it % 2 needs every peer done with row it - nslots
+                if peer != r and it - nslots >= 0 and read_upto[(peer, r)] < it - nslots:
+                    raise ProtocolViolation(f"CTA {r} overwrites row {it - nslots} in slot {slot} before CTA {peer} "
+                                            f"read it")
+            words[(r, slot)] = (it + 1, cluster_partial(r, it))
+            yield True
+            vals = []
+            for c in range(C):
+                if c == r:
+                    vals.append(cluster_partial(r, it))
+                    continue
+                while (w := words[(c, slot)])[0] != it + 1:
+                    yield False
+                if w[1] != cluster_partial(c, it):
+                    raise ProtocolViolation(f"CTA {r} row {it} read {w} from CTA {c}")
+                read_upto[(r, c)] = it
+                vals.append(w[1])
+                yield True
+            sums[r].append(sum(vals))
+
+    gens = {r: cta(r) for r in range(C)}
+    weights = {r: (1.0 / slow_factor if r == slow else 1.0) for r in range(C)}
+    steps = idle = 0
+    while gens:
+        live = list(gens)
+        r = rng.choices(live, weights=[weights[x] for x in live])[0]
+        try:
+            progressed = next(gens[r])
+        except StopIteration:
+            del gens[r]
+            progressed = True
+        idle = 0 if progressed else idle + 1
+        steps += 1
+        if idle > 100 * C * C + 1000:
+            raise ProtocolViolation("deadlock in the cluster exchange")
+        if steps > max_steps:
+            raise ProtocolViolation("step budget exhausted")
+    if any(sums[r] != sums[0] for r in range(C)):
+        raise ProtocolViolation("CTAs disagree on the row sums")
+    return dict(steps=steps, sums=sums[0])

@@ -14,7 +14,8 @@ import json
 from dataclasses import asdict, dataclass
 from pathlib import Path
 
-VARIANTS = {"lamport_1s": 1, "lamport_2s": 2, "nvls_1s": 3, "nvls_2s": 4, "pull_1s": 5, "pull_2s": 6}
+VARIANTS = {"lamport_1s": 1, "lamport_2s": 2, "nvls_1s": 3, "nvls_2s": 4, "pull_1s": 5, "pull_2s": 6,
+            "lamport_1sx": 7}
 VARIANT_NAMES = {v: k for k, v in VARIANTS.items()}
 NVLS_VARIANTS = {3, 4}
 TWO_SHOT = {2, 4, 6}

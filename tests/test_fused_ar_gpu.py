@@ -6,6 +6,7 @@ without separate launches that wait on one another. Oracle: fp32 sum + residual 
 relative error <= 2^-5 (the reference's criterion, exp/M17_epoch_ab/bench_ab.py:160-164); fp32
 inputs are held to 1e-5.
 """
+import os
 import random
 
 import pytest
@@ -17,6 +18,10 @@ from comm_opt_b200.parallel import TPCommTimeout, TPCommunicator
 pytestmark = pytest.mark.gpu
 
 EMU_VARIANTS = ["lamport_1s", "lamport_2s", "pull_1s", "pull_2s"]
+
+# Kernels written without a GPU at hand: they run only when asked for, until they have passed here.
+experimental = pytest.mark.skipif(os.environ.get("COB_EXPERIMENTAL") != "1",
+                                  reason="not yet run on a GPU; COB_EXPERIMENTAL=1 runs it")
 
 
 def make_inputs(world, rows, hidden, dtype, dev, seed=0, scale=1.0):
@@ -96,11 +101,15 @@ def test_interleaving(cuda, mode):
     """Port of the reference's interleaving test (exp/M16_epoch_fix/test_interleave.py): 60 calls,
     random token counts, block counts and variants, no state reset; graph mode keeps one CUDA graph
     per combination and replays them in random order."""
+    interleave(cuda, mode, EMU_VARIANTS)
+
+
+def interleave(cuda, mode, variants):
     world, H, dtype = 8, 5120, torch.bfloat16
     comm = TPCommunicator(emulate_world=world, device=cuda, dtype=dtype, max_rows=128, max_hidden=H)
     rng = random.Random(0)
     tokens, blocks = [1, 3, 8, 13, 40, 64, 128], [1, 2, 4, 8, 16]
-    seq = [(rng.choice(tokens), rng.choice(blocks), rng.choice(EMU_VARIANTS)) for _ in range(60)]
+    seq = [(rng.choice(tokens), rng.choice(blocks), rng.choice(variants)) for _ in range(60)]
     g = torch.Generator(device=cuda).manual_seed(7)
     gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).to(dtype)
     graphs = {}
@@ -189,3 +198,48 @@ def test_phase_stamps_and_overhead(cuda):
             ph = summ[r]
             assert 0 <= ph["sent"] <= ph["done"] and ph["received"] <= ph["done"] + 1e-3, (v, ph)
     comm.disable_stamps()
+
+
+# ------------------------------------------------------------------ lamport_1sx (experimental)
+@experimental
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_lamport_1sx_matches_lamport_1s(cuda, world, dtype):
+    """The cluster row-sum exchange changes only how the partial sums meet: outputs and residuals
+    equal lamport_1s bit for bit, for every cluster size and for rows spread over several CTAs."""
+    comm = TPCommunicator(emulate_world=world, device=cuda, dtype=dtype, max_rows=64, max_hidden=8192)
+    budget = 148 // world
+    for rows, hidden in [(1, 8192), (3, 4096), (17, 2048), (64, 1024)]:
+        x, res0, gamma = make_inputs(world, rows, hidden, dtype, cuda, seed=rows)
+        for cluster in (1, 2, 4, 8):
+            blocks = cluster * max(1, min(rows, budget // cluster, 4))
+            out_a, res_a = check(comm, x, res0, gamma, 1e-6, "lamport_1s", cluster=cluster, blocks=blocks)
+            out_b, res_b = check(comm, x, res0, gamma, 1e-6, "lamport_1sx", cluster=cluster, blocks=blocks)
+            assert comm.last_choice.cluster == cluster
+            assert torch.equal(out_a, out_b) and torch.equal(res_a, res_b), (rows, hidden, cluster)
+
+
+@experimental
+@pytest.mark.parametrize("mode", ["eager", "graph"])
+def test_lamport_1sx_interleaving(cuda, mode):
+    interleave(cuda, mode, ["lamport_1sx", "lamport_1s", "lamport_2s", "lamport_1sx"])
+
+
+@experimental
+def test_lamport_1sx_times_out_without_peer(cuda):
+    comm = TPCommunicator(emulate_world=2, device=cuda, dtype=torch.bfloat16, max_rows=4, max_hidden=1024,
+                          timeout_ms=50)
+    from comm_opt_b200._ext import native
+
+    x = torch.randn(2, 1024, device=cuda).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    for cluster in (1, 4):
+        rc = native().fused_ar(comm.heap.bases, 0, comm._layout_list, x, x, x[0], out, 0, 2, 1024, 1e-6, 7, 0,
+                               0, cluster, 0, 0, 1, comm.timeout_ns, 0, 0, 0, False)
+        assert rc[0] == 0
+        torch.cuda.synchronize()
+        with pytest.raises(TPCommTimeout):
+            comm.check()
+        comm.reset()
+    xe, res0, gamma = make_inputs(2, 2, 1024, torch.bfloat16, cuda)
+    check(comm, xe, res0, gamma, 1e-6, "lamport_1sx")

@@ -115,7 +115,7 @@ def test_fused_ar_geometry_rules():
                     if hv > L[14]:
                         continue
                     for rows in (1, 3, 8, 17, 64, 512):
-                        for v in range(1, 7):
+                        for v in range(1, 8):
                             for mc in (False, True):
                                 rc, var, b, t, cl = C.fused_ar_config(L, world, rows, hidden, dtype, v, 0, 0, 0,
                                                                       emulate, 148, mc)

@@ -1,8 +1,8 @@
 """Host-side model checking of the synchronisation protocol (no GPU)."""
 import pytest
 
-from comm_opt_b200.parallel.protocol_sim import (L1S, L2S, P1S, P2S, Call, ProtocolViolation, random_calls,
-                                                 simulate)
+from comm_opt_b200.parallel.protocol_sim import (L1S, L1SX, L2S, P1S, P2S, Call, ProtocolViolation, random_calls,
+                                                 simulate, simulate_cluster_exchange)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -12,7 +12,7 @@ def test_random_interleavings(world):
         assert res["epochs"] == [24] * world
 
 
-@pytest.mark.parametrize("variant", [L1S, L2S, P1S, P2S])
+@pytest.mark.parametrize("variant", [L1S, L2S, P1S, P2S, L1SX])
 def test_slow_rank_each_variant(variant):
     calls = [Call(variant, b, t) for b, t in [(1, 1), (4, 8), (2, 3), (8, 8), (1, 5)] * 3]
     for slow in range(4):
@@ -81,3 +81,32 @@ def test_checker_detects_single_stage_slot_nvls():
         except ProtocolViolation:
             caught += 1
     assert caught >= 3
+
+
+def test_deferred_restore_mixed_with_one_shot():
+    """Landing cells given back after the row is finished (lamport_1sx) interleaved with the
+    restore-at-read one-shot and the two-shot calls on the same landing buffers, a slow rank."""
+    for world in (2, 4, 8):
+        for seed in range(3):
+            calls = random_calls(18, seed + 31 * world, variants=(L1SX, L1S, L1SX, L2S))
+            res = simulate(world, calls, seed=seed, slow_rank=(seed + 1) % world, slow_factor=40)
+            assert res["epochs"] == [18] * world
+
+
+@pytest.mark.parametrize("ctas", [2, 4, 8, 16])
+def test_cluster_exchange(ctas):
+    """Row sums exchanged through per-CTA shared-memory words with two slots (row_sum_xch)."""
+    for rows in (1, 3, 9):
+        for seed in range(4):
+            res = simulate_cluster_exchange(ctas, rows, seed=seed, slow=seed % ctas, slow_factor=30)
+            assert res["sums"] == [sum(c * 1000 + it for c in range(ctas)) for it in range(rows)]
+
+
+def test_checker_detects_single_slot_cluster_exchange():
+    caught = 0
+    for seed in range(6):
+        try:
+            simulate_cluster_exchange(4, 8, seed=seed, slow=seed % 4, slow_factor=30, nslots=1)
+        except ProtocolViolation:
+            caught += 1
+    assert caught >= 5
