@@ -5,6 +5,7 @@
 produces comm_opt_b200/_C*.so next to the Python sources. Kernel sources (.cu) include no torch
 headers; only the two binding files do, which keeps nvcc time low.
 """
+import importlib.util
 import os
 from pathlib import Path
 
@@ -14,26 +15,12 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 ROOT = Path(__file__).resolve().parent
 CSRC = ROOT / "comm_opt_b200" / "csrc"
 
-ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-NVCC = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xptxas=-v" if os.environ.get(
-    "COB_PTXAS_VERBOSE") else "-Xptxas=-O3"]
-if os.environ.get("COB_CHECKED"):  # range-checked heap accesses in the collective kernels (debug builds)
-    NVCC.append("-DCOB_CHECKED")
-CXX = ["-O3", "-std=c++17"]
+_spec = importlib.util.spec_from_file_location("cob_build_flags", CSRC / "build_flags.py")
+flags = importlib.util.module_from_spec(_spec)
+_spec.loader.exec_module(flags)
 
-SOURCES = [
-    "bindings.cpp",
-    "ops_bindings.cpp",
-    "ipc_bindings.cpp",
-    "fused_ar.cu",
-    "fused_gemm.cu",
-    "decode_ops.cu",
-    "attention.cu",
-    "gemm_sm100.cu",
-    "tma_host.cpp",
-    "probes.cu",
-]
-SOURCES += [s for s in os.environ.get("COB_EXTRA_SOURCES", "").split(",") if s]
+NVCC = flags.NVCC + ["-Xptxas=-v" if os.environ.get("COB_PTXAS_VERBOSE") else "-Xptxas=-O3"]
+SOURCES = flags.SOURCES + [s for s in os.environ.get("COB_EXTRA_SOURCES", "").split(",") if s]
 
 setup(
     name="comm_opt_b200",
@@ -44,7 +31,7 @@ setup(
             name="comm_opt_b200._C",
             sources=[str(CSRC / s) for s in SOURCES],
             include_dirs=[str(CSRC)],
-            extra_compile_args={"cxx": CXX, "nvcc": NVCC},
+            extra_compile_args={"cxx": flags.CXX, "nvcc": NVCC},
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

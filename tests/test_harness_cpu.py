@@ -289,3 +289,26 @@ def test_expected_nvlink_bytes_and_link_table():
             dict(impl="nccl_norm", world=8, tokens=1, bytes=S, correct=True, nvlink_tx_bytes_per_op=2.0 * S)]
     t = link_table(rows)
     assert "| ours:auto | 8 | 1 | 16 | 113.6 | 112.0 | 1.01 |" in t and "| nccl_norm | 8 | 1 | 16 | 32.0 | - | - |" in t
+
+
+def test_ptxas_report_parse():
+    """Resource lines of `-Xptxas -v` -> one row per kernel; names shortened for the table."""
+    from comm_opt_b200.harness.ptxas_report import markdown, parse, short
+
+    log = """ptxas info    : Compiling entry function '_Z1kv' for 'sm_100a'
+ptxas info    : Function properties for _Z1kv
+    40 bytes stack frame, 40 bytes spill stores, 44 bytes spill loads
+ptxas info    : Used 128 registers, used 1 barriers, 136 bytes smem
+ptxas info    : Compiling entry function '_Z1jv' for 'sm_100a'
+ptxas info    : Function properties for _Z1jv
+    0 bytes stack frame, 0 bytes spill stores, 0 bytes spill loads
+ptxas info    : Used 74 registers
+"""
+    rows = parse(log)
+    assert [(r["name"], r["regs"], r["spill_st"], r["spill_ld"], r["smem"]) for r in rows] == [
+        ("_Z1kv", 128, 40, 44, 136), ("_Z1jv", 74, 0, 0, 0)]
+    assert short("void cob::(anonymous namespace)::k_oneshot<__nv_bfloat16, 8, 1, 1, false>(cob::ARParams)") == \
+        "k_oneshot<bfloat16, 8, 1, 1, false>"
+    for r in rows:
+        r.update(source="x.cu", kernel=r["name"])
+    assert markdown(rows).count("\n") == 4
