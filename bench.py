@@ -92,9 +92,14 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.thread.join(timeout=5)
+        return self.summarize(self.rows)
+
+    @staticmethod
+    def summarize(rows: list[list[str]]) -> dict:
+        """Median SM clock, max clock, active throttle reasons over nvidia-smi rows of QUERY."""
         mhz, mx, reasons, power = [], [], set(), []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
+        for r in rows:
             try:
                 mhz.append(float(r[1]))
                 mx.append(float(r[2]))

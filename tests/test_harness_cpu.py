@@ -312,3 +312,32 @@ ptxas info    : Used 74 registers
     for r in rows:
         r.update(source="x.cu", kernel=r["name"])
     assert markdown(rows).count("\n") == 4
+
+
+def test_bench_reference_arm_line():
+    """`bench.py --impl reference` prints one JSON line naming why the reference arm cannot run."""
+    import json
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    p = subprocess.run([sys.executable, "bench.py", "--impl", "reference"], cwd=ROOT, capture_output=True, text=True,
+                       timeout=300)
+    assert p.returncode == 0, p.stderr[-2000:]
+    line = json.loads(p.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and len(line["unavailable"]) > 20
+
+
+def test_bench_clock_summary():
+    """Clock record of the timed region: median SM clock, max clock, the throttle reasons seen."""
+    import bench
+
+    rows = [["0", "1965", "1965", "650.1", "0x0", "Not Active", "Not Active", "Not Active", "Not Active"],
+            ["0", "1320", "1965", "997.0", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+            ["0", "1410", "1965", "990.0", "0x4", "Not Active", "Not Active", "Not Active", "Active"],
+            ["[N/A]"]]
+    s = bench.ClockSampler.summarize(rows)
+    assert s["sm_mhz"] == 1410.0 and s["sm_max_mhz"] == 1965.0 and s["samples"] == 3
+    assert s["reasons"] == ["sw_power_cap"] and s["power_w_max"] == 997.0
+    assert bench.ClockSampler.summarize([])["sm_mhz"] is None
