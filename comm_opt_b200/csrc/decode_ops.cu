@@ -81,9 +81,11 @@ __global__ void k_embedding(const int32_t* __restrict__ ids, const T* __restrict
 }
 
 // One block per (sequence, head): q and k heads are rotated (rotate-half RoPE), q goes to q_out,
-// k and v heads go to their slot of the paged cache.
+// k and v heads go to their slot of the paged cache. `bias` ([(nq + 2 nkv) * D], or nullptr) is the
+// QKV projection's bias (Qwen2-style attention), added before the rotation.
 template <typename T>
-__global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, const int32_t* __restrict__ positions,
+__global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, const T* __restrict__ bias,
+                                                    const int32_t* __restrict__ positions,
                                                     const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                                                     const int32_t* __restrict__ block_tables, int max_blocks,
                                                     T* __restrict__ q_out, T* __restrict__ k_cache,
@@ -93,6 +95,7 @@ __global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, c
   const int pos = positions[b];
   const int half = D / 2;
   const T* src = qkv + ((size_t)b * (nq + 2 * nkv) + head) * D;
+  const T* bh = bias ? bias + (size_t)head * D : nullptr;
   T* dst;
   if (head < nq) {
     dst = q_out + ((size_t)b * nq + head) * D;
@@ -105,12 +108,16 @@ __global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, c
   if (head < nq + nkv) {
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
       const float c = cos_t[(size_t)pos * half + i], sn = sin_t[(size_t)pos * half + i];
-      const float x1 = to_f(src[i]), x2 = to_f(src[i + half]);
+      float x1 = to_f(src[i]), x2 = to_f(src[i + half]);
+      if (bh) {
+        x1 += to_f(bh[i]);
+        x2 += to_f(bh[i + half]);
+      }
       dst[i] = from_f<T>(x1 * c - x2 * sn);
       dst[i + half] = from_f<T>(x2 * c + x1 * sn);
     }
   } else {
-    for (int i = threadIdx.x; i < D; i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < D; i += blockDim.x) dst[i] = bh ? from_f<T>(to_f(src[i]) + to_f(bh[i])) : src[i];
   }
 }
 
@@ -237,15 +244,15 @@ cudaError_t embedding(const int32_t* ids, const void* table, void* out, int rows
   });
 }
 
-cudaError_t rope_append_kv(const void* qkv, const int32_t* positions, const float* cos_t, const float* sin_t,
-                           const int32_t* block_tables, int max_blocks_per_seq, void* q_out, void* k_cache,
-                           void* v_cache, int batch, int nq, int nkv, int head_dim, int block_size, int dtype,
-                           cudaStream_t s) {
+cudaError_t rope_append_kv(const void* qkv, const void* bias, const int32_t* positions, const float* cos_t,
+                           const float* sin_t, const int32_t* block_tables, int max_blocks_per_seq, void* q_out,
+                           void* k_cache, void* v_cache, int batch, int nq, int nkv, int head_dim, int block_size,
+                           int dtype, cudaStream_t s) {
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
     if (batch <= 0 || head_dim % 2) return cudaErrorInvalidValue;
     return launch_k(k_rope_append<T>, dim3(batch, nq + 2 * nkv), dim3(64), 0, s, reinterpret_cast<const T*>(qkv),
-                    positions, cos_t, sin_t, block_tables, max_blocks_per_seq, reinterpret_cast<T*>(q_out),
+                    reinterpret_cast<const T*>(bias), positions, cos_t, sin_t, block_tables, max_blocks_per_seq, reinterpret_cast<T*>(q_out),
                     reinterpret_cast<T*>(k_cache), reinterpret_cast<T*>(v_cache), nq, nkv, head_dim, block_size);
   });
 }

@@ -17,11 +17,12 @@ cudaError_t embedding(const int32_t* ids, const void* table, void* out, int rows
                       cudaStream_t s);
 // qkv: [B, (nq + 2*nkv) * D]; rotates q and k by position (rotate-half RoPE, cos/sin tables
 // [max_pos, D/2] fp32), writes rotated q to q_out [B, nq, D] and k, v into the paged caches
-// [num_blocks, nkv, block, D] at slot (block_tables[b][pos / block], pos % block).
-cudaError_t rope_append_kv(const void* qkv, const int32_t* positions, const float* cos_t, const float* sin_t,
-                           const int32_t* block_tables, int max_blocks_per_seq, void* q_out, void* k_cache,
-                           void* v_cache, int batch, int nq, int nkv, int head_dim, int block_size, int dtype,
-                           cudaStream_t s);
+// [num_blocks, nkv, block, D] at slot (block_tables[b][pos / block], pos % block). `bias`
+// ([(nq + 2*nkv) * D] of the qkv dtype, or nullptr) is added to q, k and v first.
+cudaError_t rope_append_kv(const void* qkv, const void* bias, const int32_t* positions, const float* cos_t,
+                           const float* sin_t, const int32_t* block_tables, int max_blocks_per_seq, void* q_out,
+                           void* k_cache, void* v_cache, int batch, int nq, int nkv, int head_dim, int block_size,
+                           int dtype, cudaStream_t s);
 // out[b, i] = silu(gu[b, i]) * gu[b, I + i]
 cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s);
 // Per row: fold max over the local vocabulary into keys[row] (atomicMax of an order-preserving

@@ -68,13 +68,20 @@ void py_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
 
 void py_rope_append_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_t, torch::Tensor sin_t,
                        torch::Tensor block_tables, torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
-                       int64_t nq, int64_t nkv) {
+                       int64_t nq, int64_t nkv, c10::optional<torch::Tensor> bias) {
   for (auto* t : {&qkv, &positions, &cos_t, &sin_t, &block_tables, &q_out, &k_cache, &v_cache}) dense(*t, "arg");
   COB_CHECK(positions.scalar_type() == torch::kInt32 && block_tables.scalar_type() == torch::kInt32,
               "positions and block_tables must be int32");
-  const c10::cuda::CUDAGuard g(qkv.device());
   const int D = (int)k_cache.size(3), bs = (int)k_cache.size(2);
-  ok(cob::rope_append_kv(qkv.data_ptr(), positions.data_ptr<int32_t>(), cos_t.data_ptr<float>(),
+  const void* bptr = nullptr;
+  if (bias.has_value()) {
+    dense(*bias, "bias");
+    COB_CHECK(bias->scalar_type() == qkv.scalar_type() && bias->numel() == (nq + 2 * nkv) * D,
+              "bias must have the qkv dtype and (nq + 2 nkv) * head_dim elements");
+    bptr = bias->data_ptr();
+  }
+  const c10::cuda::CUDAGuard g(qkv.device());
+  ok(cob::rope_append_kv(qkv.data_ptr(), bptr, positions.data_ptr<int32_t>(), cos_t.data_ptr<float>(),
                          sin_t.data_ptr<float>(), block_tables.data_ptr<int32_t>(), (int)block_tables.size(1),
                          q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), (int)qkv.size(0), (int)nq,
                          (int)nkv, D, bs, code_of(qkv), cur()),
@@ -315,7 +322,9 @@ void register_ops(pybind11::module& m) {
   m.def("rmsnorm", &py_rmsnorm);
   m.def("add_rmsnorm", &py_add_rmsnorm);
   m.def("embedding", &py_embedding);
-  m.def("rope_append_kv", &py_rope_append_kv);
+  m.def("rope_append_kv", &py_rope_append_kv, pybind11::arg("qkv"), pybind11::arg("positions"), pybind11::arg("cos_t"),
+        pybind11::arg("sin_t"), pybind11::arg("block_tables"), pybind11::arg("q_out"), pybind11::arg("k_cache"),
+        pybind11::arg("v_cache"), pybind11::arg("nq"), pybind11::arg("nkv"), pybind11::arg("bias") = pybind11::none());
   m.def("silu_mul", &py_silu_mul);
   m.def("argmax_local", &py_argmax_local);
   m.def("argmax_combine", &py_argmax_combine, pybind11::arg("gathered"), pybind11::arg("ids"),

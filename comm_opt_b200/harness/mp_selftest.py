@@ -24,7 +24,8 @@ Parts:
   decode_fused - the same with the layer boundaries fused (GEMM push epilogue -> all-reduce + RMSNorm
                inside the next GEMM); decode_fused_epi also moves SiLU * up and RoPE + KV append
                into the consumer GEMMs' epilogues; decode_nccl runs the baseline step (NCCL all-reduce +
-               add/RMSNorm kernel) through the same runner.
+               add/RMSNorm kernel) through the same runner; decode_qkv_bias runs the fused step on the
+               Qwen2.5 attention shape (QKV bias, 5 query heads per KV head at 4 ranks).
 Rank 0 prints one JSON summary; the exit code is non-zero on any failure.
 """
 from __future__ import annotations
@@ -284,15 +285,18 @@ def stress(C: Checker, dev, world, calls: int = 120):
     comm.close()
 
 
-def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False, collective: str = "ours"):
+def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False, collective: str = "ours",
+                 model: str = "tiny"):
     import math
 
     import torch.nn.functional as F
 
-    from ..models.llama import LlamaWeights, TPDecodeRunner, tiny_config
+    from dataclasses import replace
+
+    from ..models.llama import PRESETS, LlamaWeights, TPDecodeRunner
     from ..ops.reference import rope_tables
 
-    cfg = tiny_config(layers=2)
+    cfg = replace(PRESETS[model], layers=2)
     full = LlamaWeights.full_random(cfg, device=dev, seed=3)
     w = LlamaWeights(cfg, dist.get_rank(), world, dev, full=full)
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)
@@ -318,7 +322,8 @@ def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = 
         for L in full["layers"]:
             L = {k: v.float() for k, v in L.items()}
             h = F.rms_norm(x, (cfg.hidden,), L["ln1"], cfg.eps)
-            q, k, v = (h @ L["wqkv"].t()).split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
+            qkv = h @ L["wqkv"].t() + (L["bqkv"] if "bqkv" in L else 0.0)
+            q, k, v = qkv.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
             q, k = rope(q.view(B, P, cfg.heads, D)), rope(k.view(B, P, cfg.kv_heads, D))
             a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
                                                v.view(B, P, cfg.kv_heads, D).transpose(1, 2), is_causal=True,
@@ -364,7 +369,9 @@ def main():
             {"functional": functional, "fault": fault, "leave": leave, "decode": decode_check, "stress": stress,
              "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True),
              "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True),
-             "decode_nccl": lambda C, dev, world: decode_check(C, dev, world, collective="nccl")
+             "decode_nccl": lambda C, dev, world: decode_check(C, dev, world, collective="nccl"),
+             # Qwen2.5-shaped attention: QKV bias, 5 query heads per KV head at 4 ranks
+             "decode_qkv_bias": lambda C, dev, world: decode_check(C, dev, world, fused=True, model="tiny-qkv-bias")
              }[part](C, dev, world)
     except Exception:
         err = traceback.format_exc()

@@ -40,6 +40,7 @@ class LlamaConfig:
     vocab: int
     eps: float = 1e-5
     rope_theta: float = 500000.0
+    qkv_bias: bool = False  # Qwen2-style attention: the QKV projection has a bias
 
     def shard(self, tp: int) -> dict:
         assert self.heads % tp == 0 and self.kv_heads % tp == 0 and self.inter % tp == 0 and self.vocab % tp == 0, \
@@ -50,19 +51,29 @@ class LlamaConfig:
     def params(self) -> int:
         H, D = self.hidden, self.head_dim
         per_layer = H * (self.heads + 2 * self.kv_heads) * D + self.heads * D * H + 3 * H * self.inter + 2 * H
+        if self.qkv_bias:
+            per_layer += (self.heads + 2 * self.kv_heads) * D
         return self.layers * per_layer + 2 * self.vocab * H + H
 
 
 LLAMA3_8B = LlamaConfig("llama3-8b", 4096, 32, 32, 8, 128, 14336, 128256)
 LLAMA3_70B = LlamaConfig("llama3-70b", 8192, 80, 64, 8, 128, 28672, 128256)
 LLAMA3_1B = LlamaConfig("llama3-1b", 2048, 16, 32, 8, 64, 8192, 128256)
+# Qwen2.5-32B-Instruct shapes, the larger model of the reference's end-to-end inference study
+# (exp/M5_e2e_comm_share/run_infer.py:15-19): hidden 5120 is the hidden size of the reference's fused-op
+# measurements; 40 query / 8 KV heads, SwiGLU 27648, vocab 152064, QKV bias, RoPE theta 1e6.
+QWEN25_32B = LlamaConfig("qwen2.5-32b", 5120, 64, 40, 8, 128, 27648, 152064, eps=1e-6, rope_theta=1e6, qkv_bias=True)
 TINY = LlamaConfig("tiny", 1024, 2, 16, 8, 128, 2048, 4096)
-PRESETS = {"llama3-1b": LLAMA3_1B, "1b": LLAMA3_1B, "llama3-8b": LLAMA3_8B, "8b": LLAMA3_8B, "llama3-70b": LLAMA3_70B, "70b": LLAMA3_70B, "tiny": TINY}
+TINY_BIAS = replace(TINY, name="tiny-qkv-bias", heads=20, kv_heads=4, qkv_bias=True)  # 5 query heads per KV head
+PRESETS = {"llama3-1b": LLAMA3_1B, "1b": LLAMA3_1B, "llama3-8b": LLAMA3_8B, "8b": LLAMA3_8B, "llama3-70b": LLAMA3_70B,
+           "70b": LLAMA3_70B, "qwen2.5-32b": QWEN25_32B, "qwen32b": QWEN25_32B, "tiny": TINY,
+           "tiny-qkv-bias": TINY_BIAS}
 
 
 class LayerWeights:
-    def __init__(self, wqkv, wo, wgu, wdown, ln1, ln2):
+    def __init__(self, wqkv, wo, wgu, wdown, ln1, ln2, bqkv=None):
         self.wqkv, self.wo, self.wgu, self.wdown, self.ln1, self.ln2 = wqkv, wo, wgu, wdown, ln1, ln2
+        self.bqkv = bqkv  # [(nq + 2 nkv) * head_dim] of this rank, or None
 
 
 class LlamaWeights:
@@ -88,15 +99,19 @@ class LlamaWeights:
             self.final_norm = full["final_norm"].to(device)
             self.lm_head = full["lm_head"].chunk(tp, 0)[tp_rank].contiguous().to(device)
             self.layers = []
+            def qkv_rows(t):  # this rank's q, k and v heads of a [(heads + 2 kv_heads) * D, ...] tensor
+                q, k, v = t.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], 0)
+                return torch.cat([q.chunk(tp, 0)[tp_rank], k.chunk(tp, 0)[tp_rank], v.chunk(tp, 0)[tp_rank]], 0)
+
             for L in full["layers"]:
-                q, k, v = L["wqkv"].split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], 0)
-                wqkv = torch.cat([q.chunk(tp, 0)[tp_rank], k.chunk(tp, 0)[tp_rank], v.chunk(tp, 0)[tp_rank]], 0)
+                wqkv = qkv_rows(L["wqkv"])
                 g, u = L["wgu"].chunk(2, 0)
                 wgu = torch.cat([g.chunk(tp, 0)[tp_rank], u.chunk(tp, 0)[tp_rank]], 0)
+                bqkv = qkv_rows(L["bqkv"]).contiguous().to(device) if L.get("bqkv") is not None else None
                 self.layers.append(LayerWeights(
                     wqkv.contiguous().to(device), L["wo"].chunk(tp, 1)[tp_rank].contiguous().to(device),
                     wgu.contiguous().to(device), L["wdown"].chunk(tp, 1)[tp_rank].contiguous().to(device),
-                    L["ln1"].to(device), L["ln2"].to(device)))
+                    L["ln1"].to(device), L["ln2"].to(device), bqkv))
             return
         gen.manual_seed(seed * 1_000_003 + 1)  # replicated tensors: same seed on every rank
         self.embed = torch.empty(cfg.vocab, H, dtype=dtype, device=device).normal_(0.0, 1.0, generator=gen)
@@ -107,7 +122,8 @@ class LlamaWeights:
             k0 = 16 + 8 * i
             self.layers.append(LayerWeights(
                 rnd(((s["nq"] + 2 * s["nkv"]) * D, H), k0), rnd((H, s["nq"] * D), k0 + 1),
-                rnd((2 * s["inter"], H), k0 + 2), rnd((H, s["inter"]), k0 + 3), norm_w(k0 + 4), norm_w(k0 + 5)))
+                rnd((2 * s["inter"], H), k0 + 2), rnd((H, s["inter"]), k0 + 3), norm_w(k0 + 4), norm_w(k0 + 5),
+                rnd(((s["nq"] + 2 * s["nkv"]) * D,), k0 + 6) if cfg.qkv_bias else None))
 
     @staticmethod
     def full_random(cfg: LlamaConfig, device="cpu", dtype=torch.bfloat16, seed: int = 0, std: float = 0.02) -> dict:
@@ -124,6 +140,9 @@ class LlamaWeights:
         layers = [dict(wqkv=rnd((cfg.heads + 2 * cfg.kv_heads) * D, H), wo=rnd(H, cfg.heads * D),
                        wgu=rnd(2 * cfg.inter, H), wdown=rnd(H, cfg.inter), ln1=nw(), ln2=nw())
                   for _ in range(cfg.layers)]
+        if cfg.qkv_bias:  # only present with a bias, so every tensor of a layer dict is a real tensor
+            for L in layers:
+                L["bqkv"] = rnd((cfg.heads + 2 * cfg.kv_heads) * D, scale=0.5)
         return dict(embed=rnd(cfg.vocab, H, scale=1.0), final_norm=nw(), lm_head=rnd(cfg.vocab, H), layers=layers)
 
 
@@ -243,6 +262,8 @@ class TPDecodeRunner:
         for i, L in enumerate(self.w.layers):
             h = F.rms_norm(res.float(), (cfg.hidden,), L.ln1.float(), cfg.eps).to(self.dtype)
             qkv = h @ L.wqkv.t()
+            if L.bqkv is not None:
+                qkv = qkv + L.bqkv
             q, k, v = qkv.split([s["nq"] * D, s["nkv"] * D, s["nkv"] * D], -1)
             q = rope(q.view(B, P, s["nq"], D))
             k = rope(k.view(B, P, s["nkv"], D))
@@ -309,7 +330,7 @@ class TPDecodeRunner:
         for i, L in enumerate(w.layers):
             self.lin[(i, "qkv")](buf["h"], out=buf["qkv"])
             K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
-                             self.cache.v[i], s["nq"], s["nkv"])
+                             self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
             buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
             self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
             self._allreduce_add_rmsnorm(buf, L.ln2)
@@ -349,7 +370,8 @@ class TPDecodeRunner:
             comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, dry_run=True, epilogue="swiglu")
             sw = comm.last_fused_gemm[1][2] > 0 and s["inter"] % 64 == 0
             comm.ar_norm_gemm(buf["res"], L.ln1, L.wqkv, dry_run=True, epilogue="rope_kv")
-            rp = comm.last_fused_gemm[1][2] > 0 and cfg.head_dim == 128
+            # the QKV epilogue has no bias term: a QKV bias keeps RoPE + append in its own kernel
+            rp = comm.last_fused_gemm[1][2] > 0 and cfg.head_dim == 128 and not cfg.qkv_bias
             if sw and self._wgu_il is None:  # tile-interleaved gate/up copies (allocated outside capture)
                 self._wgu_il = [comm.interleave_gate_up(Lw.wgu) for Lw in self.w.layers]
             self._fuse_epi[B] = (sw, rp)
@@ -367,7 +389,7 @@ class TPDecodeRunner:
         for i, L in enumerate(w.layers):
             if i == 0 or not rp:
                 K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
-                                 self.cache.v[i], s["nq"], s["nkv"])
+                                 self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
                 n += 1
             buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
             comm.gemm_push(buf["attn"].view(B, -1), L.wo)
@@ -505,7 +527,8 @@ def reference_greedy(cfg: LlamaConfig, full: dict, prompts: torch.Tensor, steps:
         for L in layers:
             L = {k: v.to(device).float() for k, v in L.items()}
             h = F.rms_norm(x, (cfg.hidden,), L["ln1"], cfg.eps)
-            q, k, v = (h @ L["wqkv"].t()).split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
+            qkv = h @ L["wqkv"].t() + (L["bqkv"] if "bqkv" in L else 0.0)
+            q, k, v = qkv.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
             q, k = rope(q.view(B, P, cfg.heads, D)), rope(k.view(B, P, cfg.kv_heads, D))
             v = v.view(B, P, cfg.kv_heads, D)
             a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,

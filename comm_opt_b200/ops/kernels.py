@@ -25,8 +25,10 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None =
     return out
 
 
-def rope_append_kv(qkv, positions, cos, sin, block_tables, q_out, k_cache, v_cache, nq: int, nkv: int):
-    native().rope_append_kv(qkv, positions, cos, sin, block_tables, q_out, k_cache, v_cache, nq, nkv)
+def rope_append_kv(qkv, positions, cos, sin, block_tables, q_out, k_cache, v_cache, nq: int, nkv: int, bias=None):
+    """RoPE on q and k of the fused qkv rows, q to q_out, k and v into the paged caches; `bias`
+    ([(nq + 2 nkv) * head_dim], optional) is the QKV projection's bias, added first."""
+    native().rope_append_kv(qkv, positions, cos, sin, block_tables, q_out, k_cache, v_cache, nq, nkv, bias)
     return q_out
 
 

@@ -33,26 +33,32 @@ def test_embedding(cuda):
     assert torch.equal(K.embedding(ids, table), table[ids.long()])
 
 
-@pytest.mark.parametrize("nq,nkv", [(8, 1), (32, 8), (4, 4)])
-def test_rope_append_kv(cuda, nq, nkv):
+@pytest.mark.parametrize("nq,nkv,bias", [(8, 1, False), (32, 8, False), (4, 4, False), (5, 1, True), (20, 4, True)])
+def test_rope_append_kv(cuda, nq, nkv, bias):
+    """RoPE + paged append against fp32; with `bias` (the Qwen2.5 QKV bias, 5 query heads per KV head at
+    TP=8 / TP=2) added to q, k and v before the rotation."""
     B, D, bs, maxb = 5, 128, 16, 8
     dtype = torch.bfloat16
     cos, sin = rope_tables(maxb * bs, D, 500000.0, cuda)
     qkv = torch.randn(B, (nq + 2 * nkv) * D, device=cuda).to(dtype)
+    b_qkv = torch.randn((nq + 2 * nkv) * D, device=cuda).to(dtype) if bias else None
     pos = torch.tensor([0, 17, 33, 127, 64], device=cuda, dtype=torch.int32)
     bt = torch.randperm(B * maxb, device=cuda).to(torch.int32).view(B, maxb)
     kc = torch.zeros(B * maxb, nkv, bs, D, device=cuda, dtype=dtype)
     vc = torch.zeros_like(kc)
     q = torch.empty(B, nq, D, device=cuda, dtype=dtype)
-    K.rope_append_kv(qkv, pos, cos, sin, bt, q, kc, vc, nq, nkv)
-    heads = qkv.view(B, nq + 2 * nkv, D)
+    K.rope_append_kv(qkv, pos, cos, sin, bt, q, kc, vc, nq, nkv, bias=b_qkv)
+    heads = (qkv.float() + (b_qkv.float() if bias else 0.0)).view(B, nq + 2 * nkv, D)
     assert rel_err(q, rope_ref(heads[:, :nq], pos, cos, sin)) <= 2 ** -7
     kref = rope_ref(heads[:, nq:nq + nkv], pos, cos, sin)
     for b in range(B):
         p = int(pos[b])
         blk = int(bt[b, p // bs])
         assert rel_err(kc[blk, :, p % bs], kref[b]) <= 2 ** -7
-        assert torch.equal(vc[blk, :, p % bs], heads[b, nq + nkv:])
+        if bias:
+            assert rel_err(vc[blk, :, p % bs], heads[b, nq + nkv:]) <= 2 ** -7
+        else:
+            assert torch.equal(vc[blk, :, p % bs], heads[b, nq + nkv:].to(dtype))
 
 
 @pytest.mark.parametrize("dtype", DTYPES)

@@ -1,4 +1,6 @@
 """Llama-shaped decode runner (world 1) against an unsharded fp32 PyTorch forward."""
+from dataclasses import replace
+
 import pytest
 import torch
 
@@ -29,7 +31,8 @@ def _ref_logits(cfg, full, tokens, device):
     for L in full["layers"]:
         L = {k: v.to(device).float() for k, v in L.items()}
         h = F.rms_norm(x, (cfg.hidden,), L["ln1"], cfg.eps)
-        q, k, v = (h @ L["wqkv"].t()).split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
+        qkv = h @ L["wqkv"].t() + (L["bqkv"] if "bqkv" in L else 0.0)
+        q, k, v = qkv.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
         q, k = rope(q.view(B, P, cfg.heads, D)), rope(k.view(B, P, cfg.kv_heads, D))
         a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2),
                                            v.view(B, P, cfg.kv_heads, D).transpose(1, 2), is_causal=True,
@@ -42,9 +45,13 @@ def _ref_logits(cfg, full, tokens, device):
     return h @ full["lm_head"].to(device).float().t()
 
 
-@pytest.mark.parametrize("gemm_impl", ["cob", "torch"])
-def test_decode_logits_match_reference(cuda, gemm_impl):
-    cfg = tiny_config(layers=2)
+@pytest.mark.parametrize("gemm_impl,model", [("cob", "tiny"), ("torch", "tiny"), ("cob", "tiny-qkv-bias")])
+def test_decode_logits_match_reference(cuda, gemm_impl, model):
+    """Decode logits against the fp32 forward; `tiny-qkv-bias` has the Qwen2.5 attention shape (QKV bias,
+    5 query heads per KV head)."""
+    from comm_opt_b200.models.llama import PRESETS
+
+    cfg = replace(PRESETS[model], layers=2)
     full = LlamaWeights.full_random(cfg, device=cuda, seed=3)
     w = LlamaWeights(cfg, 0, 1, cuda, full=full)
     comm = TPCommunicator(None, device=cuda, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)

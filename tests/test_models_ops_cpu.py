@@ -133,3 +133,37 @@ def test_repeat_statistics_effectiveness_rule():
     out = {r["tokens"]: r for r in repeats(rows, "ours:x", "base")}
     assert out[1]["effective"] and abs(out[1]["ours"]["med"] - 10.1) < 1e-9 and out[1]["ours"]["n"] == 3
     assert not out[2]["effective"]  # the first launch's outlier makes the intervals overlap
+
+
+def test_qwen25_32b_preset_and_bias_sharding():
+    """Qwen2.5-32B shapes (the reference's end-to-end inference model, hidden 5120): 32.8 B parameters,
+    5 query heads per KV head at TP=8, and the QKV bias sharded with the same q / k / v head split as
+    the weight rows."""
+    from comm_opt_b200.models.llama import PRESETS, QWEN25_32B
+
+    assert abs(QWEN25_32B.params / 1e9 - 32.76) < 0.05
+    for tp in (1, 2, 4, 8):
+        s = QWEN25_32B.shard(tp)
+        assert s["nq"] // s["nkv"] == 5 and s["nq"] * tp == 40
+    s = QWEN25_32B.shard(8)
+    assert s == dict(nq=5, nkv=1, inter=3456, vocab=19008)
+    cfg = PRESETS["tiny-qkv-bias"]
+    full = LlamaWeights.full_random(cfg, device="cpu", seed=2)
+    assert all("bqkv" in L for L in full["layers"])
+    assert all("bqkv" not in L for L in LlamaWeights.full_random(tiny_config(layers=1), device="cpu")["layers"])
+    tp, D = 2, cfg.head_dim
+    parts = [LlamaWeights(cfg, r, tp, "cpu", full=full) for r in range(tp)]
+    b = full["layers"][0]["bqkv"]
+    w = full["layers"][0]["wqkv"]
+    nq, nkv = cfg.heads // tp, cfg.kv_heads // tp
+    for r, p in enumerate(parts):
+        L = p.layers[0]
+        assert L.bqkv.shape == ((nq + 2 * nkv) * D,)
+        q0, k0, v0 = r * nq * D, cfg.heads * D + r * nkv * D, (cfg.heads + cfg.kv_heads) * D + r * nkv * D
+        assert torch.equal(L.bqkv[:nq * D], b[q0:q0 + nq * D])
+        assert torch.equal(L.bqkv[nq * D:(nq + nkv) * D], b[k0:k0 + nkv * D])
+        assert torch.equal(L.bqkv[(nq + nkv) * D:], b[v0:v0 + nkv * D])
+        assert torch.equal(L.wqkv[nq * D:(nq + nkv) * D], w[k0:k0 + nkv * D])  # weight rows split alike
+    # random-init (unsliced) shards carry a bias of the right length too
+    own = LlamaWeights(cfg, 1, tp, "cpu", seed=4)
+    assert own.layers[0].bqkv.shape == ((nq + 2 * nkv) * D,)
