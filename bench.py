@@ -49,6 +49,9 @@ def parse():
     p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=1,
                    help="fuse o_proj/down_proj -> all-reduce + RMSNorm -> next GEMM (TP > 1; 0 = separate "
                         "GEMM, fused all-reduce + RMSNorm kernel, GEMM)")
+    p.add_argument("--tune-boundaries", type=int, choices=[0, 1], default=1,
+                   help="with fused boundaries: time each fused / separate choice of the two boundary kinds at "
+                        "capture and keep the fastest (0 = both fused)")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--layers", type=int, default=None, help="override the layer count (debug only; invalid for bench)")
     p.add_argument("--out", default=None, help="also write the JSON line to this file")
@@ -160,7 +163,8 @@ def main():
     comm = TPCommunicator(group, device=dev, dtype=torch.bfloat16, max_rows=max(B, 8), max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, weights, comm, max_batch=B, max_seq=max_seq, device=dev, gemm=args.gemm,
                             nccl_group=group, fuse_boundary=bool(args.fuse_boundary),
-                            fuse_epilogues=bool(args.fuse_epilogues), collective=args.collective)
+                            fuse_epilogues=bool(args.fuse_epilogues), collective=args.collective,
+                            tune_boundaries=bool(args.tune_boundaries))
     prompts = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(1234))
     first = runner.prefill(prompts)
     runner.start(B, first, P)
@@ -238,6 +242,9 @@ def main():
                        "gemm": args.gemm, "collective": args.collective, "fuse_boundary": runner.fuse_boundary,
                        "fuse_epilogues": runner.fuse_boundary and runner.fuse_epilogues,
                        "fuse_fallback": runner.fuse_error[:200] or None,
+                       "fused_boundaries": (dict(zip(("attention_out", "mlp_out"), runner.fuse_kinds.get(B, (True, True))),
+                                                 step_ms_by_choice=runner.boundary_times.get(B))
+                                            if runner.fuse_boundary else None),
                        "tokens_per_s": round(B * 1000.0 / ms, 1),
                        "l2": "no flush: each step streams the full weight set (141 GB / N) >> 126 MB L2",
                        "setup_s": round(setup_s, 1)},

@@ -25,7 +25,9 @@ Parts:
                inside the next GEMM); decode_fused_epi also moves SiLU * up and RoPE + KV append
                into the consumer GEMMs' epilogues; decode_nccl runs the baseline step (NCCL all-reduce +
                add/RMSNorm kernel) through the same runner; decode_qkv_bias runs the fused step on the
-               Qwen2.5 attention shape (QKV bias, 5 query heads per KV head at 4 ranks).
+               Qwen2.5 attention shape (QKV bias, 5 query heads per KV head at 4 ranks); decode_mixed fuses
+               only one of the two boundary kinds per layer (attention output or MLP output), the
+               mixes the capture-time tuning may choose (decode_fused runs that tuning).
 Rank 0 prints one JSON summary; the exit code is non-zero on any failure.
 """
 from __future__ import annotations
@@ -286,7 +288,7 @@ def stress(C: Checker, dev, world, calls: int = 120):
 
 
 def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = False, collective: str = "ours",
-                 model: str = "tiny"):
+                 model: str = "tiny", kinds: tuple[bool, bool] | None = None):
     import math
 
     import torch.nn.functional as F
@@ -301,7 +303,10 @@ def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = 
     w = LlamaWeights(cfg, dist.get_rank(), world, dev, full=full)
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)
     runner = TPDecodeRunner(cfg, w, comm, max_batch=4, max_seq=96, device=dev, nccl_group=dist.group.WORLD,
-                            fuse_boundary=fused, fuse_epilogues=epilogues, collective=collective)
+                            fuse_boundary=fused, fuse_epilogues=epilogues, collective=collective,
+                            tune_boundaries=kinds is None)
+    if kinds is not None:  # a fixed mix of fused and separate boundaries instead of the timed choice
+        runner.fuse_kinds[3] = kinds
     C.check(runner.fuse_boundary == fused, "layer-boundary fusion engaged as requested")
     prompts = torch.randint(0, cfg.vocab, (3, 29), generator=torch.Generator().manual_seed(1))
     first = runner.prefill(prompts)
@@ -371,7 +376,9 @@ def main():
              "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True),
              "decode_nccl": lambda C, dev, world: decode_check(C, dev, world, collective="nccl"),
              # Qwen2.5-shaped attention: QKV bias, 5 query heads per KV head at 4 ranks
-             "decode_qkv_bias": lambda C, dev, world: decode_check(C, dev, world, fused=True, model="tiny-qkv-bias")
+             "decode_qkv_bias": lambda C, dev, world: decode_check(C, dev, world, fused=True, model="tiny-qkv-bias"),
+             "decode_mixed": lambda C, dev, world: [decode_check(C, dev, world, fused=True, kinds=k)
+                                                    for k in ((True, False), (False, True))]
              }[part](C, dev, world)
     except Exception:
         err = traceback.format_exc()

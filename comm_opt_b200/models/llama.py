@@ -197,7 +197,7 @@ class TPDecodeRunner:
 
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
                  device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
-                 fuse_epilogues: bool = False, collective: str = "ours"):
+                 fuse_epilogues: bool = False, collective: str = "ours", tune_boundaries: bool = True):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -232,6 +232,11 @@ class TPDecodeRunner:
         self.fuse_epilogues = bool(fuse_epilogues)
         self._fuse_epi: dict[int, tuple[bool, bool]] = {}
         self._wgu_il: list | None = None
+        # per batch size: (attention-output boundary fused, MLP-output boundary fused); with
+        # tune_boundaries the capture times each combination and keeps the fastest (max over ranks)
+        self.fuse_kinds: dict[int, tuple[bool, bool]] = {}
+        self.tune_boundaries = bool(tune_boundaries)
+        self.boundary_times: dict[int, dict[str, float]] = {}
         if self.fuse_boundary:
             comm.prepare_fused_gemm(cfg.hidden)
 
@@ -378,11 +383,16 @@ class TPDecodeRunner:
         return self._fuse_epi[B]
 
     def _step_fused(self, B: int, buf: dict, bt: torch.Tensor) -> int:
-        """Decode step with the layer boundaries fused (after the embedding and first norm). Where the
-        consumer GEMM supports it, SiLU * up runs in the gate_up epilogue and RoPE + the paged-KV append
-        in the QKV epilogue (5 kernels per layer instead of 7)."""
+        """Decode step with fused layer boundaries (after the embedding and first norm). Each of the two
+        boundary kinds of a layer - attention output (o_proj -> all-reduce + residual + RMSNorm ->
+        gate_up) and MLP output (down_proj -> ... -> next layer's QKV, or the LM head) - is either fused
+        (push GEMM + consumer GEMM, 2 kernels) or separate (GEMM, fused all-reduce kernel, GEMM), as
+        `fuse_kinds[B]` says (both fused by default). Where the consumer GEMM supports it, SiLU * up runs
+        in the gate_up epilogue and RoPE + the paged-KV append in the QKV epilogue."""
         cfg, s, w, comm = self.cfg, self.s, self.w, self.comm
+        fa, fm = self.fuse_kinds.get(B, (True, True))
         sw, rp = self._fused_epilogues(B, buf)
+        sw, rp = sw and fa, rp and fm
         n = 0
         self.lin[(0, "qkv")](buf["h"], out=buf["qkv"])
         n += 1
@@ -392,31 +402,95 @@ class TPDecodeRunner:
                                  self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
                 n += 1
             buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
-            comm.gemm_push(buf["attn"].view(B, -1), L.wo)
-            if sw:
-                comm.ar_norm_gemm(buf["res"], L.ln2, self._wgu_il[i], cfg.eps, out=buf["act"], epilogue="swiglu")
+            n += 1
+            # attention-output boundary
+            if fa:
+                comm.gemm_push(buf["attn"].view(B, -1), L.wo)
+                if sw:
+                    comm.ar_norm_gemm(buf["res"], L.ln2, self._wgu_il[i], cfg.eps, out=buf["act"], epilogue="swiglu")
+                else:
+                    comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, cfg.eps, out=buf["gu"])
+                n += 2
             else:
-                comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, cfg.eps, out=buf["gu"])
+                self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
+                self._allreduce_add_rmsnorm(buf, L.ln2)
+                self.lin[(i, "gu")](buf["h"], out=buf["gu"])
+                n += 3
+            if not sw:
                 K.silu_mul(buf["gu"], out=buf["act"])
                 n += 1
-            comm.gemm_push(buf["act"], L.wdown)
-            if i + 1 < len(w.layers):
-                nxt = w.layers[i + 1]
-                if rp:
-                    comm.ar_norm_gemm(buf["res"], nxt.ln1, nxt.wqkv, cfg.eps, out=buf["q"], epilogue="rope_kv",
+            # MLP-output boundary
+            last = i + 1 == len(w.layers)
+            nxt = None if last else w.layers[i + 1]
+            gamma = w.final_norm if last else nxt.ln1
+            if fm:
+                comm.gemm_push(buf["act"], L.wdown)
+                if last:
+                    comm.ar_norm_gemm(buf["res"], gamma, w.lm_head, cfg.eps, out=buf["logits"])
+                elif rp:
+                    comm.ar_norm_gemm(buf["res"], gamma, nxt.wqkv, cfg.eps, out=buf["q"], epilogue="rope_kv",
                                       rope=dict(positions=buf["pos"], cos=self.cos, sin=self.sin, block_tables=bt,
                                                 k_cache=self.cache.k[i + 1], v_cache=self.cache.v[i + 1],
                                                 nq=s["nq"], nkv=s["nkv"]))
                 else:
-                    comm.ar_norm_gemm(buf["res"], nxt.ln1, nxt.wqkv, cfg.eps, out=buf["qkv"])
+                    comm.ar_norm_gemm(buf["res"], gamma, nxt.wqkv, cfg.eps, out=buf["qkv"])
+                n += 2
             else:
-                comm.ar_norm_gemm(buf["res"], w.final_norm, w.lm_head, cfg.eps, out=buf["logits"])
-            n += 5
+                self.lin[(i, "down")](buf["act"], out=buf["part"])
+                self._allreduce_add_rmsnorm(buf, gamma)
+                if last:
+                    self.lin["head"](buf["h"], out=buf["logits"])
+                else:
+                    self.lin[(i + 1, "qkv")](buf["h"], out=buf["qkv"])
+                n += 3
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         comm.all_gather_u32(buf["keys"].view(torch.int32), out=buf["gathered"].view(torch.int32).view(self.tp, 2 * B))
         K.argmax_combine(buf["gathered"], self.tp, ids=buf["ids"], positions=buf["pos"], seq_lens=buf["lens"],
                          local_keys=buf["keys"])
         return n + 3
+
+    def _tune_fusion(self, B: int, buf: dict, saved: dict, warm: int = 2, reps: int = 5) -> tuple[bool, bool]:
+        """Time one captured decode step per choice of fused / separate boundaries (attention output,
+        MLP output) and return the fastest. The per-choice times are reduced with MAX over the ranks
+        before the choice, so every rank takes the same one; the decode state is restored after each."""
+        import torch.distributed as dist
+
+        combos = [(True, True), (True, False), (False, True), (False, False)]
+        times = torch.zeros(len(combos), dtype=torch.float64, device=self.device)
+        for j, kinds in enumerate(combos):
+            self.fuse_kinds[B] = kinds
+            s = torch.cuda.Stream(self.device)  # one eager step first, as before any capture
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                self._step(B, buf)
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            torch.cuda.synchronize(self.device)
+            for k, v in saved.items():
+                buf[k].copy_(v)
+            g = torch.cuda.CUDAGraph()
+            old = K.set_pdl(self.pdl)
+            try:
+                with torch.cuda.graph(g):
+                    self._step(B, buf)
+            finally:
+                K.set_pdl(old)
+            for _ in range(warm):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize(self.device)
+            times[j] = e0.elapsed_time(e1) / reps
+            del g
+            for k, v in saved.items():
+                buf[k].copy_(v)
+        dist.all_reduce(times, op=dist.ReduceOp.MAX, group=self.nccl_group)
+        self.comm.check()
+        t = times.tolist()
+        self.boundary_times[B] = {("F" if a else "S") + ("F" if m else "S"): round(x, 4) for (a, m), x in zip(combos, t)}
+        return combos[min(range(len(combos)), key=lambda k: (t[k], k))]
 
     def start(self, B: int, first_ids: torch.Tensor, prompt_len: int):
         """Set up decoding of B sequences whose prompts (length prompt_len) are in the cache."""
@@ -461,6 +535,8 @@ class TPDecodeRunner:
         torch.cuda.synchronize(self.device)
         for k, v in saved.items():
             buf[k].copy_(v)
+        if self.fuse_boundary and self.tune_boundaries and self.nccl_group is not None and B not in self.fuse_kinds:
+            self.fuse_kinds[B] = self._tune_fusion(B, buf, saved)
         g = torch.cuda.CUDAGraph()
         old = K.set_pdl(self.pdl)
         try:
