@@ -103,6 +103,37 @@ def link_table(rows: list[dict]) -> str:
     return "\n".join(out)
 
 
+LINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this pool's B200s (NVLink 5)
+
+
+def roofline_table(rows: list[dict], link_gbs: float = LINK_GBS) -> tuple[str, list[dict]]:
+    """Achieved fraction of the NVLink roofline per size: the fused op has no FLOPs worth counting, so
+    its target time is the bytes an all-reduce must move per GPU and direction without in-switch
+    reduction, 2 (W - 1) / W S (a one-shot moves (W - 1) S; NVSwitch multicast needs only about S),
+    at `link_gbs`. fraction = target / measured p50 of the fastest of our variants (and of the best
+    baseline); small messages are latency-bound, which the fraction shows."""
+    out = ["| world | tokens | KB | target us | best ours | us | fraction | best baseline | us | fraction |",
+           "|---|---|---|---|---|---|---|---|---|---|"]
+    summary = []
+    for world in sorted({r["world"] for r in rows}):
+        sub = [r for r in rows if r["world"] == world and r.get("correct") and r.get("p50_us")]
+        for T in sorted({r["tokens"] for r in sub}):
+            at = [r for r in sub if r["tokens"] == T]
+            ours = min((r for r in at if r["impl"].startswith("ours") and r["impl"] != "ours:auto"),
+                       key=lambda r: r["p50_us"], default=None)
+            base = min((r for r in at if r["impl"] in BASELINES), key=lambda r: r["p50_us"], default=None)
+            msg = at[0]["bytes"]
+            target = 2 * (world - 1) / world * msg / (link_gbs * 1e3)  # us (GB/s = 1e3 bytes/us)
+            fo = target / ours["p50_us"] if ours else None
+            fb = target / base["p50_us"] if base else None
+            out.append(f"| {world} | {T} | {msg >> 10} | {target:.2f} | " +
+                       (f"{ours['impl']} | {ours['p50_us']:.2f} | {fo:.3f} | " if ours else "- | - | - | ") +
+                       (f"{base['impl']} | {base['p50_us']:.2f} | {fb:.3f} |" if base else "- | - | - |"))
+            summary.append(dict(world=world, tokens=T, target_us=target, ours=ours and ours["impl"],
+                                fraction=fo, baseline=base and base["impl"], baseline_fraction=fb))
+    return "\n".join(out), summary
+
+
 def calibrate(rows: list[dict], table_path: Path | None = None) -> VariantTable:
     """Fastest correct variant (with its geometry) per (world, dtype, hidden, rows bucket)."""
     import torch
@@ -127,6 +158,7 @@ def main():
     ap.add_argument("--calibrate", action="store_true", help="update the committed variant table")
     ap.add_argument("--table", default=None)
     ap.add_argument("--nvlink", action="store_true", help="measured vs expected NVLink bytes per call")
+    ap.add_argument("--roofline", action="store_true", help="achieved fraction of the NVLink roofline per size")
     ap.add_argument("--repeats", nargs=2, metavar=("OURS", "BASELINE"),
                     help="median [min, max] over the given sweeps (independent launches) and the effectiveness rule")
     a = ap.parse_args()
@@ -142,6 +174,9 @@ def main():
         return
     if a.nvlink:
         print(link_table(rows))
+        return
+    if a.roofline:
+        print(roofline_table(rows)[0])
         return
     text, _ = table(rows)
     print(text)
