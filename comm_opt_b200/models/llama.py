@@ -536,7 +536,17 @@ class TPDecodeRunner:
         for k, v in saved.items():
             buf[k].copy_(v)
         if self.fuse_boundary and self.tune_boundaries and self.nccl_group is not None and B not in self.fuse_kinds:
-            self.fuse_kinds[B] = self._tune_fusion(B, buf, saved)
+            try:
+                self.fuse_kinds[B] = self._tune_fusion(B, buf, saved)
+            except RuntimeError as e:
+                # a host-side rejection is the same on every rank (same shapes), so every rank lands
+                # here at the same point: re-initialise the collective state and keep both kinds fused
+                torch.cuda.synchronize(self.device)
+                self.comm.reset()
+                self.fuse_kinds[B] = (True, True)
+                self.fuse_error = f"boundary tuning: {e}"
+                for k, v in saved.items():
+                    buf[k].copy_(v)
         g = torch.cuda.CUDAGraph()
         old = K.set_pdl(self.pdl)
         try:
