@@ -23,7 +23,7 @@ namespace {
 
 namespace cg = cooperative_groups;
 
-constexpr int kD = 128, kBS = 16, kWarps = 4, kRows = 16;
+constexpr int kBS = 16, kWarps = 4, kRows = 16;  // head dims: 64 and 128 (template parameter D)
 constexpr float kLog2e = 1.4426950408889634f;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -83,16 +83,18 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// element offset of 16-byte chunk `ch` of row `r` in the Q tile ([16][kD], chunk ^= row % 8)
-__device__ __forceinline__ int swz(int r, int ch) { return r * kD + ((ch ^ (r & 7)) << 3); }
-// element offset of chunk `ch` (0..15) of row `r` in a KV page loaded by two TMA boxes of 64 columns
-// with the 128-byte swizzle: [2 halves][16 rows][64 cols], chunk-within-half ^= row % 8
+// element offset of 16-byte chunk `ch` of row `r` in the Q tile ([16][D], chunk ^= row % 8)
+template <int D>
+__device__ __forceinline__ int swz(int r, int ch) { return r * D + ((ch ^ (r & 7)) << 3); }
+// element offset of chunk `ch` (0..D/8-1) of row `r` in a KV page loaded by D/64 TMA boxes of 64 columns
+// with the 128-byte swizzle: [D/64 halves][16 rows][64 cols], chunk-within-half ^= row % 8
 __device__ __forceinline__ int swzp(int r, int ch) { return ((ch >> 3) << 10) + r * 64 + (((ch & 7) ^ (r & 7)) << 3); }
 
 __device__ __forceinline__ float safe_exp2_diff(float a, float b) { return a == -INFINITY ? 0.f : exp2f(a - b); }
 
 constexpr int kStages = 3;                    // KV pages in flight per warp
-constexpr int kPageElems = kBS * kD;          // one K (or V) page: 16 x 128
+template <int D>
+constexpr int kPageElems = kBS * D;           // one K (or V) page: 16 x D
 constexpr int kMaxPagesPerSplit = 512;
 
 struct alignas(64) AttnArgs {
@@ -100,22 +102,24 @@ struct alignas(64) AttnArgs {
   AttnParams p;
 };
 
+template <int D>
 __host__ __device__ constexpr size_t attn_smem_bytes() {
-  return 1024 /*align*/ + (size_t)kWarps * kStages * 2 * kPageElems * 2 + (size_t)kRows * kD * 2 +
+  return 1024 /*align*/ + (size_t)kWarps * kStages * 2 * kPageElems<D> * 2 + (size_t)kRows * D * 2 +
          (size_t)kWarps * kStages * 8 + kMaxPagesPerSplit * 4 + 64;
 }
 
 // CLUSTER: the splits of one (sequence, kv head) pair form a thread-block cluster (splits <= 16) and
 // are merged through distributed shared memory; otherwise they are merged through the global
 // scratch by the last split to finish.
-template <typename T, bool CLUSTER>
+template <typename T, bool CLUSTER, int D>
 __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_constant__ AttnArgs args) {
+  constexpr int kD = D, PE = kPageElems<D>;
   using namespace sm100;
   const AttnParams& p = args.p;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   T* sKV = reinterpret_cast<T*>(base);  // [kWarps][kStages][K,V][2 halves][16][64]
-  T* sQ = sKV + (size_t)kWarps * kStages * 2 * kPageElems;
+  T* sQ = sKV + (size_t)kWarps * kStages * 2 * PE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + kRows * kD);  // [kWarps][kStages]
   int* s_pages = reinterpret_cast<int*>(bars + kWarps * kStages);
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -137,7 +141,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
   __syncthreads();  // page list (and the barrier initialisation) visible to every warp
 
-  T* myKV = sKV + (size_t)warp * kStages * 2 * kPageElems;
+  T* myKV = sKV + (size_t)warp * kStages * 2 * PE;
   uint64_t* mybar = bars + warp * kStages;
   // page i of this warp is pg0 + warp + i * kWarps
   const int my_pages = pg1 - pg0 > warp ? (pg1 - pg0 - warp + kWarps - 1) / kWarps : 0;
@@ -146,13 +150,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     const int st = i % kStages;
     const int blk = s_pages[warp + i * kWarps];
     const int row = (blk * p.nkv + kvh) * kBS;
-    T* dk = myKV + (size_t)st * 2 * kPageElems;
-    T* dv = dk + kPageElems;
-    mbar_arrive_expect_tx(&mybar[st], 2 * kPageElems * sizeof(T));
-    tma_load_2d(dk, &args.tk, &mybar[st], 0, row);
-    tma_load_2d(dk + kPageElems / 2, &args.tk, &mybar[st], 64, row);
-    tma_load_2d(dv, &args.tv, &mybar[st], 0, row);
-    tma_load_2d(dv + kPageElems / 2, &args.tv, &mybar[st], 64, row);
+    T* dk = myKV + (size_t)st * 2 * PE;
+    T* dv = dk + PE;
+    mbar_arrive_expect_tx(&mybar[st], 2 * PE * sizeof(T));
+#pragma unroll
+    for (int h = 0; h < D / 64; ++h) {  // boxes of 64 columns (128 bytes, the swizzle span)
+      tma_load_2d(dk + h * kBS * 64, &args.tk, &mybar[st], 64 * h, row);
+      tma_load_2d(dv + h * kBS * 64, &args.tv, &mybar[st], 64 * h, row);
+    }
   };
 #pragma unroll
   for (int i = 0; i < kStages; ++i) issue(i);
@@ -162,14 +167,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     const int r = c / CH, ch = c % CH;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < G) v = reinterpret_cast<const uint4*>(q + (size_t)r * kD)[ch];
-    *reinterpret_cast<uint4*>(sQ + swz(r, ch)) = v;
+    *reinterpret_cast<uint4*>(sQ + swz<D>(r, ch)) = v;
   }
   __syncthreads();
   uint32_t qa[kD / 16][4];
 #pragma unroll
   for (int ks = 0; ks < kD / 16; ++ks) {
     const int r = lane & 15, ch = ks * 2 + (lane >> 4);
-    ldsm_x4(qa[ks], sQ + swz(r, ch));
+    ldsm_x4(qa[ks], sQ + swz<D>(r, ch));
   }
 
   const float sl2 = p.scale * kLog2e;
@@ -187,8 +192,8 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
       if (p.err) atomicOr(p.err, 1);
       break;
     }
-    const T* sK = myKV + (size_t)st * 2 * kPageElems;
-    const T* sV = sK + kPageElems;
+    const T* sK = myKV + (size_t)st * 2 * PE;
+    const T* sV = sK + PE;
     float s[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -390,14 +395,15 @@ size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_di
          pairs * sizeof(int32_t);
 }
 
-cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
-  if (p.head_dim != kD || p.block_size != kBS || p.nkv <= 0 || p.nq % p.nkv != 0 || p.nq / p.nkv > kRows ||
-      p.splits <= 0 || p.pages_per_split <= 0 || p.pages_per_split > kMaxPagesPerSplit || p.batch <= 0 ||
-      (size_t)p.splits * (p.nq / p.nkv) * 2 + kRows > (size_t)kWarps * kStages * 2 * kPageElems / 2 ||
-      (p.dtype != kBF16 && p.dtype != kF16))
-    return cudaErrorInvalidValue;
-  static_assert(kWarps * kRows * kD * 4 + kWarps * kRows * 2 * 4 + kRows * kD * 4 + kRows * 2 * 4 <=
-                    kWarps * kStages * 2 * kPageElems * 2,
+namespace {
+
+template <int D>
+cudaError_t launch_attention(const AttnParams& p, cudaStream_t s) {
+  constexpr int PE = kPageElems<D>;
+  if ((size_t)p.splits * (p.nq / p.nkv) * 2 + kRows > (size_t)kWarps * kStages * 2 * PE / 2)
+    return cudaErrorInvalidValue;  // the global merge's split weights must fit in the KV stages
+  static_assert(kWarps * kRows * D * 4 + kWarps * kRows * 2 * 4 + kRows * D * 4 + kRows * 2 * 4 <=
+                    kWarps * kStages * 2 * PE * 2,
                 "merge buffers must fit in the KV stages");
   AttnArgs a;
   a.p = p;
@@ -405,15 +411,15 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
   // (only rows named by the block tables are ever read)
   const uint64_t rows = (uint64_t)(p.num_blocks > 0 ? p.num_blocks : (1 << 22)) * p.nkv * kBS;
   const bool bf16 = p.dtype == kBF16;
-  cudaError_t e = tensor_map_2d(p.k_cache, rows, kD, kD * 2, kBS, 64, bf16, &a.tk);
+  cudaError_t e = tensor_map_2d(p.k_cache, rows, D, D * 2, kBS, 64, bf16, &a.tk);
   if (e != cudaSuccess) return e;
-  e = tensor_map_2d(p.v_cache, rows, kD, kD * 2, kBS, 64, bf16, &a.tv);
+  e = tensor_map_2d(p.v_cache, rows, D, D * 2, kBS, 64, bf16, &a.tv);
   if (e != cudaSuccess) return e;
-  const size_t smem = attn_smem_bytes();
+  const size_t smem = attn_smem_bytes<D>();
   const dim3 grid(p.splits, p.nkv, p.batch);
   const bool cluster = p.cluster && p.splits > 1 && p.splits <= 16;
-  auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true> : k_decode_attn<__nv_bfloat16, false>)
-                 : (cluster ? k_decode_attn<__half, true> : k_decode_attn<__half, false>);
+  auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true, D> : k_decode_attn<__nv_bfloat16, false, D>)
+                 : (cluster ? k_decode_attn<__half, true, D> : k_decode_attn<__half, false, D>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (cluster && p.splits > 8) {  // clusters of 9..16 CTAs are non-portable (two CTAs per SM here)
@@ -440,6 +446,16 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
   cfg.attrs = attr;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+}  // namespace
+
+cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
+  if ((p.head_dim != 64 && p.head_dim != 128) || p.block_size != kBS || p.nkv <= 0 || p.nq % p.nkv != 0 ||
+      p.nq / p.nkv > kRows || p.splits <= 0 || p.pages_per_split <= 0 || p.pages_per_split > kMaxPagesPerSplit ||
+      p.batch <= 0 || (p.dtype != kBF16 && p.dtype != kF16))
+    return cudaErrorInvalidValue;
+  return p.head_dim == 128 ? launch_attention<128>(p, s) : launch_attention<64>(p, s);
 }
 
 }  // namespace cob

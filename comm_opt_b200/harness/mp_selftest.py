@@ -27,7 +27,8 @@ Parts:
                add/RMSNorm kernel) through the same runner; decode_qkv_bias runs the fused step on the
                Qwen2.5 attention shape (QKV bias, 5 query heads per KV head at 4 ranks); decode_mixed fuses
                only one of the two boundary kinds per layer (attention output or MLP output), the
-               mixes the capture-time tuning may choose (decode_fused runs that tuning).
+               mixes the capture-time tuning may choose (decode_fused runs that tuning); decode_hd64 runs
+               the TinyLlama attention shape (head_dim 64, KV heads replicated across ranks at 4 ranks).
 Rank 0 prints one JSON summary; the exit code is non-zero on any failure.
 """
 from __future__ import annotations
@@ -378,7 +379,9 @@ def main():
              # Qwen2.5-shaped attention: QKV bias, 5 query heads per KV head at 4 ranks
              "decode_qkv_bias": lambda C, dev, world: decode_check(C, dev, world, fused=True, model="tiny-qkv-bias"),
              "decode_mixed": lambda C, dev, world: [decode_check(C, dev, world, fused=True, kinds=k)
-                                                    for k in ((True, False), (False, True))]
+                                                    for k in ((True, False), (False, True))],
+             # TinyLlama-shaped attention: head_dim 64, KV heads replicated when world > 2
+             "decode_hd64": lambda C, dev, world: decode_check(C, dev, world, fused=True, model="tiny-hd64")
              }[part](C, dev, world)
     except Exception:
         err = traceback.format_exc()

@@ -195,7 +195,7 @@ def e2e_share_jobs(ngpus: int = 8, reps: int = 3) -> list[Job]:
     """The reference's M5 matrix (exp/M5_e2e_comm_share/run_train.py:14-16 and run_infer.py): training of
     Llama-3 1B / 8B at TP 8 / 4 / 2 x FSDP ngpus / TP, 8 x 2048 tokens per step, `reps` launches each; and
     the communication share of TP decode (70B, batch 1 / 8 / 128, fused and separate layer boundaries;
-    Qwen2.5-32B shapes, prompt 128, batch 1 / 8 / 32 / 128)."""
+    Qwen2.5-32B and TinyLlama-1.1B shapes, prompt 128, batch 1 / 8 / 32 / 128)."""
     jobs = [Job("train_share", ngpus, variant=f"{m}_tp{tp}", rep=r, timeout_s=1800,
                 args=("--model", m, "--tp", str(tp), "--seq", "2048", "--global-seqs", "8", "--steps", "10",
                       "--profile", "5"))
@@ -204,11 +204,12 @@ def e2e_share_jobs(ngpus: int = 8, reps: int = 3) -> list[Job]:
         for fb in (1, 0):
             jobs.append(Job("comm_share", ngpus, variant=f"70b_b{B}_fb{fb}",
                             args=("--model", "70b", "--batch", str(B), "--fuse-boundary", str(fb))))
-    # the reference's own decode matrix on its model's shapes (exp/M5_e2e_comm_share/run_infer.py:17-18:
-    # Qwen2.5-32B, decode:<batch>:128 for batch 1 / 8 / 32 / 128)
+    # the reference's own decode matrix on its models' shapes (exp/M5_e2e_comm_share/run_infer.py:14-19:
+    # Qwen2.5-32B and TinyLlama-1.1B, decode:<batch>:128 for batch 1 / 8 / 32 / 128)
     for B in (1, 8, 32, 128):
-        jobs.append(Job("comm_share", ngpus, variant=f"qwen32b_b{B}",
-                        args=("--model", "qwen2.5-32b", "--batch", str(B), "--prompt", "128")))
+        for model, tag in (("qwen2.5-32b", "qwen32b"), ("tinyllama-1.1b", "tinyllama")):
+            jobs.append(Job("comm_share", ngpus, variant=f"{tag}_b{B}",
+                            args=("--model", model, "--batch", str(B), "--prompt", "128")))
     return jobs
 
 

@@ -43,9 +43,17 @@ class LlamaConfig:
     qkv_bias: bool = False  # Qwen2-style attention: the QKV projection has a bias
 
     def shard(self, tp: int) -> dict:
-        assert self.heads % tp == 0 and self.kv_heads % tp == 0 and self.inter % tp == 0 and self.vocab % tp == 0, \
+        """Per-rank head counts and sizes. With more ranks than KV heads (tp a multiple of kv_heads) each
+        rank keeps one KV head, replicated on tp / kv_heads ranks (as vLLM shards such models)."""
+        kv_ok = self.kv_heads % tp == 0 or tp % self.kv_heads == 0
+        assert self.heads % tp == 0 and kv_ok and self.inter % tp == 0 and self.vocab % tp == 0, \
             f"{self.name} does not shard {tp} ways"
-        return dict(nq=self.heads // tp, nkv=self.kv_heads // tp, inter=self.inter // tp, vocab=self.vocab // tp)
+        return dict(nq=self.heads // tp, nkv=max(1, self.kv_heads // tp), inter=self.inter // tp,
+                    vocab=self.vocab // tp)
+
+    def kv_head0(self, rank: int, tp: int) -> int:
+        """First KV head held by `rank`: the one its query heads attend to (grouped-query attention)."""
+        return rank * (self.heads // tp) // (self.heads // self.kv_heads)
 
     @property
     def params(self) -> int:
@@ -59,15 +67,19 @@ class LlamaConfig:
 LLAMA3_8B = LlamaConfig("llama3-8b", 4096, 32, 32, 8, 128, 14336, 128256)
 LLAMA3_70B = LlamaConfig("llama3-70b", 8192, 80, 64, 8, 128, 28672, 128256)
 LLAMA3_1B = LlamaConfig("llama3-1b", 2048, 16, 32, 8, 64, 8192, 128256)
+# TinyLlama-1.1B shapes, the smaller model of the reference's end-to-end inference study
+# (exp/M5_e2e_comm_share/run_infer.py:15-16): head_dim 64, 4 KV heads (replicated at TP = 8), vocab 32000.
+TINYLLAMA = LlamaConfig("tinyllama-1.1b", 2048, 22, 32, 4, 64, 5632, 32000, eps=1e-5, rope_theta=10000.0)
 # Qwen2.5-32B-Instruct shapes, the larger model of the reference's end-to-end inference study
 # (exp/M5_e2e_comm_share/run_infer.py:15-19): hidden 5120 is the hidden size of the reference's fused-op
 # measurements; 40 query / 8 KV heads, SwiGLU 27648, vocab 152064, QKV bias, RoPE theta 1e6.
 QWEN25_32B = LlamaConfig("qwen2.5-32b", 5120, 64, 40, 8, 128, 27648, 152064, eps=1e-6, rope_theta=1e6, qkv_bias=True)
 TINY = LlamaConfig("tiny", 1024, 2, 16, 8, 128, 2048, 4096)
 TINY_BIAS = replace(TINY, name="tiny-qkv-bias", heads=20, kv_heads=4, qkv_bias=True)  # 5 query heads per KV head
+TINY_HD64 = replace(TINY, name="tiny-hd64", heads=16, kv_heads=2, head_dim=64)  # KV heads replicated at TP >= 4
 PRESETS = {"llama3-1b": LLAMA3_1B, "1b": LLAMA3_1B, "llama3-8b": LLAMA3_8B, "8b": LLAMA3_8B, "llama3-70b": LLAMA3_70B,
-           "70b": LLAMA3_70B, "qwen2.5-32b": QWEN25_32B, "qwen32b": QWEN25_32B, "tiny": TINY,
-           "tiny-qkv-bias": TINY_BIAS}
+           "70b": LLAMA3_70B, "qwen2.5-32b": QWEN25_32B, "qwen32b": QWEN25_32B, "tinyllama-1.1b": TINYLLAMA,
+           "tinyllama": TINYLLAMA, "tiny": TINY, "tiny-qkv-bias": TINY_BIAS, "tiny-hd64": TINY_HD64}
 
 
 class LayerWeights:
@@ -99,9 +111,11 @@ class LlamaWeights:
             self.final_norm = full["final_norm"].to(device)
             self.lm_head = full["lm_head"].chunk(tp, 0)[tp_rank].contiguous().to(device)
             self.layers = []
+            kv0, nkv = cfg.kv_head0(tp_rank, tp), s["nkv"]
+
             def qkv_rows(t):  # this rank's q, k and v heads of a [(heads + 2 kv_heads) * D, ...] tensor
                 q, k, v = t.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], 0)
-                return torch.cat([q.chunk(tp, 0)[tp_rank], k.chunk(tp, 0)[tp_rank], v.chunk(tp, 0)[tp_rank]], 0)
+                return torch.cat([q.chunk(tp, 0)[tp_rank], k[kv0 * D:(kv0 + nkv) * D], v[kv0 * D:(kv0 + nkv) * D]], 0)
 
             for L in full["layers"]:
                 wqkv = qkv_rows(L["wqkv"])
@@ -118,10 +132,20 @@ class LlamaWeights:
         self.final_norm = norm_w(2)
         self.lm_head = rnd((s["vocab"], H), 3)
         self.layers = []
+        replicated = tp > cfg.kv_heads
+
+        def qkv_weight(k0):
+            if not replicated:
+                return rnd(((s["nq"] + 2 * s["nkv"]) * D, H), k0)
+            # ranks that share a KV head get the same k and v rows (seeded by the head, not the rank)
+            gen.manual_seed(seed * 1_000_003 + (k0 + 7) * 8 + cfg.kv_head0(tp_rank, tp))
+            kv = torch.empty((2 * D, H), dtype=dtype, device=device).normal_(0.0, std, generator=gen)
+            return torch.cat([rnd((s["nq"] * D, H), k0), kv], 0)
+
         for i in range(cfg.layers):
             k0 = 16 + 8 * i
             self.layers.append(LayerWeights(
-                rnd(((s["nq"] + 2 * s["nkv"]) * D, H), k0), rnd((H, s["nq"] * D), k0 + 1),
+                qkv_weight(k0), rnd((H, s["nq"] * D), k0 + 1),
                 rnd((2 * s["inter"], H), k0 + 2), rnd((H, s["inter"]), k0 + 3), norm_w(k0 + 4), norm_w(k0 + 5),
                 rnd(((s["nq"] + 2 * s["nkv"]) * D,), k0 + 6) if cfg.qkv_bias else None))
 

@@ -1,5 +1,6 @@
 """Numerics of the single-GPU decode kernels against plain PyTorch fp32 references."""
 import math
+import os
 
 import pytest
 import torch
@@ -90,7 +91,19 @@ def test_argmax_local_and_combine(cuda):
 @pytest.mark.parametrize("nq,nkv", [(8, 1), (32, 8), (16, 4)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_decode_attention(cuda, nq, nkv, dtype):
-    B, D, bs, maxb = 6, 128, 16, 40
+    check_decode_attention(cuda, nq, nkv, dtype, 128)
+
+
+@pytest.mark.skipif(os.environ.get("COB_EXPERIMENTAL") != "1",
+                    reason="head_dim 64 has not run on a GPU yet; COB_EXPERIMENTAL=1 runs it")
+@pytest.mark.parametrize("nq,nkv", [(4, 1), (32, 4)])
+def test_decode_attention_head_dim_64(cuda, nq, nkv):
+    """TinyLlama-1.1B heads (head_dim 64, 8 query heads per KV head; 4 per rank at TP=8)."""
+    check_decode_attention(cuda, nq, nkv, torch.bfloat16, 64)
+
+
+def check_decode_attention(cuda, nq, nkv, dtype, D):
+    B, bs, maxb = 6, 16, 40
     seq = torch.tensor([1, 15, 16, 17, 300, 640], device=cuda, dtype=torch.int32)
     nblocks = B * maxb
     kc = torch.randn(nblocks, nkv, bs, D, device=cuda).to(dtype)

@@ -145,11 +145,11 @@ def test_e2e_share_plan():
     train = [j for j in jobs if j.entry == "train_share"]
     assert len(train) == 18 and {j.variant for j in train} == {f"{m}_tp{t}" for m in ("1b", "8b") for t in (8, 4, 2)}
     share = [j for j in jobs if j.entry == "comm_share"]
-    assert len(share) == 6 + 4 and {j.variant for j in share if j.variant.startswith("qwen32b")} == {
+    assert len(share) == 6 + 8 and {j.variant for j in share if j.variant.startswith("qwen32b")} == {
         f"qwen32b_b{b}" for b in (1, 8, 32, 128)}
     cmd, _ = command(Job("train_share", 8, variant="8b_tp4"), ROOT / "results" / "x", 29999)
     assert cmd[-1].endswith("runs/train_share_g8A_8b_tp4_r0") and "comm_opt_b200.harness.train_share" in cmd
-    assert len(e2e_share_jobs(4, reps=1)) == 4 + 6 + 4  # TP 8 needs 8 GPUs
+    assert len(e2e_share_jobs(4, reps=1)) == 4 + 6 + 8  # TP 8 needs 8 GPUs
 
 
 def test_nccl_log_summary_and_gpuset_comparison(tmp_path):

@@ -1,5 +1,6 @@
 """CPU tier for the model description, the fp32 oracles and the analyzers (no GPU, no native code)."""
 import json
+from dataclasses import replace
 
 import torch
 
@@ -174,3 +175,34 @@ def test_qwen25_32b_preset_and_bias_sharding():
     # random-init (unsliced) shards carry a bias of the right length too
     own = LlamaWeights(cfg, 1, tp, "cpu", seed=4)
     assert own.layers[0].bqkv.shape == ((nq + 2 * nkv) * D,)
+
+
+def test_tinyllama_kv_head_replication():
+    """TinyLlama-1.1B (the reference's small end-to-end model): at TP = 8 its 4 KV heads are replicated
+    on 2 ranks each; ranks that share a KV head hold the same k / v rows, and its query heads are the
+    ones that attend to that head."""
+    from comm_opt_b200.models.llama import PRESETS, TINYLLAMA
+
+    assert abs(TINYLLAMA.params / 1e9 - 1.10) < 0.01
+    assert TINYLLAMA.shard(8) == dict(nq=4, nkv=1, inter=704, vocab=4000)
+    assert [TINYLLAMA.kv_head0(r, 8) for r in range(8)] == [0, 0, 1, 1, 2, 2, 3, 3]
+    assert [TINYLLAMA.kv_head0(r, 2) for r in range(2)] == [0, 2]
+    cfg = replace(PRESETS["tiny-hd64"], layers=1)
+    full = LlamaWeights.full_random(cfg, device="cpu", seed=3)
+    tp, D = 4, cfg.head_dim
+    parts = [LlamaWeights(cfg, r, tp, "cpu", full=full) for r in range(tp)]
+    w = full["layers"][0]["wqkv"]
+    k_full = w[cfg.heads * D:(cfg.heads + cfg.kv_heads) * D]
+    for r, p in enumerate(parts):
+        wq = p.layers[0].wqkv
+        assert wq.shape[0] == (cfg.heads // tp + 2) * D
+        kv = cfg.kv_head0(r, tp)
+        assert kv * (cfg.heads // cfg.kv_heads) <= r * (cfg.heads // tp) < (kv + 1) * (cfg.heads // cfg.kv_heads)
+        assert torch.equal(wq[cfg.heads // tp * D:(cfg.heads // tp + 1) * D], k_full[kv * D:(kv + 1) * D])
+    assert torch.equal(parts[0].layers[0].wqkv[4 * D:], parts[1].layers[0].wqkv[4 * D:])
+    # random-init shards: replicas of one KV head get the same k / v rows, different q rows
+    own = [LlamaWeights(cfg, r, tp, "cpu", seed=5) for r in (0, 1, 2)]
+    q = cfg.heads // tp * D
+    assert torch.equal(own[0].layers[0].wqkv[q:], own[1].layers[0].wqkv[q:])
+    assert not torch.equal(own[0].layers[0].wqkv[q:], own[2].layers[0].wqkv[q:])
+    assert not torch.equal(own[0].layers[0].wqkv[:q], own[1].layers[0].wqkv[:q])
