@@ -206,3 +206,89 @@ def test_tinyllama_kv_head_replication():
     assert torch.equal(own[0].layers[0].wqkv[q:], own[1].layers[0].wqkv[q:])
     assert not torch.equal(own[0].layers[0].wqkv[q:], own[2].layers[0].wqkv[q:])
     assert not torch.equal(own[0].layers[0].wqkv[:q], own[1].layers[0].wqkv[:q])
+
+
+def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
+    """A TPDecodeRunner whose kernels, GEMMs and collective are recorders (no GPU): the decode step's
+    composition and its kernel count can be checked on CPU."""
+    from types import SimpleNamespace
+
+    import comm_opt_b200.models.llama as M
+
+    calls = []
+
+    class Rec:
+        def __getattr__(self, name):
+            return lambda *a, **k: calls.append(name)
+
+    class Comm:
+        def gemm_push(self, *a, **k):
+            calls.append("gemm_push")
+
+        def ar_norm_gemm(self, *a, epilogue=None, **k):
+            calls.append("ar_norm_gemm" + (f":{epilogue}" if epilogue else ""))
+
+        def fused_allreduce_add_rmsnorm(self, *a, **k):
+            calls.append("fused_ar")
+
+        def all_gather_u32(self, *a, **k):
+            calls.append("all_gather")
+
+    monkeypatch.setattr(M, "K", Rec())
+    cfg = replace(M.TINY, layers=layers)
+    r = object.__new__(M.TPDecodeRunner)
+    r.cfg, r.s, r.tp, r.rank = cfg, cfg.shard(tp), tp, 0
+    r.w = M.LlamaWeights(cfg, 0, tp, "cpu", seed=1)
+    r.comm, r.collective, r.nccl_group, r.gemm = Comm(), "ours", None, "cob"
+    keys = [(i, n) for i in range(layers) for n in ("qkv", "o", "gu", "down")] + ["head"]
+    r.lin = {k: (lambda *a, **kw: calls.append("gemm")) for k in keys}
+    r.cache = SimpleNamespace(block_tables=torch.zeros(4, 8, dtype=torch.int32), k=[None] * layers, v=[None] * layers)
+    r.cos = r.sin = None
+    r.scale = 1.0
+    r.fuse_boundary, r.fuse_kinds, r.fuse_epilogues = fuse, {4: kinds}, any(epi)
+    r._fuse_epi, r._wgu_il = {4: epi}, [None] * layers
+    buf = {k: torch.zeros(4, 8) for k in ("ids", "pos", "lens", "res", "h", "part", "qkv", "q", "attn", "gu", "act",
+                                           "logits")}
+    buf["keys"] = torch.zeros(4, dtype=torch.int64)
+    buf["gathered"] = torch.zeros(tp, 4, dtype=torch.int64)
+    buf["attn_op"] = lambda *a, **k: calls.append("attention")
+    return r, buf, calls
+
+
+def _expected_step(layers, fuse, kinds, epi):
+    fa, fm = kinds if fuse else (False, False)
+    sw, rp = (epi[0] and fa, epi[1] and fm) if fuse else (False, False)
+    seq = ["embedding", "rmsnorm", "gemm"]
+    for i in range(layers):
+        last = i + 1 == layers
+        if i == 0 or not rp:
+            seq.append("rope_append_kv")
+        seq.append("attention")
+        seq += (["gemm_push", "ar_norm_gemm:swiglu" if sw else "ar_norm_gemm"] if fa else
+                ["gemm", "fused_ar", "gemm"])
+        if not sw:
+            seq.append("silu_mul")
+        if fm:
+            seq += ["gemm_push", "ar_norm_gemm:rope_kv" if rp and not last else "ar_norm_gemm"]
+        else:
+            seq += ["gemm", "fused_ar", "gemm"]
+    if not fuse:  # the separate step issues the next layer's QKV GEMM at the top of the layer
+        seq = ["embedding", "rmsnorm"]
+        for i in range(layers):
+            seq += ["gemm", "rope_append_kv", "attention", "gemm", "fused_ar", "gemm", "silu_mul", "gemm", "fused_ar"]
+        seq.append("gemm")
+    return seq + ["argmax_local", "all_gather", "argmax_combine"]
+
+
+def test_decode_step_composition_every_boundary_mix(monkeypatch):
+    """Every mix of fused / separate layer boundaries (and the GEMM epilogues) issues the expected
+    kernel sequence, and the step's kernel count (the bench's `gpu_launches`) matches it."""
+    import itertools
+
+    for fuse in (True, False):
+        for kinds in itertools.product((True, False), repeat=2):
+            for epi in itertools.product((False, True), repeat=2):
+                r, buf, calls = _recording_runner(monkeypatch, 3, 2, fuse, kinds, epi)
+                n = r._step(4, buf)
+                assert calls == _expected_step(3, fuse, kinds, epi), (fuse, kinds, epi)
+                assert n == len(calls), (fuse, kinds, epi, n, len(calls))
