@@ -556,7 +556,8 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
   // ---- phase 2: a warp per (row, unit of the owned slice)
   // LAMPORT: units over all warps of the grid; PULL / NVLS: the block's rows, units over its warps
   const int nunits = MODE == kLamport2S ? p.rows * U : ((p.rows - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) * U;
-  for (int g = (MODE == kLamport2S ? gw : warp); g < nunits; g += (MODE == kLamport2S ? total_warps : NW)) {
+  for (int g = (MODE == kLamport2S ? gw : warp); MODE != kNvls2S && g < nunits;
+       g += (MODE == kLamport2S ? total_warps : NW)) {
     const int row = MODE == kLamport2S ? g / U : (int)blockIdx.x + (g / U) * (int)gridDim.x;
     const int c0 = (g % U) * UV;
     float ss = 0.f;
@@ -571,17 +572,7 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
       for (int q = 0; q < V::N; ++q) a[k][q] = 0.f;
       if (i < sv && p.norm) rv[k] = rr[rank * sv + i];  // issued before the peer data is awaited
     }
-    if (MODE == kNvls2S) {
-      uint4 sred[kChunk];
-#pragma unroll
-      for (int k = 0; k < kChunk; ++k) {
-        const int i = c0 + k * 32 + lane;
-        if (i < sv && ok) sred[k] = mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, row, rank * sv + i) * 16);
-        else sred[k] = make_uint4(0, 0, 0, 0);
-      }
-#pragma unroll
-      for (int k = 0; k < kChunk; ++k) V::to_float(sred[k], a[k]);
-    } else {
+    {
       // every source's vector of every chunk element is requested before any is awaited
       uint4 d[kChunk][W];
 #pragma unroll
@@ -636,19 +627,57 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
       V::to_float(hb, hf);
 #pragma unroll
       for (int q = 0; q < V::N; ++q) ss += hf[q] * hf[q];
-      if (MODE == kNvls2S) {
-        mm_st_v4(p.mc + p.L.hbuf + ((size_t)row * p.L.max_hv + rank * sv + i) * 16, hb);
-      } else {
 #pragma unroll
-        for (int dd = 0; dd < W; ++dd) st_vol_v4(ag_at(p, (rank + dd) % W, slot, rank, row, i), hb);
-      }
+      for (int dd = 0; dd < W; ++dd) st_vol_v4(ag_at(p, (rank + dd) % W, slot, rank, row, i), hb);
     }
     const float part = warp_sum(ss);
     const unsigned long long word = ((unsigned long long)etag << 32) | __float_as_uint(part);
-    if (MODE == kNvls2S) {
-      if (lane == 0) mm_st_u64(p.mc + p.L.hpart + hpart_idx(p, row, rank, g % U) * 8, word);
-    } else if (lane < W) {
-      st_vol_u64(agp_at(p, lane, slot, rank, row, g % U), word);
+    if (lane < W) st_vol_u64(agp_at(p, lane, slot, rank, row, g % U), word);
+  }
+  if (MODE == kNvls2S) {
+    // kNvB units per warp and step: one 16-byte multimem.ld_reduce per lane and unit is a round trip
+    // through the switch, so every unit's load is issued before the first is used (the per-unit
+    // arithmetic, and so the result, is the same as one unit at a time)
+    constexpr int kNvB = 4;
+    for (int g0 = warp; g0 < nunits; g0 += NW * kNvB) {
+      uint4 sred[kNvB], rv[kNvB];
+      int rowj[kNvB];
+#pragma unroll
+      for (int j = 0; j < kNvB; ++j) {
+        const int g = g0 + j * NW, i = (g % U) * UV + lane;
+        rowj[j] = g < nunits ? (int)blockIdx.x + (g / U) * (int)gridDim.x : -1;
+        sred[j] = make_uint4(0, 0, 0, 0);
+        if (rowj[j] >= 0 && i < sv) {
+          if (p.norm) rv[j] = reinterpret_cast<const uint4*>(res + (size_t)rowj[j] * p.hidden)[rank * sv + i];
+          if (ok) sred[j] = mm_ld_reduce<T>(p.mc + p.L.stage + stage_idx(p, slot, rowj[j], rank * sv + i) * 16);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kNvB; ++j) {
+        if (rowj[j] < 0) continue;  // warp-uniform: g depends on the warp only
+        const int g = g0 + j * NW, i = (g % U) * UV + lane;
+        float ss = 0.f;
+        if (i < sv) {
+          float a[V::N];
+          V::to_float(sred[j], a);
+          if (p.norm) {
+            float r[V::N];
+            V::to_float(rv[j], r);
+#pragma unroll
+            for (int q = 0; q < V::N; ++q) a[q] += r[q];
+          }
+          const uint4 hb = LP::clean(V::from_float(a));
+          float hf[V::N];
+          V::to_float(hb, hf);
+#pragma unroll
+          for (int q = 0; q < V::N; ++q) ss += hf[q] * hf[q];
+          mm_st_v4(p.mc + p.L.hbuf + ((size_t)rowj[j] * p.L.max_hv + rank * sv + i) * 16, hb);
+        }
+        const float part = warp_sum(ss);
+        if (lane == 0)
+          mm_st_u64(p.mc + p.L.hpart + hpart_idx(p, rowj[j], rank, g % U) * 8,
+                    ((unsigned long long)etag << 32) | __float_as_uint(part));
+      }
     }
   }
   stamp(p, rank, e, 2);
@@ -659,17 +688,47 @@ __global__ void __launch_bounds__(256) k_twoshot(const ARParams p) {
     const uint32_t nc = st->nvls_calls[blockIdx.x][1] + 1u;
     ok = nvls_barrier(p, rank, st, 1, nc, w) && ok;
     if (tid == 0) st->nvls_calls[blockIdx.x][1] = nc;
-    // phase 3 (NVLS): this block's rows (the barrier covered exactly these rows), a warp per row
-    for (int row = (int)blockIdx.x + warp * (int)gridDim.x; row < p.rows; row += NW * (int)gridDim.x) {
-      float tot = 0.f;
-      if (p.norm && ok && !row_partials<W>(p, rank, slot, row, U, etag, true, w, st, e, tot)) ok = false;
-      const float rstd = rsqrtf(tot / (float)p.hidden + p.eps);
-      for (int v = lane; v < hv; v += 32) {
-        const uint4 hb = ld_vol_v4(p.base[rank] + p.L.hbuf + ((size_t)row * p.L.max_hv + v) * 16);
-        float hf[V::N];
-        V::to_float(hb, hf);
-        store_norm<T>(p, out, res, row, v, hf, hb, rstd);
+    // phase 3 (NVLS): this block's rows (the barrier covered exactly these rows), in groups of up to
+    // 32: first each row's norm from its partial words (a warp per row), then every thread of the
+    // block over the group's vectors with four 16-byte loads (and their gamma vectors) in flight
+    __shared__ float s_rstd[32];
+    const int nrows_b = (p.rows - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    for (int r0 = 0; r0 < nrows_b; r0 += 32) {
+      const int nr = min(32, nrows_b - r0);
+      for (int rl = warp; rl < nr; rl += NW) {
+        const int row = (int)blockIdx.x + (r0 + rl) * (int)gridDim.x;
+        float tot = 0.f;
+        if (p.norm && ok && !row_partials<W>(p, rank, slot, row, U, etag, true, w, st, e, tot)) ok = false;
+        if (lane == 0) s_rstd[rl] = rsqrtf(tot / (float)p.hidden + p.eps);
       }
+      __syncthreads();
+      const int items = nr * hv;
+      for (int i0 = tid; i0 < items; i0 += 4 * NT) {
+        uint4 hb[4], gv[4];
+        int rowk[4], vk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int idx = i0 + k * NT;
+          rowk[k] = -1;
+          if (idx < items) {
+            const int rl = idx / hv;
+            vk[k] = idx - rl * hv;
+            rowk[k] = rl;
+            hb[k] = ld_vol_v4(p.base[rank] + p.L.hbuf +
+                              ((size_t)((int)blockIdx.x + (r0 + rl) * (int)gridDim.x) * p.L.max_hv + vk[k]) * 16);
+            if (p.norm) gv[k] = ld_nc_v4(reinterpret_cast<const uint4*>(p.gamma) + vk[k]);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (rowk[k] < 0) continue;
+          float hf[V::N];
+          V::to_float(hb[k], hf);
+          store_norm<T>(p, out, res, (int)blockIdx.x + (r0 + rowk[k]) * (int)gridDim.x, vk[k], hf, hb[k],
+                        s_rstd[rowk[k]], &gv[k]);
+        }
+      }
+      __syncthreads();  // s_rstd is rewritten by the next group
     }
   } else {
     // phase 3 (LAMPORT/PULL): flat over (row, v), two vectors per lane per step; a warp shares one
