@@ -951,13 +951,16 @@ cudaError_t resolve_config(ARParams& p, int num_sms) {
     p.cluster = 1;
     if (p.blocks <= 0) {
       // LAMPORT: enough CTAs that every (row, unit) has a warp and the flat push / gather phases
-      // have ~1 vector per thread; PULL / NVLS: a CTA per row (their barriers are per CTA); capped
-      // by one resident CTA per SM
+      // have ~1 vector per thread; PULL: a CTA per row for the staging and reduce phases (their
+      // barriers are per CTA), more when the flat all-gather phase wants them (CTAs without a row
+      // pass their barrier and only gather); NVLS: a CTA per row; capped by one resident CTA per SM
       const int warps = p.threads / 32;
       const int units = (hv / p.world + 31) / 32;
       const long long by_units = ((long long)p.rows * units + warps - 1) / warps;
       const long long by_flat = ((long long)p.rows * hv + p.threads - 1) / p.threads;
-      const long long b = p.variant == kLamport2S ? std::max(by_units, by_flat) : (long long)p.rows;
+      const long long b = p.variant == kLamport2S ? std::max(by_units, by_flat)
+                          : p.variant == kPull2S  ? std::max((long long)p.rows, by_flat)
+                                                  : (long long)p.rows;
       p.blocks = (int)std::max<long long>(1, std::min<long long>(b, budget));
     }
   }
