@@ -241,15 +241,16 @@ std::vector<int64_t> py_clock_calibration(int64_t ns, int64_t device) {
 }
 
 std::vector<int64_t> py_prim_layout(int64_t world, int64_t n) {
-  long long f = 0, st = 0, l = 0;
-  const size_t total = cob::prim_heap_bytes((int)world, (int)n, &f, &st, &l);
-  return {(int64_t)total, f, st, l};
+  long long f = 0, st = 0, l = 0, nv = 0;
+  const size_t total = cob::prim_heap_bytes((int)world, (int)n, &f, &st, &l, &nv);
+  return {(int64_t)total, f, st, l, nv};
 }
 
 void py_prim_probe(std::vector<int64_t> bases, std::vector<int64_t> offs, int64_t rank, int64_t n, int64_t mode,
                    int64_t emulate, int64_t blocks, int64_t threads, int64_t timeout_ns, torch::Tensor bad,
-                   torch::Tensor err) {
-  COB_CHECK(bases.size() >= 1 && bases.size() <= 8 && offs.size() == 3, "world 1..8, offsets {flags, stage, land}");
+                   torch::Tensor err, int64_t mc) {
+  COB_CHECK(bases.size() >= 1 && bases.size() <= 8 && (offs.size() == 3 || offs.size() == 4),
+            "world 1..8, offsets {flags, stage, land[, nvls]}");
   COB_CHECK(bad.is_cuda() && bad.scalar_type() == torch::kInt32 && err.is_cuda() && err.scalar_type() == torch::kInt32,
             "bad / err must be CUDA int32");
   cob::PrimParams p = {};
@@ -257,6 +258,8 @@ void py_prim_probe(std::vector<int64_t> bases, std::vector<int64_t> offs, int64_
   p.flags_off = offs[0];
   p.stage_off = offs[1];
   p.land_off = offs[2];
+  p.nvls_off = offs.size() == 4 ? offs[3] : 0;
+  p.mc = reinterpret_cast<char*>(mc);
   p.rank = (int)rank;
   p.world = (int)bases.size();
   p.n = (int)n;
@@ -314,7 +317,10 @@ void py_line_probe(std::vector<int64_t> bases, int64_t heap_bytes, int64_t lines
 void register_ops(pybind11::module& m) {
   m.def("line_probe", &py_line_probe);
   m.def("prim_layout", &py_prim_layout);
-  m.def("prim_probe", &py_prim_probe);
+  m.def("prim_probe", &py_prim_probe, pybind11::arg("bases"), pybind11::arg("offs"), pybind11::arg("rank"),
+        pybind11::arg("n"), pybind11::arg("mode"), pybind11::arg("emulate"), pybind11::arg("blocks"),
+        pybind11::arg("threads"), pybind11::arg("timeout_ns"), pybind11::arg("bad"), pybind11::arg("err"),
+        pybind11::arg("mc") = 0);
   m.def("rs_atomic_probe", &py_rs_atomic_probe);
   m.def("clock_calibration", &py_clock_calibration);
   m.def("gemm", &py_gemm);

@@ -111,6 +111,14 @@ __device__ __forceinline__ uint32_t ld_vol_u32p(const uint32_t* p) {
 __device__ __forceinline__ void st_vol_u32p(uint32_t* p, uint32_t v) {
   asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ __forceinline__ uint32_t mm_ld_reduce_add_u32(const void* mc) {
+  uint32_t v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.u32 %0, [%1];" : "=r"(v) : "l"(mc) : "memory");
+  return v;
+}
+__device__ __forceinline__ void mm_st_u32(void* mc, uint32_t v) {
+  asm volatile("multimem.st.relaxed.sys.global.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
+}
 
 __global__ void __launch_bounds__(1024) k_prim(const PrimParams p) {
   const int rank = p.emulate ? (int)blockIdx.y : p.rank;
@@ -134,7 +142,43 @@ __global__ void __launch_bounds__(1024) k_prim(const PrimParams p) {
     if (t0 == 0) t0 = t;
     return t - t0 > p.timeout_ns;
   };
-  if (p.mode == kAgPull || p.mode == kRsPull) {
+  if (p.mode == kRsNvls || p.mode == kAgNvls) {
+    // same thread -> in-slice index mapping on every rank, so block b's barrier covers every word
+    // that block b then reads
+    if (p.mode == kRsNvls) {
+      for (int d = 0; d < W; ++d)
+        for (int i = tid; i < S; i += nthreads) stage(rank)[d * S + i] = prim_word(rank, d * S + i, e);
+    } else {
+      for (int i = tid; i < S; i += nthreads)
+        mm_st_u32(p.mc + p.stage_off + ((size_t)slot * p.n + (size_t)rank * S + i) * 4, prim_word(rank, rank * S + i, e));
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {  // multicast barrier of block b: one add per rank and call
+      const size_t off = (size_t)p.nvls_off + (size_t)blockIdx.x * 4;
+      mm_red_add_u32(p.mc + off, 1u);
+      const uint32_t target = (uint32_t)e * (uint32_t)W;
+      uint32_t spins = 0;
+      while ((int)(ld_acquire_u32(p.base[rank] + off) - target) < 0) {
+        if (expired(spins)) {
+          atomicOr(p.err, 1);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    if (p.mode == kRsNvls) {
+      for (int i = tid; i < S; i += nthreads) {
+        const uint32_t acc = mm_ld_reduce_add_u32(p.mc + p.stage_off + ((size_t)slot * p.n + (size_t)rank * S + i) * 4);
+        uint32_t want = 0;
+        for (int src = 0; src < W; ++src) want += prim_word(src, rank * S + i, e);
+        bad += acc != want;
+      }
+    } else {
+      for (int src = 0; src < W; ++src)
+        for (int i = tid; i < S; i += nthreads) bad += ld_vol_u32p(stage(rank) + src * S + i) != prim_word(src, src * S + i, e);
+    }
+  } else if (p.mode == kAgPull || p.mode == kRsPull) {
     // stage: AG contributes this rank's slice, RS the whole vector, slice by slice, so that thread
     // `tid` of every rank handles the same in-slice indices (the flag barrier is per block)
     for (int d = (p.mode == kAgPull ? rank : 0); d < (p.mode == kAgPull ? rank + 1 : W); ++d)
@@ -404,16 +448,19 @@ cudaError_t line_check(const LineProbeParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
-size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off) {
+size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off,
+                       long long* nvls_off) {
   auto up = [](long long v) { return (v + 4095) / 4096 * 4096; };
   *flags_off = up(8LL * kPrimMaxBlocks);
-  *stage_off = *flags_off + up(8LL * kPrimMaxBlocks * 8);
+  *nvls_off = *flags_off + up(8LL * kPrimMaxBlocks * 8);
+  *stage_off = *nvls_off + up(4LL * kPrimMaxBlocks);
   *land_off = *stage_off + up(2LL * n * 4);
   return (size_t)(*land_off + up(2LL * 8 * (n / world) * 4));
 }
 
 cudaError_t prim_probe(const PrimParams& p, int blocks, int threads, cudaStream_t s) {
-  if (p.world < 1 || p.world > 8 || p.n <= 0 || p.n % p.world || p.mode < 0 || p.mode > 3) return cudaErrorInvalidValue;
+  if (p.world < 1 || p.world > 8 || p.n <= 0 || p.n % p.world || p.mode < 0 || p.mode > 5) return cudaErrorInvalidValue;
+  if ((p.mode == kRsNvls || p.mode == kAgNvls) && (p.mc == nullptr || p.emulate)) return cudaErrorNotSupported;
   if (blocks < 1 || blocks > kPrimMaxBlocks || threads < 32 || threads > 1024 || threads % 32) return cudaErrorInvalidValue;
   // blocks wait for blocks of other ranks (and, emulated, of the same launch): all must be resident
   int dev = 0, sms = 0, per_sm = 0;

@@ -24,18 +24,25 @@ cudaError_t rs_atomic_probe(const RsProbeParams& p, int blocks, cudaStream_t s);
 //   flags: u64 [kPrimMaxBlocks][8]            flag-barrier slots written by peers (pull forms)
 //   stage: u32 [2][n]                         staged input for the pull forms (by epoch parity)
 //   land : u32 [2][8][n / world]              Lamport landing for the push forms (sentinel 0x80000000)
+//   nvls : u32 [kPrimMaxBlocks]               multicast-barrier counters (NVSwitch forms)
 // Payload words are a hash of (source rank, index, epoch) so data of an earlier call is detected.
+// NVSwitch forms: RS stages the whole vector and reduces its own slice in the switch
+// (multimem.ld_reduce.add.u32); AG stores its slice into every rank's stage through the switch
+// (multimem.st); both meet at a per-block multicast barrier (one multimem.red per rank, wait for
+// epoch x world on the local copy, so a heap runs either these forms or the others, not both).
 constexpr int kPrimMaxBlocks = 256;
-enum PrimMode : int { kAgPull = 0, kAgPush = 1, kRsPull = 2, kRsPush = 3 };
+enum PrimMode : int { kAgPull = 0, kAgPush = 1, kRsPull = 2, kRsPush = 3, kRsNvls = 4, kAgNvls = 5 };
 struct PrimParams {
   char* base[8];
-  long long flags_off, stage_off, land_off;  // byte offsets in every heap
+  char* mc;                                  // multicast view of the heaps (NVSwitch forms), or nullptr
+  long long flags_off, stage_off, land_off, nvls_off;  // byte offsets in every heap
   int rank, world, n, mode, emulate;
   unsigned long long timeout_ns;
   unsigned int* bad;  // [ranks] words whose value did not match the expected payload
   int* err;           // set on a timed-out wait
 };
-size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off);
+size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_off, long long* land_off,
+                       long long* nvls_off);
 cudaError_t prim_probe(const PrimParams& p, int blocks, int threads, cudaStream_t s);
 // Line-atomicity probe (the premise behind LL128-style flag-in-line protocols): writer ranks hit every
 // 128-byte line (32 u32 words; word 31 is the line's flag) of the target rank's buffer with one warp-wide

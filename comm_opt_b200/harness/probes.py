@@ -94,7 +94,8 @@ def run_rs(world: int, n: int, variant: int, dev, emulate: bool, blocks: int = 6
                 push_gbs=round((world - 1) * n * es / t / 1e3, 1), rel_err=rel, timeout=bool(e))
 
 
-PRIM_MODES = {0: "ag_pull", 1: "ag_push", 2: "rs_pull", 3: "rs_push"}
+PRIM_MODES = {0: "ag_pull", 1: "ag_push", 2: "rs_pull", 3: "rs_push", 4: "rs_nvls", 5: "ag_nvls"}
+NVLS_MODES = (4, 5)  # NVSwitch multicast (multimem.ld_reduce / multimem.st): real ranks with a multicast heap
 
 
 def run_prim(world: int, n: int, mode: int, dev, emulate: bool, blocks: int = 64, threads: int = 256,
@@ -102,9 +103,14 @@ def run_prim(world: int, n: int, mode: int, dev, emulate: bool, blocks: int = 64
     """Steady state (the reference's M13 'steady' mode): `graph_ops` launches per CUDA graph on buffers
     that are never cleared between launches; every word is checked against its (rank, index, epoch)
     hash inside the kernel. n = 32-bit words per rank (AG: n / world contributed, n gathered; RS: n
-    contributed, n / world reduced). Returns per-op p50 us (max over ranks) and the mismatch count."""
+    contributed, n / world reduced). Returns per-op p50 us (max over ranks) and the mismatch count.
+    The NVSwitch forms (modes 4, 5) need real ranks and a heap bound to a multicast object; without one
+    the row says so instead of a time."""
     C = native()
-    total, f_off, st_off, l_off = C.prim_layout(world, n)
+    total, f_off, st_off, l_off, nv_off = C.prim_layout(world, n)
+    if mode in NVLS_MODES and emulate:
+        return dict(mode=PRIM_MODES[mode], world=world, emulated=True, words=n, skip="multicast needs real ranks")
+    mc = 0
     rank = 0 if emulate else dist.get_rank(group)
     S = n // world
     if emulate:
@@ -118,15 +124,20 @@ def run_prim(world: int, n: int, mode: int, dev, emulate: bool, blocks: int = 64
         heap = symm_mem.empty(total, dtype=torch.uint8, device=dev)
         heap.zero_()
         heap[l_off:].view(torch.int32).fill_(-2 ** 31)
-        bases = list(symm_mem.rendezvous(heap, group or dist.group.WORLD).buffer_ptrs)
+        hdl = symm_mem.rendezvous(heap, group or dist.group.WORLD)
+        bases = list(hdl.buffer_ptrs)
+        mc = int(getattr(hdl, "multicast_ptr", 0) or 0)
+        if mode in NVLS_MODES and not mc:  # every rank takes this branch alike (same heap kind)
+            dist.barrier(group=group)
+            return dict(mode=PRIM_MODES[mode], world=world, emulated=False, words=n, skip="no multicast object")
         torch.cuda.synchronize()
         dist.barrier(group=group)
     bad = torch.zeros(world if emulate else 1, dtype=torch.int32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
 
     def call():
-        C.prim_probe(bases, [f_off, st_off, l_off], rank, n, mode, int(emulate), blocks, threads,
-                     int(timeout_ms * 1e6), bad, err)
+        C.prim_probe(bases, [f_off, st_off, l_off, nv_off], rank, n, mode, int(emulate), blocks, threads,
+                     int(timeout_ms * 1e6), bad, err, mc)
 
     for _ in range(3):
         call()
@@ -156,7 +167,10 @@ def run_prim(world: int, n: int, mode: int, dev, emulate: bool, blocks: int = 64
         dist.all_reduce(tt, op=dist.ReduceOp.MAX, group=group)
         t, nbad, nerr = [float(v) for v in tt.cpu()]
         dist.barrier(group=group)
-    moved = (world - 1) * S * 4  # bytes each rank sends over NVLink per call
+    # NVLink bytes per GPU and call in the busier direction: (W - 1) slices for the peer forms; the whole
+    # vector for the switch forms (ld_reduce pulls every GPU's part of every rank's slice through the
+    # switch; multimem.st brings every slice, the own one included, back from the switch)
+    moved = (world - 1) * S * 4 if mode not in NVLS_MODES else world * S * 4
     return dict(mode=PRIM_MODES[mode], world=world, emulated=emulate, words=n, us=round(t, 2),
                 link_gbs=round(moved / t / 1e3, 1), bad_words=int(nbad), timeout=bool(nerr),
                 calls=3 + graph_ops * (replays + 1))

@@ -180,3 +180,21 @@ def test_streamk_gemm_plans():
                     assert tiles == -(-N // 128) and 1 <= ctas <= min(148, total)
                     assert -(-KT * ctas // total) + 1 <= 48
                     assert ws == ctas * 2 * 128 * bn * 4
+
+
+@pytest.mark.skipif(not available(), reason="native extension not built")
+def test_primitive_probe_heap_and_multicast_modes():
+    """Probe heap regions in order (epochs, flags, multicast-barrier counters, stage, landing) and large
+    enough; the NVSwitch modes are refused without real ranks (no multicast object when emulated)."""
+    from comm_opt_b200._ext import native
+    from comm_opt_b200.harness.probes import NVLS_MODES, PRIM_MODES, run_prim
+
+    for world in (2, 4, 8):
+        n = 4096 * world
+        total, f, st, land, nv = native().prim_layout(world, n)
+        assert 0 < f < nv < st < land < total
+        assert nv - f >= 8 * 256 * 8 and st - nv >= 4 * 256 and land - st >= 2 * n * 4
+        assert total - land >= 2 * 8 * (n // world) * 4
+    assert {PRIM_MODES[m] for m in NVLS_MODES} == {"rs_nvls", "ag_nvls"}
+    r = run_prim(4, 4096 * 4, 4, "cpu", emulate=True)
+    assert r["skip"] and r["mode"] == "rs_nvls"
