@@ -96,6 +96,7 @@ constexpr int kStages = 3;                    // KV pages in flight per warp
 template <int D>
 constexpr int kPageElems = kBS * D;           // one K (or V) page: 16 x D
 constexpr int kMaxPagesPerSplit = 512;
+constexpr int kMaxClusterSplits = 16;         // splits merged inside one (non-portable) cluster
 
 struct alignas(64) AttnArgs {
   CUtensorMap tk, tv;  // K / V caches as 2-D [num_blocks * nkv * 16, 128], box 64 x 16, 128-byte swizzle
@@ -318,18 +319,33 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   if (CLUSTER) {
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    const int cs = p.splits, r = split;  // cluster spans the splits of this pair
+    const int cs = p.splits, r = split;  // cluster spans the splits of this pair (<= kMaxClusterSplits)
+    // every split's (max, sum) per query row, copied once into this CTA's shared memory (one DSMEM
+    // load per thread, all in flight together), then each output element's partials of all splits
+    // requested together; sums in split order, as one pass over the splits would give
+    float* sMLall = cML + kRows * 2;  // [cs][G][2], past the buffers the peers read
+    for (int i = threadIdx.x; i < cs * G * 2; i += blockDim.x) {
+      const int c = i / (G * 2);
+      sMLall[i] = cluster.map_shared_rank(cML, c)[i - c * G * 2];
+    }
+    __syncthreads();
     const int per = (G * kD + cs - 1) / cs;
     for (int idx = r * per + threadIdx.x; idx < min(G * kD, (r + 1) * per); idx += blockDim.x) {
       const int g = idx / kD;
+      float ov[kMaxClusterSplits];
+#pragma unroll
+      for (int c = 0; c < kMaxClusterSplits; ++c)
+        if (c < cs) ov[c] = cluster.map_shared_rank(cO, c)[idx];
       float M = -INFINITY;
-      for (int c = 0; c < cs; ++c) M = fmaxf(M, cluster.map_shared_rank(cML, c)[g * 2]);
+      for (int c = 0; c < cs; ++c) M = fmaxf(M, sMLall[(c * G + g) * 2]);
       float L = 0.f, O = 0.f;
-      for (int c = 0; c < cs; ++c) {
-        const float* ml = cluster.map_shared_rank(cML, c);
-        const float f = safe_exp2_diff(ml[g * 2], M);
-        L += f * ml[g * 2 + 1];
-        O += f * cluster.map_shared_rank(cO, c)[idx];
+#pragma unroll
+      for (int c = 0; c < kMaxClusterSplits; ++c) {
+        if (c < cs) {
+          const float f = safe_exp2_diff(sMLall[(c * G + g) * 2], M);
+          L += f * sMLall[(c * G + g) * 2 + 1];
+          O += f * ov[c];
+        }
       }
       out[idx] = from_f<T>(O / L);
     }
@@ -402,7 +418,8 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s) {
   constexpr int PE = kPageElems<D>;
   if ((size_t)p.splits * (p.nq / p.nkv) * 2 + kRows > (size_t)kWarps * kStages * 2 * PE / 2)
     return cudaErrorInvalidValue;  // the global merge's split weights must fit in the KV stages
-  static_assert(kWarps * kRows * D * 4 + kWarps * kRows * 2 * 4 + kRows * D * 4 + kRows * 2 * 4 <=
+  static_assert(kWarps * kRows * D * 4 + kWarps * kRows * 2 * 4 + kRows * D * 4 + kRows * 2 * 4 +
+                        kMaxClusterSplits * kRows * 2 * 4 <=
                     kWarps * kStages * 2 * PE * 2,
                 "merge buffers must fit in the KV stages");
   AttnArgs a;
@@ -417,7 +434,7 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   const size_t smem = attn_smem_bytes<D>();
   const dim3 grid(p.splits, p.nkv, p.batch);
-  const bool cluster = p.cluster && p.splits > 1 && p.splits <= 16;
+  const bool cluster = p.cluster && p.splits > 1 && p.splits <= kMaxClusterSplits;
   auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true, D> : k_decode_attn<__nv_bfloat16, false, D>)
                  : (cluster ? k_decode_attn<__half, true, D> : k_decode_attn<__half, false, D>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
