@@ -135,11 +135,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     fence_barrier_init();
   }
   pdl_wait_then_trigger();  // the next kernel (the o_proj GEMM) may start streaming its weights
+  // the split's page-table entries do not depend on the sequence length: they are requested together
+  // with it (entries past the sequence are never used)
+  const int pg0 = split * p.pages_per_split;
+  const int pg_cap = min(p.pages_per_split, p.max_blocks_per_seq - pg0);
+  for (int i = threadIdx.x; i < pg_cap; i += blockDim.x)
+    s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
   const int seq = p.seq_lens[b];
   const int npages = (seq + kBS - 1) / kBS;
-  const int pg0 = split * p.pages_per_split, pg1 = min(npages, pg0 + p.pages_per_split);
-  for (int i = threadIdx.x; i < pg1 - pg0; i += blockDim.x)
-    s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
+  const int pg1 = min(npages, pg0 + p.pages_per_split);
   __syncthreads();  // page list (and the barrier initialisation) visible to every warp
 
   T* myKV = sKV + (size_t)warp * kStages * 2 * PE;
