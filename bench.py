@@ -42,8 +42,9 @@ def parse():
     p.add_argument("--batch", type=int, default=8)
     p.add_argument("--prompt", type=int, default=2048)
     p.add_argument("--gemm", choices=["cob", "torch"], default="cob")
-    p.add_argument("--collective", choices=["ours", "nccl"], default="ours",
-                   help="nccl: the same runner with NCCL all-reduce + add/RMSNorm kernel (baseline decode step)")
+    p.add_argument("--collective", choices=["ours", "nccl", "vllm"], default="ours",
+                   help="nccl: the same runner with NCCL all-reduce + add/RMSNorm kernel (baseline decode step); "
+                        "vllm: vLLM custom all-reduce + vLLM fused_add_rms_norm (the reference's baseline stack)")
     p.add_argument("--fuse-epilogues", type=int, choices=[0, 1], default=0,
                    help="with fused boundaries: SiLU * up and RoPE + KV append in the consumer GEMMs")
     p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=1,
@@ -161,8 +162,9 @@ def main():
     t0 = time.time()
     weights = LlamaWeights(cfg, rank, world, dev, seed=0)
     comm = TPCommunicator(group, device=dev, dtype=torch.bfloat16, max_rows=max(B, 8), max_hidden=cfg.hidden)
+    car_group = dist.new_group(backend="gloo") if args.collective == "vllm" and world > 1 else None
     runner = TPDecodeRunner(cfg, weights, comm, max_batch=B, max_seq=max_seq, device=dev, gemm=args.gemm,
-                            nccl_group=group, fuse_boundary=bool(args.fuse_boundary),
+                            nccl_group=group, car_group=car_group, fuse_boundary=bool(args.fuse_boundary),
                             fuse_epilogues=bool(args.fuse_epilogues), collective=args.collective,
                             tune_boundaries=bool(args.tune_boundaries))
     prompts = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(1234))

@@ -24,7 +24,8 @@ Parts:
   decode_fused - the same with the layer boundaries fused (GEMM push epilogue -> all-reduce + RMSNorm
                inside the next GEMM); decode_fused_epi also moves SiLU * up and RoPE + KV append
                into the consumer GEMMs' epilogues; decode_nccl runs the baseline step (NCCL all-reduce +
-               add/RMSNorm kernel) through the same runner; decode_qkv_bias runs the fused step on the
+               add/RMSNorm kernel) through the same runner, decode_vllm the reference's baseline stack (vLLM
+               custom all-reduce + vLLM fused_add_rms_norm); decode_qkv_bias runs the fused step on the
                Qwen2.5 attention shape (QKV bias, 5 query heads per KV head at 4 ranks); decode_mixed fuses
                only one of the two boundary kinds per layer (attention output or MLP output), the
                mixes the capture-time tuning may choose (decode_fused runs that tuning); decode_hd64 runs
@@ -308,7 +309,9 @@ def decode_check(C: Checker, dev, world, fused: bool = False, epilogues: bool = 
     full = LlamaWeights.full_random(cfg, device=dev, seed=3)
     w = LlamaWeights(cfg, dist.get_rank(), world, dev, full=full)
     comm = TPCommunicator(dist.group.WORLD, device=dev, dtype=torch.bfloat16, max_rows=8, max_hidden=cfg.hidden)
+    car_group = dist.new_group(backend="gloo") if collective == "vllm" else None
     runner = TPDecodeRunner(cfg, w, comm, max_batch=4, max_seq=96, device=dev, nccl_group=dist.group.WORLD,
+                            car_group=car_group,
                             fuse_boundary=fused, fuse_epilogues=epilogues, collective=collective,
                             tune_boundaries=kinds is None)
     if kinds is not None:  # a fixed mix of fused and separate boundaries instead of the timed choice
@@ -381,6 +384,7 @@ def main():
              "decode_fused": lambda C, dev, world: decode_check(C, dev, world, fused=True),
              "decode_fused_epi": lambda C, dev, world: decode_check(C, dev, world, fused=True, epilogues=True),
              "decode_nccl": lambda C, dev, world: decode_check(C, dev, world, collective="nccl"),
+             "decode_vllm": lambda C, dev, world: decode_check(C, dev, world, collective="vllm"),
              # Qwen2.5-shaped attention: QKV bias, 5 query heads per KV head at 4 ranks
              "decode_qkv_bias": lambda C, dev, world: decode_check(C, dev, world, fused=True, model="tiny-qkv-bias"),
              "decode_mixed": lambda C, dev, world: [decode_check(C, dev, world, fused=True, kinds=k)

@@ -175,7 +175,7 @@ def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
                               "--dtype", "float16", "--tokens", "1,2,4,8,16,32,64,128", "--replays", "20")))
         jobs.append(Job("boundary", g))
         for variant, extra in (("fused", ()), ("separate", ("--fuse-boundary", "0")),
-                               ("nccl", ("--collective", "nccl"))):
+                               ("nccl", ("--collective", "nccl")), ("vllm", ("--collective", "vllm"))):
             jobs.append(Job("bench", g, variant=variant, args=("--steps", "64", "--warmup", "4", *extra)))
     for B in batches:
         if B != 8:

@@ -16,6 +16,7 @@ row-parallel, the LM head is vocab-parallel, the embedding table is replicated (
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass, replace
 
@@ -221,7 +222,8 @@ class TPDecodeRunner:
 
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
                  device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
-                 fuse_epilogues: bool = False, collective: str = "ours", tune_boundaries: bool = True):
+                 fuse_epilogues: bool = False, collective: str = "ours", tune_boundaries: bool = True,
+                 car_group=None):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -246,9 +248,22 @@ class TPDecodeRunner:
         # all-reduce landing buffers, and the all-reduce + residual + RMSNorm runs inside the next
         # GEMM (gate_up, the next layer's qkv, the LM head); needs TP > 1, bf16 and this package's GEMMs
         # "ours": the fused all-reduce + residual + RMSNorm kernel; "nccl": the baseline decode step, NCCL
-        # all-reduce (captured in the graph) followed by this package's add + RMSNorm kernel
-        assert collective in ("ours", "nccl")
+        # all-reduce (captured in the graph) followed by this package's add + RMSNorm kernel; "vllm": the
+        # reference's baseline stack, vLLM's custom all-reduce (NCCL where vLLM declines a size, as vLLM
+        # does) followed by vLLM's fused_add_rms_norm; it needs a gloo group (`car_group`) for vLLM's
+        # buffer exchange
+        assert collective in ("ours", "nccl", "vllm")
         self.collective = collective
+        self._car = self._vllm_ops = None
+        if collective == "vllm" and self.tp > 1:
+            import vllm._custom_ops  # noqa: F401  registers torch.ops._C
+            from vllm.distributed.device_communicators.custom_all_reduce import CustomAllreduce
+
+            assert car_group is not None, "collective='vllm' needs a gloo process group (car_group)"
+            self._vllm_ops = torch.ops._C
+            self._car = CustomAllreduce(car_group, self.device, max_size=max(8 << 20, 2 * max_batch * cfg.hidden * 2))
+            if self._car.disabled:
+                raise RuntimeError("vLLM custom all-reduce is disabled on this system")
         self.fuse_boundary = bool(fuse_boundary and self.tp > 1 and self.dtype == torch.bfloat16 and gemm == "cob"
                                   and collective == "ours")
         self.fuse_error = ""
@@ -354,22 +369,24 @@ class TPDecodeRunner:
         K.rmsnorm(buf["res"], w.layers[0].ln1, cfg.eps, out=buf["h"])
         n += 2
         ours = 1 if self.gemm == "cob" else 0
+        ar_ours = 0 if self._car is not None else 1  # the vLLM stack's two kernels per boundary are not ours
         if self.fuse_boundary:
             return n + self._step_fused(B, buf, bt)
+        h = buf["h"]
         for i, L in enumerate(w.layers):
-            self.lin[(i, "qkv")](buf["h"], out=buf["qkv"])
+            self.lin[(i, "qkv")](h, out=buf["qkv"])
             K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
                              self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
             buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
             self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
-            self._allreduce_add_rmsnorm(buf, L.ln2)
-            self.lin[(i, "gu")](buf["h"], out=buf["gu"])
+            h = self._allreduce_add_rmsnorm(buf, L.ln2)
+            self.lin[(i, "gu")](h, out=buf["gu"])
             K.silu_mul(buf["gu"], out=buf["act"])
             self.lin[(i, "down")](buf["act"], out=buf["part"])
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
-            self._allreduce_add_rmsnorm(buf, nxt)
-            n += 5 + 4 * ours
-        self.lin["head"](buf["h"], out=buf["logits"])
+            h = self._allreduce_add_rmsnorm(buf, nxt)
+            n += 3 + 2 * ar_ours + 4 * ours
+        self.lin["head"](h, out=buf["logits"])
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         n += 1 + ours
         if self.tp > 1:
@@ -379,15 +396,23 @@ class TPDecodeRunner:
                          positions=buf["pos"], seq_lens=buf["lens"], local_keys=buf["keys"])
         return n + 1
 
-    def _allreduce_add_rmsnorm(self, buf: dict, gamma: torch.Tensor):
-        """h = RMSNorm(residual + sum_ranks(part)) * gamma, residual updated (one or two kernels)."""
-        if self.collective == "nccl" and self.tp > 1:
+    def _allreduce_add_rmsnorm(self, buf: dict, gamma: torch.Tensor) -> torch.Tensor:
+        """h = RMSNorm(residual + sum_ranks(part)) * gamma, residual updated (one or two kernels). Returns
+        the tensor that holds h: buf["h"], or on the vLLM path the all-reduce's own output."""
+        if self.tp > 1 and self.collective in ("nccl", "vllm"):
             import torch.distributed as dist
 
-            dist.all_reduce(buf["part"], group=self.nccl_group)
-            K.add_rmsnorm(buf["part"], buf["res"], gamma, self.cfg.eps, out=buf["h"])
-        else:
-            self.comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], gamma, self.cfg.eps, out=buf["h"])
+            out = self._car.custom_all_reduce(buf["part"]) if self._car is not None else None
+            if out is None:  # NCCL (the "nccl" step, or a size vLLM's custom all-reduce declines)
+                dist.all_reduce(buf["part"], group=self.nccl_group)
+                out = buf["part"]
+            if self._car is not None:
+                self._vllm_ops.fused_add_rms_norm(out, buf["res"], gamma, self.cfg.eps)
+                return out
+            K.add_rmsnorm(out, buf["res"], gamma, self.cfg.eps, out=buf["h"])
+            return buf["h"]
+        self.comm.fused_allreduce_add_rmsnorm(buf["part"], buf["res"], gamma, self.cfg.eps, out=buf["h"])
+        return buf["h"]
 
     def _fused_epilogues(self, B: int, buf: dict) -> tuple[bool, bool]:
         """(swiglu in the gate_up GEMM, RoPE + KV append in the QKV GEMM) for batch B: used when the
@@ -437,8 +462,8 @@ class TPDecodeRunner:
                 n += 2
             else:
                 self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
-                self._allreduce_add_rmsnorm(buf, L.ln2)
-                self.lin[(i, "gu")](buf["h"], out=buf["gu"])
+                h = self._allreduce_add_rmsnorm(buf, L.ln2)
+                self.lin[(i, "gu")](h, out=buf["gu"])
                 n += 3
             if not sw:
                 K.silu_mul(buf["gu"], out=buf["act"])
@@ -461,11 +486,11 @@ class TPDecodeRunner:
                 n += 2
             else:
                 self.lin[(i, "down")](buf["act"], out=buf["part"])
-                self._allreduce_add_rmsnorm(buf, gamma)
+                h = self._allreduce_add_rmsnorm(buf, gamma)
                 if last:
-                    self.lin["head"](buf["h"], out=buf["logits"])
+                    self.lin["head"](h, out=buf["logits"])
                 else:
-                    self.lin[(i + 1, "qkv")](buf["h"], out=buf["qkv"])
+                    self.lin[(i + 1, "qkv")](h, out=buf["qkv"])
                 n += 3
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         comm.all_gather_u32(buf["keys"].view(torch.int32), out=buf["gathered"].view(torch.int32).view(self.tp, 2 * B))
@@ -574,8 +599,10 @@ class TPDecodeRunner:
         g = torch.cuda.CUDAGraph()
         old = K.set_pdl(self.pdl)
         try:
-            with torch.cuda.graph(g):
-                self.kernels_per_step[B] = self._step(B, buf)
+            # vLLM registers the buffers its all-reduce used in the graph when its capture context ends
+            with (self._car.capture() if self._car is not None else contextlib.nullcontext()):
+                with torch.cuda.graph(g):
+                    self.kernels_per_step[B] = self._step(B, buf)
         finally:
             K.set_pdl(old)
         self.graphs[B] = (g, buf)
@@ -613,8 +640,12 @@ class TPDecodeRunner:
         return host_out
 
     def release_graphs(self):
-        """Drop captured graphs (required before destroying the process group)."""
+        """Drop captured graphs (required before destroying the process group) and, on the vLLM path,
+        vLLM's all-reduce buffers (collective: every rank calls it)."""
         self.graphs = {B: (None, buf) for B, (g, buf) in self.graphs.items()}
+        if self._car is not None:
+            self._car.close()
+            self._car = None
 
 
 def reference_greedy(cfg: LlamaConfig, full: dict, prompts: torch.Tensor, steps: int, device) -> torch.Tensor:

@@ -37,10 +37,12 @@ def test_runner_headline_plan():
     from comm_opt_b200.harness.runner import command, headline_jobs
 
     jobs = headline_jobs((2, 4, 8))
-    # per GPU count: 2 sweeps, boundary, 3 decode forms, 8B x 3 batches x 2 collectives; 3 extra 70B batches at 8
-    assert len(jobs) == 3 * (6 + 6) + 3
+    # per GPU count: 2 sweeps, boundary, 4 decode forms (fused, separate, NCCL stack, vLLM stack),
+    # 8B x 3 batches x 2 collectives; 3 extra 70B batches at 8
+    assert len(jobs) == 3 * (7 + 6) + 3
     cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
     assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3 + 9
+    assert sum("bench.py" in c and "--collective vllm" in c for c in cmds) == 3
     assert sum("--model 8b --prompt 1024" in c for c in cmds) == 18
     assert all(("bench.py" in c) != (" -m comm_opt_b200" in c.split("torch.distributed.run")[1]) for c in cmds)
     assert sum("ref_m16nf" in c for c in cmds) == 2  # both sweeps at 8 GPUs

@@ -240,6 +240,7 @@ def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
     r.cfg, r.s, r.tp, r.rank = cfg, cfg.shard(tp), tp, 0
     r.w = M.LlamaWeights(cfg, 0, tp, "cpu", seed=1)
     r.comm, r.collective, r.nccl_group, r.gemm = Comm(), "ours", None, "cob"
+    r._car = r._vllm_ops = None
     keys = [(i, n) for i in range(layers) for n in ("qkv", "o", "gu", "down")] + ["head"]
     r.lin = {k: (lambda *a, **kw: calls.append("gemm")) for k in keys}
     r.cache = SimpleNamespace(block_tables=torch.zeros(4, 8, dtype=torch.int32), k=[None] * layers, v=[None] * layers)
@@ -292,3 +293,33 @@ def test_decode_step_composition_every_boundary_mix(monkeypatch):
                 n = r._step(4, buf)
                 assert calls == _expected_step(3, fuse, kinds, epi), (fuse, kinds, epi)
                 assert n == len(calls), (fuse, kinds, epi, n, len(calls))
+
+
+def test_decode_step_composition_vllm_stack(monkeypatch):
+    """The reference's baseline stack in the same step: vLLM custom all-reduce (out of place) + vLLM
+    fused_add_rms_norm at both boundaries, the next GEMM reading the all-reduce's output; the kernel count
+    names only this package's kernels."""
+    from types import SimpleNamespace
+
+    r, buf, calls = _recording_runner(monkeypatch, 2, 2, False, (False, False), (False, False))
+    seen = {}
+
+    def car_ar(x):
+        calls.append("car_ar")
+        seen["out"] = torch.zeros_like(x)
+        return seen["out"]
+
+    r.collective = "vllm"
+    r._car = SimpleNamespace(custom_all_reduce=car_ar)
+    r._vllm_ops = SimpleNamespace(fused_add_rms_norm=lambda out, res, g, eps: calls.append("vllm_norm"))
+    gemm_inputs = []
+    for k in list(r.lin):
+        r.lin[k] = (lambda x, out=None, _k=k: (gemm_inputs.append((_k, x)), calls.append("gemm")))
+    n = r._step(4, buf)
+    layer = ["gemm", "rope_append_kv", "attention", "gemm", "car_ar", "vllm_norm", "gemm", "silu_mul", "gemm",
+             "car_ar", "vllm_norm"]
+    assert calls == ["embedding", "rmsnorm"] + layer * 2 + ["gemm", "argmax_local", "all_gather", "argmax_combine"]
+    assert n == len(calls) - 4 * 2  # two vLLM kernels at each of the two boundaries of both layers
+    # the GEMM after a boundary reads the all-reduce's output, not buf["h"]
+    gu = [x for k, x in gemm_inputs if k == (1, "gu")][0]
+    assert gu is not buf["h"] and [x for k, x in gemm_inputs if k == "head"][0] is seen["out"]
