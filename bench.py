@@ -53,6 +53,8 @@ def parse():
     p.add_argument("--tune-boundaries", type=int, choices=[0, 1], default=1,
                    help="with fused boundaries: time each fused / separate choice of the two boundary kinds at "
                         "capture and keep the fastest (0 = both fused)")
+    p.add_argument("--l2-prefetch", type=int, default=0,
+                   help="weight tiles each GEMM prefetches into L2 beyond its ring while it waits (0 = none)")
     p.add_argument("--e2e-steps", type=int, default=None)
     p.add_argument("--layers", type=int, default=None, help="override the layer count (debug only; invalid for bench)")
     p.add_argument("--out", default=None, help="also write the JSON line to this file")
@@ -166,7 +168,7 @@ def main():
     runner = TPDecodeRunner(cfg, weights, comm, max_batch=B, max_seq=max_seq, device=dev, gemm=args.gemm,
                             nccl_group=group, car_group=car_group, fuse_boundary=bool(args.fuse_boundary),
                             fuse_epilogues=bool(args.fuse_epilogues), collective=args.collective,
-                            tune_boundaries=bool(args.tune_boundaries))
+                            tune_boundaries=bool(args.tune_boundaries), l2_prefetch=args.l2_prefetch)
     prompts = torch.randint(0, cfg.vocab, (B, P), generator=torch.Generator().manual_seed(1234))
     first = runner.prefill(prompts)
     runner.start(B, first, P)
@@ -247,7 +249,7 @@ def main():
                        "fused_boundaries": (dict(zip(("attention_out", "mlp_out"), runner.fuse_kinds.get(B, (True, True))),
                                                  step_ms_by_choice=runner.boundary_times.get(B))
                                             if runner.fuse_boundary else None),
-                       "tokens_per_s": round(B * 1000.0 / ms, 1),
+                       "tokens_per_s": round(B * 1000.0 / ms, 1), "l2_prefetch_tiles": args.l2_prefetch,
                        "l2": "no flush: each step streams the full weight set (141 GB / N) >> 126 MB L2",
                        "setup_s": round(setup_s, 1)},
             "e2e": {"value": round(ms_e2e, 4), "unit": "ms/token", "h2d_bytes_per_step": B * 4,

@@ -269,6 +269,9 @@ __device__ __forceinline__ void pdl_wait_then_trigger() {
 // library calls pdl_wait() before it reads data produced by (or writes data read by) its
 // predecessor. Defined in decode_ops.cu.
 bool& pdl_flag();
+// Process-wide: weight tiles beyond its shared-memory ring that a GEMM prefetches into L2 before it waits
+// for its activations (the previous kernel, or the all-reduce pieces); 0 = none. Defined in decode_ops.cu.
+int& l2_prefetch_tiles();
 
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,

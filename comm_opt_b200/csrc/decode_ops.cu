@@ -15,6 +15,11 @@ bool& pdl_flag() {
   return on;
 }
 
+int& l2_prefetch_tiles() {
+  static int tiles = 0;
+  return tiles;
+}
+
 namespace {
 
 constexpr int kVPT = 4;

@@ -191,6 +191,8 @@ __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtenso
         mbar_arrive_expect_tx(&c.full[i], C::STAGE);
         tma_load_2d(sA + i * C::A_BYTES, tmW, &c.full[i], kx(i), wr(i));
       }
+      // the next weight tiles into L2 while the activations are awaited (later stages then hit L2)
+      for (int i = pre; i < min(total, pre + p.l2_prefetch); ++i) tma_prefetch_l2(tmW, kx(i), wr(i));
       if (!WAIT_ACT) pdl_wait();
     }
     bool ok = true;
@@ -674,6 +676,7 @@ cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUte
   cfg.numAttrs = na;
   FusedGemmParams q = p;
   q.kps = pl.kps;
+  if (q.l2_prefetch == 0) q.l2_prefetch = l2_prefetch_tiles();
   return cudaLaunchKernelEx(&cfg, fn, tw, tb, q);
 }
 

@@ -29,6 +29,7 @@ struct FusedGemmParams {
   int M, N, K;               // this rank's GEMM: [M, K] x [N, K]^T, weights stacked by rank when emulating
   int kps;                   // 64-wide k-steps per split (splits = gridDim.y)
   unsigned long long timeout_ns;
+  int l2_prefetch;           // weight tiles beyond the ring prefetched into L2 before the activations are awaited
   int* err;                  // device word: nonzero after a timed-out wait in this kernel
   // ar_norm_gemm only
   void* residual;            // [M, K] in / out (each element read and written by one thread)

@@ -78,7 +78,7 @@ template <int BN, bool BF16, bool SMALL, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
                    int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
-                   int kps) {
+                   int kps, int l2pf) {
   using C = Cfg<BN, SMALL>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -141,6 +141,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const long long g = beg + i;
         mbar_arrive_expect_tx(&full[i], C::STAGE);
         tma_load_2d(sA + i * C::A_BYTES, &tmW, &full[i], (int)(g % KT) * BK, (int)(g / KT) * BM);
+      }
+      // the next l2pf weight tiles into L2 while the previous kernel finishes (later stages hit L2)
+      for (int i = pre; i < min(nsteps, pre + l2pf); ++i) {
+        const long long g = beg + i;
+        tma_prefetch_l2(&tmW, (int)(g % KT) * BK, (int)(g / KT) * BM);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) {
@@ -379,7 +384,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps);
+  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps, l2_prefetch_tiles());
 }
 
 template <bool BF16, bool SMALL>

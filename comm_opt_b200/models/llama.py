@@ -223,7 +223,7 @@ class TPDecodeRunner:
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
                  device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
                  fuse_epilogues: bool = False, collective: str = "ours", tune_boundaries: bool = True,
-                 car_group=None):
+                 car_group=None, l2_prefetch: int = 0):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -244,6 +244,8 @@ class TPDecodeRunner:
         self.graphs: dict[int, tuple] = {}
         self.kernels_per_step: dict[int, int] = {}
         self.pdl = pdl  # programmatic dependent launch between the kernels of a captured step
+        # weight tiles each GEMM prefetches into L2 beyond its ring while it waits for its activations
+        self.l2_prefetch = int(l2_prefetch)
         # layer-boundary fusion: o_proj / down_proj push their partial sums straight into the
         # all-reduce landing buffers, and the all-reduce + residual + RMSNorm runs inside the next
         # GEMM (gate_up, the next layer's qkv, the LM head); needs TP > 1, bf16 and this package's GEMMs
@@ -557,6 +559,14 @@ class TPDecodeRunner:
 
     def capture(self, B: int, tune: bool = True):
         """Capture one decode step for batch B in a CUDA graph (buffers are static)."""
+        old = K.set_l2_prefetch(self.l2_prefetch) if self.gemm == "cob" else None
+        try:
+            return self._capture(B, tune)
+        finally:
+            if old is not None:
+                K.set_l2_prefetch(old)
+
+    def _capture(self, B: int, tune: bool):
         if tune and self.gemm == "cob":
             self.tune(B)
         buf = self.graphs[B][1]

@@ -39,6 +39,15 @@ def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     return out
 
 
+def set_l2_prefetch(tiles: int) -> int:
+    """Weight tiles beyond its shared-memory ring that every GEMM of this package prefetches into L2
+    before it waits for its activations (0 = none); returns the old value. Read at launch time, so a
+    CUDA graph keeps the value it was captured with."""
+    old = native().get_l2_prefetch()
+    native().set_l2_prefetch(int(tiles))
+    return old
+
+
 def set_pdl(on: bool) -> bool:
     """Launch every kernel of this package with programmatic dependent launch (returns the old value)."""
     old = native().get_pdl()
