@@ -77,3 +77,24 @@ def test_gemm_tuner_picks_valid_config(cuda):
     assert isinstance(cfg, dict)
     x = torch.randn(8, 8192, device=cuda).to(torch.bfloat16)
     assert rel_err(lin(x), x.float() @ w.float().t()) <= 2 ** -7
+
+
+@pytest.mark.skipif(__import__("os").environ.get("COB_EXPERIMENTAL") != "1",
+                    reason="L2 prefetch has not run on a GPU yet; COB_EXPERIMENTAL=1 runs it")
+@pytest.mark.parametrize("tiles", [4, 16, 64])
+def test_gemm_l2_prefetch_same_bits(cuda, tiles):
+    """Prefetching weight tiles into L2 is only a hint: stream-K and cluster split-K results are bitwise
+    those without it (partial last tile, M not a multiple of the batch tile, K beyond the ring)."""
+    from comm_opt_b200.ops.kernels import set_l2_prefetch
+
+    x = torch.randn(5, 8192, device=cuda).to(torch.bfloat16)
+    w = (0.05 * torch.randn(1000, 8192, device=cuda)).to(torch.bfloat16)
+    base = [gemm(x, w), gemm(x, w, cluster_splits=4)]
+    old = set_l2_prefetch(tiles)
+    try:
+        got = [gemm(x, w), gemm(x, w, cluster_splits=4)]
+    finally:
+        set_l2_prefetch(old)
+    torch.cuda.synchronize()
+    assert int(gemm_error_word(cuda)) == 0
+    assert all(torch.equal(a, b) for a, b in zip(base, got))
