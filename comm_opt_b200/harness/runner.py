@@ -191,6 +191,26 @@ def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
     return jobs
 
 
+def validate_jobs(gpus=(2, 4, 8)) -> list[Job]:
+    """First runs of what was written without a GPU at hand (the kernels' own one-GPU tests run with
+    `COB_EXPERIMENTAL=1 pytest -m gpu`): the multi-GPU self-test parts that cover them, the one-shot with
+    and without the cluster row-sum exchange against the two-shot forms and FlashInfer's one-shot, and
+    the decode bench with the L2 weight prefetch and the boundary choice switched on and off."""
+    exp = {"COB_EXPERIMENTAL": "1"}
+    jobs = [Job("selftest", 2, variant="experimental", env=exp,
+                args=("--parts", "functional,stress,decode_mixed,decode_qkv_bias,decode_hd64,decode_vllm")),
+            Job("selftest", 4, variant="kv_replicated", env=exp, args=("--parts", "decode_hd64,decode_mixed"))]
+    impls = "ours:lamport_1s,ours:lamport_1sx,ours:lamport_2s,ours:pull_2s,ours:nvls_2s,trt_oneshot,trt_twoshot"
+    for g in gpus:
+        jobs.append(Job("fused_sweep", g, variant="experimental", env=exp, args=("--impls", impls, "--replays", "20")))
+    top = max(gpus)
+    for variant, extra in (("default", ()), ("no_tuning", ("--tune-boundaries", "0")),
+                           ("l2pf8", ("--l2-prefetch", "8")), ("l2pf16", ("--l2-prefetch", "16"))):
+        jobs.append(Job("bench", top, variant=variant, args=("--steps", "64", "--warmup", "4", *extra)))
+    jobs.append(Job("bench", 1, variant="l2pf8", args=("--steps", "32", "--warmup", "3", "--l2-prefetch", "8")))
+    return jobs
+
+
 def e2e_share_jobs(ngpus: int = 8, reps: int = 3) -> list[Job]:
     """The reference's M5 matrix (exp/M5_e2e_comm_share/run_train.py:14-16 and run_infer.py): training of
     Llama-3 1B / 8B at TP 8 / 4 / 2 x FSDP ngpus / TP, 8 x 2048 tokens per step, `reps` launches each; and
@@ -233,7 +253,7 @@ if __name__ == "__main__":
 
     ap = argparse.ArgumentParser()
     ap.add_argument("plan", choices=["collective_baseline", "nccl_variants", "fused_hidden", "headline", "e2e_share",
-                                     "repeat", "p2p_channels"])
+                                     "repeat", "p2p_channels", "validate"])
     ap.add_argument("--gpus", default="2,4,8")
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args()
@@ -241,5 +261,5 @@ if __name__ == "__main__":
     jobs = {"collective_baseline": lambda: collective_baseline_jobs(gp), "nccl_variants": lambda: nccl_variant_jobs(max(gp)),
             "fused_hidden": lambda: fused_hidden_jobs(max(gp)), "headline": lambda: headline_jobs(gp),
             "e2e_share": lambda: e2e_share_jobs(max(gp)), "repeat": repeat_jobs,
-            "p2p_channels": p2p_channel_jobs}[a.plan]()
+            "p2p_channels": p2p_channel_jobs, "validate": lambda: validate_jobs(gp)}[a.plan]()
     print(run_all(jobs, a.plan, a.seed))

@@ -345,3 +345,17 @@ def test_bench_clock_summary():
     assert s["sm_mhz"] == 1410.0 and s["sm_max_mhz"] == 1965.0 and s["samples"] == 3
     assert s["reasons"] == ["sw_power_cap"] and s["power_w_max"] == 997.0
     assert bench.ClockSampler.summarize([])["sm_mhz"] is None
+
+
+def test_validate_plan():
+    """The first-GPU-run plan: self-test parts with the experimental variants, A/B sweeps at every GPU
+    count, the decode bench with the new switches on and off."""
+    from comm_opt_b200.harness.runner import command, validate_jobs
+
+    jobs = validate_jobs((2, 4, 8))
+    assert sum(j.entry == "selftest" for j in jobs) == 2 and all(j.env.get("COB_EXPERIMENTAL") == "1"
+                                                                 for j in jobs if j.entry != "bench")
+    assert sorted(j.ngpus for j in jobs if j.entry == "fused_sweep") == [2, 4, 8]
+    cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
+    assert sum("--l2-prefetch" in c for c in cmds) == 3 and sum("--tune-boundaries 0" in c for c in cmds) == 1
+    assert any("decode_vllm" in c for c in cmds) and any("ours:lamport_1sx" in c for c in cmds)
