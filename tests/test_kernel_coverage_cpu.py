@@ -1,0 +1,168 @@
+"""Work partitioning of the fused all-reduce kernels, restated on CPU (no GPU).
+
+For every geometry the host launcher accepts (resolve_config through `fused_ar_config`), the index
+arithmetic of csrc/fused_ar.cu is replayed thread by thread in Python and every (row, 16-byte vector)
+of the message must be handled exactly once in each phase, with every index inside the heap layout.
+This checks the thread/vector mapping (the one-vector one-shot form chosen at launch, the two-shot
+units and flat phases, the multicast two-shot's last phase in row groups of 32) without running a
+kernel.
+"""
+import numpy as np
+import pytest
+
+from comm_opt_b200._ext import available
+
+pytestmark = pytest.mark.skipif(not available(), reason="native extension not built")
+
+EPV = {0: 4, 1: 8, 2: 8}  # elements per 16-byte vector by dtype code (f32, f16, bf16)
+KVPT = 4
+
+
+def _config(world, rows, hidden, dtype, variant, emulate=0, sms=148, blocks=0, threads=0, cluster=0):
+    from comm_opt_b200._ext import native
+
+    C = native()
+    esz = 4 if dtype == 0 else 2
+    L = C.plan_layout(world, 512, 8192, esz, 4096)
+    rc, v, b, t, cl = C.fused_ar_config(L, world, rows, hidden, dtype, variant, blocks, threads, cluster, emulate,
+                                        sms, True)
+    return rc, b, t, cl, L
+
+
+def oneshot_cover(rows, hv, blocks, threads, cluster):
+    """k_oneshot: cluster cl = b // C owns rows cl, cl + ncl, ...; CTA crank = b % C owns the vector chunk
+    [crank * chunk, ...); thread tid handles v0 + tid + k * NT for k < VPT (VPT = 1 when the chunk fits)."""
+    C = cluster
+    chunk = (hv + C - 1) // C
+    vpt = 1 if chunk <= threads else KVPT
+    seen = np.zeros((rows, hv), dtype=np.int32)
+    ncl = blocks // C
+    tid = np.arange(threads)
+    for b in range(blocks):
+        crank, cl = b % C, b // C
+        v0, v1 = crank * chunk, min(hv, crank * chunk + chunk)
+        for row in range(cl, rows, ncl):
+            for k in range(vpt):
+                v = v0 + tid + k * threads
+                v = v[v < v1]
+                np.add.at(seen[row], v, 1)
+    return seen
+
+
+def twoshot_phase2_units(rows, hv, world, blocks, threads, variant):
+    """k_twoshot phase 2: units of 32 vectors of each rank's owned column slice; LAMPORT spreads
+    (row, unit) over all warps of the grid, PULL / NVLS keep a row in the block that staged it. Returns
+    how often each (row, owned vector) is reduced by one rank."""
+    sv = hv // world
+    U = (sv + 31) // 32
+    nw = threads // 32
+    seen = np.zeros((rows, sv), dtype=np.int32)
+    if variant == 2:  # LAMPORT: flat over grid warps
+        total_warps = blocks * nw
+        for gw in range(total_warps):
+            for g in range(gw, rows * U, total_warps):
+                row, c0 = g // U, (g % U) * 32
+                i = c0 + np.arange(32)
+                np.add.at(seen[row], i[i < sv], 1)
+    else:
+        for b in range(blocks):
+            nunits = ((rows - b + blocks - 1) // blocks) * U
+            if variant == 4:  # NVLS: kNvB = 4 units per warp and step
+                for warp in range(nw):
+                    for g0 in range(warp, nunits, nw * 4):
+                        for j in range(4):
+                            g = g0 + j * nw
+                            if g < nunits:
+                                row, c0 = b + (g // U) * blocks, (g % U) * 32
+                                i = c0 + np.arange(32)
+                                np.add.at(seen[row], i[i < sv], 1)
+            else:
+                for warp in range(nw):
+                    for g in range(warp, nunits, nw):
+                        row, c0 = b + (g // U) * blocks, (g % U) * 32
+                        i = c0 + np.arange(32)
+                        np.add.at(seen[row], i[i < sv], 1)
+    return seen
+
+
+def twoshot_phase3(rows, hv, blocks, threads, variant):
+    """k_twoshot phase 3: LAMPORT / PULL flat over (row, v), two vectors per lane per step (a warp shares
+    one row per step); NVLS: the block's rows in groups of 32, every thread four vectors per step."""
+    seen = np.zeros((rows, hv), dtype=np.int32)
+    if variant != 4:
+        total, gthreads = rows * hv, blocks * threads
+        for gtid0 in range(0, gthreads, 32):  # warps: u0 = gtid - lane
+            for u0 in range(gtid0, total, 2 * gthreads):
+                for k in range(2):
+                    ub = u0 + k * gthreads
+                    if ub < total:
+                        row = ub // hv
+                        v = ub + np.arange(32) - row * hv
+                        assert (v < hv).all(), "a warp's 32 vectors stay in one row (hv % 32 == 0)"
+                        np.add.at(seen[row], v, 1)
+    else:
+        for b in range(blocks):
+            nrows_b = (rows - b + blocks - 1) // blocks
+            for r0 in range(0, nrows_b, 32):
+                nr = min(32, nrows_b - r0)
+                items = nr * hv
+                tid = np.arange(threads)
+                for i0 in range(0, items, 4 * threads):
+                    for k in range(4):
+                        idx = i0 + tid + k * threads
+                        idx = idx[idx < items]
+                        rl, v = idx // hv, idx % hv
+                        for r, vv in zip(rl, v):
+                            seen[b + (r0 + r) * blocks, vv] += 1
+    return seen
+
+
+SHAPES = [(1, 8192), (3, 5120), (8, 8192), (17, 2048), (64, 4096), (128, 8192)]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("variant", [1, 3, 5, 7])
+def test_oneshot_covers_every_vector_once(world, variant):
+    for rows, hidden in SHAPES:
+        for emulate in (0, 1):
+            rc, b, t, cl, L = _config(world, rows, hidden, 2, variant, emulate)
+            assert rc == 0, (world, variant, rows, hidden)
+            hv = hidden // EPV[2]
+            seen = oneshot_cover(rows, hv, b, t, cl)
+            assert (seen == 1).all(), (world, variant, rows, hidden, b, t, cl)
+    # explicit clusters and block counts, as the calibrated table and the tests use them
+    for cluster in (1, 2, 4, 8):
+        rc, b, t, cl, L = _config(world, 4, 8192, 2, variant, blocks=4 * cluster, cluster=cluster)
+        assert rc == 0
+        assert (oneshot_cover(4, 1024, b, t, cl) == 1).all()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("variant", [2, 4, 6])
+def test_twoshot_phases_cover_every_vector_once(world, variant):
+    for rows, hidden in SHAPES:
+        rc, b, t, cl, L = _config(world, rows, hidden, 2, variant)
+        hv = hidden // EPV[2]
+        if hv % world or hv % 32:
+            assert rc != 0
+            continue
+        assert rc == 0 and cl == 1 and b <= 148
+        p2 = twoshot_phase2_units(rows, hv, world, b, t, variant)
+        assert (p2 == 1).all(), ("phase 2", world, variant, rows, hidden, b, t)
+        p3 = twoshot_phase3(rows, hv, b, t, variant)
+        assert (p3 == 1).all(), ("phase 3", world, variant, rows, hidden, b, t)
+    # more CTAs than rows (the pull two-shot's default for small messages, and explicit grids)
+    for blocks in (1, 3, 16, 40):
+        rc, b, t, cl, L = _config(world, 4, 8192, 2, variant, blocks=blocks, threads=256)
+        if rc != 0:
+            continue
+        assert (twoshot_phase2_units(4, 1024, world, b, t, variant) == 1).all()
+        assert (twoshot_phase3(4, 1024, b, t, variant) == 1).all()
+
+
+def test_pull_twoshot_default_grid_has_gather_ctas():
+    """The pull two-shot now starts enough CTAs for its flat gather phase even for one row."""
+    rc, b, t, cl, L = _config(8, 1, 8192, 2, 6)
+    assert rc == 0 and b == 1024 // t
+    rc, b, t, cl, L = _config(8, 8, 8192, 2, 6)
+    assert rc == 0 and b == 8 * 1024 // t
