@@ -166,3 +166,36 @@ def test_pull_twoshot_default_grid_has_gather_ctas():
     assert rc == 0 and b == 1024 // t
     rc, b, t, cl, L = _config(8, 8, 8192, 2, 6)
     assert rc == 0 and b == 8 * 1024 // t
+
+
+def test_attention_pages_and_merge_cover_once():
+    """k_decode_attn: split s reads page-table entries [pg0, pg0 + min(pps, max_blocks - pg0)) (inside the
+    row), attends pages [pg0, pg1) with warp w taking pg0 + w, pg0 + w + 4, ...; the cluster merge gives
+    CTA r output elements [r * per, (r + 1) * per). Every page of every sequence is attended once and
+    every output element written once, for the split plans of the decode shapes."""
+    from comm_opt_b200.ops.kernels import attention_split_plan
+
+    kWarps, kBS = 4, 16
+    for batch, nkv, G, D in [(8, 1, 8, 128), (8, 8, 8, 128), (1, 1, 8, 128), (32, 1, 5, 128), (8, 1, 4, 64)]:
+        for max_pages in (1, 7, 33, 129, 513):
+            splits, pps, cluster = attention_split_plan(batch, nkv, max_pages, 148)
+            for seq in {x for x in (1, 15, 16, 17, max_pages * kBS // 2 + 3, max_pages * kBS) if x <= max_pages * kBS}:
+                npages = (seq + kBS - 1) // kBS
+                seen = np.zeros(npages, dtype=np.int32)
+                for split in range(splits):
+                    pg0 = split * pps
+                    pg_cap = min(pps, max_pages - pg0)
+                    assert pg0 + max(pg_cap, 0) <= max_pages  # table reads stay inside the row
+                    pg1 = min(npages, pg0 + pps)
+                    for warp in range(kWarps):
+                        my = (pg1 - pg0 - warp + kWarps - 1) // kWarps if pg1 - pg0 > warp else 0
+                        assert my <= pps
+                        for i in range(my):
+                            seen[pg0 + warp + i * kWarps] += 1
+                assert (seen == 1).all(), (batch, nkv, max_pages, seq, splits, pps)
+            if cluster:
+                per = (G * D + splits - 1) // splits
+                out = np.zeros(G * D, dtype=np.int32)
+                for r in range(splits):
+                    out[r * per:min(G * D, (r + 1) * per)] += 1
+                assert (out == 1).all()
