@@ -199,3 +199,45 @@ def test_attention_pages_and_merge_cover_once():
                 for r in range(splits):
                     out[r * per:min(G * D, (r + 1) * per)] += 1
                 assert (out == 1).all()
+
+
+def test_layer_boundary_pieces_and_push_groups_cover_once():
+    """Layer-boundary GEMMs (csrc/fused_gemm.cu) for every decode projection of the model presets at
+    TP 2/4/8: the consumer's pieces (CTA (t, r) reduces vectors [vb, ve) of split r's k-range) cover the
+    K vectors of every row exactly once, and the push epilogue's feature groups (split r of tile t
+    pushes features [r * BM / cs, (r + 1) * BM / cs)) cover every output feature exactly once."""
+    from comm_opt_b200._ext import native
+    from comm_opt_b200.models.llama import PRESETS
+
+    C = native()
+    BM, BK = 128, 64
+    for model in ("70b", "8b", "qwen2.5-32b", "tinyllama-1.1b"):
+        cfg = PRESETS[model]
+        for tp in (2, 4, 8):
+            s, D, H = cfg.shard(tp), cfg.head_dim, cfg.hidden
+            consumers = [((s["nq"] + 2 * s["nkv"]) * D, H), (2 * s["inter"], H), (s["vocab"], H)]
+            pushes = [(H, s["nq"] * D), (H, s["inter"])]
+            for M in (1, 8, 32, 128):
+                for N, K in consumers:
+                    bn, tiles, splits, kps, xctas, ctas, smem = C.fused_gemm_plan(M, N, K, 0, 148, True, 0)
+                    if splits == 0:
+                        continue
+                    KT, KV = K // BK, K // 8
+                    assert splits * kps >= KT and ctas <= min(148 * (2 if bn <= 64 else 1), 160)
+                    seen = np.zeros(KV, dtype=np.int32)
+                    for r in range(splits):
+                        k0 = r * kps
+                        s0, slen = k0 * 8, min(KV, (k0 + kps) * 8) - k0 * 8
+                        for t in range(xctas):
+                            vb, ve = s0 + slen * t // xctas, s0 + slen * (t + 1) // xctas
+                            seen[vb:ve] += 1
+                    assert (seen == 1).all(), (model, tp, M, N, K, splits, kps, xctas)
+                for N, K in pushes:
+                    bn, tiles, splits, kps, xctas, ctas, smem = C.fused_gemm_plan(M, N, K, 0, 148, False, 0)
+                    assert splits >= 1 and BM % (8 * splits) == 0 and splits * kps >= K // BK
+                    per = BM // splits
+                    feats = np.zeros(tiles * BM, dtype=np.int32)
+                    for t in range(tiles):
+                        for r in range(splits):
+                            feats[t * BM + r * per:t * BM + (r + 1) * per] += 1
+                    assert (feats[:N] == 1).all(), (model, tp, M, N, K, splits)
