@@ -141,7 +141,22 @@ def sweep_figures(doc: dict, out: Path) -> list[Path]:
                              f"hidden {r0.get('hidden')} {r0.get('dtype')} (p50 per op, max over ranks)",
                      "message size (bytes)", "us", xfmt=_kb)
     (out / "latency.svg").write_text(svg)
-    return [out / "per_op.csv", out / "latency.svg"]
+    # achieved fraction of the NVLink roofline (analyze_sweep.roofline_table): ours and the best baseline
+    from .analyze_sweep import roofline_table
+
+    _, summ = roofline_table(doc["rows"])
+    frac = {"best of ours": [(s["target_us"] * 770e3, s["fraction"]) for s in summ if s["fraction"]],
+            "best baseline": [(s["target_us"] * 770e3, s["baseline_fraction"]) for s in summ
+                              if s["baseline_fraction"]]}
+    # x: the message size (target_us x link bandwidth is 2 (W-1)/W of it; the size itself is plotted)
+    w = doc.get("world") or 2
+    frac = {k: [(x * w / (2 * (w - 1)), y) for x, y in v] for k, v in frac.items()}
+    _write_csv(out / "roofline.csv", summ, ["world", "tokens", "target_us", "ours", "fraction", "baseline",
+                                            "baseline_fraction"])
+    (out / "roofline.svg").write_text(line_chart(
+        frac, f"fraction of the NVLink roofline (2 (W-1)/W x S at 770 GB/s), {w} GPUs", "message size (bytes)",
+        "fraction", xfmt=_kb))
+    return [out / "per_op.csv", out / "latency.svg", out / "roofline.csv", out / "roofline.svg"]
 
 
 def boundary_figures(doc: dict, out: Path) -> list[Path]:
