@@ -62,7 +62,7 @@ def fused_ar(a, dev) -> dict:
 
 
 def attention(a, dev) -> dict:
-    B, nq, nkv, D, blk = a.batch, a.heads, a.kv_heads, 128, 16
+    B, nq, nkv, D, blk = a.batch, a.heads, a.kv_heads, a.head_dim, 16
     pages = (a.ctx + blk - 1) // blk
     nblocks = B * pages + 16
     g = torch.Generator(device=dev).manual_seed(0)
@@ -84,8 +84,8 @@ def attention(a, dev) -> dict:
                                  device=dev)
     r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5), a.iters)
     kv_bytes = 2 * B * nkv * a.ctx * D * 2
-    return dict(r, batch=B, ctx=a.ctx, heads=nq, kv_heads=nkv, splits=op.splits, pages_per_split=op.pps,
-                cluster=op.cluster, kv_bytes=kv_bytes)
+    return dict(r, batch=B, ctx=a.ctx, heads=nq, kv_heads=nkv, head_dim=D, splits=op.splits,
+                pages_per_split=op.pps, cluster=op.cluster, kv_bytes=kv_bytes)
 
 
 def decode_ops(a, dev) -> dict:
@@ -104,10 +104,19 @@ def decode_ops(a, dev) -> dict:
     q = torch.empty(B, nq, D, device=dev).bfloat16()
     gu = torch.randn(B, 2 * inter, generator=g, device=dev).bfloat16()
     act = torch.empty(B, inter, device=dev).bfloat16()
+    res = torch.randn(B, H, generator=g, device=dev).bfloat16()
+    table = torch.randn(a.vocab, H, generator=g, device=dev).bfloat16()
+    ids = torch.randint(0, a.vocab, (B,), generator=torch.Generator().manual_seed(2)).to(torch.int32).to(dev)
+    logits = torch.randn(B, a.vocab, generator=g, device=dev).bfloat16()
+    keys = torch.zeros(B, dtype=torch.int64, device=dev)
     out = {}
     out["rmsnorm"] = timed(lambda: K.rmsnorm(x, gamma, 1e-5, out=h), a.iters)
+    out["add_rmsnorm"] = timed(lambda: K.add_rmsnorm(x, res, gamma, 1e-5, out=h), a.iters)
     out["rope_append"] = timed(lambda: K.rope_append_kv(qkv, pos, cos, sin, bt, q, kc, vc, nq, nkv), a.iters)
     out["silu_mul"] = timed(lambda: K.silu_mul(gu, out=act), a.iters)
+    out["embedding"] = timed(lambda: K.embedding(ids, table, out=h), a.iters)
+    out["argmax"] = timed(lambda: K.argmax_combine(K.argmax_local(logits, 0, keys=keys).view(1, B), 1,
+                                                   local_keys=keys), a.iters)
     return dict(batch=B, hidden=H, inter=inter, **out)
 
 
@@ -123,6 +132,8 @@ def main():
     ap.add_argument("--heads", type=int, default=8)
     ap.add_argument("--kv-heads", type=int, default=1)
     ap.add_argument("--inter", type=int, default=3584)
+    ap.add_argument("--head-dim", type=int, default=128, choices=[64, 128])
+    ap.add_argument("--vocab", type=int, default=16032, help="decode_ops: embedding rows and argmax width")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--splits", type=int, default=0, help="attention: override the split plan")
     ap.add_argument("--graph", type=int, default=0, help="time CUDA graphs of this many launches")
