@@ -359,3 +359,23 @@ def test_validate_plan():
     cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
     assert sum("--l2-prefetch" in c for c in cmds) == 3 and sum("--tune-boundaries 0" in c for c in cmds) == 1
     assert any("decode_vllm" in c for c in cmds) and any("ours:lamport_1sx" in c for c in cmds)
+
+
+def test_launch_geometry_table():
+    """Host-planner geometry of the decode step: every kernel row present at TP 1 and 8, attention at
+    TP = 8 leaves SMs free and a push-GEMM CTA fits beside it."""
+    import pytest
+
+    from comm_opt_b200._ext import available
+
+    if not available():
+        pytest.skip("native extension not built")
+    from comm_opt_b200.harness.launch_geometry import markdown, pair_fits, rows_for
+
+    r8 = rows_for("70b", 8, 2048, 8)
+    names = [r["kernel"].split(" ")[0] for r in r8]
+    assert names[:4] == ["gemm_push", "ar_norm_gemm", "gemm_push", "ar_norm_gemm"] and "attention" in names
+    att = next(r for r in r8 if r["kernel"].startswith("attention"))
+    assert att["ctas"] == 64 and pair_fits(att, r8[0])
+    assert all(r["ctas"] <= 160 for r in r8 if "gemm" in r["kernel"])
+    assert "stream-K" in markdown("8b", 8, 1024, [1])
