@@ -220,7 +220,8 @@ def test_figures_from_runs(tmp_path):
                               for B in (1, 8) for i, v in (("fused", 27.0), ("split", 34.0))])
     share = dict(model="llama3-8b", world=8, tp=4, dp=2, step_ms=700.0, tokens_per_s=23000.0,
                  breakdown=dict(compute_pct=68.0, hidden_cost_pct=3.0, transfer_pct=14.0, other_pct=15.0))
-    for exp, name, doc, files in (("fused_sweep", "sweep.json", sweep, ("per_op.csv", "latency.svg")),
+    for exp, name, doc, files in (("fused_sweep", "sweep.json", sweep,
+                                   ("per_op.csv", "latency.svg", "roofline.csv", "roofline.svg")),
                                   ("boundary_bench", "boundary.json", bnd, ("boundary.csv", "boundary.svg")),
                                   ("train_share", "summary.json", share, ("share.csv", "share.svg"))):
         out = render(run(exp, name, doc), base=tmp_path)
