@@ -19,7 +19,7 @@
 namespace cob {
 
 constexpr int kMaxWorld = 8;
-constexpr int kMaxBlocks = 160;  // >= 148 SMs, per-block barrier slots
+constexpr int kMaxBlocks = 296;  // per-block barrier slots and epoch words: two CTAs on each of 148 SMs
 
 enum Variant : int {
   kAuto = 0,

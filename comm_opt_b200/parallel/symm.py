@@ -27,9 +27,9 @@ from .._ext import available, native
 FIELDS = ("state", "flags", "nvls", "land1", "rs", "ag", "agp", "stage", "hbuf", "hpart", "gather", "total",
           "world", "max_rows", "max_hv", "sv_max", "esize", "max_gather")
 
-MAX_BLOCKS = 160        # per-block barrier slots (>= 148 SMs)
+MAX_BLOCKS = 296        # per-block barrier slots and epoch words (two CTAs on each of 148 SMs)
 MAX_WORLD = 8
-RANK_STATE_BYTES = 3328  # sizeof(cob::RankState)
+RANK_STATE_BYTES = 6144  # sizeof(cob::RankState)
 
 
 @dataclass(frozen=True)

@@ -378,5 +378,5 @@ def test_launch_geometry_table():
     assert names[:4] == ["gemm_push", "ar_norm_gemm", "gemm_push", "ar_norm_gemm"] and "attention" in names
     att = next(r for r in r8 if r["kernel"].startswith("attention"))
     assert att["ctas"] == 64 and pair_fits(att, r8[0])
-    assert all(r["ctas"] <= 160 for r in r8 if r["kernel"].startswith("ar_norm_gemm"))  # per-block epoch words
+    assert all(r["ctas"] <= 296 for r in r8 if r["kernel"].startswith("ar_norm_gemm"))  # per-block epoch words
     assert "stream-K" in markdown("8b", 8, 1024, [1])

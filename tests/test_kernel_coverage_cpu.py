@@ -223,7 +223,7 @@ def test_layer_boundary_pieces_and_push_groups_cover_once():
                     if splits == 0:
                         continue
                     KT, KV = K // BK, K // 8
-                    assert splits * kps >= KT and ctas <= min(148 * (2 if bn <= 64 else 1), 160)
+                    assert splits * kps >= KT and ctas <= min(148 * (2 if bn <= 64 else 1), 296)
                     seen = np.zeros(KV, dtype=np.int32)
                     for r in range(splits):
                         k0 = r * kps
