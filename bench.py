@@ -131,6 +131,45 @@ def reference_arm(args):
         print(json.dumps(line), flush=True)
 
 
+def result_line(args, cfg, world: int, ms: float, ms_e2e: float, e2e_steps: int, setup_s: float, clocks, runner) -> dict:
+    """The driver's JSON line: device-timed ms per decode step (max over ranks), the end-to-end figure
+    through TPDecodeRunner.decode, our kernel launches in the timed region, and the clock record."""
+    B, P, K, W = args.batch, args.prompt, args.steps, args.warmup
+    weights_gb = cfg.params * 2 / 1e9
+    return {
+        "metric": "llama3_70b_tp_decode_ms_per_token" if args.model in ("70b", "llama3-70b") else
+        f"{cfg.name}_tp_decode_ms_per_token",
+        "value": round(ms, 4),
+        "unit": "ms/token",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: uniform-random prompt token ids (seed 1234), random-init weights N(0, 0.02)",
+        "config": {"model": cfg.name + ("" if args.layers is None else f"-L{cfg.layers}-INVALID"),
+                   "global_batch": B, "seq_len": P, "decode_tokens_timed": K, "parallelism": f"tp{world}",
+                   "gemm": args.gemm, "collective": args.collective, "fuse_boundary": runner.fuse_boundary,
+                   "fuse_epilogues": runner.fuse_boundary and runner.fuse_epilogues,
+                   "fuse_fallback": runner.fuse_error[:200] or None,
+                   "fused_boundaries": (dict(zip(("attention_out", "mlp_out"), runner.fuse_kinds.get(B, (True, True))),
+                                             step_ms_by_choice=runner.boundary_times.get(B))
+                                        if runner.fuse_boundary else None),
+                   "tokens_per_s": round(B * 1000.0 / ms, 1), "l2_prefetch_tiles": args.l2_prefetch,
+                   "l2": f"no flush: each step streams the full weight set ({weights_gb:.0f} GB / {world} GPUs) "
+                         ">> 126 MB L2",
+                   "setup_s": round(setup_s, 1)},
+        "e2e": {"value": round(ms_e2e, 4), "unit": "ms/token", "h2d_bytes_per_step": B * 4,
+                "d2h_bytes_per_step": B * 4, "steps": e2e_steps, "api": "TPDecodeRunner.decode"},
+        "gpu_launches": runner.kernels_per_step[B] * K,
+        "kernels_per_step": runner.kernels_per_step[B],
+        "clocks": clocks,
+    }
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -225,39 +264,8 @@ def main():
     if world > 1:
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
     ms, ms_e2e = [float(v) for v in stats.cpu()]
-    launches = runner.kernels_per_step[B] * K
     if rank == 0:
-        line = {
-            "metric": "llama3_70b_tp_decode_ms_per_token" if args.model in ("70b", "llama3-70b") else
-            f"{cfg.name}_tp_decode_ms_per_token",
-            "value": round(ms, 4),
-            "unit": "ms/token",
-            "n_gpus": world,
-            "steps": K,
-            "warmup": W,
-            "ms_per_step": round(ms, 4),
-            "higher_is_better": False,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "bf16",
-            "data": "synthetic: uniform-random prompt token ids (seed 1234), random-init weights N(0, 0.02)",
-            "config": {"model": cfg.name + ("" if args.layers is None else f"-L{cfg.layers}-INVALID"),
-                       "global_batch": B, "seq_len": P, "decode_tokens_timed": K, "parallelism": f"tp{world}",
-                       "gemm": args.gemm, "collective": args.collective, "fuse_boundary": runner.fuse_boundary,
-                       "fuse_epilogues": runner.fuse_boundary and runner.fuse_epilogues,
-                       "fuse_fallback": runner.fuse_error[:200] or None,
-                       "fused_boundaries": (dict(zip(("attention_out", "mlp_out"), runner.fuse_kinds.get(B, (True, True))),
-                                                 step_ms_by_choice=runner.boundary_times.get(B))
-                                            if runner.fuse_boundary else None),
-                       "tokens_per_s": round(B * 1000.0 / ms, 1), "l2_prefetch_tiles": args.l2_prefetch,
-                       "l2": "no flush: each step streams the full weight set (141 GB / N) >> 126 MB L2",
-                       "setup_s": round(setup_s, 1)},
-            "e2e": {"value": round(ms_e2e, 4), "unit": "ms/token", "h2d_bytes_per_step": B * 4,
-                    "d2h_bytes_per_step": B * 4, "steps": E, "api": "TPDecodeRunner.decode"},
-            "gpu_launches": launches,
-            "kernels_per_step": runner.kernels_per_step[B],
-            "clocks": clocks,
-        }
+        line = result_line(args, cfg, world, ms, ms_e2e, E, setup_s, clocks, runner)
         s = json.dumps(line)
         print(s, flush=True)
         if args.out:

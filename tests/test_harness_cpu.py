@@ -380,3 +380,30 @@ def test_launch_geometry_table():
     assert att["ctas"] == 64 and pair_fits(att, r8[0])
     assert all(r["ctas"] <= 296 for r in r8 if r["kernel"].startswith("ar_norm_gemm"))  # per-block epoch words
     assert "stream-K" in markdown("8b", 8, 1024, [1])
+
+
+def test_bench_result_line_contract():
+    """The JSON line the driver parses: every required key, with the types it expects, and the whole-job
+    value, the end-to-end figure with its host transfers, and our launches in the timed region."""
+    import json
+    from types import SimpleNamespace
+
+    import bench
+    from comm_opt_b200.models.llama import PRESETS
+
+    args = SimpleNamespace(batch=8, prompt=2048, steps=64, warmup=4, model="70b", layers=None, gemm="cob",
+                           collective="ours", l2_prefetch=0)
+    runner = SimpleNamespace(fuse_boundary=True, fuse_epilogues=False, fuse_error="", fuse_kinds={8: (False, True)},
+                             boundary_times={8: {"FF": 7.8, "SF": 7.5}}, kernels_per_step={8: 566})
+    clocks = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
+    line = bench.result_line(args, PRESETS["70b"], 8, 7.5, 7.55, 64, 5.0, clocks, runner)
+    json.dumps(line)
+    for k, t in (("metric", str), ("value", float), ("unit", str), ("n_gpus", int), ("steps", int), ("warmup", int),
+                 ("ms_per_step", float), ("higher_is_better", bool), ("scaling", str), ("dtype", str), ("data", str),
+                 ("config", dict), ("e2e", dict), ("gpu_launches", int), ("clocks", dict)):
+        assert isinstance(line[k], t), k
+    assert "vs_baseline" in line and line["higher_is_better"] is False and line["scaling"] in ("weak", "strong")
+    assert {"model", "global_batch", "seq_len", "parallelism"} <= set(line["config"])
+    assert line["config"]["parallelism"] == "tp8" and line["gpu_launches"] == 566 * 64
+    assert {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"} <= set(line["e2e"])
+    assert line["config"]["fused_boundaries"]["attention_out"] is False and "141 GB" in line["config"]["l2"]
