@@ -203,6 +203,10 @@ def validate_jobs(gpus=(2, 4, 8)) -> list[Job]:
     impls = "ours:lamport_1s,ours:lamport_1sx,ours:lamport_2s,ours:pull_2s,ours:nvls_2s,trt_oneshot,trt_twoshot"
     for g in gpus:
         jobs.append(Job("fused_sweep", g, variant="experimental", env=exp, args=("--impls", impls, "--replays", "20")))
+        # the attention-output boundary at Llama-70B shapes (o_proj -> all-reduce + RMSNorm -> gate_up), the
+        # kind the whole-step measurement points at; the MLP-output boundary is the bench's default shape
+        jobs.append(Job("boundary", g, variant="attn_out", args=("--k1", str(8192 // g), "--n2",
+                                                                  str(2 * 28672 // g))))
     top = max(gpus)
     for variant, extra in (("default", ()), ("no_tuning", ("--tune-boundaries", "0")),
                            ("l2pf8", ("--l2-prefetch", "8")), ("l2pf16", ("--l2-prefetch", "16"))):

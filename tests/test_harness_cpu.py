@@ -357,6 +357,8 @@ def test_validate_plan():
     assert sum(j.entry == "selftest" for j in jobs) == 2 and all(j.env.get("COB_EXPERIMENTAL") == "1"
                                                                  for j in jobs if j.entry != "bench")
     assert sorted(j.ngpus for j in jobs if j.entry == "fused_sweep") == [2, 4, 8]
+    attn = [j for j in jobs if j.entry == "boundary"]
+    assert [(j.ngpus, j.args) for j in attn if j.ngpus == 8] == [(8, ("--k1", "1024", "--n2", "7168"))]
     cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
     assert sum("--l2-prefetch" in c for c in cmds) == 3 and sum("--tune-boundaries 0" in c for c in cmds) == 1
     assert any("decode_vllm" in c for c in cmds) and any("ours:lamport_1sx" in c for c in cmds)
