@@ -355,7 +355,7 @@ def test_validate_plan():
 
     jobs = validate_jobs((2, 4, 8))
     assert sum(j.entry == "selftest" for j in jobs) == 2 and all(j.env.get("COB_EXPERIMENTAL") == "1"
-                                                                 for j in jobs if j.entry != "bench")
+                                                                 for j in jobs if j.entry in ("selftest", "fused_sweep"))
     assert sorted(j.ngpus for j in jobs if j.entry == "fused_sweep") == [2, 4, 8]
     attn = [j for j in jobs if j.entry == "boundary"]
     assert [(j.ngpus, j.args) for j in attn if j.ngpus == 8] == [(8, ("--k1", "1024", "--n2", "7168"))]
