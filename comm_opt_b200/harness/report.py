@@ -63,7 +63,14 @@ def bench_table(lines: list[dict]) -> str:
             out.append(f"| {d.get('impl')} | - | - | - | - | unavailable: {d['unavailable'][:60]} |")
             continue
         cfg = d.get("config", {})
-        extra = ", ".join(f"{k}={cfg[k]}" for k in ("parallelism", "global_batch", "fuse_boundary") if k in cfg)
+        extra = ", ".join(f"{k}={cfg[k]}" for k in ("parallelism", "global_batch", "fuse_boundary", "collective",
+                                                    "l2_prefetch_tiles") if cfg.get(k) not in (None, 0))
+        fb = cfg.get("fused_boundaries")
+        if fb:  # which boundary kinds the capture kept fused, and the step time of each choice
+            kinds = "+".join(k for k in ("attention_out", "mlp_out") if fb.get(k)) or "none"
+            times = fb.get("step_ms_by_choice") or {}
+            extra += f", fused={kinds}" + (" (" + " ".join(f"{k}:{v:.3f}" for k, v in sorted(times.items())) + ")"
+                                           if times else "")
         out.append(f"| {d['metric']} | {d['n_gpus']} | {_fmt(d['value'], 3)} | {_fmt(d.get('e2e', {}).get('value'), 3)} "
                    f"| {d.get('kernels_per_step', '-')} | {extra} |")
     return "\n".join(out)
