@@ -163,8 +163,8 @@ def headline_jobs(gpus=(2, 4, 8), batches=(1, 8, 32, 128)) -> list[Job]:
     baselines (hidden 8192 bf16, and the reference's fp16 hidden 5120), the layer-boundary bench, and the TP decode (fused / separate boundaries / NCCL baseline
     step) at each GPU count, the 70B decode batch sweep at 8 GPUs, and the 8B decode (prompt 1024, batch
     1 / 8 / 64) against the NCCL step at each GPU count."""
-    sweep_impls = ("ours:auto,ours:lamport_1s,ours:lamport_1sx,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,"
-                   "ours:nvls_2s,nccl_norm,vllm_car,trt_oneshot,trt_twoshot")
+    sweep_impls = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,"
+                   "ours:nvls_2s,nccl_norm,vllm_car,trt_oneshot,trt_twoshot")  # lamport_1sx: the validate plan
     jobs = []
     for g in gpus:
         jobs.append(Job("fused_sweep", g, args=("--impls", sweep_impls + (",ref_m16nf" if g == 8 else ""),
