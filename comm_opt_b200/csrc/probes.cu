@@ -155,9 +155,13 @@ __global__ void __launch_bounds__(1024) k_prim(const PrimParams p) {
     __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {  // multicast barrier of block b: one add per rank and call
+      // counters [0, K) gather every rank's adds; [K, 2K) count this rank's multicast calls of each
+      // block locally, so that calls of the other modes (and grids) in between need no matching adds
       const size_t off = (size_t)p.nvls_off + (size_t)blockIdx.x * 4;
+      uint32_t* calls = reinterpret_cast<uint32_t*>(mine + p.nvls_off) + kPrimMaxBlocks + blockIdx.x;
+      const uint32_t nc = *calls + 1u;
       mm_red_add_u32(p.mc + off, 1u);
-      const uint32_t target = (uint32_t)e * (uint32_t)W;
+      const uint32_t target = nc * (uint32_t)W;
       uint32_t spins = 0;
       while ((int)(ld_acquire_u32(p.base[rank] + off) - target) < 0) {
         if (expired(spins)) {
@@ -165,6 +169,7 @@ __global__ void __launch_bounds__(1024) k_prim(const PrimParams p) {
           break;
         }
       }
+      *calls = nc;
     }
     __syncthreads();
     if (p.mode == kRsNvls) {
@@ -453,7 +458,7 @@ size_t prim_heap_bytes(int world, int n, long long* flags_off, long long* stage_
   auto up = [](long long v) { return (v + 4095) / 4096 * 4096; };
   *flags_off = up(8LL * kPrimMaxBlocks);
   *nvls_off = *flags_off + up(8LL * kPrimMaxBlocks * 8);
-  *stage_off = *nvls_off + up(4LL * kPrimMaxBlocks);
+  *stage_off = *nvls_off + up(8LL * kPrimMaxBlocks);  // barrier counters, then local call counts
   *land_off = *stage_off + up(2LL * n * 4);
   return (size_t)(*land_off + up(2LL * 8 * (n / world) * 4));
 }

@@ -193,7 +193,7 @@ def test_primitive_probe_heap_and_multicast_modes():
         n = 4096 * world
         total, f, st, land, nv = native().prim_layout(world, n)
         assert 0 < f < nv < st < land < total
-        assert nv - f >= 8 * 256 * 8 and st - nv >= 4 * 256 and land - st >= 2 * n * 4
+        assert nv - f >= 8 * 256 * 8 and st - nv >= 8 * 256 and land - st >= 2 * n * 4
         assert total - land >= 2 * 8 * (n // world) * 4
     assert {PRIM_MODES[m] for m in NVLS_MODES} == {"rs_nvls", "ag_nvls"}
     r = run_prim(4, 4096 * 4, 4, "cpu", emulate=True)
