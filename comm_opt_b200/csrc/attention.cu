@@ -515,11 +515,31 @@ extern "C" __attribute__((visibility("default"))) const char* cob_noalloc_last_e
 
 extern "C" __attribute__((visibility("default"))) int cob_decode_attention_noalloc(
     const void* q, const void* k_cache, const void* v_cache, const int32_t* block_tables, const int32_t* seq_lens,
-    void* out, int batch, int nq, int nkv, int head_dim, int block_size, int max_blocks_per_seq, int splits,
-    int pages_per_split, float scale, int dtype, void* stream) {
+    void* out, int batch, int nq, int nkv, int head_dim, int block_size, int max_blocks_per_seq, int num_blocks,
+    int splits, int pages_per_split, float scale, int dtype, void* stream) {
   g_noalloc_err.clear();
-  if (batch <= 0 || nkv <= 0 || nq <= 0 || nq % nkv != 0 || splits <= 0 || head_dim <= 0)
-    return noalloc_fail(cudaErrorInvalidValue, "invalid geometry");
+  if (batch <= 0 || nkv <= 0 || nq <= 0 || nq % nkv != 0)
+    return noalloc_fail(cudaErrorInvalidValue, "invalid head geometry: need batch > 0, nkv > 0 and nq a multiple of nkv");
+  if (head_dim != 64 && head_dim != 128)
+    return noalloc_fail(cudaErrorInvalidValue, "head_dim must be 64 or 128, got " + std::to_string(head_dim));
+  if (block_size != 16)
+    return noalloc_fail(cudaErrorInvalidValue, "block_size must be 16 (tokens per KV page), got " +
+                                                   std::to_string(block_size));
+  if (dtype != cob::kBF16 && dtype != cob::kF16)
+    return noalloc_fail(cudaErrorInvalidValue, "dtype must be 1 (fp16) or 2 (bf16)");
+  if (max_blocks_per_seq <= 0)
+    return noalloc_fail(cudaErrorInvalidValue, "max_blocks_per_seq must be positive");
+  if (num_blocks <= 0)
+    return noalloc_fail(cudaErrorInvalidValue, "num_blocks (pages in each cache) must be positive");
+  if ((unsigned long long)num_blocks * (unsigned long long)nkv * 16ull >= (1ull << 32))
+    return noalloc_fail(cudaErrorInvalidValue, "cache too large: num_blocks * nkv * 16 rows must stay below 2^32");
+  if (splits <= 0 || pages_per_split <= 0 || pages_per_split > 512)
+    return noalloc_fail(cudaErrorInvalidValue, "need splits > 0 and 0 < pages_per_split <= 512");
+  if ((long long)splits * pages_per_split < max_blocks_per_seq)
+    return noalloc_fail(cudaErrorInvalidValue,
+                        "splits * pages_per_split (" + std::to_string((long long)splits * pages_per_split) +
+                            ") does not cover max_blocks_per_seq (" + std::to_string(max_blocks_per_seq) +
+                            "): the tokens beyond it would be dropped");
   const size_t need = cob::attn_scratch_bytes(batch, nkv, splits, nq / nkv, head_dim);
   if (need > COB_NOALLOC_SCRATCH_BYTES)
     return noalloc_fail(cudaErrorInvalidValue, "split-KV scratch of " + std::to_string(need) +
@@ -562,6 +582,7 @@ extern "C" __attribute__((visibility("default"))) int cob_decode_attention_noall
   p.head_dim = head_dim;
   p.block_size = block_size;
   p.max_blocks_per_seq = max_blocks_per_seq;
+  p.num_blocks = num_blocks;  // the K/V tensor maps end at the caller's cache: stray pages read zeros
   p.splits = splits;
   p.pages_per_split = pages_per_split;
   p.scale = scale;

@@ -347,6 +347,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("v_cache") = pybind11::none(), pybind11::arg("nq") = 0, pybind11::arg("nkv") = 0);
   m.attr("kMaxPieces") = cob::kMaxPieces;
   m.def("fused_gemm_plan", &py_fused_gemm_plan);
+  m.def("ar_norm_gemm_resident_clusters",
+        [](int64_t bn, int64_t splits) { return (int64_t)cob::ar_norm_gemm_resident_clusters((int)bn, (int)splits); });
   m.def("fused_ar_config", &py_fused_ar_config);
   register_ops(m);
   register_ipc(m);

@@ -674,6 +674,21 @@ cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUte
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
+  if (!PUSH) {
+    // CTAs of the consumer wait for pieces that other CTAs of the same launch produce, so every cluster
+    // of the grid must be resident at once. Ask the occupancy calculator for this exact configuration
+    // (cluster shape, shared memory, registers) instead of assuming CTAs per SM; cached per cluster size.
+    static int max_clusters[17] = {};
+    int& mc = max_clusters[pl.splits];
+    if (mc == 0) {
+      cudaLaunchConfig_t q = cfg;
+      q.numAttrs = 1;  // the cluster shape alone
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&mc, fn, &q);
+      if (e != cudaSuccess) return e;
+      if (mc <= 0) mc = -1;
+    }
+    if ((long long)mc < (long long)pl.xctas * ranks) return cudaErrorInvalidValue;
+  }
   FusedGemmParams q = p;
   q.kps = pl.kps;
   if (q.l2_prefetch == 0) q.l2_prefetch = l2_prefetch_tiles();
@@ -782,12 +797,48 @@ cudaError_t launch_ar_norm_gemm(const FusedGemmParams& p, const CUtensorMap& tmW
   // every piece's per-item sums of squares fit in shared memory
   const int KV = p.K / 8, slen = std::min(KV, pl.kps * 8);
   if ((long long)p.M * ((slen + pl.xctas - 1) / pl.xctas + 1) > kQCap) return cudaErrorInvalidValue;
-  // CTAs wait for pieces of other CTAs of the launch: the whole grid must be resident at once
+  // CTAs wait for pieces of other CTAs of the launch: the whole grid must be resident at once (a quick
+  // bound here; launch_t asks the occupancy calculator for the exact cluster configuration)
   int dev = 0, sms = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if ((long long)pl.ctas * ranks > (long long)sms * (pl.bn <= 64 ? 2 : 1)) return cudaErrorInvalidValue;
   return launch_sel<false>(p, tmW, tmA, pl, ranks, pdl, stream);
+}
+
+namespace {
+template <int BN, bool SMALL>
+int consumer_clusters(int splits) {
+  using C = FCfg<BN, SMALL>;
+  auto fn = k_ar_norm_gemm<BN, SMALL>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess ||
+      cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return -1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, splits, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeClusterDimension;
+  a.val.clusterDim.x = 1;
+  a.val.clusterDim.y = splits;
+  a.val.clusterDim.z = 1;
+  cfg.attrs = &a;
+  cfg.numAttrs = 1;
+  int n = 0;
+  return cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess ? n : -1;
+}
+}  // namespace
+
+int ar_norm_gemm_resident_clusters(int bn, int splits) {
+  if (splits < 1 || splits > 16) return -1;
+  switch (bn) {
+    case 16: return consumer_clusters<16, true>(splits);
+    case 32: return consumer_clusters<32, true>(splits);
+    case 64: return consumer_clusters<64, true>(splits);
+    case 128: return consumer_clusters<128, false>(splits);
+    default: return -1;
+  }
 }
 
 }  // namespace cob

@@ -71,6 +71,9 @@ struct FusedGemmPlan {
 // (swiglu, rope) need 2..8 splits per tile (each CTA of a cluster finishes whole row pairs); a plan
 // that cannot meet that returns splits == 0.
 FusedGemmPlan plan_fused_gemm(int M, int N, int K, int splits, int num_sms, bool consumer, int epi = kEpiPlain);
+// Clusters of `splits` consumer CTAs (batch tile width bn) that the occupancy calculator says can be
+// resident on this device at once (-1 on error). launch_ar_norm_gemm rejects grids with more.
+int ar_norm_gemm_resident_clusters(int bn, int splits);
 
 // tmW: [ranks * N, K] weights, box 64 x 128; tmX: [rows, K] activations, box 64 x BN.
 cudaError_t launch_gemm_push(const FusedGemmParams& p, const CUtensorMap& tmW, const CUtensorMap& tmX,

@@ -14,6 +14,12 @@ struct GemmPlan {
 };
 
 GemmPlan plan_gemm(int M, int N, int K, int num_sms, int ctas_override);
+
+// Profiling: when non-null, every decode GEMM launch writes kStampSlots %globaltimer stamps per CTA
+// (entry, set-up, weights issued, dependency wait, last load, first stage landed, last MMA, last
+// accumulator ready, last tile stored, end) at stamps[cta * kStampSlots + phase].
+constexpr int kStampSlots = 16;
+long long*& gemm_stamps();
 // fp32 workspace needed for the partial tiles of a launch with `num_ctas` CTAs
 size_t gemm_workspace_bytes(int num_ctas, int bn);
 

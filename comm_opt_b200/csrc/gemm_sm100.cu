@@ -35,6 +35,19 @@ constexpr int BM = 128, BK = 64;
 constexpr int kThreads = 192;  // warp 0 TMA producer, warp 1 MMA issuer, warps 2-5 epilogue
 constexpr int kSmemBudget = 220 * 1024;
 constexpr int kMaxContrib = 48;  // CTAs sharing one tile (the planner keeps it below this)
+// phase stamp slots per CTA (profiling only; gemm_stamps() == nullptr switches them off)
+enum : int {
+  kStEntry = 0,         // kernel entry
+  kStSetup = 1,         // barriers initialised, TMEM allocated
+  kStWeightsIssued = 2, // producer: first ring of weight tiles issued (before the dependency wait)
+  kStPdlWait = 3,       // producer: previous kernel's data visible
+  kStLastLoad = 4,      // producer: every load issued
+  kStFirstFull = 5,     // MMA issuer: first stage landed
+  kStLastMma = 6,       // MMA issuer: last MMA issued
+  kStAccReady = 7,      // epilogue: last accumulator complete
+  kStEpiDone = 8,       // epilogue: last tile stored (or its partial written)
+  kStEnd = 9,           // all threads done (cluster reduction included), before teardown
+};
 
 // SMALL: half the shared-memory ring, so two CTAs (this kernel and the next one in the stream under
 // programmatic dependent launch) fit on one SM.
@@ -78,8 +91,14 @@ template <int BN, bool BF16, bool SMALL, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
                    int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
-                   int kps, int l2pf) {
+                   int kps, int l2pf, long long* stamps) {
   using C = Cfg<BN, SMALL>;
+  // optional phase stamps (%globaltimer, ns): stamps[cta * kStampSlots + phase]
+  const int lin = blockIdx.x + blockIdx.y * gridDim.x;
+  auto stamp = [&](int phase) {
+    if (stamps != nullptr) stamps[(size_t)lin * kStampSlots + phase] = (long long)globaltimer();
+  };
+  if (threadIdx.x == 0) stamp(kStEntry);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -130,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) stamp(kStSetup);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -147,7 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const long long g = beg + i;
         tma_prefetch_l2(&tmW, (int)(g % KT) * BK, (int)(g / KT) * BM);
       }
+      stamp(kStWeightsIssued);
       pdl_wait();
+      stamp(kStPdlWait);
       for (int i = 0; i < pre; ++i) {
         const long long g = beg + i;
         tma_load_2d(sB + i * C::B_BYTES, &tmX, &full[i], (int)(g % KT) * BK, 0);
@@ -166,6 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = i + 1;
       }
       *s_issued = issued;
+      stamp(kStLastLoad);
       pdl_trigger();  // every load is issued: the next kernel may start its prologue
     }
   } else if (warp == 1) {
@@ -192,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          if (i == 0) stamp(kStFirstFull);
           const uint32_t a = smem_addr(sA + s * C::A_BYTES), b = smem_addr(sB + s * C::B_BYTES);
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk)
@@ -202,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         g += k1 - k0;
       }
       *s_consumed = i;
+      stamp(kStLastMma);
     }
   } else {
     // ------------------------------------------------ epilogue: warps 2..5, TMEM lane quarter = warp % 4
@@ -219,6 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[acc], (j >> 1) & 1, timeout_ns)) *s_fail = 1;
       __syncwarp();
       tc_fence_after();
+      if (q == 2 && lane == 0) stamp(kStAccReady);
       const uint32_t taddr = tmem + acc * C::TC + ((uint32_t)(q * 32) << 16);
       // partial segments go to workspace slot 0 (first tile of this CTA) or 1 (its last tile),
       // row-major [row][BN] so the finisher reads 16-byte vectors; in cluster mode to this CTA's
@@ -242,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
+      if (q == 2 && lane == 0) stamp(kStEpiDone);
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&tempty[acc])) : "memory");
       if (!CLUSTER && !whole) {
         // last contributor of tile t sums every contributor's partial in CTA order
@@ -332,6 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ------------------------------------------------ teardown
   __syncthreads();
+  if (threadIdx.x == 0) stamp(kStEnd);
   if (threadIdx.x == 0 && *s_fail) {
     atomicOr(err, 1);
     // drain TMA loads that were issued but never consumed before shared memory is released
@@ -384,7 +412,8 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps, l2_prefetch_tiles());
+  return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps, l2_prefetch_tiles(),
+                            gemm_stamps());
 }
 
 template <bool BF16, bool SMALL>
@@ -410,6 +439,11 @@ cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, v
 }
 
 }  // namespace
+
+long long*& gemm_stamps() {
+  static long long* p = nullptr;
+  return p;
+}
 
 GemmPlan plan_gemm(int M, int N, int K, int num_sms, int ctas_override) {
   GemmPlan p = {};

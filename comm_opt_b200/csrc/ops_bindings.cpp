@@ -338,6 +338,7 @@ void register_ops(pybind11::module& m) {
         pybind11::arg("local_keys") = pybind11::none());
   m.def("set_pdl", [](bool on) { cob::pdl_flag() = on; });
   m.def("get_pdl", []() { return cob::pdl_flag(); });
+  m.def("set_gemm_stamps", [](int64_t ptr) { cob::gemm_stamps() = reinterpret_cast<long long*>(ptr); });
   m.def("set_l2_prefetch", [](int64_t tiles) { cob::l2_prefetch_tiles() = (int)std::max<int64_t>(0, tiles); });
   m.def("get_l2_prefetch", []() { return (int64_t)cob::l2_prefetch_tiles(); });
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);

@@ -658,38 +658,44 @@ class TPDecodeRunner:
             self._car = None
 
 
+def reference_logits(cfg: LlamaConfig, full: dict, tokens: torch.Tensor, device) -> torch.Tensor:
+    """Unsharded fp32 forward of `tokens` [B, T] (no KV cache: full recompute); logits [B, vocab] of
+    the last position."""
+    W = {k: v for k, v in full.items() if k != "layers"}
+    D = cfg.head_dim
+    toks = tokens.to(device).long()
+    B, P = toks.shape
+    cos, sin = rope_tables(P, D, cfg.rope_theta, device)
+    c, sn = cos[:P][None, :, None, :], sin[:P][None, :, None, :]
+
+    def rope(t):
+        t1, t2 = t[..., :D // 2], t[..., D // 2:]
+        return torch.cat([t1 * c - t2 * sn, t2 * c + t1 * sn], -1)
+
+    x = W["embed"].to(device).float()[toks]
+    for L in full["layers"]:
+        L = {k: v.to(device).float() for k, v in L.items()}
+        h = F.rms_norm(x, (cfg.hidden,), L["ln1"], cfg.eps)
+        qkv = h @ L["wqkv"].t() + (L["bqkv"] if "bqkv" in L else 0.0)
+        q, k, v = qkv.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
+        q, k = rope(q.view(B, P, cfg.heads, D)), rope(k.view(B, P, cfg.kv_heads, D))
+        v = v.view(B, P, cfg.kv_heads, D)
+        a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
+                                           enable_gqa=True, scale=1.0 / math.sqrt(D))
+        x = x + a.transpose(1, 2).reshape(B, P, -1) @ L["wo"].t()
+        h = F.rms_norm(x, (cfg.hidden,), L["ln2"], cfg.eps)
+        g, u = (h @ L["wgu"].t()).chunk(2, -1)
+        x = x + (F.silu(g) * u) @ L["wdown"].t()
+    h = F.rms_norm(x[:, -1], (cfg.hidden,), W["final_norm"].to(device).float(), cfg.eps)
+    return h @ W["lm_head"].to(device).float().t()
+
+
 def reference_greedy(cfg: LlamaConfig, full: dict, prompts: torch.Tensor, steps: int, device) -> torch.Tensor:
     """Unsharded fp32 greedy decoding (no KV cache: full recompute), tokens [B, steps+1]."""
-    W = {k: v for k, v in full.items() if k != "layers"}
-    layers = full["layers"]
-    D = cfg.head_dim
-    cos, sin = rope_tables(prompts.shape[1] + steps + 1, D, cfg.rope_theta, device)
     toks = prompts.to(device).long()
     out = []
     for _ in range(steps + 1):
-        B, P = toks.shape
-        x = W["embed"].to(device).float()[toks]
-        c, sn = cos[:P][None, :, None, :], sin[:P][None, :, None, :]
-
-        def rope(t):
-            t1, t2 = t[..., :D // 2], t[..., D // 2:]
-            return torch.cat([t1 * c - t2 * sn, t2 * c + t1 * sn], -1)
-
-        for L in layers:
-            L = {k: v.to(device).float() for k, v in L.items()}
-            h = F.rms_norm(x, (cfg.hidden,), L["ln1"], cfg.eps)
-            qkv = h @ L["wqkv"].t() + (L["bqkv"] if "bqkv" in L else 0.0)
-            q, k, v = qkv.split([cfg.heads * D, cfg.kv_heads * D, cfg.kv_heads * D], -1)
-            q, k = rope(q.view(B, P, cfg.heads, D)), rope(k.view(B, P, cfg.kv_heads, D))
-            v = v.view(B, P, cfg.kv_heads, D)
-            a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
-                                               enable_gqa=True, scale=1.0 / math.sqrt(D))
-            x = x + a.transpose(1, 2).reshape(B, P, -1) @ L["wo"].t()
-            h = F.rms_norm(x, (cfg.hidden,), L["ln2"], cfg.eps)
-            g, u = (h @ L["wgu"].t()).chunk(2, -1)
-            x = x + (F.silu(g) * u) @ L["wdown"].t()
-        h = F.rms_norm(x[:, -1], (cfg.hidden,), W["final_norm"].to(device).float(), cfg.eps)
-        nxt = (h @ W["lm_head"].to(device).float().t()).argmax(-1)
+        nxt = reference_logits(cfg, full, toks, device).argmax(-1)
         out.append(nxt)
         toks = torch.cat([toks, nxt[:, None]], 1)
     return torch.stack(out, 1)

@@ -44,8 +44,27 @@ def env_snapshot() -> str:
 
 
 def gpu_state() -> str:
-    q = _sh("nvidia-smi --query-gpu=clocks.sm,temperature.gpu,power.draw --format=csv,noheader,nounits")
-    return ";".join(l.replace(", ", "/") for l in q.splitlines() if l)
+    """SM clock (MHz), temperature (C) and power (W) of every GPU, read through NVML, as
+    'clock/temp/power' per GPU joined by ';' ('' when NVML cannot be read)."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+    except Exception:
+        return ""
+    parts = []
+    try:
+        for i in range(pynvml.nvmlDeviceGetCount()):
+            h = pynvml.nvmlDeviceGetHandleByIndex(i)
+            clk = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+            temp = pynvml.nvmlDeviceGetTemperature(h, pynvml.NVML_TEMPERATURE_GPU)
+            watts = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+            parts.append(f"{clk}/{temp}/{watts:.0f}")
+    except Exception:
+        pass
+    finally:
+        pynvml.nvmlShutdown()
+    return ";".join(parts)
 
 
 class RunDir:
@@ -53,6 +72,16 @@ class RunDir:
         self.path = (base or ROOT / "results") / exp / (ts or time.strftime("%Y%m%d_%H%M%S"))
         self.path.mkdir(parents=True, exist_ok=True)
         self._sched = None
+
+    @classmethod
+    def at(cls, path: Path) -> "RunDir":
+        """An existing run directory (to resume a plan into it)."""
+        path = Path(path)
+        if not path.is_dir():
+            raise FileNotFoundError(path)
+        obj = cls.__new__(cls)
+        obj.path, obj._sched = path, None
+        return obj
 
     def snapshot(self):
         (self.path / "env.txt").write_text(env_snapshot())

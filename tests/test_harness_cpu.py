@@ -4,6 +4,8 @@ import os
 import subprocess
 import sys
 
+import pytest
+
 from conftest import ROOT, free_port
 
 
@@ -24,25 +26,82 @@ def test_collectives_gloo_two_ranks(tmp_path):
 
 def test_runner_dry_run_prints_commands():
     env = dict(os.environ, DRY_RUN="1")
-    code = ("from comm_opt_b200.harness.runner import *; run_all(collective_baseline_jobs((2, 8)), 'x', 3);"
-            "run_all(nccl_variant_jobs(8), 'y', 4); run_all(fused_hidden_jobs(8), 'z', 5)")
+    code = ("from comm_opt_b200.harness.runner import *; execute(collective_baseline_plan((2, 8)), 'x', 3);"
+            "execute(nccl_variant_plan(8), 'y', 4); execute(fused_hidden_plan(8), 'z', 5)")
     p = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True)
     assert p.returncode == 0, p.stderr
     lines = [l for l in p.stdout.splitlines() if "torch.distributed.run" in l]
     assert len(lines) == 2 + 6 + 6 and all("127.0.0.1" in l and "timeout" in l for l in lines)
     assert sum("--hidden 1024" in l and "--tokens 8,16,32" in l for l in lines) == 1
+    assert "dry run of plan 'x': 2 launches" in p.stderr
+
+
+def test_runner_order_is_seeded_and_independent_of_list_order():
+    from comm_opt_b200.harness.runner import Launch, ordered
+
+    plan = [Launch("bench", 8, label=f"v{i}") for i in range(12)]
+    a, b = ordered(plan, 1), ordered(list(reversed(plan)), 1)
+    assert [l.name for l in a] == [l.name for l in b]
+    assert [l.name for l in ordered(plan, 2)] != [l.name for l in a]
+    with pytest.raises(ValueError):
+        ordered(plan + [Launch("bench", 8, label="v0")], 0)
+
+
+def test_runner_placements():
+    from comm_opt_b200.harness.runner import Launch, compose, placement_devices
+
+    assert placement_devices(2) == [0, 1] and placement_devices(2, "mirror") == [7, 6]
+    assert placement_devices(8, "mirror") == list(range(7, -1, -1))
+    with pytest.raises(ValueError):
+        placement_devices(9)
+    _, env = compose(Launch("bench", 4, placement="mirror"), ROOT / "results" / "x", 29999)
+    assert env["CUDA_VISIBLE_DEVICES"] == "7,6,5,4"
+
+
+def test_runner_resume_skips_finished_launches(tmp_path, monkeypatch):
+    """A launch whose log exists in the run directory is not run again; the others are, in seeded order,
+    each recorded in schedule.tsv with its placement."""
+    import comm_opt_b200.harness.runner as R
+
+    ran = []
+
+    def fake_run(cmd, stdout, stderr, env, cwd):
+        ran.append(env["CUDA_VISIBLE_DEVICES"])
+        return subprocess.CompletedProcess(cmd, 0)
+
+    monkeypatch.setattr(R.subprocess, "run", fake_run)
+    monkeypatch.setattr(R, "foreign_gpu_pids", lambda devices: [])
+    monkeypatch.setattr(R, "gpu_state", lambda: "")
+    (tmp_path / "r").mkdir()
+    plan = [R.Launch("bench", 2, label="a"), R.Launch("bench", 2, placement="mirror", label="b")]
+    (tmp_path / "r" / f"{plan[0].name}.log").write_text("done before")
+    out = R.execute(plan, "p", 0, resume=tmp_path / "r")
+    assert out == tmp_path / "r" and ran == ["7,6"]
+    sched = (tmp_path / "r" / "schedule.tsv").read_text().splitlines()
+    assert len(sched) == 2 and '"placement": "mirror"' in sched[1]
+
+
+def test_runner_halts_beside_foreign_processes(tmp_path, monkeypatch):
+    import comm_opt_b200.harness.runner as R
+
+    monkeypatch.setattr(R, "foreign_gpu_pids", lambda devices: [(devices[0], 4242, 1000)])
+    monkeypatch.setattr(R, "gpu_state", lambda: "")
+    monkeypatch.setattr(R.subprocess, "run", lambda *a, **k: pytest.fail("must not launch"))
+    (tmp_path / "r").mkdir()
+    with pytest.raises(SystemExit, match="pid 4242"):
+        R.execute([R.Launch("bench", 2)], "p", 0, resume=tmp_path / "r")
 
 
 def test_runner_headline_plan():
-    from comm_opt_b200.harness.runner import command, headline_jobs
+    from comm_opt_b200.harness.runner import compose, headline_plan
 
-    jobs = headline_jobs((2, 4, 8))
-    # per GPU count: 2 sweeps, boundary, 4 decode forms (fused, separate, NCCL stack, vLLM stack),
-    # 8B x 3 batches x 2 collectives; 3 extra 70B batches at 8
-    assert len(jobs) == 3 * (7 + 6) + 3
-    cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
-    assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3 + 9
-    assert sum("bench.py" in c and "--collective vllm" in c for c in cmds) == 3
+    plan = headline_plan((2, 4, 8))
+    # per world: 2 sweeps, boundary, 4 decode forms (fused, separate, NCCL stack, vLLM stack),
+    # 8B x 3 batches x 2 collectives; 3 extra 70B batches at 8 in the same 4 forms
+    assert len(plan) == 3 * (7 + 6) + 3 * 4
+    cmds = [" ".join(compose(l, ROOT / "results" / "x", 29000 + i)[0]) for i, l in enumerate(plan)]
+    assert sum("bench.py" in c and "--collective nccl" in c for c in cmds) == 3 + 3 + 9
+    assert sum("bench.py" in c and "--collective vllm" in c for c in cmds) == 3 + 3
     assert sum("--model 8b --prompt 1024" in c for c in cmds) == 18
     assert all(("bench.py" in c) != (" -m comm_opt_b200" in c.split("torch.distributed.run")[1]) for c in cmds)
     assert sum("ref_m16nf" in c for c in cmds) == 2  # both sweeps at 8 GPUs
@@ -111,12 +170,12 @@ def test_phase_decomposition_from_stamps():
 
 def test_bakeoff_shapes_and_runner_entries():
     from comm_opt_b200.harness.allreduce_bakeoff import shape_of
-    from comm_opt_b200.harness.runner import ENTRY, Job, command
+    from comm_opt_b200.harness.runner import TARGETS, Launch, compose
 
     assert shape_of(1024, 2) == (1, 512) and shape_of(8 << 20, 2) == (512, 8192) and shape_of(48 << 10, 2) == (3, 8192)
-    for e in ("bakeoff", "phases", "collectives", "fused_sweep", "selftest"):
-        assert e in ENTRY
-    cmd, env = command(Job("bakeoff", 8), ROOT / "results" / "x", 29999)
+    for e in ("bakeoff", "phases", "collectives", "fused_sweep", "selftest", "probes"):
+        assert e in TARGETS
+    cmd, env = compose(Launch("bakeoff", 8), ROOT / "results" / "x", 29999)
     assert "--out-dir" in cmd and env["CUDA_VISIBLE_DEVICES"] == "0,1,2,3,4,5,6,7"
 
 
@@ -141,17 +200,17 @@ def test_report_tables(tmp_path):
 def test_e2e_share_plan():
     """The M5 matrix: 1B / 8B x TP 8 / 4 / 2 x 3 launches of training, plus the decode comm-share jobs; each
     job writes its traces into its own directory."""
-    from comm_opt_b200.harness.runner import Job, command, e2e_share_jobs
+    from comm_opt_b200.harness.runner import Launch, compose, e2e_share_plan
 
-    jobs = e2e_share_jobs(8)
-    train = [j for j in jobs if j.entry == "train_share"]
-    assert len(train) == 18 and {j.variant for j in train} == {f"{m}_tp{t}" for m in ("1b", "8b") for t in (8, 4, 2)}
-    share = [j for j in jobs if j.entry == "comm_share"]
-    assert len(share) == 6 + 8 and {j.variant for j in share if j.variant.startswith("qwen32b")} == {
+    plan = e2e_share_plan(8)
+    train = [l for l in plan if l.target == "train_share"]
+    assert len(train) == 18 and {l.label for l in train} == {f"{m}_tp{t}" for m in ("1b", "8b") for t in (8, 4, 2)}
+    share = [l for l in plan if l.target == "comm_share"]
+    assert len(share) == 6 + 8 and {l.label for l in share if l.label.startswith("qwen32b")} == {
         f"qwen32b_b{b}" for b in (1, 8, 32, 128)}
-    cmd, _ = command(Job("train_share", 8, variant="8b_tp4"), ROOT / "results" / "x", 29999)
-    assert cmd[-1].endswith("runs/train_share_g8A_8b_tp4_r0") and "comm_opt_b200.harness.train_share" in cmd
-    assert len(e2e_share_jobs(4, reps=1)) == 4 + 6 + 8  # TP 8 needs 8 GPUs
+    cmd, _ = compose(Launch("train_share", 8, label="8b_tp4"), ROOT / "results" / "x", 29999)
+    assert cmd[-1].endswith("runs/train_share.w8.low.8b_tp4.0") and "comm_opt_b200.harness.train_share" in cmd
+    assert len(e2e_share_plan(4, repeats=1)) == 4 + 6 + 8  # TP 8 needs 8 GPUs
 
 
 def test_nccl_log_summary_and_gpuset_comparison(tmp_path):
@@ -188,16 +247,16 @@ def test_nccl_log_summary_and_gpuset_comparison(tmp_path):
 
 
 def test_repeat_and_p2p_channel_plans():
-    from comm_opt_b200.harness.runner import Job, command, p2p_channel_jobs, repeat_jobs
+    from comm_opt_b200.harness.runner import Launch, compose, p2p_channel_plan, repeat_plan
 
-    rj = repeat_jobs(5)
-    assert len(rj) == (3 + 2 * 5) * 2 * 5 and {j.gpuset for j in rj} == {"A", "B"}
-    pj = p2p_channel_jobs(5)
-    assert len(pj) == 5 * 2 * 5 + 3 * 5
-    assert any(j.env.get("NCCL_MIN_P2P_NCHANNELS") == "64" for j in pj)
-    cmd, env = command(Job("collectives", 8, env={"NCCL_DEBUG": "WARN"}), ROOT / "results" / "x", 29999)
+    rp = repeat_plan(5)
+    assert len(rp) == (3 + 2 * 5) * 2 * 5 and {l.placement for l in rp} == {"low", "mirror"}
+    pp = p2p_channel_plan(5)
+    assert len(pp) == 5 * 2 * 5 + 3 * 5
+    assert any(l.env.get("NCCL_MIN_P2P_NCHANNELS") == "64" for l in pp)
+    cmd, env = compose(Launch("collectives", 8, env={"NCCL_DEBUG": "WARN"}), ROOT / "results" / "x", 29999)
     assert env["NCCL_DEBUG"] == "WARN" and env["NCCL_DEBUG_SUBSYS"] == "INIT,ENV,GRAPH"
-    assert env["NCCL_DEBUG_FILE"].endswith("collectives_g8A_default_r0.nccl.%h.%p.log")
+    assert env["NCCL_DEBUG_FILE"].endswith("collectives.w8.low.default.0.nccl.%h.%p.log")
 
 
 def test_figures_from_runs(tmp_path):
@@ -351,15 +410,15 @@ def test_bench_clock_summary():
 def test_validate_plan():
     """The first-GPU-run plan: self-test parts with the experimental variants, A/B sweeps at every GPU
     count, the decode bench with the new switches on and off."""
-    from comm_opt_b200.harness.runner import command, validate_jobs
+    from comm_opt_b200.harness.runner import compose, validate_plan
 
-    jobs = validate_jobs((2, 4, 8))
-    assert sum(j.entry == "selftest" for j in jobs) == 2 and all(j.env.get("COB_EXPERIMENTAL") == "1"
-                                                                 for j in jobs if j.entry in ("selftest", "fused_sweep"))
-    assert sorted(j.ngpus for j in jobs if j.entry == "fused_sweep") == [2, 4, 8]
-    attn = [j for j in jobs if j.entry == "boundary"]
-    assert [(j.ngpus, j.args) for j in attn if j.ngpus == 8] == [(8, ("--k1", "1024", "--n2", "7168"))]
-    cmds = [" ".join(command(j, ROOT / "results" / "x", 29000 + i)[0]) for i, j in enumerate(jobs)]
+    plan = validate_plan((2, 4, 8))
+    assert sum(l.target == "selftest" for l in plan) == 2 and all(l.env.get("COB_EXPERIMENTAL") == "1"
+                                                                  for l in plan if l.target in ("selftest", "fused_sweep"))
+    assert sorted(l.world for l in plan if l.target == "fused_sweep") == [2, 4, 8]
+    attn = [l for l in plan if l.target == "boundary"]
+    assert [(l.world, l.argv) for l in attn if l.world == 8] == [(8, ("--k1", "1024", "--n2", "7168"))]
+    cmds = [" ".join(compose(l, ROOT / "results" / "x", 29000 + i)[0]) for i, l in enumerate(plan)]
     assert sum("--l2-prefetch" in c for c in cmds) == 3 and sum("--tune-boundaries 0" in c for c in cmds) == 1
     assert any("decode_vllm" in c for c in cmds) and any("ours:lamport_1sx" in c for c in cmds)
 
