@@ -186,7 +186,7 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
                                    c10::optional<torch::Tensor> positions, c10::optional<torch::Tensor> cos_t,
                                    c10::optional<torch::Tensor> sin_t, c10::optional<torch::Tensor> block_tables,
                                    c10::optional<torch::Tensor> k_cache, c10::optional<torch::Tensor> v_cache,
-                                   int64_t nq, int64_t nkv) {
+                                   int64_t nq, int64_t nkv, bool packed) {
   cob::FusedGemmParams p = {};
   COB_CHECK(bases.size() >= 1 && bases.size() <= cob::kMaxWorld, "world must be 1..8");
   for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
@@ -203,7 +203,14 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
   check_dense(w, "w");
   check_dense(err, "err");
   COB_CHECK(w.scalar_type() == torch::kBFloat16, "fused GEMMs take bf16 weights");
-  COB_CHECK(w.numel() == (int64_t)ranks * N * K, "w must hold ranks * N * K elements");
+  const int64_t wtiles = (N + 127) / 128;
+  if (packed)  // [ranks * ceil(N / 128), K / 64, 128, 64] blocks (see gemm.h)
+    COB_CHECK(K % 64 == 0 && w.numel() == (int64_t)ranks * wtiles * 128 * K,
+              "packed w must hold ranks * ceil(N / 128) * 128 * K elements");
+  else
+    COB_CHECK(w.numel() == (int64_t)ranks * N * K, "w must hold ranks * N * K elements");
+  p.wp = packed ? reinterpret_cast<const uint8_t*>(w.data_ptr()) : nullptr;
+  p.w_tiles = (int)wtiles;
   COB_CHECK(err.scalar_type() == torch::kInt32, "err must be int32");
   COB_CHECK(p.L.world == p.world && p.L.esize == 2, "communicator layout must be bf16 with this world");
   p.err = reinterpret_cast<int*>(err.data_ptr());
@@ -238,9 +245,10 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
     p.bs = (int)k_cache->size(-2);
     p.cache_rs = emulate ? k_cache->numel() / ranks : 0;
   }
-  CUtensorMap tw, tb;
-  check_cuda(cob::tensor_map_2d(w.data_ptr(), (uint64_t)ranks * N, (uint64_t)K, (uint64_t)K * 2, 128, 64, true, &tw),
-             "weight tensor map");
+  CUtensorMap tw = {}, tb;
+  if (!packed)
+    check_cuda(cob::tensor_map_2d(w.data_ptr(), (uint64_t)ranks * N, (uint64_t)K, (uint64_t)K * 2, 128, 64, true, &tw),
+               "weight tensor map");
   cudaError_t rc;
   if (kind == 0) {
     COB_CHECK(x.has_value(), "gemm_push needs x");
@@ -344,7 +352,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("dry_run"), pybind11::arg("epi") = 0, pybind11::arg("positions") = pybind11::none(),
         pybind11::arg("cos") = pybind11::none(), pybind11::arg("sin") = pybind11::none(),
         pybind11::arg("block_tables") = pybind11::none(), pybind11::arg("k_cache") = pybind11::none(),
-        pybind11::arg("v_cache") = pybind11::none(), pybind11::arg("nq") = 0, pybind11::arg("nkv") = 0);
+        pybind11::arg("v_cache") = pybind11::none(), pybind11::arg("nq") = 0, pybind11::arg("nkv") = 0,
+        pybind11::arg("packed") = false);
   m.attr("kMaxPieces") = cob::kMaxPieces;
   m.def("fused_gemm_plan", &py_fused_gemm_plan);
   m.def("ar_norm_gemm_resident_clusters",

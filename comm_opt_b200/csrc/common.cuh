@@ -158,6 +158,13 @@ __device__ __forceinline__ uint64_t globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// The same clock for phase stamps: the memory clobber keeps the read in program order with the
+// surrounding barriers and memory operations (a plain read may be scheduled ahead of a barrier).
+__device__ __forceinline__ uint64_t globaltimer_ordered() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
+  return t;
+}
 
 __device__ __forceinline__ uint4 ld_vol_v4(const void* p) {
   uint4 v;

@@ -37,6 +37,9 @@
 // wait is bounded (%globaltimer) and a timeout sets the rank's error word and *err.
 #include <cooperative_groups.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "fused_gemm.h"
 #include "sm100.cuh"
 #include "tma_host.h"
@@ -176,7 +179,7 @@ template <int BN, bool SMALL, bool WAIT_ACT>
 __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtensorMap* tmW, const CUtensorMap* tmB,
                                          uint8_t* smem, const Ctrl& c, uint32_t tmem, int k0, int nsteps, int wrow,
                                          int wstride, int nt, int brow, const uint32_t* split_flags, int nflags,
-                                         uint32_t tag) {
+                                         uint32_t tag, int wtile0) {
   using C = FCfg<BN, SMALL>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint8_t* sA = smem;
@@ -186,13 +189,29 @@ __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtenso
     const int pre = min(C::STAGES, total);
     auto wr = [&](int i) { return wrow + (i / nsteps) * wstride; };
     auto kx = [&](int i) { return (k0 + i % nsteps) * BK; };
+    // packed weights (p.wp): 16 KB block (tile, k-step) of this rank at wp + (tile * KT + k) * 16 KB
+    const int KT = p.K / BK;
+    auto wblock = [&](int i) {
+      return p.wp + ((size_t)(wtile0 + (i / nsteps) * (wstride / BM)) * KT + (k0 + i % nsteps)) * C::A_BYTES;
+    };
+    auto load_w = [&](int s, int i) {
+      if (p.wp != nullptr)
+        bulk_load(sA + s * C::A_BYTES, wblock(i), C::A_BYTES, &c.full[s]);
+      else
+        tma_load_2d(sA + s * C::A_BYTES, tmW, &c.full[s], kx(i), wr(i));
+    };
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&c.full[i], C::STAGE);
-        tma_load_2d(sA + i * C::A_BYTES, tmW, &c.full[i], kx(i), wr(i));
+        load_w(i, i);
       }
       // the next weight tiles into L2 while the activations are awaited (later stages then hit L2)
-      for (int i = pre; i < min(total, pre + p.l2_prefetch); ++i) tma_prefetch_l2(tmW, kx(i), wr(i));
+      for (int i = pre; i < min(total, pre + p.l2_prefetch); ++i) {
+        if (p.wp != nullptr)
+          bulk_prefetch_l2(wblock(i), C::A_BYTES);
+        else
+          tma_prefetch_l2(tmW, kx(i), wr(i));
+      }
       if (!WAIT_ACT) pdl_wait();
     }
     bool ok = true;
@@ -214,7 +233,7 @@ __device__ __forceinline__ void mainloop(const FusedGemmParams& p, const CUtenso
             break;
           }
           mbar_arrive_expect_tx(&c.full[s], C::STAGE);
-          tma_load_2d(sA + s * C::A_BYTES, tmW, &c.full[s], kx(i), wr(i));
+          load_w(s, i);
           tma_load_2d(sB + s * C::B_BYTES, tmB, &c.full[s], kx(i), brow);
           issued = i + 1;
         }
@@ -327,7 +346,7 @@ __device__ __forceinline__ uint32_t setup(uint8_t* smem, const Ctrl& c, int full
                                           const CUtensorMap* b) {
   using C = FCfg<BN, SMALL>;
   if (threadIdx.x == 0) {
-    prefetch_tmap(a);
+    if (a != nullptr) prefetch_tmap(a);
     prefetch_tmap(b);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&c.full[s], full_count);
@@ -364,10 +383,10 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   const int t = blockIdx.x, r = blockIdx.y, cs = gridDim.y;
   const int KT = p.K / BK;
   const int k0 = r * p.kps, nsteps = min(KT, k0 + p.kps) - k0;
-  const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, &tmW, &tmX);
+  const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, p.wp != nullptr ? nullptr : &tmW, &tmX);
 
   mainloop<BN, SMALL, false>(p, &tmW, &tmX, smem, c, tmem, k0, nsteps, (p.emulate ? rank * p.N : 0) + t * BM, 0, 1,
-                             p.emulate ? rank * p.M : 0, nullptr, 0, 0u);
+                             p.emulate ? rank * p.M : 0, nullptr, 0, 0u, (p.emulate ? rank : 0) * p.w_tiles + t);
   if (threadIdx.x >= 64) tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
   pdl_wait();  // every thread: the epoch below was written by an earlier kernel of the stream
   const uint64_t e = fg_epoch(p, rank);
@@ -417,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   const int piece = r * tiles + t;
   uint32_t* flags = p.flags + (size_t)wsr * kMaxPieces;
   float* pss = p.pss + (size_t)wsr * kMaxPieces * p.act_rows;
-  const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, &tmW, &tmA);
+  const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, p.wp != nullptr ? nullptr : &tmW, &tmA);
   // The weight stream needs nothing from earlier kernels and starts at once (warp 0). The pieces
   // (warps 2-5) first wait, in hardware, for the preceding kernel - this rank's gemm_push - to
   // complete, so on this GPU nothing spins on a kernel that runs concurrently; the polls that
@@ -428,7 +447,8 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   const int slot = (int)(e & 1);
 
   mainloop<BN, SMALL, true>(p, &tmW, &tmA, smem, c, tmem, k0, nsteps, (p.emulate ? rank * p.N : 0) + t * BM,
-                            tiles * BM, nt, wsr * p.act_rows, flags + (size_t)r * tiles, tiles, tag);
+                            tiles * BM, nt, wsr * p.act_rows, flags + (size_t)r * tiles, tiles, tag,
+                            (p.emulate ? rank : 0) * p.w_tiles + t);
 
   if (threadIdx.x >= 64) {
     const int tid = threadIdx.x - 64;
@@ -641,6 +661,44 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   teardown<BN, SMALL>(p, c, tmem, rank);
 }
 
+// Clusters of `splits` consumer CTAs that can be resident on this device at once. The occupancy
+// calculator places clusters on the GPCs (cudaOccupancyMaxActiveClusters), but for this kernel it
+// reports one CTA per SM, while its resources (registers from the compiled function, shared memory,
+// threads) admit two SMALL CTAs per SM and launches of 224 mutually waiting CTAs complete on B200; so
+// its cluster count is scaled by the per-SM count computed here from the same resources. Cached per
+// cluster size; COB_CLUSTER_OCCUPANCY=0 switches the check off. Returns -1 if a query failed.
+template <int BN, bool SMALL>
+int consumer_cluster_capacity(const void* fn, const cudaLaunchConfig_t& cfg, int splits) {
+  static int cap[17] = {};
+  static const bool check = [] {
+    const char* v = getenv("COB_CLUSTER_OCCUPANCY");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (!check) return 1 << 20;
+  if (splits < 1 || splits > 16) return -1;
+  if (cap[splits] != 0) return cap[splits];
+  using C = FCfg<BN, SMALL>;
+  int dev = 0, regs_sm = 0, smem_sm = 0, reserved = 0, threads_sm = 0, calc = 0, clusters = 0;
+  cudaFuncAttributes fa;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaFuncGetAttributes(&fa, fn) != cudaSuccess ||
+      cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&threads_sm, cudaDevAttrMaxThreadsPerMultiProcessor, dev) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&calc, fn, kThreads, C::SMEM) != cudaSuccess)
+    return -1;
+  cudaLaunchConfig_t q = cfg;
+  q.numAttrs = 1;  // the cluster shape alone
+  if (cudaOccupancyMaxActiveClusters(&clusters, fn, &q) != cudaSuccess) return -1;
+  const int regs_cta = ((fa.numRegs * 32 + 255) / 256) * 256 * (kThreads / 32);
+  int own = std::min({regs_sm / std::max(1, regs_cta),
+                      smem_sm / (C::SMEM + (int)fa.sharedSizeBytes + reserved), threads_sm / kThreads,
+                      SMALL ? 2 : 1});
+  own = std::max(own, calc);
+  cap[splits] = calc > 0 ? clusters * own / calc : 0;
+  return cap[splits];
+}
+
 template <int BN, bool SMALL, bool PUSH>
 cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUtensorMap& tb, const FusedGemmPlan& pl,
                      int ranks, bool pdl, cudaStream_t stream) {
@@ -652,6 +710,10 @@ cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUte
     if (e != cudaSuccess) return e;
     // clusters of 16 CTAs (split-K 16 for narrow outputs such as QKV at TP=8) are non-portable
     e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    // the whole shared-memory carve-out, so that two SMALL CTAs fit on an SM (and the occupancy
+    // calculator, which follows this preference, says so)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -676,17 +738,9 @@ cudaError_t launch_t(const FusedGemmParams& p, const CUtensorMap& tw, const CUte
   cfg.numAttrs = na;
   if (!PUSH) {
     // CTAs of the consumer wait for pieces that other CTAs of the same launch produce, so every cluster
-    // of the grid must be resident at once. Ask the occupancy calculator for this exact configuration
-    // (cluster shape, shared memory, registers) instead of assuming CTAs per SM; cached per cluster size.
-    static int max_clusters[17] = {};
-    int& mc = max_clusters[pl.splits];
-    if (mc == 0) {
-      cudaLaunchConfig_t q = cfg;
-      q.numAttrs = 1;  // the cluster shape alone
-      cudaError_t e = cudaOccupancyMaxActiveClusters(&mc, fn, &q);
-      if (e != cudaSuccess) return e;
-      if (mc <= 0) mc = -1;
-    }
+    // of the grid must be resident at once: reject grids larger than that (the caller falls back).
+    const int mc = consumer_cluster_capacity<BN, SMALL>(reinterpret_cast<const void*>(fn), cfg, pl.splits);
+    if (mc < 0) return cudaErrorUnknown;
     if ((long long)mc < (long long)pl.xctas * ranks) return cudaErrorInvalidValue;
   }
   FusedGemmParams q = p;
@@ -732,6 +786,9 @@ cudaError_t check_common(const FusedGemmParams& p, const FusedGemmPlan& pl, int 
       return cudaErrorInvalidValue;
   }
   if ((long long)pl.kps * (pl.splits - 1) >= p.K / BK) return cudaErrorInvalidValue;  // every split non-empty
+  // packed weights: whole 16 KB blocks, one block row per 128-row tile of each rank
+  if (p.wp != nullptr && ((reinterpret_cast<uintptr_t>(p.wp) & 15) || p.w_tiles != (p.N + BM - 1) / BM))
+    return cudaErrorInvalidValue;
   return cudaSuccess;
 }
 
@@ -812,26 +869,31 @@ int consumer_clusters(int splits) {
   using C = FCfg<BN, SMALL>;
   auto fn = k_ar_norm_gemm<BN, SMALL>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess ||
-      cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess ||
+      cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) !=
+          cudaSuccess)
     return -1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1, splits, 1);
+  cfg.gridDim = dim3(1, splits > 0 ? splits : 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cudaLaunchAttribute a;
   a.id = cudaLaunchAttributeClusterDimension;
   a.val.clusterDim.x = 1;
-  a.val.clusterDim.y = splits;
+  a.val.clusterDim.y = splits > 0 ? splits : 1;
   a.val.clusterDim.z = 1;
   cfg.attrs = &a;
   cfg.numAttrs = 1;
   int n = 0;
-  return cudaOccupancyMaxActiveClusters(&n, fn, &cfg) == cudaSuccess ? n : -1;
+  if (splits == 0) {  // CTAs per SM by the occupancy calculator (diagnostic)
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, kThreads, C::SMEM) == cudaSuccess ? n : -1;
+  }
+  return consumer_cluster_capacity<BN, SMALL>(reinterpret_cast<const void*>(fn), cfg, splits);
 }
 }  // namespace
 
 int ar_norm_gemm_resident_clusters(int bn, int splits) {
-  if (splits < 1 || splits > 16) return -1;
+  if (splits < 0 || splits > 16) return -1;
   switch (bn) {
     case 16: return consumer_clusters<16, true>(splits);
     case 32: return consumer_clusters<32, true>(splits);

@@ -30,6 +30,11 @@ struct FusedGemmParams {
   int kps;                   // 64-wide k-steps per split (splits = gridDim.y)
   unsigned long long timeout_ns;
   int l2_prefetch;           // weight tiles beyond the ring prefetched into L2 before the activations are awaited
+  // packed weights (nullptr: the row-major weight through its tensor map): per rank, ceil(N / 128)
+  // x (K / 64) blocks of 128 x 64 elements in the swizzled shared-memory image (see gemm.h), ranks
+  // stacked when emulating; w_tiles = ceil(N / 128)
+  const uint8_t* wp;
+  int w_tiles;
   int* err;                  // device word: nonzero after a timed-out wait in this kernel
   // ar_norm_gemm only
   void* residual;            // [M, K] in / out (each element read and written by one thread)

@@ -91,12 +91,12 @@ template <int BN, bool BF16, bool SMALL, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
                    int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
-                   int kps, int l2pf, long long* stamps) {
+                   int kps, int l2pf, long long* stamps, const uint8_t* __restrict__ Wp) {
   using C = Cfg<BN, SMALL>;
   // optional phase stamps (%globaltimer, ns): stamps[cta * kStampSlots + phase]
   const int lin = blockIdx.x + blockIdx.y * gridDim.x;
   auto stamp = [&](int phase) {
-    if (stamps != nullptr) stamps[(size_t)lin * kStampSlots + phase] = (long long)globaltimer();
+    if (stamps != nullptr) stamps[(size_t)lin * kStampSlots + phase] = (long long)globaltimer_ordered();
   };
   if (threadIdx.x == 0) stamp(kStEntry);
   extern __shared__ uint8_t smem_raw[];
@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int first_tile = (int)(beg / KT);
 
   if (threadIdx.x == 0) {
-    prefetch_tmap(&tmW);
+    if (Wp == nullptr) prefetch_tmap(&tmW);
     prefetch_tmap(&tmX);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -154,38 +154,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
+      // (tile, k-step) of flattened step g advanced incrementally: no 64-bit divisions in the loop.
+      // Packed weights (Wp != nullptr): tile t, k-step k is the contiguous 16 KB block t * KT + k, stored
+      // as the swizzled shared-memory image, so one bulk copy replaces the 2-D tensor load and each CTA
+      // reads its whole share of the weights as one contiguous range.
       const int nsteps = (int)(end - beg);
       const int pre = min(C::STAGES, nsteps);
+      const int k_beg = (int)(beg % KT), t_beg = (int)(beg / KT);
+      auto load_w = [&](int s, int k, int t, long long g) {
+        if (Wp != nullptr)
+          bulk_load(sA + s * C::A_BYTES, Wp + (size_t)g * C::A_BYTES, C::A_BYTES, &full[s]);
+        else
+          tma_load_2d(sA + s * C::A_BYTES, &tmW, &full[s], k * BK, t * BM);
+      };
       // weights first: they do not depend on the previous kernel
-      for (int i = 0; i < pre; ++i) {
-        const long long g = beg + i;
-        mbar_arrive_expect_tx(&full[i], C::STAGE);
-        tma_load_2d(sA + i * C::A_BYTES, &tmW, &full[i], (int)(g % KT) * BK, (int)(g / KT) * BM);
-      }
-      // the next l2pf weight tiles into L2 while the previous kernel finishes (later stages hit L2)
-      for (int i = pre; i < min(nsteps, pre + l2pf); ++i) {
-        const long long g = beg + i;
-        tma_prefetch_l2(&tmW, (int)(g % KT) * BK, (int)(g / KT) * BM);
+      {
+        int k = k_beg, t = t_beg;
+        for (int i = 0; i < pre; ++i) {
+          mbar_arrive_expect_tx(&full[i], C::STAGE);
+          load_w(i, k, t, beg + i);
+          if (++k == KT) k = 0, ++t;
+        }
+        // the next l2pf weight tiles into L2 while the previous kernel finishes (later stages hit L2)
+        for (int i = pre; i < min(nsteps, pre + l2pf); ++i) {
+          if (Wp != nullptr)
+            bulk_prefetch_l2(Wp + (size_t)(beg + i) * C::A_BYTES, C::A_BYTES);
+          else
+            tma_prefetch_l2(&tmW, k * BK, t * BM);
+          if (++k == KT) k = 0, ++t;
+        }
       }
       stamp(kStWeightsIssued);
       pdl_wait();
       stamp(kStPdlWait);
+      int k = k_beg, t = t_beg;
       for (int i = 0; i < pre; ++i) {
-        const long long g = beg + i;
-        tma_load_2d(sB + i * C::B_BYTES, &tmX, &full[i], (int)(g % KT) * BK, 0);
+        tma_load_2d(sB + i * C::B_BYTES, &tmX, &full[i], k * BK, 0);
+        if (++k == KT) k = 0, ++t;
       }
       int issued = pre;
-      for (int i = pre; i < nsteps; ++i) {
-        const int s = i % C::STAGES;
-        if (!mbar_wait(&empty[s], ((i / C::STAGES) & 1) ^ 1, timeout_ns) || *s_fail) {
+      for (int i = pre, s = pre % C::STAGES, ph = (pre / C::STAGES) & 1; i < nsteps; ++i) {
+        if (!mbar_wait(&empty[s], ph ^ 1, timeout_ns) || *s_fail) {
           *s_fail = 1;
           break;
         }
-        const long long g = beg + i;
         mbar_arrive_expect_tx(&full[s], C::STAGE);
-        tma_load_2d(sA + s * C::A_BYTES, &tmW, &full[s], (int)(g % KT) * BK, (int)(g / KT) * BM);
-        tma_load_2d(sB + s * C::B_BYTES, &tmX, &full[s], (int)(g % KT) * BK, 0);
+        load_w(s, k, t, beg + i);
+        tma_load_2d(sB + s * C::B_BYTES, &tmX, &full[s], k * BK, 0);
         issued = i + 1;
+        if (++k == KT) k = 0, ++t;
+        if (++s == C::STAGES) s = 0, ph ^= 1;
       }
       *s_issued = issued;
       stamp(kStLastLoad);
@@ -379,13 +397,15 @@ cudaError_t tensor_map(const void* ptr, int rows, int cols, int box_rows, bool b
 template <int BN, bool BF16, bool SMALL>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int M, int N, int K, int ctas, int ldy,
                       float* ws, int* ctr, int* err, unsigned long long timeout_ns, bool pdl, int splits,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const uint8_t* Wp) {
   using C = Cfg<BN, SMALL>;
   const bool clustered = splits > 0;
   auto fn = clustered ? k_gemm_streamk<BN, BF16, SMALL, true> : k_gemm_streamk<BN, BF16, SMALL, false>;
   static bool attr_set[2] = {false, false};
   if (!attr_set[clustered]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     attr_set[clustered] = true;
   }
@@ -413,19 +433,19 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   cfg.attrs = attrs;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps, l2_prefetch_tiles(),
-                            gemm_stamps());
+                            gemm_stamps(), Wp);
 }
 
 template <bool BF16, bool SMALL>
 cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K,
                           int ctas, int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl,
-                          int splits, cudaStream_t s) {
+                          int splits, cudaStream_t s, const uint8_t* Wp) {
   switch (bn) {
-    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
-    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
-    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
-    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
-    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
+    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
+    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
+    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
+    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
+    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -433,9 +453,9 @@ cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, 
 template <bool BF16>
 cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K, int ctas,
                          int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl, bool small,
-                         int splits, cudaStream_t s) {
-  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s)
-               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s);
+                         int splits, cudaStream_t s, const uint8_t* Wp) {
+  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp)
+               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
 }
 
 }  // namespace
@@ -468,23 +488,26 @@ size_t gemm_workspace_bytes(int num_ctas, int bn) { return (size_t)num_ctas * 2 
 cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
                         size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
                         bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
-                        cudaStream_t stream, GemmPlan* used) {
+                        cudaStream_t stream, GemmPlan* used, bool packed) {
   if (cluster_splits > 8 || (cluster_splits > 0 && M > 64)) return cudaErrorInvalidValue;
   if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % 8 || (dtype != kBF16 && dtype != kF16))
     return cudaErrorInvalidValue;
+  // packed weights: whole 128 x 64 blocks, 16-byte aligned
+  if (packed && (K % BK || (reinterpret_cast<uintptr_t>(W) & 15))) return cudaErrorInvalidValue;
   const GemmPlan p = plan_gemm(M, N, K, num_sms, ctas_override);
   if (used) *used = p;
   if (p.tiles > max_tiles || gemm_workspace_bytes(p.ctas, p.bn) > ws_bytes) return cudaErrorInvalidValue;
   const bool bf16 = dtype == kBF16;
-  CUtensorMap mw, mx;
-  cudaError_t e = tensor_map(W, N, K, BM, bf16, &mw);
+  CUtensorMap mw = {}, mx;
+  cudaError_t e = packed ? cudaSuccess : tensor_map(W, N, K, BM, bf16, &mw);
   if (e != cudaSuccess) return e;
   e = tensor_map(X, M, K, p.bn, bf16, &mx);
   if (e != cudaSuccess) return e;
+  const uint8_t* Wp = packed ? static_cast<const uint8_t*>(W) : nullptr;
   return bf16 ? launch_typed<true>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
-                                   small_smem, cluster_splits, stream)
+                                   small_smem, cluster_splits, stream, Wp)
               : launch_typed<false>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
-                                    small_smem, cluster_splits, stream);
+                                    small_smem, cluster_splits, stream, Wp);
 }
 
 }  // namespace cob

@@ -183,13 +183,21 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
 // (zero-initialised, left zero). Returns {bn, tiles, ctas}.
 std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor ws, torch::Tensor ctr,
                              torch::Tensor err, int64_t ctas, bool pdl, bool small_smem, int64_t cluster_splits,
-                             int64_t timeout_ns) {
+                             int64_t timeout_ns, int64_t packed_n) {
   dense(x, "x");
   dense(w, "w");
   dense(err, "err");
   COB_CHECK(y.is_cuda() && y.stride(-1) == 1, "y must be row-major");
-  COB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
-  COB_CHECK(y.size(0) == x.size(0) && y.size(1) == w.size(0), "y must be [M, N]");
+  // packed_n > 0: w is the packed layout [tiles, K / 64, 128, 64] of an [packed_n, K] weight
+  const bool packed = packed_n > 0;
+  const int64_t N = packed ? packed_n : w.size(0);
+  if (packed)
+    COB_CHECK(w.dim() == 4 && w.size(2) == 128 && w.size(3) == 64 && w.size(0) == (N + 127) / 128 &&
+                  x.dim() == 2 && x.size(1) == w.size(1) * 64,
+              "packed w must be [ceil(N / 128), K / 64, 128, 64] for x [M, K]");
+  else
+    COB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
+  COB_CHECK(y.size(0) == x.size(0) && y.size(1) == N, "y must be [M, N]");
   COB_CHECK(x.scalar_type() == w.scalar_type() && y.scalar_type() == x.scalar_type(), "dtypes must match");
   COB_CHECK(err.scalar_type() == torch::kInt32 && ctr.scalar_type() == torch::kInt32, "err, ctr must be int32");
   COB_CHECK(ws.scalar_type() == torch::kFloat && ws.is_cuda() && ctr.is_cuda(), "ws must be float32 CUDA");
@@ -197,10 +205,10 @@ std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, 
   static int sms = 0;
   if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, x.device().index());
   cob::GemmPlan p;
-  ok(cob::gemm_decode(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)w.size(0), (int)x.size(1),
+  ok(cob::gemm_decode(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)N, (int)x.size(1),
                       (int)y.stride(0), code_of(x), ws.data_ptr<float>(), (size_t)ws.numel() * 4,
                       ctr.data_ptr<int32_t>(), (int)ctr.numel(), err.data_ptr<int32_t>(), sms, (int)ctas, pdl,
-                      small_smem, (int)cluster_splits, (unsigned long long)timeout_ns, cur(), &p),
+                      small_smem, (int)cluster_splits, (unsigned long long)timeout_ns, cur(), &p, packed),
      "gemm_decode");
   return {p.bn, p.tiles, p.ctas};
 }

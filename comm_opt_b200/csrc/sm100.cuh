@@ -64,6 +64,19 @@ __device__ __forceinline__ void tma_prefetch_l2(const CUtensorMap* map, int x, i
                "r"(x), "r"(y)
                : "memory");
 }
+// Contiguous bulk copy global -> this CTA's shared memory, completing on `bar` (complete_tx). Both
+// addresses 16-byte aligned, `bytes` a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+// Contiguous range into L2 only (no shared memory, no barrier).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

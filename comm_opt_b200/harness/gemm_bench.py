@@ -15,7 +15,7 @@ from pathlib import Path
 
 import torch
 
-from ..models.gemm import gemm
+from ..models.gemm import gemm, pack_weight
 from ..models.llama import PRESETS
 
 L2_BYTES = 126 << 20
@@ -72,6 +72,17 @@ VARIANTS = {  # name -> gemm() keyword arguments
 }
 
 
+def variant_kwargs(v: str, N: int) -> tuple[dict, bool]:
+    """gemm() keyword arguments of a variant name, and whether it runs on packed weights ("pk_" prefix:
+    the same schedule on PackedWeight blocks)."""
+    packed = v.startswith("pk_") or v == "pk"
+    base = v[3:] if v.startswith("pk_") else ("default" if v == "pk" else v)
+    kw = dict(VARIANTS[base])
+    if kw.get("ctas") == -1:
+        kw["ctas"] = (N + 127) // 128
+    return kw, packed
+
+
 def sweep(shape_sets: list[str], batches: list[int], variants: list[str], iters: int = 50, dev=None,
           ops: list[str] | None = None) -> list[dict]:
     """Time several launch variants of our kernel per shape (graph-captured, weights > L2)."""
@@ -91,10 +102,10 @@ def sweep(shape_sets: list[str], batches: list[int], variants: list[str], iters:
                 nbytes = wbytes + (M * K + M * N) * 2
                 row = dict(set=sset, op=name, M=M, N=N, K=K)
                 for v in variants:
-                    kw = dict(VARIANTS[v])
-                    if kw.get("ctas") == -1:
-                        kw["ctas"] = (N + 127) // 128
-                    t = time_fn(lambda i: gemm(x, ws[i % copies], y, **kw), iters)
+                    kw, packed = variant_kwargs(v, N)
+                    wv = [pack_weight(w) for w in ws] if packed else ws
+                    t = time_fn(lambda i: gemm(x, wv[i % copies], y, **kw), iters)
+                    del wv
                     row[v] = round(t, 2)
                     row[v + "_frac"] = round(nbytes / t / 1e3 / peak, 3)
                 row["cublas"] = round(time_fn(lambda i: torch.matmul(x, ws[i % copies].t(), out=y), iters), 2)

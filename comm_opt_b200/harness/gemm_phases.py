@@ -20,8 +20,8 @@ import statistics
 import torch
 
 from .._ext import native
-from ..models.gemm import gemm
-from .gemm_bench import L2_BYTES, VARIANTS, shapes_for, time_fn
+from ..models.gemm import gemm, pack_weight
+from .gemm_bench import L2_BYTES, shapes_for, time_fn, variant_kwargs
 
 PHASES = ("entry", "setup", "weights_issued", "pdl_wait", "last_load", "first_full", "last_mma", "acc_ready",
           "epi_done", "end")
@@ -42,10 +42,12 @@ def timeline(stamps: torch.Tensor, ctas: int) -> dict:
 
 
 def measure(op, N, K, M, variant, runs, dev):
-    kw = dict(VARIANTS[variant])
-    if kw.get("ctas") == -1:
-        kw["ctas"] = (N + 127) // 128
+    kw, packed = variant_kwargs(variant, N)
     w = torch.empty(N, K, dtype=torch.bfloat16, device=dev).normal_(0, 0.02)
+    ref = None
+    if packed:
+        w0 = w
+        w = pack_weight(w0)
     x = torch.randn(M, K, device=dev).to(torch.bfloat16)
     y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
@@ -69,8 +71,13 @@ def measure(op, N, K, M, variant, runs, dev):
     per_cta_bytes = N * K * 2 / ctas
     stream_ns = (st[:, 6] - st[:, 5]).double().clamp_min(1)
     rate = sorted((per_cta_bytes / stream_ns).tolist())  # bytes/ns = GB/s
+    if packed:  # the packed launch computes the same product as the row-major weight
+        ref = x.float() @ w0.float().t()
+        err = float((gemm(x, w, y, **kw).float() - ref).abs().max() / ref.abs().max())
+        assert err < 2 ** -6, f"packed weights: relative error {err}"
     copies = max(2, (2 * L2_BYTES) // (N * K * 2) + 1)
-    wc = [w] + [torch.empty_like(w).normal_(0, 0.02) for _ in range(copies - 1)]
+    wc = [w] + [(pack_weight if packed else (lambda t: t))(torch.empty(N, K, dtype=torch.bfloat16, device=dev)
+                                                          .normal_(0, 0.02)) for _ in range(copies - 1)]
     ev_us = time_fn(lambda i: gemm(x, wc[i % copies], y, **kw), 20)
     return dict(op=op, M=M, N=N, K=K, variant=variant, ctas=ctas, span_ns=tl["end"][2], event_us=round(ev_us, 2),
                 phases_ns=tl, stream_gbs_per_cta=dict(min=round(rate[0], 1), med=round(rate[len(rate) // 2], 1),

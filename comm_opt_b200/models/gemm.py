@@ -11,6 +11,72 @@ from .._ext import native
 
 _STATE: dict[int, dict] = {}
 MAX_TILES = 1 << 14
+BM, BK = 128, 64
+
+
+def _swizzle_index(device) -> torch.Tensor:
+    """idx[r, c, e] = c ^ (r % 8): the 16-byte chunk of row r stored at chunk position c (128-byte swizzle)."""
+    r = torch.arange(BM, device=device).view(BM, 1, 1)
+    c = torch.arange(8, device=device).view(1, 8, 1)
+    return (c ^ (r & 7)).expand(BM, 8, 8)
+
+
+class PackedWeight:
+    """A weight [N, K] stored for the decode GEMMs' bulk loads: 128 x 64 blocks (16 KB for 16-bit types)
+    in (output tile, k-step) order, each block laid out exactly as the 128-byte-swizzled shared-memory
+    image the tensor cores read (16-byte chunk c of row r at chunk position c ^ (r % 8)); rows past N are
+    zero. A CTA's share of the weight stream is then one contiguous range of memory, read by 16 KB bulk
+    copies (no tensor-map descriptor, no per-row 128-byte pieces). Static weights are packed once at
+    load. `ranks` > 1 stacks the weights of emulated ranks ([ranks, N, K] -> ranks x the blocks)."""
+
+    def __init__(self, data: torch.Tensor, n: int, k: int, ranks: int = 1):
+        T = (n + BM - 1) // BM
+        assert data.dim() == 4 and tuple(data.shape[1:]) == (k // BK, BM, BK) and data.shape[0] == ranks * T
+        self.data, self.n, self.k, self.ranks = data, n, k, ranks
+
+    @property
+    def shape(self) -> tuple:
+        return (self.n, self.k) if self.ranks == 1 else (self.ranks, self.n, self.k)
+
+    @property
+    def dtype(self):
+        return self.data.dtype
+
+    @property
+    def device(self):
+        return self.data.device
+
+    def dense(self) -> torch.Tensor:
+        """The row-major weight ([N, K], or [ranks, N, K]) as a new tensor."""
+        RT, KT = self.data.shape[:2]
+        T = RT // self.ranks
+        v = self.data.view(RT, KT, BM, 8, 8)
+        idx = _swizzle_index(self.device).expand(RT, KT, BM, 8, 8)
+        blocks = v.gather(3, idx)  # the same permutation undoes itself (XOR)
+        w = blocks.view(self.ranks, T, KT, BM, 8, 8).permute(0, 1, 3, 2, 4, 5).reshape(self.ranks, T * BM, KT * BK)
+        w = w[:, : self.n].contiguous()
+        return w[0] if self.ranks == 1 else w
+
+
+def pack_weight(w: torch.Tensor) -> PackedWeight:
+    """Pack a row-major weight [N, K] (or [ranks, N, K]), K a multiple of 64, into the decode GEMMs'
+    block layout."""
+    ranks = 1 if w.dim() == 2 else w.shape[0]
+    w3 = w.reshape(ranks, w.shape[-2], w.shape[-1])
+    _, N, K = w3.shape
+    if K % BK:
+        raise ValueError(f"K = {K} is not a multiple of {BK}")
+    T, KT = (N + BM - 1) // BM, K // BK
+    if T * BM != N:
+        w3 = torch.cat([w3, w3.new_zeros(ranks, T * BM - N, K)], 1)
+    v = w3.reshape(ranks * T, BM, KT, 8, 8).permute(0, 2, 1, 3, 4)
+    idx = _swizzle_index(w.device).expand(ranks * T, KT, BM, 8, 8)
+    return PackedWeight(v.gather(3, idx).view(ranks * T, KT, BM, BK), N, K, ranks)
+
+
+def dense(w) -> torch.Tensor:
+    """Row-major [N, K] form of a weight (unpacks a PackedWeight)."""
+    return w.dense() if isinstance(w, PackedWeight) else w
 
 
 def _state(device) -> dict:
@@ -39,14 +105,17 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ctas
 
     Schedules: persistent stream-K (default) or, with ``cluster_splits`` = s > 0 (M <= 64), one CTA per
     (tile, K split) with the s CTAs of a tile in a cluster reducing through distributed shared memory.
-    ``small_smem`` halves the TMA ring so the next kernel can share the SM (programmatic launch)."""
+    ``small_smem`` halves the TMA ring so the next kernel can share the SM (programmatic launch).
+    ``w`` is a row-major [N, K] tensor or a PackedWeight (bulk loads of contiguous weight blocks)."""
     M, N = x.shape[0], w.shape[0]
     out = torch.empty(M, N, dtype=x.dtype, device=x.device) if out is None else out
     st = _state(x.device)
+    packed = isinstance(w, PackedWeight)
+    wt, pn = (w.data, w.n) if packed else (w, 0)
     for m0 in range(0, M, 256):
         m1 = min(M, m0 + 256)
-        native().gemm(x[m0:m1], w, out[m0:m1], st["ws"], st["ctr"], st["err"], ctas, pdl, small_smem,
-                      cluster_splits if m1 - m0 <= 64 else 0, int(timeout_ms * 1e6))
+        native().gemm(x[m0:m1], wt, out[m0:m1], st["ws"], st["ctr"], st["err"], ctas, pdl, small_smem,
+                      cluster_splits if m1 - m0 <= 64 else 0, int(timeout_ms * 1e6), pn)
     return out
 
 
@@ -68,7 +137,7 @@ def tune(w: torch.Tensor, M: int, iters: int = 15) -> dict:
     """Measure every candidate schedule for (M, N, K) with CUDA events around single launches (L2
     flushed before each, as in decode where other layers evict the weights); cache the fastest."""
     N, K = w.shape
-    key = (M, N, K, w.dtype, w.device.index)
+    key = (M, N, K, w.dtype, w.device.index, isinstance(w, PackedWeight))
     if key in _TUNED:
         return _TUNED[key]
     dev = w.device

@@ -26,7 +26,7 @@ import torch.nn.functional as F
 from ..ops import kernels as K
 from ..ops.reference import rope_tables
 from ..parallel.communicator import TPCommunicator
-from .gemm import Linear
+from .gemm import Linear, dense, pack_weight
 
 
 @dataclass(frozen=True)
@@ -223,7 +223,7 @@ class TPDecodeRunner:
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
                  device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
                  fuse_epilogues: bool = False, collective: str = "ours", tune_boundaries: bool = True,
-                 car_group=None, l2_prefetch: int = 0):
+                 car_group=None, l2_prefetch: int = 0, pack_weights: bool = True):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -234,6 +234,13 @@ class TPDecodeRunner:
         self.cos, self.sin = rope_tables(max_seq, cfg.head_dim, cfg.rope_theta, self.device)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.gemm = gemm
+        # packed weights (this package's GEMMs only): every projection matrix is converted in place, once,
+        # into the bulk-load block layout (models.gemm.PackedWeight); the prefill unpacks one matrix at a time
+        self.packed = bool(pack_weights and gemm == "cob")
+        if self.packed:
+            for L in weights.layers:
+                L.wqkv, L.wo, L.wgu, L.wdown = (pack_weight(dense(t)) for t in (L.wqkv, L.wo, L.wgu, L.wdown))
+            weights.lm_head = pack_weight(dense(weights.lm_head))
         self.lin = {}
         for i, L in enumerate(weights.layers):
             self.lin[(i, "qkv")] = Linear(L.wqkv, gemm)
@@ -307,7 +314,7 @@ class TPDecodeRunner:
         res = x
         for i, L in enumerate(self.w.layers):
             h = F.rms_norm(res.float(), (cfg.hidden,), L.ln1.float(), cfg.eps).to(self.dtype)
-            qkv = h @ L.wqkv.t()
+            qkv = h @ dense(L.wqkv).t()
             if L.bqkv is not None:
                 qkv = qkv + L.bqkv
             q, k, v = qkv.split([s["nq"] * D, s["nkv"] * D, s["nkv"] * D], -1)
@@ -322,14 +329,14 @@ class TPDecodeRunner:
             self.cache.v[i][bt[:, :nb]] = vp
             a = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
                                                is_causal=True, enable_gqa=True, scale=self.scale)
-            o = self._ar(a.transpose(1, 2).reshape(B, P, -1) @ L.wo.t())
+            o = self._ar(a.transpose(1, 2).reshape(B, P, -1) @ dense(L.wo).t())
             res = res + o
             h = F.rms_norm(res.float(), (cfg.hidden,), L.ln2.float(), cfg.eps).to(self.dtype)
-            g, u = (h @ L.wgu.t()).chunk(2, -1)
-            d = self._ar((F.silu(g.float()) * u.float()).to(self.dtype) @ L.wdown.t())
+            g, u = (h @ dense(L.wgu).t()).chunk(2, -1)
+            d = self._ar((F.silu(g.float()) * u.float()).to(self.dtype) @ dense(L.wdown).t())
             res = res + d
         h = F.rms_norm(res[:, -1].float(), (cfg.hidden,), self.w.final_norm.float(), cfg.eps).to(self.dtype)
-        logits = (h @ self.w.lm_head.t()).float()
+        logits = (h @ dense(self.w.lm_head).t()).float()
         val, idx = logits.max(-1)
         idx = idx + self.rank * self.s["vocab"]
         if self.tp > 1:
@@ -429,7 +436,8 @@ class TPDecodeRunner:
             # the QKV epilogue has no bias term: a QKV bias keeps RoPE + append in its own kernel
             rp = comm.last_fused_gemm[1][2] > 0 and cfg.head_dim == 128 and not cfg.qkv_bias
             if sw and self._wgu_il is None:  # tile-interleaved gate/up copies (allocated outside capture)
-                self._wgu_il = [comm.interleave_gate_up(Lw.wgu) for Lw in self.w.layers]
+                il = [comm.interleave_gate_up(dense(Lw.wgu)) for Lw in self.w.layers]
+                self._wgu_il = [pack_weight(t) for t in il] if self.packed else il
             self._fuse_epi[B] = (sw, rp)
         return self._fuse_epi[B]
 

@@ -74,6 +74,15 @@ def default_timeout_ms() -> float:
     return float(os.environ.get("COB_WAIT_TIMEOUT_MS", "1000"))
 
 
+def _weight_operand(w):
+    """(tensor handed to the kernel, output features N, packed?) of a row-major or packed weight."""
+    from ..models.gemm import PackedWeight
+
+    if isinstance(w, PackedWeight):
+        return w.data, w.n, True
+    return w, w.shape[-2], False
+
+
 class TPCommunicator:
     def __init__(self, group=None, *, emulate_world: int | None = None, device=None, dtype=torch.bfloat16,
                  max_rows: int = 512, max_hidden: int = 8192, max_gather: int = 4096,
@@ -298,20 +307,21 @@ class TPCommunicator:
             return t[0].numel() // t.shape[-1], t.shape[-1]
         return t.numel() // t.shape[-1], t.shape[-1]
 
-    def gemm_push(self, x: torch.Tensor, w: torch.Tensor, splits: int = 0, dry_run: bool = False):
+    def gemm_push(self, x: torch.Tensor, w, splits: int = 0, dry_run: bool = False):
         """Row-parallel GEMM whose epilogue is the first half of the all-reduce: x [M, K] @ w[N, K]^T is
         pushed (bf16) into every rank's landing buffers; `ar_norm_gemm` (or nothing else) must follow.
-        Emulation: x [W, M, K], w [W, N, K]."""
+        Emulation: x [W, M, K], w [W, N, K]. `w` may be a PackedWeight (models.gemm.pack_weight)."""
         if self.world == 1 or self.dtype != torch.bfloat16:
             raise TPCommError("fused GEMMs need world > 1 and a bf16 communicator")
         M, K = self._fg_dims(x)
-        N = w.shape[-2]
+        wt, N, packed = _weight_operand(w)
         if M > self.max_rows or N > self.max_hidden:
             raise TPCommError(f"gemm_push [{M}, {N}] exceeds the communicator capacity")
         with torch.cuda.device(self.device):
-            plan = native().fused_gemm(0, self.heap.bases, self._layout_list, w, x=x, err=self._fg_err(),
+            plan = native().fused_gemm(0, self.heap.bases, self._layout_list, wt, x=x, err=self._fg_err(),
                                        rank=self.rank, M=M, N=N, K=K, eps=0.0, emulate=int(self.emulated), splits=splits,
-                                       pdl=int(self.pdl), timeout_ns=self.timeout_ns, res_rs=0, dry_run=dry_run)
+                                       pdl=int(self.pdl), timeout_ns=self.timeout_ns, res_rs=0, dry_run=dry_run,
+                                       packed=packed)
         self.last_fused_gemm = ("gemm_push", tuple(plan))
         return plan
 
@@ -334,7 +344,7 @@ class TPCommunicator:
         u = w[..., I:, :].reshape(*lead, I // 64, 64, K)
         return torch.stack([g, u], dim=-3).reshape(*lead, I2, K).contiguous()
 
-    def ar_norm_gemm(self, residual: torch.Tensor, gamma: torch.Tensor, w: torch.Tensor, eps: float = 1e-6,
+    def ar_norm_gemm(self, residual: torch.Tensor, gamma: torch.Tensor, w, eps: float = 1e-6,
                      out: torch.Tensor | None = None, splits: int = 0, dry_run: bool = False,
                      epilogue: str = "plain", rope: dict | None = None) -> torch.Tensor:
         """Second half of the all-reduce fused with RMSNorm and the next column-parallel GEMM:
@@ -342,11 +352,12 @@ class TPCommunicator:
         epilogue "plain": out = z [M, N]. "swiglu": w tile-interleaved (`interleave_gate_up`), out = silu(gate)
         * up [M, N / 2]. "rope_kv": z holds [q heads | k heads | v heads] of 128; out = RoPE(q) [M, nq, 128],
         RoPE(k) and v written into the paged caches at rope["positions"] (keys: positions, cos, sin,
-        block_tables, k_cache, v_cache, nq, nkv). Emulation: residual [W, M, K], w [W, N, K]."""
+        block_tables, k_cache, v_cache, nq, nkv). Emulation: residual [W, M, K], w [W, N, K]. `w` may be a
+        PackedWeight (models.gemm.pack_weight)."""
         if self.world == 1 or self.dtype != torch.bfloat16:
             raise TPCommError("fused GEMMs need world > 1 and a bf16 communicator")
         M, K = self._fg_dims(residual)
-        N = w.shape[-2]
+        wt, N, packed = _weight_operand(w)
         epi = self.EPILOGUES[epilogue]
         if M > self.max_rows or K > self.max_hidden:
             raise TPCommError(f"ar_norm_gemm [{M}, {K}] exceeds the communicator capacity")
@@ -357,7 +368,7 @@ class TPCommunicator:
         ws = self._fg_workspace(K)
         r = rope or {}
         with torch.cuda.device(self.device):
-            plan = native().fused_gemm(1, self.heap.bases, self._layout_list, w, residual=residual, gamma=gamma,
+            plan = native().fused_gemm(1, self.heap.bases, self._layout_list, wt, residual=residual, gamma=gamma,
                                        y=out if out is not None else residual, act=ws["act"], flags=ws["flags"],
                                        pss=ws["pss"], err=self._fg_err(), rank=self.rank, M=M, N=N, K=K,
                                        eps=float(eps), emulate=int(self.emulated), splits=splits,
@@ -365,7 +376,8 @@ class TPCommunicator:
                                        res_rs=M * K if self.emulated else 0, dry_run=dry_run, epi=epi,
                                        positions=r.get("positions"), cos=r.get("cos"), sin=r.get("sin"),
                                        block_tables=r.get("block_tables"), k_cache=r.get("k_cache"),
-                                       v_cache=r.get("v_cache"), nq=r.get("nq", 0), nkv=r.get("nkv", 0))
+                                       v_cache=r.get("v_cache"), nq=r.get("nq", 0), nkv=r.get("nkv", 0),
+                                       packed=packed)
         self.last_fused_gemm = ("ar_norm_gemm", tuple(plan))
         return out
 

@@ -220,3 +220,33 @@ def test_layer_boundary_rope_kv_epilogue(cuda, world):
             blk, off = int(bt[b, int(pos[b]) // bs]), int(pos[b]) % bs
             assert rel_err(kc[r, blk, :, off], kref[b]) <= TOL, (r, b)
             assert rel_err(vc[r, blk, :, off], vref[b]) <= TOL, (r, b)
+
+
+@pytest.mark.parametrize("world,M,K1,H,N2,splits2", [(2, 8, 3584, 8192, 1280, 0), (4, 5, 512, 1024, 24576, 0),
+                                                    (2, 8, 512, 2048, 640, 16), (2, 3, 256, 1024, 296, 0)])
+def test_layer_boundary_packed_weights(cuda, world, M, K1, H, N2, splits2):
+    """Both fused GEMMs on packed (bulk-load) weights give the bits of the row-major launches: 70B TP=8
+    shapes, many tiles per CTA, a 16-CTA cluster, and an output width that is not a multiple of 128."""
+    from comm_opt_b200.models.gemm import pack_weight
+
+    eps = 1e-5
+    g = torch.Generator(device=cuda).manual_seed(M + N2)
+    w1 = (0.02 * torch.randn(world, H, K1, generator=g, device=cuda)).bfloat16()
+    w2 = (0.02 * torch.randn(world, N2, H, generator=g, device=cuda)).bfloat16()
+    gamma = (1 + 0.1 * torch.randn(H, generator=g, device=cuda)).bfloat16()
+    res0 = torch.randn(M, H, generator=g, device=cuda).bfloat16()
+    x = torch.randn(world, M, K1, generator=g, device=cuda).bfloat16()
+    outs = []
+    for packed in (False, True):
+        comm = TPCommunicator(emulate_world=world, device=cuda, dtype=torch.bfloat16, max_rows=16, max_hidden=H)
+        res = res0.unsqueeze(0).repeat(world, 1, 1).contiguous()
+        a, b = (pack_weight(w1), pack_weight(w2)) if packed else (w1, w2)
+        out = layer_boundary(comm, x, a, res, gamma, b, eps, splits2=splits2)
+        torch.cuda.synchronize()
+        comm.check()
+        outs.append((res, out))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    h_ref, out_ref = reference(x, w1, res0, gamma, w2, eps)
+    for r in range(world):
+        assert rel_err(outs[1][0][r], h_ref) <= TOL
+        assert rel_err(outs[1][1][r], out_ref[r]) <= TOL

@@ -98,3 +98,27 @@ def test_gemm_l2_prefetch_same_bits(cuda, tiles):
     torch.cuda.synchronize()
     assert int(gemm_error_word(cuda)) == 0
     assert all(torch.equal(a, b) for a, b in zip(base, got))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 128, 64), (8, 1280, 8192), (3, 300, 192), (16, 8192, 1024),
+                                   (64, 1024, 3584), (128, 16032, 512), (200, 512, 4096)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sched", [dict(), dict(small_smem=True, pdl=True), dict(cluster_splits=4),
+                                   dict(ctas=5)])
+def test_packed_weights_match_row_major(cuda, M, N, K, dtype, sched):
+    """The packed (bulk-load) weight layout gives the bits of the row-major launch of the same schedule."""
+    from comm_opt_b200.models.gemm import pack_weight
+
+    if sched.get("cluster_splits") and M > 64:
+        pytest.skip("cluster split-K is for M <= 64")
+    g = torch.Generator(device=cuda).manual_seed(M * 5 + N + K)
+    x = torch.randn(M, K, device=cuda, generator=g).to(dtype)
+    w = (0.05 * torch.randn(N, K, device=cuda, generator=g)).to(dtype)
+    pw = pack_weight(w)
+    assert torch.equal(pw.dense(), w)
+    y_rm = gemm(x, w, **sched)
+    y_pk = gemm(x, pw, **sched)
+    torch.cuda.synchronize()
+    assert int(gemm_error_word(cuda)) == 0
+    assert torch.equal(y_rm, y_pk)
+    assert rel_err(y_pk, x.float() @ w.float().t()) <= 2 ** -7

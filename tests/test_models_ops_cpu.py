@@ -2,6 +2,7 @@
 import json
 from dataclasses import replace
 
+import pytest
 import torch
 
 from comm_opt_b200.harness.analyze_sweep import calibrate, table
@@ -323,3 +324,26 @@ def test_decode_step_composition_vllm_stack(monkeypatch):
     # the GEMM after a boundary reads the all-reduce's output, not buf["h"]
     gu = [x for k, x in gemm_inputs if k == (1, "gu")][0]
     assert gu is not buf["h"] and [x for k, x in gemm_inputs if k == "head"][0] is seen["out"]
+
+
+def test_pack_weight_layout_and_round_trip():
+    """Packed decode-GEMM weights: 128 x 64 blocks in (tile, k-step) order, 16-byte chunk c of row r at
+    chunk position c ^ (r % 8), rows past N zero; dense() restores the row-major weight."""
+    from comm_opt_b200.models.gemm import pack_weight
+
+    for N, K in [(128, 64), (300, 192), (1280, 1024)]:
+        w = torch.randn(N, K).bfloat16()
+        p = pack_weight(w)
+        assert p.shape == (N, K) and p.data.shape == ((N + 127) // 128, K // 64, 128, 64)
+        assert torch.equal(p.dense(), w)
+        blocks = p.data.view(p.data.shape[0], K // 64, 128, 8, 8)
+        for t in range(blocks.shape[0]):
+            for ks in range(K // 64):
+                for r in (0, 5, 77, 127):
+                    for c in range(8):
+                        n = t * 128 + r
+                        got = blocks[t, ks, r, c ^ (r & 7)]
+                        want = w[n, ks * 64 + c * 8: ks * 64 + c * 8 + 8] if n < N else torch.zeros(8).bfloat16()
+                        assert torch.equal(got, want)
+    with pytest.raises(ValueError):
+        pack_weight(torch.zeros(128, 100))
