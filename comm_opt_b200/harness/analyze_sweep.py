@@ -103,15 +103,17 @@ def link_table(rows: list[dict]) -> str:
     return "\n".join(out)
 
 
-LINK_GBS = 770.0  # measured peer-copy bandwidth per direction per GPU on this pool's B200s (NVLink 5)
-
-
-def roofline_table(rows: list[dict], link_gbs: float = LINK_GBS) -> tuple[str, list[dict]]:
+def roofline_table(rows: list[dict], link_gbs: float | None = None) -> tuple[str, list[dict]]:
     """Achieved fraction of the NVLink roofline per size: the fused op has no FLOPs worth counting, so
     its target time is the bytes an all-reduce must move per GPU and direction without in-switch
     reduction, 2 (W - 1) / W S (a one-shot moves (W - 1) S; NVSwitch multicast needs only about S),
     at `link_gbs`. fraction = target / measured p50 of the fastest of our variants (and of the best
-    baseline); small messages are latency-bound, which the fraction shows."""
+    baseline); small messages are latency-bound, which the fraction shows. `link_gbs` defaults to the
+    measured per-direction peer copy of the newest committed platform record (utils.peaks.link_gbs)."""
+    if link_gbs is None:
+        from ..utils.peaks import link_gbs as measured_link_gbs
+
+        link_gbs = measured_link_gbs()
     out = ["| world | tokens | KB | target us | best ours | us | fraction | best baseline | us | fraction |",
            "|---|---|---|---|---|---|---|---|---|---|"]
     summary = []
@@ -129,8 +131,9 @@ def roofline_table(rows: list[dict], link_gbs: float = LINK_GBS) -> tuple[str, l
             out.append(f"| {world} | {T} | {msg >> 10} | {target:.2f} | " +
                        (f"{ours['impl']} | {ours['p50_us']:.2f} | {fo:.3f} | " if ours else "- | - | - | ") +
                        (f"{base['impl']} | {base['p50_us']:.2f} | {fb:.3f} |" if base else "- | - | - |"))
-            summary.append(dict(world=world, tokens=T, target_us=target, ours=ours and ours["impl"],
-                                fraction=fo, baseline=base and base["impl"], baseline_fraction=fb))
+            summary.append(dict(world=world, tokens=T, bytes=msg, link_gbs=link_gbs, target_us=target,
+                                ours=ours and ours["impl"], fraction=fo, baseline=base and base["impl"],
+                                baseline_fraction=fb))
     return "\n".join(out), summary
 
 

@@ -9,7 +9,8 @@ Implementations (each one call = the whole boundary, captured K times in a CUDA 
   vllm_cublas  cuBLAS GEMM -> vLLM custom all-reduce -> fused_add_rms_norm -> cuBLAS GEMM
 Timing as in the fused-op sweep: graph of K calls, R replays, per replay the MAX over ranks, p50 / p99.
 Roofline per call: the slower of the weight bytes at the measured HBM copy bandwidth and the bytes
-each rank must push over NVLink ((W - 1) x B x 8192 x 2) at the measured peer bandwidth (770 GB/s);
+each rank must push over NVLink ((W - 1) x B x 8192 x 2) at the measured peer bandwidth (the newest
+committed results/platform record, utils.peaks.link_gbs);
 reported as roofline_us / p50_us. Correctness of every implementation against an fp32 oracle
 (max|out - ref| / max|ref| <= 2^-5).
 
@@ -28,21 +29,14 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
-from ..models.gemm import Linear
+from ..models.gemm import Linear, pack_weight
 from ..ops.reference import TOL, rel_err
 from ..parallel import TPCommunicator
 from ..utils.results import RunDir, gpu_state
 from ..utils.stats import summary
 
 ROOT = Path(__file__).resolve().parents[2]
-PEER_GBS = 770.0
-
-
-def hbm_gbs() -> float:
-    try:
-        return float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["hbm_gbs"])
-    except (OSError, KeyError, ValueError):
-        return 6650.0
+from ..utils.peaks import NoRecord, hbm_gbs, link_gbs
 
 
 def main():
@@ -56,6 +50,8 @@ def main():
     ap.add_argument("--replays", type=int, default=30)
     ap.add_argument("--eps", type=float, default=1e-5)
     ap.add_argument("--out-dir", default=None)
+    ap.add_argument("--packed", type=int, choices=[0, 1], default=1,
+                    help="our GEMMs (fused and ours_split) read packed weights (models.gemm.pack_weight)")
     a = ap.parse_args()
     local = int(os.environ["LOCAL_RANK"])
     dev = torch.device("cuda", local)
@@ -73,7 +69,9 @@ def main():
     w2 = (0.02 * torch.randn(N2, H, generator=g, device=dev)).bfloat16()
     gs = torch.Generator(device=dev).manual_seed(7)  # replicated
     gamma = (1 + 0.1 * torch.randn(H, generator=gs, device=dev)).bfloat16()
-    lin1, lin2 = Linear(w1, "cob"), Linear(w2, "cob")
+    # our kernels read packed weights (as the decode runner's); cuBLAS keeps the row-major ones
+    pw1, pw2 = (pack_weight(w1), pack_weight(w2)) if a.packed else (w1, w2)
+    lin1, lin2 = Linear(pw1, "cob"), Linear(pw2, "cob")
     try:
         import vllm._custom_ops  # noqa: F401
 
@@ -93,6 +91,12 @@ def main():
     if run:
         run.snapshot()
     roof_hbm = (H * K1 + N2 * H) * 2 / (hbm_gbs() * 1e3)  # us
+    try:
+        peer_gbs = link_gbs()
+    except NoRecord as e:  # the roofline then counts the weight bytes only
+        peer_gbs = None
+        if rank == 0:
+            print(f"note: {e}", flush=True)
     rows, n_job = [], 0
     for B in batches:
         x = torch.randn(B, K1, generator=g, device=dev).bfloat16()
@@ -115,8 +119,8 @@ def main():
             ctx = None
             if impl == "fused":
                 def fn():
-                    comm.gemm_push(x, w1)
-                    comm.ar_norm_gemm(res, gamma, w2, a.eps, out=out)
+                    comm.gemm_push(x, pw1)
+                    comm.ar_norm_gemm(res, gamma, pw2, a.eps, out=out)
             elif impl == "ours_split":
                 lin1.tune(B)
                 lin2.tune(B)
@@ -193,7 +197,7 @@ def main():
                 st = summary(per) if per else {}
                 worst = max((t[1] for t in gathered if t[1] == t[1]), default=float("nan"))
                 errs = next((t[2] for t in gathered if t[2]), "" if all(ok_all) else "unavailable")
-                roof_link = (world - 1) * B * H * 2 / (PEER_GBS * 1e3)
+                roof_link = (world - 1) * B * H * 2 / (peer_gbs * 1e3) if peer_gbs else 0.0
                 roof = max(roof_hbm, roof_link)
                 row = dict(impl=impl, world=world, batch=B, p50_us=st.get("p50"), p99_us=st.get("p99"),
                            max_rel_err=worst, correct=bool(worst == worst and worst <= TOL), error=errs,
@@ -206,7 +210,7 @@ def main():
                 run.schedule(n_job, f"{impl}_B{B}", t0, time.time() - t0, 1 if errs else 0, state)
                 n_job += 1
     if rank == 0:
-        run.write_json("boundary.json", dict(args=vars(a), world=world, hbm_gbs=hbm_gbs(), peer_gbs=PEER_GBS,
+        run.write_json("boundary.json", dict(args=vars(a), world=world, hbm_gbs=hbm_gbs(), peer_gbs=peer_gbs,
                                              comm=comm.describe(), rows=rows,
                                              baseline_norm="vllm fused_add_rms_norm" if vops is not None
                                              else "torch add + rms_norm (vLLM missing)"))

@@ -129,7 +129,9 @@ def _write_csv(path: Path, rows: list[dict], cols: list[str]):
             w.writerow(r)
 
 
-def sweep_figures(doc: dict, out: Path) -> list[Path]:
+def sweep_figures(doc: dict, out: Path, link_gbs: float | None = None) -> list[Path]:
+    """Latency per message size, and the achieved fraction of the NVLink roofline at `link_gbs` (default:
+    the newest committed platform record, utils.peaks.link_gbs)."""
     rows = [r for r in doc["rows"] if r.get("correct") and r.get("p50_us")]
     series: dict[str, list] = {}
     for r in rows:
@@ -144,17 +146,16 @@ def sweep_figures(doc: dict, out: Path) -> list[Path]:
     # achieved fraction of the NVLink roofline (analyze_sweep.roofline_table): ours and the best baseline
     from .analyze_sweep import roofline_table
 
-    _, summ = roofline_table(doc["rows"])
-    frac = {"best of ours": [(s["target_us"] * 770e3, s["fraction"]) for s in summ if s["fraction"]],
-            "best baseline": [(s["target_us"] * 770e3, s["baseline_fraction"]) for s in summ
-                              if s["baseline_fraction"]]}
-    # x: the message size (target_us x link bandwidth is 2 (W-1)/W of it; the size itself is plotted)
+    _, summ = roofline_table(doc["rows"], link_gbs)
+    frac = {"best of ours": [(s["bytes"], s["fraction"]) for s in summ if s["fraction"]],
+            "best baseline": [(s["bytes"], s["baseline_fraction"]) for s in summ if s["baseline_fraction"]]}
     w = doc.get("world") or 2
-    frac = {k: [(x * w / (2 * (w - 1)), y) for x, y in v] for k, v in frac.items()}
+    gbs = summ[0]["link_gbs"] if summ else link_gbs
     _write_csv(out / "roofline.csv", summ, ["world", "tokens", "target_us", "ours", "fraction", "baseline",
                                             "baseline_fraction"])
     (out / "roofline.svg").write_text(line_chart(
-        frac, f"fraction of the NVLink roofline (2 (W-1)/W x S at 770 GB/s), {w} GPUs", "message size (bytes)",
+        frac, f"fraction of the NVLink roofline (2 (W-1)/W x S at {gbs:.0f} GB/s measured), {w} GPUs",
+        "message size (bytes)",
         "fraction", xfmt=_kb))
     return [out / "per_op.csv", out / "latency.svg", out / "roofline.csv", out / "roofline.svg"]
 
@@ -187,12 +188,14 @@ def share_figures(doc: dict, out: Path) -> list[Path]:
     return [out / "share.csv", out / "share.svg"]
 
 
-def render(run_dir: Path, base: Path | None = None) -> list[Path]:
+def render(run_dir: Path, base: Path | None = None, link_gbs: float | None = None) -> list[Path]:
     """Figures of one run directory into <base>/figures/<exp>/<ts>/ (exp and ts from the run's path)."""
     run_dir = Path(run_dir)
     out = (base or ROOT) / "figures" / run_dir.parent.name / run_dir.name
     out.mkdir(parents=True, exist_ok=True)
-    for name, fn in (("sweep.json", sweep_figures), ("boundary.json", boundary_figures), ("summary.json", share_figures)):
+    if (run_dir / "sweep.json").exists():
+        return sweep_figures(json.loads((run_dir / "sweep.json").read_text()), out, link_gbs)
+    for name, fn in (("boundary.json", boundary_figures), ("summary.json", share_figures)):
         if (run_dir / name).exists():
             return fn(json.loads((run_dir / name).read_text()), out)
     raise ValueError(f"no known result file in {run_dir}")

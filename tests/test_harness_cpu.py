@@ -283,7 +283,7 @@ def test_figures_from_runs(tmp_path):
                                    ("per_op.csv", "latency.svg", "roofline.csv", "roofline.svg")),
                                   ("boundary_bench", "boundary.json", bnd, ("boundary.csv", "boundary.svg")),
                                   ("train_share", "summary.json", share, ("share.csv", "share.svg"))):
-        out = render(run(exp, name, doc), base=tmp_path)
+        out = render(run(exp, name, doc), base=tmp_path, link_gbs=770.0)
         assert [p.name for p in out] == list(files)
         assert out[0].parent == tmp_path / "figures" / exp / "20260101_000000"
         xml.dom.minidom.parse(str(out[1]))
@@ -468,3 +468,21 @@ def test_bench_result_line_contract():
     assert line["config"]["parallelism"] == "tp8" and line["gpu_launches"] == 566 * 64
     assert {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"} <= set(line["e2e"])
     assert line["config"]["fused_boundaries"]["attention_out"] is False and "141 GB" in line["config"]["l2"]
+
+
+def test_measured_link_rate_from_newest_record(tmp_path):
+    """The NVLink denominator comes from the newest platform record; no record, no number."""
+    from comm_opt_b200.utils.peaks import NoRecord, hbm_gbs, link_gbs
+
+    with pytest.raises(NoRecord):
+        link_gbs(tmp_path)
+    for ts, v in (("20261201_000000", 700.0), ("20261202_000000", 771.5)):
+        (tmp_path / ts).mkdir()
+        (tmp_path / ts / "link.json").write_text(json.dumps(dict(gpus=8, peer_copy_gbs_median=v)))
+    assert link_gbs(tmp_path) == 771.5
+    (tmp_path / "20261203_000000").mkdir()
+    (tmp_path / "20261203_000000" / "link.json").write_text(json.dumps(dict(gpus=1, hbm_copy_gbs=[6500.0])))
+    with pytest.raises(NoRecord):
+        link_gbs(tmp_path)  # a one-GPU record has no peer copy
+    (tmp_path / "peaks.json").write_text(json.dumps(dict(hbm_gbs=6542.4)))
+    assert hbm_gbs(tmp_path / "peaks.json") == 6542.4

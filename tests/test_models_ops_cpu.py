@@ -107,10 +107,10 @@ def test_analyze_and_calibrate_synthetic_sweep(tmp_path):
     again = VariantTable.load(tmp_path / "vt.json")
     assert again.lookup(8, torch.bfloat16, 2, 8192, 64, False).variant == VARIANTS["lamport_2s"]
     json.loads((tmp_path / "vt.json").read_text())
-    # NVLink roofline: 2 (W - 1) / W x 1 MB at 770 GB/s = 2.38 us; fastest of ours at 64 tokens is 12 us
+    # NVLink roofline at a given link rate: 2 (W - 1) / W x 1 MB at 770 GB/s = 2.38 us; fastest of ours at 64 tokens is 12 us
     from comm_opt_b200.harness.analyze_sweep import roofline_table
 
-    text, summ = roofline_table(rows)
+    text, summ = roofline_table(rows, link_gbs=770.0)
     r64 = next(r for r in summ if r["tokens"] == 64)
     assert r64["ours"] == "ours:lamport_2s" and abs(r64["target_us"] - 2.383) < 1e-2
     assert abs(r64["fraction"] - r64["target_us"] / 12.0) < 1e-9 and r64["baseline"] == "vllm_car"
