@@ -45,8 +45,9 @@ def parse():
     p.add_argument("--collective", choices=["ours", "nccl", "vllm"], default="ours",
                    help="nccl: the same runner with NCCL all-reduce + add/RMSNorm kernel (baseline decode step); "
                         "vllm: vLLM custom all-reduce + vLLM fused_add_rms_norm (the reference's baseline stack)")
-    p.add_argument("--fuse-epilogues", type=int, choices=[0, 1], default=0,
-                   help="with fused boundaries: SiLU * up and RoPE + KV append in the consumer GEMMs")
+    p.add_argument("--fuse-epilogues", type=int, choices=[0, 1], default=1,
+                   help="with fused boundaries: SiLU * up and RoPE + KV append in the consumer GEMMs where they "
+                        "have a geometry for them (with --tune-boundaries, kept only where measured faster)")
     p.add_argument("--fuse-boundary", type=int, choices=[0, 1], default=1,
                    help="fuse o_proj/down_proj -> all-reduce + RMSNorm -> next GEMM (TP > 1; 0 = separate "
                         "GEMM, fused all-reduce + RMSNorm kernel, GEMM)")
@@ -156,6 +157,8 @@ def result_line(args, cfg, world: int, ms: float, ms_e2e: float, e2e_steps: int,
                    "fuse_epilogues": runner.fuse_boundary and runner.fuse_epilogues,
                    "fuse_fallback": runner.fuse_error[:200] or None,
                    "fused_boundaries": (dict(zip(("attention_out", "mlp_out"), runner.fuse_kinds.get(B, (True, True))),
+                                             epilogues=dict(zip(("swiglu", "rope_kv"),
+                                                                runner.fused_epilogues_used(B))),
                                              step_ms_by_choice=runner.boundary_times.get(B))
                                         if runner.fuse_boundary else None),
                    "tokens_per_s": round(B * 1000.0 / ms, 1), "l2_prefetch_tiles": args.l2_prefetch,

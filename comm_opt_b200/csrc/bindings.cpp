@@ -219,8 +219,19 @@ std::vector<int64_t> py_fused_gemm(int64_t kind, std::vector<int64_t> bases, std
   check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, w.device().index()), "sm count");
   COB_CHECK(epi >= 0 && epi <= 2 && (kind == 1 || epi == 0), "epilogue 0 plain, 1 swiglu, 2 rope_kv (consumer only)");
   p.epi = (int)epi;
-  const cob::FusedGemmPlan pl =
+  cob::FusedGemmPlan pl =
       cob::plan_fused_gemm((int)M, (int)N, (int)K, (int)splits, std::max(1, sms / ranks), kind == 1, (int)epi);
+  if (kind == 1 && splits <= 0 && !dry_run) {
+    // automatic plan of the consumer: fewer K-splits while the occupancy bound says its clusters do not
+    // all fit at once (launch_ar_norm_gemm would reject the grid)
+    while (pl.splits > 1) {
+      const int cap = cob::ar_norm_gemm_resident_clusters(pl.bn, pl.splits);
+      if (cap < 0 || (long long)pl.xctas * ranks <= cap) break;
+      const int fewer = pl.splits / 2;
+      if (epi != cob::kEpiPlain && fewer < 2) break;
+      pl = cob::plan_fused_gemm((int)M, (int)N, (int)K, fewer, std::max(1, sms / ranks), true, (int)epi);
+    }
+  }
   if (dry_run) return {pl.bn, pl.tiles, pl.splits, pl.kps, pl.xctas};
   COB_CHECK(pl.splits > 0, "no launch geometry supports this epilogue for [", M, ", ", N, ", ", K, "]");
   if (epi == cob::kEpiRopeKv) {

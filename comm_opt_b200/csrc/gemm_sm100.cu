@@ -51,18 +51,27 @@ enum : int {
 
 // SMALL: half the shared-memory ring, so two CTAs (this kernel and the next one in the stream under
 // programmatic dependent launch) fit on one SM.
-template <int BN, bool SMALL = false>
+// CL: cluster split-K, which adds a reduction area for the partial tiles that the cluster's CTAs push
+// to each other (outside the ring, so a peer can write it while this CTA's MMAs still read the ring).
+template <int BN, bool SMALL = false, bool CL = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK * 2;  // 16 KB weight tile
   static constexpr int B_BYTES = BN * BK * 2;  // activation tile
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int STAGES_RAW = ((SMALL ? kSmemBudget / 2 : kSmemBudget) - 2048) / STAGE;
+  static constexpr int RED = CL ? ((BM + 8) * (BN + 4) * 4 + 127) / 128 * 128 : 0;
+  static constexpr int STAGES_RAW = ((SMALL ? kSmemBudget / 2 : kSmemBudget) - 2048 - RED) / STAGE;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   static constexpr int PIPE = STAGES * STAGE;
-  static constexpr int SMEM = PIPE + 1024 + 512;  // alignment slack + barriers + contributor table
-  static constexpr int TC = BN < 32 ? 32 : BN;    // TMEM columns per accumulator buffer
-  static constexpr int TMEM_COLS = 2 * TC;        // double-buffered accumulator
+  static constexpr int SMEM = PIPE + RED + 1024 + 512;  // alignment slack + barriers + contributor table
+  static constexpr int TC = BN < 32 ? 32 : BN;          // TMEM columns per accumulator buffer
+  static constexpr int TMEM_COLS = 2 * TC;              // double-buffered accumulator
 };
+
+// Cluster barrier halves (non-aligned forms: lanes of a warp may reach them at different points).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
 
 template <bool BF16>
 __device__ __forceinline__ void store_out(void* Y, size_t idx, float v) {
@@ -92,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
                    int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
                    int kps, int l2pf, long long* stamps, const uint8_t* __restrict__ Wp) {
-  using C = Cfg<BN, SMALL>;
+  using C = Cfg<BN, SMALL, CLUSTER>;
   // optional phase stamps (%globaltimer, ns): stamps[cta * kStampSlots + phase]
   const int lin = blockIdx.x + blockIdx.y * gridDim.x;
   auto stamp = [&](int phase) {
@@ -103,7 +112,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::PIPE);
+  float* red = reinterpret_cast<float*>(smem + C::PIPE);  // [cs][per][BN + 4] partial rows pushed here (CLUSTER)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::PIPE + C::RED);
   uint64_t* empty = full + C::STAGES;
   uint64_t* tfull = empty + C::STAGES;  // [2] accumulator ready for the epilogue
   uint64_t* tempty = tfull + 2;         // [2] accumulator drained by the epilogue
@@ -150,6 +160,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) stamp(kStSetup);
+  // cluster split-K: peers push partial rows into this CTA's reduction area; the first half of a cluster
+  // barrier here, its second half before the first push, makes sure every CTA of the cluster has started
+  const bool split_cluster = CLUSTER && gridDim.y > 1;
+  if (split_cluster) cluster_arrive_relaxed();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -251,6 +265,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const int row = q * 32 + lane;
     const int mcols = min(M, BN);
+    // cluster split-K: row `row` of this CTA's partial tile goes to the CTA that owns it (rows
+    // [o * per, (o + 1) * per) belong to CTA o of the cluster), slot blockIdx.y of that CTA's reduction area
+    float* push_dst = nullptr;
+    if (split_cluster) {
+      const int per = (BM + gridDim.y - 1) / gridDim.y, o = row / per;
+      cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
+      push_dst = cg::this_cluster().map_shared_rank(red, o) + ((size_t)blockIdx.y * per + (row - o * per)) * (BN + 4);
+    }
     int j = 0;
     for (long long g = beg; g < end; ++j) {
       const int t = (int)(g / KT);
@@ -265,9 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (q == 2 && lane == 0) stamp(kStAccReady);
       const uint32_t taddr = tmem + acc * C::TC + ((uint32_t)(q * 32) << 16);
       // partial segments go to workspace slot 0 (first tile of this CTA) or 1 (its last tile),
-      // row-major [row][BN] so the finisher reads 16-byte vectors; in cluster mode to this CTA's
-      // own shared memory (the ring is drained: this is the CTA's only segment)
-      float* part = CLUSTER ? reinterpret_cast<float*>(smem) + (size_t)row * (BN + 4)
+      // row-major [row][BN] so the finisher reads 16-byte vectors; in cluster mode straight into the
+      // owning CTA's shared memory (distributed shared memory stores; this is the CTA's only segment)
+      float* part = CLUSTER ? push_dst
                             : ws + ((size_t)cta * 2 + (t == first_tile ? 0 : 1)) * BN * BM + (size_t)row * BN;
       for (int c0 = 0; c0 < mcols; c0 += 16) {
         float v[16];
@@ -344,27 +366,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ------------------------------------------------ cluster split-K: sum the partials over DSMEM (all threads)
-  if (CLUSTER && gridDim.y > 1) {
-    __syncthreads();  // this CTA's partial tile is in its shared memory
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
+  // ------------------------------------------------ cluster split-K: sum the pushed partial rows (all threads)
+  if (split_cluster) {
+    if (warp < 2) cluster_wait();  // second half of the start-up barrier (the epilogue warps passed it)
+    __syncthreads();               // warps 0 and 1 reconverged (their lane 0 had its own role)
+    cg::this_cluster().sync();     // release / acquire: every partial row has reached its owner
     const int cs = gridDim.y, r = blockIdx.y, t = blockIdx.x;
     const int mcols = min(M, BN);
-    const int per = (BM + cs - 1) / cs, r0 = r * per, r1 = min(BM, r0 + per), nr = r1 - r0;
+    const int per = (BM + cs - 1) / cs, r0 = r * per, nr = min(BM, r0 + per) - r0;
     const int ncol4 = (mcols + 3) / 4;
     for (int idx = threadIdx.x; idx < nr * ncol4; idx += kThreads) {
-      const int rr = r0 + idx % nr, c4 = (idx / nr) * 4;
+      const int lr = idx % nr, c4 = (idx / nr) * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = 0; c < cs; ++c) {
-        const float4 v = *reinterpret_cast<const float4*>(
-            cluster.map_shared_rank(reinterpret_cast<float*>(smem), c) + (size_t)rr * (BN + 4) + c4);
+      for (int c = 0; c < cs; ++c) {  // sources in cluster order: deterministic
+        const float4 v = *reinterpret_cast<const float4*>(red + ((size_t)c * per + lr) * (BN + 4) + c4);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
         acc.w += v.w;
       }
-      const int nn = t * BM + rr;
+      const int nn = t * BM + r0 + lr;
       if (nn < N) {
         const float o[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
@@ -372,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c4 + u < M) store_out<BF16>(Y, (size_t)(c4 + u) * ldy + nn, o[u]);
       }
     }
-    cluster.sync();  // no CTA leaves while another still reads its shared memory
+    // no second cluster barrier: after the one above nobody touches another CTA's shared memory
   }
 
   // ------------------------------------------------ teardown
@@ -398,12 +419,12 @@ template <int BN, bool BF16, bool SMALL>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int M, int N, int K, int ctas, int ldy,
                       float* ws, int* ctr, int* err, unsigned long long timeout_ns, bool pdl, int splits,
                       cudaStream_t stream, const uint8_t* Wp) {
-  using C = Cfg<BN, SMALL>;
   const bool clustered = splits > 0;
+  const int smem = clustered ? Cfg<BN, SMALL, true>::SMEM : Cfg<BN, SMALL, false>::SMEM;
   auto fn = clustered ? k_gemm_streamk<BN, BF16, SMALL, true> : k_gemm_streamk<BN, BF16, SMALL, false>;
   static bool attr_set[2] = {false, false};
   if (!attr_set[clustered]) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
@@ -414,7 +435,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = clustered ? dim3((N + BM - 1) / BM, (KT + kps - 1) / kps, 1) : dim3(ctas, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   int na = 0;

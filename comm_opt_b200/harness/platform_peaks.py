@@ -53,8 +53,9 @@ def measure(gib: float = 1.0, reps: int = 10) -> dict:
     n = torch.cuda.device_count()
     nbytes = int(gib * (1 << 30))
     out = dict(gpus=n, bytes=nbytes, reps=reps, name=torch.cuda.get_device_name(0))
-    bufs = [torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{d}") for d in range(n)]
-    recv = [torch.empty(nbytes, dtype=torch.uint8, device=f"cuda:{d}") for d in range(n)]
+    # bf16 elements, as the driver's own HBM copy measurement
+    bufs = [torch.empty(nbytes // 2, dtype=torch.bfloat16, device=f"cuda:{d}") for d in range(n)]
+    recv = [torch.empty(nbytes // 2, dtype=torch.bfloat16, device=f"cuda:{d}") for d in range(n)]
     streams = [torch.cuda.Stream(device=d) for d in range(n)]
     hbm = []
     for d in range(n):
@@ -84,7 +85,7 @@ def measure(gib: float = 1.0, reps: int = 10) -> dict:
     bidir()
     out["peer_bidir_gbs"] = round(nbytes / _time(bidir, reps, [streams[0], streams[1]]) / 1e9, 1)
 
-    chunk = nbytes // (n - 1) // 256 * 256
+    chunk = nbytes // 2 // (n - 1) // 128 * 128  # elements per peer
     fan = [torch.cuda.Stream(device=0) for _ in range(n - 1)]
 
     def fanout():
@@ -92,7 +93,7 @@ def measure(gib: float = 1.0, reps: int = 10) -> dict:
             with torch.cuda.device(0), torch.cuda.stream(fan[j - 1]):
                 recv[j][:chunk].copy_(bufs[0][:chunk], non_blocking=True)
     fanout()
-    out["fanout_gbs"] = round(chunk * (n - 1) / _time(fanout, reps, fan) / 1e9, 1)
+    out["fanout_gbs"] = round(2 * chunk * (n - 1) / _time(fanout, reps, fan) / 1e9, 1)
     return out
 
 

@@ -283,6 +283,9 @@ class TPDecodeRunner:
         # per batch size: (attention-output boundary fused, MLP-output boundary fused); with
         # tune_boundaries the capture times each combination and keeps the fastest (max over ranks)
         self.fuse_kinds: dict[int, tuple[bool, bool]] = {}
+        # per batch size: (SiLU epilogue in the gate_up consumer, RoPE + KV append in the QKV consumer)
+        # used where available; chosen together with the boundary kinds when tuning
+        self.epi_use: dict[int, tuple[bool, bool]] = {}
         self.tune_boundaries = bool(tune_boundaries)
         self.boundary_times: dict[int, dict[str, float]] = {}
         if self.fuse_boundary:
@@ -441,6 +444,15 @@ class TPDecodeRunner:
             self._fuse_epi[B] = (sw, rp)
         return self._fuse_epi[B]
 
+    def fused_epilogues_used(self, B: int) -> tuple[bool, bool]:
+        """(SiLU in gate_up, RoPE + KV append in QKV) as the captured step for batch B runs them."""
+        if not self.fuse_boundary or B not in self._fuse_epi:
+            return False, False
+        fa, fm = self.fuse_kinds.get(B, (True, True))
+        ua, um = self.epi_use.get(B, (True, True))
+        sw, rp = self._fuse_epi[B]
+        return bool(sw and fa and ua), bool(rp and fm and um)
+
     def _step_fused(self, B: int, buf: dict, bt: torch.Tensor) -> int:
         """Decode step with fused layer boundaries (after the embedding and first norm). Each of the two
         boundary kinds of a layer - attention output (o_proj -> all-reduce + residual + RMSNorm ->
@@ -450,8 +462,9 @@ class TPDecodeRunner:
         in the gate_up epilogue and RoPE + the paged-KV append in the QKV epilogue."""
         cfg, s, w, comm = self.cfg, self.s, self.w, self.comm
         fa, fm = self.fuse_kinds.get(B, (True, True))
+        ua, um = self.epi_use.get(B, (True, True))
         sw, rp = self._fused_epilogues(B, buf)
-        sw, rp = sw and fa, rp and fm
+        sw, rp = sw and fa and ua, rp and fm and um
         n = 0
         self.lin[(0, "qkv")](buf["h"], out=buf["qkv"])
         n += 1
@@ -510,14 +523,22 @@ class TPDecodeRunner:
 
     def _tune_fusion(self, B: int, buf: dict, saved: dict, warm: int = 2, reps: int = 5) -> tuple[bool, bool]:
         """Time one captured decode step per choice of fused / separate boundaries (attention output,
-        MLP output) and return the fastest. The per-choice times are reduced with MAX over the ranks
-        before the choice, so every rank takes the same one; the decode state is restored after each."""
+        MLP output) and, where a fused boundary's consumer GEMM supports its epilogue (SiLU * up in
+        gate_up, RoPE + KV append in the next QKV) and `fuse_epilogues` is set, with and without it.
+        The per-choice times are reduced with MAX over the ranks before the choice, so every rank takes
+        the same one; the decode state is restored after each. Sets `epi_use[B]`, returns the kinds."""
         import torch.distributed as dist
 
-        combos = [(True, True), (True, False), (False, True), (False, False)]
+        sw_ok, rp_ok = self._fused_epilogues(B, buf)
+        combos = []
+        for fa in (True, False):
+            for fm in (True, False):
+                for ua in ((True, False) if fa and sw_ok else (False,)):
+                    for um in ((True, False) if fm and rp_ok else (False,)):
+                        combos.append((fa, fm, ua, um))
         times = torch.zeros(len(combos), dtype=torch.float64, device=self.device)
-        for j, kinds in enumerate(combos):
-            self.fuse_kinds[B] = kinds
+        for j, (fa, fm, ua, um) in enumerate(combos):
+            self.fuse_kinds[B], self.epi_use[B] = (fa, fm), (ua, um)
             s = torch.cuda.Stream(self.device)  # one eager step first, as before any capture
             s.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(s):
@@ -547,8 +568,18 @@ class TPDecodeRunner:
                 buf[k].copy_(v)
         dist.all_reduce(times, op=dist.ReduceOp.MAX, group=self.nccl_group)
         t = times.tolist()
-        self.boundary_times[B] = {("F" if a else "S") + ("F" if m else "S"): round(x, 4) for (a, m), x in zip(combos, t)}
-        return combos[min(range(len(combos)), key=lambda k: (t[k], k))]
+
+        def label(c):  # S: separate, F: fused, E: fused with the consumer's epilogue
+            fa, fm, ua, um = c
+            return ("E" if ua else "F" if fa else "S") + ("E" if um else "F" if fm else "S")
+
+        self.boundary_times[B] = {label(c): round(x, 4) for c, x in zip(combos, t)}
+        best = combos[min(range(len(combos)), key=lambda k: (t[k], k))]
+        self.epi_use[B] = best[2:]
+        if not best[2] and self._wgu_il is not None and all(not u[0] for u in self.epi_use.values()):
+            self._wgu_il = None  # the interleaved gate/up copies are not used by the chosen step
+            self._fuse_epi = {b: (False, v[1]) for b, v in self._fuse_epi.items()}
+        return best[:2]
 
     def start(self, B: int, first_ids: torch.Tensor, prompt_len: int):
         """Set up decoding of B sequences whose prompts (length prompt_len) are in the cache."""

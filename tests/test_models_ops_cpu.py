@@ -248,7 +248,7 @@ def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
     r.cos = r.sin = None
     r.scale = 1.0
     r.fuse_boundary, r.fuse_kinds, r.fuse_epilogues = fuse, {4: kinds}, any(epi)
-    r._fuse_epi, r._wgu_il = {4: epi}, [None] * layers
+    r._fuse_epi, r._wgu_il, r.epi_use = {4: epi}, [None] * layers, {}
     buf = {k: torch.zeros(4, 8) for k in ("ids", "pos", "lens", "res", "h", "part", "qkv", "q", "attn", "gu", "act",
                                            "logits")}
     buf["keys"] = torch.zeros(4, dtype=torch.int64)
