@@ -32,7 +32,7 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
                         bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
                         cudaStream_t stream, GemmPlan* used, bool packed = false);
 // cluster_splits > 0 selects the cluster split-K schedule (grid tiles x splits, DSMEM reduction,
-// M <= 64, splits <= 8) instead of stream-K.
+// M <= 64, splits <= 16; above 8 a non-portable cluster size) instead of stream-K.
 // packed: W is the packed weight layout (see pack_weight in the Python package): for output tile
 // t = n / 128 and k-step k = K-column / 64, block t * (K / 64) + k of 128 x 64 elements (16 KB) holds
 // rows t*128.. and columns k*64.. exactly as the 128-byte-swizzled shared-memory image (16-byte chunk c

@@ -428,6 +428,10 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
+    if (clustered) {  // 9..16 splits: non-portable cluster sizes (narrow outputs such as QKV at TP = 8)
+      e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+    }
     attr_set[clustered] = true;
   }
   const int KT = (K + BK - 1) / BK;
@@ -510,7 +514,7 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
                         size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
                         bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
                         cudaStream_t stream, GemmPlan* used, bool packed) {
-  if (cluster_splits > 8 || (cluster_splits > 0 && M > 64)) return cudaErrorInvalidValue;
+  if (cluster_splits > 16 || (cluster_splits > 0 && M > 64)) return cudaErrorInvalidValue;
   if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % 8 || (dtype != kBF16 && dtype != kF16))
     return cudaErrorInvalidValue;
   // packed weights: whole 128 x 64 blocks, 16-byte aligned

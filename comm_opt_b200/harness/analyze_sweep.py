@@ -137,6 +137,39 @@ def roofline_table(rows: list[dict], link_gbs: float | None = None) -> tuple[str
     return "\n".join(out), summary
 
 
+def validate(rows: list[dict], tol: float = 0.03) -> list[dict]:
+    """Check the variant table in fresh launches (the reference's validate step,
+    exp/M18_incremental/run_b.py:60-76 and README.md:131-140): `rows` hold several independent sweeps,
+    each with `ours:auto` (the table's choice) and the individual variants. Per (world, dtype, hidden,
+    tokens): median [min, max] over launches of auto and of every fixed variant; `within` = auto is within
+    `tol` of the best fixed variant's median; `retune` = a fixed variant beats auto by >= `tol` with
+    disjoint [min, max] intervals over >= 3 launches (the only case in which the table entry changes)."""
+    from ..utils.stats import disjoint, median_minmax
+
+    out = []
+    keys = sorted({(r["world"], r["dtype"], r["hidden"], r["tokens"]) for r in rows if r["impl"] == "ours:auto"})
+    for w, dt, h, T in keys:
+        at = [r for r in rows if (r["world"], r["dtype"], r["hidden"], r["tokens"]) == (w, dt, h, T)
+              and r.get("correct") and r.get("p50_us")]
+        per: dict[str, list[float]] = {}
+        for r in at:
+            if r["impl"].startswith("ours:"):
+                per.setdefault(r["impl"], []).append(r["p50_us"])
+        if "ours:auto" not in per:
+            continue
+        auto = median_minmax(per.pop("ours:auto"))
+        if not per:
+            continue
+        stats = {k: median_minmax(v) for k, v in per.items()}
+        best = min(stats, key=lambda k: stats[k]["med"])
+        b = stats[best]
+        gain = auto["med"] / b["med"] - 1.0
+        out.append(dict(world=w, dtype=dt, hidden=h, tokens=T, auto=auto, best=best, best_stats=b, gain=gain,
+                        within=gain <= tol,
+                        retune=gain >= tol and disjoint(auto, b) and auto["n"] >= 3 and b["n"] >= 3))
+    return out
+
+
 def calibrate(rows: list[dict], table_path: Path | None = None) -> VariantTable:
     """Fastest correct variant (with its geometry) per (world, dtype, hidden, rows bucket)."""
     import torch
@@ -162,10 +195,22 @@ def main():
     ap.add_argument("--table", default=None)
     ap.add_argument("--nvlink", action="store_true", help="measured vs expected NVLink bytes per call")
     ap.add_argument("--roofline", action="store_true", help="achieved fraction of the NVLink roofline per size")
+    ap.add_argument("--validate", action="store_true",
+                    help="the given sweeps are fresh launches with ours:auto: check the table (3 % rule)")
     ap.add_argument("--repeats", nargs=2, metavar=("OURS", "BASELINE"),
                     help="median [min, max] over the given sweeps (independent launches) and the effectiveness rule")
     a = ap.parse_args()
     rows = load(a.sweeps)
+    if a.validate:
+        print("| world | dtype | hidden | tokens | auto med [min, max] | best fixed | med [min, max] | auto slower by | "
+              "within 3 % | retune |")
+        print("|---|---|---|---|---|---|---|---|---|---|")
+        for r in validate(rows):
+            o, b = r["auto"], r["best_stats"]
+            print(f"| {r['world']} | {r['dtype']} | {r['hidden']} | {r['tokens']} | {o['med']:.2f} [{o['lo']:.2f}, "
+                  f"{o['hi']:.2f}] (n={o['n']}) | {r['best']} | {b['med']:.2f} [{b['lo']:.2f}, {b['hi']:.2f}] | "
+                  f"{100 * r['gain']:+.1f}% | {'yes' if r['within'] else 'no'} | {'yes' if r['retune'] else 'no'} |")
+        return
     if a.repeats:
         print(f"| world | tokens | {a.repeats[0]} med [min, max] | {a.repeats[1]} med [min, max] | gain | effective |")
         print("|---|---|---|---|---|---|")

@@ -69,6 +69,7 @@ VARIANTS = {  # name -> gemm() keyword arguments
     "cl2_small_pdl": dict(cluster_splits=2, small_smem=True, pdl=True),
     "cl4_small_pdl": dict(cluster_splits=4, small_smem=True, pdl=True),
     "cl8_small_pdl": dict(cluster_splits=8, small_smem=True, pdl=True),
+    "cl16_small_pdl": dict(cluster_splits=16, small_smem=True, pdl=True),
 }
 
 

@@ -328,6 +328,24 @@ def fused_hidden_plan(world: int = 8, impls: str = "ours:auto,vllm_car,trt_onesh
     return plan
 
 
+def calibrate_validate_plan(worlds=(2, 8), repeats: int = 3, hiddens=(8192, 5120, 4096),
+                            dtypes=("bfloat16", "float16")) -> list[Launch]:
+    """Sweeps of every variant plus ours:auto per (world, hidden, dtype), `repeats` independent launches
+    each. Calibrate: `analyze_sweep --calibrate` over one run of this plan writes the variant table.
+    Validate: run the plan again (fresh launches reading the new table) and `analyze_sweep --validate`
+    over its sweeps applies the >= 3 % / disjoint-interval rule to ours:auto against every variant."""
+    impls = "ours:auto,ours:lamport_1s,ours:lamport_1sx,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,ours:nvls_2s"
+    plan = []
+    for w in worlds:
+        for h in hiddens:
+            for dt in dtypes:
+                for r in range(repeats):
+                    plan.append(Launch("fused_sweep", w, repeat=r, label=f"h{h}_{dt}", env={"COB_EXPERIMENTAL": "1"},
+                                       argv=("--impls", impls, "--hidden", str(h), "--dtype", dt,
+                                             "--tokens", "1,2,4,8,16,32,64,128,256,512", "--replays", "20")))
+    return plan
+
+
 def primitives_plan(worlds=(2, 4, 8)) -> list[Launch]:
     """Which NVLink primitive wins where (the reference's M11 / M12-M13 / M8 probes, re-asked on B200):
     the reduce-scatter by remote vector atomics, push vs pull all-gather / reduce-scatter in steady state
@@ -350,6 +368,7 @@ PLANS = {
     "p2p_channels": lambda w: p2p_channel_plan(),
     "validate": lambda w: validate_plan(w),
     "primitives": lambda w: primitives_plan(w),
+    "calibrate_validate": lambda w: calibrate_validate_plan(w),
 }
 
 

@@ -126,10 +126,10 @@ def candidates(M: int, N: int, K: int, num_sms: int = 148) -> list[dict]:
     cands = [dict(), dict(small_smem=True)]
     tiles = (N + 127) // 128
     if M <= 64 and tiles < num_sms:
-        for s in (2, 3, 4, 6, 8):
+        for s in (2, 3, 4, 6, 8, 12, 16):
             if s > (K + 63) // 64:
                 continue
-            if tiles * s <= num_sms * 1.25:
+            if tiles * s <= num_sms * 1.25 and s <= 8:
                 cands.append(dict(cluster_splits=s))
             if tiles * s <= num_sms * 2:
                 cands.append(dict(cluster_splits=s, small_smem=True))

@@ -53,10 +53,13 @@ def test_gemm_into_strided_output_and_graph(cuda):
     assert torch.all(big[:, :1024] == 0) and torch.all(big[:, 3072:] == 0)
 
 
-@pytest.mark.parametrize("splits", [2, 3, 5, 8])
+@pytest.mark.parametrize("splits", [2, 3, 5, 8, 12, 16])
 @pytest.mark.parametrize("small", [False, True])
 def test_gemm_cluster_split_k(cuda, splits, small):
-    """Cluster split-K schedule (DSMEM reduction) against fp32, deterministic across calls."""
+    """Cluster split-K schedule (partial rows pushed to their owner CTA over distributed shared memory)
+    against fp32, deterministic across calls; 12 and 16 splits are non-portable clusters (half ring)."""
+    if splits > 8 and not small:
+        pytest.skip("clusters above 8 CTAs run with the half ring (two CTAs per SM)")
     for M, N, K in [(1, 1280, 8192), (8, 300, 1000), (64, 8192, 1024)]:
         x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
         w = (0.05 * torch.randn(N, K, device=cuda)).to(torch.bfloat16)

@@ -347,3 +347,24 @@ def test_pack_weight_layout_and_round_trip():
                         assert torch.equal(got, want)
     with pytest.raises(ValueError):
         pack_weight(torch.zeros(128, 100))
+
+
+def test_variant_table_validation_rule():
+    """Fresh launches of ours:auto against fixed variants: within 3 %, or retuned only when a variant is
+    >= 3 % faster with disjoint [min, max] intervals over >= 3 launches."""
+    from comm_opt_b200.harness.analyze_sweep import validate
+
+    def rows(auto, fixed, T):
+        out = []
+        for a, f in zip(auto, fixed):
+            out.append(dict(world=8, dtype="bfloat16", hidden=8192, tokens=T, impl="ours:auto", p50_us=a, correct=True))
+            out.append(dict(world=8, dtype="bfloat16", hidden=8192, tokens=T, impl="ours:lamport_2s", p50_us=f,
+                            correct=True))
+        return out
+
+    res = {r["tokens"]: r for r in validate(rows([10.0, 10.1, 10.2], [9.9, 10.0, 10.3], 8) +
+                                            rows([12.0, 12.2, 12.1], [10.0, 10.1, 10.2], 64) +
+                                            rows([12.0, 9.0, 12.1], [10.0, 10.1, 10.2], 128))}
+    assert res[8]["within"] and not res[8]["retune"]
+    assert not res[64]["within"] and res[64]["retune"] and res[64]["best"] == "ours:lamport_2s"
+    assert not res[128]["retune"]  # 18 % slower by the median, but the intervals overlap
