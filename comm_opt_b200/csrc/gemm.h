@@ -20,6 +20,11 @@ GemmPlan plan_gemm(int M, int N, int K, int num_sms, int ctas_override);
 // accumulator ready, last tile stored, end) at stamps[cta * kStampSlots + phase].
 constexpr int kStampSlots = 16;
 long long*& gemm_stamps();
+// With a stride > 0, launch n (counted from the last reset of gemm_stamp_launches) writes at
+// gemm_stamps() + n * stride, so every GEMM of a captured decode step keeps its own stamps.
+long long& gemm_stamp_stride();
+long long& gemm_stamp_launches();
+long long* next_gemm_stamps();
 // fp32 workspace needed for the partial tiles of a launch with `num_ctas` CTAs
 size_t gemm_workspace_bytes(int num_ctas, int bn);
 

@@ -458,7 +458,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   cfg.attrs = attrs;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps, l2_prefetch_tiles(),
-                            gemm_stamps(), Wp);
+                            next_gemm_stamps(), Wp);
 }
 
 template <bool BF16, bool SMALL>
@@ -488,6 +488,19 @@ cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, v
 long long*& gemm_stamps() {
   static long long* p = nullptr;
   return p;
+}
+long long& gemm_stamp_stride() {
+  static long long s = 0;
+  return s;
+}
+long long& gemm_stamp_launches() {
+  static long long n = 0;
+  return n;
+}
+long long* next_gemm_stamps() {
+  long long* p = gemm_stamps();
+  if (p == nullptr) return nullptr;
+  return p + gemm_stamp_stride() * gemm_stamp_launches()++;
 }
 
 GemmPlan plan_gemm(int M, int N, int K, int num_sms, int ctas_override) {

@@ -346,7 +346,15 @@ void register_ops(pybind11::module& m) {
         pybind11::arg("local_keys") = pybind11::none());
   m.def("set_pdl", [](bool on) { cob::pdl_flag() = on; });
   m.def("get_pdl", []() { return cob::pdl_flag(); });
-  m.def("set_gemm_stamps", [](int64_t ptr) { cob::gemm_stamps() = reinterpret_cast<long long*>(ptr); });
+  m.def(
+      "set_gemm_stamps",
+      [](int64_t ptr, int64_t stride) {
+        cob::gemm_stamps() = reinterpret_cast<long long*>(ptr);
+        cob::gemm_stamp_stride() = stride;
+        cob::gemm_stamp_launches() = 0;
+      },
+      pybind11::arg("ptr"), pybind11::arg("stride") = 0);
+  m.def("gemm_stamp_launches", []() { return (int64_t)cob::gemm_stamp_launches(); });
   m.def("set_l2_prefetch", [](int64_t tiles) { cob::l2_prefetch_tiles() = (int)std::max<int64_t>(0, tiles); });
   m.def("get_l2_prefetch", []() { return (int64_t)cob::l2_prefetch_tiles(); });
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);

@@ -71,8 +71,9 @@ def main():
     ap.add_argument("--eps", type=float, default=1e-6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--warm-s", type=float, default=2.0)
-    ap.add_argument("--nvlink", type=int, choices=[0, 1], default=1,
-                    help="NVLink bytes per op from NVML's throughput counters around the timed replays")
+    ap.add_argument("--nvlink", type=int, choices=[0, 1], default=0,
+                    help="NVLink bytes per op from NVML's throughput counters around the timed replays (off by "
+                         "default: the first 2-GPU sweep that read them aborted with host heap corruption)")
     ap.add_argument("--discard-first", type=int, choices=[0, 1], default=1,
                     help="measure the first (impl, tokens) config twice and drop the first copy")
     ap.add_argument("--exp", default="fused_sweep")

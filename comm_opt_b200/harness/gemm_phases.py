@@ -92,14 +92,25 @@ def main(argv=None):
     ap.add_argument("--variants", default="default")
     ap.add_argument("--ops", default=None)
     ap.add_argument("--runs", type=int, default=5)
+    ap.add_argument("--out-dir", default=None, help="base directory of results/ (default: the repository's)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    rows = []
     for name, N, K in shapes_for(a.shapes):
         if a.ops and name not in a.ops.split(","):
             continue
         for v in a.variants.split(","):
-            print(json.dumps(measure(name, N, K, a.batch, v, a.runs, dev)), flush=True)
+            rows.append(measure(name, N, K, a.batch, v, a.runs, dev))
+            print(json.dumps(rows[-1]), flush=True)
+    from pathlib import Path
+
+    from ..utils.results import RunDir
+
+    run = RunDir("gemm_phases", Path(a.out_dir) if a.out_dir else None)
+    run.snapshot()
+    run.write_json("phases.json", dict(args=vars(a), rows=rows))
+    print(run.path)
 
 
 if __name__ == "__main__":
