@@ -92,6 +92,54 @@ __device__ __forceinline__ int swzp(int r, int ch) { return ((ch >> 3) << 10) + 
 
 __device__ __forceinline__ float safe_exp2_diff(float a, float b) { return a == -INFINITY ? 0.f : exp2f(a - b); }
 
+// 16-byte chunk `ch` (8 elements) of head `head` of one token's projection row `src` (+ bias), rotated by
+// RoPE at position `pos`: element i of the first half pairs with i + D / 2. Rounded to T once, as the
+// separate append kernel stores it.
+template <typename T, int D>
+__device__ __forceinline__ uint4 rope_chunk(const AttnParams& p, const T* src, int head, int ch, int pos) {
+  using V = Vec<T>;
+  constexpr int H = D / 2, HC = H / 8;  // half width, chunks per half
+  const bool lo = ch < HC;
+  const int pc = lo ? ch + HC : ch - HC;  // partner chunk
+  const uint4* row = reinterpret_cast<const uint4*>(src + (size_t)head * D);
+  float x[8], y[8];
+  V::to_float(row[ch], x);
+  V::to_float(row[pc], y);
+  if (p.qkv_bias != nullptr) {
+    const uint4* bias = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.qkv_bias) + (size_t)head * D);
+    float bx[8], by[8];
+    V::to_float(bias[ch], bx);
+    V::to_float(bias[pc], by);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      x[j] += bx[j];
+      y[j] += by[j];
+    }
+  }
+  const int i0 = (lo ? ch : pc) * 8;  // index into the cos / sin row of this position
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float c = p.cos_t[(size_t)pos * H + i0 + j], sn = p.sin_t[(size_t)pos * H + i0 + j];
+    o[j] = lo ? x[j] * c - y[j] * sn : x[j] * c + y[j] * sn;
+  }
+  return V::from_float(o);
+}
+
+// chunk `ch` of head `head` of a projection row (+ bias): the new token's v
+template <typename T>
+__device__ __forceinline__ uint4 plain_chunk(const AttnParams& p, const T* src, int head, int ch, int D) {
+  using V = Vec<T>;
+  const uint4 raw = reinterpret_cast<const uint4*>(src + (size_t)head * D)[ch];
+  if (p.qkv_bias == nullptr) return raw;
+  float x[8], bx[8];
+  V::to_float(raw, x);
+  V::to_float(reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.qkv_bias) + (size_t)head * D)[ch], bx);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) x[j] += bx[j];
+  return V::from_float(x);
+}
+
 constexpr int kStages = 3;                    // KV pages in flight per warp
 template <int D>
 constexpr int kPageElems = kBS * D;           // one K (or V) page: 16 x D
@@ -134,8 +182,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     for (int i = 0; i < kWarps * kStages; ++i) mbar_init(&bars[i], 1);
     fence_barrier_init();
   }
-  pdl_wait_then_trigger();  // the next kernel (the o_proj GEMM) may start streaming its weights
-  // the split's page-table entries do not depend on the sequence length: they are requested together
+  // The block table and the sequence lengths were written before the previous kernel of the stream
+  // started (the step's last kernel, or the host), and every KV page except the one holding the new
+  // token is unchanged by the previous kernel (RoPE + KV append, or the QKV GEMM with that epilogue):
+  // they are read, and those pages requested, before the dependency wait, so the KV stream overlaps the
+  // previous kernel. The page of the new token and the query wait for it.
+  // The split's page-table entries do not depend on the sequence length: they are requested together
   // with it (entries past the sequence are never used)
   const int pg0 = split * p.pages_per_split;
   const int pg_cap = min(p.pages_per_split, p.max_blocks_per_seq - pg0);
@@ -164,14 +216,33 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
       tma_load_2d(dv + h * kBS * 64, &args.tv, &mybar[st], 64 * h, row);
     }
   };
+  // Without the fused append, the page holding the new token is written by the previous kernel and is
+  // requested after the dependency wait; with it, its cache row is stale until this kernel writes it,
+  // and the warp that owns the page patches the row in shared memory once the page has landed.
+  const bool rope = p.qkv != nullptr;
+  const int last_pg = npages - 1;
 #pragma unroll
-  for (int i = 0; i < kStages; ++i) issue(i);
-  // the query tile is staged while the first pages are in flight
-  const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G) * kD;
+  for (int i = 0; i < kStages; ++i)
+    if (rope || pg0 + warp + i * kWarps != last_pg) issue(i);
+  pdl_wait_then_trigger();  // the next kernel (the o_proj GEMM) may start streaming its weights
+  if (!rope) {
+#pragma unroll
+    for (int i = 0; i < kStages; ++i)
+      if (pg0 + warp + i * kWarps == last_pg) issue(i);
+  }
+  // the query tile is staged while the first pages are in flight (rotated here in the fused form)
+  const int qkv_stride = (p.nq + 2 * p.nkv) * kD;
+  const int pos = rope ? p.positions[b] : 0;
   for (int c = threadIdx.x; c < kRows * CH; c += blockDim.x) {
     const int r = c / CH, ch = c % CH;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < G) v = reinterpret_cast<const uint4*>(q + (size_t)r * kD)[ch];
+    if (r < G) {
+      if (rope)
+        v = rope_chunk<T, D>(p, reinterpret_cast<const T*>(p.qkv) + (size_t)b * qkv_stride, kvh * G + r, ch, pos);
+      else
+        v = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G + r) *
+                                           kD)[ch];
+    }
     *reinterpret_cast<uint4*>(sQ + swz<D>(r, ch)) = v;
   }
   __syncthreads();
@@ -199,6 +270,21 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     }
     const T* sK = myKV + (size_t)st * 2 * PE;
     const T* sV = sK + PE;
+    if (rope && pg == pos / kBS) {
+      // the new token's row: k rotated, v (+ bias) from the projection, into the landed page and the cache
+      const T* src = reinterpret_cast<const T*>(p.qkv) + (size_t)b * qkv_stride;
+      const int r = pos % kBS, blk = s_pages[pg - pg0];
+      for (int c = lane; c < 2 * CH; c += 32) {
+        const bool is_k = c < CH;
+        const int ch = is_k ? c : c - CH;
+        const uint4 v = is_k ? rope_chunk<T, D>(p, src, p.nq + kvh, ch, pos)
+                             : plain_chunk<T>(p, src, p.nq + p.nkv + kvh, ch, kD);
+        *reinterpret_cast<uint4*>(const_cast<T*>(is_k ? sK : sV) + swzp(r, ch)) = v;
+        T* cache = reinterpret_cast<T*>(const_cast<void*>(is_k ? p.k_cache : p.v_cache));  // the append writes the caches
+        reinterpret_cast<uint4*>(cache + (((size_t)blk * p.nkv + kvh) * kBS + r) * kD)[ch] = v;
+      }
+      __syncwarp();
+    }
     float s[2][4];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
@@ -476,6 +562,7 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s) {
       p.nq / p.nkv > kRows || p.splits <= 0 || p.pages_per_split <= 0 || p.pages_per_split > kMaxPagesPerSplit ||
       p.batch <= 0 || (p.dtype != kBF16 && p.dtype != kF16))
     return cudaErrorInvalidValue;
+  if (p.qkv != nullptr && (p.positions == nullptr || p.cos_t == nullptr || p.sin_t == nullptr)) return cudaErrorInvalidValue;
   return p.head_dim == 128 ? launch_attention<128>(p, s) : launch_attention<64>(p, s);
 }
 

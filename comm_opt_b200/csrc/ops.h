@@ -51,6 +51,15 @@ struct AttnParams {
   int num_blocks;            // rows of the caches / (nkv * block); 0 = unknown
   int* err;                  // optional: set to 1 if a bounded wait gave up
   int cluster;               // 1: merge splits (<= 8) inside a thread-block cluster, no scratch used
+  // Optional RoPE + KV append of the new token (qkv != nullptr; q is then not read): the query heads of
+  // each KV group and the new token's k / v head come from the QKV projection output, the bias (if any)
+  // is added, RoPE is applied at positions[b], and the new k / v row is written into the caches at
+  // positions[b] and used for the newest token (one kernel instead of the append kernel + attention).
+  const void* qkv;           // [B, (nq + 2 nkv) * D]
+  const void* qkv_bias;      // [(nq + 2 nkv) * D] or nullptr
+  const int32_t* positions;  // [B]: position of the new token (= seq_lens[b] - 1)
+  const float* cos_t;        // [max_pos, D / 2]
+  const float* sin_t;
 };
 // bytes of scratch needed for a given geometry
 size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_dim);

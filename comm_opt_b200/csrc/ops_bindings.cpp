@@ -142,7 +142,9 @@ int64_t py_attn_scratch_bytes(int64_t batch, int64_t nkv, int64_t splits, int64_
 // first call (the kernel leaves it zero).
 void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                          torch::Tensor seq_lens, torch::Tensor out, torch::Tensor scratch, int64_t splits,
-                         int64_t pages_per_split, double scale, bool cluster) {
+                         int64_t pages_per_split, double scale, bool cluster, c10::optional<torch::Tensor> qkv,
+                         c10::optional<torch::Tensor> qkv_bias, c10::optional<torch::Tensor> positions,
+                         c10::optional<torch::Tensor> cos_t, c10::optional<torch::Tensor> sin_t) {
   for (auto* t : {&q, &k_cache, &v_cache, &block_tables, &seq_lens, &out, &scratch}) dense(*t, "arg");
   COB_CHECK(block_tables.scalar_type() == torch::kInt32 && seq_lens.scalar_type() == torch::kInt32,
               "block_tables and seq_lens must be int32");
@@ -175,6 +177,26 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
   p.num_blocks = (int)k_cache.size(0);
   p.err = nullptr;
   p.cluster = cluster ? 1 : 0;
+  if (qkv.has_value()) {  // RoPE + KV append of the new token inside the attention kernel
+    COB_CHECK(positions.has_value() && cos_t.has_value() && sin_t.has_value(), "fused append needs positions, cos, sin");
+    for (auto* t : {&*qkv, &*positions, &*cos_t, &*sin_t}) dense(*t, "fused append operand");
+    COB_CHECK(qkv->scalar_type() == q.scalar_type() && qkv->dim() == 2 && qkv->size(0) == p.batch &&
+                  qkv->size(1) == (int64_t)(p.nq + 2 * p.nkv) * p.head_dim,
+              "qkv must be [batch, (nq + 2 nkv) * head_dim] of the query dtype");
+    COB_CHECK(positions->scalar_type() == torch::kInt32 && positions->numel() >= p.batch, "positions: int32 [batch]");
+    COB_CHECK(cos_t->scalar_type() == torch::kFloat && sin_t->scalar_type() == torch::kFloat &&
+                  cos_t->size(-1) == p.head_dim / 2 && sin_t->size(-1) == p.head_dim / 2,
+              "cos / sin: float32 [max_pos, head_dim / 2]");
+    p.qkv = qkv->data_ptr();
+    p.positions = positions->data_ptr<int32_t>();
+    p.cos_t = cos_t->data_ptr<float>();
+    p.sin_t = sin_t->data_ptr<float>();
+    if (qkv_bias.has_value()) {
+      dense(*qkv_bias, "qkv_bias");
+      COB_CHECK(qkv_bias->scalar_type() == q.scalar_type() && qkv_bias->numel() == qkv->size(1), "qkv_bias size");
+      p.qkv_bias = qkv_bias->data_ptr();
+    }
+  }
   const c10::cuda::CUDAGuard g(q.device());
   ok(cob::paged_decode_attention(p, cur()), "paged_decode_attention");
 }
@@ -358,5 +380,10 @@ void register_ops(pybind11::module& m) {
   m.def("set_l2_prefetch", [](int64_t tiles) { cob::l2_prefetch_tiles() = (int)std::max<int64_t>(0, tiles); });
   m.def("get_l2_prefetch", []() { return (int64_t)cob::l2_prefetch_tiles(); });
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);
-  m.def("decode_attention", &py_decode_attention);
+  m.def("decode_attention", &py_decode_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
+        pybind11::arg("v_cache"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"), pybind11::arg("out"),
+        pybind11::arg("scratch"), pybind11::arg("splits"), pybind11::arg("pages_per_split"), pybind11::arg("scale"),
+        pybind11::arg("cluster"), pybind11::arg("qkv") = pybind11::none(), pybind11::arg("qkv_bias") = pybind11::none(),
+        pybind11::arg("positions") = pybind11::none(), pybind11::arg("cos") = pybind11::none(),
+        pybind11::arg("sin") = pybind11::none());
 }

@@ -34,11 +34,8 @@ from ..parallel import TPCommunicator
 from ..utils.results import RunDir, gpu_state
 from ..utils.stats import summary
 
-DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,ours:nvls_2s,"
-                 "nccl_norm,vllm_car,trt_oneshot,trt_twoshot")
-# variants that have not run on a GPU yet join the default list only on request
-if os.environ.get("COB_EXPERIMENTAL") == "1":
-    DEFAULT_IMPLS = DEFAULT_IMPLS.replace("ours:lamport_1s,", "ours:lamport_1s,ours:lamport_1sx,", 1)
+DEFAULT_IMPLS = ("ours:auto,ours:lamport_1s,ours:lamport_1sx,ours:lamport_2s,ours:pull_1s,ours:pull_2s,ours:nvls_1s,"
+                 "ours:nvls_2s,nccl_norm,vllm_car,trt_oneshot,trt_twoshot")
 
 
 def warm_gpu(seconds: float, dev):

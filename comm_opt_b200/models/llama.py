@@ -223,7 +223,7 @@ class TPDecodeRunner:
     def __init__(self, cfg: LlamaConfig, weights: LlamaWeights, comm: TPCommunicator, max_batch: int, max_seq: int,
                  device, gemm: str = "cob", nccl_group=None, pdl: bool = True, fuse_boundary: bool = False,
                  fuse_epilogues: bool = False, collective: str = "ours", tune_boundaries: bool = True,
-                 car_group=None, l2_prefetch: int = 0, pack_weights: bool = True):
+                 car_group=None, l2_prefetch: int = 0, pack_weights: bool = True, fuse_append: bool = True):
         self.cfg, self.w, self.comm, self.device = cfg, weights, comm, torch.device(device)
         self.tp, self.rank = comm.world, comm.rank
         self.s = cfg.shard(self.tp)
@@ -234,6 +234,8 @@ class TPDecodeRunner:
         self.cos, self.sin = rope_tables(max_seq, cfg.head_dim, cfg.rope_theta, self.device)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.gemm = gemm
+        # RoPE + KV append of the new token inside the attention kernel (one kernel less per layer)
+        self.fuse_append = bool(fuse_append)
         # packed weights (this package's GEMMs only): every projection matrix is converted in place, once,
         # into the bulk-load block layout (models.gemm.PackedWeight); the prefill unpacks one matrix at a time
         self.packed = bool(pack_weights and gemm == "cob")
@@ -387,9 +389,7 @@ class TPDecodeRunner:
         h = buf["h"]
         for i, L in enumerate(w.layers):
             self.lin[(i, "qkv")](h, out=buf["qkv"])
-            K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
-                             self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
-            buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
+            n += self._attention(i, L, B, buf, bt)
             self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
             h = self._allreduce_add_rmsnorm(buf, L.ln2)
             self.lin[(i, "gu")](h, out=buf["gu"])
@@ -397,7 +397,7 @@ class TPDecodeRunner:
             self.lin[(i, "down")](buf["act"], out=buf["part"])
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
             h = self._allreduce_add_rmsnorm(buf, nxt)
-            n += 3 + 2 * ar_ours + 4 * ours
+            n += 1 + 2 * ar_ours + 4 * ours
         self.lin["head"](h, out=buf["logits"])
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         n += 1 + ours
@@ -444,6 +444,19 @@ class TPDecodeRunner:
             self._fuse_epi[B] = (sw, rp)
         return self._fuse_epi[B]
 
+    def _attention(self, i: int, L, B: int, buf: dict, bt: torch.Tensor) -> int:
+        """RoPE + paged-KV append of the new token and the attention of layer i from buf["qkv"]; one kernel
+        with `fuse_append` (the attention kernel rotates and appends), else two. Returns the kernel count."""
+        s = self.s
+        if self.fuse_append:
+            buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale,
+                           append=dict(qkv=buf["qkv"], positions=buf["pos"], cos=self.cos, sin=self.sin, bias=L.bqkv))
+            return 1
+        K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
+                         self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
+        buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
+        return 2
+
     def fused_epilogues_used(self, B: int) -> tuple[bool, bool]:
         """(SiLU in gate_up, RoPE + KV append in QKV) as the captured step for batch B runs them."""
         if not self.fuse_boundary or B not in self._fuse_epi:
@@ -470,11 +483,10 @@ class TPDecodeRunner:
         n += 1
         for i, L in enumerate(w.layers):
             if i == 0 or not rp:
-                K.rope_append_kv(buf["qkv"], buf["pos"], self.cos, self.sin, bt, buf["q"], self.cache.k[i],
-                                 self.cache.v[i], s["nq"], s["nkv"], bias=L.bqkv)
+                n += self._attention(i, L, B, buf, bt)
+            else:  # the previous consumer GEMM's epilogue rotated q and appended k / v
+                buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
                 n += 1
-            buf["attn_op"](buf["q"], self.cache.k[i], self.cache.v[i], bt, buf["lens"], buf["attn"], self.scale)
-            n += 1
             # attention-output boundary
             if fa:
                 comm.gemm_push(buf["attn"].view(B, -1), L.wo)

@@ -104,7 +104,12 @@ class DecodeAttention:
         nbytes = native().attn_scratch_bytes(batch, nkv, self.splits, nq // nkv, head_dim)
         self.scratch = torch.zeros(nbytes, dtype=torch.uint8, device=device)
 
-    def __call__(self, q, k_cache, v_cache, block_tables, seq_lens, out, scale: float):
+    def __call__(self, q, k_cache, v_cache, block_tables, seq_lens, out, scale: float, append: dict | None = None):
+        """`append` (keys qkv, positions, cos, sin, optional bias): RoPE + KV append of the new token in the
+        same kernel - the query and the new k / v head come from the QKV projection output `qkv`
+        [B, (nq + 2 nkv) * D], the new k / v are written into the caches at `positions` (`q` is not read)."""
+        a = append or {}
         native().decode_attention(q, k_cache, v_cache, block_tables, seq_lens, out, self.scratch, self.splits,
-                                  self.pps, float(scale), self.cluster)
+                                  self.pps, float(scale), self.cluster, qkv=a.get("qkv"), qkv_bias=a.get("bias"),
+                                  positions=a.get("positions"), cos=a.get("cos"), sin=a.get("sin"))
         return out

@@ -1,6 +1,5 @@
 """Numerics of the single-GPU decode kernels against plain PyTorch fp32 references."""
 import math
-import os
 
 import pytest
 import torch
@@ -94,8 +93,6 @@ def test_decode_attention(cuda, nq, nkv, dtype):
     check_decode_attention(cuda, nq, nkv, dtype, 128)
 
 
-@pytest.mark.skipif(os.environ.get("COB_EXPERIMENTAL") != "1",
-                    reason="head_dim 64 has not run on a GPU yet; COB_EXPERIMENTAL=1 runs it")
 @pytest.mark.parametrize("nq,nkv", [(4, 1), (32, 4)])
 def test_decode_attention_head_dim_64(cuda, nq, nkv):
     """TinyLlama-1.1B heads (head_dim 64, 8 query heads per KV head; 4 per rank at TP=8)."""
@@ -132,3 +129,41 @@ def check_decode_attention(cuda, nq, nkv, dtype, D):
         attn(q, kc, vc, bt, seq, out, scale)
         torch.cuda.synchronize()
         assert rel_err(out, ref) <= 2 ** -7, (splits, rel_err(out, ref))
+
+
+@pytest.mark.parametrize("nq,nkv,bias,D", [(8, 1, False, 128), (32, 8, False, 128), (5, 1, True, 128),
+                                           (20, 4, True, 128), (4, 1, False, 64)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_attention_with_fused_append(cuda, nq, nkv, bias, D, dtype):
+    """RoPE + KV append of the new token inside the attention kernel equals the append kernel followed by
+    the attention: same output (fp32 oracle too) and the same cache rows, for the global merge, the
+    cluster merge and a single split, with the new token at the start, middle and end of a page."""
+    B, bs, maxb = 6, 16, 40
+    seq = torch.tensor([1, 16, 17, 33, 300, 640], device=cuda, dtype=torch.int32)
+    pos = seq - 1
+    g = torch.Generator(device=cuda).manual_seed(nq * 3 + D)
+    nblocks = B * maxb
+    kc0 = torch.randn(nblocks, nkv, bs, D, device=cuda, generator=g).to(dtype)
+    vc0 = torch.randn(nblocks, nkv, bs, D, device=cuda, generator=g).to(dtype)
+    bt = torch.randperm(nblocks, device=cuda).to(torch.int32).view(B, maxb)
+    qkv = torch.randn(B, (nq + 2 * nkv) * D, device=cuda, generator=g).to(dtype)
+    b_qkv = torch.randn((nq + 2 * nkv) * D, device=cuda, generator=g).to(dtype) if bias else None
+    cos, sin = rope_tables(maxb * bs, D, 500000.0, cuda)
+    scale = 1 / math.sqrt(D)
+    # reference path: the append kernel, then the attention
+    kc1, vc1 = kc0.clone(), vc0.clone()
+    q = torch.empty(B, nq, D, device=cuda, dtype=dtype)
+    K.rope_append_kv(qkv, pos, cos, sin, bt, q, kc1, vc1, nq, nkv, bias=b_qkv)
+    ref = paged_attention_ref(q, kc1, vc1, bt, seq, scale)
+    for num_sms in (148, 8, 1):
+        base = K.DecodeAttention(B, nq, nkv, D, maxb, cuda, num_sms=num_sms)
+        want = torch.empty_like(q)
+        base(q, kc1, vc1, bt, seq, want, scale)
+        kc2, vc2 = kc0.clone(), vc0.clone()
+        got = torch.full_like(q, float("nan"))
+        base(torch.empty_like(q), kc2, vc2, bt, seq, got, scale,
+             append=dict(qkv=qkv, positions=pos, cos=cos, sin=sin, bias=b_qkv))
+        torch.cuda.synchronize()
+        assert rel_err(got, want) <= 2 ** -7, (num_sms, rel_err(got, want))
+        assert rel_err(got, ref) <= 2 ** -7
+        assert rel_err(kc2, kc1) <= 2 ** -7 and rel_err(vc2, vc1) <= 2 ** -7

@@ -82,8 +82,6 @@ def test_gemm_tuner_picks_valid_config(cuda):
     assert rel_err(lin(x), x.float() @ w.float().t()) <= 2 ** -7
 
 
-@pytest.mark.skipif(__import__("os").environ.get("COB_EXPERIMENTAL") != "1",
-                    reason="L2 prefetch has not run on a GPU yet; COB_EXPERIMENTAL=1 runs it")
 @pytest.mark.parametrize("tiles", [4, 16, 64])
 def test_gemm_l2_prefetch_same_bits(cuda, tiles):
     """Prefetching weight tiles into L2 is only a hint: stream-K and cluster split-K results are bitwise

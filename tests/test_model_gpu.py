@@ -1,5 +1,4 @@
 """Llama-shaped decode runner (world 1) against an unsharded fp32 PyTorch forward."""
-import os
 from dataclasses import replace
 
 import pytest
@@ -46,12 +45,8 @@ def _ref_logits(cfg, full, tokens, device):
     return h @ full["lm_head"].to(device).float().t()
 
 
-# head_dim 64 attention has not run on a GPU yet: that case runs only with COB_EXPERIMENTAL=1
-_hd64 = pytest.mark.skipif(os.environ.get("COB_EXPERIMENTAL") != "1", reason="not yet run on a GPU")
-
-
 @pytest.mark.parametrize("gemm_impl,model", [("cob", "tiny"), ("torch", "tiny"), ("cob", "tiny-qkv-bias"),
-                                             pytest.param("cob", "tiny-hd64", marks=_hd64)])
+                                             ("cob", "tiny-hd64")])
 def test_decode_logits_match_reference(cuda, gemm_impl, model):
     """Decode logits against the fp32 forward; `tiny-qkv-bias` has the Qwen2.5 attention shape (QKV bias,
     5 query heads per KV head)."""

@@ -249,6 +249,7 @@ def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
     r.scale = 1.0
     r.fuse_boundary, r.fuse_kinds, r.fuse_epilogues = fuse, {4: kinds}, any(epi)
     r._fuse_epi, r._wgu_il, r.epi_use = {4: epi}, [None] * layers, {}
+    r.fuse_append = False
     buf = {k: torch.zeros(4, 8) for k in ("ids", "pos", "lens", "res", "h", "part", "qkv", "q", "attn", "gu", "act",
                                            "logits")}
     buf["keys"] = torch.zeros(4, dtype=torch.int64)
@@ -257,7 +258,13 @@ def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
     return r, buf, calls
 
 
-def _expected_step(layers, fuse, kinds, epi):
+def _expected_step(layers, fuse, kinds, epi, append=False):
+    seq = _expected_step_kernels(layers, fuse, kinds, epi)
+    # the fused append folds every RoPE + KV append kernel into the attention kernel that follows it
+    return [k for k in seq if k != "rope_append_kv"] if append else seq
+
+
+def _expected_step_kernels(layers, fuse, kinds, epi):
     fa, fm = kinds if fuse else (False, False)
     sw, rp = (epi[0] and fa, epi[1] and fm) if fuse else (False, False)
     seq = ["embedding", "rmsnorm", "gemm"]
@@ -290,10 +297,12 @@ def test_decode_step_composition_every_boundary_mix(monkeypatch):
     for fuse in (True, False):
         for kinds in itertools.product((True, False), repeat=2):
             for epi in itertools.product((False, True), repeat=2):
-                r, buf, calls = _recording_runner(monkeypatch, 3, 2, fuse, kinds, epi)
-                n = r._step(4, buf)
-                assert calls == _expected_step(3, fuse, kinds, epi), (fuse, kinds, epi)
-                assert n == len(calls), (fuse, kinds, epi, n, len(calls))
+                for append in (False, True):
+                    r, buf, calls = _recording_runner(monkeypatch, 3, 2, fuse, kinds, epi)
+                    r.fuse_append = append
+                    n = r._step(4, buf)
+                    assert calls == _expected_step(3, fuse, kinds, epi, append), (fuse, kinds, epi, append)
+                    assert n == len(calls), (fuse, kinds, epi, append, n, len(calls))
 
 
 def test_decode_step_composition_vllm_stack(monkeypatch):
