@@ -296,6 +296,36 @@ __device__ __forceinline__ void tile_to_smem(const FusedGemmParams& p, uint8_t* 
   tc_fence_before();
 }
 
+// Cluster barrier halves (non-aligned forms: lanes of a warp may reach them at different points).
+__device__ __forceinline__ void cl_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory"); }
+__device__ __forceinline__ void cl_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
+
+// gemm_push with a small batch tile (BN * BM floats fit the per-item area `c.q`, unused by this kernel):
+// accumulator row `row` (one output feature) goes straight from TMEM to the CTA of the cluster that
+// pushes that feature - owner o = row / per - as red_o[r][b][row - o * per] (distributed shared memory
+// stores), so the cluster needs one barrier and no remote loads before the owners sum and push.
+template <int BN, bool SMALL>
+__device__ __forceinline__ void tile_to_owners(const FusedGemmParams& p, const Ctrl& c, uint32_t tmem, int M) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, row = q * 32 + lane;
+  const int cs = gridDim.y, r = blockIdx.y, per = BM / cs, o = row / per;
+  if (!mbar_wait(&c.tfull[0], 0, p.timeout_ns)) *c.fail = 1;
+  __syncwarp();
+  tc_fence_after();
+  cl_wait();  // every CTA of the cluster has started: its shared memory may be written
+  float* dst = cg::this_cluster().map_shared_rank(c.q, o) + (size_t)r * BN * per + (row - o * per);
+  const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+  const int mcols = min(M, BN);
+  for (int c0 = 0; c0 < mcols; c0 += 16) {
+    float v[16];
+    tmem_ld16(taddr + c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < mcols) dst[(size_t)(c0 + j) * per] = v[j];
+  }
+  tc_fence_before();
+}
+
 // Sum of this CTA's feature share [f0, f0 + 8) of batch row b over the cs CTAs of the cluster.
 __device__ __forceinline__ void cluster_sum8(float* part, int cs, int b, int f, float (&acc)[8]) {
 #pragma unroll
@@ -384,15 +414,27 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   const int KT = p.K / BK;
   const int k0 = r * p.kps, nsteps = min(KT, k0 + p.kps) - k0;
   const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, p.wp != nullptr ? nullptr : &tmW, &tmX);
+  // small batch tile: partial rows are pushed to their owner CTA (one cluster barrier); else every CTA
+  // keeps its tile and the owners read the peers' tiles (two barriers)
+  constexpr bool kPushRed = BN * BM <= kQCap;
+  const bool push_red = kPushRed && cs > 1;
+  if (push_red) cl_arrive_relaxed();  // first half of a start-up barrier, waited for before the first push
 
   mainloop<BN, SMALL, false>(p, &tmW, &tmX, smem, c, tmem, k0, nsteps, (p.emulate ? rank * p.N : 0) + t * BM, 0, 1,
                              p.emulate ? rank * p.M : 0, nullptr, 0, 0u, (p.emulate ? rank : 0) * p.w_tiles + t);
-  if (threadIdx.x >= 64) tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
+  if (threadIdx.x >= 64) {
+    if (push_red)
+      tile_to_owners<BN, SMALL>(p, c, tmem, p.M);
+    else
+      tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
+  } else if (push_red) {
+    cl_wait();  // warps 0 and 1: second half of the start-up barrier
+  }
   pdl_wait();  // every thread: the epoch below was written by an earlier kernel of the stream
   const uint64_t e = fg_epoch(p, rank);
   const int slot = (int)(e & 1);
   __syncthreads();
-  if (cs > 1) cg::this_cluster().sync();
+  if (cs > 1) cg::this_cluster().sync();  // release / acquire: partial tiles (or pushed rows) complete
   // this CTA pushes features [f0, f0 + per) of the tile for every batch row, 8 per 16-byte vector
   const int per = BM / cs, f0 = r * per, groups = per / 8;
   if (!*c.fail) {
@@ -402,7 +444,25 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
       const int n = t * BM + f;
       if (n >= p.N) continue;
       float acc[8];
-      cluster_sum8(part, cs, b, f, acc);
+      if (push_red) {  // sources in cluster order from the local area: the sums of cluster_sum8
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        for (int cc = 0; cc < cs; ++cc) {
+          const float* src = c.q + ((size_t)cc * BN + b) * per + (f - f0);
+          const float4 u = *reinterpret_cast<const float4*>(src);
+          const float4 w = *reinterpret_cast<const float4*>(src + 4);
+          acc[0] += u.x;
+          acc[1] += u.y;
+          acc[2] += u.z;
+          acc[3] += u.w;
+          acc[4] += w.x;
+          acc[5] += w.y;
+          acc[6] += w.z;
+          acc[7] += w.w;
+        }
+      } else {
+        cluster_sum8(part, cs, b, f, acc);
+      }
       const uint4 d = LP::clean(pack_bf16x8(acc));
       for (int i = 0; i < p.world; ++i) {
         const int q = (rank + i) % p.world;  // start with the own heap, then peers in ring order
@@ -410,7 +470,8 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
       }
     }
   }
-  if (cs > 1) cg::this_cluster().sync();  // keep this CTA's tile alive until the cluster has read it
+  // the two-barrier form keeps this CTA's tile alive until the cluster has read it
+  if (cs > 1 && !push_red) cg::this_cluster().sync();
   teardown<BN, SMALL>(p, c, tmem, rank);
 }
 
