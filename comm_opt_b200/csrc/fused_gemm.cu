@@ -67,7 +67,10 @@ struct FCfg {
   static constexpr int RING = STAGES * STAGE;
   static constexpr int PIPE = RING > PART ? RING : PART;
   static constexpr int CTRL = 1024 + BN * 8;  // barriers, flags, per-row sums / rstd
-  static constexpr int SMEM = PIPE + 1024 + CTRL + kQCap * 4;
+  // batch tile 16: area into which the cluster's CTAs push partial rows and row sums of squares (the
+  // consumer's one-barrier reduction; outside the ring, the piece buffers and `q`)
+  static constexpr int RED = BN == 16 ? (BN * BM + 16 * BN) * 4 : 0;
+  static constexpr int SMEM = PIPE + 1024 + CTRL + kQCap * 4 + RED;
   static constexpr int TC = BN < 32 ? 32 : BN;  // TMEM columns per accumulator (two are allocated)
   // SMALL: two CTAs per SM (228 KB per SM, 1 KB reserved per CTA)
   static_assert(!SMALL || SMEM <= 113 * 1024, "two CTAs per SM");
@@ -86,6 +89,8 @@ struct Ctrl {
   float* ss;     // [BN] this split's per-row sum of squares (ar_norm_gemm)
   float* rstd;   // [BN]
   float* q;      // [kQCap] per-item sums of squares (ar_norm_gemm)
+  float* red;    // batch tile 16: [cs][BN][BM / cs] partial rows pushed by the cluster (ar_norm_gemm)
+  float* red_ss; // batch tile 16: [cs][BN] per-split row sums of squares pushed by the cluster
 };
 
 template <int BN, bool SMALL>
@@ -104,6 +109,8 @@ __device__ __forceinline__ Ctrl carve(uint8_t* smem) {
   c.ss = reinterpret_cast<float*>(ctrl + 1024);
   c.rstd = c.ss + BN;
   c.q = reinterpret_cast<float*>(ctrl + C::CTRL);
+  c.red = c.q + kQCap;
+  c.red_ss = c.red + BN * BM;
   return c;
 }
 
@@ -326,6 +333,59 @@ __device__ __forceinline__ void tile_to_owners(const FusedGemmParams& p, const C
   tc_fence_before();
 }
 
+// ar_norm_gemm with a batch tile of 16: accumulator row `row` to the CTA that finishes it - plain
+// epilogue: owner row / (BM / cs); paired epilogue (rows f and 64 + f together): owner (row % 64) / ph,
+// the low half at [0, ph) and the high half at [ph, 2 ph) of the owner's per-source slice.
+template <int BN, bool SMALL>
+__device__ __forceinline__ void consumer_tile_to_owners(const FusedGemmParams& p, const Ctrl& c, uint32_t tmem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = warp & 3, row = q * 32 + lane;
+  const int cs = gridDim.y, r = blockIdx.y, per = BM / cs;
+  int o, lf;
+  if (p.epi == kEpiPlain) {
+    o = row / per;
+    lf = row - o * per;
+  } else {
+    const int ph = (BM / 2) / cs, f = row % (BM / 2);
+    o = f / ph;
+    lf = (row < BM / 2 ? 0 : ph) + f - o * ph;
+  }
+  if (!mbar_wait(&c.tfull[0], 0, p.timeout_ns)) *c.fail = 1;
+  __syncwarp();
+  tc_fence_after();
+  float* dst = cg::this_cluster().map_shared_rank(c.red, o) + (size_t)r * BN * per + lf;
+  const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+  const int mcols = min(p.M, BN);
+  for (int c0 = 0; c0 < mcols; c0 += 16) {
+    float v[16];
+    tmem_ld16(taddr + c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (c0 + j < mcols) dst[(size_t)(c0 + j) * per] = v[j];
+  }
+  tc_fence_before();
+}
+
+// Sum over the cluster's sources of 8 pushed values at owner-local index `lf` of batch row b.
+template <int BN>
+__device__ __forceinline__ void red_sum8(const float* red, int cs, int per, int b, int lf, float (&acc)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  for (int cc = 0; cc < cs; ++cc) {
+    const float* src = red + ((size_t)cc * BN + b) * per + lf;
+    const float4 u = *reinterpret_cast<const float4*>(src);
+    const float4 w = *reinterpret_cast<const float4*>(src + 4);
+    acc[0] += u.x;
+    acc[1] += u.y;
+    acc[2] += u.z;
+    acc[3] += u.w;
+    acc[4] += w.x;
+    acc[5] += w.y;
+    acc[6] += w.z;
+    acc[7] += w.w;
+  }
+}
+
 // Sum of this CTA's feature share [f0, f0 + 8) of batch row b over the cs CTAs of the cluster.
 __device__ __forceinline__ void cluster_sum8(float* part, int cs, int b, int f, float (&acc)[8]) {
 #pragma unroll
@@ -498,6 +558,11 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
   uint32_t* flags = p.flags + (size_t)wsr * kMaxPieces;
   float* pss = p.pss + (size_t)wsr * kMaxPieces * p.act_rows;
   const uint32_t tmem = setup<BN, SMALL>(smem, c, 1, p.wp != nullptr ? nullptr : &tmW, &tmA);
+  // batch tile 16: the split-K partial rows and row sums of squares are pushed to the CTA that finishes
+  // them (one cluster barrier, no remote loads); the first half of a start-up barrier here, its second
+  // half before the first push
+  const bool push_red = BN == 16 && cs > 1;
+  if (push_red) cl_arrive_relaxed();
   // The weight stream needs nothing from earlier kernels and starts at once (warp 0). The pieces
   // (warps 2-5) first wait, in hardware, for the preceding kernel - this rank's gemm_push - to
   // complete, so on this GPU nothing spins on a kernel that runs concurrently; the polls that
@@ -594,6 +659,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
     // this split's per-row sum of squares over its pieces: lanes stride the pieces, warp tree
     const int warp = (threadIdx.x >> 5) - 2, lane = threadIdx.x & 31;
     if (!wait_flags(flags + (size_t)r * tiles, tiles, tag, p.timeout_ns, c.fail)) *c.fail = 1;
+    if (push_red) cl_wait();  // every CTA of the cluster has started: its shared memory may be written
     for (int b = warp; b < p.M; b += 4) {
       float s = 0.f;
       for (int j = lane; j < tiles; j += 32) s += __ldcg(pss + (size_t)(r * tiles + j) * p.act_rows + b);
@@ -602,6 +668,7 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
         c.ss[b] = s;
         c.rstd[b] = rsqrtf(s / (float)p.K + p.eps);  // final when splits == 1
       }
+      if (push_red && lane < cs) cg::this_cluster().map_shared_rank(c.red_ss, lane)[r * BN + b] = s;
     }
     if (cs == 1) {
       // several tiles per CTA: accumulator -> registers -> scaled bf16 stores, row-major Y
@@ -629,17 +696,21 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
         __syncwarp();
         if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&c.tempty[acc])) : "memory");
       }
+    } else if (push_red) {
+      consumer_tile_to_owners<BN, SMALL>(p, c, tmem);
     } else {
       tile_to_smem<BN, SMALL>(p, smem, c, tmem, p.M);
     }
+  } else if (push_red) {
+    cl_wait();  // warps 0 and 1: second half of the start-up barrier
   }
   __syncthreads();
   cg::cluster_group cluster = cg::this_cluster();
   if (cs > 1) {
-    cluster.sync();
+    cluster.sync();  // release / acquire: partial tiles and row sums complete (pushed, or readable)
     for (int b = threadIdx.x; b < p.M; b += kThreads) {
       float s = 0.f;
-      for (int cc = 0; cc < cs; ++cc) s += *cluster.map_shared_rank(c.ss + b, cc);
+      for (int cc = 0; cc < cs; ++cc) s += push_red ? c.red_ss[cc * BN + b] : *cluster.map_shared_rank(c.ss + b, cc);
       c.rstd[b] = rsqrtf(s / (float)p.K + p.eps);
     }
     __syncthreads();
@@ -651,8 +722,13 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
     for (int idx = threadIdx.x; idx < p.M * hgroups; idx += kThreads) {
       const int b = idx / hgroups, f = r * ph + (idx % hgroups) * 8;
       float lo[8], hi[8];
-      cluster_sum8(part, cs, b, f, lo);
-      cluster_sum8(part, cs, b, BM / 2 + f, hi);
+      if (push_red) {
+        red_sum8<BN>(c.red, cs, BM / cs, b, f - r * ph, lo);
+        red_sum8<BN>(c.red, cs, BM / cs, b, ph + f - r * ph, hi);
+      } else {
+        cluster_sum8(part, cs, b, f, lo);
+        cluster_sum8(part, cs, b, BM / 2 + f, hi);
+      }
       const float rs = c.rstd[b];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {  // the values a plain epilogue would have stored (bf16)
@@ -706,14 +782,18 @@ __global__ void __launch_bounds__(kThreads, SMALL ? 2 : 1)
       const int n = t * BM + f;
       if (n >= p.N) continue;
       float acc[8];
-      cluster_sum8(part, cs, b, f, acc);
+      if (push_red)
+        red_sum8<BN>(c.red, cs, per, b, f - f0, acc);
+      else
+        cluster_sum8(part, cs, b, f, acc);
       const float rs = c.rstd[b];
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] *= rs;
       *reinterpret_cast<uint4*>(Y + (size_t)b * p.N + n) = pack_bf16x8(acc);
     }
   }
-  if (cs > 1) cluster.sync();
+  // the two-barrier form keeps this CTA's tile and row sums alive until the cluster has read them
+  if (cs > 1 && !push_red) cluster.sync();
   // publish the epoch for the next call (same rule as the fused all-reduce kernels)
   const int G = tiles * cs;
   RankState* st = fg_state(p, rank);
