@@ -187,15 +187,16 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   // token is unchanged by the previous kernel (RoPE + KV append, or the QKV GEMM with that epilogue):
   // they are read, and those pages requested, before the dependency wait, so the KV stream overlaps the
   // previous kernel. The page of the new token and the query wait for it.
-  // The split's page-table entries do not depend on the sequence length: they are requested together
-  // with it (entries past the sequence are never used)
-  const int pg0 = split * p.pages_per_split;
-  const int pg_cap = min(p.pages_per_split, p.max_blocks_per_seq - pg0);
-  for (int i = threadIdx.x; i < pg_cap; i += blockDim.x)
-    s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
+  // The sequence's pages are cut into `splits` equal parts by its actual length (at most
+  // pages_per_split each, the plan's bound for the block table's capacity), so a cache sized for long
+  // sequences still keeps every split of a shorter one busy.
   const int seq = p.seq_lens[b];
   const int npages = (seq + kBS - 1) / kBS;
-  const int pg1 = min(npages, pg0 + p.pages_per_split);
+  const int pps = min(p.pages_per_split, max(1, (npages + p.splits - 1) / p.splits));
+  const int pg0 = split * pps;
+  const int pg1 = min(npages, pg0 + pps);
+  for (int i = threadIdx.x; i < pg1 - pg0; i += blockDim.x)
+    s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
   __syncthreads();  // page list (and the barrier initialisation) visible to every warp
 
   T* myKV = sKV + (size_t)warp * kStages * 2 * PE;

@@ -169,10 +169,12 @@ def test_pull_twoshot_default_grid_has_gather_ctas():
 
 
 def test_attention_pages_and_merge_cover_once():
-    """k_decode_attn: split s reads page-table entries [pg0, pg0 + min(pps, max_blocks - pg0)) (inside the
-    row), attends pages [pg0, pg1) with warp w taking pg0 + w, pg0 + w + 4, ...; the cluster merge gives
-    CTA r output elements [r * per, (r + 1) * per). Every page of every sequence is attended once and
-    every output element written once, for the split plans of the decode shapes."""
+    """k_decode_attn: the sequence's pages are cut by its actual length into `splits` parts of
+    min(pps, ceil(npages / splits)) pages; split s reads page-table entries [pg0, pg1) (inside the row)
+    and attends them with warp w taking pg0 + w, pg0 + w + 4, ...; the cluster merge gives CTA r output
+    elements [r * per, (r + 1) * per). Every page of every sequence is attended once, no split holds more
+    than the plan's pps pages, and every output element is written once, for the split plans of the
+    decode shapes."""
     from comm_opt_b200.ops.kernels import attention_split_plan
 
     kWarps, kBS = 4, 16
@@ -182,11 +184,11 @@ def test_attention_pages_and_merge_cover_once():
             for seq in {x for x in (1, 15, 16, 17, max_pages * kBS // 2 + 3, max_pages * kBS) if x <= max_pages * kBS}:
                 npages = (seq + kBS - 1) // kBS
                 seen = np.zeros(npages, dtype=np.int32)
+                dyn = min(pps, max(1, -(-npages // splits)))
                 for split in range(splits):
-                    pg0 = split * pps
-                    pg_cap = min(pps, max_pages - pg0)
-                    assert pg0 + max(pg_cap, 0) <= max_pages  # table reads stay inside the row
-                    pg1 = min(npages, pg0 + pps)
+                    pg0 = split * dyn
+                    pg1 = min(npages, pg0 + dyn)
+                    assert pg1 <= max_pages  # table reads stay inside the row
                     for warp in range(kWarps):
                         my = (pg1 - pg0 - warp + kWarps - 1) // kWarps if pg1 - pg0 > warp else 0
                         assert my <= pps
