@@ -35,7 +35,7 @@ def peak_hbm_gbs() -> float:
     try:
         return float(json.loads(p.read_text())["hbm_gbs"])
     except (OSError, KeyError, ValueError):
-        return 6650.0  # fallback measurement of this pool
+        return 6650.0  # no MEASURED_PEAKS.json: the earlier measurement of this pool (reported as "of fallback")
 
 
 def time_fn(fn, iters: int) -> float:
