@@ -161,6 +161,8 @@ def result_line(args, cfg, world: int, ms: float, ms_e2e: float, e2e_steps: int,
                                                                 runner.fused_epilogues_used(B))),
                                              step_ms_by_choice=runner.boundary_times.get(B))
                                         if runner.fuse_boundary else None),
+                   "gate_up_swiglu_epilogue": (runner.lin[(0, "gu")].kernels(B) == 1
+                                               if args.gemm == "cob" else False),
                    "tokens_per_s": round(B * 1000.0 / ms, 1), "l2_prefetch_tiles": args.l2_prefetch,
                    "l2": f"no flush: each step streams the full weight set ({weights_gb:.0f} GB / {world} GPUs) "
                          ">> 126 MB L2",

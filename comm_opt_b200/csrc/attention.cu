@@ -190,14 +190,21 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   // The sequence's pages are cut into `splits` equal parts by its actual length (at most
   // pages_per_split each, the plan's bound for the block table's capacity), so a cache sized for long
   // sequences still keeps every split of a shorter one busy.
+  // When the block table's row fits the page list, the whole row is requested together with the
+  // sequence length (no dependent load between them); longer rows read the split's range afterwards.
+  const int* bt_row = p.block_tables + (size_t)b * p.max_blocks_per_seq;
+  const bool whole_row = p.max_blocks_per_seq <= kMaxPagesPerSplit;
   const int seq = p.seq_lens[b];
-  const int npages = (seq + kBS - 1) / kBS;
+  if (whole_row)
+    for (int i = threadIdx.x; i < p.max_blocks_per_seq; i += blockDim.x) s_pages[i] = bt_row[i];
+  const int npages = min((seq + kBS - 1) / kBS, p.max_blocks_per_seq);  // a length past the table is clamped
   const int pps = min(p.pages_per_split, max(1, (npages + p.splits - 1) / p.splits));
   const int pg0 = split * pps;
   const int pg1 = min(npages, pg0 + pps);
-  for (int i = threadIdx.x; i < pg1 - pg0; i += blockDim.x)
-    s_pages[i] = p.block_tables[(size_t)b * p.max_blocks_per_seq + pg0 + i];
+  if (!whole_row)
+    for (int i = threadIdx.x; i < pg1 - pg0; i += blockDim.x) s_pages[i] = bt_row[pg0 + i];
   __syncthreads();  // page list (and the barrier initialisation) visible to every warp
+  const int* my_list = s_pages + (whole_row ? pg0 : 0);  // entry i: page pg0 + i of the sequence
 
   T* myKV = sKV + (size_t)warp * kStages * 2 * PE;
   uint64_t* mybar = bars + warp * kStages;
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   auto issue = [&](int i) {
     if (i >= my_pages || lane != 0) return;
     const int st = i % kStages;
-    const int blk = s_pages[warp + i * kWarps];
+    const int blk = my_list[warp + i * kWarps];
     const int row = (blk * p.nkv + kvh) * kBS;
     T* dk = myKV + (size_t)st * 2 * PE;
     T* dv = dk + PE;
@@ -274,7 +281,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     if (rope && pg == pos / kBS) {
       // the new token's row: k rotated, v (+ bias) from the projection, into the landed page and the cache
       const T* src = reinterpret_cast<const T*>(p.qkv) + (size_t)b * qkv_stride;
-      const int r = pos % kBS, blk = s_pages[pg - pg0];
+      const int r = pos % kBS, blk = my_list[pg - pg0];
       for (int c = lane; c < 2 * CH; c += 32) {
         const bool is_k = c < CH;
         const int ch = is_k ? c : c - CH;
@@ -440,7 +447,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
       }
       out[idx] = from_f<T>(O / L);
     }
-    cluster.sync();
+    // keeps this CTA's partial alive until every peer has read it; nothing is published after the
+    // barrier above, so the arrive needs no release ordering
+    asm volatile("barrier.cluster.arrive.relaxed;\n\tbarrier.cluster.wait;" ::: "memory");
     return;
   }
   // ---- the last split of this (sequence, head) pair merges all splits

@@ -126,19 +126,22 @@ __global__ void __launch_bounds__(64) k_rope_append(const T* __restrict__ qkv, c
   }
 }
 
+// il == 0: row = [gate (inter) | up (inter)]; il > 0: blocks of il gate then il up features
+// (the decode GEMMs' gate/up interleave), il a multiple of the vector width.
 template <typename T>
-__global__ void k_silu_mul(const T* __restrict__ gu, T* __restrict__ out, int inter) {
+__global__ void k_silu_mul(const T* __restrict__ gu, T* __restrict__ out, int inter, int il) {
   using V = Vec<T>;
   pdl_wait_then_trigger();
   const int b = blockIdx.y;
-  const int iv = inter / V::N;
-  const uint4* g = reinterpret_cast<const uint4*>(gu + (size_t)b * 2 * inter);
-  const uint4* u = g + iv;
+  const int iv = inter / V::N, ilv = il / V::N;
+  const uint4* row = reinterpret_cast<const uint4*>(gu + (size_t)b * 2 * inter);
   uint4* o = reinterpret_cast<uint4*>(out + (size_t)b * inter);
   for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < iv; v += gridDim.x * blockDim.x) {
+    const int gv = ilv ? (v / ilv) * 2 * ilv + v % ilv : v;
+    const int uvec = ilv ? gv + ilv : v + iv;
     float a[V::N], c[V::N], r[V::N];
-    V::to_float(g[v], a);
-    V::to_float(u[v], c);
+    V::to_float(row[gv], a);
+    V::to_float(row[uvec], c);
 #pragma unroll
     for (int i = 0; i < V::N; ++i) r[i] = a[i] / (1.f + __expf(-a[i])) * c[i];
     o[v] = V::from_float(r);
@@ -262,14 +265,16 @@ cudaError_t rope_append_kv(const void* qkv, const void* bias, const int32_t* pos
   });
 }
 
-cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s) {
+cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s, int interleave) {
   return by_dtype(dtype, [&](auto t) {
     using T = decltype(t);
-    if (inter % Vec<T>::N || rows <= 0) return cudaErrorInvalidValue;
+    if (inter % Vec<T>::N || rows <= 0 || interleave < 0 || interleave % Vec<T>::N ||
+        (interleave > 0 && inter % interleave))
+      return cudaErrorInvalidValue;
     const int iv = inter / Vec<T>::N;
     const int bx = std::min(64, (iv + 255) / 256);
     return launch_k(k_silu_mul<T>, dim3(bx, rows), dim3(256), 0, s, reinterpret_cast<const T*>(gu),
-                    reinterpret_cast<T*>(out), inter);
+                    reinterpret_cast<T*>(out), inter, interleave);
   });
 }
 

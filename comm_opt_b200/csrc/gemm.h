@@ -35,12 +35,16 @@ size_t gemm_workspace_bytes(int num_ctas, int bn);
 cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
                         size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
                         bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
-                        cudaStream_t stream, GemmPlan* used, bool packed = false);
+                        cudaStream_t stream, GemmPlan* used, bool packed = false, bool swiglu = false);
 // cluster_splits > 0 selects the cluster split-K schedule (grid tiles x splits, DSMEM reduction,
 // M <= 64, splits <= 16; above 8 a non-portable cluster size) instead of stream-K.
 // packed: W is the packed weight layout (see pack_weight in the Python package): for output tile
 // t = n / 128 and k-step k = K-column / 64, block t * (K / 64) + k of 128 x 64 elements (16 KB) holds
 // rows t*128.. and columns k*64.. exactly as the 128-byte-swizzled shared-memory image (16-byte chunk c
 // of row r stored at chunk c ^ (r % 8)), rows past N zero. K must be a multiple of 64.
+// swiglu: W's rows are gate and up features interleaved by 64 (rows 128t..128t+63 gate features
+// 64t.., rows 128t+64..128t+127 the matching up features), Y is [M, N / 2] (row stride ldy) holding
+// silu(gate) * up of the bf16/fp16-rounded projections. Needs the cluster schedule with a split count
+// (after rounding K into equal k-step shares) of 2, 4, 8 or 16, and N a multiple of 128.
 
 }  // namespace cob

@@ -73,6 +73,12 @@ __device__ __forceinline__ void cluster_arrive_relaxed() {
 }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
 
+// v as the output type would hold it (the value a plain GEMM stores)
+template <bool BF16>
+__device__ __forceinline__ float round_out(float v) {
+  return BF16 ? __bfloat162float(__float2bfloat16_rn(v)) : __half2float(__float2half_rn(v));
+}
+
 template <bool BF16>
 __device__ __forceinline__ void store_out(void* Y, size_t idx, float v) {
   if (BF16)
@@ -96,11 +102,15 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" :::
 // CLUSTER: instead of the stream-K partition, CTA (t, r) of grid (tiles, s) owns k-range r of tile t and
 // the s CTAs of a tile form a thread-block cluster that sums its partial tiles through distributed
 // shared memory (no global workspace, no L2 round trips on the tail). `kps` = k-steps per split.
+// swiglu (CLUSTER with s in {2, 4, 8, 16}): W holds gate and up rows interleaved by 64 (tile t = gate
+// features 64t..64t+63, then the matching up features), Y is [M, N / 2] = silu(gate) * up. CTA r of the
+// cluster receives gate rows [r * 64 / s, (r + 1) * 64 / s) of the tile together with their up rows, so
+// the product is formed where the sums are: the SiLU * up kernel and its round trip disappear.
 template <int BN, bool BF16, bool SMALL, bool CLUSTER>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
                    int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
-                   int kps, int l2pf, long long* stamps, const uint8_t* __restrict__ Wp) {
+                   int kps, int l2pf, long long* stamps, const uint8_t* __restrict__ Wp, int swiglu) {
   using C = Cfg<BN, SMALL, CLUSTER>;
   // optional phase stamps (%globaltimer, ns): stamps[cta * kStampSlots + phase]
   const int lin = blockIdx.x + blockIdx.y * gridDim.x;
@@ -269,9 +279,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // [o * per, (o + 1) * per) belong to CTA o of the cluster), slot blockIdx.y of that CTA's reduction area
     float* push_dst = nullptr;
     if (split_cluster) {
-      const int per = (BM + gridDim.y - 1) / gridDim.y, o = row / per;
+      const int per = (BM + gridDim.y - 1) / gridDim.y;
+      int o = row / per, slot = row - o * per;
+      if (swiglu) {  // gate row f and up row 64 + f go to the same owner: slots [0, ph) gate, [ph, 2 ph) up
+        const int ph = (BM / 2) / gridDim.y, f = row & (BM / 2 - 1);
+        o = f / ph;
+        slot = f - o * ph + (row >= BM / 2 ? ph : 0);
+      }
       cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
-      push_dst = cg::this_cluster().map_shared_rank(red, o) + ((size_t)blockIdx.y * per + (row - o * per)) * (BN + 4);
+      push_dst = cg::this_cluster().map_shared_rank(red, o) + ((size_t)blockIdx.y * per + slot) * (BN + 4);
     }
     int j = 0;
     for (long long g = beg; g < end; ++j) {
@@ -375,7 +391,38 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int mcols = min(M, BN);
     const int per = (BM + cs - 1) / cs, r0 = r * per, nr = min(BM, r0 + per) - r0;
     const int ncol4 = (mcols + 3) / 4;
-    for (int idx = threadIdx.x; idx < nr * ncol4; idx += kThreads) {
+    if (swiglu) {
+      const int ph = (BM / 2) / cs;
+      for (int idx = threadIdx.x; idx < ph * ncol4; idx += kThreads) {
+        const int lr = idx % ph, c4 = (idx / ph) * 4;
+        float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), ua = ga;
+        for (int c = 0; c < cs; ++c) {  // sources in cluster order, as the plain sums
+          const float4 g4 = *reinterpret_cast<const float4*>(red + ((size_t)c * per + lr) * (BN + 4) + c4);
+          const float4 u4 = *reinterpret_cast<const float4*>(red + ((size_t)c * per + ph + lr) * (BN + 4) + c4);
+          ga.x += g4.x;
+          ga.y += g4.y;
+          ga.z += g4.z;
+          ga.w += g4.w;
+          ua.x += u4.x;
+          ua.y += u4.y;
+          ua.z += u4.z;
+          ua.w += u4.w;
+        }
+        const int nn = t * (BM / 2) + r * ph + lr;  // output feature
+        if (nn < N / 2) {
+          const float gv[4] = {ga.x, ga.y, ga.z, ga.w}, uv[4] = {ua.x, ua.y, ua.z, ua.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (c4 + u < M) {
+              // gate and up rounded as a plain GEMM would store them, then SiLU(gate) * up in fp32
+              const float g = round_out<BF16>(gv[u]), up = round_out<BF16>(uv[u]);
+              store_out<BF16>(Y, (size_t)(c4 + u) * ldy + nn, g / (1.f + __expf(-g)) * up);
+            }
+          }
+        }
+      }
+    }
+    for (int idx = threadIdx.x; !swiglu && idx < nr * ncol4; idx += kThreads) {
       const int lr = idx % nr, c4 = (idx / nr) * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int c = 0; c < cs; ++c) {  // sources in cluster order: deterministic
@@ -418,7 +465,7 @@ cudaError_t tensor_map(const void* ptr, int rows, int cols, int box_rows, bool b
 template <int BN, bool BF16, bool SMALL>
 cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int M, int N, int K, int ctas, int ldy,
                       float* ws, int* ctr, int* err, unsigned long long timeout_ns, bool pdl, int splits,
-                      cudaStream_t stream, const uint8_t* Wp) {
+                      cudaStream_t stream, const uint8_t* Wp, bool swiglu) {
   const bool clustered = splits > 0;
   const int smem = clustered ? Cfg<BN, SMALL, true>::SMEM : Cfg<BN, SMALL, false>::SMEM;
   auto fn = clustered ? k_gemm_streamk<BN, BF16, SMALL, true> : k_gemm_streamk<BN, BF16, SMALL, false>;
@@ -458,19 +505,19 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
   cfg.attrs = attrs;
   cfg.numAttrs = na;
   return cudaLaunchKernelEx(&cfg, fn, mw, mx, Y, M, N, K, ldy, ws, ctr, err, timeout_ns, kps, l2_prefetch_tiles(),
-                            next_gemm_stamps(), Wp);
+                            next_gemm_stamps(), Wp, (int)swiglu);
 }
 
 template <bool BF16, bool SMALL>
 cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K,
                           int ctas, int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl,
-                          int splits, cudaStream_t s, const uint8_t* Wp) {
+                          int splits, cudaStream_t s, const uint8_t* Wp, bool sw) {
   switch (bn) {
-    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
-    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
-    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
-    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
-    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
+    case 16: return launch_bn<16, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw);
+    case 32: return launch_bn<32, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw);
+    case 64: return launch_bn<64, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw);
+    case 128: return launch_bn<128, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw);
+    case 256: return launch_bn<256, BF16, SMALL>(mw, mx, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -478,9 +525,9 @@ cudaError_t launch_bn_sel(const CUtensorMap& mw, const CUtensorMap& mx, int bn, 
 template <bool BF16>
 cudaError_t launch_typed(const CUtensorMap& mw, const CUtensorMap& mx, int bn, void* Y, int M, int N, int K, int ctas,
                          int ldy, float* ws, int* ctr, int* err, unsigned long long t, bool pdl, bool small,
-                         int splits, cudaStream_t s, const uint8_t* Wp) {
-  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp)
-               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp);
+                         int splits, cudaStream_t s, const uint8_t* Wp, bool sw) {
+  return small ? launch_bn_sel<BF16, true>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw)
+               : launch_bn_sel<BF16, false>(mw, mx, bn, Y, M, N, K, ctas, ldy, ws, ctr, err, t, pdl, splits, s, Wp, sw);
 }
 
 }  // namespace
@@ -526,8 +573,13 @@ size_t gemm_workspace_bytes(int num_ctas, int bn) { return (size_t)num_ctas * 2 
 cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int K, int ldy, int dtype, float* ws,
                         size_t ws_bytes, int* tile_ctr, int max_tiles, int* err, int num_sms, int ctas_override,
                         bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
-                        cudaStream_t stream, GemmPlan* used, bool packed) {
+                        cudaStream_t stream, GemmPlan* used, bool packed, bool swiglu) {
   if (cluster_splits > 16 || (cluster_splits > 0 && M > 64)) return cudaErrorInvalidValue;
+  if (swiglu) {  // cluster split-K whose split count divides 64 (gate / up row pairs split evenly)
+    if (cluster_splits <= 0 || N % BM) return cudaErrorInvalidValue;
+    const int KT = (K + BK - 1) / BK, kps = (KT + cluster_splits - 1) / cluster_splits, s = (KT + kps - 1) / kps;
+    if (s < 2 || (BM / 2) % s) return cudaErrorInvalidValue;
+  }
   if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % 8 || (dtype != kBF16 && dtype != kF16))
     return cudaErrorInvalidValue;
   // packed weights: whole 128 x 64 blocks, 16-byte aligned
@@ -543,9 +595,9 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
   if (e != cudaSuccess) return e;
   const uint8_t* Wp = packed ? static_cast<const uint8_t*>(W) : nullptr;
   return bf16 ? launch_typed<true>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
-                                   small_smem, cluster_splits, stream, Wp)
+                                   small_smem, cluster_splits, stream, Wp, swiglu)
               : launch_typed<false>(mw, mx, p.bn, Y, M, N, K, p.ctas, ldy, ws, tile_ctr, err, timeout_ns, pdl,
-                                    small_smem, cluster_splits, stream, Wp);
+                                    small_smem, cluster_splits, stream, Wp, swiglu);
 }
 
 }  // namespace cob

@@ -23,8 +23,9 @@ cudaError_t rope_append_kv(const void* qkv, const void* bias, const int32_t* pos
                            const float* sin_t, const int32_t* block_tables, int max_blocks_per_seq, void* q_out,
                            void* k_cache, void* v_cache, int batch, int nq, int nkv, int head_dim, int block_size,
                            int dtype, cudaStream_t s);
-// out[b, i] = silu(gu[b, i]) * gu[b, I + i]
-cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s);
+// out[b, i] = silu(gu[b, i]) * gu[b, I + i]; with interleave = c > 0 the row holds blocks of c gate
+// then c up features: out[b, i] = silu(gu[b, 2c (i / c) + i % c]) * gu[b, 2c (i / c) + c + i % c]
+cudaError_t silu_mul(const void* gu, void* out, int rows, int inter, int dtype, cudaStream_t s, int interleave = 0);
 // Per row: fold max over the local vocabulary into keys[row] (atomicMax of an order-preserving
 // 64-bit key: value high, inverted global index low; keys must be zero before).
 cudaError_t argmax_local(const void* logits, unsigned long long* keys, int rows, int vocab, int vocab_offset,

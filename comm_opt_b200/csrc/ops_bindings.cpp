@@ -88,11 +88,15 @@ void py_rope_append_kv(torch::Tensor qkv, torch::Tensor positions, torch::Tensor
      "rope_append_kv");
 }
 
-void py_silu_mul(torch::Tensor gu, torch::Tensor out) {
+void py_silu_mul(torch::Tensor gu, torch::Tensor out, int64_t interleave) {
   dense(gu, "gu");
   dense(out, "out");
+  COB_CHECK(gu.dim() == 2 && out.dim() == 2 && gu.size(0) == out.size(0) && gu.size(1) == 2 * out.size(1),
+            "gu [M, 2I], out [M, I]");
+  COB_CHECK(gu.scalar_type() == out.scalar_type(), "dtypes must match");
   const c10::cuda::CUDAGuard g(gu.device());
-  ok(cob::silu_mul(gu.data_ptr(), out.data_ptr(), (int)gu.size(0), (int)out.size(1), code_of(gu), cur()),
+  ok(cob::silu_mul(gu.data_ptr(), out.data_ptr(), (int)gu.size(0), (int)out.size(1), code_of(gu), cur(),
+                   (int)interleave),
      "silu_mul");
 }
 
@@ -205,7 +209,7 @@ void py_decode_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v
 // (zero-initialised, left zero). Returns {bn, tiles, ctas}.
 std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, torch::Tensor ws, torch::Tensor ctr,
                              torch::Tensor err, int64_t ctas, bool pdl, bool small_smem, int64_t cluster_splits,
-                             int64_t timeout_ns, int64_t packed_n) {
+                             int64_t timeout_ns, int64_t packed_n, bool swiglu) {
   dense(x, "x");
   dense(w, "w");
   dense(err, "err");
@@ -219,7 +223,10 @@ std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, 
               "packed w must be [ceil(N / 128), K / 64, 128, 64] for x [M, K]");
   else
     COB_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [M, K], w [N, K]");
-  COB_CHECK(y.size(0) == x.size(0) && y.size(1) == N, "y must be [M, N]");
+  if (swiglu)
+    COB_CHECK(y.size(0) == x.size(0) && 2 * y.size(1) == N, "y must be [M, N / 2] with the SwiGLU epilogue");
+  else
+    COB_CHECK(y.size(0) == x.size(0) && y.size(1) == N, "y must be [M, N]");
   COB_CHECK(x.scalar_type() == w.scalar_type() && y.scalar_type() == x.scalar_type(), "dtypes must match");
   COB_CHECK(err.scalar_type() == torch::kInt32 && ctr.scalar_type() == torch::kInt32, "err, ctr must be int32");
   COB_CHECK(ws.scalar_type() == torch::kFloat && ws.is_cuda() && ctr.is_cuda(), "ws must be float32 CUDA");
@@ -230,7 +237,7 @@ std::vector<int64_t> py_gemm(torch::Tensor x, torch::Tensor w, torch::Tensor y, 
   ok(cob::gemm_decode(x.data_ptr(), w.data_ptr(), y.data_ptr(), (int)x.size(0), (int)N, (int)x.size(1),
                       (int)y.stride(0), code_of(x), ws.data_ptr<float>(), (size_t)ws.numel() * 4,
                       ctr.data_ptr<int32_t>(), (int)ctr.numel(), err.data_ptr<int32_t>(), sms, (int)ctas, pdl,
-                      small_smem, (int)cluster_splits, (unsigned long long)timeout_ns, cur(), &p, packed),
+                      small_smem, (int)cluster_splits, (unsigned long long)timeout_ns, cur(), &p, packed, swiglu),
      "gemm_decode");
   return {p.bn, p.tiles, p.ctas};
 }
@@ -361,7 +368,7 @@ void register_ops(pybind11::module& m) {
   m.def("rope_append_kv", &py_rope_append_kv, pybind11::arg("qkv"), pybind11::arg("positions"), pybind11::arg("cos_t"),
         pybind11::arg("sin_t"), pybind11::arg("block_tables"), pybind11::arg("q_out"), pybind11::arg("k_cache"),
         pybind11::arg("v_cache"), pybind11::arg("nq"), pybind11::arg("nkv"), pybind11::arg("bias") = pybind11::none());
-  m.def("silu_mul", &py_silu_mul);
+  m.def("silu_mul", &py_silu_mul, pybind11::arg("gu"), pybind11::arg("out"), pybind11::arg("interleave") = 0);
   m.def("argmax_local", &py_argmax_local);
   m.def("argmax_combine", &py_argmax_combine, pybind11::arg("gathered"), pybind11::arg("ids"),
         pybind11::arg("world"), pybind11::arg("positions") = pybind11::none(), pybind11::arg("seq_lens") = pybind11::none(),

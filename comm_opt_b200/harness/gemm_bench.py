@@ -75,10 +75,13 @@ VARIANTS = {  # name -> gemm() keyword arguments
 
 def variant_kwargs(v: str, N: int) -> tuple[dict, bool]:
     """gemm() keyword arguments of a variant name, and whether it runs on packed weights ("pk_" prefix:
-    the same schedule on PackedWeight blocks)."""
+    the same schedule on PackedWeight blocks; "_sw" suffix: a cluster schedule with the SwiGLU epilogue,
+    output [M, N / 2], for the gate_up projection)."""
     packed = v.startswith("pk_") or v == "pk"
+    sw = v.endswith("_sw")
+    v = v[:-3] if sw else v
     base = v[3:] if v.startswith("pk_") else ("default" if v == "pk" else v)
-    kw = dict(VARIANTS[base])
+    kw = dict(VARIANTS[base], **({"swiglu": True} if sw else {}))
     if kw.get("ctas") == -1:
         kw["ctas"] = (N + 127) // 128
     return kw, packed
@@ -104,11 +107,15 @@ def sweep(shape_sets: list[str], batches: list[int], variants: list[str], iters:
                 row = dict(set=sset, op=name, M=M, N=N, K=K)
                 for v in variants:
                     kw, packed = variant_kwargs(v, N)
-                    wv = [pack_weight(w) for w in ws] if packed else ws
-                    t = time_fn(lambda i: gemm(x, wv[i % copies], y, **kw), iters)
+                    sw = kw.get("swiglu", False)
+                    if sw and name != "gate_up":
+                        continue
+                    wv = [pack_weight(w, interleave=64 if sw else 0) for w in ws] if packed else ws
+                    yv = torch.empty(M, N // 2, device=dev, dtype=torch.bfloat16) if sw else y
+                    t = time_fn(lambda i: gemm(x, wv[i % copies], yv, **kw), iters)
                     del wv
                     row[v] = round(t, 2)
-                    row[v + "_frac"] = round(nbytes / t / 1e3 / peak, 3)
+                    row[v + "_frac"] = round((nbytes - (M * N // 2 * 2 if sw else 0)) / t / 1e3 / peak, 3)
                 row["cublas"] = round(time_fn(lambda i: torch.matmul(x, ws[i % copies].t(), out=y), iters), 2)
                 rows.append(row)
                 print(json.dumps(row), flush=True)

@@ -5,6 +5,7 @@ removes the host launch interval), and the command a profiler capture of that ke
     python -m comm_opt_b200.harness.kernel_probe fused_ar --variant lamport_1s --world 2 --rows 8
     python -m comm_opt_b200.harness.kernel_probe attention --batch 8 --ctx 2048
     python -m comm_opt_b200.harness.kernel_probe decode_ops --batch 8
+    python -m comm_opt_b200.harness.kernel_probe allgather --world 8 --rows 16
     ncu --set full --clock-control none -k regex:k_oneshot -s 3 -c 1 -o oneshot \
         python -m comm_opt_b200.harness.kernel_probe fused_ar --variant lamport_1s --world 2 --rows 8 --iters 4
 
@@ -59,6 +60,17 @@ def fused_ar(a, dev) -> dict:
     comm.check()
     return dict(r, variant=a.variant, world=a.world, rows=a.rows, hidden=a.hidden, choice=comm.last_choice.__dict__,
                 bytes_per_rank=a.rows * a.hidden * 2)
+
+
+def allgather(a, dev) -> dict:
+    """The argmax all-gather (`k_allgather_u32`): `--rows` 32-bit words per rank, ranks emulated in one launch."""
+    comm = TPCommunicator(emulate_world=a.world, device=dev, dtype=torch.bfloat16, max_rows=a.rows, max_hidden=a.hidden)
+    inp = torch.arange(a.world * a.rows, dtype=torch.int32, device=dev).view(a.world, a.rows)
+    out = torch.empty(a.world, a.world, a.rows, dtype=torch.int32, device=dev)
+    r = timed(lambda: comm.all_gather_u32(inp, out=out), a.iters)
+    comm.check()
+    assert torch.equal(out, inp.unsqueeze(0).expand(a.world, -1, -1)), "all-gather mismatch"
+    return dict(r, world=a.world, words=a.rows)
 
 
 def attention(a, dev) -> dict:
@@ -122,7 +134,7 @@ def decode_ops(a, dev) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["fused_ar", "attention", "decode_ops"])
+    ap.add_argument("kernel", choices=["fused_ar", "allgather", "attention", "decode_ops"])
     ap.add_argument("--variant", default="lamport_1s")
     ap.add_argument("--world", type=int, default=2)
     ap.add_argument("--rows", type=int, default=8)
@@ -142,7 +154,8 @@ def main():
     GRAPH_OPS = a.graph
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    r = {"fused_ar": fused_ar, "attention": attention, "decode_ops": decode_ops}[a.kernel](a, dev)
+    r = {"fused_ar": fused_ar, "allgather": allgather, "attention": attention,
+         "decode_ops": decode_ops}[a.kernel](a, dev)
     print(json.dumps(dict(kernel=a.kernel, **r)))
 
 

@@ -26,7 +26,7 @@ import torch.nn.functional as F
 from ..ops import kernels as K
 from ..ops.reference import rope_tables
 from ..parallel.communicator import TPCommunicator
-from .gemm import Linear, dense, pack_weight
+from .gemm import GateUpLinear, Linear, PackedWeight, dense, pack_weight
 
 
 @dataclass(frozen=True)
@@ -237,17 +237,22 @@ class TPDecodeRunner:
         # RoPE + KV append of the new token inside the attention kernel (one kernel less per layer)
         self.fuse_append = bool(fuse_append)
         # packed weights (this package's GEMMs only): every projection matrix is converted in place, once,
-        # into the bulk-load block layout (models.gemm.PackedWeight); the prefill unpacks one matrix at a time
+        # into the bulk-load block layout (models.gemm.PackedWeight); the prefill unpacks one matrix at a time.
+        # The gate/up rows are interleaved by 64 on the way (every output tile pairs 64 gate features with
+        # their up features), so SiLU * up runs in the GEMM's cluster reduction or in a consumer GEMM's
+        # epilogue from the same copy of the weights
         self.packed = bool(pack_weights and gemm == "cob")
+        il = 64 if self.s["inter"] % 64 == 0 else 0
         if self.packed:
             for L in weights.layers:
-                L.wqkv, L.wo, L.wgu, L.wdown = (pack_weight(dense(t)) for t in (L.wqkv, L.wo, L.wgu, L.wdown))
+                L.wqkv, L.wo, L.wdown = (pack_weight(dense(t)) for t in (L.wqkv, L.wo, L.wdown))
+                L.wgu = pack_weight(dense(L.wgu), interleave=il)
             weights.lm_head = pack_weight(dense(weights.lm_head))
         self.lin = {}
         for i, L in enumerate(weights.layers):
             self.lin[(i, "qkv")] = Linear(L.wqkv, gemm)
             self.lin[(i, "o")] = Linear(L.wo, gemm)
-            self.lin[(i, "gu")] = Linear(L.wgu, gemm)
+            self.lin[(i, "gu")] = GateUpLinear(L.wgu, gemm)  # gate_up GEMM + SiLU * up (one kernel or two)
             self.lin[(i, "down")] = Linear(L.wdown, gemm)
         self.lin["head"] = Linear(weights.lm_head, gemm)
         self.graphs: dict[int, tuple] = {}
@@ -392,12 +397,11 @@ class TPDecodeRunner:
             n += self._attention(i, L, B, buf, bt)
             self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
             h = self._allreduce_add_rmsnorm(buf, L.ln2)
-            self.lin[(i, "gu")](h, out=buf["gu"])
-            K.silu_mul(buf["gu"], out=buf["act"])
+            n += self._gate_up(i, h, B, buf)
             self.lin[(i, "down")](buf["act"], out=buf["part"])
             nxt = w.layers[i + 1].ln1 if i + 1 < len(w.layers) else w.final_norm
             h = self._allreduce_add_rmsnorm(buf, nxt)
-            n += 1 + 2 * ar_ours + 4 * ours
+            n += 2 * ar_ours + 3 * ours
         self.lin["head"](h, out=buf["logits"])
         K.argmax_local(buf["logits"], self.rank * s["vocab"], keys=buf["keys"])
         n += 1 + ours
@@ -407,6 +411,13 @@ class TPDecodeRunner:
         K.argmax_combine(buf["gathered"] if self.tp > 1 else buf["keys"].view(1, B), self.tp, ids=buf["ids"],
                          positions=buf["pos"], seq_lens=buf["lens"], local_keys=buf["keys"])
         return n + 1
+
+    def _gate_up(self, i: int, h: torch.Tensor, B: int, buf: dict) -> int:
+        """buf["act"] = silu(gate) * up of layer i's gate/up projection of h; returns this package's kernel
+        count (the GEMM with the SwiGLU epilogue, or the GEMM and the SiLU * up kernel)."""
+        lin = self.lin[(i, "gu")]
+        lin(h, out=buf["act"])
+        return 1 if lin.kernels(B) == 1 else 1 + (1 if self.gemm == "cob" else 0)
 
     def _allreduce_add_rmsnorm(self, buf: dict, gamma: torch.Tensor) -> torch.Tensor:
         """h = RMSNorm(residual + sum_ranks(part)) * gamma, residual updated (one or two kernels). Returns
@@ -438,11 +449,19 @@ class TPDecodeRunner:
             comm.ar_norm_gemm(buf["res"], L.ln1, L.wqkv, dry_run=True, epilogue="rope_kv")
             # the QKV epilogue has no bias term: a QKV bias keeps RoPE + append in its own kernel
             rp = comm.last_fused_gemm[1][2] > 0 and cfg.head_dim == 128 and not cfg.qkv_bias
-            if sw and self._wgu_il is None:  # tile-interleaved gate/up copies (allocated outside capture)
-                il = [comm.interleave_gate_up(dense(Lw.wgu)) for Lw in self.w.layers]
-                self._wgu_il = [pack_weight(t) for t in il] if self.packed else il
+            if sw and self._wgu_il is None:
+                if self._gu_interleave() == 64:  # the packed gate/up weights are already in that order
+                    self._wgu_il = [Lw.wgu for Lw in self.w.layers]
+                else:  # tile-interleaved gate/up copies (allocated outside capture)
+                    il = [comm.interleave_gate_up(dense(Lw.wgu)) for Lw in self.w.layers]
+                    self._wgu_il = [pack_weight(t) for t in il] if self.packed else il
             self._fuse_epi[B] = (sw, rp)
         return self._fuse_epi[B]
+
+    def _gu_interleave(self) -> int:
+        """Row interleave of the gate/up weights as stored (0: [gate; up])."""
+        wgu = self.w.layers[0].wgu
+        return wgu.il if isinstance(wgu, PackedWeight) else 0
 
     def _attention(self, i: int, L, B: int, buf: dict, bt: torch.Tensor) -> int:
         """RoPE + paged-KV append of the new token and the attention of layer i from buf["qkv"]; one kernel
@@ -492,17 +511,15 @@ class TPDecodeRunner:
                 comm.gemm_push(buf["attn"].view(B, -1), L.wo)
                 if sw:
                     comm.ar_norm_gemm(buf["res"], L.ln2, self._wgu_il[i], cfg.eps, out=buf["act"], epilogue="swiglu")
-                else:
+                else:  # outputs in the stored gate/up order
                     comm.ar_norm_gemm(buf["res"], L.ln2, L.wgu, cfg.eps, out=buf["gu"])
+                    K.silu_mul(buf["gu"], out=buf["act"], interleave=self._gu_interleave())
+                    n += 1
                 n += 2
             else:
                 self.lin[(i, "o")](buf["attn"].view(B, -1), out=buf["part"])
                 h = self._allreduce_add_rmsnorm(buf, L.ln2)
-                self.lin[(i, "gu")](h, out=buf["gu"])
-                n += 3
-            if not sw:
-                K.silu_mul(buf["gu"], out=buf["act"])
-                n += 1
+                n += 2 + self._gate_up(i, h, B, buf)
             # MLP-output boundary
             last = i + 1 == len(w.layers)
             nxt = None if last else w.layers[i + 1]

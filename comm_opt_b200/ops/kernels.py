@@ -32,10 +32,12 @@ def rope_append_kv(qkv, positions, cos, sin, block_tables, q_out, k_cache, v_cac
     return q_out
 
 
-def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def silu_mul(gu: torch.Tensor, out: torch.Tensor | None = None, interleave: int = 0) -> torch.Tensor:
+    """out[M, I] = silu(gate) * up of gu [M, 2I]: [gate | up] halves, or with `interleave` = c blocks of c
+    gate then c up features (the layout of gate/up weights packed with `pack_weight(w, interleave=c)`)."""
     inter = gu.shape[-1] // 2
     out = torch.empty(gu.shape[0], inter, dtype=gu.dtype, device=gu.device) if out is None else out
-    native().silu_mul(gu, out)
+    native().silu_mul(gu, out, int(interleave))
     return out
 
 

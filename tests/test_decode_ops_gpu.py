@@ -68,6 +68,16 @@ def test_silu_mul(cuda, dtype):
     assert rel_err(K.silu_mul(gu), silu_mul_ref(gu)) <= tol
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_silu_mul_interleaved(cuda, dtype):
+    """Gate/up rows interleaved in blocks of 64 (the packed gate/up weights' output order)."""
+    from comm_opt_b200.models.gemm import interleave_rows
+
+    gu = torch.randn(5, 2 * 3584, device=cuda).to(dtype)
+    il = interleave_rows(gu.t().contiguous(), 64).t().contiguous()  # columns in the interleaved order
+    assert torch.equal(K.silu_mul(il, interleave=64), K.silu_mul(gu))
+
+
 def test_argmax_local_and_combine(cuda):
     V, world, rows = 16032, 4, 6
     logits = torch.randn(world, rows, V, device=cuda).to(torch.bfloat16)

@@ -123,3 +123,69 @@ def test_packed_weights_match_row_major(cuda, M, N, K, dtype, sched):
     assert int(gemm_error_word(cuda)) == 0
     assert torch.equal(y_rm, y_pk)
     assert rel_err(y_pk, x.float() @ w.float().t()) <= 2 ** -7
+
+
+@pytest.mark.parametrize("M,I,K", [(1, 64, 64), (8, 3584, 8192), (5, 192, 1024), (16, 7168, 1024), (64, 128, 512)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("splits,small", [(2, False), (4, True), (8, True), (16, True)])
+@pytest.mark.parametrize("packed", [True, False])
+def test_gemm_swiglu_epilogue(cuda, M, I, K, dtype, splits, small, packed):
+    """GEMM with the SwiGLU epilogue (gate/up rows interleaved by 64): silu(gate) * up of the fp32
+    projection within bf16/fp16 tolerance, and the same bits as the plain launch of the same schedule
+    followed by the SiLU * up kernel on its interleaved output."""
+    from comm_opt_b200.models.gemm import interleave_rows, pack_weight, swiglu_splits
+    from comm_opt_b200.ops import kernels as K_
+
+    if not swiglu_splits(K, splits):
+        pytest.skip("split count the epilogue does not accept for this K")
+    g = torch.Generator(device=cuda).manual_seed(M * 3 + I + K + splits)
+    x = torch.randn(M, K, device=cuda, generator=g).to(dtype)
+    w = (0.05 * torch.randn(2 * I, K, device=cuda, generator=g)).to(dtype)
+    wi = pack_weight(w, interleave=64) if packed else interleave_rows(w, 64)
+    if packed:
+        assert torch.equal(wi.dense(), w)
+    sched = dict(cluster_splits=splits, small_smem=small, pdl=small)
+    act = gemm(x, wi, swiglu=True, **sched)
+    plain = gemm(x, wi, **sched)
+    torch.cuda.synchronize()
+    assert int(gemm_error_word(cuda)) == 0
+    assert act.shape == (M, I)
+    assert torch.equal(act, K_.silu_mul(plain, interleave=64))
+    gu = x.float() @ w.float().t()
+    ref = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    assert rel_err(act, ref) <= 2 ** -6, rel_err(act, ref)
+
+
+def test_gemm_swiglu_rejects_other_schedules(cuda):
+    """The SwiGLU epilogue is refused (not silently wrong) for stream-K and for split counts that do not
+    pair every gate row with its up row inside one CTA."""
+    x = torch.randn(8, 1024, device=cuda).bfloat16()
+    w = torch.randn(256, 1024, device=cuda).bfloat16()
+    with pytest.raises(ValueError):
+        gemm(x, w, swiglu=True)
+    with pytest.raises(RuntimeError):
+        gemm(x, w, cluster_splits=3, swiglu=True)  # 3 CTAs per tile
+    with pytest.raises(RuntimeError):
+        gemm(x, torch.randn(192, 1024, device=cuda).bfloat16(), cluster_splits=2, swiglu=True)  # N % 128
+
+
+def test_gate_up_linear_tuned_and_fallback(cuda):
+    """GateUpLinear: the tuned SwiGLU-epilogue launch and the two-kernel fallback give the same bits."""
+    from comm_opt_b200.models.gemm import GateUpLinear, pack_weight
+
+    g = torch.Generator(device=cuda).manual_seed(11)
+    x = torch.randn(8, 2048, device=cuda, generator=g).bfloat16()
+    w = (0.05 * torch.randn(2 * 1024, 2048, device=cuda, generator=g)).bfloat16()
+    lin = GateUpLinear(pack_weight(w, interleave=64))
+    lin.tune(8)  # either form, whichever measured faster
+    tuned = lin(x)
+    lin.fused[8] = dict(cluster_splits=4, small_smem=True)
+    assert lin.kernels(8) == 1
+    fused = lin(x)
+    lin.fused[8] = {}
+    lin.cfg[8] = dict(cluster_splits=4, small_smem=True)
+    assert lin.kernels(8) == 2
+    two = lin(x)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, two)  # same schedule: same bits with or without the epilogue
+    assert rel_err(tuned, fused) <= 2 ** -7

@@ -456,7 +456,8 @@ def test_bench_result_line_contract():
                            collective="ours", l2_prefetch=0)
     runner = SimpleNamespace(fuse_boundary=True, fuse_epilogues=False, fuse_error="", fuse_kinds={8: (False, True)},
                              boundary_times={8: {"FF": 7.8, "SF": 7.5}}, kernels_per_step={8: 566},
-                             fused_epilogues_used=lambda B: (False, True))
+                             fused_epilogues_used=lambda B: (False, True),
+                             lin={(0, "gu"): SimpleNamespace(kernels=lambda B: 1)})
     clocks = {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []}
     line = bench.result_line(args, PRESETS["70b"], 8, 7.5, 7.55, 64, 5.0, clocks, runner)
     json.dumps(line)
@@ -467,6 +468,7 @@ def test_bench_result_line_contract():
     assert "vs_baseline" in line and line["higher_is_better"] is False and line["scaling"] in ("weak", "strong")
     assert {"model", "global_batch", "seq_len", "parallelism"} <= set(line["config"])
     assert line["config"]["parallelism"] == "tp8" and line["gpu_launches"] == 566 * 64
+    assert line["config"]["gate_up_swiglu_epilogue"] is True
     assert {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"} <= set(line["e2e"])
     assert line["config"]["fused_boundaries"]["attention_out"] is False and "141 GB" in line["config"]["l2"]
     assert line["config"]["fused_boundaries"]["epilogues"] == {"swiglu": False, "rope_kv": True}

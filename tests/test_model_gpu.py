@@ -90,7 +90,9 @@ def test_graph_replay_equals_eager(cuda):
     graph = [runner.step(4).clone() for _ in range(4)]
     torch.cuda.synchronize()
     assert all(torch.equal(a, b) for a, b in zip(eager, graph))
-    per_layer = 8 if runner.fuse_append else 9  # the fused append folds RoPE + KV append into attention
+    # qkv, attention, o, norm, down, norm; RoPE + KV append in its own kernel without the fused append; the
+    # gate/up projection with its SiLU * up epilogue (one kernel) or the GEMM and the SiLU * up kernel
+    per_layer = 6 + (0 if runner.fuse_append else 1) + runner.lin[(0, "gu")].kernels(4)
     assert runner.kernels_per_step[4] == 2 + 2 * per_layer + 2 + 1
 
 

@@ -209,7 +209,23 @@ def test_tinyllama_kv_head_replication():
     assert not torch.equal(own[0].layers[0].wqkv[:q], own[1].layers[0].wqkv[:q])
 
 
-def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
+class _GateUpRec:
+    """Recorder for the runner's gate/up projection (GateUpLinear): one GEMM with the SwiGLU epilogue
+    (`fused`), or the GEMM and the SiLU * up kernel."""
+
+    def __init__(self, calls, fused=False, inputs=None, key=None):
+        self.calls, self.fused, self.inputs, self.key = calls, fused, inputs, key
+
+    def kernels(self, M):
+        return 1 if self.fused else 2
+
+    def __call__(self, x, out=None):
+        if self.inputs is not None:
+            self.inputs.append((self.key, x))
+        self.calls += ["gemm:swiglu"] if self.fused else ["gemm", "silu_mul"]
+
+
+def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi, gu_fused=False):
     """A TPDecodeRunner whose kernels, GEMMs and collective are recorders (no GPU): the decode step's
     composition and its kernel count can be checked on CPU."""
     from types import SimpleNamespace
@@ -243,7 +259,8 @@ def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
     r.comm, r.collective, r.nccl_group, r.gemm = Comm(), "ours", None, "cob"
     r._car = r._vllm_ops = None
     keys = [(i, n) for i in range(layers) for n in ("qkv", "o", "gu", "down")] + ["head"]
-    r.lin = {k: (lambda *a, **kw: calls.append("gemm")) for k in keys}
+    r.lin = {k: (_GateUpRec(calls, gu_fused) if k[1:] == ("gu",) else (lambda *a, **kw: calls.append("gemm")))
+             for k in keys}
     r.cache = SimpleNamespace(block_tables=torch.zeros(4, 8, dtype=torch.int32), k=[None] * layers, v=[None] * layers)
     r.cos = r.sin = None
     r.scale = 1.0
@@ -258,25 +275,26 @@ def _recording_runner(monkeypatch, layers, tp, fuse, kinds, epi):
     return r, buf, calls
 
 
-def _expected_step(layers, fuse, kinds, epi, append=False):
-    seq = _expected_step_kernels(layers, fuse, kinds, epi)
+def _expected_step(layers, fuse, kinds, epi, append=False, gu_fused=False):
+    seq = _expected_step_kernels(layers, fuse, kinds, epi, gu_fused)
     # the fused append folds every RoPE + KV append kernel into the attention kernel that follows it
     return [k for k in seq if k != "rope_append_kv"] if append else seq
 
 
-def _expected_step_kernels(layers, fuse, kinds, epi):
+def _expected_step_kernels(layers, fuse, kinds, epi, gu_fused=False):
     fa, fm = kinds if fuse else (False, False)
     sw, rp = (epi[0] and fa, epi[1] and fm) if fuse else (False, False)
+    gu = ["gemm:swiglu"] if gu_fused else ["gemm", "silu_mul"]  # the separate gate/up projection
     seq = ["embedding", "rmsnorm", "gemm"]
     for i in range(layers):
         last = i + 1 == layers
         if i == 0 or not rp:
             seq.append("rope_append_kv")
         seq.append("attention")
-        seq += (["gemm_push", "ar_norm_gemm:swiglu" if sw else "ar_norm_gemm"] if fa else
-                ["gemm", "fused_ar", "gemm"])
-        if not sw:
-            seq.append("silu_mul")
+        if fa:
+            seq += ["gemm_push", "ar_norm_gemm:swiglu"] if sw else ["gemm_push", "ar_norm_gemm", "silu_mul"]
+        else:
+            seq += ["gemm", "fused_ar"] + gu
         if fm:
             seq += ["gemm_push", "ar_norm_gemm:rope_kv" if rp and not last else "ar_norm_gemm"]
         else:
@@ -284,7 +302,7 @@ def _expected_step_kernels(layers, fuse, kinds, epi):
     if not fuse:  # the separate step issues the next layer's QKV GEMM at the top of the layer
         seq = ["embedding", "rmsnorm"]
         for i in range(layers):
-            seq += ["gemm", "rope_append_kv", "attention", "gemm", "fused_ar", "gemm", "silu_mul", "gemm", "fused_ar"]
+            seq += ["gemm", "rope_append_kv", "attention", "gemm", "fused_ar"] + gu + ["gemm", "fused_ar"]
         seq.append("gemm")
     return seq + ["argmax_local", "all_gather", "argmax_combine"]
 
@@ -298,11 +316,13 @@ def test_decode_step_composition_every_boundary_mix(monkeypatch):
         for kinds in itertools.product((True, False), repeat=2):
             for epi in itertools.product((False, True), repeat=2):
                 for append in (False, True):
-                    r, buf, calls = _recording_runner(monkeypatch, 3, 2, fuse, kinds, epi)
-                    r.fuse_append = append
-                    n = r._step(4, buf)
-                    assert calls == _expected_step(3, fuse, kinds, epi, append), (fuse, kinds, epi, append)
-                    assert n == len(calls), (fuse, kinds, epi, append, n, len(calls))
+                    for gf in (False, True):
+                        r, buf, calls = _recording_runner(monkeypatch, 3, 2, fuse, kinds, epi, gu_fused=gf)
+                        r.fuse_append = append
+                        n = r._step(4, buf)
+                        case = (fuse, kinds, epi, append, gf)
+                        assert calls == _expected_step(3, fuse, kinds, epi, append, gf), case
+                        assert n == len(calls), (case, n, len(calls))
 
 
 def test_decode_step_composition_vllm_stack(monkeypatch):
@@ -324,7 +344,8 @@ def test_decode_step_composition_vllm_stack(monkeypatch):
     r._vllm_ops = SimpleNamespace(fused_add_rms_norm=lambda out, res, g, eps: calls.append("vllm_norm"))
     gemm_inputs = []
     for k in list(r.lin):
-        r.lin[k] = (lambda x, out=None, _k=k: (gemm_inputs.append((_k, x)), calls.append("gemm")))
+        r.lin[k] = (_GateUpRec(calls, False, gemm_inputs, k) if k[1:] == ("gu",) else
+                    (lambda x, out=None, _k=k: (gemm_inputs.append((_k, x)), calls.append("gemm"))))
     n = r._step(4, buf)
     layer = ["gemm", "rope_append_kv", "attention", "gemm", "car_ar", "vllm_norm", "gemm", "silu_mul", "gemm",
              "car_ar", "vllm_norm"]
@@ -356,6 +377,34 @@ def test_pack_weight_layout_and_round_trip():
                         assert torch.equal(got, want)
     with pytest.raises(ValueError):
         pack_weight(torch.zeros(128, 100))
+
+
+def test_gate_up_interleave_round_trip_and_split_rule():
+    """Gate/up rows interleaved by 64 for the SwiGLU epilogue: every 128-row tile holds 64 gate rows and
+    their up rows; packing with the interleave keeps dense() the original [gate; up] weight; the split
+    counts the epilogue accepts are the launched ones that divide 64."""
+    from comm_opt_b200.models.gemm import (candidates, cluster_split_count, deinterleave_rows, interleave_rows,
+                                           pack_weight, swiglu_splits)
+
+    I, K = 192, 128
+    w = torch.randn(2 * I, K).bfloat16()
+    wi = interleave_rows(w, 64)
+    for t in range(I // 64):
+        assert torch.equal(wi[128 * t:128 * t + 64], w[64 * t:64 * t + 64])
+        assert torch.equal(wi[128 * t + 64:128 * t + 128], w[I + 64 * t:I + 64 * t + 64])
+    assert torch.equal(deinterleave_rows(wi, 64), w)
+    p = pack_weight(w, interleave=64)
+    assert p.il == 64 and torch.equal(p.dense(), w) and torch.equal(pack_weight(wi).data, p.data)
+    w3 = torch.randn(2, 2 * I, K).bfloat16()  # emulated ranks
+    assert torch.equal(pack_weight(w3, interleave=64).dense(), w3)
+    with pytest.raises(ValueError):
+        interleave_rows(torch.zeros(2 * 96, 64), 64)
+    assert cluster_split_count(8192, 16) == 16 and cluster_split_count(512, 16) == 8
+    assert cluster_split_count(1024, 3) == 3 and cluster_split_count(1024, 6) == 6
+    assert [s for s in (2, 3, 4, 6, 8, 12, 16) if swiglu_splits(8192, s)] == [2, 4, 8, 16]
+    assert not swiglu_splits(64, 2)  # one k-step: one CTA per tile
+    c = candidates(8, 7168, 8192, 148, swiglu=True)
+    assert c and all(x.get("swiglu") and swiglu_splits(8192, x["cluster_splits"]) for x in c)
 
 
 def test_variant_table_validation_rule():
