@@ -252,6 +252,13 @@ void py_rs_atomic_probe(std::vector<int64_t> bases, int64_t acc_off, int64_t ctr
                         int64_t timeout_ns, torch::Tensor err) {
   dense(x, "x");
   COB_CHECK(bases.size() >= 1 && bases.size() <= 8, "world must be 1..8");
+  COB_CHECK(variant >= 0 && variant <= 3 && n > 0 && rank >= 0 && rank < (int64_t)bases.size(), "bad probe geometry");
+  // input bytes the kernel reads: every rank's [world, n] slices (emulated ranks at x_rank_bytes apart),
+  // or this rank's own slices on a real rank (no per-rank offset there)
+  const int64_t es = variant <= 1 ? 4 : 2, W = (int64_t)bases.size();
+  const int64_t need = emulate ? (W - 1) * x_rank_bytes + W * n * es : W * n * es;
+  COB_CHECK(x.numel() * x.element_size() >= need && (emulate ? x_rank_bytes >= W * n * es : x_rank_bytes == 0),
+            "x is smaller than the slices the probe reads (x_rank_bytes must be 0 on a real rank)");
   cob::RsProbeParams p = {};
   for (size_t i = 0; i < bases.size(); ++i) p.base[i] = reinterpret_cast<char*>(bases[i]);
   p.acc_off = acc_off;

@@ -38,7 +38,8 @@ __device__ __forceinline__ void red_v4_bf16x2(void* p, const uint4& v) {
 __global__ void __launch_bounds__(256) k_rs_atomic(const RsProbeParams p) {
   const int rank = p.emulate ? (int)blockIdx.y : p.rank;
   const int W = p.world;
-  const char* xb = reinterpret_cast<const char*>(p.x) + (size_t)rank * p.x_rank_bytes;
+  // emulated ranks read their own input at rank * x_rank_bytes; a real rank's x is its own input
+  const char* xb = reinterpret_cast<const char*>(p.x) + (p.emulate ? (size_t)rank * p.x_rank_bytes : 0);
   const int es = p.variant <= 1 ? 4 : 2;
   const size_t slice_bytes = (size_t)p.n * es;
   pdl_wait();

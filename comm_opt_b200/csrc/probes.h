@@ -10,7 +10,7 @@ struct RsProbeParams {
   char* base[8];          // per-rank probe heap (accumulator at acc_off, arrival counter at ctr_off)
   long long acc_off, ctr_off;
   const void* x;          // this rank's input: world slices of n elements (f32 or bf16)
-  long long x_rank_bytes; // emulate mode: bytes between ranks' inputs
+  long long x_rank_bytes; // emulate mode: bytes between ranks' inputs (unused, and 0, on a real rank)
   int rank, world, n, variant, emulate;  // variant 0 red.f32, 1 red.v4.f32, 2 red.bf16x2, 3 red.v4.bf16x2
   unsigned long long timeout_ns;
   int* err;

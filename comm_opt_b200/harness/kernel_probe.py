@@ -91,7 +91,7 @@ def attention(a, dev) -> dict:
 
         op.pps = -(-pages // a.splits)
         op.splits = -(-pages // op.pps)
-        op.cluster = op.splits <= 16
+        op.cluster = op.splits <= 16 and not a.no_cluster
         op.scratch = torch.zeros(native().attn_scratch_bytes(B, nkv, op.splits, nq // nkv, D), dtype=torch.uint8,
                                  device=dev)
     r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5), a.iters)
@@ -149,6 +149,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--splits", type=int, default=0, help="attention: override the split plan")
     ap.add_argument("--graph", type=int, default=0, help="time CUDA graphs of this many launches")
+    ap.add_argument("--no-cluster", action="store_true", help="attention with --splits: merge through global memory")
     a = ap.parse_args()
     global GRAPH_OPS
     GRAPH_OPS = a.graph

@@ -67,7 +67,8 @@ def run_rs(world: int, n: int, variant: int, dev, emulate: bool, blocks: int = 6
             dist.barrier(group=group)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        C.rs_atomic_probe(bases, 0, acc_bytes, x, rank, n, variant, int(emulate), world * n * es, blocks,
+        x_rank_bytes = world * n * es if emulate else 0  # a real rank's x holds only its own slices
+        C.rs_atomic_probe(bases, 0, acc_bytes, x, rank, n, variant, int(emulate), x_rank_bytes, blocks,
                           int(1e9), err)
         b.record()
         torch.cuda.synchronize()
