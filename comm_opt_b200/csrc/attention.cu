@@ -140,7 +140,8 @@ __device__ __forceinline__ uint4 plain_chunk(const AttnParams& p, const T* src, 
   return V::from_float(x);
 }
 
-constexpr int kStages = 3;                    // KV pages in flight per warp
+constexpr int kStages = 3;                    // KV pages in flight per warp (two CTAs per SM)
+constexpr int kStagesDeep = 6;                // the deep ring: one CTA per SM
 template <int D>
 constexpr int kPageElems = kBS * D;           // one K (or V) page: 16 x D
 constexpr int kMaxPagesPerSplit = 512;
@@ -151,18 +152,19 @@ struct alignas(64) AttnArgs {
   AttnParams p;
 };
 
-template <int D>
+template <int D, int S>
 __host__ __device__ constexpr size_t attn_smem_bytes() {
-  return 1024 /*align*/ + (size_t)kWarps * kStages * 2 * kPageElems<D> * 2 + (size_t)kRows * D * 2 +
-         (size_t)kWarps * kStages * 8 + kMaxPagesPerSplit * 4 + 64;
+  return 1024 /*align*/ + (size_t)kWarps * S * 2 * kPageElems<D> * 2 + (size_t)kRows * D * 2 +
+         (size_t)kWarps * S * 8 + kMaxPagesPerSplit * 4 + 64;
 }
 
 // CLUSTER: the splits of one (sequence, kv head) pair form a thread-block cluster (splits <= 16) and
 // are merged through distributed shared memory; otherwise they are merged through the global
 // scratch by the last split to finish.
-template <typename T, bool CLUSTER, int D>
+// S: KV pages in flight per warp (kStages, or kStagesDeep when the grid fits one CTA per SM).
+template <typename T, bool CLUSTER, int D, int S>
 __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_constant__ AttnArgs args) {
-  constexpr int kD = D, PE = kPageElems<D>;
+  constexpr int kD = D, PE = kPageElems<D>, kStages = S;
   using namespace sm100;
   const AttnParams& p = args.p;
   extern __shared__ uint8_t smem_raw[];
@@ -511,10 +513,39 @@ size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_di
          pairs * sizeof(int32_t);
 }
 
+int& attn_stage_mode() {
+  static int mode = 0;
+  return mode;
+}
+
 namespace {
+
+// KV ring depth of one launch. The deep ring (all four pages of every warp of a 2048-token, 8-way split
+// in flight) needs one CTA per SM at head_dim 128, so it is used only for grids that fit in one wave at
+// one CTA per SM and clusters of at most 8 (portable sizes); mode kStagesDeep asks for it, any other
+// mode keeps the shallow ring (two CTAs per SM).
+int attn_stages_for(int ctas, int cluster_size) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return attn_stage_mode() == kStagesDeep && ctas <= sms && cluster_size <= 8 ? kStagesDeep : kStages;
+}
+
+template <int D, int S>
+cudaError_t launch_attention_s(const AttnParams& p, cudaStream_t s);
 
 template <int D>
 cudaError_t launch_attention(const AttnParams& p, cudaStream_t s) {
+  const int ctas = p.splits * p.nkv * p.batch;
+  return attn_stages_for(ctas, p.cluster ? p.splits : 1) == kStagesDeep ? launch_attention_s<D, kStagesDeep>(p, s)
+                                                                        : launch_attention_s<D, kStages>(p, s);
+}
+
+template <int D, int S>
+cudaError_t launch_attention_s(const AttnParams& p, cudaStream_t s) {
   constexpr int PE = kPageElems<D>;
   if ((size_t)p.splits * (p.nq / p.nkv) * 2 + kRows > (size_t)kWarps * kStages * 2 * PE / 2)
     return cudaErrorInvalidValue;  // the global merge's split weights must fit in the KV stages
@@ -532,11 +563,11 @@ cudaError_t launch_attention(const AttnParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   e = tensor_map_2d(p.v_cache, rows, D, D * 2, kBS, 64, bf16, &a.tv);
   if (e != cudaSuccess) return e;
-  const size_t smem = attn_smem_bytes<D>();
+  const size_t smem = attn_smem_bytes<D, S>();
   const dim3 grid(p.splits, p.nkv, p.batch);
   const bool cluster = p.cluster && p.splits > 1 && p.splits <= kMaxClusterSplits;
-  auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true, D> : k_decode_attn<__nv_bfloat16, false, D>)
-                 : (cluster ? k_decode_attn<__half, true, D> : k_decode_attn<__half, false, D>);
+  auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true, D, S> : k_decode_attn<__nv_bfloat16, false, D, S>)
+                 : (cluster ? k_decode_attn<__half, true, D, S> : k_decode_attn<__half, false, D, S>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (cluster && p.splits > 8) {  // clusters of 9..16 CTAs are non-portable (two CTAs per SM here)

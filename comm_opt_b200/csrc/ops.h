@@ -65,5 +65,8 @@ struct AttnParams {
 // bytes of scratch needed for a given geometry
 size_t attn_scratch_bytes(int batch, int nkv, int splits, int group, int head_dim);
 cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s);
+// KV ring depth of the attention kernel, read at launch: 6 = the deep ring (one CTA per SM) where the
+// grid fits one wave at one CTA per SM and clusters of at most 8; any other value = 3 pages per warp.
+int& attn_stage_mode();
 
 }  // namespace cob

@@ -393,6 +393,11 @@ void register_ops(pybind11::module& m) {
   m.def("gemm_stamp_launches", []() { return (int64_t)cob::gemm_stamp_launches(); });
   m.def("set_l2_prefetch", [](int64_t tiles) { cob::l2_prefetch_tiles() = (int)std::max<int64_t>(0, tiles); });
   m.def("get_l2_prefetch", []() { return (int64_t)cob::l2_prefetch_tiles(); });
+  m.def("set_attn_stages", [](int64_t n) {
+    const int old = cob::attn_stage_mode();
+    cob::attn_stage_mode() = (int)n;
+    return (int64_t)old;
+  });
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);
   m.def("decode_attention", &py_decode_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
         pybind11::arg("v_cache"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"), pybind11::arg("out"),

@@ -94,7 +94,14 @@ def attention(a, dev) -> dict:
         op.cluster = op.splits <= 16 and not a.no_cluster
         op.scratch = torch.zeros(native().attn_scratch_bytes(B, nkv, op.splits, nq // nkv, D), dtype=torch.uint8,
                                  device=dev)
-    r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5), a.iters)
+    if a.append:  # the decode step's form: q and the new token's k / v from the QKV output, rotated here
+        qkv = torch.randn(B, (nq + 2 * nkv) * D, generator=g, device=dev).bfloat16()
+        pos = (lens - 1).contiguous()
+        cos, sin = rope_tables(a.ctx + 16, D, 5e5, dev)
+        app = dict(qkv=qkv, positions=pos, cos=cos, sin=sin)
+        r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5, append=app), a.iters)
+    else:
+        r = timed(lambda: op(q, kc, vc, bt, lens, out, D ** -0.5), a.iters)
     kv_bytes = 2 * B * nkv * a.ctx * D * 2
     return dict(r, batch=B, ctx=a.ctx, heads=nq, kv_heads=nkv, head_dim=D, splits=op.splits,
                 pages_per_split=op.pps, cluster=op.cluster, kv_bytes=kv_bytes)
@@ -150,11 +157,15 @@ def main():
     ap.add_argument("--splits", type=int, default=0, help="attention: override the split plan")
     ap.add_argument("--graph", type=int, default=0, help="time CUDA graphs of this many launches")
     ap.add_argument("--no-cluster", action="store_true", help="attention with --splits: merge through global memory")
+    ap.add_argument("--attn-stages", type=int, default=0, help="attention KV ring depth (6: deep ring; 0: default)")
+    ap.add_argument("--append", action="store_true", help="attention with the fused RoPE + KV append")
     a = ap.parse_args()
     global GRAPH_OPS
     GRAPH_OPS = a.graph
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if a.attn_stages:
+        K.set_attn_stages(a.attn_stages)
     r = {"fused_ar": fused_ar, "allgather": allgather, "attention": attention,
          "decode_ops": decode_ops}[a.kernel](a, dev)
     print(json.dumps(dict(kernel=a.kernel, **r)))

@@ -31,12 +31,17 @@ def main():
     ap.add_argument("--gemm-timeline", action="store_true",
                     help="stamp every GEMM of the captured step (%%globaltimer) and print when each ran inside one "
                          "replay: the gaps between GEMMs hold the other kernels and the transitions")
+    ap.add_argument("--attn-stages", type=int, default=0, help="attention KV ring depth (6: deep ring; 0: default)")
     ap.add_argument("--tp-shape", type=int, default=1,
                     help="shard the weights this many ways (one GPU, the all-reduce replaced by add+RMSNorm) to "
                          "profile the per-rank kernels of a TP run")
     a = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
+    if a.attn_stages:
+        from ..ops import kernels as K
+
+        K.set_attn_stages(a.attn_stages)
     cfg = replace(PRESETS[a.model], layers=a.layers)
     w = LlamaWeights(cfg, 0, a.tp_shape, dev, seed=0)
     comm = TPCommunicator(None, device=dev, dtype=torch.bfloat16, max_rows=max(8, a.batch), max_hidden=cfg.hidden)
@@ -96,7 +101,8 @@ def main():
         print(f"gemm time {tot:.1f} us of a {span:.1f} us span ({len(rows)} GEMMs)")
     runner.release_graphs()
     print(f"ok kernels/step {runner.kernels_per_step.get(a.batch)} ms/step {e0.elapsed_time(e1) / a.steps:.3f} "
-          f"(layers {a.layers}, tp-shape {a.tp_shape}, batch {a.batch}, l2 prefetch {a.l2_prefetch})")
+          f"(layers {a.layers}, tp-shape {a.tp_shape}, batch {a.batch}, l2 prefetch {a.l2_prefetch}, "
+          f"attention stages {a.attn_stages or 'default'})")
 
 
 if __name__ == "__main__":

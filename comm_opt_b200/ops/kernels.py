@@ -50,6 +50,13 @@ def set_l2_prefetch(tiles: int) -> int:
     return old
 
 
+def set_attn_stages(n: int) -> int:
+    """KV pages in flight per warp of the decode attention kernel: 6 (the deep ring, one CTA per SM; used
+    where the grid fits one wave at one CTA per SM) or 3 (two CTAs per SM). Read at launch time (a CUDA
+    graph keeps the launch it captured); returns the old setting."""
+    return int(native().set_attn_stages(int(n)))
+
+
 def set_pdl(on: bool) -> bool:
     """Launch every kernel of this package with programmatic dependent launch (returns the old value)."""
     old = native().get_pdl()
@@ -81,20 +88,21 @@ def attention_split_plan(batch: int, nkv: int, max_pages: int, num_sms: int = 14
     """Split-KV geometry (splits, pages per split, cluster merge).
 
     As many CTAs over (batch, kv head, split) as fit in ONE wave of resident CTAs (a partial second
-    wave would double the kernel time). When that needs at most 8 splits per pair, or 8 splits leave
-    each CTA at most 32 pages, the splits of a pair form a cluster and merge through distributed
-    shared memory; long contexts with few pairs use more splits and the global merge."""
+    wave would double the kernel time), but merged inside a thread-block cluster (distributed shared
+    memory) wherever possible: when one wave allows more than 8 splits per pair, 8 splits while each
+    CTA keeps at most 32 pages, else 16 (a non-portable cluster size the kernel supports) if 16 still
+    fit one wave. Only sequences longer than 16 x 512 pages use more splits and the global merge."""
     pairs = max(1, batch * nkv)
     slots = ATTN_CTAS_PER_SM * num_sms
     splits = max(1, min(max_pages, slots // pairs))
-    if splits > 8 and (max_pages + 7) // 8 <= 32:
-        # a cluster merge (DSMEM) of 8 splits when each CTA keeps a modest page chain. Measured at
-        # batch 8, one KV head, 2048 tokens (CUDA graphs, one B200): 8 splits 8.8 us, 16 (a
-        # non-portable cluster, which the kernel supports) 9.9 us, 32 with the global merge 26.2 us.
-        splits = 8
+    if splits > 8:
+        # Measured at batch 8, one KV head (CUDA graphs, one B200): 2048 tokens - 8 splits 9.9 us, 16
+        # 10.8 us, 32 with the global merge 26.4 us; 8192 tokens - 8 splits 18.6 us, 37 with the global
+        # merge 34.4 us (the global merge, one CTA folding every split, costs more than a longer chain)
+        splits = 16 if (max_pages + 7) // 8 > 32 and pairs * 16 <= slots else 8
     pps = min(512, (max_pages + splits - 1) // splits)
     splits = (max_pages + pps - 1) // pps
-    return splits, pps, 1 < splits <= 8
+    return splits, pps, 1 < splits <= 16
 
 
 class DecodeAttention:

@@ -177,3 +177,39 @@ def test_attention_with_fused_append(cuda, nq, nkv, bias, D, dtype):
         assert rel_err(got, want) <= 2 ** -7, (num_sms, rel_err(got, want))
         assert rel_err(got, ref) <= 2 ** -7
         assert rel_err(kc2, kc1) <= 2 ** -7 and rel_err(vc2, vc1) <= 2 ** -7
+
+
+@pytest.fixture
+def deep_ring():
+    old = K.set_attn_stages(6)
+    yield
+    K.set_attn_stages(old)
+
+
+@pytest.mark.parametrize("nq,nkv,D", [(8, 1, 128), (16, 4, 128), (4, 1, 64)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_decode_attention_deep_ring(cuda, deep_ring, nq, nkv, D, dtype):
+    """The deep KV ring (six pages in flight per warp, one CTA per SM) gives the shallow ring's bits: the
+    same pages in the same order per warp, only requested earlier; every merge form and the fused append."""
+    check_decode_attention(cuda, nq, nkv, dtype, D)
+    B, bs, maxb = 6, 16, 40
+    seq = torch.tensor([1, 16, 17, 33, 300, 640], device=cuda, dtype=torch.int32)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    kc0 = torch.randn(B * maxb, nkv, bs, D, device=cuda, generator=g).to(dtype)
+    vc0 = torch.randn(B * maxb, nkv, bs, D, device=cuda, generator=g).to(dtype)
+    bt = torch.randperm(B * maxb, device=cuda).to(torch.int32).view(B, maxb)
+    qkv = torch.randn(B, (nq + 2 * nkv) * D, device=cuda, generator=g).to(dtype)
+    cos, sin = rope_tables(maxb * bs, D, 500000.0, cuda)
+    app = dict(qkv=qkv, positions=seq - 1, cos=cos, sin=sin)
+    for num_sms in (148, 8):  # cluster merge (deep ring), then more CTAs than that
+        outs = []
+        for stages in (6, 3):
+            K.set_attn_stages(stages)
+            attn = K.DecodeAttention(B, nq, nkv, D, maxb, cuda, num_sms=num_sms)
+            kc, vc = kc0.clone(), vc0.clone()
+            out = torch.empty(B, nq, D, device=cuda, dtype=dtype)
+            attn(torch.empty_like(out), kc, vc, bt, seq, out, 1 / math.sqrt(D), append=app)
+            torch.cuda.synchronize()
+            outs.append((out, kc, vc))
+        K.set_attn_stages(6)
+        assert all(torch.equal(a, b) for a, b in zip(outs[0], outs[1])), num_sms

@@ -118,7 +118,7 @@ def test_analyze_and_calibrate_synthetic_sweep(tmp_path):
 
 def test_attention_split_plans():
     """Split-KV geometry: covers every page, at most 512 pages per split (the kernel's page list),
-    one wave of resident CTAs, cluster merge only for 2..8 splits."""
+    one wave of resident CTAs, cluster merge for 2..16 splits, 16 only for long contexts."""
     from comm_opt_b200.ops.kernels import ATTN_CTAS_PER_SM, attention_split_plan
 
     for batch in (1, 2, 8, 32, 128):
@@ -126,9 +126,14 @@ def test_attention_split_plans():
             for pages in (1, 7, 64, 136, 512, 2048):
                 splits, pps, cluster = attention_split_plan(batch, nkv, pages, 148)
                 assert splits >= 1 and 1 <= pps <= 512 and splits * pps >= pages and (splits - 1) * pps < pages
-                assert cluster == (1 < splits <= 8)
+                assert cluster == (1 < splits <= 16)
                 if splits > 1:
                     assert batch * nkv * splits <= ATTN_CTAS_PER_SM * 148 or pps == 512
+                if splits > 8 and pps < 512:
+                    assert (pages + 7) // 8 > 32  # 16-way clusters only where 8 splits keep > 32 pages
+    assert attention_split_plan(8, 1, 128, 148) == (8, 16, True)  # 70B TP=8, 2048 tokens
+    assert attention_split_plan(8, 1, 512, 148) == (16, 32, True)  # 8192 tokens: a 16-CTA cluster
+    assert attention_split_plan(32, 1, 512, 148)[2] and attention_split_plan(32, 1, 512, 148)[0] == 8
 
 
 def test_repeat_statistics_effectiveness_rule():
