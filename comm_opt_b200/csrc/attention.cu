@@ -93,10 +93,11 @@ __device__ __forceinline__ int swzp(int r, int ch) { return ((ch >> 3) << 10) + 
 __device__ __forceinline__ float safe_exp2_diff(float a, float b) { return a == -INFINITY ? 0.f : exp2f(a - b); }
 
 // 16-byte chunk `ch` (8 elements) of head `head` of one token's projection row `src` (+ bias), rotated by
-// RoPE at position `pos`: element i of the first half pairs with i + D / 2. Rounded to T once, as the
-// separate append kernel stores it.
+// RoPE with the position's table row `cs` (cos at [0, D/2), sin at [D/2, D), staged in shared memory):
+// element i of the first half pairs with i + D / 2. Rounded to T once, as the separate append kernel
+// stores it.
 template <typename T, int D>
-__device__ __forceinline__ uint4 rope_chunk(const AttnParams& p, const T* src, int head, int ch, int pos) {
+__device__ __forceinline__ uint4 rope_chunk(const AttnParams& p, const T* src, int head, int ch, const float* cs) {
   using V = Vec<T>;
   constexpr int H = D / 2, HC = H / 8;  // half width, chunks per half
   const bool lo = ch < HC;
@@ -120,7 +121,7 @@ __device__ __forceinline__ uint4 rope_chunk(const AttnParams& p, const T* src, i
   float o[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const float c = p.cos_t[(size_t)pos * H + i0 + j], sn = p.sin_t[(size_t)pos * H + i0 + j];
+    const float c = cs[i0 + j], sn = cs[H + i0 + j];
     o[j] = lo ? x[j] * c - y[j] * sn : x[j] * c + y[j] * sn;
   }
   return V::from_float(o);
@@ -150,12 +151,19 @@ constexpr int kMaxClusterSplits = 16;         // splits merged inside one (non-p
 struct alignas(64) AttnArgs {
   CUtensorMap tk, tv;  // K / V caches as 2-D [num_blocks * nkv * 16, 128], box 64 x 16, 128-byte swizzle
   AttnParams p;
+  int push;  // cluster merge by pushes into the owners' shared memory (2..8 splits)
 };
+
+// Shared memory of the push merge: [splits][per] partial outputs, then [splits][G][2] (max, sum), where
+// per = ceil(G * D / splits) output elements belong to each CTA of the cluster.
+__host__ __device__ constexpr size_t attn_push_bytes(int splits, int G, int D) {
+  return ((size_t)splits * ((G * D + splits - 1) / splits) + (size_t)splits * G * 2) * sizeof(float);
+}
 
 template <int D, int S>
 __host__ __device__ constexpr size_t attn_smem_bytes() {
   return 1024 /*align*/ + (size_t)kWarps * S * 2 * kPageElems<D> * 2 + (size_t)kRows * D * 2 +
-         (size_t)kWarps * S * 8 + kMaxPagesPerSplit * 4 + 64;
+         (size_t)kWarps * S * 8 + kMaxPagesPerSplit * 4 + (size_t)D * 4 /*cos / sin row*/ + 64;
 }
 
 // CLUSTER: the splits of one (sequence, kv head) pair form a thread-block cluster (splits <= 16) and
@@ -173,9 +181,14 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   T* sQ = sKV + (size_t)kWarps * kStages * 2 * PE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sQ + kRows * kD);  // [kWarps][kStages]
   int* s_pages = reinterpret_cast<int*>(bars + kWarps * kStages);
+  float* s_cs = reinterpret_cast<float*>(s_pages + kMaxPagesPerSplit);  // [D]: cos, sin of the new position
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.nq / p.nkv;
+  float* s_red = s_cs + kD;  // push merge: what the cluster's CTAs push to this one (attn_push_bytes)
+  // push merge: first half of a cluster barrier that every CTA passes before its first remote store,
+  // so each CTA of the cluster has started before its shared memory is written
+  if (CLUSTER && args.push) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   constexpr int CH = kD / 8;  // 16-byte chunks per row
 
   if (threadIdx.x == 0) {
@@ -196,6 +209,9 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   // sequence length (no dependent load between them); longer rows read the split's range afterwards.
   const int* bt_row = p.block_tables + (size_t)b * p.max_blocks_per_seq;
   const bool whole_row = p.max_blocks_per_seq <= kMaxPagesPerSplit;
+  const bool rope = p.qkv != nullptr;
+  // positions, like the lengths, are written before the step starts; the RoPE tables are constant
+  const int pos = rope ? p.positions[b] : 0;
   const int seq = p.seq_lens[b];
   if (whole_row)
     for (int i = threadIdx.x; i < p.max_blocks_per_seq; i += blockDim.x) s_pages[i] = bt_row[i];
@@ -229,11 +245,17 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   // Without the fused append, the page holding the new token is written by the previous kernel and is
   // requested after the dependency wait; with it, its cache row is stale until this kernel writes it,
   // and the warp that owns the page patches the row in shared memory once the page has landed.
-  const bool rope = p.qkv != nullptr;
   const int last_pg = npages - 1;
 #pragma unroll
   for (int i = 0; i < kStages; ++i)
     if (rope || pg0 + warp + i * kWarps != last_pg) issue(i);
+  if (rope) {  // the position's RoPE row, staged before the wait: after it only the projection is loaded
+    for (int i = threadIdx.x; i < kD / 2; i += blockDim.x) {
+      s_cs[i] = p.cos_t[(size_t)pos * (kD / 2) + i];
+      s_cs[kD / 2 + i] = p.sin_t[(size_t)pos * (kD / 2) + i];
+    }
+    __syncthreads();
+  }
   pdl_wait_then_trigger();  // the next kernel (the o_proj GEMM) may start streaming its weights
   if (!rope) {
 #pragma unroll
@@ -242,13 +264,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
   }
   // the query tile is staged while the first pages are in flight (rotated here in the fused form)
   const int qkv_stride = (p.nq + 2 * p.nkv) * kD;
-  const int pos = rope ? p.positions[b] : 0;
   for (int c = threadIdx.x; c < kRows * CH; c += blockDim.x) {
     const int r = c / CH, ch = c % CH;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < G) {
       if (rope)
-        v = rope_chunk<T, D>(p, reinterpret_cast<const T*>(p.qkv) + (size_t)b * qkv_stride, kvh * G + r, ch, pos);
+        v = rope_chunk<T, D>(p, reinterpret_cast<const T*>(p.qkv) + (size_t)b * qkv_stride, kvh * G + r, ch, s_cs);
       else
         v = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.q) + ((size_t)b * p.nq + (size_t)kvh * G + r) *
                                            kD)[ch];
@@ -287,7 +308,7 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
       for (int c = lane; c < 2 * CH; c += 32) {
         const bool is_k = c < CH;
         const int ch = is_k ? c : c - CH;
-        const uint4 v = is_k ? rope_chunk<T, D>(p, src, p.nq + kvh, ch, pos)
+        const uint4 v = is_k ? rope_chunk<T, D>(p, src, p.nq + kvh, ch, s_cs)
                              : plain_chunk<T>(p, src, p.nq + p.nkv + kvh, ch, kD);
         *reinterpret_cast<uint4*>(const_cast<T*>(is_k ? sK : sV) + swzp(r, ch)) = v;
         T* cache = reinterpret_cast<T*>(const_cast<void*>(is_k ? p.k_cache : p.v_cache));  // the append writes the caches
@@ -416,6 +437,41 @@ __global__ void __launch_bounds__(kWarps * 32) k_decode_attn(const __grid_consta
     }
   }
   if (p.splits == 1) return;
+  if (CLUSTER && args.push) {
+    // Push merge: every CTA stores its partial of output element idx into the shared memory of the CTA
+    // that owns idx (and its (max, sum) rows into every CTA), one cluster barrier, then each owner folds
+    // the splits from local memory in split order - the arithmetic of the pull merge below, without its
+    // remote-load round trips and its second barrier.
+    cg::cluster_group cluster = cg::this_cluster();
+    const int cs = p.splits, r = split, per = (G * kD + cs - 1) / cs;
+    float* redML = s_red + (size_t)cs * per;  // [cs][G][2]
+    __syncthreads();  // this CTA's partial (cO, cML) complete
+    asm volatile("barrier.cluster.wait;" ::: "memory");  // second half of the start-up barrier
+    for (int idx = threadIdx.x; idx < G * kD; idx += blockDim.x) {
+      const int o = idx / per;
+      cluster.map_shared_rank(s_red, o)[(size_t)split * per + (idx - o * per)] = cO[idx];
+    }
+    for (int i = threadIdx.x; i < cs * G; i += blockDim.x) {  // (destination CTA, row)
+      const int c = i / G, g = i - c * G;
+      float* ml = cluster.map_shared_rank(redML, c) + ((size_t)split * G + g) * 2;
+      ml[0] = cML[g * 2];
+      ml[1] = cML[g * 2 + 1];
+    }
+    cluster.sync();  // release / acquire: every push has landed in its owner
+    for (int idx = r * per + threadIdx.x; idx < min(G * kD, (r + 1) * per); idx += blockDim.x) {
+      const int g = idx / kD, li = idx - r * per;
+      float M = -INFINITY;
+      for (int c = 0; c < cs; ++c) M = fmaxf(M, redML[(c * G + g) * 2]);
+      float L = 0.f, O = 0.f;
+      for (int c = 0; c < cs; ++c) {
+        const float f = safe_exp2_diff(redML[(c * G + g) * 2], M);
+        L += f * redML[(c * G + g) * 2 + 1];
+        O += f * s_red[(size_t)c * per + li];
+      }
+      out[idx] = from_f<T>(O / L);
+    }
+    return;  // no peer reads this CTA's shared memory after the barrier
+  }
   if (CLUSTER) {
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
@@ -555,6 +611,7 @@ cudaError_t launch_attention_s(const AttnParams& p, cudaStream_t s) {
                 "merge buffers must fit in the KV stages");
   AttnArgs a;
   a.p = p;
+  a.push = 0;
   // rows of the 2-D cache view; when the caller does not know the block count a large bound is used
   // (only rows named by the block tables are ever read)
   const uint64_t rows = (uint64_t)(p.num_blocks > 0 ? p.num_blocks : (1 << 22)) * p.nkv * kBS;
@@ -563,9 +620,11 @@ cudaError_t launch_attention_s(const AttnParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   e = tensor_map_2d(p.v_cache, rows, D, D * 2, kBS, 64, bf16, &a.tv);
   if (e != cudaSuccess) return e;
-  const size_t smem = attn_smem_bytes<D, S>();
   const dim3 grid(p.splits, p.nkv, p.batch);
   const bool cluster = p.cluster && p.splits > 1 && p.splits <= kMaxClusterSplits;
+  // the push merge for portable clusters (its buffer keeps two CTAs per SM with the shallow ring)
+  a.push = cluster && p.splits <= 8;
+  const size_t smem = attn_smem_bytes<D, S>() + (a.push ? attn_push_bytes(p.splits, p.nq / p.nkv, D) : 0);
   auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true, D, S> : k_decode_attn<__nv_bfloat16, false, D, S>)
                  : (cluster ? k_decode_attn<__half, true, D, S> : k_decode_attn<__half, false, D, S>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
