@@ -32,6 +32,10 @@ def main():
                     help="stamp every GEMM of the captured step (%%globaltimer) and print when each ran inside one "
                          "replay: the gaps between GEMMs hold the other kernels and the transitions")
     ap.add_argument("--attn-stages", type=int, default=0, help="attention KV ring depth (6: deep ring; 0: default)")
+    ap.add_argument("--lin-cfg", action="append", default=[],
+                    help="after tuning, force one projection's launch in every layer, e.g. "
+                         "o=cluster_splits:2,small_smem:1 (ops qkv, o, gu, down; repeatable; 'tuned' keeps "
+                         "the tuner's choices and prints them)")
     ap.add_argument("--tp-shape", type=int, default=1,
                     help="shard the weights this many ways (one GPU, the all-reduce replaced by add+RMSNorm) to "
                          "profile the per-rank kernels of a TP run")
@@ -54,6 +58,23 @@ def main():
     first = runner.prefill(prompts)
     runner.start(a.batch, first, a.prompt)
     stamps = None
+    if a.lin_cfg and not a.eager:
+        runner.tune(a.batch)
+        print("tuned:", {op: runner.lin[(0, op)].cfg.get(a.batch) for op in ("qkv", "o", "down")},
+              "gu fused:", runner.lin[(0, "gu")].fused.get(a.batch))
+        for spec in a.lin_cfg:
+            if spec == "tuned":  # keep the tuner's choices (a baseline run that prints them)
+                continue
+            op, kv = spec.split("=", 1)
+            cfg_o = {k: int(v) for k, v in (item.split(":") for item in kv.split(",") if item)}
+            for i in range(cfg.layers):
+                lin = runner.lin[(i, op)]
+                if op == "gu" and lin.fused.get(a.batch):
+                    lin.fused[a.batch] = dict(cfg_o)
+                else:
+                    lin.cfg[a.batch] = dict(cfg_o)
+        print("forced:", a.lin_cfg, {op: runner.lin[(0, op)].cfg.get(a.batch) for op in ("qkv", "o", "down")},
+              "gu fused:", runner.lin[(0, "gu")].fused.get(a.batch))
     if a.gemm_timeline and not a.eager:
         from .._ext import native
 
@@ -65,7 +86,7 @@ def main():
         n_total = native().gemm_stamp_launches()
         native().set_gemm_stamps(0, 0)
     elif not a.eager:
-        runner.capture(a.batch)
+        runner.capture(a.batch, tune=not a.lin_cfg)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.nvtx.range_push("decode")
