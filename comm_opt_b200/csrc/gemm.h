@@ -44,7 +44,8 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
 // of row r stored at chunk c ^ (r % 8)), rows past N zero. K must be a multiple of 64.
 // swiglu: W's rows are gate and up features interleaved by 64 (rows 128t..128t+63 gate features
 // 64t.., rows 128t+64..128t+127 the matching up features), Y is [M, N / 2] (row stride ldy) holding
-// silu(gate) * up of the bf16/fp16-rounded projections. Needs the cluster schedule with a split count
-// (after rounding K into equal k-step shares) of 2, 4, 8 or 16, and N a multiple of 128.
+// silu(gate) * up of the bf16/fp16-rounded projections. Needs N a multiple of 128 and either the cluster
+// schedule with a split count (after rounding K into equal k-step shares) of 2, 4, 8 or 16, or stream-K
+// with M <= 16 (the workspace then also holds a [64][16] float exchange area per CTA).
 
 }  // namespace cob

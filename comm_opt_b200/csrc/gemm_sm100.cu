@@ -102,16 +102,22 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" :::
 // CLUSTER: instead of the stream-K partition, CTA (t, r) of grid (tiles, s) owns k-range r of tile t and
 // the s CTAs of a tile form a thread-block cluster that sums its partial tiles through distributed
 // shared memory (no global workspace, no L2 round trips on the tail). `kps` = k-steps per split.
-// swiglu (CLUSTER with s in {2, 4, 8, 16}): W holds gate and up rows interleaved by 64 (tile t = gate
-// features 64t..64t+63, then the matching up features), Y is [M, N / 2] = silu(gate) * up. CTA r of the
+// swiglu: W holds gate and up rows interleaved by 64 (tile t = gate features 64t..64t+63, then the
+// matching up features), Y is [M, N / 2] = silu(gate) * up. CLUSTER (s in {2, 4, 8, 16}): CTA r of the
 // cluster receives gate rows [r * 64 / s, (r + 1) * 64 / s) of the tile together with their up rows, so
-// the product is formed where the sums are: the SiLU * up kernel and its round trip disappear.
-template <int BN, bool BF16, bool SMALL, bool CLUSTER>
+// the product is formed where the sums are. Stream-K (BN = 16): the epilogue warps holding the up rows
+// (TMEM lanes 64..127) hand them to the warps holding the gate rows through a per-CTA area of the
+// workspace (written, epilogue barrier, read) - for whole tiles and in the finisher of split tiles.
+// Either way the SiLU * up kernel and the [M, N] round trip disappear.
+// SW: the stream-K SwiGLU epilogue compiled in (BN = 16, stream-K only): a separate instance, so the
+// plain kernels keep their register budget (two CTAs per SM with the half ring).
+template <int BN, bool BF16, bool SMALL, bool CLUSTER, bool SW = false>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_streamk(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, void* Y, int M,
                    int N, int K, int ldy, float* ws, int* tile_ctr, int* err, unsigned long long timeout_ns,
                    int kps, int l2pf, long long* stamps, const uint8_t* __restrict__ Wp, int swiglu) {
   using C = Cfg<BN, SMALL, CLUSTER>;
+  static_assert(!SW || (BN == 16 && !CLUSTER), "the stream-K SwiGLU epilogue is for 16-column batch tiles");
   // optional phase stamps (%globaltimer, ns): stamps[cta * kStampSlots + phase]
   const int lin = blockIdx.x + blockIdx.y * gridDim.x;
   auto stamp = [&](int phase) {
@@ -289,6 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       cluster_wait();  // every CTA of the cluster has started: its shared memory may be written
       push_dst = cg::this_cluster().map_shared_rank(red, o) + ((size_t)blockIdx.y * per + slot) * (BN + 4);
     }
+    // stream-K SwiGLU: [64][BN] up-row values of the current tile, per CTA, past the partial slots
+    float* xch = ws + (size_t)P * 2 * BN * BM + (size_t)cta * (BM / 2) * BN;
     int j = 0;
     for (long long g = beg; g < end; ++j) {
       const int t = (int)(g / KT);
@@ -307,10 +315,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       // owning CTA's shared memory (distributed shared memory stores; this is the CTA's only segment)
       float* part = CLUSTER ? push_dst
                             : ws + ((size_t)cta * 2 + (t == first_tile ? 0 : 1)) * BN * BM + (size_t)row * BN;
+      float sw_gate[16];  // stream-K SwiGLU, whole tile: this gate row's 16 columns
       for (int c0 = 0; c0 < mcols; c0 += 16) {
         float v[16];
         tmem_ld16(taddr + c0, v);
-        if (whole) {
+        if (SW && whole) {
+          if (q >= 2) {  // up rows: to the exchange area
+#pragma unroll
+            for (int jj = 0; jj < 16; jj += 4)
+              *reinterpret_cast<float4*>(xch + (size_t)(row - BM / 2) * BN + jj) =
+                  make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) sw_gate[jj] = v[jj];
+          }
+        } else if (whole) {
           if (n < N) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj)
@@ -326,6 +345,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (q == 2 && lane == 0) stamp(kStEpiDone);
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&tempty[acc])) : "memory");
+      if (SW && whole) {
+        epi_sync();  // the up rows are in the exchange area
+        if (q < 2) {
+          const float* up = xch + (size_t)row * BN;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            if (jj < M) {
+              const float gv = round_out<BF16>(sw_gate[jj]), uv = round_out<BF16>(up[jj]);
+              store_out<BF16>(Y, (size_t)jj * ldy + t * (BM / 2) + row, gv / (1.f + __expf(-gv)) * uv);
+            }
+          }
+        }
+        epi_sync();  // the area is free for the next tile
+      }
       if (!CLUSTER && !whole) {
         // last contributor of tile t sums every contributor's partial in CTA order
         const int cfirst = sk_owner((long long)t * KT, total, P);
@@ -345,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           epi_sync();
           const float* base = ws + (size_t)row * BN;
           const int ncap = nc < kMaxContrib ? nc : kMaxContrib;
-          for (int c0 = 0; c0 < mcols; c0 += 4) {
+          auto sum4 = [&](int c0) {  // columns c0..c0+3 of this row over every contributor, in CTA order
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
             int c = 0;
             for (; c + 8 <= ncap; c += 8) {
@@ -367,11 +400,44 @@ __global__ void __launch_bounds__(kThreads, 1)
               a.z += v.z;
               a.w += v.w;
             }
-            if (n < N) {
-              const float o[4] = {a.x, a.y, a.z, a.w};
+            return a;
+          };
+          if (SW) {
+            // the up rows' sums go through the exchange area to the threads of their gate rows
+            float4 sw_sum[4];
 #pragma unroll
-              for (int u = 0; u < 4; ++u)
-                if (c0 + u < M) store_out<BF16>(Y, (size_t)(c0 + u) * ldy + n, o[u]);
+            for (int c4 = 0; c4 < 4; ++c4) sw_sum[c4] = 4 * c4 < mcols ? sum4(4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (q >= 2) {
+#pragma unroll
+              for (int c4 = 0; c4 < 4; ++c4)
+                *reinterpret_cast<float4*>(xch + (size_t)(row - BM / 2) * BN + 4 * c4) = sw_sum[c4];
+            }
+            epi_sync();
+            if (q < 2) {
+#pragma unroll
+              for (int c4 = 0; c4 < 4; ++c4) {
+                const float4 u4 = *reinterpret_cast<const float4*>(xch + (size_t)row * BN + 4 * c4);
+                const float gs[4] = {sw_sum[c4].x, sw_sum[c4].y, sw_sum[c4].z, sw_sum[c4].w};
+                const float us[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  if (4 * c4 + u < M) {
+                    const float gv = round_out<BF16>(gs[u]), uv = round_out<BF16>(us[u]);
+                    store_out<BF16>(Y, (size_t)(4 * c4 + u) * ldy + t * (BM / 2) + row, gv / (1.f + __expf(-gv)) * uv);
+                  }
+                }
+              }
+            }
+            epi_sync();
+          } else {
+            for (int c0 = 0; c0 < mcols; c0 += 4) {
+              const float4 a = sum4(c0);
+              if (n < N) {
+                const float o[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                  if (c0 + u < M) store_out<BF16>(Y, (size_t)(c0 + u) * ldy + n, o[u]);
+              }
             }
           }
           if (q == 2 && lane == 0) tile_ctr[t] = 0;
@@ -468,9 +534,13 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
                       cudaStream_t stream, const uint8_t* Wp, bool swiglu) {
   const bool clustered = splits > 0;
   const int smem = clustered ? Cfg<BN, SMALL, true>::SMEM : Cfg<BN, SMALL, false>::SMEM;
-  auto fn = clustered ? k_gemm_streamk<BN, BF16, SMALL, true> : k_gemm_streamk<BN, BF16, SMALL, false>;
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[clustered]) {
+  // stream-K SwiGLU: its own instance (BN = 16 only; the host rejects it for wider batch tiles)
+  const int form = clustered ? 1 : (swiglu && BN == 16 ? 2 : 0);
+  auto fn = form == 1 ? k_gemm_streamk<BN, BF16, SMALL, true>
+                      : (form == 2 ? k_gemm_streamk<BN, BF16, SMALL, false, BN == 16>
+                                   : k_gemm_streamk<BN, BF16, SMALL, false>);
+  static bool attr_set[3] = {false, false, false};
+  if (!attr_set[form]) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
@@ -479,7 +549,7 @@ cudaError_t launch_bn(const CUtensorMap& mw, const CUtensorMap& mx, void* Y, int
       e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return e;
     }
-    attr_set[clustered] = true;
+    attr_set[form] = true;
   }
   const int KT = (K + BK - 1) / BK;
   const int kps = clustered ? (KT + splits - 1) / splits : 0;
@@ -575,10 +645,14 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
                         bool pdl, bool small_smem, int cluster_splits, unsigned long long timeout_ns,
                         cudaStream_t stream, GemmPlan* used, bool packed, bool swiglu) {
   if (cluster_splits > 16 || (cluster_splits > 0 && M > 64)) return cudaErrorInvalidValue;
-  if (swiglu) {  // cluster split-K whose split count divides 64 (gate / up row pairs split evenly)
-    if (cluster_splits <= 0 || N % BM) return cudaErrorInvalidValue;
-    const int KT = (K + BK - 1) / BK, kps = (KT + cluster_splits - 1) / cluster_splits, s = (KT + kps - 1) / kps;
-    if (s < 2 || (BM / 2) % s) return cudaErrorInvalidValue;
+  if (swiglu) {
+    if (N % BM) return cudaErrorInvalidValue;
+    if (cluster_splits > 0) {  // cluster split-K whose split count divides 64 (gate / up row pairs split evenly)
+      const int KT = (K + BK - 1) / BK, kps = (KT + cluster_splits - 1) / cluster_splits, s = (KT + kps - 1) / kps;
+      if (s < 2 || (BM / 2) % s) return cudaErrorInvalidValue;
+    } else if (M > 16) {  // stream-K: the 16-column batch tile only
+      return cudaErrorInvalidValue;
+    }
   }
   if (M <= 0 || M > 256 || N <= 0 || K <= 0 || K % 8 || (dtype != kBF16 && dtype != kF16))
     return cudaErrorInvalidValue;
@@ -586,7 +660,10 @@ cudaError_t gemm_decode(const void* X, const void* W, void* Y, int M, int N, int
   if (packed && (K % BK || (reinterpret_cast<uintptr_t>(W) & 15))) return cudaErrorInvalidValue;
   const GemmPlan p = plan_gemm(M, N, K, num_sms, ctas_override);
   if (used) *used = p;
-  if (p.tiles > max_tiles || gemm_workspace_bytes(p.ctas, p.bn) > ws_bytes) return cudaErrorInvalidValue;
+  // stream-K SwiGLU also uses a [64][bn] exchange area per CTA past the partial slots
+  const size_t ws_need = gemm_workspace_bytes(p.ctas, p.bn) +
+                         (swiglu && cluster_splits <= 0 ? (size_t)p.ctas * (BM / 2) * p.bn * sizeof(float) : 0);
+  if (p.tiles > max_tiles || ws_need > ws_bytes) return cudaErrorInvalidValue;
   const bool bf16 = dtype == kBF16;
   CUtensorMap mw = {}, mx;
   cudaError_t e = packed ? cudaSuccess : tensor_map(W, N, K, BM, bf16, &mw);

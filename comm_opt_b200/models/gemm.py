@@ -138,16 +138,17 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ctas
     ``small_smem`` halves the TMA ring so the next kernel can share the SM (programmatic launch).
     ``w`` is a row-major [N, K] tensor or a PackedWeight (bulk loads of contiguous weight blocks).
     ``swiglu``: w's rows are gate/up interleaved by 64 (`pack_weight(w, interleave=64)`) and out is
-    [M, N / 2] = silu(gate) * up, formed in the cluster reduction (needs a cluster split count of 2, 4, 8
-    or 16, `swiglu_splits`)."""
+    [M, N / 2] = silu(gate) * up, formed in the cluster reduction (a cluster split count of 2, 4, 8 or 16,
+    `swiglu_splits`) or, with stream-K and M <= 16, in the epilogue (up rows handed to the gate rows'
+    threads through the workspace)."""
     M, N = x.shape[0], w.shape[0]
     if out is None:
         out = torch.empty(M, N // 2 if swiglu else N, dtype=x.dtype, device=x.device)
     st = _state(x.device)
     packed = isinstance(w, PackedWeight)
     wt, pn = (w.data, w.n) if packed else (w, 0)
-    if swiglu and (M > 64 or not cluster_splits):
-        raise ValueError("the SwiGLU epilogue needs M <= 64 and the cluster schedule")
+    if swiglu and (M > 64 or (not cluster_splits and M > 16)):
+        raise ValueError("the SwiGLU epilogue needs M <= 64 with the cluster schedule, M <= 16 with stream-K")
     for m0 in range(0, M, 256):
         m1 = min(M, m0 + 256)
         native().gemm(x[m0:m1], wt, out[m0:m1], st["ws"], st["ctr"], st["err"], ctas, pdl, small_smem,
@@ -172,8 +173,8 @@ def swiglu_splits(K: int, splits: int) -> bool:
 def candidates(M: int, N: int, K: int, num_sms: int = 148, swiglu: bool = False) -> list[dict]:
     """Launch configurations worth measuring for one decode shape: stream-K with the full or the half
     ring, and cluster split-K with 2..16 splits while the grid stays within one wave (two CTAs per SM with
-    the half ring). With `swiglu` only the cluster splits the SwiGLU epilogue accepts."""
-    cands = [] if swiglu else [dict(), dict(small_smem=True)]
+    the half ring). With `swiglu` only the schedules the SwiGLU epilogue accepts (stream-K for M <= 16)."""
+    cands = [] if swiglu and M > 16 else [dict(), dict(small_smem=True)]
     tiles = (N + 127) // 128
     # the SwiGLU epilogue exists only in the cluster schedule: for wide outputs (more tiles than SMs) its
     # multi-wave grids are measured too, and the caller weighs them against stream-K + the SiLU kernel

@@ -156,13 +156,41 @@ def test_gemm_swiglu_epilogue(cuda, M, I, K, dtype, splits, small, packed):
     assert rel_err(act, ref) <= 2 ** -6, rel_err(act, ref)
 
 
+@pytest.mark.parametrize("M,I,K", [(1, 64, 1024), (8, 3584, 8192), (5, 192, 4096), (16, 1024, 2048)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("sched", [dict(), dict(small_smem=True, pdl=True), dict(ctas=5), dict(ctas=7),
+                                   dict(ctas="tiles")])
+def test_gemm_swiglu_epilogue_stream_k(cuda, M, I, K, dtype, sched):
+    """Stream-K with the SwiGLU epilogue (M <= 16): whole tiles and tiles split between CTAs (their last
+    contributor finishes them) give the bits of the plain launch of the same schedule followed by the
+    SiLU * up kernel, and silu(gate) * up of the fp32 projection within tolerance."""
+    from comm_opt_b200.models.gemm import pack_weight
+    from comm_opt_b200.ops import kernels as K_
+
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + I + K)
+    x = torch.randn(M, K, device=cuda, generator=g).to(dtype)
+    w = (0.05 * torch.randn(2 * I, K, device=cuda, generator=g)).to(dtype)
+    wi = pack_weight(w, interleave=64)
+    sched = dict(sched)
+    if sched.get("ctas") == "tiles":
+        sched["ctas"] = (2 * I) // 128  # one CTA per output tile: whole tiles only
+    act = gemm(x, wi, swiglu=True, **sched)
+    plain = gemm(x, wi, **sched)
+    torch.cuda.synchronize()
+    assert int(gemm_error_word(cuda)) == 0
+    assert torch.equal(act, K_.silu_mul(plain, interleave=64))
+    gu = x.float() @ w.float().t()
+    ref = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+    assert rel_err(act, ref) <= 2 ** -6, rel_err(act, ref)
+
+
 def test_gemm_swiglu_rejects_other_schedules(cuda):
-    """The SwiGLU epilogue is refused (not silently wrong) for stream-K and for split counts that do not
-    pair every gate row with its up row inside one CTA."""
+    """The SwiGLU epilogue is refused (not silently wrong) for stream-K beyond 16 rows and for split counts
+    that do not pair every gate row with its up row inside one CTA."""
     x = torch.randn(8, 1024, device=cuda).bfloat16()
     w = torch.randn(256, 1024, device=cuda).bfloat16()
     with pytest.raises(ValueError):
-        gemm(x, w, swiglu=True)
+        gemm(torch.randn(32, 1024, device=cuda).bfloat16(), w, swiglu=True)
     with pytest.raises(RuntimeError):
         gemm(x, w, cluster_splits=3, swiglu=True)  # 3 CTAs per tile
     with pytest.raises(RuntimeError):

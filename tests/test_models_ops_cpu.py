@@ -409,7 +409,10 @@ def test_gate_up_interleave_round_trip_and_split_rule():
     assert [s for s in (2, 3, 4, 6, 8, 12, 16) if swiglu_splits(8192, s)] == [2, 4, 8, 16]
     assert not swiglu_splits(64, 2)  # one k-step: one CTA per tile
     c = candidates(8, 7168, 8192, 148, swiglu=True)
-    assert c and all(x.get("swiglu") and swiglu_splits(8192, x["cluster_splits"]) for x in c)
+    assert c and all(x.get("swiglu") and (not x.get("cluster_splits") or swiglu_splits(8192, x["cluster_splits"]))
+                     for x in c)
+    assert {"small_smem": True, "swiglu": True} in c and {"swiglu": True} in c  # stream-K at M <= 16
+    assert all(x.get("cluster_splits") for x in candidates(32, 7168, 8192, 148, swiglu=True))
 
 
 def test_variant_table_validation_rule():
