@@ -574,6 +574,14 @@ int& attn_stage_mode() {
   return mode;
 }
 
+size_t attn_launch_smem_bytes(int splits, int group, int head_dim, bool cluster, int stages) {
+  const bool deep = stages == kStagesDeep;
+  const size_t base = head_dim == 128 ? (deep ? attn_smem_bytes<128, kStagesDeep>() : attn_smem_bytes<128, kStages>())
+                                      : (deep ? attn_smem_bytes<64, kStagesDeep>() : attn_smem_bytes<64, kStages>());
+  const bool cl = cluster && splits > 1 && splits <= kMaxClusterSplits;
+  return base + (cl && splits <= 8 ? attn_push_bytes(splits, group, head_dim) : 0);
+}
+
 namespace {
 
 // KV ring depth of one launch. The deep ring (all four pages of every warp of a 2048-token, 8-way split
@@ -624,7 +632,7 @@ cudaError_t launch_attention_s(const AttnParams& p, cudaStream_t s) {
   const bool cluster = p.cluster && p.splits > 1 && p.splits <= kMaxClusterSplits;
   // the push merge for portable clusters (its buffer keeps two CTAs per SM with the shallow ring)
   a.push = cluster && p.splits <= 8;
-  const size_t smem = attn_smem_bytes<D, S>() + (a.push ? attn_push_bytes(p.splits, p.nq / p.nkv, D) : 0);
+  const size_t smem = attn_launch_smem_bytes(p.splits, p.nq / p.nkv, D, cluster, S);
   auto fn = bf16 ? (cluster ? k_decode_attn<__nv_bfloat16, true, D, S> : k_decode_attn<__nv_bfloat16, false, D, S>)
                  : (cluster ? k_decode_attn<__half, true, D, S> : k_decode_attn<__half, false, D, S>);
   e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

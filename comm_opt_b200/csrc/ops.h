@@ -68,5 +68,8 @@ cudaError_t paged_decode_attention(const AttnParams& p, cudaStream_t s);
 // KV ring depth of the attention kernel, read at launch: 6 = the deep ring (one CTA per SM) where the
 // grid fits one wave at one CTA per SM and clusters of at most 8; any other value = 3 pages per warp.
 int& attn_stage_mode();
+// Dynamic shared memory of one attention launch (the KV ring of `stages` pages per warp, the query tile,
+// barriers, the page list, the RoPE row, and the push merge's buffer for clusters of 2..8).
+size_t attn_launch_smem_bytes(int splits, int group, int head_dim, bool cluster, int stages);
 
 }  // namespace cob

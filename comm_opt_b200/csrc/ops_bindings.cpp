@@ -399,6 +399,9 @@ void register_ops(pybind11::module& m) {
     return (int64_t)old;
   });
   m.def("attn_scratch_bytes", &py_attn_scratch_bytes);
+  m.def("attn_launch_smem_bytes", [](int64_t splits, int64_t group, int64_t head_dim, bool cluster, int64_t stages) {
+    return (int64_t)cob::attn_launch_smem_bytes((int)splits, (int)group, (int)head_dim, cluster, (int)stages);
+  });
   m.def("decode_attention", &py_decode_attention, pybind11::arg("q"), pybind11::arg("k_cache"),
         pybind11::arg("v_cache"), pybind11::arg("block_tables"), pybind11::arg("seq_lens"), pybind11::arg("out"),
         pybind11::arg("scratch"), pybind11::arg("splits"), pybind11::arg("pages_per_split"), pybind11::arg("scale"),

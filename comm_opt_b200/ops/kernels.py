@@ -81,7 +81,7 @@ def argmax_combine(gathered: torch.Tensor, world: int, ids: torch.Tensor | None 
     return ids
 
 
-ATTN_CTAS_PER_SM = 2  # the kernel's shared memory (~106 KB) allows two resident CTAs per SM
+ATTN_CTAS_PER_SM = 2  # the kernel's shared memory (104-114 KB with the push merge) allows two CTAs per SM
 
 
 def attention_split_plan(batch: int, nkv: int, max_pages: int, num_sms: int = 148) -> tuple[int, int, bool]:

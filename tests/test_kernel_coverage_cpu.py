@@ -243,3 +243,27 @@ def test_layer_boundary_pieces_and_push_groups_cover_once():
                         for r in range(splits):
                             feats[t * BM + r * per:t * BM + (r + 1) * per] += 1
                     assert (feats[:N] == 1).all(), (model, tp, M, N, K, splits)
+
+
+def test_attention_shared_memory_keeps_two_ctas_per_sm():
+    """The split planner assumes two resident attention CTAs per SM (ATTN_CTAS_PER_SM): with the shallow KV
+    ring every launch form - no merge, the push merge of 2..8-CTA clusters (its buffer grows with the
+    query group and the split count), the pull merge of 9..16 - fits twice into one SM's 228 KB (each
+    CTA also holds 1 KB for the driver); the deep ring fits one CTA per SM (227 KB per block)."""
+    from comm_opt_b200._ext import native
+    from comm_opt_b200.ops.kernels import ATTN_CTAS_PER_SM
+
+    C = native()
+    sm_bytes, block_max = 228 * 1024, 227 * 1024
+    for D in (64, 128):
+        for group in range(1, 17):
+            for splits in range(1, 17):
+                for cluster in (False, True):
+                    shallow = C.attn_launch_smem_bytes(splits, group, D, cluster, 3)
+                    assert ATTN_CTAS_PER_SM * (shallow + 1024) <= sm_bytes, (D, group, splits, cluster, shallow)
+                    deep = C.attn_launch_smem_bytes(splits, group, D, cluster, 6)
+                    assert deep + 1024 <= block_max, (D, group, splits, cluster, deep)
+                    if cluster and 1 < splits <= 8:  # the push merge's buffer: partials + (max, sum) rows
+                        per = -(-group * D // splits)
+                        assert shallow - C.attn_launch_smem_bytes(splits, group, D, False, 3) == \
+                            4 * (splits * per + splits * group * 2)
