@@ -267,3 +267,56 @@ def test_attention_shared_memory_keeps_two_ctas_per_sm():
                         per = -(-group * D // splits)
                         assert shallow - C.attn_launch_smem_bytes(splits, group, D, False, 3) == \
                             4 * (splits * per + splits * group * 2)
+
+
+def test_attention_push_merge_slots():
+    """k_decode_attn's push merge (clusters of 2..8): split s stores its partial of output element idx at
+    slot s * per + (idx - o * per) of owner o = idx // per and its (max, sum) of row g at (s * G + g) * 2
+    of every CTA; owner r folds, for each of its elements, slot c * per + (idx - r * per) of every split c.
+    Every owner slot is written exactly once, stays inside the buffer that attn_push_bytes sizes, and
+    holds exactly the partial the owner reads for that (split, element)."""
+    for G in (1, 4, 5, 8, 16):
+        for D in (64, 128):
+            for cs in range(2, 9):
+                per = -(-G * D // cs)
+                written = {}
+                for s in range(cs):
+                    for idx in range(G * D):
+                        o = idx // per
+                        key = (o, s * per + (idx - o * per))
+                        assert key not in written and key[1] < cs * per
+                        written[key] = (s, idx)
+                    for c in range(cs):
+                        for g in range(G):
+                            assert (s * G + g) * 2 + 1 < cs * G * 2
+                for r in range(cs):
+                    for idx in range(r * per, min(G * D, (r + 1) * per)):
+                        for c in range(cs):
+                            assert written[(r, c * per + (idx - r * per))] == (c, idx)
+                assert len(written) == cs * G * D
+
+
+def test_gemm_swiglu_row_pairing():
+    """Decode GEMM SwiGLU epilogue, gate/up rows interleaved by 64 in a 128-row tile. Cluster form (s CTAs,
+    s | 64): row `row` goes to owner f // ph, slot f - o * ph (+ ph for up rows), f = row % 64, ph = 64 / s;
+    owner r pairs slot lr (gate) with slot ph + lr (up) and writes output feature t * 64 + r * ph + lr.
+    Stream-K form: the up row 64 + f is exchanged through entry f of the [64][16] area and read by the
+    thread of gate row f. Either way every output feature f of a tile gets gate row f and up row 64 + f,
+    once."""
+    BM = 128
+    for s in (2, 4, 8, 16):
+        ph, per = (BM // 2) // s, BM // s
+        slots = {}
+        for row in range(BM):
+            f = row % (BM // 2)
+            o = f // ph
+            slot = f - o * ph + (ph if row >= BM // 2 else 0)
+            assert 0 <= slot < per and (o, slot) not in slots
+            slots[(o, slot)] = row
+        for r in range(s):
+            for lr in range(ph):
+                gate, up = slots[(r, lr)], slots[(r, ph + lr)]
+                feature = r * ph + lr
+                assert gate == feature and up == BM // 2 + feature
+    for row in range(BM // 2, BM):  # stream-K exchange: the up thread's entry is its gate row's index
+        assert row - BM // 2 == row % (BM // 2)
