@@ -434,3 +434,32 @@ def test_variant_table_validation_rule():
     assert res[8]["within"] and not res[8]["retune"]
     assert not res[64]["within"] and res[64]["retune"] and res[64]["best"] == "ours:lamport_2s"
     assert not res[128]["retune"]  # 18 % slower by the median, but the intervals overlap
+
+
+def test_gate_up_linear_keeps_the_faster_form(monkeypatch):
+    """GateUpLinear.tune: the SwiGLU-epilogue launch is kept only when it measures no slower than the best
+    plain launch plus the SiLU * up kernel; weights not interleaved by 64 (or cuBLAS) never use it."""
+    import comm_opt_b200.models.gemm as G
+
+    w = G.pack_weight(torch.zeros(256, 128).bfloat16(), interleave=64)
+    times = {}
+
+    def fake_tune(weight, M, iters=20, swiglu=False):
+        return dict(times["sw" if swiglu else "plain"], us=times["sw_us" if swiglu else "plain_us"])
+
+    monkeypatch.setattr(G, "tune", fake_tune)
+    monkeypatch.setattr(G, "_silu_us", lambda M, inter, dtype, device: 2.0)
+    for sw_us, plain_us, fused in ((143.0, 141.5, True), (144.0, 141.5, False), (20.8, 20.5, True)):
+        times.update(sw=dict(cluster_splits=4, small_smem=True, swiglu=True), plain=dict(small_smem=True),
+                     sw_us=sw_us, plain_us=plain_us)
+        lin = G.GateUpLinear(w)
+        lin.tune(8)
+        assert (lin.kernels(8) == 1) == fused, (sw_us, plain_us)
+        assert (lin.fused[8] == times["sw"]) if fused else (lin.cfg[8] == {"small_smem": True})
+    plain_w = G.pack_weight(torch.zeros(256, 128).bfloat16())  # [gate; up] rows: no epilogue
+    lin = G.GateUpLinear(plain_w)
+    lin.tune(8)
+    assert lin.kernels(8) == 2 and lin.il == 0
+    lin = G.GateUpLinear(torch.zeros(256, 128).bfloat16(), impl="torch")
+    lin.tune(8)
+    assert lin.kernels(8) == 2
